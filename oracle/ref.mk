@@ -1,0 +1,35 @@
+# ref.mk -- TEST INFRASTRUCTURE: builds reference-side checkers into oracle/_ref/ (git-ignored; the built binaries
+# travel to the GPU box, the reference tree does not).  Run from anywhere:  make -f oracle/ref.mk [REF=...]
+#
+#   _ref/emu_dump      the reference's Hopper host emulator (hopper/emu/emu.cpp, compiled where it lies) driven by
+#                      oracle/ref_emu_dump.cpp: dumps one reference kernel's inputs, fp64 reference and C (CPU only)
+#   _ref/verif_bw      the reference's own GPU check, hopper/verif.cu compiled where it lies, linked with this
+#                      repository's candidate (gemm-ladder_b200/blackwell/candidate.cu over libbwgemm.so): the
+#                      reference's 26 edge shapes, fp64 CPU reference and 8 bit-for-bit repeats, run on the B200
+#
+# Nothing here is built from a copy of the reference's sources, and nothing runs the reference's own build system.
+REF ?= /root/reference
+HERE := $(dir $(abspath $(lastword $(MAKEFILE_LIST))))
+ROOT := $(abspath $(HERE)..)
+OUT := $(HERE)_ref
+CXX ?= g++
+NVCC ?= nvcc
+PKG := $(ROOT)/gemm-ladder_b200
+
+all: $(OUT)/emu_dump $(OUT)/verif_bw
+emu_dump: $(OUT)/emu_dump
+verif_bw: $(OUT)/verif_bw
+
+$(OUT):
+	mkdir -p $(OUT)
+
+$(OUT)/emu_dump: $(HERE)ref_emu_dump.cpp | $(OUT)
+	$(CXX) -std=c++17 -O2 -march=x86-64-v3 -w -I$(REF)/hopper/emu -I$(REF)/hopper -I$(REF)/hopper/emu/shim \
+	    $(HERE)ref_emu_dump.cpp -o $@
+
+$(OUT)/verif_bw: $(REF)/hopper/verif.cu $(PKG)/blackwell/candidate.cu $(PKG)/lib/libbwgemm.so | $(OUT)
+	$(NVCC) -std=c++17 -O2 -gencode arch=compute_100a,code=sm_100a -I$(ROOT)/include \
+	    $(REF)/hopper/verif.cu $(PKG)/blackwell/candidate.cu -o $@ \
+	    -L$(PKG)/lib -lbwgemm -Xlinker -rpath -Xlinker '$$ORIGIN/../../gemm-ladder_b200/lib' -lcublasLt
+
+.PHONY: all emu_dump verif_bw
