@@ -1,0 +1,413 @@
+#!/usr/bin/env python
+"""bench.py -- throughput of the Blackwell rung's GEMM (C = A B, fp16 in, fp32 accumulate, fp16 out) on B200.
+
+One step = one GEMM over one batch of synthetic inputs (seeded uniform [-1, 1) fp16, the value distribution of the
+judge's fill, judge/judge.cu:127-134), three input sets rotating as in the judge (so the working set, 3 x (A + B),
+is larger than the 126 MB L2 and no flush is needed).
+
+Default workload (N = 1): BASELINE config 1, M x N x K = 4608 x 5632 x 8192, TFLOP/s.  With --gpus N (torchrun, one
+rank per GPU) each rank computes its own column shard of a wider GEMM (the column-parallel split of a Megatron MLP:
+N = 5632 per rank, no communication): weak scaling, value = all ranks' FLOPs / the slowest rank's device time.
+
+Printed (rank 0, one JSON line): value (device time, inputs resident in HBM), e2e (the same through the public API
+with host buffers: pinned host -> device copies of A and B and the device -> host read of C inside the timed region),
+roofline (the kernel against the measured cuBLAS peak), cpu_baseline (the fp64 oracle on a bounded sample of rows,
+all host threads), clocks sampled through NVML during the timed region, gpu_launches.  --sweep adds the judge's 17
+B200 shapes timed against torch.matmul (cuBLAS) in CUDA graphs, with the geometric mean of the time ratios.
+
+--impl reference: the reference's CPU path (its fp64 i-k-j GEMM, restated in oracle/oracle.c; the reference's GPU
+harness needs its judge, which needs CUDA 13) timed on the host cores on the same workload, in bounded row samples.
+"""
+import argparse
+import datetime
+import json
+import math
+import os
+import re
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "gemm-ladder_b200")
+for _p in (ROOT, PKG, os.path.join(ROOT, "tests")):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+WORKLOADS = {
+    "config1": (4608, 5632, 8192),
+    "ladder": (8192, 8192, 8192),
+    "ladder_4096": (4096, 6144, 8192),
+}
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="config1")
+    ap.add_argument("--variant", type=int, default=0)
+    ap.add_argument("--sweep", action="store_true", help="also time the judge's 17 shapes against cuBLAS")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    return ap.parse_args()
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return p, "measured"
+    except OSError:
+        return dict(FALLBACK_PEAKS), "fallback"
+
+
+def profile_traffic(workload):
+    """DRAM bytes per launch of the GEMM kernel at this workload, from the committed ncu summary (or None)."""
+    path = os.path.join(ROOT, "profiles", f"gemm_kernel_{workload}.md")
+    try:
+        with open(path) as f:
+            m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", f.read())
+        return float(m.group(1)) if m else None
+    except OSError:
+        return None
+
+
+# ------------------------------------------------------------------------------------------------------ clocks
+class ClockSampler:
+    """NVML samples of the SM clock and the clock-event reasons while the timed region runs."""
+
+    REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
+               0x10: "sync_boost", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+               0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting"}
+
+    def __init__(self, device_index):
+        self.samples, self.reasons, self.max_mhz = [], 0, None
+        self._stop = threading.Event()
+        self._h = None
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self._nv = pynvml
+            self._h = self._handle(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self._h = None
+
+    def _handle(self, device_index):
+        import torch
+
+        nv = self._nv
+        try:
+            uuid = str(torch.cuda.get_device_properties(device_index).uuid)
+            return nv.nvmlDeviceGetHandleByUUID(("GPU-" + uuid) if not uuid.startswith("GPU-") else uuid)
+        except Exception:
+            return nv.nvmlDeviceGetHandleByIndex(device_index)
+
+    def _run(self):
+        nv = self._nv
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM))
+                self.reasons |= nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+            except Exception:
+                pass
+            time.sleep(0.01)
+
+    def __enter__(self):
+        if self._h is not None:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        return self
+
+    def __exit__(self, *exc):
+        if self._h is not None:
+            self._stop.set()
+            self._t.join()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["nvml unavailable"]}
+        names = [n for bit, n in self.REASONS.items() if self.reasons & bit]
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz, "reasons": names,
+                "samples": len(self.samples)}
+
+
+# ------------------------------------------------------------------------------------------------------ distributed
+def dist_setup(args):
+    import torch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return rank, world, local
+
+
+def dist_max(x, world):
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world):
+    import torch
+
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+# ------------------------------------------------------------------------------------------------------ our arm
+def make_sets(M, N, K, seed, sets=3):
+    import torch
+
+    g = torch.Generator(device="cuda")
+    g.manual_seed(seed)
+    A = [(torch.rand((M, K), generator=g, device="cuda") * 2 - 1).half() for _ in range(sets)]
+    B = [(torch.rand((K, N), generator=g, device="cuda") * 2 - 1).half() for _ in range(sets)]
+    return A, B
+
+
+def cpu_baseline(M, N, K, seconds):
+    """The fp64 oracle (oracle/oracle.c, the reference's i-k-j loop) on a bounded sample of rows, all host threads."""
+    import numpy as np
+
+    from oracle import oracle
+
+    threads = os.cpu_count() or 1
+    rows0 = min(M, max(threads, 8))
+    A, B = oracle.judge_inputs(rows0, N, K)
+    t0 = time.perf_counter()
+    oracle.gemm_f64(A, B, threads=threads)
+    t = time.perf_counter() - t0
+    rows = int(min(M, max(rows0, rows0 * seconds / max(t, 1e-6))))
+    rows = max(threads, rows // threads * threads) if rows >= threads else rows
+    A, B = oracle.judge_inputs(rows, N, K)
+    t0 = time.perf_counter()
+    oracle.gemm_f64(A, B, threads=threads)
+    t = time.perf_counter() - t0
+    del np
+    return {"value": 2.0 * rows * N * K / t / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+            "sample": f"{rows} of {M} rows of {M}x{N}x{K}, fp64 i-k-j oracle (oracle/oracle.c), {t:.1f} s"}
+
+
+def sweep(args, stream_runs=3):
+    """The judge's 17 shapes (+ BASELINE's ladder variants): ours and torch.matmul (cuBLAS), CUDA graphs of G calls
+    on 3 rotating input sets, interleaved rounds, median; ratio = cuBLAS time / ours (the judge's ratio)."""
+    import torch
+
+    import bwgemm
+    from shapes import CONFIG1, JUDGE_B200, LADDER_4096
+
+    out = {}
+    ratios = []
+    for name, M, N, K in list(JUDGE_B200) + [LADDER_4096, CONFIG1]:
+        A, B = make_sets(M, N, K, seed=M * 7 + N)
+        C = torch.empty((M, N), dtype=torch.float16, device="cuda")
+        flops = 2.0 * M * N * K
+        G = max(3, min(60, int(20e-3 / max(flops / 1.2e15, 5e-6))))
+        bwgemm.gemm(A[0], B[0], C, variant=args.variant)  # the first call of a shape (workspace)
+        torch.matmul(A[0], B[0], out=C)
+        torch.cuda.synchronize()
+        graphs = {}
+        for arm in ("ours", "cublas"):
+            g = torch.cuda.CUDAGraph()
+            s = torch.cuda.Stream()
+            s.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(s):
+                with torch.cuda.graph(g, stream=s):
+                    for i in range(G):
+                        if arm == "ours":
+                            bwgemm.gemm(A[i % 3], B[i % 3], C, variant=args.variant)
+                        else:
+                            torch.matmul(A[i % 3], B[i % 3], out=C)
+            torch.cuda.synchronize()
+            graphs[arm] = g
+        times = {"ours": [], "cublas": []}
+        for rnd in range(stream_runs):
+            for arm in (("ours", "cublas") if rnd % 2 == 0 else ("cublas", "ours")):
+                g = graphs[arm]
+                g.replay()  # warm-up
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                reps = max(1, int(0.15 / max(G * flops / 1.2e15, 1e-5)))
+                e0.record()
+                for _ in range(reps):
+                    g.replay()
+                e1.record()
+                torch.cuda.synchronize()
+                times[arm].append(e0.elapsed_time(e1) / 1e3 / (reps * G))
+        t_ours, t_cub = statistics.median(times["ours"]), statistics.median(times["cublas"])
+        ratio = t_cub / t_ours
+        ratios.append(ratio)
+        bytes_alg = 2.0 * (M * K + K * N + M * N)
+        out[name] = {"M": M, "N": N, "K": K, "us": round(t_ours * 1e6, 2), "cublas_us": round(t_cub * 1e6, 2),
+                     "ratio": round(ratio, 4), "tflops": round(flops / t_ours / 1e12, 1),
+                     "gbs": round(bytes_alg / t_ours / 1e9, 1)}
+        del graphs, A, B, C
+        torch.cuda.empty_cache()
+    judge = [out[n]["ratio"] for n, *_ in JUDGE_B200]
+    return {"shapes": out, "geomean_ratio_vs_cublas_17": round(math.exp(sum(map(math.log, judge)) / len(judge)), 4),
+            "reference": "torch.matmul fp16 (cuBLAS heuristic), CUDA graphs, 3 rotating input sets"}
+
+
+def run_ours(args):
+    import torch
+
+    import bwgemm
+
+    rank, world, local = dist_setup(args)
+    M, N, K = WORKLOADS[args.workload]
+    flops_rank = 2.0 * M * N * K
+    A, B = make_sets(M, N, K, seed=1234 + rank)
+    C = torch.empty((M, N), dtype=torch.float16, device="cuda")
+    stream = torch.cuda.current_stream()
+    for i in range(max(3, args.warmup)):
+        bwgemm.gemm(A[i % 3], B[i % 3], C, variant=args.variant)
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        barrier(world)
+        e0.record(stream)
+        for i in range(args.steps):
+            bwgemm.gemm(A[i % 3], B[i % 3], C, variant=args.variant)
+        e1.record(stream)
+        barrier(world)
+    t_rank = e0.elapsed_time(e1) / 1e3
+    t = dist_max(t_rank, world)
+    code = bwgemm.status()[0]
+    value = flops_rank * world * args.steps / t / 1e12
+    ms_per_step = t / args.steps * 1e3
+
+    # end to end through the public API with host buffers
+    e2e = None
+    if not args.no_e2e:
+        hA = torch.empty((M, K), dtype=torch.float16, pin_memory=True)
+        hB = torch.empty((K, N), dtype=torch.float16, pin_memory=True)
+        hC = torch.empty((M, N), dtype=torch.float16, pin_memory=True)
+        hA.copy_(A[0])
+        hB.copy_(B[0])
+        dA, dB = A[1], B[1]
+        steps_e2e = max(3, min(args.steps, 20))
+        for _ in range(2):
+            dA.copy_(hA, non_blocking=True)
+            dB.copy_(hB, non_blocking=True)
+            bwgemm.gemm(dA, dB, C)
+            hC.copy_(C, non_blocking=True)
+        barrier(world)
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record(stream)
+        for _ in range(steps_e2e):
+            dA.copy_(hA, non_blocking=True)
+            dB.copy_(hB, non_blocking=True)
+            bwgemm.gemm(dA, dB, C)
+            hC.copy_(C, non_blocking=True)
+        f1.record(stream)
+        barrier(world)
+        te = dist_max(f0.elapsed_time(f1) / 1e3, world)
+        e2e = {"value": round(flops_rank * world * steps_e2e / te / 1e12, 2), "unit": "TFLOP/s",
+               "h2d_bytes_per_step": (M * K + K * N) * 2, "d2h_bytes_per_step": M * N * 2,
+               "steps": steps_e2e, "path": "bwgemm.gemm (ctypes -> bw_gemm_f16) with pinned host buffers"}
+
+    pk, pk_kind = peaks()
+    achieved = flops_rank / (t_rank / args.steps) / 1e12
+    traffic = profile_traffic(args.workload)
+    roofline = {"bound": "tensor", "achieved": round(achieved, 1), "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                "frac": round(achieved / pk["bf16_tflops"], 4), "traffic": traffic,
+                "peak_kind": f"{pk_kind}: dense 16-bit GEMM (cuBLAS bf16 8192^3, burst)",
+                "algorithmic_bytes_per_launch": (M * K + K * N + M * N) * 2}
+    result = {
+        "metric": "TFLOP/s of C = A.B (fp16 in, fp32 accumulate, fp16 out), BASELINE config 1",
+        "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms_per_step, 5), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "fp16 (fp32 accumulate)", "data": "synthetic: seeded uniform [-1, 1) fp16",
+        "config": {"workload": f"{args.workload} {M}x{N}x{K}" + (f" per rank (column shards, N total {N * world})"
+                                                                  if world > 1 else ""),
+                   "M": M, "N": N, "K": K, "variant": args.variant,
+                   "l2": "3 rotating input sets (%.0f MB) > 126 MB L2, no flush" % (3 * (M * K + K * N) * 2 / 1e6),
+                   "parallelism": f"column shards x{world}, no collective" if world > 1 else "1 GPU"},
+        "clocks": clk.summary(), "gpu_launches": args.steps, "device_status": code,
+        "roofline": roofline, "e2e": e2e,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu:
+        result["cpu_baseline"] = cpu_baseline(M, N, K, args.cpu_seconds)
+    if rank == 0 and args.sweep and world == 1:
+        result["sweep"] = sweep(args)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+
+
+# ------------------------------------------------------------------------------------------------------ reference arm
+def run_reference(args):
+    """The reference's CPU GEMM path on the host cores, in bounded row samples of the same workload."""
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if rank != 0:
+        return
+    from oracle import oracle
+
+    M, N, K = WORKLOADS[args.workload]
+    threads = os.cpu_count() or 1
+    budget = 90.0  # seconds for warm-up + timed steps
+    per_step = budget / max(1, args.steps + args.warmup)
+    rows0 = min(M, threads)
+    A, B = oracle.judge_inputs(rows0, N, K)
+    t0 = time.perf_counter()
+    oracle.gemm_f64(A, B, threads=threads)
+    rate = rows0 / max(time.perf_counter() - t0, 1e-6)  # rows per second
+    rows = int(max(1, min(M, rate * per_step)))
+    A, B = oracle.judge_inputs(rows, N, K)
+    for _ in range(args.warmup):
+        oracle.gemm_f64(A, B, threads=threads)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        oracle.gemm_f64(A, B, threads=threads)
+    t = time.perf_counter() - t0
+    value = 2.0 * rows * N * K * args.steps / t / 1e12
+    sample = f"{rows} of {M} rows of {M}x{N}x{K} per step, fp64 i-k-j (oracle/oracle.c restating hopper/verif.cu:171-178)"
+    print(json.dumps({
+        "impl": "reference", "metric": "TFLOP/s of C = A.B (fp16 in, fp32 accumulate, fp16 out), BASELINE config 1",
+        "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": t / args.steps * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f64 accumulate of fp16 inputs", "data": "synthetic: the judge's fill",
+        "config": {"workload": f"{args.workload} {M}x{N}x{K}", "M": M, "N": N, "K": K},
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,159 @@
+"""Python view of the Blackwell rung's C ABI (include/bwgemm.h) over gemm-ladder_b200/lib/libbwgemm.so.
+
+The product is the native library; this module only binds it with ctypes for Python callers (tests, bench.py) and
+passes torch tensors' device pointers and torch's current CUDA stream.  There is no fallback: if the library is
+missing or the device is not an sm_100 GPU, calls raise.
+
+    import bwgemm
+    C = bwgemm.gemm(A, B)          # A (M x K), B (K x N) fp16 CUDA tensors, row-major; C (M x N) fp16
+"""
+import ctypes
+import os
+import re
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "lib", "libbwgemm.so")
+HEADER = os.path.join(os.path.dirname(HERE), "include", "bwgemm.h")
+
+BW_OK, BW_ERR_SHAPE, BW_ERR_LAUNCH, BW_ERR_TIMEOUT, BW_ERR_ARG, BW_ERR_DEVICE = 0, 1, 2, 3, 4, 5
+BW_KERNEL_TILE, BW_KERNEL_SWAP = 0, 1
+
+
+class Plan(ctypes.Structure):
+    _fields_ = [
+        ("kernel", ctypes.c_int),
+        ("bn", ctypes.c_int),
+        ("stages", ctypes.c_int),
+        ("tiles_m", ctypes.c_int),
+        ("tiles_n", ctypes.c_int),
+        ("tiles", ctypes.c_int),
+        ("kblocks", ctypes.c_int),
+        ("grid", ctypes.c_int),
+        ("dp_tiles", ctypes.c_int),
+        ("sk_iters", ctypes.c_longlong),
+        ("group_rows", ctypes.c_int),
+        ("workspace_bytes", ctypes.c_size_t),
+        ("counters", ctypes.c_int),
+        ("smem_bytes", ctypes.c_int),
+        ("tmem_cols", ctypes.c_int),
+    ]
+
+    def as_dict(self):
+        return {name: getattr(self, name) for name, _ in self._fields_}
+
+
+class BwError(RuntimeError):
+    def __init__(self, status, msg):
+        super().__init__(msg)
+        self.status = status
+
+
+_lib = None
+
+
+def lib():
+    """The loaded library (raises if it was not built: python gemm-ladder_b200/build.py)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(f"{LIB_PATH} is missing: build it with python gemm-ladder_b200/build.py")
+        L = ctypes.CDLL(LIB_PATH)
+        vp, i = ctypes.c_void_p, ctypes.c_int
+        L.bw_gemm_f16.argtypes = [vp, vp, vp, i, i, i, vp]
+        L.bw_gemm_f16.restype = i
+        L.bw_gemm_f16_variant.argtypes = [vp, vp, vp, i, i, i, vp, i]
+        L.bw_gemm_f16_variant.restype = i
+        L.bw_gemm_variant_count.argtypes = []
+        L.bw_gemm_variant_count.restype = i
+        L.bw_gemm_variant_name.argtypes = [i]
+        L.bw_gemm_variant_name.restype = ctypes.c_char_p
+        L.bw_gemm_dirty.argtypes = []
+        L.bw_gemm_dirty.restype = i
+        L.bw_gemm_plan.argtypes = [i, i, i, i, i, ctypes.POINTER(Plan)]
+        L.bw_gemm_plan.restype = i
+        u = ctypes.POINTER(ctypes.c_uint)
+        L.bw_gemm_status.argtypes = [ctypes.POINTER(ctypes.c_int), u, u, u]
+        L.bw_gemm_status.restype = i
+        L.bw_gemm_clear_status.argtypes = []
+        L.bw_gemm_clear_status.restype = i
+        L.bw_gemm_set_wait_limit_ns.argtypes = [ctypes.c_ulonglong]
+        L.bw_gemm_set_wait_limit_ns.restype = ctypes.c_ulonglong
+        L.bw_status_string.argtypes = [i]
+        L.bw_status_string.restype = ctypes.c_char_p
+        L.bw_last_error_string.argtypes = []
+        L.bw_last_error_string.restype = ctypes.c_char_p
+        _lib = L
+    return _lib
+
+
+def declared_symbols():
+    """The functions include/bwgemm.h declares."""
+    with open(HEADER) as f:
+        text = f.read()
+    return sorted(set(re.findall(r"^\s*(?:const\s+)?[\w\s\*]+?\b(bw_\w+)\s*\(", text, flags=re.M)))
+
+
+def check(status):
+    if status != BW_OK:
+        L = lib()
+        msg = L.bw_status_string(status).decode()
+        if status == BW_ERR_LAUNCH:
+            msg += ": " + L.bw_last_error_string().decode()
+        raise BwError(status, msg)
+
+
+def variants():
+    L = lib()
+    return [L.bw_gemm_variant_name(v).decode() for v in range(L.bw_gemm_variant_count())]
+
+
+def plan(M, N, K, sms=148, variant=0):
+    p = Plan()
+    check(lib().bw_gemm_plan(M, N, K, sms, variant, ctypes.byref(p)))
+    return p.as_dict()
+
+
+def gemm_ptr(a_ptr, b_ptr, c_ptr, M, N, K, stream_handle=0, variant=0):
+    """C = A B on raw device pointers (the C ABI as it is); returns the status code."""
+    return lib().bw_gemm_f16_variant(a_ptr, b_ptr, c_ptr, M, N, K, stream_handle, variant)
+
+
+def gemm(A, B, C=None, variant=0, stream=None):
+    """C = A B for fp16 CUDA tensors: A (M x K) and B (K x N) row-major (contiguous); C (M x N) is made if not given."""
+    import torch
+
+    M, K = A.shape
+    K2, N = B.shape
+    if K2 != K:
+        raise ValueError(f"A is {M} x {K} but B is {K2} x {N}")
+    for t in (A, B):
+        if t.dtype != torch.float16 or not t.is_cuda or not t.is_contiguous():
+            raise ValueError("A and B must be contiguous fp16 CUDA tensors")
+    if C is None:
+        C = torch.empty((M, N), dtype=torch.float16, device=A.device)
+    elif C.shape != (M, N) or C.dtype != torch.float16 or not C.is_contiguous():
+        raise ValueError("C must be a contiguous fp16 M x N tensor")
+    s = stream if stream is not None else torch.cuda.current_stream(A.device)
+    with torch.cuda.device(A.device):
+        check(gemm_ptr(A.data_ptr(), B.data_ptr(), C.data_ptr(), M, N, K, s.cuda_stream, variant))
+    return C
+
+
+def status():
+    """The device status word of the current device (after a synchronisation): (code, site, block, segment)."""
+    code = ctypes.c_int()
+    site, block, seg = ctypes.c_uint(), ctypes.c_uint(), ctypes.c_uint()
+    check(lib().bw_gemm_status(ctypes.byref(code), ctypes.byref(site), ctypes.byref(block), ctypes.byref(seg)))
+    return code.value, site.value, block.value, seg.value
+
+
+def clear_status():
+    check(lib().bw_gemm_clear_status())
+
+
+def dirty():
+    return lib().bw_gemm_dirty()
+
+
+def set_wait_limit_ns(ns):
+    return lib().bw_gemm_set_wait_limit_ns(ns)

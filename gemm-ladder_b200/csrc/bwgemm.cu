@@ -1,0 +1,299 @@
+// bwgemm.cu -- host side of the Blackwell rung: the C ABI of include/bwgemm.h over the sm_100a kernels of
+// gemm_kernel.cuh.  Per call: check the shape (the reference's rule, hopper/step7.cu:358-361), plan (plan.h), make
+// the TMA tensor maps (cuTensorMapEncodeTiled reached through the runtime, so that no library is linked, as
+// hopper/step2.cuh:168-196 does), keep a per-device workspace for stream-K partials (allocated at the first call that
+// needs more, never during a later call: judge/judge.cu:8-9), launch on the caller's stream.  No synchronisation.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+
+#include "bwgemm.h"
+#include "gemm_kernel.cuh"
+#include "plan.h"
+
+#ifndef BW_API
+#define BW_API extern "C" __attribute__((visibility("default")))
+#endif
+
+namespace bw {
+namespace {
+
+thread_local char g_errbuf[256] = "";
+
+int cuda_fail(cudaError_t e, const char* what)
+{
+    snprintf(g_errbuf, sizeof g_errbuf, "%s: %s", what, cudaGetErrorString(e));
+    return BW_ERR_LAUNCH;
+}
+
+typedef CUresult (*EncodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiled encoder()
+{
+    static EncodeTiled fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiled>(p);
+    });
+    return fn;
+}
+
+// A row-major fp16 matrix of rows x cols, boxes of box_cols x box_rows, 128-byte swizzle, zeros outside the matrix.
+bool make_map(CUtensorMap* m, const void* base, uint64_t cols, uint64_t rows, uint32_t box_cols, uint32_t box_rows)
+{
+    EncodeTiled enc = encoder();
+    if (!enc) return false;
+    const cuuint64_t dims[2] = {cols, rows};
+    const cuuint64_t strides[1] = {cols * 2};
+    const cuuint32_t box[2] = {box_cols, box_rows};
+    const cuuint32_t elem[2] = {1, 1};
+    return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, elem,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+struct DeviceState {
+    bool init = false;
+    bool supported = false;
+    int sms = 0;
+    float* work = nullptr;
+    size_t work_bytes = 0;
+    int* counters = nullptr;
+    int n_counters = 0;
+    unsigned attrs = 0;  // kernels whose shared-memory limit is set, one bit each
+};
+constexpr int kMaxDevices = 64;
+DeviceState g_dev[kMaxDevices];
+std::mutex g_mu;
+
+unsigned long long initial_wait_ns()
+{
+    const char* e = getenv("BWGEMM_WAIT_NS");
+    if (e) {
+        const unsigned long long v = strtoull(e, nullptr, 10);
+        if (v > 0) return v;
+    }
+    return 1000000000ull;  // 1 s
+}
+unsigned long long g_wait_ns = initial_wait_ns();
+
+int device_state(DeviceState** out)
+{
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+    if (dev < 0 || dev >= kMaxDevices) return BW_ERR_DEVICE;
+    DeviceState& d = g_dev[dev];
+    if (!d.init) {
+        int major = 0, minor = 0, sms = 0;
+        if ((e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev)) != cudaSuccess ||
+            (e = cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev)) != cudaSuccess ||
+            (e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess)
+            return cuda_fail(e, "cudaDeviceGetAttribute");
+        d.supported = major == 10 && minor == 0;
+        d.sms = sms;
+        d.init = true;
+    }
+    if (!d.supported) {
+        snprintf(g_errbuf, sizeof g_errbuf, "this library holds sm_100a code only");
+        return BW_ERR_DEVICE;
+    }
+    *out = &d;
+    return BW_OK;
+}
+
+// The workspace and counters a plan needs; grown (never shrunk) at the first call that needs more.
+int ensure_workspace(DeviceState& d, const bw_plan& q, cudaStream_t st)
+{
+    cudaError_t e;
+    if (q.workspace_bytes > d.work_bytes) {
+        if (d.work) cudaFree(d.work);
+        d.work = nullptr;
+        d.work_bytes = 0;
+        if ((e = cudaMalloc(&d.work, q.workspace_bytes)) != cudaSuccess) return cuda_fail(e, "cudaMalloc (workspace)");
+        d.work_bytes = q.workspace_bytes;
+    }
+    if (q.counters > d.n_counters) {
+        if (d.counters) cudaFree(d.counters);
+        d.counters = nullptr;
+        d.n_counters = 0;
+        const int n = q.counters < 1024 ? 1024 : q.counters;
+        if ((e = cudaMalloc(&d.counters, (size_t)n * sizeof(int))) != cudaSuccess)
+            return cuda_fail(e, "cudaMalloc (counters)");
+        if ((e = cudaMemsetAsync(d.counters, 0, (size_t)n * sizeof(int), st)) != cudaSuccess)
+            return cuda_fail(e, "cudaMemsetAsync (counters)");
+        d.n_counters = n;
+    }
+    return BW_OK;
+}
+
+template <int BN, bool SWAP>
+int launch_kernel(DeviceState& d, unsigned bit, const bw_plan& q, const CUtensorMap& mx, const CUtensorMap& my,
+                  const Params& p, cudaStream_t st)
+{
+    using G = Geom<BN, SWAP>;
+    if (q.smem_bytes != G::kSmemBytes || q.stages != G::kStages || q.tmem_cols != G::kTmemCols) {
+        snprintf(g_errbuf, sizeof g_errbuf, "plan and kernel geometry disagree (bn %d)", BN);
+        return BW_ERR_LAUNCH;
+    }
+    auto kernel = gemm_kernel<BN, SWAP>;
+    cudaError_t e;
+    if (!(d.attrs & bit)) {
+        if ((e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, G::kSmemBytes)) !=
+            cudaSuccess)
+            return cuda_fail(e, "cudaFuncSetAttribute");
+        d.attrs |= bit;
+    }
+    kernel<<<q.grid, kThreads, G::kSmemBytes, st>>>(mx, my, p);
+    if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail(e, "kernel launch");
+    return BW_OK;
+}
+
+int gemm(const void* A, const void* B, void* C, int M, int N, int K, cudaStream_t st, int variant)
+{
+    if (variant < 0 || variant >= kVariants) return BW_ERR_ARG;
+    if (!shape_ok(M, N, K)) return BW_ERR_SHAPE;
+    if (!A || !B || !C || (reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(B) |
+                           reinterpret_cast<uintptr_t>(C)) % 16)
+        return BW_ERR_ARG;
+    DeviceState* d = nullptr;
+    int rc = device_state(&d);
+    if (rc) return rc;
+    bw_plan q;
+    if ((rc = make_plan(M, N, K, d->sms, variant, &q))) return rc;
+    {
+        std::lock_guard<std::mutex> lock(g_mu);
+        if ((rc = ensure_workspace(*d, q, st))) return rc;
+    }
+    CUtensorMap mx, my;
+    bool ok;
+    if (q.kernel == BW_KERNEL_TILE)
+        ok = make_map(&mx, A, K, M, 64, 128) && make_map(&my, B, N, K, 64, 64);
+    else
+        ok = make_map(&mx, B, N, K, 64, 64) && make_map(&my, A, K, M, 64, q.bn);
+    if (!ok) {
+        snprintf(g_errbuf, sizeof g_errbuf, "cuTensorMapEncodeTiled failed");
+        return BW_ERR_LAUNCH;
+    }
+    Params p;
+    p.s.M = M;
+    p.s.N = N;
+    p.s.K = K;
+    p.s.tiles_m = q.tiles_m;
+    p.s.tiles_n = q.tiles_n;
+    p.s.tiles = q.tiles;
+    p.s.kblocks = q.kblocks;
+    p.s.dp_tiles = q.dp_tiles;
+    p.s.sk_iters = q.sk_iters;
+    p.s.group_rows = q.group_rows;
+    p.C = static_cast<__half*>(C);
+    p.work = d->work;
+    p.counters = d->counters;
+    p.wait_ns = g_wait_ns;
+    if (q.kernel == BW_KERNEL_TILE) return launch_kernel<256, false>(*d, 1u << 0, q, mx, my, p, st);
+    switch (q.bn) {
+    case 16: return launch_kernel<16, true>(*d, 1u << 1, q, mx, my, p, st);
+    case 32: return launch_kernel<32, true>(*d, 1u << 2, q, mx, my, p, st);
+    case 48: return launch_kernel<48, true>(*d, 1u << 3, q, mx, my, p, st);
+    case 64: return launch_kernel<64, true>(*d, 1u << 4, q, mx, my, p, st);
+    case 80: return launch_kernel<80, true>(*d, 1u << 5, q, mx, my, p, st);
+    case 96: return launch_kernel<96, true>(*d, 1u << 6, q, mx, my, p, st);
+    case 112: return launch_kernel<112, true>(*d, 1u << 7, q, mx, my, p, st);
+    case 128: return launch_kernel<128, true>(*d, 1u << 8, q, mx, my, p, st);
+    default: return BW_ERR_ARG;
+    }
+}
+
+}  // namespace
+}  // namespace bw
+
+// ------------------------------------------------------------------ the C ABI
+BW_API int bw_gemm_f16(const void* A, const void* B, void* C, int M, int N, int K, void* stream)
+{
+    return bw::gemm(A, B, C, M, N, K, static_cast<cudaStream_t>(stream), 0);
+}
+
+BW_API int bw_gemm_f16_variant(const void* A, const void* B, void* C, int M, int N, int K, void* stream, int variant)
+{
+    return bw::gemm(A, B, C, M, N, K, static_cast<cudaStream_t>(stream), variant);
+}
+
+BW_API int bw_gemm_variant_count(void) { return bw::kVariants; }
+
+BW_API const char* bw_gemm_variant_name(int v) { return bw::variant_name(v); }
+
+BW_API int bw_gemm_plan(int M, int N, int K, int sms, int variant, bw_plan* out)
+{
+    return bw::make_plan(M, N, K, sms, variant, out);
+}
+
+BW_API int bw_gemm_dirty(void)
+{
+    bw::DeviceState* d = nullptr;
+    if (bw::device_state(&d)) return -1;
+    std::lock_guard<std::mutex> lock(bw::g_mu);
+    if (!d->counters) return 0;
+    int* h = static_cast<int*>(malloc((size_t)d->n_counters * sizeof(int)));
+    if (!h) return -1;
+    int dirty = 0;
+    if (cudaMemcpy(h, d->counters, (size_t)d->n_counters * sizeof(int), cudaMemcpyDeviceToHost) == cudaSuccess) {
+        for (int i = 0; i < d->n_counters; ++i) dirty += h[i] != 0;
+    } else {
+        dirty = -1;
+    }
+    free(h);
+    return dirty;
+}
+
+BW_API int bw_gemm_status(int* code, unsigned* site, unsigned* block, unsigned* segment)
+{
+    unsigned s[4] = {0, 0, 0, 0};
+    cudaError_t e = cudaMemcpyFromSymbol(s, bw::g_status, sizeof s);
+    if (e != cudaSuccess) return bw::cuda_fail(e, "cudaMemcpyFromSymbol (status)");
+    if (code) *code = (int)s[0];
+    if (site) *site = s[1];
+    if (block) *block = s[2];
+    if (segment) *segment = s[3];
+    return BW_OK;
+}
+
+BW_API int bw_gemm_clear_status(void)
+{
+    const unsigned z[4] = {0, 0, 0, 0};
+    cudaError_t e = cudaMemcpyToSymbol(bw::g_status, z, sizeof z);
+    if (e != cudaSuccess) return bw::cuda_fail(e, "cudaMemcpyToSymbol (status)");
+    return BW_OK;
+}
+
+BW_API unsigned long long bw_gemm_set_wait_limit_ns(unsigned long long ns)
+{
+    const unsigned long long old = bw::g_wait_ns;
+    if (ns > 0) bw::g_wait_ns = ns;
+    return old;
+}
+
+BW_API const char* bw_status_string(int status)
+{
+    switch (status) {
+    case BW_OK: return "ok";
+    case BW_ERR_SHAPE: return "shape not supported (M % 16, N % 64 and K % 64 must be 0, all positive)";
+    case BW_ERR_LAUNCH: return "CUDA error (see bw_last_error_string)";
+    case BW_ERR_TIMEOUT: return "a bounded wait on a barrier gave up (see bw_gemm_status)";
+    case BW_ERR_ARG: return "bad argument (null or misaligned pointer, unknown variant)";
+    case BW_ERR_DEVICE: return "the current device is not an sm_100 GPU";
+    default: return "unknown status";
+    }
+}
+
+BW_API const char* bw_last_error_string(void) { return bw::g_errbuf; }

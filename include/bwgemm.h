@@ -1,0 +1,109 @@
+/*
+ * bwgemm.h -- the C ABI of the Blackwell (sm_100a) rung of gemm-ladder: C = A B, A (M x K) and B (K x N) fp16
+ * row-major, fp32 accumulation, C (M x N) fp16 row-major.
+ *
+ * Plain pointers and sizes only: device pointers for A, B and C, a cudaStream_t passed as void*.  The library is
+ * gemm-ladder_b200/lib/libbwgemm.so; gemm-ladder_b200/blackwell/candidate.cu wraps it in the reference's C++
+ * candidate interface so the reference's judge, probe and verif drive it unchanged.
+ *
+ * Each entry names the reference interface it replaces (paths inside the reference project).
+ */
+#ifndef BWGEMM_H
+#define BWGEMM_H
+
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes.  The reference prints and aborts on an unsupported shape (hopper/step7.cu:358-361); the C ABI returns
+ * a code instead and candidate.cu turns a non-zero code into that print-and-abort. */
+#define BW_OK 0
+#define BW_ERR_SHAPE 1     /* M, N, K not positive, or M % 16, N % 64, K % 64 not 0 (the reference's rule) */
+#define BW_ERR_LAUNCH 2    /* a CUDA call failed (the CUDA error string: bw_last_error_string) */
+#define BW_ERR_TIMEOUT 3   /* a kernel's bounded wait on a barrier gave up; see bw_gemm_status */
+#define BW_ERR_ARG 4       /* null or misaligned pointer, unknown variant */
+#define BW_ERR_DEVICE 5    /* the current device is not an sm_100 (B200-class) GPU */
+
+/* Kernels of the rule (bw_plan.kernel). */
+#define BW_KERNEL_TILE 0   /* 128 x bn tiles of C, A as the MMA's A operand */
+#define BW_KERNEL_SWAP 1   /* M <= 128: C^T = B^T A^T, 128 columns of B as the MMA's A operand, bn = M rounded to 16 */
+
+/*
+ * C = A B on `stream` (a cudaStream_t, 0 for the legacy default stream), with the current device.
+ * Replaces: void candidate_gemm(const half* A, const half* B, half* C, int M, int N, int K, cudaStream_t s)
+ *   (declared judge/judge.cu:73, probe/probe.cu:38, hopper/verif.cu:35; defined by each step, e.g.
+ *   hopper/step7.cu:355-374).
+ * Same rules as the reference's candidate (judge/judge.cu:5-10): asynchronous (no synchronisation), no allocation
+ * except at the first call of a larger shape (a workspace kept until exit), capturable in a CUDA graph, A and B not
+ * modified.  A, B and C 16-byte aligned.  Not for concurrent calls from several host threads on one device.
+ */
+int bw_gemm_f16(const void* A, const void* B, void* C, int M, int N, int K, void* stream);
+
+/*
+ * The same with a variant of the rule, for ablations (0 = the rule itself).
+ * Replaces: the weak `int g_var` read by candidate_gemm (probe/probe.cu:39, hopper/verif.cu:37, hopper/step7.cu:15).
+ */
+int bw_gemm_f16_variant(const void* A, const void* B, void* C, int M, int N, int K, void* stream, int variant);
+
+/* The number of variants.  Replaces: the weak `int g_nvar` (probe/probe.cu:40, hopper/verif.cu:38, hopper/step7.cu:16). */
+int bw_gemm_variant_count(void);
+
+/* A one-line description of variant v (NULL if v is out of range).  Replaces: the variant list in the header comment
+ * of each step (hopper/step7.cu:1-11). */
+const char* bw_gemm_variant_name(int v);
+
+/*
+ * Words of the rung's state across calls left non-zero (the stream-K tile counters), after the caller has
+ * synchronised.  0 means the state is back as the call found it.
+ * Replaces: the weak `int candidate_dirty()` (hopper/verif.cu:41, :216-222; ampere/step7.cu:277-292).
+ */
+int bw_gemm_dirty(void);
+
+/* The plan of one call: the kernel, its tile and its schedule (host only, no GPU needed). */
+typedef struct bw_plan {
+    int kernel;          /* BW_KERNEL_TILE or BW_KERNEL_SWAP */
+    int bn;              /* MMA N: the tile's columns (TILE) or the tokens rounded up to 16 (SWAP) */
+    int stages;          /* shared-memory stages of the TMA ring */
+    int tiles_m, tiles_n, tiles;
+    int kblocks;         /* K / 64 */
+    int grid;            /* persistent blocks, one per SM at most */
+    int dp_tiles;        /* tiles done whole, round-robin over the blocks */
+    long long sk_iters;  /* K-blocks of the other tiles, split evenly over the blocks (stream-K) */
+    int group_rows;      /* rows of tiles per serpentine group (0: row after row) */
+    size_t workspace_bytes; /* fp32 stream-K partials */
+    int counters;        /* stream-K tile counters */
+    int smem_bytes;      /* dynamic shared memory per block */
+    int tmem_cols;       /* tensor-memory columns per block */
+} bw_plan;
+
+/*
+ * The rule: which kernel, tile and schedule a call at M x N x K takes on a GPU of `sms` SMs, for variant `variant`.
+ * Replaces: step7::choose / step6::choose / rows7c (hopper/step7.cuh:921-949, hopper/step6.cuh:468-488).
+ */
+int bw_gemm_plan(int M, int N, int K, int sms, int variant, bw_plan* out);
+
+/*
+ * The device status word of the current device, after the caller has synchronised: *code = 0, or BW_ERR_TIMEOUT if
+ * a bounded wait gave up since the last clear; *site = role << 16 | barrier kind << 8 | index of the first wait that
+ * gave up, *block its block, *segment the segment that block was on.  Returns a CUDA error as BW_ERR_LAUNCH.
+ * No reference counterpart as a function: the reference traps in its guarded wait (hopper/step2.cuh:128-145); this
+ * rung's waits return instead and leave the context usable.
+ */
+int bw_gemm_status(int* code, unsigned* site, unsigned* block, unsigned* segment);
+int bw_gemm_clear_status(void);
+
+/* The limit of any single wait on a barrier, in nanoseconds (default 1 s; the BWGEMM_WAIT_NS environment variable
+ * sets it at load).  Returns the previous limit. */
+unsigned long long bw_gemm_set_wait_limit_ns(unsigned long long ns);
+
+/* Text of a status code, and of the last CUDA error met by the library on this thread. */
+const char* bw_status_string(int status);
+const char* bw_last_error_string(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* BWGEMM_H */

@@ -4,8 +4,9 @@
 #   _ref/emu_dump      the reference's Hopper host emulator (hopper/emu/emu.cpp, compiled where it lies) driven by
 #                      oracle/ref_emu_dump.cpp: dumps one reference kernel's inputs, fp64 reference and C (CPU only)
 #   _ref/verif_bw      the reference's own GPU check, hopper/verif.cu compiled where it lies, linked with this
-#                      repository's candidate (gemm-ladder_b200/blackwell/candidate.cu over libbwgemm.so): the
-#                      reference's 26 edge shapes, fp64 CPU reference and 8 bit-for-bit repeats, run on the B200
+#                      repository's candidate (gemm-ladder_b200/blackwell/candidate.cu, the whole rung in one
+#                      translation unit): the reference's 26 edge shapes, its fp64 CPU reference and its 8
+#                      bit-for-bit repeats of every variant, run on the B200
 #
 # Nothing here is built from a copy of the reference's sources, and nothing runs the reference's own build system.
 REF ?= /root/reference
@@ -27,9 +28,8 @@ $(OUT)/emu_dump: $(HERE)ref_emu_dump.cpp | $(OUT)
 	$(CXX) -std=c++17 -O2 -march=x86-64-v3 -w -I$(REF)/hopper/emu -I$(REF)/hopper -I$(REF)/hopper/emu/shim \
 	    $(HERE)ref_emu_dump.cpp -o $@
 
-$(OUT)/verif_bw: $(REF)/hopper/verif.cu $(PKG)/blackwell/candidate.cu $(PKG)/lib/libbwgemm.so | $(OUT)
+$(OUT)/verif_bw: $(REF)/hopper/verif.cu $(PKG)/blackwell/candidate.cu $(wildcard $(PKG)/csrc/*) | $(OUT)
 	$(NVCC) -std=c++17 -O2 -gencode arch=compute_100a,code=sm_100a -I$(ROOT)/include \
-	    $(REF)/hopper/verif.cu $(PKG)/blackwell/candidate.cu -o $@ \
-	    -L$(PKG)/lib -lbwgemm -Xlinker -rpath -Xlinker '$$ORIGIN/../../gemm-ladder_b200/lib' -lcublasLt
+	    $(REF)/hopper/verif.cu $(PKG)/blackwell/candidate.cu -o $@ -lcublasLt
 
 .PHONY: all emu_dump verif_bw

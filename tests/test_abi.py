@@ -1,0 +1,82 @@
+"""The C ABI on the CPU: the library loads, exports what include/bwgemm.h declares, rejects bad calls before touching
+a GPU, and plans as the rule says.  The candidate object carries the reference's C++ symbols."""
+import ctypes
+import os
+import shutil
+import subprocess
+
+import pytest
+
+import bwgemm
+from shapes import JUDGE_B200
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def test_library_exports_every_declared_symbol():
+    L = bwgemm.lib()
+    declared = bwgemm.declared_symbols()
+    assert len(declared) >= 11
+    for name in declared:
+        assert hasattr(L, name), f"{name} declared in include/bwgemm.h but not exported"
+
+
+def test_only_the_abi_is_exported():
+    out = subprocess.run(["nm", "-D", "--defined-only", bwgemm.LIB_PATH], capture_output=True, text=True).stdout
+    exported = {l.split()[-1] for l in out.splitlines() if " T " in l}
+    assert exported == set(bwgemm.declared_symbols())
+
+
+def test_status_strings_and_variants():
+    L = bwgemm.lib()
+    for st in range(6):
+        assert L.bw_status_string(st)
+    assert L.bw_gemm_variant_count() == len(bwgemm.variants()) >= 5
+    assert L.bw_gemm_variant_name(-1) is None
+    assert L.bw_gemm_variant_name(L.bw_gemm_variant_count()) is None
+
+
+@pytest.mark.parametrize("shape", [(0, 64, 64), (15, 64, 64), (16, 32, 64), (16, 64, 32), (16, 64, -64), (-16, 64, 64)])
+def test_bad_shape_is_refused_without_a_gpu(shape):
+    M, N, K = shape
+    assert bwgemm.gemm_ptr(16, 16, 16, M, N, K) == bwgemm.BW_ERR_SHAPE
+
+
+def test_bad_pointers_and_variant_are_refused_without_a_gpu():
+    assert bwgemm.gemm_ptr(0, 256, 512, 16, 64, 64) == bwgemm.BW_ERR_ARG
+    assert bwgemm.gemm_ptr(256, 256, 8, 16, 64, 64) == bwgemm.BW_ERR_ARG  # misaligned C
+    assert bwgemm.gemm_ptr(256, 256, 512, 16, 64, 64, variant=99) == bwgemm.BW_ERR_ARG
+
+
+def test_plan_rule_on_the_judge_shapes():
+    for name, M, N, K in JUDGE_B200:
+        p = bwgemm.plan(M, N, K, sms=148)
+        if M <= 128:
+            assert p["kernel"] == bwgemm.BW_KERNEL_SWAP and p["bn"] == M and p["dp_tiles"] == 0
+            assert p["grid"] == 148 and p["sk_iters"] == p["tiles"] * (K // 64)
+        else:
+            assert p["kernel"] == bwgemm.BW_KERNEL_TILE and p["bn"] == 256
+            assert p["tiles"] == -(-M // 128) * -(-N // 256)
+        assert p["smem_bytes"] <= 227 * 1024 and p["tmem_cols"] <= 512 and p["stages"] >= 4
+        assert p["sk_iters"] == 0 or p["sk_iters"] >= p["grid"]
+
+
+def test_plan_variants_take_out_one_mechanism():
+    assert bwgemm.plan(16, 8192, 8192, variant=1)["sk_iters"] == 0          # no stream-K
+    assert bwgemm.plan(16, 8192, 8192, variant=2)["kernel"] == bwgemm.BW_KERNEL_TILE  # no swap-AB
+    assert bwgemm.plan(8192, 8192, 8192, variant=3)["group_rows"] == 0      # row order
+    assert bwgemm.plan(8192, 8192, 8192, variant=4)["dp_tiles"] == 0        # stream-K everywhere
+    with pytest.raises(bwgemm.BwError):
+        bwgemm.plan(16, 64, 64, variant=5)
+
+
+@pytest.mark.skipif(shutil.which("nvcc") is None, reason="nvcc")
+def test_candidate_object_has_the_reference_symbols(tmp_path):
+    obj = str(tmp_path / "candidate.o")
+    subprocess.check_call(["nvcc", "-std=c++17", "-O1", "-gencode", "arch=compute_100a,code=sm_100a",
+                           f"-I{os.path.join(ROOT, 'include')}",
+                           "-c", os.path.join(ROOT, "gemm-ladder_b200", "blackwell", "candidate.cu"), "-o", obj])
+    syms = subprocess.run(["nm", obj], capture_output=True, text=True).stdout
+    # judge/modal_judge.py:73 keeps exactly this symbol global
+    assert " T _Z14candidate_gemmPK6__halfS1_PS_iiiP11CUstream_st" in syms
+    assert " D g_nvar" in syms and " B g_var" in syms and " T _Z15candidate_dirtyv" in syms
