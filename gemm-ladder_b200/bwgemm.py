@@ -16,7 +16,7 @@ LIB_PATH = os.path.join(HERE, "lib", "libbwgemm.so")
 HEADER = os.path.join(os.path.dirname(HERE), "include", "bwgemm.h")
 
 BW_OK, BW_ERR_SHAPE, BW_ERR_LAUNCH, BW_ERR_TIMEOUT, BW_ERR_ARG, BW_ERR_DEVICE = 0, 1, 2, 3, 4, 5
-BW_KERNEL_TILE, BW_KERNEL_SWAP = 0, 1
+BW_KERNEL_TILE, BW_KERNEL_SWAP, BW_KERNEL_PAIR = 0, 1, 2
 
 
 class Plan(ctypes.Structure):
@@ -30,6 +30,8 @@ class Plan(ctypes.Structure):
         ("kblocks", ctypes.c_int),
         ("grid", ctypes.c_int),
         ("dp_tiles", ctypes.c_int),
+        ("sk_tiles", ctypes.c_int),
+        ("splits", ctypes.c_int),
         ("sk_iters", ctypes.c_longlong),
         ("group_rows", ctypes.c_int),
         ("workspace_bytes", ctypes.c_size_t),

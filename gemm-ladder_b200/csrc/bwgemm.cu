@@ -1,8 +1,9 @@
 // bwgemm.cu -- host side of the Blackwell rung: the C ABI of include/bwgemm.h over the sm_100a kernels of
 // gemm_kernel.cuh.  Per call: check the shape (the reference's rule, hopper/step7.cu:358-361), plan (plan.h), make
 // the TMA tensor maps (cuTensorMapEncodeTiled reached through the runtime, so that no library is linked, as
-// hopper/step2.cuh:168-196 does), keep a per-device workspace for stream-K partials (allocated at the first call that
-// needs more, never during a later call: judge/judge.cu:8-9), launch on the caller's stream.  No synchronisation.
+// hopper/step2.cuh:168-196 does), keep a per-device workspace for the partials of split tiles (allocated at the first
+// call that needs more, never during a later call: judge/judge.cu:8-9), launch on the caller's stream (a cluster of
+// two blocks for the pair kernel).  No synchronisation.
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -72,6 +73,7 @@ struct DeviceState {
     int* counters = nullptr;
     int n_counters = 0;
     unsigned attrs = 0;  // kernels whose shared-memory limit is set, one bit each
+    int pairs = -1;      // pairs of SMs the pair kernel holds at once (its cluster occupancy); -1: not asked yet
 };
 constexpr int kMaxDevices = 64;
 DeviceState g_dev[kMaxDevices];
@@ -138,25 +140,67 @@ int ensure_workspace(DeviceState& d, const bw_plan& q, cudaStream_t st)
     return BW_OK;
 }
 
-template <int BN, bool SWAP>
+template <int BN, bool SWAP, bool PAIR>
+cudaLaunchConfig_t launch_config(int grid, cudaStream_t st, cudaLaunchAttribute* attr)
+{
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = Geom<BN, SWAP, PAIR>::kSmemBytes;
+    cfg.stream = st;
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = PAIR ? 2 : 1;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = PAIR ? 1 : 0;
+    return cfg;
+}
+
+template <int BN, bool SWAP, bool PAIR>
+int set_smem_limit(DeviceState& d, unsigned bit)
+{
+    if (d.attrs & bit) return BW_OK;
+    cudaError_t e = cudaFuncSetAttribute(gemm_kernel<BN, SWAP, PAIR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         Geom<BN, SWAP, PAIR>::kSmemBytes);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
+    d.attrs |= bit;
+    return BW_OK;
+}
+
+constexpr unsigned kBitPair = 1u << 9;
+
+// The pairs of SMs the pair kernel can hold at once, asked once per device (a cluster may not straddle GPCs, so this
+// can be below sms / 2).
+int pair_occupancy(DeviceState& d)
+{
+    if (d.pairs >= 0) return BW_OK;
+    int rc = set_smem_limit<256, false, true>(d, kBitPair);
+    if (rc) return rc;
+    cudaLaunchAttribute attr[1];
+    const cudaLaunchConfig_t cfg = launch_config<256, false, true>(2, 0, attr);
+    int n = 0;
+    cudaError_t e = cudaOccupancyMaxActiveClusters(&n, gemm_kernel<256, false, true>, &cfg);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveClusters");
+    d.pairs = n;
+    return BW_OK;
+}
+
+template <int BN, bool SWAP, bool PAIR>
 int launch_kernel(DeviceState& d, unsigned bit, const bw_plan& q, const CUtensorMap& mx, const CUtensorMap& my,
                   const Params& p, cudaStream_t st)
 {
-    using G = Geom<BN, SWAP>;
+    using G = Geom<BN, SWAP, PAIR>;
     if (q.smem_bytes != G::kSmemBytes || q.stages != G::kStages || q.tmem_cols != G::kTmemCols) {
         snprintf(g_errbuf, sizeof g_errbuf, "plan and kernel geometry disagree (bn %d)", BN);
         return BW_ERR_LAUNCH;
     }
-    auto kernel = gemm_kernel<BN, SWAP>;
-    cudaError_t e;
-    if (!(d.attrs & bit)) {
-        if ((e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, G::kSmemBytes)) !=
-            cudaSuccess)
-            return cuda_fail(e, "cudaFuncSetAttribute");
-        d.attrs |= bit;
-    }
-    kernel<<<q.grid, kThreads, G::kSmemBytes, st>>>(mx, my, p);
-    if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail(e, "kernel launch");
+    int rc = set_smem_limit<BN, SWAP, PAIR>(d, bit);
+    if (rc) return rc;
+    cudaLaunchAttribute attr[1];
+    const cudaLaunchConfig_t cfg = launch_config<BN, SWAP, PAIR>(q.grid, st, attr);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_kernel<BN, SWAP, PAIR>, mx, my, p);
+    if (e != cudaSuccess) return cuda_fail(e, "kernel launch");
     return BW_OK;
 }
 
@@ -171,14 +215,15 @@ int gemm(const void* A, const void* B, void* C, int M, int N, int K, cudaStream_
     int rc = device_state(&d);
     if (rc) return rc;
     bw_plan q;
-    if ((rc = make_plan(M, N, K, d->sms, variant, &q))) return rc;
     {
         std::lock_guard<std::mutex> lock(g_mu);
+        if ((rc = pair_occupancy(*d))) return rc;
+        if ((rc = make_plan(M, N, K, d->sms, d->pairs, variant, &q))) return rc;
         if ((rc = ensure_workspace(*d, q, st))) return rc;
     }
     CUtensorMap mx, my;
     bool ok;
-    if (q.kernel == BW_KERNEL_TILE)
+    if (q.kernel == BW_KERNEL_TILE || q.kernel == BW_KERNEL_PAIR)
         ok = make_map(&mx, A, K, M, 64, 128) && make_map(&my, B, N, K, 64, 64);
     else
         ok = make_map(&mx, B, N, K, 64, 64) && make_map(&my, A, K, M, 64, q.bn);
@@ -195,22 +240,25 @@ int gemm(const void* A, const void* B, void* C, int M, int N, int K, cudaStream_
     p.s.tiles = q.tiles;
     p.s.kblocks = q.kblocks;
     p.s.dp_tiles = q.dp_tiles;
+    p.s.sk_tiles = q.sk_tiles;
+    p.s.splits = q.splits;
     p.s.sk_iters = q.sk_iters;
     p.s.group_rows = q.group_rows;
     p.C = static_cast<__half*>(C);
     p.work = d->work;
     p.counters = d->counters;
     p.wait_ns = g_wait_ns;
-    if (q.kernel == BW_KERNEL_TILE) return launch_kernel<256, false>(*d, 1u << 0, q, mx, my, p, st);
+    if (q.kernel == BW_KERNEL_PAIR) return launch_kernel<256, false, true>(*d, kBitPair, q, mx, my, p, st);
+    if (q.kernel == BW_KERNEL_TILE) return launch_kernel<256, false, false>(*d, 1u << 0, q, mx, my, p, st);
     switch (q.bn) {
-    case 16: return launch_kernel<16, true>(*d, 1u << 1, q, mx, my, p, st);
-    case 32: return launch_kernel<32, true>(*d, 1u << 2, q, mx, my, p, st);
-    case 48: return launch_kernel<48, true>(*d, 1u << 3, q, mx, my, p, st);
-    case 64: return launch_kernel<64, true>(*d, 1u << 4, q, mx, my, p, st);
-    case 80: return launch_kernel<80, true>(*d, 1u << 5, q, mx, my, p, st);
-    case 96: return launch_kernel<96, true>(*d, 1u << 6, q, mx, my, p, st);
-    case 112: return launch_kernel<112, true>(*d, 1u << 7, q, mx, my, p, st);
-    case 128: return launch_kernel<128, true>(*d, 1u << 8, q, mx, my, p, st);
+    case 16: return launch_kernel<16, true, false>(*d, 1u << 1, q, mx, my, p, st);
+    case 32: return launch_kernel<32, true, false>(*d, 1u << 2, q, mx, my, p, st);
+    case 48: return launch_kernel<48, true, false>(*d, 1u << 3, q, mx, my, p, st);
+    case 64: return launch_kernel<64, true, false>(*d, 1u << 4, q, mx, my, p, st);
+    case 80: return launch_kernel<80, true, false>(*d, 1u << 5, q, mx, my, p, st);
+    case 96: return launch_kernel<96, true, false>(*d, 1u << 6, q, mx, my, p, st);
+    case 112: return launch_kernel<112, true, false>(*d, 1u << 7, q, mx, my, p, st);
+    case 128: return launch_kernel<128, true, false>(*d, 1u << 8, q, mx, my, p, st);
     default: return BW_ERR_ARG;
     }
 }
@@ -235,7 +283,7 @@ BW_API const char* bw_gemm_variant_name(int v) { return bw::variant_name(v); }
 
 BW_API int bw_gemm_plan(int M, int N, int K, int sms, int variant, bw_plan* out)
 {
-    return bw::make_plan(M, N, K, sms, variant, out);
+    return bw::make_plan(M, N, K, sms, sms / 2, variant, out);
 }
 
 BW_API int bw_gemm_dirty(void)

@@ -1,27 +1,29 @@
 // gemm_kernel.cuh -- the rung's sm_100a GEMM kernel: C = A B, A (M x K) and B (K x N) fp16 row-major, fp32
 // accumulation in tensor memory, C (M x N) fp16 row-major (the judge's convention, judge/judge.cu:5-7).
 //
-// One persistent block per SM, 6 warps with fixed roles:
-//   warp 0      TMA producer: fills a ring of STAGES shared-memory stages (full / empty mbarriers).
-//   warp 1      allocates tensor memory, then one thread issues tcgen05.mma (128 x BN x 16 per instruction) into one
-//               of two accumulators and commits each stage back to the producer and each finished tile to the
-//               epilogue.
+// One persistent block per SM (PAIR: one block pair per two SMs), 6 warps with fixed roles:
+//   warp 0      TMA producer: fills a ring of shared-memory stages (full / empty mbarriers).
+//   warp 1      allocates tensor memory; one thread issues tcgen05.mma into one of two accumulators and commits
+//               each stage back to the producer and each finished segment to the epilogue.
 //   warps 2-5   epilogue: tcgen05.ld of the accumulator (warp w reads TMEM lanes 32 (w % 4) .. +31), fp32 -> fp16
 //               round-to-nearest, stores to C; the accumulator is released as soon as it is read, so the next tile's
 //               MMA overlaps this tile's stores.
 //
-// Two operand forms (the reference's tiles and transposed bands, hopper/step7.cuh:429-631 and :671-910):
-//   SWAP = false  MMA-A = a 128-row tile of A (K-major), MMA-B = a BN-column tile of B (MN-major: B is K x N with N
-//                 contiguous).  TMEM lane = row of C, TMEM column = column of C.
-//   SWAP = true   for M <= 128: C^T = B^T A^T.  MMA-A = 128 columns of B (MN-major), MMA-B = the M rows of A (K-major,
-//                 BN = M rounded up to 16).  TMEM lane = column of C, TMEM column = row of C.  The weights fill the
-//                 128-row MMA dimension whatever the number of tokens.
+// Three operand forms (the reference's tiles and transposed bands, hopper/step7.cuh:429-631 and :671-910):
+//   TILE  (SWAP = false, PAIR = false)  MMA 128 x BN x 16: A = a 128-row tile of A (K-major), B = a BN-column tile of
+//         B (MN-major: B is K x N with N contiguous).  TMEM lane = row of C, TMEM column = column of C.
+//   PAIR  (SWAP = false, PAIR = true)   MMA 256 x BN x 16 on a cluster of two blocks (cta_group::2): each block loads
+//         its own 128 rows of A and BN / 2 columns of B, the leader block issues the MMA that reads both blocks'
+//         shared memory, each block's tensor memory holds its 128 rows x BN.  Per SM the operand traffic of a
+//         256 x 256 tile is that of a 128 x 128 tile.
+//   SWAP  (SWAP = true)   for M <= 128: C^T = B^T A^T.  MMA-A = 128 columns of B (MN-major), MMA-B = the M rows of A
+//         (K-major, BN = M rounded up to 16).  TMEM lane = column of C, TMEM column = row of C.  The weights fill the
+//         128-row MMA dimension whatever the number of tokens.
 //
-// Work: tiles in the serpentine order of hopper/step5.cuh:149-163 (groups of rows of tiles, column after column, odd
-// groups backwards).  The first dp_tiles tiles go round-robin to the blocks (data-parallel); the K-blocks of the other
-// tiles are split evenly over the blocks (stream-K).  A block whose share covers a tile only in part writes an fp32
-// partial to its workspace slot; the last block to finish a tile (a counter per tile) sums the tile's partials in
-// block order -- a fixed order, so results are bit-for-bit repeatable -- writes C and puts the counter back to zero.
+// Work (schedule.h): data-parallel whole tiles in serpentine order, then split-K or stream-K segments; a tile split
+// over several blocks is summed by the last of them in a fixed order, so results are bit-for-bit repeatable.
+// Every wait on a barrier is bounded (ptx.cuh, wait_bounded): a stalled pipeline ends the kernel with an error status
+// instead of hanging the GPU.
 #pragma once
 #include <cuda.h>
 #include <cuda_fp16.h>
@@ -37,17 +39,19 @@ constexpr int kBK = 64;          // K per stage: one 128-byte swizzle row of fp1
 struct Params {
     Sched s;
     __half* C;
-    float* work;               // 2 * gridDim.x slots of 128 * BN floats (stream-K partials)
-    int* counters;             // one per stream-K tile, zero between calls
+    float* work;                 // the partials: workspace_slots() x (PAIR ? 2 : 1) slots of 128 x BN fp32, row-major
+    int* counters;               // one per split tile (per block of the pair), zero between calls
     unsigned long long wait_ns;  // the limit of any single wait on a barrier
 };
 
 __host__ __device__ constexpr int pow2_at_least(int v, int p) { return p >= v ? p : pow2_at_least(v, 2 * p); }
 
-template <int BN, bool SWAP>
+template <int BN, bool SWAP, bool PAIR>
 struct Geom {
-    static constexpr int kXBytes = 128 * kBK * 2;  // MMA-A operand tile: 128 rows x 64 K
-    static constexpr int kYBytes = BN * kBK * 2;   // MMA-B operand tile: BN rows x 64 K
+    static constexpr int kRanks = PAIR ? 2 : 1;
+    static constexpr int kTileM = PAIR ? 256 : 128;          // rows of C per tile (TILE, PAIR)
+    static constexpr int kXBytes = 128 * kBK * 2;            // this block's MMA-A operand: 128 rows x 64 K
+    static constexpr int kYBytes = (BN / kRanks) * kBK * 2;  // this block's MMA-B operand: BN (PAIR: BN / 2) x 64 K
     static constexpr int kStageBytes = kXBytes + kYBytes;
     static constexpr int kStages = (204800 / kStageBytes) < 12 ? (204800 / kStageBytes) : 12;
     static constexpr int kTmemCols = pow2_at_least(2 * BN < 32 ? 32 : 2 * BN, 32);  // two accumulators
@@ -55,8 +59,9 @@ struct Geom {
     static constexpr int kNumBars = 2 * kStages + 5;  // full, empty, tmem full x2, tmem empty x2, drain
     static constexpr int kMiscOffset = kBarOffset + kNumBars * 8;
     static constexpr int kSmemBytes = 1024 + kMiscOffset + 32;  // + slack to align the stages to 1024 bytes
-    static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "MMA N: a multiple of 16 in [16, 256] at M = 128");
-    static_assert(SWAP || BN % 64 == 0, "B tiles are boxes of 64 columns");
+    static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "MMA N: a multiple of 16 in [16, 256]");
+    static_assert(SWAP || BN % (64 * kRanks) == 0, "B tiles are boxes of 64 columns (per block)");
+    static_assert(!(SWAP && PAIR), "the swap-AB form runs on single blocks");
     static_assert(kYBytes % 1024 == 0 && kXBytes % 1024 == 0, "operand tiles on 1024-byte swizzle atoms");
     static_assert(kStages >= 2 && kSmemBytes <= 227 * 1024, "shared memory");
     static_assert(kTmemCols <= 512, "tensor memory");
@@ -84,12 +89,12 @@ __device__ __forceinline__ uint64_t desc_mnmajor(uint32_t tile, int k) { return 
 // ------------------------------------------------------------------ the epilogue's stores
 // 16 accumulator columns of TMEM lane `lane` (v) -> C.  Not swapped: C[m0 + lane][n0 + c0 .. +15], two 16-byte stores.
 // Swapped: C[c0 + j][n0 + lane] for j < 16, one fp16 each (a warp writes 64 contiguous bytes per row of C).
-template <int BN, bool SWAP>
-__device__ __forceinline__ void store_chunk(const Params& p, int tm, int tn, int lane, int c0, const float (&v)[16])
+template <bool SWAP>
+__device__ __forceinline__ void store_chunk(const Params& p, int m0, int n0, int lane, int c0, const float (&v)[16])
 {
     const Sched& s = p.s;
     if (!SWAP) {
-        const int m = tm * 128 + lane, n = tn * BN + c0;
+        const int m = m0 + lane, n = n0 + c0;
         if (m >= s.M || n >= s.N) return;
         uint32_t h[8];
 #pragma unroll
@@ -101,7 +106,7 @@ __device__ __forceinline__ void store_chunk(const Params& p, int tm, int tn, int
         dst[0] = make_uint4(h[0], h[1], h[2], h[3]);
         dst[1] = make_uint4(h[4], h[5], h[6], h[7]);
     } else {
-        const int n = tn * 128 + lane;
+        const int n = n0 + lane;
         if (n >= s.N) return;
         __half* col = p.C + n;
 #pragma unroll
@@ -112,13 +117,72 @@ __device__ __forceinline__ void store_chunk(const Params& p, int tm, int tn, int
     }
 }
 
+// ------------------------------------------------------------------ the partials of a split tile
+// Slot layout: 128 rows x BN columns of fp32, row-major: TMEM lane `row`'s 16 columns are 64 contiguous bytes.
+// A block of a pair keeps its half in slot 2 s + rank.
+template <int BN>
+__device__ __forceinline__ float* slot_ptr(const Params& p, long long slot, int row, int c0)
+{
+    return p.work + ((size_t)slot * 128 + row) * BN + c0;
+}
+
+// Sums the tile's nseg partials in their fixed order (partial f.mine from `own` when own_mine, from its slot
+// otherwise) for 16 columns of one row, loading up to four partials at once.
+template <int BN, int RANKS>
+__device__ __forceinline__ void sum_partials(const Params& p, int P, int tile, int rank, const Fixup& f, bool own_mine,
+                                             const float (&own)[16], int row, int c0, float (&v)[16])
+{
+    const Sched& s = p.s;
+#pragma unroll 1
+    for (int i0 = 0; i0 < f.nseg; i0 += 4) {
+        float4 buf[4][4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int i = i0 + j;
+            if (i < f.nseg && !(own_mine && i == f.mine)) {
+                const long long slot = (long long)fixup_slot(s, P, tile, f, i) * RANKS + rank;
+                const float4* src = reinterpret_cast<const float4*>(slot_ptr<BN>(p, slot, row, c0));
+#pragma unroll
+                for (int q = 0; q < 4; ++q) buf[j][q] = __ldcg(src + q);
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int i = i0 + j;
+            if (i < f.nseg) {
+                float x[16];
+                if (own_mine && i == f.mine) {
+#pragma unroll
+                    for (int q = 0; q < 16; ++q) x[q] = own[q];
+                } else {
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        x[4 * q] = buf[j][q].x;
+                        x[4 * q + 1] = buf[j][q].y;
+                        x[4 * q + 2] = buf[j][q].z;
+                        x[4 * q + 3] = buf[j][q].w;
+                    }
+                }
+                if (i == 0) {
+#pragma unroll
+                    for (int q = 0; q < 16; ++q) v[q] = x[q];
+                } else {
+#pragma unroll
+                    for (int q = 0; q < 16; ++q) v[q] += x[q];
+                }
+            }
+        }
+    }
+}
+
 // ------------------------------------------------------------------ the kernel
-template <int BN, bool SWAP>
+template <int BN, bool SWAP, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmy, const Params p)
 {
-    using G = Geom<BN, SWAP>;
+    using G = Geom<BN, SWAP, PAIR>;
     constexpr int S = G::kStages;
+    constexpr int R = G::kRanks;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + G::kBarOffset);
@@ -133,16 +197,18 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const Sched& s = p.s;
-    const int P = gridDim.x, c = blockIdx.x;
+    const int rank = PAIR ? (int)cluster_ctarank() : 0;
+    const bool leader = rank == 0;
+    const int P = gridDim.x / R, c = blockIdx.x / R;  // the two blocks of a pair share their segments
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < S; ++i) {
-            mbar_init(&full[i], 1);   // the producer's arrive.expect_tx; the TMA bytes complete it
+            mbar_init(&full[i], 1);   // the (leader's) producer's arrive.expect_tx; the TMA bytes complete it
             mbar_init(&empty[i], 1);  // one tcgen05.commit
         }
         for (int i = 0; i < 2; ++i) {
-            mbar_init(&tfull[i], 1);     // one tcgen05.commit at the end of a segment
-            mbar_init(&tempty[i], 128);  // every epilogue thread, once its loads of the accumulator are done
+            mbar_init(&tfull[i], 1);       // one tcgen05.commit at the end of a segment
+            mbar_init(&tempty[i], 4 * R);  // one arrival per epilogue warp (of both blocks of a pair)
         }
         mbar_init(drain, 1);
         *abort_flag = 0;
@@ -155,47 +221,67 @@ __global__ void __launch_bounds__(kThreads, 1)
         prefetch_tmap(&tmy);
     }
     if (warp == 1) {
-        tmem_alloc(tmem_slot, G::kTmemCols);
-        tmem_relinquish();
+        if (PAIR) {
+            tmem_alloc_pair(tmem_slot, G::kTmemCols);
+            tmem_relinquish_pair();
+        } else {
+            tmem_alloc(tmem_slot, G::kTmemCols);
+            tmem_relinquish();
+        }
     }
+    __syncwarp();
     tc_fence_before();
-    __syncthreads();
+    if (PAIR)
+        cluster_sync();  // the leader's barriers exist before the other block's loads and arrivals reach them
+    else
+        __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
 
     if (warp == 0) {
-        // ---------------------------------------------------------- TMA producer (one thread)
+        // ---------------------------------------------------------- TMA producer (one thread per block)
         if (lane == 0) {
             SegIter it(s, c, P);
-            int stage = 0, issued = 0, seg = 0, tile, k0, k1;
+            Seg sg;
+            int stage = 0, issued = 0, seg = 0;
             uint32_t ph = 0;
             bool ok = true;
-            while (ok && it.next(s, P, tile, k0, k1)) {
+            while (ok && it.next(s, P, sg)) {
                 int tm, tn;
                 if (SWAP) {
                     tm = 0;
-                    tn = tile;
+                    tn = sg.tile;
                 } else {
-                    tile_coords(s, tile, tm, tn);
+                    tile_coords(s, sg.tile, tm, tn);
                 }
-                for (int kb = k0; kb < k1; ++kb) {
+                for (int kb = sg.k0; kb < sg.k1; ++kb) {
                     if (!wait_bounded(&empty[stage], ph ^ 1u, abort_flag, p.wait_ns, site(0, 1, stage), seg)) {
                         ok = false;
                         break;
                     }
                     uint8_t* sx = smem + stage * G::kStageBytes;
                     uint8_t* sy = sx + G::kXBytes;
-                    mbar_arrive_expect_tx(&full[stage], G::kStageBytes);
-                    if (!SWAP) {
-                        tma_load_2d(sx, &tmx, kb * kBK, tm * 128, &full[stage]);  // A: 64 K x 128 rows
+                    if (PAIR) {
+                        // both blocks' halves complete on the leader's barrier, which expects them all
+                        const uint32_t bar = mapa_shared(smem_u32(&full[stage]), 0);
+                        if (leader) mbar_arrive_expect_tx(&full[stage], 2 * G::kStageBytes);
+                        tma_load_2d_pair(sx, &tmx, kb * kBK, tm * 256 + rank * 128, bar);  // A: 64 K x 128 rows
 #pragma unroll
-                        for (int j = 0; j < BN / 64; ++j)  // B: 64 columns x 64 K per box
-                            tma_load_2d(sy + j * 8192, &tmy, tn * BN + 64 * j, kb * kBK, &full[stage]);
+                        for (int j = 0; j < BN / 128; ++j)  // B: this block's BN / 2 columns, boxes of 64 x 64 K
+                            tma_load_2d_pair(sy + j * 8192, &tmy, tn * BN + rank * (BN / 2) + 64 * j, kb * kBK, bar);
                     } else {
+                        mbar_arrive_expect_tx(&full[stage], G::kStageBytes);
+                        if (!SWAP) {
+                            tma_load_2d(sx, &tmx, kb * kBK, tm * 128, &full[stage]);  // A: 64 K x 128 rows
 #pragma unroll
-                        for (int j = 0; j < 2; ++j)  // B: 128 columns as two boxes of 64 columns x 64 K
-                            tma_load_2d(sx + j * 8192, &tmx, tn * 128 + 64 * j, kb * kBK, &full[stage]);
-                        tma_load_2d(sy, &tmy, kb * kBK, 0, &full[stage]);  // A: 64 K x BN rows (M <= BN)
+                            for (int j = 0; j < BN / 64; ++j)  // B: 64 columns x 64 K per box
+                                tma_load_2d(sy + j * 8192, &tmy, tn * BN + 64 * j, kb * kBK, &full[stage]);
+                        } else {
+#pragma unroll
+                            for (int j = 0; j < 2; ++j)  // B: 128 columns as two boxes of 64 columns x 64 K
+                                tma_load_2d(sx + j * 8192, &tmx, tn * 128 + 64 * j, kb * kBK, &full[stage]);
+                            tma_load_2d(sy, &tmy, kb * kBK, 0, &full[stage]);  // A: 64 K x BN rows (M <= BN)
+                        }
                     }
                     ++issued;
                     if (++stage == S) {
@@ -205,7 +291,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 ++seg;
             }
-            if (!ok) {  // let the loads in flight land before the block leaves
+            if (!ok && leader) {  // let the loads in flight land (a pair's land on the leader's barriers)
                 const int n = issued < S ? issued : S;
                 for (int i = 1; i <= n; ++i) {
                     const int q = issued - i;
@@ -214,21 +300,22 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
         }
     } else if (warp == 1) {
-        // ---------------------------------------------------------- MMA issuer (one thread)
-        if (lane == 0) {
-            constexpr uint32_t idesc = idesc_f16_f32(128, BN, SWAP, !SWAP);
+        // ---------------------------------------------------------- MMA issuer (one thread; the leader of a pair)
+        if (lane == 0 && leader) {
+            constexpr uint32_t idesc = idesc_f16_f32(PAIR ? 256 : 128, BN, SWAP, !SWAP);
             SegIter it(s, c, P);
-            int stage = 0, acc = 0, seg = 0, tile, k0, k1;
+            Seg sg;
+            int stage = 0, acc = 0, seg = 0;
             uint32_t ph = 0, aph = 0;
             bool ok = true;
-            while (ok && it.next(s, P, tile, k0, k1)) {
+            while (ok && it.next(s, P, sg)) {
                 if (!wait_bounded(&tempty[acc], aph ^ 1u, abort_flag, p.wait_ns, site(1, 3, acc), seg)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
                 const uint32_t d = tmem_base + (uint32_t)(acc * BN);
-                for (int kb = k0; kb < k1; ++kb) {
+                for (int kb = sg.k0; kb < sg.k1; ++kb) {
                     if (!wait_bounded(&full[stage], ph, abort_flag, p.wait_ns, site(1, 0, stage), seg)) {
                         ok = false;
                         break;
@@ -239,16 +326,28 @@ __global__ void __launch_bounds__(kThreads, 1)
                     for (int k = 0; k < kBK / 16; ++k) {
                         const uint64_t ad = SWAP ? desc_mnmajor(sx, k) : desc_kmajor(sx, k);
                         const uint64_t bd = SWAP ? desc_kmajor(sy, k) : desc_mnmajor(sy, k);
-                        mma_f16(d, ad, bd, idesc, (kb > k0 || k > 0) ? 1u : 0u);
+                        const uint32_t accumulate = (kb > sg.k0 || k > 0) ? 1u : 0u;
+                        if (PAIR)
+                            mma_f16_pair(d, ad, bd, idesc, accumulate);
+                        else
+                            mma_f16(d, ad, bd, idesc, accumulate);
                     }
-                    mma_commit(&empty[stage]);  // the stage is free once these MMAs have read it
+                    // the stage is free (in both blocks of a pair) once these MMAs have read it
+                    if (PAIR)
+                        mma_commit_pair(&empty[stage], 0x3);
+                    else
+                        mma_commit(&empty[stage]);
                     if (++stage == S) {
                         stage = 0;
                         ph ^= 1u;
                     }
                 }
                 if (!ok) break;
-                mma_commit(&tfull[acc]);  // the accumulator is complete once every MMA so far has finished
+                // the accumulator (both blocks' halves) is complete once every MMA so far has finished
+                if (PAIR)
+                    mma_commit_pair(&tfull[acc], 0x3);
+                else
+                    mma_commit(&tfull[acc]);
                 if (++acc == 2) {
                     acc = 0;
                     aph ^= 1u;
@@ -256,19 +355,35 @@ __global__ void __launch_bounds__(kThreads, 1)
                 ++seg;
             }
             if (!ok) {  // let the MMAs in flight finish before the tensor memory is freed
-                mma_commit(drain);
+                if (PAIR)
+                    mma_commit_pair(drain, 0x1);
+                else
+                    mma_commit(drain);
                 wait_drain(drain, 0, p.wait_ns);
             }
         }
         __syncwarp();
     } else {
-        // ---------------------------------------------------------- epilogue (warps 2-5, 128 threads)
+        // ---------------------------------------------------------- epilogue (warps 2-5, 128 threads per block)
         const int q = warp & 3;         // the TMEM lane quarter this warp may access
         const int row = q * 32 + lane;  // accumulator row = TMEM lane
+        const uint32_t tempty_leader0 = PAIR ? mapa_shared(smem_u32(&tempty[0]), 0) : smem_u32(&tempty[0]);
         SegIter it(s, c, P);
-        int acc = 0, seg = 0, tile, k0, k1;
+        Seg sg;
+        int acc = 0, seg = 0;
         uint32_t aph = 0;
-        while (it.next(s, P, tile, k0, k1)) {
+        // the accumulator is read: one arrival per warp on the (leader's) tmem-empty barrier
+        auto release_acc = [&](int a) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+                if (PAIR)
+                    mbar_arrive_cluster(tempty_leader0 + 8u * (uint32_t)a);
+                else
+                    mbar_arrive(&tempty[a]);
+            }
+        };
+        while (it.next(s, P, sg)) {
             // one thread waits (bounded); a named barrier hands its outcome to the other 127, so that an abort
             // takes the whole group out together and no thread is left at a later barrier
             if (threadIdx.x == kEpiThread0)
@@ -276,15 +391,18 @@ __global__ void __launch_bounds__(kThreads, 1)
             named_bar_sync(1, 128);
             if (!epi_go[seg & 1]) break;
             tc_fence_after();
-            int tm, tn;
+            int m0, n0;
             if (SWAP) {
-                tm = 0;
-                tn = tile;
+                m0 = 0;
+                n0 = sg.tile * 128;
             } else {
-                tile_coords(s, tile, tm, tn);
+                int tm, tn;
+                tile_coords(s, sg.tile, tm, tn);
+                m0 = tm * G::kTileM + rank * 128;
+                n0 = tn * BN;
             }
             const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
-            if (k0 == 0 && k1 == s.kblocks) {
+            if (sg.k0 == 0 && sg.k1 == s.kblocks) {
                 // a whole tile: straight to C
 #pragma unroll 1
                 for (int c0 = 0; c0 < BN; c0 += 16) {
@@ -294,52 +412,67 @@ __global__ void __launch_bounds__(kThreads, 1)
                     float v[16];
 #pragma unroll
                     for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[j]);
-                    store_chunk<BN, SWAP>(p, tm, tn, row, c0, v);
+                    store_chunk<SWAP>(p, m0, n0, row, c0, v);
                 }
-                tc_fence_before();
-                mbar_arrive(&tempty[acc]);
+                release_acc(acc);
             } else {
-                // part of a stream-K tile: the fp32 partial to this block's slot, column-major (a warp's 32 lanes
-                // write 128 contiguous bytes per column)
-                float* w = p.work + (size_t)sk_slot(s, c, P, tile) * (128 * BN);
-#pragma unroll 1
-                for (int c0 = 0; c0 < BN; c0 += 16) {
-                    uint32_t r[16];
-                    tmem_ld16(tbase + (uint32_t)c0, r);
-                    tmem_wait_ld();
-#pragma unroll
-                    for (int j = 0; j < 16; ++j) __stcg(w + (size_t)(c0 + j) * 128 + row, __uint_as_float(r[j]));
-                }
-                tc_fence_before();
-                mbar_arrive(&tempty[acc]);
-                __threadfence();
+                // part of a split tile
+                const Fixup f = fixup_of(s, c, P, sg);
+                int* counter = p.counters + (sg.tile - s.dp_tiles) * R + rank;
+                // every other partial already written: this block is the last; sum them with its own accumulator
+                // straight from tensor memory (no round trip of its own partial)
+                if (threadIdx.x == kEpiThread0) *reduce_flag = ld_acquire_gpu(counter) == f.nseg - 1 ? 2 : 0;
                 named_bar_sync(1, 128);
-                const long long gf = (long long)(tile - s.dp_tiles) * s.kblocks;
-                const int cf = sk_owner(s, gf, P), cl = sk_owner(s, gf + s.kblocks - 1, P);
-                if (threadIdx.x == kEpiThread0) {
-                    const int old = atomicAdd(&p.counters[tile - s.dp_tiles], 1);
-                    *reduce_flag = (old == cl - cf) ? 1 : 0;
-                }
-                named_bar_sync(1, 128);
-                if (*reduce_flag) {
-                    // the last block of this tile: sum the partials in block order, then C
-                    __threadfence();
+                const int fast = *reduce_flag;
+                if (fast == 2) {
 #pragma unroll 1
                     for (int c0 = 0; c0 < BN; c0 += 16) {
-                        float v[16];
-                        const float* w0 = p.work + (size_t)sk_slot(s, cf, P, tile) * (128 * BN);
+                        uint32_t r[16];
+                        tmem_ld16(tbase + (uint32_t)c0, r);
+                        tmem_wait_ld();
+                        float own[16], v[16];
 #pragma unroll
-                        for (int j = 0; j < 16; ++j) v[j] = __ldcg(w0 + (size_t)(c0 + j) * 128 + row);
-                        for (int cc = cf + 1; cc <= cl; ++cc) {
-                            const float* wc = p.work + (size_t)sk_slot(s, cc, P, tile) * (128 * BN);
-#pragma unroll
-                            for (int j = 0; j < 16; ++j) v[j] += __ldcg(wc + (size_t)(c0 + j) * 128 + row);
-                        }
-                        store_chunk<BN, SWAP>(p, tm, tn, row, c0, v);
+                        for (int j = 0; j < 16; ++j) own[j] = __uint_as_float(r[j]);
+                        sum_partials<BN, R>(p, P, sg.tile, rank, f, true, own, row, c0, v);
+                        store_chunk<SWAP>(p, m0, n0, row, c0, v);
                     }
-                    if (threadIdx.x == kEpiThread0) p.counters[tile - s.dp_tiles] = 0;
+                    release_acc(acc);
+                    if (threadIdx.x == kEpiThread0) atomicExch(counter, 0);
+                } else {
+                    // this block's partial to its slot; the last block to finish the tile sums them
+                    const long long myslot = (long long)fixup_slot(s, P, sg.tile, f, f.mine) * R + rank;
+#pragma unroll 1
+                    for (int c0 = 0; c0 < BN; c0 += 16) {
+                        uint32_t r[16];
+                        tmem_ld16(tbase + (uint32_t)c0, r);
+                        tmem_wait_ld();
+                        float4* dst = reinterpret_cast<float4*>(slot_ptr<BN>(p, myslot, row, c0));
+#pragma unroll
+                        for (int j = 0; j < 4; ++j)
+                            __stcg(dst + j, make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
+                                                        __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3])));
+                    }
+                    release_acc(acc);
+                    __threadfence();
+                    named_bar_sync(1, 128);
+                    if (threadIdx.x == kEpiThread0) {
+                        const int old = atomicAdd(counter, 1);
+                        if (old == f.nseg - 1) __threadfence();
+                        *reduce_flag = old == f.nseg - 1 ? 1 : 0;
+                    }
+                    named_bar_sync(1, 128);
+                    if (*reduce_flag == 1) {
+                        const float none[16] = {};
+#pragma unroll 1
+                        for (int c0 = 0; c0 < BN; c0 += 16) {
+                            float v[16];
+                            sum_partials<BN, R>(p, P, sg.tile, rank, f, false, none, row, c0, v);
+                            store_chunk<SWAP>(p, m0, n0, row, c0, v);
+                        }
+                        if (threadIdx.x == kEpiThread0) atomicExch(counter, 0);
+                    }
                 }
-                named_bar_sync(1, 128);
+                named_bar_sync(1, 128);  // reduce_flag is read by all before the next segment writes it
             }
             if (++acc == 2) {
                 acc = 0;
@@ -349,12 +482,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     }
 
+    __syncwarp();
     tc_fence_before();
-    __syncthreads();
+    if (PAIR)
+        cluster_sync();  // neither block leaves while the other may still read its memory or arrive on its barriers
+    else
+        __syncthreads();
     if (warp == 1) {
         __syncwarp();
         tc_fence_after();
-        tmem_dealloc(tmem_base, G::kTmemCols);
+        if (PAIR)
+            tmem_dealloc_pair(tmem_base, G::kTmemCols);
+        else
+            tmem_dealloc(tmem_base, G::kTmemCols);
     }
 }
 

@@ -1,38 +1,42 @@
 // plan.h -- the rung's rule (host only, no CUDA): which kernel, tile and schedule a call takes.
 //
 // The reference picks a kernel per class of shape (step7::choose, hopper/step7.cuh:921-949; step6::choose,
-// hopper/step6.cuh:468-488; its 128 x 320 tile where waves x area are smaller, rows7c :921-933).  On the B200 the
-// classes are:
+// hopper/step6.cuh:468-488; its 128 x 320 tile where waves x area are smaller, rows7c :921-933).  On the B200:
 //   M <= 128   swap-AB (BW_KERNEL_SWAP): the weights' 128 columns per tile fill the MMA's 128 rows and the M tokens its
-//              N (rounded up to 16), so small M wastes no tensor-core rows; the K-blocks of all tiles are split evenly
-//              over the SMs (stream-K), so every SM streams the same share of B from HBM whatever N / 128 is.
-//   M > 128    128 x 256 tiles (BW_KERNEL_TILE), persistent; whole waves of tiles round-robin (data-parallel), the
-//              last one to two waves' K-blocks split evenly over the SMs (stream-K), so no wave runs part-empty.
+//              N (rounded up to 16), so small M wastes no tensor-core rows.  The shape streams B from HBM once; its
+//              K-blocks are cut evenly over the SMs (stream-K), so every SM streams the same share whatever N / 128 is.
+//   M > 128    256 x 256 tiles on pairs of SMs (BW_KERNEL_PAIR, tcgen05 cta_group::2), persistent: per SM the
+//              operand traffic of a 128 x 128 tile for the work of a 128 x 256 one.  Whole waves of tiles go
+//              round-robin (data-parallel); the tiles of the last, partial wave are split in K into `splits` ranges
+//              (split-K) when that fills the pairs better than leaving them idle, the cost of each extra partial
+//              included.
 // Variants take one mechanism out each, for ablations (the reference's g_var, hopper/step7.cu:1-11).
 #pragma once
 #include <cstddef>
 #include "bwgemm.h"
+#include "schedule.h"
 
 namespace bw {
 
-constexpr int kVariants = 5;
+constexpr int kVariants = 6;
 inline const char* variant_name(int v)
 {
     switch (v) {
-    case 0: return "v0: the rule (swap-AB + stream-K at M <= 128; 128x256 tiles, data-parallel + stream-K tail above)";
-    case 1: return "v1: without stream-K (whole tiles only, round-robin)";
-    case 2: return "v2: without swap-AB (128x256 tiles at every M)";
+    case 0: return "v0: the rule (swap-AB + stream-K at M <= 128; 256x256 pair tiles + split-K tail above)";
+    case 1: return "v1: without split-K / stream-K (whole tiles only, round-robin)";
+    case 2: return "v2: without swap-AB (pair tiles at every M)";
     case 3: return "v3: without the serpentine order (tiles row after row)";
-    case 4: return "v4: stream-K over every tile (no data-parallel waves)";
+    case 4: return "v4: stream-K in place of the split-K tail";
+    case 5: return "v5: without the SM pair (128x256 tiles on single SMs)";
     default: return nullptr;
     }
 }
 
-// The kernels' geometry, as gemm_kernel.cuh's Geom computes it (checked against it at compile time in bwgemm.cu).
-inline int plan_stage_bytes(int bn) { return 128 * 64 * 2 + bn * 64 * 2; }
-inline int plan_stages(int bn)
+// The kernels' geometry, as gemm_kernel.cuh's Geom computes it (checked against it at launch in bwgemm.cu).
+inline int plan_stage_bytes(int bn, int ranks) { return 128 * 64 * 2 + (bn / ranks) * 64 * 2; }
+inline int plan_stages(int bn, int ranks)
 {
-    const int s = 204800 / plan_stage_bytes(bn);
+    const int s = 204800 / plan_stage_bytes(bn, ranks);
     return s < 12 ? s : 12;
 }
 inline int plan_tmem_cols(int bn)
@@ -41,20 +45,43 @@ inline int plan_tmem_cols(int bn)
     while (c < 2 * bn) c *= 2;
     return c;
 }
-inline int plan_smem_bytes(int bn) { return 1024 + plan_stages(bn) * plan_stage_bytes(bn) + (2 * plan_stages(bn) + 5) * 8 + 32; }
+inline int plan_smem_bytes(int bn, int ranks)
+{
+    return 1024 + plan_stages(bn, ranks) * plan_stage_bytes(bn, ranks) + (2 * plan_stages(bn, ranks) + 5) * 8 + 32;
+}
 
 inline bool shape_ok(int M, int N, int K)
 {
     return M > 0 && N > 0 && K > 0 && M % 16 == 0 && N % 64 == 0 && K % 64 == 0;
 }
 
-inline int make_plan(int M, int N, int K, int sms, int variant, bw_plan* p)
+// The split-K factor for a tail of `tail` tiles on P blocks: minimises the tail's time in tile-times,
+// ceil(tail s / P) / s, plus the reduction of s partials (each about fixup_kb K-blocks of work for the last block).
+inline int tail_splits(int tail, int P, int kblocks, double fixup_kb)
+{
+    int best = 1;
+    double best_cost = 1.0;
+    for (int sp = 2; sp <= 16 && sp <= kblocks; ++sp) {
+        const double waves = (double)((tail * sp + P - 1) / P);
+        const double cost = waves / sp + sp * fixup_kb / kblocks;
+        if (cost < best_cost - 1e-9) {
+            best_cost = cost;
+            best = sp;
+        }
+    }
+    return best;
+}
+
+// sms: the SMs; pairs: the pairs of SMs the pair kernel can hold at once (its cluster occupancy).
+inline int make_plan(int M, int N, int K, int sms, int pairs, int variant, bw_plan* p)
 {
     if (!p || variant < 0 || variant >= kVariants || sms <= 0) return BW_ERR_ARG;
     if (!shape_ok(M, N, K)) return BW_ERR_SHAPE;
     bw_plan q = {};
     q.kblocks = K / 64;
     const bool swap = M <= 128 && variant != 2;
+    const bool pair = !swap && variant != 5 && pairs > 0;
+    int ranks = 1, units = sms;  // the blocks (or pairs) of the persistent grid
     if (swap) {
         q.kernel = BW_KERNEL_SWAP;
         q.bn = (M + 15) / 16 * 16;
@@ -62,35 +89,56 @@ inline int make_plan(int M, int N, int K, int sms, int variant, bw_plan* p)
         q.tiles_n = (N + 127) / 128;
         q.group_rows = 0;
     } else {
-        q.kernel = BW_KERNEL_TILE;
+        q.kernel = pair ? BW_KERNEL_PAIR : BW_KERNEL_TILE;
         q.bn = 256;
-        q.tiles_m = (M + 127) / 128;
+        ranks = pair ? 2 : 1;
+        units = pair ? pairs : sms;
+        q.tiles_m = (M + 128 * ranks - 1) / (128 * ranks);
         q.tiles_n = (N + 255) / 256;
         q.group_rows = variant == 3 ? 0 : 16;
     }
     q.tiles = q.tiles_m * q.tiles_n;
     const long long kb = q.kblocks;
-    if (variant == 1 || (!swap && variant != 4 && q.tiles % sms == 0)) {
+    const bool stream_k = swap ? variant != 1 : variant == 4;
+    if (variant == 1 || q.tiles % units == 0) {
         q.dp_tiles = q.tiles;  // whole tiles only
-        q.sk_iters = 0;
-        q.grid = q.tiles < sms ? q.tiles : sms;
-    } else if (swap || variant == 4) {
-        q.dp_tiles = 0;  // every tile's K-blocks split evenly
-        q.sk_iters = (long long)q.tiles * kb;
-        q.grid = q.sk_iters < sms ? (int)q.sk_iters : sms;
+    } else if (stream_k) {
+        // stream-K: at M <= 128 over every tile; above, over the last full wave and the partial one
+        const int waves = q.tiles / units;
+        q.dp_tiles = swap ? 0 : (waves >= 1 ? waves - 1 : 0) * units;
+        q.sk_tiles = q.tiles - q.dp_tiles;
+        q.sk_iters = (long long)q.sk_tiles * kb;
     } else {
-        const int waves = q.tiles / sms;  // full waves; keep one of them for stream-K with the partial wave
-        q.dp_tiles = (waves >= 1 ? waves - 1 : 0) * sms;
-        q.sk_iters = (long long)(q.tiles - q.dp_tiles) * kb;
-        q.grid = q.dp_tiles > 0 ? sms : (q.sk_iters < sms ? (int)q.sk_iters : sms);
+        // split-K over the partial wave, if it pays
+        const int tail = q.tiles % units;
+        const int sp = tail_splits(tail, units, q.kblocks, /*fixup_kb=*/12.0 * q.bn / 256);
+        if (sp > 1) {
+            q.dp_tiles = q.tiles - tail;
+            q.sk_tiles = tail;
+            q.splits = sp;
+        } else {
+            q.dp_tiles = q.tiles;
+        }
     }
-    // every block owns at least one stream-K K-block (the partial counts rely on it)
-    if (q.sk_iters > 0 && q.sk_iters < q.grid) return BW_ERR_ARG;
-    q.stages = plan_stages(q.bn);
-    q.smem_bytes = plan_smem_bytes(q.bn);
+    int P;  // blocks, or pairs, of the grid
+    if (q.sk_tiles == 0) {
+        P = q.tiles < units ? q.tiles : units;
+    } else if (q.splits > 0) {
+        const int u = q.sk_tiles * q.splits;
+        P = q.dp_tiles > 0 ? units : (u < units ? u : units);
+    } else {
+        P = q.dp_tiles > 0 ? units : (q.sk_iters < units ? (int)q.sk_iters : units);
+        if (q.sk_iters < P) return BW_ERR_ARG;  // every block owns at least one stream-K K-block
+    }
+    q.grid = P * ranks;
+    q.stages = plan_stages(q.bn, ranks);
+    q.smem_bytes = plan_smem_bytes(q.bn, ranks);
     q.tmem_cols = plan_tmem_cols(q.bn);
-    q.counters = q.sk_iters > 0 ? q.tiles - q.dp_tiles : 0;
-    q.workspace_bytes = q.sk_iters > 0 ? (size_t)2 * q.grid * 128 * q.bn * sizeof(float) : 0;
+    q.counters = q.sk_tiles * ranks;
+    Sched sc = {};
+    sc.sk_tiles = q.sk_tiles;
+    sc.splits = q.splits;
+    q.workspace_bytes = (size_t)workspace_slots(sc, P) * ranks * 128 * q.bn * sizeof(float);
     *p = q;
     return BW_OK;
 }

@@ -1,6 +1,21 @@
 // schedule.h -- the work of one block of the rung's persistent kernel: which tiles, and which K-blocks of them, in
-// which order.  Host and device: the kernel runs it, and the CPU tests run the same code to check that every K-block
-// of every tile is computed exactly once and that the stream-K partial counts and slots agree.
+// which order, and where the partial sums of a tile split over several blocks go.  Host and device: the kernel runs
+// it, and the CPU tests run the same code to check that every K-block of every tile is computed exactly once and that
+// the partial counts and workspace slots the reducer uses are the ones the writers used.
+//
+// A block's work, in order:
+//   1. data-parallel: whole tiles c, c + P, c + 2P, ... below dp_tiles (P blocks; consecutive tiles run at the same
+//      time, so blocks that share rows of A or columns of B read them from L2 together);
+//   2. the other sk_tiles tiles, either
+//      split-K (splits > 0): each tile's K-blocks cut in `splits` equal ranges; unit u = split * sk_tiles + tile goes
+//        to block u % P, so the units running together are the same K range of neighbouring tiles (the shared
+//        operands stay shared in L2), or
+//      stream-K (splits == 0): the sk_tiles * kblocks K-blocks cut evenly over the P blocks, block c taking
+//        [sk_iters c / P, sk_iters (c + 1) / P) -- every block the same work whatever the tile count (used where the
+//        operands are streamed once from HBM anyway: the swap-AB path at M <= 128).
+// A tile computed by several blocks: each writes its fp32 partial to a workspace slot; the last to finish (a counter
+// per tile) sums the partials in a fixed order (split order, or block order) -- so the result is the same bits
+// whichever block finishes last -- and writes C.
 #pragma once
 #if defined(__CUDACC__)
 #define BW_HD __host__ __device__
@@ -16,18 +31,30 @@ struct Sched {
     int tiles_m, tiles_n, tiles;
     int kblocks;          // K / 64
     int dp_tiles;         // tiles [0, dp_tiles): whole tiles, round-robin over the blocks
-    long long sk_iters;   // (tiles - dp_tiles) * kblocks: K-blocks split evenly over the blocks (stream-K)
+    int sk_tiles;         // tiles [dp_tiles, tiles): split-K or stream-K
+    int splits;           // > 0: split-K into this many K ranges; 0: stream-K
+    long long sk_iters;   // stream-K: sk_tiles * kblocks, split evenly over the blocks
     int group_rows;       // serpentine group height in rows of tiles; 0: row after row
 };
 
-// ------------------------------------------------------------------ the schedule
+// ------------------------------------------------------------------ stream-K bookkeeping
 BW_HD inline long long sk_begin(const Sched& s, int c, int P) { return s.sk_iters * c / P; }
 // The block whose stream-K share holds iteration g (the largest c with sk_begin(c) <= g).
 BW_HD inline int sk_owner(const Sched& s, long long g, int P)
 {
     return (int)(((g + 1) * (long long)P - 1) / s.sk_iters);
 }
+// Block cc's slot for stream-K tile `tile`: 2 cc for the tile its share starts in, 2 cc + 1 for the one it ends in
+// (a share covers whole tiles in between, which need no slot).
+BW_HD inline int sk_slot(const Sched& s, int cc, int P, int tile)
+{
+    const int first = s.dp_tiles + (int)(sk_begin(s, cc, P) / s.kblocks);
+    return 2 * cc + (tile == first ? 0 : 1);
+}
 
+// ------------------------------------------------------------------ tile order
+// Serpentine order of hopper/step5.cuh:149-163: groups of group_rows rows of tiles, column after column within a
+// group, the odd groups from the last column back.
 BW_HD inline void tile_coords(const Sched& s, int t, int& tm, int& tn)
 {
     if (s.group_rows <= 0) {
@@ -44,40 +71,89 @@ BW_HD inline void tile_coords(const Sched& s, int t, int& tm, int& tn)
     if (g & 1) tn = s.tiles_n - 1 - tn;
 }
 
-// The segments of block c, in order: its data-parallel tiles, then its stream-K share cut at tile boundaries.
+// ------------------------------------------------------------------ one block's segments
+struct Seg {
+    int tile, k0, k1;
+    int unit;  // split-K unit index (split * sk_tiles + tile - dp_tiles), -1 otherwise
+};
+
 struct SegIter {
-    int next_dp;
+    int next_dp, next_u;
     long long g, g_end;
-    BW_HD SegIter(const Sched& s, int c, int P) : next_dp(c), g(sk_begin(s, c, P)), g_end(sk_begin(s, c + 1, P)) {}
-    BW_HD bool next(const Sched& s, int P, int& tile, int& k0, int& k1)
+    BW_HD SegIter(const Sched& s, int c, int P)
+        : next_dp(c), next_u(c), g(s.splits > 0 ? 0 : sk_begin(s, c, P)), g_end(s.splits > 0 ? 0 : sk_begin(s, c + 1, P))
+    {
+    }
+    BW_HD bool next(const Sched& s, int P, Seg& seg)
     {
         if (next_dp < s.dp_tiles) {
-            tile = next_dp;
-            k0 = 0;
-            k1 = s.kblocks;
+            seg.tile = next_dp;
+            seg.k0 = 0;
+            seg.k1 = s.kblocks;
+            seg.unit = -1;
             next_dp += P;
+            return true;
+        }
+        if (s.splits > 0) {
+            if (next_u >= s.sk_tiles * s.splits) return false;
+            const int u = next_u;
+            const int sp = u / s.sk_tiles, rel = u - sp * s.sk_tiles;
+            seg.tile = s.dp_tiles + rel;
+            seg.k0 = (int)((long long)sp * s.kblocks / s.splits);
+            seg.k1 = (int)((long long)(sp + 1) * s.kblocks / s.splits);
+            seg.unit = u;
+            next_u += P;
             return true;
         }
         if (g < g_end) {
             const long long rel = g / s.kblocks;
-            k0 = (int)(g - rel * s.kblocks);
+            seg.k0 = (int)(g - rel * s.kblocks);
             const long long left = g_end - g;
-            k1 = left < (long long)(s.kblocks - k0) ? k0 + (int)left : s.kblocks;
-            tile = s.dp_tiles + (int)rel;
-            g += k1 - k0;
+            seg.k1 = left < (long long)(s.kblocks - seg.k0) ? seg.k0 + (int)left : s.kblocks;
+            seg.tile = s.dp_tiles + (int)rel;
+            seg.unit = -1;
+            g += seg.k1 - seg.k0;
             return true;
         }
         return false;
     }
 };
 
-// Block cc's workspace slot for stream-K tile `tile`: 2 cc for the tile its share starts in, 2 cc + 1 for the one it
-// ends in (a share covers whole tiles in between, which need no slot).
-BW_HD inline int sk_slot(const Sched& s, int cc, int P, int tile)
+// ------------------------------------------------------------------ the partials of one tile
+// A segment that is not a whole tile: how many partials its tile has (nseg), which of them is this block's (mine),
+// and where partial i (in summation order) lives.
+struct Fixup {
+    int nseg, mine;
+    int first;  // stream-K: the first block of the tile
+};
+
+BW_HD inline Fixup fixup_of(const Sched& s, int c, int P, const Seg& seg)
 {
-    const int first = s.dp_tiles + (int)(sk_begin(s, cc, P) / s.kblocks);
-    return 2 * cc + (tile == first ? 0 : 1);
+    Fixup f;
+    if (s.splits > 0) {
+        f.nseg = s.splits;
+        f.mine = seg.unit / s.sk_tiles;
+        f.first = 0;
+    } else {
+        const long long gf = (long long)(seg.tile - s.dp_tiles) * s.kblocks;
+        f.first = sk_owner(s, gf, P);
+        f.nseg = sk_owner(s, gf + s.kblocks - 1, P) - f.first + 1;
+        f.mine = c - f.first;
+    }
+    return f;
 }
 
+BW_HD inline int fixup_slot(const Sched& s, int P, int tile, const Fixup& f, int i)
+{
+    if (s.splits > 0) return i * s.sk_tiles + (tile - s.dp_tiles);
+    return sk_slot(s, f.first + i, P, tile);
+}
+
+// The number of workspace slots a schedule needs.
+BW_HD inline long long workspace_slots(const Sched& s, int P)
+{
+    if (s.sk_tiles <= 0) return 0;
+    return s.splits > 0 ? (long long)s.sk_tiles * s.splits : 2LL * P;
+}
 
 }  // namespace bw

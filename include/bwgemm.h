@@ -29,6 +29,7 @@ extern "C" {
 /* Kernels of the rule (bw_plan.kernel). */
 #define BW_KERNEL_TILE 0   /* 128 x bn tiles of C, A as the MMA's A operand */
 #define BW_KERNEL_SWAP 1   /* M <= 128: C^T = B^T A^T, 128 columns of B as the MMA's A operand, bn = M rounded to 16 */
+#define BW_KERNEL_PAIR 2   /* 256 x bn tiles on a pair of SMs (tcgen05 cta_group::2) */
 
 /*
  * C = A B on `stream` (a cudaStream_t, 0 for the legacy default stream), with the current device.
@@ -70,16 +71,19 @@ typedef struct bw_plan {
     int kblocks;         /* K / 64 */
     int grid;            /* persistent blocks, one per SM at most */
     int dp_tiles;        /* tiles done whole, round-robin over the blocks */
-    long long sk_iters;  /* K-blocks of the other tiles, split evenly over the blocks (stream-K) */
+    int sk_tiles;        /* the other tiles: split-K or stream-K */
+    int splits;          /* > 0: each of them split into this many K ranges (split-K); 0: stream-K */
+    long long sk_iters;  /* stream-K: their K-blocks, split evenly over the blocks */
     int group_rows;      /* rows of tiles per serpentine group (0: row after row) */
-    size_t workspace_bytes; /* fp32 stream-K partials */
-    int counters;        /* stream-K tile counters */
+    size_t workspace_bytes; /* fp32 partials of the split tiles */
+    int counters;        /* one counter per split tile */
     int smem_bytes;      /* dynamic shared memory per block */
     int tmem_cols;       /* tensor-memory columns per block */
 } bw_plan;
 
 /*
- * The rule: which kernel, tile and schedule a call at M x N x K takes on a GPU of `sms` SMs, for variant `variant`.
+ * The rule: which kernel, tile and schedule a call at M x N x K takes on a GPU of `sms` SMs (sms / 2 pairs of SMs
+ * held at once), for variant `variant`.  On a device the library uses the pairs its occupancy query reports.
  * Replaces: step7::choose / step6::choose / rows7c (hopper/step7.cuh:921-949, hopper/step6.cuh:468-488).
  */
 int bw_gemm_plan(int M, int N, int K, int sms, int variant, bw_plan* out);

@@ -5,6 +5,7 @@
 //   schedule_check M N K sms variant [M N K sms variant ...]
 #include <cstdio>
 #include <cstdlib>
+#include <algorithm>
 #include <map>
 #include <set>
 #include <vector>
@@ -15,21 +16,27 @@
 static int check(int M, int N, int K, int sms, int variant)
 {
     bw_plan q;
-    const int rc = bw::make_plan(M, N, K, sms, variant, &q);
+    const int rc = bw::make_plan(M, N, K, sms, sms / 2, variant, &q);
     if (rc) {
         printf("FAULT %d %d %d sms %d v%d: plan status %d\n", M, N, K, sms, variant, rc);
         return 1;
     }
     bw::Sched s;
     s.M = M, s.N = N, s.K = K, s.tiles_m = q.tiles_m, s.tiles_n = q.tiles_n, s.tiles = q.tiles;
-    s.kblocks = q.kblocks, s.dp_tiles = q.dp_tiles, s.sk_iters = q.sk_iters, s.group_rows = q.group_rows;
-    const int P = q.grid;
-    if (P < 1 || P > sms) {
+    s.kblocks = q.kblocks, s.dp_tiles = q.dp_tiles, s.sk_tiles = q.sk_tiles, s.splits = q.splits;
+    s.sk_iters = q.sk_iters, s.group_rows = q.group_rows;
+    if (q.dp_tiles + q.sk_tiles != q.tiles || (q.splits > 0) == (q.sk_iters > 0) && q.sk_tiles > 0) {
+        printf("FAULT %dx%dx%d v%d: inconsistent plan\n", M, N, K, variant);
+        return 1;
+    }
+    const int R = q.kernel == BW_KERNEL_PAIR ? 2 : 1;
+    const int P = q.grid / R;
+    if (P < 1 || q.grid > sms || q.grid % R) {
         printf("FAULT %dx%dx%d v%d: grid %d\n", M, N, K, variant, P);
         return 1;
     }
     // the tile order: a bijection
-    if (q.kernel == BW_KERNEL_TILE) {
+    if (q.kernel != BW_KERNEL_SWAP) {
         std::vector<int> seen((size_t)q.tiles, 0);
         for (int t = 0; t < q.tiles; ++t) {
             int tm, tn;
@@ -41,30 +48,37 @@ static int check(int M, int N, int K, int sms, int variant)
         }
     }
     std::vector<unsigned char> cover((size_t)q.tiles * q.kblocks, 0);
-    std::map<int, int> partials;        // stream-K tile -> partials written
+    std::map<int, std::vector<int>> partials;  // split tile -> the `mine` index of each partial written
     std::set<int> slots;
+    const long long nslots = bw::workspace_slots(s, P);
     for (int c = 0; c < P; ++c) {
         bw::SegIter it(s, c, P);
-        int tile, k0, k1;
-        while (it.next(s, P, tile, k0, k1)) {
-            if (tile < 0 || tile >= q.tiles || k0 < 0 || k1 > q.kblocks || k0 >= k1) {
-                printf("FAULT %dx%dx%d v%d: block %d segment tile %d k %d..%d\n", M, N, K, variant, c, tile, k0, k1);
+        bw::Seg sg;
+        while (it.next(s, P, sg)) {
+            if (sg.tile < 0 || sg.tile >= q.tiles || sg.k0 < 0 || sg.k1 > q.kblocks || sg.k0 >= sg.k1) {
+                printf("FAULT %dx%dx%d v%d: block %d segment tile %d k %d..%d\n", M, N, K, variant, c, sg.tile, sg.k0,
+                       sg.k1);
                 return 1;
             }
-            for (int k = k0; k < k1; ++k) cover[(size_t)tile * q.kblocks + k]++;
-            const bool whole = k0 == 0 && k1 == q.kblocks;
+            for (int k = sg.k0; k < sg.k1; ++k) cover[(size_t)sg.tile * q.kblocks + k]++;
+            const bool whole = sg.k0 == 0 && sg.k1 == q.kblocks;
             if (!whole) {
-                if (tile < q.dp_tiles) {
+                if (sg.tile < q.dp_tiles) {
                     printf("FAULT %dx%dx%d v%d: a data-parallel tile in part\n", M, N, K, variant);
                     return 1;
                 }
-                partials[tile]++;
-                const int slot = bw::sk_slot(s, c, P, tile);
-                if (slot < 0 || slot >= 2 * P || !slots.insert(slot).second) {
-                    printf("FAULT %dx%dx%d v%d: slot %d of block %d tile %d\n", M, N, K, variant, slot, c, tile);
+                const bw::Fixup f = bw::fixup_of(s, c, P, sg);
+                if (f.mine < 0 || f.mine >= f.nseg) {
+                    printf("FAULT %dx%dx%d v%d: block %d is partial %d of %d\n", M, N, K, variant, c, f.mine, f.nseg);
                     return 1;
                 }
-                if ((size_t)(slot + 1) * 128 * q.bn * sizeof(float) > q.workspace_bytes) {
+                partials[sg.tile].push_back(f.mine);
+                const int slot = bw::fixup_slot(s, P, sg.tile, f, f.mine);
+                if (slot < 0 || slot >= nslots || !slots.insert(slot).second) {
+                    printf("FAULT %dx%dx%d v%d: slot %d of block %d tile %d\n", M, N, K, variant, slot, c, sg.tile);
+                    return 1;
+                }
+                if ((size_t)(slot + 1) * R * 128 * q.bn * sizeof(float) > q.workspace_bytes) {
                     printf("FAULT %dx%dx%d v%d: slot %d outside the workspace\n", M, N, K, variant, slot);
                     return 1;
                 }
@@ -77,29 +91,37 @@ static int check(int M, int N, int K, int sms, int variant)
                    i % q.kblocks, cover[i]);
             return 1;
         }
-    for (int t = q.dp_tiles; t < q.tiles; ++t) {
-        const long long gf = (long long)(t - q.dp_tiles) * q.kblocks;
-        const int cf = bw::sk_owner(s, gf, P), cl = bw::sk_owner(s, gf + q.kblocks - 1, P);
-        const int expect = cl - cf + 1;
-        const int got = partials.count(t) ? partials[t] : 0;
-        if (expect == 1 ? got != 0 : got != expect) {
-            printf("FAULT %dx%dx%d v%d: stream-K tile %d: %d partials, the reducer expects %d\n", M, N, K, variant, t,
-                   got, expect);
+    for (auto& kv : partials) {
+        const int t = kv.first;
+        std::vector<int> mine = kv.second;
+        std::sort(mine.begin(), mine.end());
+        // the reducer's view: nseg partials, indices 0 .. nseg-1 each written once, slots as the writers used
+        bw::Seg probe = {t, 0, 0, -1};
+        int c0 = -1;
+        for (int c = 0; c < P && c0 < 0; ++c) {
+            bw::SegIter it(s, c, P);
+            bw::Seg sg;
+            while (it.next(s, P, sg))
+                if (sg.tile == t && !(sg.k0 == 0 && sg.k1 == q.kblocks)) {
+                    probe = sg;
+                    c0 = c;
+                    break;
+                }
+        }
+        const bw::Fixup f = bw::fixup_of(s, c0, P, probe);
+        if ((int)mine.size() != f.nseg || (t - q.dp_tiles + 1) * R > q.counters) {
+            printf("FAULT %dx%dx%d v%d: tile %d: %zu partials, the reducer expects %d\n", M, N, K, variant, t,
+                   mine.size(), f.nseg);
             return 1;
         }
-        if (t - q.dp_tiles >= q.counters && expect > 1) {
-            printf("FAULT %dx%dx%d v%d: tile %d has no counter\n", M, N, K, variant, t);
-            return 1;
-        }
-        // the reducer's slots are the writers' slots
-        for (int cc = cf; expect > 1 && cc <= cl; ++cc)
-            if (!slots.count(bw::sk_slot(s, cc, P, t))) {
-                printf("FAULT %dx%dx%d v%d: tile %d reads slot of block %d never written\n", M, N, K, variant, t, cc);
+        for (int i = 0; i < f.nseg; ++i)
+            if (mine[i] != i || !slots.count(bw::fixup_slot(s, P, t, f, i))) {
+                printf("FAULT %dx%dx%d v%d: tile %d partial %d missing\n", M, N, K, variant, t, i);
                 return 1;
             }
     }
-    printf("OK %d %d %d sms %d v%d kernel %d bn %d grid %d dp %d sk %lld\n", M, N, K, sms, variant, q.kernel, q.bn, P,
-           q.dp_tiles, q.sk_iters);
+    printf("OK %d %d %d sms %d v%d kernel %d bn %d grid %d dp %d sk_tiles %d splits %d sk_iters %lld\n", M, N, K, sms,
+           variant, q.kernel, q.bn, P, q.dp_tiles, q.sk_tiles, q.splits, q.sk_iters);
     return 0;
 }
 

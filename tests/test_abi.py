@@ -53,21 +53,25 @@ def test_plan_rule_on_the_judge_shapes():
         p = bwgemm.plan(M, N, K, sms=148)
         if M <= 128:
             assert p["kernel"] == bwgemm.BW_KERNEL_SWAP and p["bn"] == M and p["dp_tiles"] == 0
-            assert p["grid"] == 148 and p["sk_iters"] == p["tiles"] * (K // 64)
+            assert p["grid"] == 148 and p["sk_iters"] == p["tiles"] * (K // 64) and p["splits"] == 0
         else:
-            assert p["kernel"] == bwgemm.BW_KERNEL_TILE and p["bn"] == 256
-            assert p["tiles"] == -(-M // 128) * -(-N // 256)
+            assert p["kernel"] == bwgemm.BW_KERNEL_PAIR and p["bn"] == 256 and p["grid"] % 2 == 0
+            assert p["tiles"] == -(-M // 256) * -(-N // 256)
         assert p["smem_bytes"] <= 227 * 1024 and p["tmem_cols"] <= 512 and p["stages"] >= 4
         assert p["sk_iters"] == 0 or p["sk_iters"] >= p["grid"]
 
 
 def test_plan_variants_take_out_one_mechanism():
     assert bwgemm.plan(16, 8192, 8192, variant=1)["sk_iters"] == 0          # no stream-K
-    assert bwgemm.plan(16, 8192, 8192, variant=2)["kernel"] == bwgemm.BW_KERNEL_TILE  # no swap-AB
+    assert bwgemm.plan(16, 8192, 8192, variant=2)["kernel"] == bwgemm.BW_KERNEL_PAIR  # no swap-AB
+    assert bwgemm.plan(512, 8192, 8192, variant=5)["kernel"] == bwgemm.BW_KERNEL_TILE  # no SM pair
     assert bwgemm.plan(8192, 8192, 8192, variant=3)["group_rows"] == 0      # row order
-    assert bwgemm.plan(8192, 8192, 8192, variant=4)["dp_tiles"] == 0        # stream-K everywhere
+    v4 = bwgemm.plan(8192, 8192, 8192, variant=4)                           # stream-K tail in place of split-K
+    assert v4["splits"] == 0 and v4["sk_iters"] == v4["sk_tiles"] * 128 >= 0
+    v0 = bwgemm.plan(4608, 5632, 8192)                                       # config 1: a split-K tail
+    assert v0["splits"] > 1 and v0["dp_tiles"] + v0["sk_tiles"] == v0["tiles"] and v0["sk_iters"] == 0
     with pytest.raises(bwgemm.BwError):
-        bwgemm.plan(16, 64, 64, variant=5)
+        bwgemm.plan(16, 64, 64, variant=6)
 
 
 @pytest.mark.skipif(shutil.which("nvcc") is None, reason="nvcc")

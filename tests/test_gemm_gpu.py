@@ -1,7 +1,8 @@
 """Parity of the sm_100a path with the oracle, through the C ABI, on a B200.
 
 - The reference's own fixtures (tests/golden, dumped from its Hopper emulator): the same inputs, and C within the
-  per-element bound of the fp64 reference; the reference kernel's C and ours within 4 fp16 ulp of each other.
+  per-element bound of the fp64 reference; the reference kernel's C and ours within twice that bound of each other,
+  and most elements bit-identical.
 - The reference's 26 verif shapes (hopper/verif.cu:158-163) on its LCG inputs, every variant: per element
   |C - ref16| <= 2 ulp16(|ref16|) + 1e-3 sqrt(K) and normwise <= 2e-3 against the fp64 oracle, 8 calls compared bit for
   bit (hopper/verif.cu:197-215), the stream-K counters back at zero (candidate_dirty, :216-222).
@@ -105,10 +106,16 @@ def test_golden_reference_fixtures(path, oracle_mod):
     for v in range(bwgemm.lib().bw_gemm_variant_count()):
         C = bits(run(to_dev(A), to_dev(B), variant=v))
         assert_parity(C, ref, K, oracle_mod, f"{path} v{v}")
+        # ours and the reference kernel's C: each within the bound of the fp64 result, so within twice the bound of
+        # each other (both round fp32 sums of a different order; near zero that is many ulp of the value itself)
         ours = C.view(np.float16).astype(np.float64)
         theirs = g["c"].view(np.float16).astype(np.float64)
-        ulp = np.array([oracle_mod.lib().oracle_ulp16(float(x)) for x in np.abs(theirs).ravel()]).reshape(theirs.shape)
-        assert np.all(np.abs(ours - theirs) <= 4 * ulp), f"v{v}: more than 4 ulp from the reference kernel's C"
+        L = oracle_mod.lib()
+        bound = np.array([2 * L.oracle_ulp16(float(x)) for x in np.abs(theirs).ravel()]).reshape(theirs.shape)
+        bound += 1e-3 * np.sqrt(K)
+        assert np.all(np.abs(ours - theirs) <= 2 * bound), f"v{v}: farther from the reference kernel's C than 2 bounds"
+        same = np.mean(C == g["c"])
+        assert same > 0.5, f"v{v}: only {same:.1%} of C bit-identical to the reference kernel's"
 
 
 @pytest.mark.parametrize("shape", VERIF, ids=lambda s: "x".join(map(str, s)))
