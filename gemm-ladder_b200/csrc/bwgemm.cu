@@ -340,8 +340,107 @@ BW_API const char* bw_status_string(int status)
     case BW_ERR_TIMEOUT: return "a bounded wait on a barrier gave up (see bw_gemm_status)";
     case BW_ERR_ARG: return "bad argument (null or misaligned pointer, unknown variant)";
     case BW_ERR_DEVICE: return "the current device is not an sm_100 GPU";
+    case BW_ERR_SCRATCH: return "the call needs more scratch than the no-allocation entry's fixed array holds";
     default: return "unknown status";
     }
 }
 
 BW_API const char* bw_last_error_string(void) { return bw::g_errbuf; }
+
+// ------------------------------------------------------------------ the entry point that allocates nothing
+// For callers that may not call cudaMalloc (see bw_gemm_f16_noalloc in bwgemm.h): the scratch of split tiles lives in
+// one fixed array compiled into this library.  In host code `g_bw_noalloc_scratch` only names the array; the kernel
+// gets its device address, looked up once per device with cudaGetSymbolAddress.
+static __device__ __align__(256) unsigned char g_bw_noalloc_scratch[BW_NOALLOC_SCRATCH_BYTES + 4 * BW_NOALLOC_COUNTERS];
+
+namespace bw {
+namespace {
+void* g_noalloc_addr[kMaxDevices];  // the array's device address per device, 0 until the first call there
+
+int noalloc_gemm(const void* A, const void* B, void* C, int M, int N, int K, cudaStream_t st)
+{
+    if (!shape_ok(M, N, K)) return BW_ERR_SHAPE;
+    if (!A || !B || !C || (reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(B) |
+                           reinterpret_cast<uintptr_t>(C)) % 16)
+        return BW_ERR_ARG;
+    DeviceState* d = nullptr;
+    int rc = device_state(&d);
+    if (rc) return rc;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+    bw_plan q;
+    void* scratch = nullptr;
+    {
+        std::lock_guard<std::mutex> lock(g_mu);
+        if ((rc = pair_occupancy(*d))) return rc;
+        if ((rc = make_plan(M, N, K, d->sms, d->pairs, 0, &q))) return rc;
+        if (q.workspace_bytes > BW_NOALLOC_SCRATCH_BYTES || (unsigned)q.counters > BW_NOALLOC_COUNTERS) {
+            snprintf(g_errbuf, sizeof g_errbuf,
+                     "%d x %d x %d needs %zu bytes of partials and %d counters; the fixed array holds %u and %u", M, N,
+                     K, q.workspace_bytes, q.counters, BW_NOALLOC_SCRATCH_BYTES, BW_NOALLOC_COUNTERS);
+            return BW_ERR_SCRATCH;
+        }
+        if (!g_noalloc_addr[dev]) {  // once per device, this device current
+            void* ptr = nullptr;
+            if ((e = cudaGetSymbolAddress(&ptr, g_bw_noalloc_scratch)) != cudaSuccess)
+                return cuda_fail(e, "cudaGetSymbolAddress (no-allocation scratch)");
+            g_noalloc_addr[dev] = ptr;
+        }
+        scratch = g_noalloc_addr[dev];
+    }
+    float* work = static_cast<float*>(scratch);
+    int* counters = reinterpret_cast<int*>(static_cast<unsigned char*>(scratch) + BW_NOALLOC_SCRATCH_BYTES);
+    // the counters must start at zero; the array keeps whatever the last call left (a call that gave up part-way
+    // may leave some set)
+    if (q.counters > 0 && (e = cudaMemsetAsync(counters, 0, (size_t)q.counters * sizeof(int), st)) != cudaSuccess)
+        return cuda_fail(e, "cudaMemsetAsync (no-allocation counters)");
+    CUtensorMap mx, my;
+    bool ok;
+    if (q.kernel == BW_KERNEL_TILE || q.kernel == BW_KERNEL_PAIR)
+        ok = make_map(&mx, A, K, M, 64, 128) && make_map(&my, B, N, K, 64, 64);
+    else
+        ok = make_map(&mx, B, N, K, 64, 64) && make_map(&my, A, K, M, 64, q.bn);
+    if (!ok) {
+        snprintf(g_errbuf, sizeof g_errbuf, "cuTensorMapEncodeTiled failed");
+        return BW_ERR_LAUNCH;
+    }
+    Params p;
+    p.s.M = M;
+    p.s.N = N;
+    p.s.K = K;
+    p.s.tiles_m = q.tiles_m;
+    p.s.tiles_n = q.tiles_n;
+    p.s.tiles = q.tiles;
+    p.s.kblocks = q.kblocks;
+    p.s.dp_tiles = q.dp_tiles;
+    p.s.sk_tiles = q.sk_tiles;
+    p.s.splits = q.splits;
+    p.s.sk_iters = q.sk_iters;
+    p.s.group_rows = q.group_rows;
+    p.C = static_cast<__half*>(C);
+    p.work = work;
+    p.counters = counters;
+    p.wait_ns = g_wait_ns;
+    if (q.kernel == BW_KERNEL_PAIR) return launch_kernel<256, false, true>(*d, kBitPair, q, mx, my, p, st);
+    if (q.kernel == BW_KERNEL_TILE) return launch_kernel<256, false, false>(*d, 1u << 0, q, mx, my, p, st);
+    switch (q.bn) {
+    case 16: return launch_kernel<16, true, false>(*d, 1u << 1, q, mx, my, p, st);
+    case 32: return launch_kernel<32, true, false>(*d, 1u << 2, q, mx, my, p, st);
+    case 48: return launch_kernel<48, true, false>(*d, 1u << 3, q, mx, my, p, st);
+    case 64: return launch_kernel<64, true, false>(*d, 1u << 4, q, mx, my, p, st);
+    case 80: return launch_kernel<80, true, false>(*d, 1u << 5, q, mx, my, p, st);
+    case 96: return launch_kernel<96, true, false>(*d, 1u << 6, q, mx, my, p, st);
+    case 112: return launch_kernel<112, true, false>(*d, 1u << 7, q, mx, my, p, st);
+    case 128: return launch_kernel<128, true, false>(*d, 1u << 8, q, mx, my, p, st);
+    default: return BW_ERR_ARG;
+    }
+}
+
+}  // namespace
+}  // namespace bw
+
+BW_API int bw_gemm_f16_noalloc(const void* A, const void* B, void* C, int M, int N, int K, void* stream)
+{
+    return bw::noalloc_gemm(A, B, C, M, N, K, static_cast<cudaStream_t>(stream));
+}

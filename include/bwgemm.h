@@ -25,6 +25,7 @@ extern "C" {
 #define BW_ERR_TIMEOUT 3   /* a kernel's bounded wait on a barrier gave up; see bw_gemm_status */
 #define BW_ERR_ARG 4       /* null or misaligned pointer, unknown variant */
 #define BW_ERR_DEVICE 5    /* the current device is not an sm_100 (B200-class) GPU */
+#define BW_ERR_SCRATCH 6   /* bw_gemm_f16_noalloc: the call needs more scratch than its fixed array holds */
 
 /* Kernels of the rule (bw_plan.kernel). */
 #define BW_KERNEL_TILE 0   /* 128 x bn tiles of C, A as the MMA's A operand */
@@ -61,6 +62,25 @@ const char* bw_gemm_variant_name(int v);
  * Replaces: the weak `int candidate_dirty()` (hopper/verif.cu:41, :216-222; ampere/step7.cu:277-292).
  */
 int bw_gemm_dirty(void);
+
+/*
+ * C = A B like bw_gemm_f16, for callers that cannot allocate device memory: a serving process whose memory is all
+ * handed out up front by its own allocator (a cudaMalloc there would take memory outside its budget, and the first one
+ * can stall every stream of the device), or a plugin that runs inside someone else's process and may not call
+ * cudaMalloc / cudaFree at all.  No reference counterpart: the reference's candidates allocate their workspace at the
+ * first call of a shape.
+ *
+ * The scratch this call needs (the fp32 partials and counters of tiles split over several SMs) lives in one fixed
+ * array of BW_NOALLOC_SCRATCH_BYTES + 4 * BW_NOALLOC_COUNTERS bytes, compiled into the library: every GPU that loads
+ * the library holds it until the process exits.  The first call on a device looks up that array's device address
+ * (once, with the device current); make that first call before any stream capture.  Calls never allocate or free.
+ * A call whose plan needs more scratch than the array holds is refused with BW_ERR_SCRATCH before anything runs.
+ * Every call shares the one array and clears the counters it uses on its stream first: two calls that overlap on
+ * the GPU (different streams, or several host threads) race on it; order them, or use bw_gemm_f16.
+ */
+#define BW_NOALLOC_SCRATCH_BYTES (20u << 20) /* fp32 partials: 20 MiB */
+#define BW_NOALLOC_COUNTERS 4096u            /* split-tile counters */
+int bw_gemm_f16_noalloc(const void* A, const void* B, void* C, int M, int N, int K, void* stream);
 
 /* The plan of one call: the kernel, its tile and its schedule (host only, no GPU needed). */
 typedef struct bw_plan {

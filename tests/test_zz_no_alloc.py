@@ -1,0 +1,101 @@
+"""The entry point that allocates nothing (bw_gemm_f16_noalloc), on a B200, through the C ABI.
+
+Callers such as a serving process whose device memory is all owned by its own allocator, or a plugin inside someone
+else's process, may not call cudaMalloc; this entry point keeps the scratch of split tiles in a fixed array compiled
+into the library.  Checked here: two calls in a row give the same C as bw_gemm_f16 within the per-element bound the
+other tests use (2 ulp16 of the reference value + 1e-3 sqrt(K)), on shapes whose plan splits tiles (stream-K at
+M <= 128, a split-K tail on the SM pairs) and on one that splits none; and a call needing more scratch than the array
+holds is refused with BW_ERR_SCRATCH.  This file is collected last, and passes alone in a fresh process too.
+"""
+import ctypes
+import os
+import re
+
+import pytest
+
+torch = pytest.importorskip("torch")
+
+import bwgemm  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+
+BW_ERR_SCRATCH = 6
+
+
+def header_constant(name):
+    with open(bwgemm.HEADER) as f:
+        m = re.search(r"#define\s+%s\s+\((\d+)u\s*<<\s*(\d+)\)|#define\s+%s\s+(\d+)u" % (name, name), f.read())
+    return int(m.group(1)) << int(m.group(2)) if m.group(1) else int(m.group(3))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    torch.cuda.set_device(0)
+    L = bwgemm.lib()
+    L.bw_gemm_f16_noalloc.argtypes = [ctypes.c_void_p] * 3 + [ctypes.c_int] * 3 + [ctypes.c_void_p]
+    L.bw_gemm_f16_noalloc.restype = ctypes.c_int
+    return L
+
+
+def inputs(M, N, K, seed):
+    g = torch.Generator(device="cuda")
+    g.manual_seed(seed)
+    A = (torch.rand((M, K), generator=g, device="cuda") * 2 - 1).half()
+    B = (torch.rand((K, N), generator=g, device="cuda") * 2 - 1).half()
+    return A, B
+
+
+def within_bound(C, ref, K):
+    """|C - ref| <= 2 ulp16(|ref|) + 1e-3 sqrt(K), element by element (ref: the allocating entry's fp16 result)."""
+    r = ref.float().abs()
+    mant, exp = torch.frexp(r)  # r = mant * 2^exp, mant in [0.5, 1): ulp16 = 2^(exp - 11) for normal halves
+    ulp = torch.where(r < 2.0 ** -14, torch.full_like(r, 2.0 ** -24), torch.ldexp(torch.ones_like(r), exp - 11))
+    bound = 2 * ulp + 1e-3 * K ** 0.5
+    diff = (C.float() - ref.float()).abs()
+    return bool(torch.isfinite(C.float()).all()) and bool((diff <= bound).all())
+
+
+# stream-K on the swap-AB kernel (bn 16 and bn 128, the largest scratch of the judge's shapes), a split-K tail on
+# the SM pairs, whole tiles only (no scratch used)
+SHAPES = [(16, 8192, 8192), (128, 10240, 8192), (4608, 5632, 8192), (512, 8192, 8192), (272, 5376, 128)]
+
+
+@pytest.mark.parametrize("shape", SHAPES, ids=lambda s: "x".join(map(str, s)))
+def test_noalloc_agrees_with_the_allocating_entry(lib, shape):
+    M, N, K = shape
+    A, B = inputs(M, N, K, seed=M + N + K)
+    stream = torch.cuda.current_stream().cuda_stream
+    ref = torch.empty((M, N), dtype=torch.float16, device="cuda")
+    assert bwgemm.gemm_ptr(A.data_ptr(), B.data_ptr(), ref.data_ptr(), M, N, K, stream) == 0
+    torch.cuda.synchronize()
+    for call in range(2):  # two calls in a row: the second finds what the first left in the shared array
+        C = torch.empty((M, N), dtype=torch.float16, device="cuda")
+        C.view(torch.int16).fill_(-1)  # NaN: an element left unwritten shows
+        rc = lib.bw_gemm_f16_noalloc(A.data_ptr(), B.data_ptr(), C.data_ptr(), M, N, K, stream)
+        torch.cuda.synchronize()
+        assert rc == 0, f"call {call}: {lib.bw_status_string(rc).decode()}: {lib.bw_last_error_string().decode()}"
+        assert bwgemm.status()[0] == 0
+        assert within_bound(C, ref, K), f"call {call}: C differs from bw_gemm_f16's beyond the bound"
+
+
+def test_noalloc_refuses_a_call_beyond_its_array(lib):
+    limit = header_constant("BW_NOALLOC_SCRATCH_BYTES")
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    big = None
+    for M in (256, 512):
+        for N in range(256, 16385, 256):
+            if bwgemm.plan(M, N, 8192, sms=sms)["workspace_bytes"] > limit:
+                big = (M, N, 8192)
+                break
+        if big:
+            break
+    assert big, "no shape found whose plan needs more scratch than the array"
+    M, N, K = big
+    A, B = inputs(M, N, K, seed=1)
+    C = torch.empty((M, N), dtype=torch.float16, device="cuda")
+    rc = lib.bw_gemm_f16_noalloc(A.data_ptr(), B.data_ptr(), C.data_ptr(), M, N, K,
+                                 torch.cuda.current_stream().cuda_stream)
+    assert rc == BW_ERR_SCRATCH
+    assert "fixed array" in lib.bw_last_error_string().decode()
