@@ -50,6 +50,7 @@ def parse():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="config1")
+    ap.add_argument("--shape", default=None, help="MxNxK in place of the workload (profiling a shape)")
     ap.add_argument("--variant", type=int, default=0)
     ap.add_argument("--sweep", action="store_true", help="also time the judge's 17 shapes against cuBLAS")
     ap.add_argument("--no-e2e", action="store_true")
@@ -403,6 +404,10 @@ def run_reference(args):
 
 def main():
     args = parse()
+    if args.shape:
+        M, N, K = (int(x) for x in args.shape.lower().split("x"))
+        WORKLOADS[args.shape] = (M, N, K)
+        args.workload = args.shape
     if args.impl == "reference":
         run_reference(args)
     else:

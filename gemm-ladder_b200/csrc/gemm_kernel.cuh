@@ -27,6 +27,7 @@
 #pragma once
 #include <cuda.h>
 #include <cuda_fp16.h>
+#include "plan.h"
 #include "ptx.cuh"
 #include "schedule.h"
 
@@ -53,7 +54,7 @@ struct Geom {
     static constexpr int kXBytes = 128 * kBK * 2;            // this block's MMA-A operand: 128 rows x 64 K
     static constexpr int kYBytes = (BN / kRanks) * kBK * 2;  // this block's MMA-B operand: BN (PAIR: BN / 2) x 64 K
     static constexpr int kStageBytes = kXBytes + kYBytes;
-    static constexpr int kStages = (204800 / kStageBytes) < 12 ? (204800 / kStageBytes) : 12;
+    static constexpr int kStages = (BW_RING_BYTES / kStageBytes) < BW_MAX_STAGES ? (BW_RING_BYTES / kStageBytes) : BW_MAX_STAGES;
     static constexpr int kTmemCols = pow2_at_least(2 * BN < 32 ? 32 : 2 * BN, 32);  // two accumulators
     static constexpr int kBarOffset = kStages * kStageBytes;
     static constexpr int kNumBars = 2 * kStages + 5;  // full, empty, tmem full x2, tmem empty x2, drain

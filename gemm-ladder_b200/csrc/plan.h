@@ -16,6 +16,20 @@
 #include "bwgemm.h"
 #include "schedule.h"
 
+// Tuning constants (compile-time; measured on the B200, see the profiles).
+#ifndef BW_GROUP_ROWS
+#define BW_GROUP_ROWS 16       // rows of tiles per serpentine group
+#endif
+#ifndef BW_FIXUP_KB
+#define BW_FIXUP_KB 12.0       // the cost of one extra partial of a 256-column tile, in K-blocks of MMA work
+#endif
+#ifndef BW_RING_BYTES
+#define BW_RING_BYTES 204800   // shared memory for the ring of stages
+#endif
+#ifndef BW_MAX_STAGES
+#define BW_MAX_STAGES 12
+#endif
+
 namespace bw {
 
 constexpr int kVariants = 6;
@@ -36,8 +50,8 @@ inline const char* variant_name(int v)
 inline int plan_stage_bytes(int bn, int ranks) { return 128 * 64 * 2 + (bn / ranks) * 64 * 2; }
 inline int plan_stages(int bn, int ranks)
 {
-    const int s = 204800 / plan_stage_bytes(bn, ranks);
-    return s < 12 ? s : 12;
+    const int s = BW_RING_BYTES / plan_stage_bytes(bn, ranks);
+    return s < BW_MAX_STAGES ? s : BW_MAX_STAGES;
 }
 inline int plan_tmem_cols(int bn)
 {
@@ -95,7 +109,7 @@ inline int make_plan(int M, int N, int K, int sms, int pairs, int variant, bw_pl
         units = pair ? pairs : sms;
         q.tiles_m = (M + 128 * ranks - 1) / (128 * ranks);
         q.tiles_n = (N + 255) / 256;
-        q.group_rows = variant == 3 ? 0 : 16;
+        q.group_rows = variant == 3 ? 0 : BW_GROUP_ROWS;
     }
     q.tiles = q.tiles_m * q.tiles_n;
     const long long kb = q.kblocks;
@@ -111,7 +125,7 @@ inline int make_plan(int M, int N, int K, int sms, int pairs, int variant, bw_pl
     } else {
         // split-K over the partial wave, if it pays
         const int tail = q.tiles % units;
-        const int sp = tail_splits(tail, units, q.kblocks, /*fixup_kb=*/12.0 * q.bn / 256);
+        const int sp = tail_splits(tail, units, q.kblocks, /*fixup_kb=*/BW_FIXUP_KB * q.bn / 256);
         if (sp > 1) {
             q.dp_tiles = q.tiles - tail;
             q.sk_tiles = tail;
