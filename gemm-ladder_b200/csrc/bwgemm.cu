@@ -115,26 +115,28 @@ int device_state(DeviceState** out)
     return BW_OK;
 }
 
-// The workspace and counters a plan needs; grown (never shrunk) at the first call that needs more.
+// The workspace and counters a plan needs, grown at the first call that needs more.  A buffer that is outgrown is
+// never freed: a CUDA graph captured earlier still holds its address and may be replayed at any time (freeing it
+// would turn that replay into writes to freed memory).  Growth is at least 2x, so only a few buffers are ever kept;
+// all of them go with the context at exit.
 int ensure_workspace(DeviceState& d, const bw_plan& q, cudaStream_t st)
 {
     cudaError_t e;
     if (q.workspace_bytes > d.work_bytes) {
-        if (d.work) cudaFree(d.work);
-        d.work = nullptr;
-        d.work_bytes = 0;
-        if ((e = cudaMalloc(&d.work, q.workspace_bytes)) != cudaSuccess) return cuda_fail(e, "cudaMalloc (workspace)");
-        d.work_bytes = q.workspace_bytes;
+        size_t bytes = d.work_bytes * 2 > q.workspace_bytes ? d.work_bytes * 2 : q.workspace_bytes;
+        float* w = nullptr;
+        if ((e = cudaMalloc(&w, bytes)) != cudaSuccess) return cuda_fail(e, "cudaMalloc (workspace)");
+        d.work = w;  // the outgrown buffer stays allocated
+        d.work_bytes = bytes;
     }
     if (q.counters > d.n_counters) {
-        if (d.counters) cudaFree(d.counters);
-        d.counters = nullptr;
-        d.n_counters = 0;
-        const int n = q.counters < 1024 ? 1024 : q.counters;
-        if ((e = cudaMalloc(&d.counters, (size_t)n * sizeof(int))) != cudaSuccess)
-            return cuda_fail(e, "cudaMalloc (counters)");
-        if ((e = cudaMemsetAsync(d.counters, 0, (size_t)n * sizeof(int), st)) != cudaSuccess)
+        int n = d.n_counters * 2 > q.counters ? d.n_counters * 2 : q.counters;
+        if (n < 1024) n = 1024;
+        int* c = nullptr;
+        if ((e = cudaMalloc(&c, (size_t)n * sizeof(int))) != cudaSuccess) return cuda_fail(e, "cudaMalloc (counters)");
+        if ((e = cudaMemsetAsync(c, 0, (size_t)n * sizeof(int), st)) != cudaSuccess)
             return cuda_fail(e, "cudaMemsetAsync (counters)");
+        d.counters = c;  // the outgrown array stays allocated (and at zero)
         d.n_counters = n;
     }
     return BW_OK;
@@ -204,6 +206,64 @@ int launch_kernel(DeviceState& d, unsigned bit, const bw_plan& q, const CUtensor
     return BW_OK;
 }
 
+// The plan's kernel instance, launched.
+int dispatch(DeviceState& d, const bw_plan& q, const CUtensorMap& mx, const CUtensorMap& my, const Params& p,
+             cudaStream_t st)
+{
+    if (q.kernel == BW_KERNEL_PAIR) return launch_kernel<256, false, true>(d, kBitPair, q, mx, my, p, st);
+    if (q.kernel == BW_KERNEL_TILE) {
+        switch (q.bn) {
+        case 64: return launch_kernel<64, false, false>(d, 1u << 10, q, mx, my, p, st);
+        case 128: return launch_kernel<128, false, false>(d, 1u << 11, q, mx, my, p, st);
+        case 256: return launch_kernel<256, false, false>(d, 1u << 0, q, mx, my, p, st);
+        default: return BW_ERR_ARG;
+        }
+    }
+    switch (q.bn) {
+    case 16: return launch_kernel<16, true, false>(d, 1u << 1, q, mx, my, p, st);
+    case 32: return launch_kernel<32, true, false>(d, 1u << 2, q, mx, my, p, st);
+    case 48: return launch_kernel<48, true, false>(d, 1u << 3, q, mx, my, p, st);
+    case 64: return launch_kernel<64, true, false>(d, 1u << 4, q, mx, my, p, st);
+    case 80: return launch_kernel<80, true, false>(d, 1u << 5, q, mx, my, p, st);
+    case 96: return launch_kernel<96, true, false>(d, 1u << 6, q, mx, my, p, st);
+    case 112: return launch_kernel<112, true, false>(d, 1u << 7, q, mx, my, p, st);
+    case 128: return launch_kernel<128, true, false>(d, 1u << 8, q, mx, my, p, st);
+    default: return BW_ERR_ARG;
+    }
+}
+
+// The kernel parameters of a plan.
+Params make_params(const bw_plan& q, int M, int N, int K, void* C, float* work, int* counters)
+{
+    Params p;
+    p.s.M = M;
+    p.s.N = N;
+    p.s.K = K;
+    p.s.tiles_m = q.tiles_m;
+    p.s.tiles_n = q.tiles_n;
+    p.s.tiles = q.tiles;
+    p.s.kblocks = q.kblocks;
+    p.s.dp_tiles = q.dp_tiles;
+    p.s.sk_tiles = q.sk_tiles;
+    p.s.splits = q.splits;
+    p.s.sk_iters = q.sk_iters;
+    p.s.group_rows = q.group_rows;
+    p.C = static_cast<__half*>(C);
+    p.work = work;
+    p.counters = counters;
+    p.wait_ns = g_wait_ns;
+    return p;
+}
+
+// The two tensor maps of a plan: TILE and PAIR read A (K-major) and B (MN-major) in that role order; SWAP the
+// other way round.
+bool make_maps(const bw_plan& q, const void* A, const void* B, int M, int N, int K, CUtensorMap* mx, CUtensorMap* my)
+{
+    if (q.kernel == BW_KERNEL_TILE || q.kernel == BW_KERNEL_PAIR)
+        return make_map(mx, A, K, M, 64, 128) && make_map(my, B, N, K, 64, 64);
+    return make_map(mx, B, N, K, 64, 64) && make_map(my, A, K, M, 64, q.bn);
+}
+
 int gemm(const void* A, const void* B, void* C, int M, int N, int K, cudaStream_t st, int variant)
 {
     if (variant < 0 || variant >= kVariants) return BW_ERR_ARG;
@@ -222,45 +282,11 @@ int gemm(const void* A, const void* B, void* C, int M, int N, int K, cudaStream_
         if ((rc = ensure_workspace(*d, q, st))) return rc;
     }
     CUtensorMap mx, my;
-    bool ok;
-    if (q.kernel == BW_KERNEL_TILE || q.kernel == BW_KERNEL_PAIR)
-        ok = make_map(&mx, A, K, M, 64, 128) && make_map(&my, B, N, K, 64, 64);
-    else
-        ok = make_map(&mx, B, N, K, 64, 64) && make_map(&my, A, K, M, 64, q.bn);
-    if (!ok) {
+    if (!make_maps(q, A, B, M, N, K, &mx, &my)) {
         snprintf(g_errbuf, sizeof g_errbuf, "cuTensorMapEncodeTiled failed");
         return BW_ERR_LAUNCH;
     }
-    Params p;
-    p.s.M = M;
-    p.s.N = N;
-    p.s.K = K;
-    p.s.tiles_m = q.tiles_m;
-    p.s.tiles_n = q.tiles_n;
-    p.s.tiles = q.tiles;
-    p.s.kblocks = q.kblocks;
-    p.s.dp_tiles = q.dp_tiles;
-    p.s.sk_tiles = q.sk_tiles;
-    p.s.splits = q.splits;
-    p.s.sk_iters = q.sk_iters;
-    p.s.group_rows = q.group_rows;
-    p.C = static_cast<__half*>(C);
-    p.work = d->work;
-    p.counters = d->counters;
-    p.wait_ns = g_wait_ns;
-    if (q.kernel == BW_KERNEL_PAIR) return launch_kernel<256, false, true>(*d, kBitPair, q, mx, my, p, st);
-    if (q.kernel == BW_KERNEL_TILE) return launch_kernel<256, false, false>(*d, 1u << 0, q, mx, my, p, st);
-    switch (q.bn) {
-    case 16: return launch_kernel<16, true, false>(*d, 1u << 1, q, mx, my, p, st);
-    case 32: return launch_kernel<32, true, false>(*d, 1u << 2, q, mx, my, p, st);
-    case 48: return launch_kernel<48, true, false>(*d, 1u << 3, q, mx, my, p, st);
-    case 64: return launch_kernel<64, true, false>(*d, 1u << 4, q, mx, my, p, st);
-    case 80: return launch_kernel<80, true, false>(*d, 1u << 5, q, mx, my, p, st);
-    case 96: return launch_kernel<96, true, false>(*d, 1u << 6, q, mx, my, p, st);
-    case 112: return launch_kernel<112, true, false>(*d, 1u << 7, q, mx, my, p, st);
-    case 128: return launch_kernel<128, true, false>(*d, 1u << 8, q, mx, my, p, st);
-    default: return BW_ERR_ARG;
-    }
+    return dispatch(*d, q, mx, my, make_params(q, M, N, K, C, d->work, d->counters), st);
 }
 
 }  // namespace
@@ -396,45 +422,11 @@ int noalloc_gemm(const void* A, const void* B, void* C, int M, int N, int K, cud
     if (q.counters > 0 && (e = cudaMemsetAsync(counters, 0, (size_t)q.counters * sizeof(int), st)) != cudaSuccess)
         return cuda_fail(e, "cudaMemsetAsync (no-allocation counters)");
     CUtensorMap mx, my;
-    bool ok;
-    if (q.kernel == BW_KERNEL_TILE || q.kernel == BW_KERNEL_PAIR)
-        ok = make_map(&mx, A, K, M, 64, 128) && make_map(&my, B, N, K, 64, 64);
-    else
-        ok = make_map(&mx, B, N, K, 64, 64) && make_map(&my, A, K, M, 64, q.bn);
-    if (!ok) {
+    if (!make_maps(q, A, B, M, N, K, &mx, &my)) {
         snprintf(g_errbuf, sizeof g_errbuf, "cuTensorMapEncodeTiled failed");
         return BW_ERR_LAUNCH;
     }
-    Params p;
-    p.s.M = M;
-    p.s.N = N;
-    p.s.K = K;
-    p.s.tiles_m = q.tiles_m;
-    p.s.tiles_n = q.tiles_n;
-    p.s.tiles = q.tiles;
-    p.s.kblocks = q.kblocks;
-    p.s.dp_tiles = q.dp_tiles;
-    p.s.sk_tiles = q.sk_tiles;
-    p.s.splits = q.splits;
-    p.s.sk_iters = q.sk_iters;
-    p.s.group_rows = q.group_rows;
-    p.C = static_cast<__half*>(C);
-    p.work = work;
-    p.counters = counters;
-    p.wait_ns = g_wait_ns;
-    if (q.kernel == BW_KERNEL_PAIR) return launch_kernel<256, false, true>(*d, kBitPair, q, mx, my, p, st);
-    if (q.kernel == BW_KERNEL_TILE) return launch_kernel<256, false, false>(*d, 1u << 0, q, mx, my, p, st);
-    switch (q.bn) {
-    case 16: return launch_kernel<16, true, false>(*d, 1u << 1, q, mx, my, p, st);
-    case 32: return launch_kernel<32, true, false>(*d, 1u << 2, q, mx, my, p, st);
-    case 48: return launch_kernel<48, true, false>(*d, 1u << 3, q, mx, my, p, st);
-    case 64: return launch_kernel<64, true, false>(*d, 1u << 4, q, mx, my, p, st);
-    case 80: return launch_kernel<80, true, false>(*d, 1u << 5, q, mx, my, p, st);
-    case 96: return launch_kernel<96, true, false>(*d, 1u << 6, q, mx, my, p, st);
-    case 112: return launch_kernel<112, true, false>(*d, 1u << 7, q, mx, my, p, st);
-    case 128: return launch_kernel<128, true, false>(*d, 1u << 8, q, mx, my, p, st);
-    default: return BW_ERR_ARG;
-    }
+    return dispatch(*d, q, mx, my, make_params(q, M, N, K, C, work, counters), st);
 }
 
 }  // namespace

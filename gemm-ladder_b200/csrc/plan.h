@@ -32,7 +32,7 @@
 
 namespace bw {
 
-constexpr int kVariants = 6;
+constexpr int kVariants = 8;
 inline const char* variant_name(int v)
 {
     switch (v) {
@@ -42,6 +42,8 @@ inline const char* variant_name(int v)
     case 3: return "v3: without the serpentine order (tiles row after row)";
     case 4: return "v4: stream-K in place of the split-K tail";
     case 5: return "v5: without the SM pair (128x256 tiles on single SMs)";
+    case 6: return "v6: 128x64 tiles on single SMs at every M (no swap-AB, no pair)";
+    case 7: return "v7: 128x128 tiles on single SMs at every M (no swap-AB, no pair)";
     default: return nullptr;
     }
 }
@@ -93,8 +95,8 @@ inline int make_plan(int M, int N, int K, int sms, int pairs, int variant, bw_pl
     if (!shape_ok(M, N, K)) return BW_ERR_SHAPE;
     bw_plan q = {};
     q.kblocks = K / 64;
-    const bool swap = M <= 128 && variant != 2;
-    const bool pair = !swap && variant != 5 && pairs > 0;
+    const bool swap = M <= 128 && variant != 2 && variant < 6;
+    const bool pair = !swap && variant != 5 && variant < 6 && pairs > 0;
     int ranks = 1, units = sms;  // the blocks (or pairs) of the persistent grid
     if (swap) {
         q.kernel = BW_KERNEL_SWAP;
@@ -104,11 +106,11 @@ inline int make_plan(int M, int N, int K, int sms, int pairs, int variant, bw_pl
         q.group_rows = 0;
     } else {
         q.kernel = pair ? BW_KERNEL_PAIR : BW_KERNEL_TILE;
-        q.bn = 256;
+        q.bn = variant == 6 ? 64 : variant == 7 ? 128 : 256;
         ranks = pair ? 2 : 1;
         units = pair ? pairs : sms;
         q.tiles_m = (M + 128 * ranks - 1) / (128 * ranks);
-        q.tiles_n = (N + 255) / 256;
+        q.tiles_n = (N + q.bn - 1) / q.bn;
         q.group_rows = variant == 3 ? 0 : BW_GROUP_ROWS;
     }
     q.tiles = q.tiles_m * q.tiles_n;

@@ -29,7 +29,7 @@ def test_only_the_abi_is_exported():
 
 def test_status_strings_and_variants():
     L = bwgemm.lib()
-    for st in range(6):
+    for st in range(7):
         assert L.bw_status_string(st)
     assert L.bw_gemm_variant_count() == len(bwgemm.variants()) >= 5
     assert L.bw_gemm_variant_name(-1) is None
@@ -66,12 +66,15 @@ def test_plan_variants_take_out_one_mechanism():
     assert bwgemm.plan(16, 8192, 8192, variant=2)["kernel"] == bwgemm.BW_KERNEL_PAIR  # no swap-AB
     assert bwgemm.plan(512, 8192, 8192, variant=5)["kernel"] == bwgemm.BW_KERNEL_TILE  # no SM pair
     assert bwgemm.plan(8192, 8192, 8192, variant=3)["group_rows"] == 0      # row order
+    v6, v7 = bwgemm.plan(16, 8192, 8192, variant=6), bwgemm.plan(16, 8192, 8192, variant=7)
+    assert (v6["kernel"], v6["bn"], v6["tiles"]) == (bwgemm.BW_KERNEL_TILE, 64, 128)
+    assert (v7["kernel"], v7["bn"], v7["tiles"]) == (bwgemm.BW_KERNEL_TILE, 128, 64)
     v4 = bwgemm.plan(8192, 8192, 8192, variant=4)                           # stream-K tail in place of split-K
     assert v4["splits"] == 0 and v4["sk_iters"] == v4["sk_tiles"] * 128 >= 0
     v0 = bwgemm.plan(4608, 5632, 8192)                                       # config 1: a split-K tail
     assert v0["splits"] > 1 and v0["dp_tiles"] + v0["sk_tiles"] == v0["tiles"] and v0["sk_iters"] == 0
     with pytest.raises(bwgemm.BwError):
-        bwgemm.plan(16, 64, 64, variant=6)
+        bwgemm.plan(16, 64, 64, variant=bwgemm.lib().bw_gemm_variant_count())
 
 
 @pytest.mark.skipif(shutil.which("nvcc") is None, reason="nvcc")

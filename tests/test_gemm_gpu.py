@@ -236,3 +236,31 @@ def test_side_stream_and_graph_capture(oracle_mod):
     assert_parity(bits(C), oracle_mod.gemm_f64(A2, B2), K, oracle_mod, "graph, new contents")
     assert bwgemm.dirty() == 0
     assert bwgemm.status()[0] == 0
+
+
+def test_graph_survives_a_later_workspace_growth(oracle_mod):
+    """A graph captured at one shape replays correctly after a call at another shape needed a larger workspace: the
+    library never frees a workspace that a captured graph may hold."""
+    M, N, K = 16, 1024, 1024  # swap-AB + stream-K: a small workspace
+    A, B, ref = lcg_case(M, N, K, oracle_mod)
+    dA, dB = to_dev(A), to_dev(B)
+    C = torch.empty((M, N), dtype=torch.float16, device="cuda")
+    bwgemm.gemm(dA, dB, C)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        bwgemm.gemm(dA, dB, C)
+    M2, N2, K2 = 256, 9728, 8192  # a split-K tail of 38 pair tiles x 3: a much larger workspace
+    assert bwgemm.plan(M2, N2, K2)["workspace_bytes"] > 20 << 20
+    X = torch.rand((M2, K2), device="cuda").half()
+    Y = torch.rand((K2, N2), device="cuda").half()
+    Z = torch.empty((M2, N2), dtype=torch.float16, device="cuda")
+    bwgemm.gemm(X, Y, Z)
+    torch.cuda.synchronize()
+    for _ in range(2):
+        C.view(torch.int16).fill_(-1)
+        g.replay()
+        torch.cuda.synchronize()
+        assert bwgemm.status()[0] == 0
+        assert_parity(bits(C), ref, K, oracle_mod, "graph replayed after a workspace growth")
+    assert bwgemm.dirty() == 0

@@ -25,7 +25,7 @@ def all_shapes():
     return out
 
 
-@pytest.mark.parametrize("variant", range(6))
+@pytest.mark.parametrize("variant", range(8))
 @pytest.mark.parametrize("sms", [148, 132, 7, 1])
 def test_schedule_covers_every_kblock_once(checker, variant, sms):
     args = []
