@@ -436,3 +436,12 @@ BW_API int bw_gemm_f16_noalloc(const void* A, const void* B, void* C, int M, int
 {
     return bw::noalloc_gemm(A, B, C, M, N, K, static_cast<cudaStream_t>(stream));
 }
+
+#ifdef BW_TRACE
+// The timeline of the last launch (a -DBW_TRACE build only; not part of the C ABI of bwgemm.h).
+BW_API int bw_trace_read(unsigned long long* dst, int blocks)
+{
+    cudaError_t e = cudaMemcpyFromSymbol(dst, bw::g_trace, (size_t)blocks * bw::kTraceSlots * sizeof(unsigned long long));
+    return e == cudaSuccess ? BW_OK : BW_ERR_LAUNCH;
+}
+#endif

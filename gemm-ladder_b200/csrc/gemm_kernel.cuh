@@ -47,6 +47,16 @@ struct Params {
 
 __host__ __device__ constexpr int pow2_at_least(int v, int p) { return p >= v ? p : pow2_at_least(v, 2 * p); }
 
+// Optional timeline (compiled in with -DBW_TRACE only): per block, %globaltimer at kernel entry, after set-up, the
+// MMA's first full stage, its last commit, the epilogue's end, and the exit.
+#ifdef BW_TRACE
+constexpr int kTraceSlots = 8;
+__device__ unsigned long long g_trace[1024 * kTraceSlots];
+#define BW_TRACE_AT(slot) (g_trace[blockIdx.x * kTraceSlots + (slot)] = globaltimer_ns())
+#else
+#define BW_TRACE_AT(slot) ((void)0)
+#endif
+
 template <int BN, bool SWAP, bool PAIR>
 struct Geom {
     static constexpr int kRanks = PAIR ? 2 : 1;
@@ -197,6 +207,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     volatile int* epi_go = abort_flag + 2;  // two slots, alternating by segment
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) BW_TRACE_AT(0);
     const Sched& s = p.s;
     const int rank = PAIR ? (int)cluster_ctarank() : 0;
     const bool leader = rank == 0;
@@ -238,6 +249,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    if (threadIdx.x == 0) BW_TRACE_AT(1);
 
     if (warp == 0) {
         // ---------------------------------------------------------- TMA producer (one thread per block)
@@ -321,6 +333,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                         ok = false;
                         break;
                     }
+#ifdef BW_TRACE
+                    if (seg == 0 && kb == sg.k0) BW_TRACE_AT(2);
+#endif
                     tc_fence_after();
                     const uint32_t sx = smem_u32(smem + stage * G::kStageBytes), sy = sx + G::kXBytes;
 #pragma unroll
@@ -334,10 +349,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                             mma_f16(d, ad, bd, idesc, accumulate);
                     }
                     // the stage is free (in both blocks of a pair) once these MMAs have read it
-                    if (PAIR)
-                        mma_commit_pair(&empty[stage], 0x3);
-                    else
+                    if (PAIR) {
+                        mma_commit_pair(mapa_shared(smem_u32(&empty[stage]), 0));
+                        mma_commit_pair(mapa_shared(smem_u32(&empty[stage]), 1));
+                    } else {
                         mma_commit(&empty[stage]);
+                    }
                     if (++stage == S) {
                         stage = 0;
                         ph ^= 1u;
@@ -345,19 +362,22 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 if (!ok) break;
                 // the accumulator (both blocks' halves) is complete once every MMA so far has finished
-                if (PAIR)
-                    mma_commit_pair(&tfull[acc], 0x3);
-                else
+                if (PAIR) {
+                    mma_commit_pair(mapa_shared(smem_u32(&tfull[acc]), 0));
+                    mma_commit_pair(mapa_shared(smem_u32(&tfull[acc]), 1));
+                } else {
                     mma_commit(&tfull[acc]);
+                }
                 if (++acc == 2) {
                     acc = 0;
                     aph ^= 1u;
                 }
                 ++seg;
             }
+            BW_TRACE_AT(3);
             if (!ok) {  // let the MMAs in flight finish before the tensor memory is freed
                 if (PAIR)
-                    mma_commit_pair(drain, 0x1);
+                    mma_commit_pair(mapa_shared(smem_u32(drain), 0));
                 else
                     mma_commit(drain);
                 wait_drain(drain, 0, p.wait_ns);
@@ -481,6 +501,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             ++seg;
         }
+        if (threadIdx.x == kEpiThread0) BW_TRACE_AT(4);
     }
 
     __syncwarp();
@@ -497,6 +518,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         else
             tmem_dealloc(tmem_base, G::kTmemCols);
     }
+    if (threadIdx.x == 0) BW_TRACE_AT(5);
 }
 
 }  // namespace bw

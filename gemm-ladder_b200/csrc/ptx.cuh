@@ -227,14 +227,12 @@ __device__ __forceinline__ void mma_f16_pair(uint32_t d_tmem, uint64_t adesc, ui
         : "memory");
 }
 
-// Arrives once on the barrier at the same offset in each block of `mask` when every tcgen05 operation the leader
-// has issued so far has completed (the commit's multicast; no data moves).
-__device__ __forceinline__ void mma_commit_pair(uint64_t* bar, uint16_t mask)
+// Arrives once on the barrier at shared::cluster address `bar` (this block's or the other block's of the pair) when
+// every tcgen05 operation the leader has issued so far has completed.  The pair's barriers in both blocks are reached
+// by one such commit each (no multicast form is used anywhere in this library).
+__device__ __forceinline__ void mma_commit_pair(uint32_t bar)
 {
-    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
-                     smem_u32(bar)),
-                 "h"(mask)
-                 : "memory");
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
 }
 
 // Arrives once on `bar` when every tcgen05 operation issued so far by this thread has completed.
