@@ -137,49 +137,85 @@ __device__ __forceinline__ float* slot_ptr(const Params& p, long long slot, int 
     return p.work + ((size_t)slot * 128 + row) * BN + c0;
 }
 
-// Sums the tile's nseg partials in their fixed order (partial f.mine from `own` when own_mine, from its slot
-// otherwise) for 16 columns of one row, loading up to four partials at once.
-template <int BN, int RANKS>
-__device__ __forceinline__ void sum_partials(const Params& p, int P, int tile, int rank, const Fixup& f, bool own_mine,
-                                             const float (&own)[16], int row, int c0, float (&v)[16])
+// The last block of a split tile: for its row of the tile, sums the tile's nseg partials in their fixed order
+// (p_0 + p_1 + ... : the same bits whichever block is last) and stores the result to C.  Partial f.mine comes from
+// this block's accumulator in tensor memory when own_mine (tbase: its row's TMEM address), from its slot otherwise.
+// The loads from memory are a stream of (16-column chunk, partial) pairs in chunk order, kept kWin deep in flight:
+// with one partial in memory four chunks are on their way at once, instead of one L2 round trip per chunk.
+template <int BN, bool SWAP, int RANKS>
+__device__ __forceinline__ void reduce_tile(const Params& p, int P, int tile, int rank, const Fixup& f, bool own_mine,
+                                            uint32_t tbase, int row, int m0, int n0)
 {
+    constexpr int kWin = 4;
+    constexpr int kChunks = BN / 16;
     const Sched& s = p.s;
-#pragma unroll 1
-    for (int i0 = 0; i0 < f.nseg; i0 += 4) {
-        float4 buf[4][4];
+    const int L = f.nseg - (own_mine ? 1 : 0);  // partials read from memory
+    const int total = kChunks * L;
+    // the memory partial j (in order) is partial index i: j, or j + 1 past this block's own
+    auto index_of = [&](int j) { return (own_mine && j >= f.mine) ? j + 1 : j; };
+    auto issue = [&](int idx, float4 (&w)[4]) {
+        const int chunk = idx / L, j = idx - chunk * L;
+        const long long slot = (long long)fixup_slot(s, P, tile, f, index_of(j)) * RANKS + rank;
+        const float4* src = reinterpret_cast<const float4*>(slot_ptr<BN>(p, slot, row, chunk * 16));
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const int i = i0 + j;
-            if (i < f.nseg && !(own_mine && i == f.mine)) {
-                const long long slot = (long long)fixup_slot(s, P, tile, f, i) * RANKS + rank;
-                const float4* src = reinterpret_cast<const float4*>(slot_ptr<BN>(p, slot, row, c0));
+        for (int q = 0; q < 4; ++q) w[q] = __ldcg(src + q);
+    };
+    float4 win[kWin][4];
 #pragma unroll
-                for (int q = 0; q < 4; ++q) buf[j][q] = __ldcg(src + q);
-            }
-        }
+    for (int q = 0; q < kWin; ++q)
+        if (q < total) issue(q, win[q]);
+    float v[16], own[16];
+    bool own_added = false;
+    for (int base = 0; base < total; base += kWin) {
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const int i = i0 + j;
-            if (i < f.nseg) {
-                float x[16];
-                if (own_mine && i == f.mine) {
+        for (int q = 0; q < kWin; ++q) {
+            const int idx = base + q;
+            if (idx < total) {
+                const int chunk = idx / L, j = idx - chunk * L;
+                const int i = index_of(j);
+                if (j == 0) {
+                    own_added = false;
+                    if (own_mine) {
+                        uint32_t r[16];
+                        tmem_ld16(tbase + (uint32_t)(chunk * 16), r);
+                        tmem_wait_ld();
 #pragma unroll
-                    for (int q = 0; q < 16; ++q) x[q] = own[q];
-                } else {
-#pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-                        x[4 * q] = buf[j][q].x;
-                        x[4 * q + 1] = buf[j][q].y;
-                        x[4 * q + 2] = buf[j][q].z;
-                        x[4 * q + 3] = buf[j][q].w;
+                        for (int e = 0; e < 16; ++e) own[e] = __uint_as_float(r[e]);
                     }
                 }
+                // this block's own partial goes in at its place in the order
+                if (own_mine && !own_added && f.mine < i) {
+                    if (f.mine == 0) {
+#pragma unroll
+                        for (int e = 0; e < 16; ++e) v[e] = own[e];
+                    } else {
+#pragma unroll
+                        for (int e = 0; e < 16; ++e) v[e] += own[e];
+                    }
+                    own_added = true;
+                }
+                float x[16];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    x[4 * e] = win[q][e].x;
+                    x[4 * e + 1] = win[q][e].y;
+                    x[4 * e + 2] = win[q][e].z;
+                    x[4 * e + 3] = win[q][e].w;
+                }
+                if (idx + kWin < total) issue(idx + kWin, win[q]);  // refill this window slot
                 if (i == 0) {
 #pragma unroll
-                    for (int q = 0; q < 16; ++q) v[q] = x[q];
+                    for (int e = 0; e < 16; ++e) v[e] = x[e];
                 } else {
 #pragma unroll
-                    for (int q = 0; q < 16; ++q) v[q] += x[q];
+                    for (int e = 0; e < 16; ++e) v[e] += x[e];
+                }
+                if (j == L - 1) {  // the chunk is complete
+                    if (own_mine && !own_added) {
+#pragma unroll
+                        for (int e = 0; e < 16; ++e) v[e] += own[e];
+                    }
+                    store_chunk<SWAP>(p, m0, n0, row, chunk * 16, v);
                 }
             }
         }
@@ -446,17 +482,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 named_bar_sync(1, 128);
                 const int fast = *reduce_flag;
                 if (fast == 2) {
-#pragma unroll 1
-                    for (int c0 = 0; c0 < BN; c0 += 16) {
-                        uint32_t r[16];
-                        tmem_ld16(tbase + (uint32_t)c0, r);
-                        tmem_wait_ld();
-                        float own[16], v[16];
-#pragma unroll
-                        for (int j = 0; j < 16; ++j) own[j] = __uint_as_float(r[j]);
-                        sum_partials<BN, R>(p, P, sg.tile, rank, f, true, own, row, c0, v);
-                        store_chunk<SWAP>(p, m0, n0, row, c0, v);
-                    }
+                    reduce_tile<BN, SWAP, R>(p, P, sg.tile, rank, f, true, tbase, row, m0, n0);
                     release_acc(acc);
                     if (threadIdx.x == kEpiThread0) atomicExch(counter, 0);
                 } else {
@@ -483,13 +509,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                     named_bar_sync(1, 128);
                     if (*reduce_flag == 1) {
-                        const float none[16] = {};
-#pragma unroll 1
-                        for (int c0 = 0; c0 < BN; c0 += 16) {
-                            float v[16];
-                            sum_partials<BN, R>(p, P, sg.tile, rank, f, false, none, row, c0, v);
-                            store_chunk<SWAP>(p, m0, n0, row, c0, v);
-                        }
+                        reduce_tile<BN, SWAP, R>(p, P, sg.tile, rank, f, false, tbase, row, m0, n0);
                         if (threadIdx.x == kEpiThread0) atomicExch(counter, 0);
                     }
                 }

@@ -3,14 +3,14 @@
 // it, and the CPU tests run the same code to check that every K-block of every tile is computed exactly once and that
 // the partial counts and workspace slots the reducer uses are the ones the writers used.
 //
-// A block's work, in order:
-//   1. data-parallel: whole tiles c, c + P, c + 2P, ... below dp_tiles (P blocks; consecutive tiles run at the same
-//      time, so blocks that share rows of A or columns of B read them from L2 together);
-//   2. the other sk_tiles tiles, either
-//      split-K (splits > 0): each tile's K-blocks cut in `splits` equal ranges; unit u = split * sk_tiles + tile goes
-//        to block u % P, so the units running together are the same K range of neighbouring tiles (the shared
-//        operands stay shared in L2), or
-//      stream-K (splits == 0): the sk_tiles * kblocks K-blocks cut evenly over the P blocks, block c taking
+// A block's work: data-parallel whole tiles c, c + P, c + 2P, ... below dp_tiles (P blocks; consecutive tiles run at
+// the same time, so blocks that share rows of A or columns of B read them from L2 together), and the other sk_tiles
+// tiles, either
+//      split-K (splits > 0), done before the whole tiles: each tile's K-blocks cut in `splits` equal ranges; unit
+//        u = split * sk_tiles + tile goes to block u % P, so the units running together are the same K range of
+//        neighbouring tiles (the shared operands stay shared in L2), or
+//      stream-K (splits == 0), done after the whole tiles: the sk_tiles * kblocks K-blocks cut evenly over the P
+//        blocks, block c taking
 //        [sk_iters c / P, sk_iters (c + 1) / P) -- every block the same work whatever the tile count (used where the
 //        operands are streamed once from HBM anyway: the swap-AB path at M <= 128).
 // A tile computed by several blocks: each writes its fp32 partial to a workspace slot; the last to finish (a counter
@@ -86,16 +86,9 @@ struct SegIter {
     }
     BW_HD bool next(const Sched& s, int P, Seg& seg)
     {
-        if (next_dp < s.dp_tiles) {
-            seg.tile = next_dp;
-            seg.k0 = 0;
-            seg.k1 = s.kblocks;
-            seg.unit = -1;
-            next_dp += P;
-            return true;
-        }
-        if (s.splits > 0) {
-            if (next_u >= s.sk_tiles * s.splits) return false;
+        // split-K units first: the reduction of a split tile then overlaps the block's next tiles (the epilogue
+        // of one segment runs while the MMAs of the next fill the other accumulator), not the end of the kernel
+        if (s.splits > 0 && next_u < s.sk_tiles * s.splits) {
             const int u = next_u;
             const int sp = u / s.sk_tiles, rel = u - sp * s.sk_tiles;
             seg.tile = s.dp_tiles + rel;
@@ -105,6 +98,15 @@ struct SegIter {
             next_u += P;
             return true;
         }
+        if (next_dp < s.dp_tiles) {
+            seg.tile = next_dp;
+            seg.k0 = 0;
+            seg.k1 = s.kblocks;
+            seg.unit = -1;
+            next_dp += P;
+            return true;
+        }
+        if (s.splits > 0) return false;
         if (g < g_end) {
             const long long rel = g / s.kblocks;
             seg.k0 = (int)(g - rel * s.kblocks);
