@@ -78,6 +78,23 @@ struct Geom {
     static_assert(kTmemCols <= 512, "tensor memory");
 };
 
+// The L2 policy of a hint setting (0 none, 1 evict-last, 2 evict-first).
+__device__ __forceinline__ uint64_t l2_policy(int hint) { return hint == 1 ? policy_evict_last() : policy_evict_first(); }
+
+// A tile load with an optional L2 policy; `bar` is this block's barrier (or, PAIR, the leader's shared::cluster one).
+template <bool PAIR, int HINT>
+__device__ __forceinline__ void load_tile(void* dst, const void* tmap, int x, int y, uint64_t* bar, uint32_t bar_cluster,
+                                          uint64_t policy)
+{
+    if (PAIR) {
+        if (HINT) tma_load_2d_pair_hint(dst, tmap, x, y, bar_cluster, policy);
+        else tma_load_2d_pair(dst, tmap, x, y, bar_cluster);
+    } else {
+        if (HINT) tma_load_2d_hint(dst, tmap, x, y, bar, policy);
+        else tma_load_2d(dst, tmap, x, y, bar);
+    }
+}
+
 // Where a wait gave up: role (0 producer, 1 MMA, 2 epilogue) << 16 | barrier kind << 8 | index.
 __device__ __forceinline__ uint32_t site(uint32_t role, uint32_t kind, uint32_t idx) { return role << 16 | kind << 8 | idx; }
 
@@ -129,12 +146,14 @@ __device__ __forceinline__ void store_chunk(const Params& p, int m0, int n0, int
 }
 
 // ------------------------------------------------------------------ the partials of a split tile
-// Slot layout: 128 rows x BN columns of fp32, row-major: TMEM lane `row`'s 16 columns are 64 contiguous bytes.
-// A block of a pair keeps its half in slot 2 s + rank.
+// Slot layout: 128 rows x BN columns of fp32, interleaved by groups of 4 columns: [col / 4][row][col % 4].  TMEM lane
+// `row`'s 4-column group is one 16-byte vector, and the 32 lanes of a warp touch 512 contiguous bytes per vector
+// access (stores of a partial and loads of the reduction alike).  A block of a pair keeps its half in slot
+// 2 s + rank.
 template <int BN>
-__device__ __forceinline__ float* slot_ptr(const Params& p, long long slot, int row, int c0)
+__device__ __forceinline__ float4* slot_vec(const Params& p, long long slot, int row, int col4)
 {
-    return p.work + ((size_t)slot * 128 + row) * BN + c0;
+    return reinterpret_cast<float4*>(p.work + (size_t)slot * 128 * BN) + (size_t)col4 * 128 + row;
 }
 
 // The last block of a split tile: for its row of the tile, sums the tile's nseg partials in their fixed order
@@ -156,9 +175,8 @@ __device__ __forceinline__ void reduce_tile(const Params& p, int P, int tile, in
     auto issue = [&](int idx, float4 (&w)[4]) {
         const int chunk = idx / L, j = idx - chunk * L;
         const long long slot = (long long)fixup_slot(s, P, tile, f, index_of(j)) * RANKS + rank;
-        const float4* src = reinterpret_cast<const float4*>(slot_ptr<BN>(p, slot, row, chunk * 16));
 #pragma unroll
-        for (int q = 0; q < 4; ++q) w[q] = __ldcg(src + q);
+        for (int q = 0; q < 4; ++q) w[q] = __ldcg(slot_vec<BN>(p, slot, row, chunk * 4 + q));
     };
     float4 win[kWin][4];
 #pragma unroll
@@ -292,6 +310,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) {
             SegIter it(s, c, P);
             Seg sg;
+            const uint64_t pol_a = BW_HINT_A ? l2_policy(BW_HINT_A) : 0ull;
+            const uint64_t pol_b = BW_HINT_B ? l2_policy(BW_HINT_B) : 0ull;
             int stage = 0, issued = 0, seg = 0;
             uint32_t ph = 0;
             bool ok = true;
@@ -310,27 +330,23 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                     uint8_t* sx = smem + stage * G::kStageBytes;
                     uint8_t* sy = sx + G::kXBytes;
-                    if (PAIR) {
-                        // both blocks' halves complete on the leader's barrier, which expects them all
-                        const uint32_t bar = mapa_shared(smem_u32(&full[stage]), 0);
-                        if (leader) mbar_arrive_expect_tx(&full[stage], 2 * G::kStageBytes);
-                        tma_load_2d_pair(sx, &tmx, kb * kBK, tm * 256 + rank * 128, bar);  // A: 64 K x 128 rows
+                    // both blocks of a pair complete their halves on the leader's barrier, which expects them all
+                    const uint32_t barc = PAIR ? mapa_shared(smem_u32(&full[stage]), 0) : 0u;
+                    if (!PAIR || leader) mbar_arrive_expect_tx(&full[stage], R * G::kStageBytes);
+                    if (!SWAP) {
+                        // A: 64 K x 128 rows (this block's rows of a pair tile)
+                        load_tile<PAIR, BW_HINT_A>(sx, &tmx, kb * kBK, tm * G::kTileM + rank * 128, &full[stage], barc,
+                                                   pol_a);
 #pragma unroll
-                        for (int j = 0; j < BN / 128; ++j)  // B: this block's BN / 2 columns, boxes of 64 x 64 K
-                            tma_load_2d_pair(sy + j * 8192, &tmy, tn * BN + rank * (BN / 2) + 64 * j, kb * kBK, bar);
+                        for (int j = 0; j < BN / (64 * R); ++j)  // B: this block's BN / R columns, boxes of 64 x 64 K
+                            load_tile<PAIR, BW_HINT_B>(sy + j * 8192, &tmy, tn * BN + rank * (BN / R) + 64 * j, kb * kBK,
+                                                       &full[stage], barc, pol_b);
                     } else {
-                        mbar_arrive_expect_tx(&full[stage], G::kStageBytes);
-                        if (!SWAP) {
-                            tma_load_2d(sx, &tmx, kb * kBK, tm * 128, &full[stage]);  // A: 64 K x 128 rows
 #pragma unroll
-                            for (int j = 0; j < BN / 64; ++j)  // B: 64 columns x 64 K per box
-                                tma_load_2d(sy + j * 8192, &tmy, tn * BN + 64 * j, kb * kBK, &full[stage]);
-                        } else {
-#pragma unroll
-                            for (int j = 0; j < 2; ++j)  // B: 128 columns as two boxes of 64 columns x 64 K
-                                tma_load_2d(sx + j * 8192, &tmx, tn * 128 + 64 * j, kb * kBK, &full[stage]);
-                            tma_load_2d(sy, &tmy, kb * kBK, 0, &full[stage]);  // A: 64 K x BN rows (M <= BN)
-                        }
+                        for (int j = 0; j < 2; ++j)  // B: 128 columns as two boxes of 64 columns x 64 K
+                            load_tile<false, BW_HINT_B>(sx + j * 8192, &tmx, tn * 128 + 64 * j, kb * kBK, &full[stage], 0u,
+                                                        pol_b);
+                        load_tile<false, BW_HINT_A>(sy, &tmy, kb * kBK, 0, &full[stage], 0u, pol_a);  // A: 64 K x BN rows
                     }
                     ++issued;
                     if (++stage == S) {
@@ -493,11 +509,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                         uint32_t r[16];
                         tmem_ld16(tbase + (uint32_t)c0, r);
                         tmem_wait_ld();
-                        float4* dst = reinterpret_cast<float4*>(slot_ptr<BN>(p, myslot, row, c0));
 #pragma unroll
                         for (int j = 0; j < 4; ++j)
-                            __stcg(dst + j, make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
-                                                        __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3])));
+                            __stcg(slot_vec<BN>(p, myslot, row, c0 / 4 + j),
+                                   make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
+                                               __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3])));
                     }
                     release_acc(acc);
                     __threadfence();

@@ -29,6 +29,12 @@
 #ifndef BW_MAX_STAGES
 #define BW_MAX_STAGES 12
 #endif
+#ifndef BW_HINT_A
+#define BW_HINT_A 0            // L2 policy of the A tiles: 0 none, 1 evict-last, 2 evict-first
+#endif
+#ifndef BW_HINT_B
+#define BW_HINT_B 0            // L2 policy of the B tiles: 0 none, 1 evict-last, 2 evict-first
+#endif
 
 namespace bw {
 

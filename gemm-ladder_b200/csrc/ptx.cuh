@@ -177,6 +177,17 @@ __device__ __forceinline__ void tma_load_2d_pair(void* dst, const void* tmap, in
         : "memory");
 }
 
+// The same with an L2 cache policy.
+__device__ __forceinline__ void tma_load_2d_pair_hint(void* dst, const void* tmap, int x, int y, uint32_t bar,
+                                                      uint64_t policy)
+{
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], "
+        "[%1, {%2, %3}], [%4], %5;" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(bar), "l"(policy)
+        : "memory");
+}
+
 // ------------------------------------------------------------------ tcgen05: tensor memory
 __device__ __forceinline__ void tmem_alloc(uint32_t* slot, uint32_t ncols)
 {
