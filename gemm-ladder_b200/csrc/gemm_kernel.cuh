@@ -50,10 +50,12 @@ __host__ __device__ constexpr int pow2_at_least(int v, int p) { return p >= v ? 
 // Optional timeline (compiled in with -DBW_TRACE only): per block, %globaltimer at kernel entry, after set-up, the
 // MMA's first full stage, its last commit, the epilogue's end, and the exit.
 #ifdef BW_TRACE
-constexpr int kTraceSlots = 8;
+constexpr int kTraceSlots = 12;
 __device__ unsigned long long g_trace[1024 * kTraceSlots];
 #define BW_TRACE_AT(slot) (g_trace[blockIdx.x * kTraceSlots + (slot)] = globaltimer_ns())
+#define BW_TRACE_VAL(slot, v) (g_trace[blockIdx.x * kTraceSlots + (slot)] = (unsigned long long)(v))
 #else
+#define BW_TRACE_VAL(slot, v) ((void)0)
 #define BW_TRACE_AT(slot) ((void)0)
 #endif
 
@@ -67,7 +69,9 @@ struct Geom {
     static constexpr int kStages = (BW_RING_BYTES / kStageBytes) < BW_MAX_STAGES ? (BW_RING_BYTES / kStageBytes) : BW_MAX_STAGES;
     static constexpr int kTmemCols = pow2_at_least(2 * BN < 32 ? 32 : 2 * BN, 32);  // two accumulators
     static constexpr int kBarOffset = kStages * kStageBytes;
-    static constexpr int kNumBars = 2 * kStages + 5;  // full, empty, tmem full x2, tmem empty x2, drain
+    static constexpr int kNumBars = 2 * kStages + 6;  // full, empty, tmem full x2, tmem empty x2, drain, reduce
+    static constexpr int kSlotBytes = 128 * BN * 4;   // one partial of this block's rows
+    static constexpr int kRingSlots = kBarOffset / kSlotBytes;  // partials the idle ring holds at once
     static constexpr int kMiscOffset = kBarOffset + kNumBars * 8;
     static constexpr int kSmemBytes = 1024 + kMiscOffset + 32;  // + slack to align the stages to 1024 bytes
     static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "MMA N: a multiple of 16 in [16, 256]");
@@ -162,7 +166,7 @@ __device__ __forceinline__ float4* slot_vec(const Params& p, long long slot, int
 // The loads from memory are a stream of (16-column chunk, partial) pairs in chunk order, kept kWin deep in flight:
 // with one partial in memory four chunks are on their way at once, instead of one L2 round trip per chunk.
 template <int BN, bool SWAP, int RANKS>
-__device__ __forceinline__ void reduce_tile(const Params& p, int P, int tile, int rank, const Fixup& f, bool own_mine,
+__device__ __noinline__ void reduce_tile(const Params& p, int P, int tile, int rank, const Fixup& f, bool own_mine,
                                             uint32_t tbase, int row, int m0, int n0)
 {
     constexpr int kWin = 4;
@@ -240,6 +244,73 @@ __device__ __forceinline__ void reduce_tile(const Params& p, int P, int tile, in
     }
 }
 
+// The same at a block's last segment, when its stage ring is idle (every load consumed, none to come): the partials
+// in memory are copied into the ring by the TMA engine at once (cp.async.bulk, one per partial), then summed from
+// shared memory.  Returns false if the copy did not complete within the wait limit (the block's abort flag is up).
+template <int BN, bool SWAP, int RANKS>
+__device__ __noinline__ bool reduce_tile_bulk(const Params& p, int P, int tile, int rank, const Fixup& f,
+                                                 bool own_mine, uint32_t tbase, int row, int m0, int n0,
+                                                 uint8_t* ring, uint64_t* rbar, volatile int* abort_flag, int seg)
+{
+    constexpr int kSlotBytes = 128 * BN * 4;
+    constexpr int kChunks = BN / 16;
+    const Sched& s = p.s;
+    const int L = f.nseg - (own_mine ? 1 : 0);
+    auto index_of = [&](int j) { return (own_mine && j >= f.mine) ? j + 1 : j; };
+    if (threadIdx.x == kEpiThread0) {
+        mbar_arrive_expect_tx(rbar, (uint32_t)(L * kSlotBytes));
+        for (int j = 0; j < L; ++j) {
+            const long long slot = (long long)fixup_slot(s, P, tile, f, index_of(j)) * RANKS + rank;
+            const uint8_t* src = reinterpret_cast<const uint8_t*>(p.work + (size_t)slot * 128 * BN);
+            for (int off = 0; off < kSlotBytes; off += 32768) {
+                const int n = kSlotBytes - off < 32768 ? kSlotBytes - off : 32768;
+                bulk_load(ring + (size_t)j * kSlotBytes + off, src + off, (uint32_t)n, rbar);
+            }
+        }
+    }
+    if (!wait_bounded(rbar, 0, abort_flag, p.wait_ns, site(2, 4, 0), seg)) return false;
+    const float4* sm = reinterpret_cast<const float4*>(ring);
+#pragma unroll 1
+    for (int chunk = 0; chunk < kChunks; ++chunk) {
+        float own[16], v[16];
+        if (own_mine) {
+            uint32_t r[16];
+            tmem_ld16(tbase + (uint32_t)(chunk * 16), r);
+            tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 16; ++e) own[e] = __uint_as_float(r[e]);
+        }
+        for (int i = 0, j = 0; i < f.nseg; ++i) {
+            float x[16];
+            if (own_mine && i == f.mine) {
+#pragma unroll
+                for (int e = 0; e < 16; ++e) x[e] = own[e];
+            } else {
+                // [col / 4][row][4] within the slot: consecutive rows are consecutive 16-byte vectors
+                const float4* src = sm + (size_t)j * (kSlotBytes / 16) + (size_t)(chunk * 4) * 128 + row;
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const float4 w = src[q * 128];
+                    x[4 * q] = w.x;
+                    x[4 * q + 1] = w.y;
+                    x[4 * q + 2] = w.z;
+                    x[4 * q + 3] = w.w;
+                }
+                ++j;
+            }
+            if (i == 0) {
+#pragma unroll
+                for (int e = 0; e < 16; ++e) v[e] = x[e];
+            } else {
+#pragma unroll
+                for (int e = 0; e < 16; ++e) v[e] += x[e];
+            }
+        }
+        store_chunk<SWAP>(p, m0, n0, row, chunk * 16, v);
+    }
+    return true;
+}
+
 // ------------------------------------------------------------------ the kernel
 template <int BN, bool SWAP, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -255,6 +326,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* tfull = empty + S;
     uint64_t* tempty = tfull + 2;
     uint64_t* drain = tempty + 2;
+    uint64_t* rbar = drain + 1;  // the bulk reduction's copies of partials
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + G::kMiscOffset);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
     volatile int* reduce_flag = abort_flag + 1;
@@ -277,6 +349,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&tempty[i], 4 * R);  // one arrival per epilogue warp (of both blocks of a pair)
         }
         mbar_init(drain, 1);
+        mbar_init(rbar, 1);
         *abort_flag = 0;
         *reduce_flag = 0;
         epi_go[0] = epi_go[1] = 0;
@@ -312,6 +385,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             Seg sg;
             const uint64_t pol_a = BW_HINT_A ? l2_policy(BW_HINT_A) : 0ull;
             const uint64_t pol_b = BW_HINT_B ? l2_policy(BW_HINT_B) : 0ull;
+            const uint64_t pol_sb = BW_SWAP_HINT_B ? l2_policy(BW_SWAP_HINT_B) : 0ull;
             int stage = 0, issued = 0, seg = 0;
             uint32_t ph = 0;
             bool ok = true;
@@ -344,8 +418,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                     } else {
 #pragma unroll
                         for (int j = 0; j < 2; ++j)  // B: 128 columns as two boxes of 64 columns x 64 K
-                            load_tile<false, BW_HINT_B>(sx + j * 8192, &tmx, tn * 128 + 64 * j, kb * kBK, &full[stage], 0u,
-                                                        pol_b);
+                            load_tile<false, BW_SWAP_HINT_B>(sx + j * 8192, &tmx, tn * 128 + 64 * j, kb * kBK,
+                                                             &full[stage], 0u, pol_sb);
                         load_tile<false, BW_HINT_A>(sy, &tmy, kb * kBK, 0, &full[stage], 0u, pol_a);  // A: 64 K x BN rows
                     }
                     ++issued;
@@ -463,6 +537,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                 epi_go[seg & 1] = wait_bounded(&tfull[acc], aph, abort_flag, p.wait_ns, site(2, 2, acc), seg) ? 1 : 0;
             named_bar_sync(1, 128);
             if (!epi_go[seg & 1]) break;
+            if (threadIdx.x == kEpiThread0) {
+                BW_TRACE_AT(6);  // the last segment's accumulator is ready (kept: overwritten per segment)
+                BW_TRACE_VAL(8, 0);
+            }
             tc_fence_after();
             int m0, n0;
             if (SWAP) {
@@ -492,13 +570,25 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // part of a split tile
                 const Fixup f = fixup_of(s, c, P, sg);
                 int* counter = p.counters + (sg.tile - s.dp_tiles) * R + rank;
+                // this block's last segment: its stage ring is idle and can take the partials by bulk copy
+                SegIter peek = it;
+                Seg nx;
+                const bool last_seg = !peek.next(s, P, nx);
                 // every other partial already written: this block is the last; sum them with its own accumulator
                 // straight from tensor memory (no round trip of its own partial)
                 if (threadIdx.x == kEpiThread0) *reduce_flag = ld_acquire_gpu(counter) == f.nseg - 1 ? 2 : 0;
                 named_bar_sync(1, 128);
                 const int fast = *reduce_flag;
+                if (threadIdx.x == kEpiThread0) {
+                    BW_TRACE_AT(7);
+                    BW_TRACE_VAL(8, (fast == 2 ? 2 : 3) | f.nseg << 8 | seg << 16);
+                }
                 if (fast == 2) {
-                    reduce_tile<BN, SWAP, R>(p, P, sg.tile, rank, f, true, tbase, row, m0, n0);
+                    if (last_seg && f.nseg - 1 <= G::kRingSlots)
+                        reduce_tile_bulk<BN, SWAP, R>(p, P, sg.tile, rank, f, true, tbase, row, m0, n0, smem, rbar,
+                                                      abort_flag, seg);
+                    else
+                        reduce_tile<BN, SWAP, R>(p, P, sg.tile, rank, f, true, tbase, row, m0, n0);
                     release_acc(acc);
                     if (threadIdx.x == kEpiThread0) atomicExch(counter, 0);
                 } else {
@@ -515,7 +605,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                                    make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
                                                __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3])));
                     }
-                    release_acc(acc);
+                    // at the last segment the accumulator stays (no later MMA needs it): the reduction reads this
+                    // block's own partial from tensor memory
+                    if (!last_seg) release_acc(acc);
                     __threadfence();
                     named_bar_sync(1, 128);
                     if (threadIdx.x == kEpiThread0) {
@@ -525,9 +617,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                     named_bar_sync(1, 128);
                     if (*reduce_flag == 1) {
-                        reduce_tile<BN, SWAP, R>(p, P, sg.tile, rank, f, false, tbase, row, m0, n0);
+                        if (threadIdx.x == kEpiThread0) {
+                            BW_TRACE_AT(9);
+                            BW_TRACE_VAL(8, 1 | f.nseg << 8 | seg << 16);
+                        }
+                        if (last_seg && f.nseg - 1 <= G::kRingSlots)
+                            reduce_tile_bulk<BN, SWAP, R>(p, P, sg.tile, rank, f, true, tbase, row, m0, n0, smem, rbar,
+                                                          abort_flag, seg);
+                        else
+                            reduce_tile<BN, SWAP, R>(p, P, sg.tile, rank, f, false, tbase, row, m0, n0);
                         if (threadIdx.x == kEpiThread0) atomicExch(counter, 0);
                     }
+                    if (last_seg) release_acc(acc);
                 }
                 named_bar_sync(1, 128);  // reduce_flag is read by all before the next segment writes it
             }

@@ -35,6 +35,9 @@
 #ifndef BW_HINT_B
 #define BW_HINT_B 0            // L2 policy of the B tiles: 0 none, 1 evict-last, 2 evict-first
 #endif
+#ifndef BW_SWAP_HINT_B
+#define BW_SWAP_HINT_B 2       // swap-AB (M <= 128): the weights are read once, evict first (measured: o_m128 -11 %)
+#endif
 
 namespace bw {
 
@@ -69,7 +72,7 @@ inline int plan_tmem_cols(int bn)
 }
 inline int plan_smem_bytes(int bn, int ranks)
 {
-    return 1024 + plan_stages(bn, ranks) * plan_stage_bytes(bn, ranks) + (2 * plan_stages(bn, ranks) + 5) * 8 + 32;
+    return 1024 + plan_stages(bn, ranks) * plan_stage_bytes(bn, ranks) + (2 * plan_stages(bn, ranks) + 6) * 8 + 32;
 }
 
 inline bool shape_ok(int M, int N, int K)

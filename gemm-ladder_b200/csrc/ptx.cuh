@@ -137,6 +137,16 @@ __device__ __forceinline__ uint64_t policy_evict_last()
     return p;
 }
 
+// A contiguous copy of `bytes` (a multiple of 16) from global to this block's shared memory by the TMA engine,
+// completing on `bar` (both addresses 16-byte aligned).
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar)
+{
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_u32(dst)),
+                 "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
+
 // ------------------------------------------------------------------ clusters (the CTA pair of cta_group::2)
 __device__ __forceinline__ uint32_t cluster_ctarank()
 {
