@@ -72,6 +72,7 @@ struct Geom {
     static constexpr int kNumBars = 2 * kStages + 6;  // full, empty, tmem full x2, tmem empty x2, drain, reduce
     static constexpr int kSlotBytes = 128 * BN * 4;   // one partial of this block's rows
     static constexpr int kRingSlots = kBarOffset / kSlotBytes;  // partials the idle ring holds at once
+    static constexpr int kMaxSum = kRingSlots + 1 < 8 ? kRingSlots + 1 : 8;  // partials the bulk reduction sums
     static constexpr int kMiscOffset = kBarOffset + kNumBars * 8;
     static constexpr int kSmemBytes = 1024 + kMiscOffset + 32;  // + slack to align the stages to 1024 bytes
     static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "MMA N: a multiple of 16 in [16, 256]");
@@ -166,7 +167,7 @@ __device__ __forceinline__ float4* slot_vec(const Params& p, long long slot, int
 // The loads from memory are a stream of (16-column chunk, partial) pairs in chunk order, kept kWin deep in flight:
 // with one partial in memory four chunks are on their way at once, instead of one L2 round trip per chunk.
 template <int BN, bool SWAP, int RANKS>
-__device__ __noinline__ void reduce_tile(const Params& p, int P, int tile, int rank, const Fixup& f, bool own_mine,
+__device__ __noinline__ void reduce_tile(const Params& p, int P, int tile, int rank, Fixup f, bool own_mine,
                                             uint32_t tbase, int row, int m0, int n0)
 {
     constexpr int kWin = 4;
@@ -246,21 +247,22 @@ __device__ __noinline__ void reduce_tile(const Params& p, int P, int tile, int r
 
 // The same at a block's last segment, when its stage ring is idle (every load consumed, none to come): the partials
 // in memory are copied into the ring by the TMA engine at once (cp.async.bulk, one per partial), then summed from
-// shared memory.  Returns false if the copy did not complete within the wait limit (the block's abort flag is up).
-template <int BN, bool SWAP, int RANKS>
-__device__ __noinline__ bool reduce_tile_bulk(const Params& p, int P, int tile, int rank, const Fixup& f,
-                                                 bool own_mine, uint32_t tbase, int row, int m0, int n0,
-                                                 uint8_t* ring, uint64_t* rbar, volatile int* abort_flag, int seg)
+// shared memory.  The sum runs over at most kMaxSum partials, unrolled and predicated, so that everything stays in
+// registers.  Returns false if the copy did not complete within the wait limit (the block's abort flag is up).
+template <int BN, bool SWAP, int RANKS, int kMaxSum>
+__device__ __noinline__ bool reduce_tile_bulk(const Params& p, int P, int tile, int rank, Fixup f, bool own_mine,
+                                              uint32_t tbase, int row, int m0, int n0, uint8_t* ring, uint64_t* rbar,
+                                              volatile int* abort_flag, int seg)
 {
     constexpr int kSlotBytes = 128 * BN * 4;
     constexpr int kChunks = BN / 16;
     const Sched& s = p.s;
     const int L = f.nseg - (own_mine ? 1 : 0);
-    auto index_of = [&](int j) { return (own_mine && j >= f.mine) ? j + 1 : j; };
     if (threadIdx.x == kEpiThread0) {
         mbar_arrive_expect_tx(rbar, (uint32_t)(L * kSlotBytes));
         for (int j = 0; j < L; ++j) {
-            const long long slot = (long long)fixup_slot(s, P, tile, f, index_of(j)) * RANKS + rank;
+            const int i = (own_mine && j >= f.mine) ? j + 1 : j;
+            const long long slot = (long long)fixup_slot(s, P, tile, f, i) * RANKS + rank;
             const uint8_t* src = reinterpret_cast<const uint8_t*>(p.work + (size_t)slot * 128 * BN);
             for (int off = 0; off < kSlotBytes; off += 32768) {
                 const int n = kSlotBytes - off < 32768 ? kSlotBytes - off : 32768;
@@ -269,45 +271,59 @@ __device__ __noinline__ bool reduce_tile_bulk(const Params& p, int P, int tile, 
         }
     }
     if (!wait_bounded(rbar, 0, abort_flag, p.wait_ns, site(2, 4, 0), seg)) return false;
-    const float4* sm = reinterpret_cast<const float4*>(ring);
+    if (threadIdx.x == kEpiThread0) BW_TRACE_AT(10);
+    // [col / 4][row][4] within a slot: consecutive rows are consecutive 16-byte vectors
+    const float4* base = reinterpret_cast<const float4*>(ring) + row;
 #pragma unroll 1
     for (int chunk = 0; chunk < kChunks; ++chunk) {
-        float own[16], v[16];
+        float4 own[4], acc[4];
         if (own_mine) {
             uint32_t r[16];
             tmem_ld16(tbase + (uint32_t)(chunk * 16), r);
             tmem_wait_ld();
 #pragma unroll
-            for (int e = 0; e < 16; ++e) own[e] = __uint_as_float(r[e]);
+            for (int q = 0; q < 4; ++q)
+                own[q] = make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]),
+                                     __uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3]));
         }
-        for (int i = 0, j = 0; i < f.nseg; ++i) {
-            float x[16];
-            if (own_mine && i == f.mine) {
 #pragma unroll
-                for (int e = 0; e < 16; ++e) x[e] = own[e];
-            } else {
-                // [col / 4][row][4] within the slot: consecutive rows are consecutive 16-byte vectors
-                const float4* src = sm + (size_t)j * (kSlotBytes / 16) + (size_t)(chunk * 4) * 128 + row;
+        for (int i = 0; i < kMaxSum; ++i) {
+            if (i < f.nseg) {
+                float4 w[4];
+                if (own_mine && i == f.mine) {
 #pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    const float4 w = src[q * 128];
-                    x[4 * q] = w.x;
-                    x[4 * q + 1] = w.y;
-                    x[4 * q + 2] = w.z;
-                    x[4 * q + 3] = w.w;
+                    for (int q = 0; q < 4; ++q) w[q] = own[q];
+                } else {
+                    const int j = (own_mine && i > f.mine) ? i - 1 : i;  // its place in the ring
+                    const float4* src = base + (size_t)j * (kSlotBytes / 16) + (size_t)chunk * 4 * 128;
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) w[q] = src[q * 128];
                 }
-                ++j;
-            }
-            if (i == 0) {
+                if (i == 0) {
 #pragma unroll
-                for (int e = 0; e < 16; ++e) v[e] = x[e];
-            } else {
+                    for (int q = 0; q < 4; ++q) acc[q] = w[q];
+                } else {
 #pragma unroll
-                for (int e = 0; e < 16; ++e) v[e] += x[e];
+                    for (int q = 0; q < 4; ++q) {
+                        acc[q].x += w[q].x;
+                        acc[q].y += w[q].y;
+                        acc[q].z += w[q].z;
+                        acc[q].w += w[q].w;
+                    }
+                }
             }
+        }
+        float v[16];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            v[4 * q] = acc[q].x;
+            v[4 * q + 1] = acc[q].y;
+            v[4 * q + 2] = acc[q].z;
+            v[4 * q + 3] = acc[q].w;
         }
         store_chunk<SWAP>(p, m0, n0, row, chunk * 16, v);
     }
+    if (threadIdx.x == kEpiThread0) BW_TRACE_AT(11);
     return true;
 }
 
@@ -584,9 +600,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                     BW_TRACE_VAL(8, (fast == 2 ? 2 : 3) | f.nseg << 8 | seg << 16);
                 }
                 if (fast == 2) {
-                    if (last_seg && f.nseg - 1 <= G::kRingSlots)
-                        reduce_tile_bulk<BN, SWAP, R>(p, P, sg.tile, rank, f, true, tbase, row, m0, n0, smem, rbar,
-                                                      abort_flag, seg);
+                    if (last_seg && f.nseg <= G::kMaxSum)
+                        reduce_tile_bulk<BN, SWAP, R, G::kMaxSum>(p, P, sg.tile, rank, f, true, tbase, row, m0, n0,
+                                                                  smem, rbar, abort_flag, seg);
                     else
                         reduce_tile<BN, SWAP, R>(p, P, sg.tile, rank, f, true, tbase, row, m0, n0);
                     release_acc(acc);
@@ -621,9 +637,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                             BW_TRACE_AT(9);
                             BW_TRACE_VAL(8, 1 | f.nseg << 8 | seg << 16);
                         }
-                        if (last_seg && f.nseg - 1 <= G::kRingSlots)
-                            reduce_tile_bulk<BN, SWAP, R>(p, P, sg.tile, rank, f, true, tbase, row, m0, n0, smem, rbar,
-                                                          abort_flag, seg);
+                        if (last_seg && f.nseg <= G::kMaxSum)
+                            reduce_tile_bulk<BN, SWAP, R, G::kMaxSum>(p, P, sg.tile, rank, f, true, tbase, row, m0, n0,
+                                                                      smem, rbar, abort_flag, seg);
                         else
                             reduce_tile<BN, SWAP, R>(p, P, sg.tile, rank, f, false, tbase, row, m0, n0);
                         if (threadIdx.x == kEpiThread0) atomicExch(counter, 0);
