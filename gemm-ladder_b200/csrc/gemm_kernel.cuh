@@ -74,7 +74,10 @@ struct Geom {
     static constexpr int kRingSlots = kBarOffset / kSlotBytes;  // partials the idle ring holds at once
     static constexpr int kMaxSum = kRingSlots + 1 < 8 ? kRingSlots + 1 : 8;  // partials the bulk reduction sums
     static constexpr int kMiscOffset = kBarOffset + kNumBars * 8;
-    static constexpr int kSmemBytes = 1024 + kMiscOffset + 32;  // + slack to align the stages to 1024 bytes
+    // swap-AB: the epilogue transposes each 16-column chunk through two 16 x 128 fp16 buffers
+    static constexpr int kCStageOffset = (kMiscOffset + 32 + 127) / 128 * 128;
+    static constexpr int kCStageBytes = SWAP ? 2 * 16 * 128 * 2 : 0;
+    static constexpr int kSmemBytes = 1024 + kCStageOffset + kCStageBytes;  // + slack to align the stages to 1024 B
     static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "MMA N: a multiple of 16 in [16, 256]");
     static_assert(SWAP || BN % (64 * kRanks) == 0, "B tiles are boxes of 64 columns (per block)");
     static_assert(!(SWAP && PAIR), "the swap-AB form runs on single blocks");
@@ -120,10 +123,15 @@ __device__ __forceinline__ uint64_t desc_kmajor(uint32_t tile, int k) { return s
 __device__ __forceinline__ uint64_t desc_mnmajor(uint32_t tile, int k) { return smem_desc_sw128(tile + 2048u * k, 8192u, 1024u); }
 
 // ------------------------------------------------------------------ the epilogue's stores
-// 16 accumulator columns of TMEM lane `lane` (v) -> C.  Not swapped: C[m0 + lane][n0 + c0 .. +15], two 16-byte stores.
-// Swapped: C[c0 + j][n0 + lane] for j < 16, one fp16 each (a warp writes 64 contiguous bytes per row of C).
+// 16 accumulator columns of TMEM lane `lane` (v) -> C, by all 128 epilogue threads together.
+// Not swapped: C[m0 + lane][n0 + c0 .. +15], two 16-byte stores per thread.
+// Swapped: the values are column n0 + lane of rows c0 .. c0 + 15 of C.  They go through shared memory (cst: two
+// 16 x 128 fp16 buffers, alternating by chunk), so that C is written by 16-byte stores, a warp covering two rows of
+// 256 contiguous bytes, instead of 16 scattered 2-byte stores per thread.  One named barrier per chunk; the buffer of
+// chunk i + 2 is written only after every thread has passed the barrier of chunk i + 1, so after it read chunk i.
 template <bool SWAP>
-__device__ __forceinline__ void store_chunk(const Params& p, int m0, int n0, int lane, int c0, const float (&v)[16])
+__device__ __forceinline__ void store_chunk(const Params& p, int m0, int n0, int lane, int c0, const float (&v)[16],
+                                            __half* cst)
 {
     const Sched& s = p.s;
     if (!SWAP) {
@@ -139,13 +147,18 @@ __device__ __forceinline__ void store_chunk(const Params& p, int m0, int n0, int
         dst[0] = make_uint4(h[0], h[1], h[2], h[3]);
         dst[1] = make_uint4(h[4], h[5], h[6], h[7]);
     } else {
-        const int n = n0 + lane;
-        if (n >= s.N) return;
-        __half* col = p.C + n;
+        __half* buf = cst + ((c0 >> 4) & 1) * (16 * 128);
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-            const int m = c0 + j;
-            if (m < s.M) col[(size_t)m * s.N] = __float2half_rn(v[j]);
+        for (int j = 0; j < 16; ++j) buf[j * 128 + lane] = __float2half_rn(v[j]);
+        named_bar_sync(1, 128);
+        const int t = threadIdx.x - kEpiThread0;
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            const int piece = t + 128 * k;  // 256 pieces of 8 fp16: 16 rows x 16 pieces
+            const int mm = piece >> 4, nn = (piece & 15) * 8;
+            const int m = c0 + mm, n = n0 + nn;
+            if (m < s.M && n < s.N)
+                *reinterpret_cast<uint4*>(p.C + (size_t)m * s.N + n) = *reinterpret_cast<const uint4*>(buf + mm * 128 + nn);
         }
     }
 }
@@ -168,7 +181,7 @@ __device__ __forceinline__ float4* slot_vec(const Params& p, long long slot, int
 // with one partial in memory four chunks are on their way at once, instead of one L2 round trip per chunk.
 template <int BN, bool SWAP, int RANKS>
 __device__ __noinline__ void reduce_tile(const Params& p, int P, int tile, int rank, Fixup f, bool own_mine,
-                                            uint32_t tbase, int row, int m0, int n0)
+                                            uint32_t tbase, int row, int m0, int n0, __half* cst)
 {
     constexpr int kWin = 4;
     constexpr int kChunks = BN / 16;
@@ -238,7 +251,7 @@ __device__ __noinline__ void reduce_tile(const Params& p, int P, int tile, int r
 #pragma unroll
                         for (int e = 0; e < 16; ++e) v[e] += own[e];
                     }
-                    store_chunk<SWAP>(p, m0, n0, row, chunk * 16, v);
+                    store_chunk<SWAP>(p, m0, n0, row, chunk * 16, v, cst);
                 }
             }
         }
@@ -251,8 +264,8 @@ __device__ __noinline__ void reduce_tile(const Params& p, int P, int tile, int r
 // registers.  Returns false if the copy did not complete within the wait limit (the block's abort flag is up).
 template <int BN, bool SWAP, int RANKS, int kMaxSum>
 __device__ __noinline__ bool reduce_tile_bulk(const Params& p, int P, int tile, int rank, Fixup f, bool own_mine,
-                                              uint32_t tbase, int row, int m0, int n0, uint8_t* ring, uint64_t* rbar,
-                                              volatile int* abort_flag, int seg)
+                                              uint32_t tbase, int row, int m0, int n0, __half* cst, uint8_t* ring,
+                                              uint64_t* rbar, volatile int* abort_flag, int seg)
 {
     constexpr int kSlotBytes = 128 * BN * 4;
     constexpr int kChunks = BN / 16;
@@ -321,7 +334,7 @@ __device__ __noinline__ bool reduce_tile_bulk(const Params& p, int P, int tile, 
             v[4 * q + 2] = acc[q].z;
             v[4 * q + 3] = acc[q].w;
         }
-        store_chunk<SWAP>(p, m0, n0, row, chunk * 16, v);
+        store_chunk<SWAP>(p, m0, n0, row, chunk * 16, v, cst);
     }
     if (threadIdx.x == kEpiThread0) BW_TRACE_AT(11);
     return true;
@@ -343,6 +356,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* tempty = tfull + 2;
     uint64_t* drain = tempty + 2;
     uint64_t* rbar = drain + 1;  // the bulk reduction's copies of partials
+    __half* cst = reinterpret_cast<__half*>(smem + G::kCStageOffset);  // swap-AB epilogue transpose buffers
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + G::kMiscOffset);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
     volatile int* reduce_flag = abort_flag + 1;
@@ -579,7 +593,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     float v[16];
 #pragma unroll
                     for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[j]);
-                    store_chunk<SWAP>(p, m0, n0, row, c0, v);
+                    store_chunk<SWAP>(p, m0, n0, row, c0, v, cst);
                 }
                 release_acc(acc);
             } else {
@@ -602,9 +616,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (fast == 2) {
                     if (last_seg && f.nseg <= G::kMaxSum)
                         reduce_tile_bulk<BN, SWAP, R, G::kMaxSum>(p, P, sg.tile, rank, f, true, tbase, row, m0, n0,
-                                                                  smem, rbar, abort_flag, seg);
+                                                                  cst, smem, rbar, abort_flag, seg);
                     else
-                        reduce_tile<BN, SWAP, R>(p, P, sg.tile, rank, f, true, tbase, row, m0, n0);
+                        reduce_tile<BN, SWAP, R>(p, P, sg.tile, rank, f, true, tbase, row, m0, n0, cst);
                     release_acc(acc);
                     if (threadIdx.x == kEpiThread0) atomicExch(counter, 0);
                 } else {
@@ -639,9 +653,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                         }
                         if (last_seg && f.nseg <= G::kMaxSum)
                             reduce_tile_bulk<BN, SWAP, R, G::kMaxSum>(p, P, sg.tile, rank, f, true, tbase, row, m0, n0,
-                                                                      smem, rbar, abort_flag, seg);
+                                                                      cst, smem, rbar, abort_flag, seg);
                         else
-                            reduce_tile<BN, SWAP, R>(p, P, sg.tile, rank, f, false, tbase, row, m0, n0);
+                            reduce_tile<BN, SWAP, R>(p, P, sg.tile, rank, f, false, tbase, row, m0, n0, cst);
                         if (threadIdx.x == kEpiThread0) atomicExch(counter, 0);
                     }
                     if (last_seg) release_acc(acc);

@@ -70,9 +70,11 @@ inline int plan_tmem_cols(int bn)
     while (c < 2 * bn) c *= 2;
     return c;
 }
-inline int plan_smem_bytes(int bn, int ranks)
+inline int plan_smem_bytes(int bn, int ranks, bool swap)
 {
-    return 1024 + plan_stages(bn, ranks) * plan_stage_bytes(bn, ranks) + (2 * plan_stages(bn, ranks) + 6) * 8 + 32;
+    const int misc = plan_stages(bn, ranks) * plan_stage_bytes(bn, ranks) + (2 * plan_stages(bn, ranks) + 6) * 8;
+    const int cstage = (misc + 32 + 127) / 128 * 128;
+    return 1024 + cstage + (swap ? 2 * 16 * 128 * 2 : 0);
 }
 
 inline bool shape_ok(int M, int N, int K)
@@ -157,7 +159,7 @@ inline int make_plan(int M, int N, int K, int sms, int pairs, int variant, bw_pl
     }
     q.grid = P * ranks;
     q.stages = plan_stages(q.bn, ranks);
-    q.smem_bytes = plan_smem_bytes(q.bn, ranks);
+    q.smem_bytes = plan_smem_bytes(q.bn, ranks, swap);
     q.tmem_cols = plan_tmem_cols(q.bn);
     q.counters = q.sk_tiles * ranks;
     Sched sc = {};
