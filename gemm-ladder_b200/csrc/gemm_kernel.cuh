@@ -66,7 +66,9 @@ struct Geom {
     static constexpr int kXBytes = 128 * kBK * 2;            // this block's MMA-A operand: 128 rows x 64 K
     static constexpr int kYBytes = (BN / kRanks) * kBK * 2;  // this block's MMA-B operand: BN (PAIR: BN / 2) x 64 K
     static constexpr int kStageBytes = kXBytes + kYBytes;
-    static constexpr int kStages = (BW_RING_BYTES / kStageBytes) < BW_MAX_STAGES ? (BW_RING_BYTES / kStageBytes) : BW_MAX_STAGES;
+    static constexpr int kCStageBytes = SWAP ? 2 * 16 * 128 * 2 : 0;  // swap-AB epilogue transpose buffers
+    static constexpr int kRingFit = (BW_SMEM_LIMIT - 1024 - 512 - kCStageBytes) / kStageBytes;
+    static constexpr int kStages = kRingFit < BW_MAX_STAGES ? kRingFit : BW_MAX_STAGES;
     static constexpr int kTmemCols = pow2_at_least(2 * BN < 32 ? 32 : 2 * BN, 32);  // two accumulators
     static constexpr int kBarOffset = kStages * kStageBytes;
     static constexpr int kNumBars = 2 * kStages + 6;  // full, empty, tmem full x2, tmem empty x2, drain, reduce
@@ -76,13 +78,12 @@ struct Geom {
     static constexpr int kMiscOffset = kBarOffset + kNumBars * 8;
     // swap-AB: the epilogue transposes each 16-column chunk through two 16 x 128 fp16 buffers
     static constexpr int kCStageOffset = (kMiscOffset + 32 + 127) / 128 * 128;
-    static constexpr int kCStageBytes = SWAP ? 2 * 16 * 128 * 2 : 0;
     static constexpr int kSmemBytes = 1024 + kCStageOffset + kCStageBytes;  // + slack to align the stages to 1024 B
     static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "MMA N: a multiple of 16 in [16, 256]");
     static_assert(SWAP || BN % (64 * kRanks) == 0, "B tiles are boxes of 64 columns (per block)");
     static_assert(!(SWAP && PAIR), "the swap-AB form runs on single blocks");
     static_assert(kYBytes % 1024 == 0 && kXBytes % 1024 == 0, "operand tiles on 1024-byte swizzle atoms");
-    static_assert(kStages >= 2 && kSmemBytes <= 227 * 1024, "shared memory");
+    static_assert(kStages >= 2 && kSmemBytes <= BW_SMEM_LIMIT, "shared memory");
     static_assert(kTmemCols <= 512, "tensor memory");
 };
 

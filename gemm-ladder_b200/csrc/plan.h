@@ -23,8 +23,8 @@
 #ifndef BW_FIXUP_KB
 #define BW_FIXUP_KB 12.0       // the cost of one extra partial of a 256-column tile, in K-blocks of MMA work
 #endif
-#ifndef BW_RING_BYTES
-#define BW_RING_BYTES 204800   // shared memory for the ring of stages
+#ifndef BW_SMEM_LIMIT
+#define BW_SMEM_LIMIT 232448   // dynamic shared memory per block on sm_100 (227 KB)
 #endif
 #ifndef BW_MAX_STAGES
 #define BW_MAX_STAGES 12
@@ -57,11 +57,13 @@ inline const char* variant_name(int v)
     }
 }
 
-// The kernels' geometry, as gemm_kernel.cuh's Geom computes it (checked against it at launch in bwgemm.cu).
+// The kernels' geometry, as gemm_kernel.cuh's Geom computes it (checked against it at launch in bwgemm.cu): the ring
+// takes what the 227 KB leave after the alignment slack, the barriers and the swap-AB epilogue's transpose buffers.
 inline int plan_stage_bytes(int bn, int ranks) { return 128 * 64 * 2 + (bn / ranks) * 64 * 2; }
-inline int plan_stages(int bn, int ranks)
+inline int plan_cstage_bytes(bool swap) { return swap ? 2 * 16 * 128 * 2 : 0; }
+inline int plan_stages(int bn, int ranks, bool swap)
 {
-    const int s = BW_RING_BYTES / plan_stage_bytes(bn, ranks);
+    const int s = (BW_SMEM_LIMIT - 1024 - 512 - plan_cstage_bytes(swap)) / plan_stage_bytes(bn, ranks);
     return s < BW_MAX_STAGES ? s : BW_MAX_STAGES;
 }
 inline int plan_tmem_cols(int bn)
@@ -72,9 +74,10 @@ inline int plan_tmem_cols(int bn)
 }
 inline int plan_smem_bytes(int bn, int ranks, bool swap)
 {
-    const int misc = plan_stages(bn, ranks) * plan_stage_bytes(bn, ranks) + (2 * plan_stages(bn, ranks) + 6) * 8;
+    const int st = plan_stages(bn, ranks, swap);
+    const int misc = st * plan_stage_bytes(bn, ranks) + (2 * st + 6) * 8;
     const int cstage = (misc + 32 + 127) / 128 * 128;
-    return 1024 + cstage + (swap ? 2 * 16 * 128 * 2 : 0);
+    return 1024 + cstage + plan_cstage_bytes(swap);
 }
 
 inline bool shape_ok(int M, int N, int K)
@@ -158,7 +161,7 @@ inline int make_plan(int M, int N, int K, int sms, int pairs, int variant, bw_pl
         if (q.sk_iters < P) return BW_ERR_ARG;  // every block owns at least one stream-K K-block
     }
     q.grid = P * ranks;
-    q.stages = plan_stages(q.bn, ranks);
+    q.stages = plan_stages(q.bn, ranks, swap);
     q.smem_bytes = plan_smem_bytes(q.bn, ranks, swap);
     q.tmem_cols = plan_tmem_cols(q.bn);
     q.counters = q.sk_tiles * ranks;
