@@ -50,7 +50,7 @@ __host__ __device__ constexpr int pow2_at_least(int v, int p) { return p >= v ? 
 // Optional timeline (compiled in with -DBW_TRACE only): per block, %globaltimer at kernel entry, after set-up, the
 // MMA's first full stage, its last commit, the epilogue's end, and the exit.
 #ifdef BW_TRACE
-constexpr int kTraceSlots = 12;
+constexpr int kTraceSlots = 16;
 __device__ unsigned long long g_trace[1024 * kTraceSlots];
 #define BW_TRACE_AT(slot) (g_trace[blockIdx.x * kTraceSlots + (slot)] = globaltimer_ns())
 #define BW_TRACE_VAL(slot, v) (g_trace[blockIdx.x * kTraceSlots + (slot)] = (unsigned long long)(v))
@@ -478,20 +478,34 @@ __global__ void __launch_bounds__(kThreads, 1)
             int stage = 0, acc = 0, seg = 0;
             uint32_t ph = 0, aph = 0;
             bool ok = true;
+#ifdef BW_TRACE
+            unsigned long long w_full = 0, w_acc = 0, n_kb = 0;
+#endif
             while (ok && it.next(s, P, sg)) {
+#ifdef BW_TRACE
+                const unsigned long long ta0 = globaltimer_ns();
+#endif
                 if (!wait_bounded(&tempty[acc], aph ^ 1u, abort_flag, p.wait_ns, site(1, 3, acc), seg)) {
                     ok = false;
                     break;
                 }
+#ifdef BW_TRACE
+                w_acc += globaltimer_ns() - ta0;
+#endif
                 tc_fence_after();
                 const uint32_t d = tmem_base + (uint32_t)(acc * BN);
                 for (int kb = sg.k0; kb < sg.k1; ++kb) {
+#ifdef BW_TRACE
+                    const unsigned long long tf0 = globaltimer_ns();
+#endif
                     if (!wait_bounded(&full[stage], ph, abort_flag, p.wait_ns, site(1, 0, stage), seg)) {
                         ok = false;
                         break;
                     }
 #ifdef BW_TRACE
                     if (seg == 0 && kb == sg.k0) BW_TRACE_AT(2);
+                    else w_full += globaltimer_ns() - tf0;
+                    ++n_kb;
 #endif
                     tc_fence_after();
                     const uint32_t sx = smem_u32(smem + stage * G::kStageBytes), sy = sx + G::kXBytes;
@@ -532,6 +546,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 ++seg;
             }
             BW_TRACE_AT(3);
+            BW_TRACE_VAL(12, w_full);
+            BW_TRACE_VAL(13, w_acc);
+            BW_TRACE_VAL(14, n_kb);
             if (!ok) {  // let the MMAs in flight finish before the tensor memory is freed
                 if (PAIR)
                     mma_commit_pair(mapa_shared(smem_u32(drain), 0));
