@@ -56,7 +56,32 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--profile-arm", choices=["ours", "cublas"], default=None,
+                    help="for ncu: 3 warm-up calls, then one call in an NVTX range named 'timed', and exit")
     return ap.parse_args()
+
+
+def profile_call(args):
+    """One call of an arm at the workload, for `ncu --nvtx --nvtx-include timed/` (no timing, no JSON line)."""
+    import torch
+
+    import bwgemm
+
+    torch.cuda.set_device(0)
+    M, N, K = WORKLOADS[args.workload]
+    A, B = make_sets(M, N, K, seed=1)
+    C = torch.empty((M, N), dtype=torch.float16, device="cuda")
+    if args.profile_arm == "cublas":
+        call = lambda i: torch.matmul(A[i % 3], B[i % 3], out=C)  # noqa: E731
+    else:
+        call = lambda i: bwgemm.gemm(A[i % 3], B[i % 3], C, variant=args.variant)  # noqa: E731
+    for i in range(3):
+        call(i)
+    torch.cuda.synchronize()
+    torch.cuda.nvtx.range_push("timed")
+    call(3)
+    torch.cuda.nvtx.range_pop()
+    torch.cuda.synchronize()
 
 
 def peaks():
@@ -408,7 +433,9 @@ def main():
         M, N, K = (int(x) for x in args.shape.lower().split("x"))
         WORKLOADS[args.shape] = (M, N, K)
         args.workload = args.shape
-    if args.impl == "reference":
+    if args.profile_arm:
+        profile_call(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)
