@@ -36,6 +36,7 @@ for _p in (ROOT, PKG, os.path.join(ROOT, "tests")):
         sys.path.insert(0, _p)
 
 WORKLOADS = {
+    "tp_mlp": None,  # the tensor-parallel MLP block (gateup + down + reduce-scatter), --tp-m tokens
     "config1": (4608, 5632, 8192),
     "ladder": (8192, 8192, 8192),
     "ladder_4096": (4096, 6144, 8192),
@@ -52,6 +53,7 @@ def parse():
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="config1")
     ap.add_argument("--shape", default=None, help="MxNxK in place of the workload (profiling a shape)")
     ap.add_argument("--variant", type=int, default=0)
+    ap.add_argument("--tp-m", type=int, default=8192, help="tokens of the tp_mlp workload (2048 or 8192)")
     ap.add_argument("--sweep", action="store_true", help="also time the judge's 17 shapes against cuBLAS")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
@@ -297,6 +299,75 @@ def sweep(args, stream_runs=3):
             "reference": "torch.matmul fp16 (cuBLAS heuristic), CUDA graphs, 3 rotating input sets"}
 
 
+def run_tp_mlp(args):
+    """the MLP block of a Llama-3-70B layer (hidden 8192, MLP 28672) over the GPUs, Megatron
+    tensor parallelism: gateup column-parallel and down row-parallel through the rung's GEMMs, the fp32 partials of
+    down reduced by an NCCL reduce-scatter (tp_mlp.py).  Total work fixed: strong scaling."""
+    import torch
+
+    import bwgemm
+    import tp_mlp
+
+    rank, world, local = dist_setup(args)
+    M, hidden, f = args.tp_m, 8192, 28672
+    gx = torch.Generator(device="cuda")
+    gx.manual_seed(7)  # the same tokens on every rank
+    X = (torch.rand((M, hidden), generator=gx, device="cuda") * 2 - 1).half()
+    gw = torch.Generator(device="cuda")
+    gw.manual_seed(100 + rank)  # this rank's shards (synthetic weights, scaled to keep the activations in range)
+    W1 = ((torch.rand((hidden, 2 * f // world), generator=gw, device="cuda") * 2 - 1) / hidden ** 0.5).half()
+    W2 = ((torch.rand((f // world, hidden), generator=gw, device="cuda") * 2 - 1) / f ** 0.5).half()
+    blk = tp_mlp.TPMLP(W1, W2, rank, world, bwgemm.gemm, bwgemm.gemm_f32out,
+                       tp_mlp.nccl_reduce_scatter if world > 1 else None)
+    stream = torch.cuda.current_stream()
+    for _ in range(max(3, args.warmup)):
+        blk.forward(X)
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        barrier(world)
+        e0.record(stream)
+        for _ in range(args.steps):
+            Y = blk.forward(X)
+        e1.record(stream)
+        barrier(world)
+    t = dist_max(e0.elapsed_time(e1) / 1e3, world)
+    flops = tp_mlp.TPMLP.flops(M, hidden, f)
+    # end to end: the tokens from pinned host memory, this rank's rows of the result back
+    hX = torch.empty((M, hidden), dtype=torch.float16, pin_memory=True)
+    hX.copy_(X)
+    hY = torch.empty((M // world, hidden), dtype=torch.float16, pin_memory=True)
+    steps_e2e = max(3, min(args.steps, 10))
+    barrier(world)
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record(stream)
+    for _ in range(steps_e2e):
+        X.copy_(hX, non_blocking=True)
+        hY.copy_(blk.forward(X), non_blocking=True)
+    f1.record(stream)
+    barrier(world)
+    te = dist_max(f0.elapsed_time(f1) / 1e3, world)
+    code = bwgemm.status()[0]
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps({
+            "metric": "TFLOP/s of the tensor-parallel MLP block (gateup + down + reduce-scatter), BASELINE config 4",
+            "value": round(flops * args.steps / t / 1e12, 2), "unit": "TFLOP/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(t / args.steps * 1e3, 4),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp16 (fp32 accumulate)",
+            "data": "synthetic: seeded uniform tokens and weights",
+            "config": {"workload": f"tp_mlp M={M} hidden={hidden} mlp={f}", "M": M, "parallelism": f"tp{world}",
+                       "collective": "NCCL reduce-scatter of fp32 partials" if world > 1 else "none"},
+            "clocks": clk.summary(), "gpu_launches": 2 * args.steps, "device_status": code,
+            "e2e": {"value": round(flops * steps_e2e / te / 1e12, 2), "unit": "TFLOP/s",
+                    "h2d_bytes_per_step": M * hidden * 2, "d2h_bytes_per_step": M // world * hidden * 2},
+        }), flush=True)
+
+
 def run_ours(args):
     import torch
 
@@ -397,7 +468,8 @@ def run_reference(args):
         return
     from oracle import oracle
 
-    M, N, K = WORKLOADS[args.workload]
+    # tp_mlp: the block's gateup GEMM (M x 57344 x 8192) stands for it on the host
+    M, N, K = WORKLOADS[args.workload] if args.workload != "tp_mlp" else (args.tp_m, 57344, 8192)
     threads = os.cpu_count() or 1
     budget = 90.0  # seconds for warm-up + timed steps
     per_step = budget / max(1, args.steps + args.warmup)
@@ -437,6 +509,8 @@ def main():
         profile_call(args)
     elif args.impl == "reference":
         run_reference(args)
+    elif args.workload == "tp_mlp":
+        run_tp_mlp(args)
     else:
         run_ours(args)
 

@@ -65,6 +65,8 @@ def lib():
         L.bw_gemm_f16.restype = i
         L.bw_gemm_f16_variant.argtypes = [vp, vp, vp, i, i, i, vp, i]
         L.bw_gemm_f16_variant.restype = i
+        L.bw_gemm_f16_f32out.argtypes = [vp, vp, vp, i, i, i, vp]
+        L.bw_gemm_f16_f32out.restype = i
         L.bw_gemm_variant_count.argtypes = []
         L.bw_gemm_variant_count.restype = i
         L.bw_gemm_variant_name.argtypes = [i]
@@ -138,6 +140,27 @@ def gemm(A, B, C=None, variant=0, stream=None):
     s = stream if stream is not None else torch.cuda.current_stream(A.device)
     with torch.cuda.device(A.device):
         check(gemm_ptr(A.data_ptr(), B.data_ptr(), C.data_ptr(), M, N, K, s.cuda_stream, variant))
+    return C
+
+
+def gemm_f32out(A, B, C=None, stream=None):
+    """C (fp32, M x N) = A B for fp16 CUDA tensors: the partial sums of a row-parallel layer."""
+    import torch
+
+    M, K = A.shape
+    K2, N = B.shape
+    if K2 != K:
+        raise ValueError(f"A is {M} x {K} but B is {K2} x {N}")
+    for t in (A, B):
+        if t.dtype != torch.float16 or not t.is_cuda or not t.is_contiguous():
+            raise ValueError("A and B must be contiguous fp16 CUDA tensors")
+    if C is None:
+        C = torch.empty((M, N), dtype=torch.float32, device=A.device)
+    elif C.shape != (M, N) or C.dtype != torch.float32 or not C.is_contiguous():
+        raise ValueError("C must be a contiguous fp32 M x N tensor")
+    s = stream if stream is not None else torch.cuda.current_stream(A.device)
+    with torch.cuda.device(A.device):
+        check(lib().bw_gemm_f16_f32out(A.data_ptr(), B.data_ptr(), C.data_ptr(), M, N, K, s.cuda_stream))
     return C
 
 

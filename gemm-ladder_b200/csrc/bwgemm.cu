@@ -159,11 +159,11 @@ cudaLaunchConfig_t launch_config(int grid, cudaStream_t st, cudaLaunchAttribute*
     return cfg;
 }
 
-template <int BN, bool SWAP, bool PAIR>
+template <int BN, bool SWAP, bool PAIR, bool F32OUT = false>
 int set_smem_limit(DeviceState& d, unsigned bit)
 {
     if (d.attrs & bit) return BW_OK;
-    cudaError_t e = cudaFuncSetAttribute(gemm_kernel<BN, SWAP, PAIR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaError_t e = cudaFuncSetAttribute(gemm_kernel<BN, SWAP, PAIR, F32OUT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          Geom<BN, SWAP, PAIR>::kSmemBytes);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
     d.attrs |= bit;
@@ -188,7 +188,7 @@ int pair_occupancy(DeviceState& d)
     return BW_OK;
 }
 
-template <int BN, bool SWAP, bool PAIR>
+template <int BN, bool SWAP, bool PAIR, bool F32OUT = false>
 int launch_kernel(DeviceState& d, unsigned bit, const bw_plan& q, const CUtensorMap& mx, const CUtensorMap& my,
                   const Params& p, cudaStream_t st)
 {
@@ -197,19 +197,25 @@ int launch_kernel(DeviceState& d, unsigned bit, const bw_plan& q, const CUtensor
         snprintf(g_errbuf, sizeof g_errbuf, "plan and kernel geometry disagree (bn %d)", BN);
         return BW_ERR_LAUNCH;
     }
-    int rc = set_smem_limit<BN, SWAP, PAIR>(d, bit);
+    int rc = set_smem_limit<BN, SWAP, PAIR, F32OUT>(d, bit);
     if (rc) return rc;
     cudaLaunchAttribute attr[1];
     const cudaLaunchConfig_t cfg = launch_config<BN, SWAP, PAIR>(q.grid, st, attr);
-    cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_kernel<BN, SWAP, PAIR>, mx, my, p);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_kernel<BN, SWAP, PAIR, F32OUT>, mx, my, p);
     if (e != cudaSuccess) return cuda_fail(e, "kernel launch");
     return BW_OK;
 }
 
 // The plan's kernel instance, launched.
 int dispatch(DeviceState& d, const bw_plan& q, const CUtensorMap& mx, const CUtensorMap& my, const Params& p,
-             cudaStream_t st)
+             cudaStream_t st, bool f32out = false)
 {
+    if (f32out) {  // fp32 C: the plan is a TILE or PAIR one (no swap-AB)
+        if (q.kernel == BW_KERNEL_PAIR) return launch_kernel<256, false, true, true>(d, 1u << 12, q, mx, my, p, st);
+        if (q.kernel == BW_KERNEL_TILE && q.bn == 256)
+            return launch_kernel<256, false, false, true>(d, 1u << 13, q, mx, my, p, st);
+        return BW_ERR_ARG;
+    }
     if (q.kernel == BW_KERNEL_PAIR) return launch_kernel<256, false, true>(d, kBitPair, q, mx, my, p, st);
     if (q.kernel == BW_KERNEL_TILE) {
         switch (q.bn) {
@@ -248,7 +254,7 @@ Params make_params(const bw_plan& q, int M, int N, int K, void* C, float* work, 
     p.s.splits = q.splits;
     p.s.sk_iters = q.sk_iters;
     p.s.group_rows = q.group_rows;
-    p.C = static_cast<__half*>(C);
+    p.C = C;
     p.work = work;
     p.counters = counters;
     p.wait_ns = g_wait_ns;
@@ -264,7 +270,7 @@ bool make_maps(const bw_plan& q, const void* A, const void* B, int M, int N, int
     return make_map(mx, B, N, K, 64, 64) && make_map(my, A, K, M, 64, q.bn);
 }
 
-int gemm(const void* A, const void* B, void* C, int M, int N, int K, cudaStream_t st, int variant)
+int gemm(const void* A, const void* B, void* C, int M, int N, int K, cudaStream_t st, int variant, bool f32out = false)
 {
     if (variant < 0 || variant >= kVariants) return BW_ERR_ARG;
     if (!shape_ok(M, N, K)) return BW_ERR_SHAPE;
@@ -286,7 +292,7 @@ int gemm(const void* A, const void* B, void* C, int M, int N, int K, cudaStream_
         snprintf(g_errbuf, sizeof g_errbuf, "cuTensorMapEncodeTiled failed");
         return BW_ERR_LAUNCH;
     }
-    return dispatch(*d, q, mx, my, make_params(q, M, N, K, C, d->work, d->counters), st);
+    return dispatch(*d, q, mx, my, make_params(q, M, N, K, C, d->work, d->counters), st, f32out);
 }
 
 }  // namespace
@@ -301,6 +307,12 @@ BW_API int bw_gemm_f16(const void* A, const void* B, void* C, int M, int N, int 
 BW_API int bw_gemm_f16_variant(const void* A, const void* B, void* C, int M, int N, int K, void* stream, int variant)
 {
     return bw::gemm(A, B, C, M, N, K, static_cast<cudaStream_t>(stream), variant);
+}
+
+BW_API int bw_gemm_f16_f32out(const void* A, const void* B, void* C, int M, int N, int K, void* stream)
+{
+    // the rule without swap-AB (variant 2): SM-pair tiles at every M, written in fp32
+    return bw::gemm(A, B, C, M, N, K, static_cast<cudaStream_t>(stream), 2, true);
 }
 
 BW_API int bw_gemm_variant_count(void) { return bw::kVariants; }

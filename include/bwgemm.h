@@ -49,6 +49,14 @@ int bw_gemm_f16(const void* A, const void* B, void* C, int M, int N, int K, void
  */
 int bw_gemm_f16_variant(const void* A, const void* B, void* C, int M, int N, int K, void* stream, int variant);
 
+/*
+ * C = A B with C written in fp32 (M x N row-major, 16-byte aligned), A and B fp16 as above: the partial sums of a
+ * row-parallel layer, reduced across GPUs by a reduce-scatter before they are rounded (the tensor-parallel MLP block
+ * of the B200 configs: down = H_r W2_r on each rank, then an NCCL reduce-scatter of the fp32 partials).  SM-pair tiles
+ * at every M.  No reference counterpart: the reference's candidates write fp16 only.
+ */
+int bw_gemm_f16_f32out(const void* A, const void* B, void* C, int M, int N, int K, void* stream);
+
 /* The number of variants.  Replaces: the weak `int g_nvar` (probe/probe.cu:40, hopper/verif.cu:38, hopper/step7.cu:16). */
 int bw_gemm_variant_count(void);
 

@@ -264,3 +264,53 @@ def test_graph_survives_a_later_workspace_growth(oracle_mod):
         assert bwgemm.status()[0] == 0
         assert_parity(bits(C), ref, K, oracle_mod, "graph replayed after a workspace growth")
     assert bwgemm.dirty() == 0
+
+
+@pytest.mark.parametrize("shape", [(256, 512, 1024), (2048, 8192, 28672 // 8), (4608, 5632, 8192), (144, 640, 320)],
+                         ids=lambda s: "x".join(map(str, s)))
+def test_f32out_partials(shape, oracle_mod):
+    """bw_gemm_f16_f32out: fp32 C within fp32 accumulation error of the fp64 oracle, and (same plan as the fp16 entry
+    above M = 128) rounded to fp16 it is the fp16 entry's result bit for bit."""
+    M, N, K = shape
+    A, B = oracle_mod.judge_inputs(M, N, K)
+    dA, dB = to_dev(A), to_dev(B)
+    C32 = torch.full((M, N), float("nan"), dtype=torch.float32, device="cuda")
+    bwgemm.gemm_f32out(dA, dB, C32)
+    torch.cuda.synchronize()
+    assert bwgemm.status()[0] == 0
+    got = C32.cpu().numpy().astype(np.float64)
+    assert np.isfinite(got).all()
+    rng = np.random.default_rng(3)
+    for i, j in zip(rng.integers(0, M, 512), rng.integers(0, N, 512)):
+        ref = oracle_mod.dot_f64(A, B, int(i), int(j))
+        assert abs(got[i, j] - ref) <= 1e-4 * K ** 0.5, (i, j, got[i, j], ref)
+    C16 = run(dA, dB)
+    if M > 128:
+        assert torch.equal(C32.half(), C16), "fp32 partials rounded differ from the fp16 entry's result"
+    assert bwgemm.dirty() == 0
+
+
+def test_tp_mlp_block_on_one_gpu():
+    """The tensor-parallel block at one rank (no collective) through the rung's GEMMs, against torch in fp32."""
+    import tp_mlp
+
+    M, hidden, f = 512, 1024, 2048
+    g = torch.Generator(device="cuda")
+    g.manual_seed(9)
+    X = (torch.rand((M, hidden), generator=g, device="cuda") * 2 - 1).half()
+    W1 = ((torch.rand((hidden, 2 * f), generator=g, device="cuda") * 2 - 1) / hidden ** 0.5).half()
+    W2 = ((torch.rand((f, hidden), generator=g, device="cuda") * 2 - 1) / f ** 0.5).half()
+    blk = tp_mlp.TPMLP(tp_mlp.shard_gateup(W1, 0, 1), tp_mlp.shard_down(W2, 0, 1), 0, 1, bwgemm.gemm,
+                       bwgemm.gemm_f32out)
+    Y = blk.forward(X)
+    torch.cuda.synchronize()
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        H = (X.float() @ W1.float()).half()
+        A = (torch.nn.functional.silu(H[:, :f].float()) * H[:, f:].float()).half()
+        ref = A.float() @ W2.float()
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+    gap = ((Y.float() - ref).abs().max() / ref.abs().max()).item()
+    assert gap <= 2e-3, gap
