@@ -54,6 +54,7 @@ def parse():
     ap.add_argument("--shape", default=None, help="MxNxK in place of the workload (profiling a shape)")
     ap.add_argument("--variant", type=int, default=0)
     ap.add_argument("--tp-m", type=int, default=8192, help="tokens of the tp_mlp workload (2048 or 8192)")
+    ap.add_argument("--tp-unfused", action="store_true", help="tp_mlp: the activation as separate torch ops")
     ap.add_argument("--sweep", action="store_true", help="also time the judge's 17 shapes against cuBLAS")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
@@ -317,8 +318,10 @@ def run_tp_mlp(args):
     gw.manual_seed(100 + rank)  # this rank's shards (synthetic weights, scaled to keep the activations in range)
     W1 = ((torch.rand((hidden, 2 * f // world), generator=gw, device="cuda") * 2 - 1) / hidden ** 0.5).half()
     W2 = ((torch.rand((f // world, hidden), generator=gw, device="cuda") * 2 - 1) / f ** 0.5).half()
+    # (random shards: the interleaved gate / up layout of the fused activation needs no permutation here)
     blk = tp_mlp.TPMLP(W1, W2, rank, world, bwgemm.gemm, bwgemm.gemm_f32out,
-                       tp_mlp.nccl_reduce_scatter if world > 1 else None)
+                       tp_mlp.nccl_reduce_scatter if world > 1 else None,
+                       gemm_swiglu=None if args.tp_unfused else bwgemm.gemm_swiglu)
     stream = torch.cuda.current_stream()
     for _ in range(max(3, args.warmup)):
         blk.forward(X)
@@ -361,6 +364,7 @@ def run_tp_mlp(args):
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp16 (fp32 accumulate)",
             "data": "synthetic: seeded uniform tokens and weights",
             "config": {"workload": f"tp_mlp M={M} hidden={hidden} mlp={f}", "M": M, "parallelism": f"tp{world}",
+                       "activation": "separate torch ops" if args.tp_unfused else "fused in the gateup epilogue",
                        "collective": "NCCL reduce-scatter of fp32 partials" if world > 1 else "none"},
             "clocks": clk.summary(), "gpu_launches": 2 * args.steps, "device_status": code,
             "e2e": {"value": round(flops * steps_e2e / te / 1e12, 2), "unit": "TFLOP/s",

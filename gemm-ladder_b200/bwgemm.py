@@ -67,6 +67,8 @@ def lib():
         L.bw_gemm_f16_variant.restype = i
         L.bw_gemm_f16_f32out.argtypes = [vp, vp, vp, i, i, i, vp]
         L.bw_gemm_f16_f32out.restype = i
+        L.bw_gemm_f16_swiglu.argtypes = [vp, vp, vp, i, i, i, vp]
+        L.bw_gemm_f16_swiglu.restype = i
         L.bw_gemm_variant_count.argtypes = []
         L.bw_gemm_variant_count.restype = i
         L.bw_gemm_variant_name.argtypes = [i]
@@ -161,6 +163,27 @@ def gemm_f32out(A, B, C=None, stream=None):
     s = stream if stream is not None else torch.cuda.current_stream(A.device)
     with torch.cuda.device(A.device):
         check(lib().bw_gemm_f16_f32out(A.data_ptr(), B.data_ptr(), C.data_ptr(), M, N, K, s.cuda_stream))
+    return C
+
+
+def gemm_swiglu(A, B, C=None, stream=None):
+    """C (M x N/2, fp16) = silu(A B_gate) * (A B_up), B's 256-column groups being 128 gate then 128 up columns."""
+    import torch
+
+    M, K = A.shape
+    K2, N = B.shape
+    if K2 != K:
+        raise ValueError(f"A is {M} x {K} but B is {K2} x {N}")
+    for t in (A, B):
+        if t.dtype != torch.float16 or not t.is_cuda or not t.is_contiguous():
+            raise ValueError("A and B must be contiguous fp16 CUDA tensors")
+    if C is None:
+        C = torch.empty((M, N // 2), dtype=torch.float16, device=A.device)
+    elif C.shape != (M, N // 2) or C.dtype != torch.float16 or not C.is_contiguous():
+        raise ValueError("C must be a contiguous fp16 M x N/2 tensor")
+    s = stream if stream is not None else torch.cuda.current_stream(A.device)
+    with torch.cuda.device(A.device):
+        check(lib().bw_gemm_f16_swiglu(A.data_ptr(), B.data_ptr(), C.data_ptr(), M, N, K, s.cuda_stream))
     return C
 
 

@@ -159,11 +159,11 @@ cudaLaunchConfig_t launch_config(int grid, cudaStream_t st, cudaLaunchAttribute*
     return cfg;
 }
 
-template <int BN, bool SWAP, bool PAIR, bool F32OUT = false>
+template <int BN, bool SWAP, bool PAIR, int EPI = kEpiF16>
 int set_smem_limit(DeviceState& d, unsigned bit)
 {
     if (d.attrs & bit) return BW_OK;
-    cudaError_t e = cudaFuncSetAttribute(gemm_kernel<BN, SWAP, PAIR, F32OUT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaError_t e = cudaFuncSetAttribute(gemm_kernel<BN, SWAP, PAIR, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          Geom<BN, SWAP, PAIR>::kSmemBytes);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
     d.attrs |= bit;
@@ -188,7 +188,7 @@ int pair_occupancy(DeviceState& d)
     return BW_OK;
 }
 
-template <int BN, bool SWAP, bool PAIR, bool F32OUT = false>
+template <int BN, bool SWAP, bool PAIR, int EPI = kEpiF16>
 int launch_kernel(DeviceState& d, unsigned bit, const bw_plan& q, const CUtensorMap& mx, const CUtensorMap& my,
                   const Params& p, cudaStream_t st)
 {
@@ -197,23 +197,31 @@ int launch_kernel(DeviceState& d, unsigned bit, const bw_plan& q, const CUtensor
         snprintf(g_errbuf, sizeof g_errbuf, "plan and kernel geometry disagree (bn %d)", BN);
         return BW_ERR_LAUNCH;
     }
-    int rc = set_smem_limit<BN, SWAP, PAIR, F32OUT>(d, bit);
+    int rc = set_smem_limit<BN, SWAP, PAIR, EPI>(d, bit);
     if (rc) return rc;
     cudaLaunchAttribute attr[1];
     const cudaLaunchConfig_t cfg = launch_config<BN, SWAP, PAIR>(q.grid, st, attr);
-    cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_kernel<BN, SWAP, PAIR, F32OUT>, mx, my, p);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_kernel<BN, SWAP, PAIR, EPI>, mx, my, p);
     if (e != cudaSuccess) return cuda_fail(e, "kernel launch");
     return BW_OK;
 }
 
 // The plan's kernel instance, launched.
 int dispatch(DeviceState& d, const bw_plan& q, const CUtensorMap& mx, const CUtensorMap& my, const Params& p,
-             cudaStream_t st, bool f32out = false)
+             cudaStream_t st, int epi = kEpiF16)
 {
-    if (f32out) {  // fp32 C: the plan is a TILE or PAIR one (no swap-AB)
-        if (q.kernel == BW_KERNEL_PAIR) return launch_kernel<256, false, true, true>(d, 1u << 12, q, mx, my, p, st);
+    if (epi == kEpiF32) {  // fp32 C: the plan is a TILE or PAIR one (no swap-AB)
+        if (q.kernel == BW_KERNEL_PAIR) return launch_kernel<256, false, true, kEpiF32>(d, 1u << 12, q, mx, my, p, st);
         if (q.kernel == BW_KERNEL_TILE && q.bn == 256)
-            return launch_kernel<256, false, false, true>(d, 1u << 13, q, mx, my, p, st);
+            return launch_kernel<256, false, false, kEpiF32>(d, 1u << 13, q, mx, my, p, st);
+        return BW_ERR_ARG;
+    }
+    if (epi == kEpiSwiGLU) {  // fused activation: TILE or PAIR, whole tiles only
+        if (q.sk_tiles != 0) return BW_ERR_ARG;
+        if (q.kernel == BW_KERNEL_PAIR)
+            return launch_kernel<256, false, true, kEpiSwiGLU>(d, 1u << 14, q, mx, my, p, st);
+        if (q.kernel == BW_KERNEL_TILE && q.bn == 256)
+            return launch_kernel<256, false, false, kEpiSwiGLU>(d, 1u << 15, q, mx, my, p, st);
         return BW_ERR_ARG;
     }
     if (q.kernel == BW_KERNEL_PAIR) return launch_kernel<256, false, true>(d, kBitPair, q, mx, my, p, st);
@@ -270,7 +278,7 @@ bool make_maps(const bw_plan& q, const void* A, const void* B, int M, int N, int
     return make_map(mx, B, N, K, 64, 64) && make_map(my, A, K, M, 64, q.bn);
 }
 
-int gemm(const void* A, const void* B, void* C, int M, int N, int K, cudaStream_t st, int variant, bool f32out = false)
+int gemm(const void* A, const void* B, void* C, int M, int N, int K, cudaStream_t st, int variant, int epi = kEpiF16)
 {
     if (variant < 0 || variant >= kVariants) return BW_ERR_ARG;
     if (!shape_ok(M, N, K)) return BW_ERR_SHAPE;
@@ -284,7 +292,8 @@ int gemm(const void* A, const void* B, void* C, int M, int N, int K, cudaStream_
     {
         std::lock_guard<std::mutex> lock(g_mu);
         if ((rc = pair_occupancy(*d))) return rc;
-        if ((rc = make_plan(M, N, K, d->sms, d->pairs, variant, &q))) return rc;
+        const unsigned flags = epi == kEpiF32 ? kPlanNoSwap : epi == kEpiSwiGLU ? kPlanNoSwap | kPlanNoSplit : 0u;
+        if ((rc = make_plan(M, N, K, d->sms, d->pairs, variant, &q, flags))) return rc;
         if ((rc = ensure_workspace(*d, q, st))) return rc;
     }
     CUtensorMap mx, my;
@@ -292,7 +301,7 @@ int gemm(const void* A, const void* B, void* C, int M, int N, int K, cudaStream_
         snprintf(g_errbuf, sizeof g_errbuf, "cuTensorMapEncodeTiled failed");
         return BW_ERR_LAUNCH;
     }
-    return dispatch(*d, q, mx, my, make_params(q, M, N, K, C, d->work, d->counters), st, f32out);
+    return dispatch(*d, q, mx, my, make_params(q, M, N, K, C, d->work, d->counters), st, epi);
 }
 
 }  // namespace
@@ -311,8 +320,14 @@ BW_API int bw_gemm_f16_variant(const void* A, const void* B, void* C, int M, int
 
 BW_API int bw_gemm_f16_f32out(const void* A, const void* B, void* C, int M, int N, int K, void* stream)
 {
-    // the rule without swap-AB (variant 2): SM-pair tiles at every M, written in fp32
-    return bw::gemm(A, B, C, M, N, K, static_cast<cudaStream_t>(stream), 2, true);
+    // the rule without swap-AB: SM-pair tiles at every M, written in fp32
+    return bw::gemm(A, B, C, M, N, K, static_cast<cudaStream_t>(stream), 0, bw::kEpiF32);
+}
+
+BW_API int bw_gemm_f16_swiglu(const void* A, const void* B, void* C, int M, int N, int K, void* stream)
+{
+    if (N % 256) return BW_ERR_SHAPE;  // each 256-column tile holds 128 gate and 128 up columns
+    return bw::gemm(A, B, C, M, N, K, static_cast<cudaStream_t>(stream), 0, bw::kEpiSwiGLU);
 }
 
 BW_API int bw_gemm_variant_count(void) { return bw::kVariants; }

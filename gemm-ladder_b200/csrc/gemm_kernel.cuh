@@ -37,9 +37,17 @@ constexpr int kThreads = 192;    // 6 warps
 constexpr int kEpiThread0 = 64;  // the first epilogue thread
 constexpr int kBK = 64;          // K per stage: one 128-byte swizzle row of fp16
 
+// Epilogue modes: what the kernel writes.
+enum : int {
+    kEpiF16 = 0,     // C = A B in fp16
+    kEpiF32 = 1,     // C = A B in fp32 (row-parallel partial sums)
+    kEpiSwiGLU = 2,  // B's tiles of BN columns hold BN/2 gate then BN/2 up columns: C = silu(gate) * up in fp16,
+                     // M x N/2 (a gated MLP's activation, from the accumulators: the gateup result never exists)
+};
+
 struct Params {
     Sched s;
-    void* C;                     // fp16, or fp32 for the F32OUT instances (row-parallel partial sums)
+    void* C;                     // fp16; fp32 for kEpiF32; M x N/2 fp16 for kEpiSwiGLU
     float* work;                 // the partials: workspace_slots() x (PAIR ? 2 : 1) slots of 128 x BN fp32, row-major
     int* counters;               // one per split tile (per block of the pair), zero between calls
     unsigned long long wait_ns;  // the limit of any single wait on a barrier
@@ -130,12 +138,12 @@ __device__ __forceinline__ uint64_t desc_mnmajor(uint32_t tile, int k) { return 
 // 16 x 128 fp16 buffers, alternating by chunk), so that C is written by 16-byte stores, a warp covering two rows of
 // 256 contiguous bytes, instead of 16 scattered 2-byte stores per thread.  One named barrier per chunk; the buffer of
 // chunk i + 2 is written only after every thread has passed the barrier of chunk i + 1, so after it read chunk i.
-template <bool SWAP, bool F32OUT = false>
+template <bool SWAP, int EPI = kEpiF16>
 __device__ __forceinline__ void store_chunk(const Params& p, int m0, int n0, int lane, int c0, const float (&v)[16],
                                             __half* cst)
 {
     const Sched& s = p.s;
-    if (F32OUT) {  // fp32 C (not swapped): four 16-byte stores
+    if (EPI == kEpiF32) {  // fp32 C (not swapped): four 16-byte stores
         const int m = m0 + lane, n = n0 + c0;
         if (m >= s.M || n >= s.N) return;
         float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.C) + (size_t)m * s.N + n);
@@ -189,7 +197,7 @@ __device__ __forceinline__ float4* slot_vec(const Params& p, long long slot, int
 // this block's accumulator in tensor memory when own_mine (tbase: its row's TMEM address), from its slot otherwise.
 // The loads from memory are a stream of (16-column chunk, partial) pairs in chunk order, kept kWin deep in flight:
 // with one partial in memory four chunks are on their way at once, instead of one L2 round trip per chunk.
-template <int BN, bool SWAP, int RANKS, bool F32OUT>
+template <int BN, bool SWAP, int RANKS, int EPI>
 __device__ __noinline__ void reduce_tile(const Params& p, int P, int tile, int rank, Fixup f, bool own_mine,
                                             uint32_t tbase, int row, int m0, int n0, __half* cst)
 {
@@ -261,7 +269,7 @@ __device__ __noinline__ void reduce_tile(const Params& p, int P, int tile, int r
 #pragma unroll
                         for (int e = 0; e < 16; ++e) v[e] += own[e];
                     }
-                    store_chunk<SWAP, F32OUT>(p, m0, n0, row, chunk * 16, v, cst);
+                    store_chunk<SWAP, EPI>(p, m0, n0, row, chunk * 16, v, cst);
                 }
             }
         }
@@ -272,7 +280,7 @@ __device__ __noinline__ void reduce_tile(const Params& p, int P, int tile, int r
 // in memory are copied into the ring by the TMA engine at once (cp.async.bulk, one per partial), then summed from
 // shared memory.  The sum runs over at most kMaxSum partials, unrolled and predicated, so that everything stays in
 // registers.  Returns false if the copy did not complete within the wait limit (the block's abort flag is up).
-template <int BN, bool SWAP, int RANKS, int kMaxSum, bool F32OUT>
+template <int BN, bool SWAP, int RANKS, int kMaxSum, int EPI>
 __device__ __noinline__ bool reduce_tile_bulk(const Params& p, int P, int tile, int rank, Fixup f, bool own_mine,
                                               uint32_t tbase, int row, int m0, int n0, __half* cst, uint8_t* ring,
                                               uint64_t* rbar, volatile int* abort_flag, int seg)
@@ -344,19 +352,20 @@ __device__ __noinline__ bool reduce_tile_bulk(const Params& p, int P, int tile, 
             v[4 * q + 2] = acc[q].z;
             v[4 * q + 3] = acc[q].w;
         }
-        store_chunk<SWAP, F32OUT>(p, m0, n0, row, chunk * 16, v, cst);
+        store_chunk<SWAP, EPI>(p, m0, n0, row, chunk * 16, v, cst);
     }
     if (threadIdx.x == kEpiThread0) BW_TRACE_AT(11);
     return true;
 }
 
 // ------------------------------------------------------------------ the kernel
-template <int BN, bool SWAP, bool PAIR, bool F32OUT = false>
+template <int BN, bool SWAP, bool PAIR, int EPI = kEpiF16>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmy, const Params p)
 {
     using G = Geom<BN, SWAP, PAIR>;
-    static_assert(!(SWAP && F32OUT), "fp32 output is written by the TILE and PAIR forms");
+    static_assert(!SWAP || EPI == kEpiF16, "fp32 and SwiGLU outputs are written by the TILE and PAIR forms");
+    static_assert(EPI != kEpiSwiGLU || BN % 32 == 0, "SwiGLU pairs the two halves of a tile");
     constexpr int S = G::kStages;
     constexpr int R = G::kRanks;
     extern __shared__ uint8_t smem_raw[];
@@ -611,7 +620,33 @@ __global__ void __launch_bounds__(kThreads, 1)
                 n0 = tn * BN;
             }
             const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
-            if (sg.k0 == 0 && sg.k1 == s.kblocks) {
+            if (EPI == kEpiSwiGLU) {
+                // a whole tile (the plan splits none): gate columns [0, BN/2), up columns [BN/2, BN) of the tile,
+                // silu(gate) * up to columns [n0 / 2, n0 / 2 + BN / 2) of the M x N/2 output
+#pragma unroll 1
+                for (int c0 = 0; c0 < BN / 2; c0 += 16) {
+                    uint32_t gr[16], ur[16];
+                    tmem_ld16(tbase + (uint32_t)c0, gr);
+                    tmem_ld16(tbase + (uint32_t)(BN / 2 + c0), ur);
+                    tmem_wait_ld();
+                    const int m = m0 + row, n = n0 / 2 + c0;
+                    if (m < s.M && n < s.N / 2) {
+                        uint32_t h[8];
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) {
+                            const float g0 = __uint_as_float(gr[2 * j]), g1 = __uint_as_float(gr[2 * j + 1]);
+                            const float a0 = g0 / (1.0f + __expf(-g0)) * __uint_as_float(ur[2 * j]);
+                            const float a1 = g1 / (1.0f + __expf(-g1)) * __uint_as_float(ur[2 * j + 1]);
+                            const __half2 x = __floats2half2_rn(a0, a1);
+                            h[j] = *reinterpret_cast<const uint32_t*>(&x);
+                        }
+                        uint4* dst = reinterpret_cast<uint4*>(static_cast<__half*>(p.C) + (size_t)m * (s.N / 2) + n);
+                        dst[0] = make_uint4(h[0], h[1], h[2], h[3]);
+                        dst[1] = make_uint4(h[4], h[5], h[6], h[7]);
+                    }
+                }
+                release_acc(acc);
+            } else if (sg.k0 == 0 && sg.k1 == s.kblocks) {
                 // a whole tile: straight to C
 #pragma unroll 1
                 for (int c0 = 0; c0 < BN; c0 += 16) {
@@ -621,7 +656,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     float v[16];
 #pragma unroll
                     for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[j]);
-                    store_chunk<SWAP, F32OUT>(p, m0, n0, row, c0, v, cst);
+                    store_chunk<SWAP, EPI>(p, m0, n0, row, c0, v, cst);
                 }
                 release_acc(acc);
             } else {
@@ -643,10 +678,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 if (fast == 2) {
                     if (last_seg && f.nseg <= G::kMaxSum)
-                        reduce_tile_bulk<BN, SWAP, R, G::kMaxSum, F32OUT>(p, P, sg.tile, rank, f, true, tbase, row, m0, n0,
+                        reduce_tile_bulk<BN, SWAP, R, G::kMaxSum, EPI>(p, P, sg.tile, rank, f, true, tbase, row, m0, n0,
                                                                   cst, smem, rbar, abort_flag, seg);
                     else
-                        reduce_tile<BN, SWAP, R, F32OUT>(p, P, sg.tile, rank, f, true, tbase, row, m0, n0, cst);
+                        reduce_tile<BN, SWAP, R, EPI>(p, P, sg.tile, rank, f, true, tbase, row, m0, n0, cst);
                     release_acc(acc);
                     if (threadIdx.x == kEpiThread0) atomicExch(counter, 0);
                 } else {
@@ -680,10 +715,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                             BW_TRACE_VAL(8, 1 | f.nseg << 8 | seg << 16);
                         }
                         if (last_seg && f.nseg <= G::kMaxSum)
-                            reduce_tile_bulk<BN, SWAP, R, G::kMaxSum, F32OUT>(p, P, sg.tile, rank, f, true, tbase, row, m0, n0,
+                            reduce_tile_bulk<BN, SWAP, R, G::kMaxSum, EPI>(p, P, sg.tile, rank, f, true, tbase, row, m0, n0,
                                                                       cst, smem, rbar, abort_flag, seg);
                         else
-                            reduce_tile<BN, SWAP, R, F32OUT>(p, P, sg.tile, rank, f, false, tbase, row, m0, n0, cst);
+                            reduce_tile<BN, SWAP, R, EPI>(p, P, sg.tile, rank, f, false, tbase, row, m0, n0, cst);
                         if (threadIdx.x == kEpiThread0) atomicExch(counter, 0);
                     }
                     if (last_seg) release_acc(acc);

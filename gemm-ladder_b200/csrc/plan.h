@@ -102,14 +102,21 @@ inline int tail_splits(int tail, int P, int kblocks, double fixup_kb)
     return best;
 }
 
+// Plan constraints of the entries that need them (on top of the variant).
+enum : unsigned {
+    kPlanNoSwap = 1u,   // A is the MMA's A operand (fp32 and fused outputs are written by TILE and PAIR only)
+    kPlanNoSplit = 2u,  // whole tiles only (a fused epilogue needs the complete sums)
+};
+
 // sms: the SMs; pairs: the pairs of SMs the pair kernel can hold at once (its cluster occupancy).
-inline int make_plan(int M, int N, int K, int sms, int pairs, int variant, bw_plan* p)
+inline int make_plan(int M, int N, int K, int sms, int pairs, int variant, bw_plan* p, unsigned flags = 0)
 {
     if (!p || variant < 0 || variant >= kVariants || sms <= 0) return BW_ERR_ARG;
     if (!shape_ok(M, N, K)) return BW_ERR_SHAPE;
     bw_plan q = {};
     q.kblocks = K / 64;
-    const bool swap = M <= 128 && variant != 2 && variant < 6;
+    if (flags & kPlanNoSplit) variant = variant == 0 || variant == 2 ? 1 : variant;
+    const bool swap = M <= 128 && variant != 2 && variant < 6 && !(flags & kPlanNoSwap);
     const bool pair = !swap && variant != 5 && variant < 6 && pairs > 0;
     int ranks = 1, units = sms;  // the blocks (or pairs) of the persistent grid
     if (swap) {

@@ -4,7 +4,9 @@ Llama-3-70B layer: hidden 8192, MLP 28672, gate and up concatenated into one 819
 Megatron-style, one rank per GPU, p ranks:
   gateup (column-parallel, no communication): rank r holds W1_r = [gate columns of shard r | up columns of shard r]
       (hidden x 2 F/p), H_r = X W1_r in fp16 through the rung's GEMM;
-  activation: A_r = silu(H_r[:, :F/p]) * H_r[:, F/p:]  (SwiGLU, on the rank's own shard, no communication);
+  activation: A_r = silu(H_r[:, :F/p]) * H_r[:, F/p:]  (SwiGLU, on the rank's own shard, no communication), or
+      fused into the gateup GEMM's epilogue (bw_gemm_f16_swiglu, W1_r in the layout of shard_gateup_interleaved):
+      then H_r is never written;
   down (row-parallel): P_r = A_r W2_r with W2_r = rows [r F/p, (r+1) F/p) of W2 (F x hidden), in fp32 through the
       rung's fp32-output GEMM (bw_gemm_f16_f32out);
   reduce-scatter (NCCL, sum, fp32): rank r receives rows [r M/p, (r+1) M/p) of Y = sum_r P_r, then rounds them to fp16.
@@ -28,6 +30,29 @@ def shard_gateup(W1, rank, world):
     return torch.cat([gate, up], dim=1).contiguous()
 
 
+def shard_gateup_interleaved(W1, rank, world, group=128):
+    """The rank's gateup shard laid out for the fused activation (bw_gemm_f16_swiglu): groups of `group` gate columns
+    each followed by the matching `group` up columns (a one-time permutation of the weight's columns)."""
+    W = shard_gateup(W1, rank, world)
+    fs = W.shape[1] // 2
+    if fs % group:
+        raise ValueError(f"the shard's MLP width {fs} is not a multiple of {group}")
+    parts = []
+    for g in range(0, fs, group):
+        parts.append(W[:, g:g + group])
+        parts.append(W[:, fs + g:fs + g + group])
+    return torch.cat(parts, dim=1).contiguous()
+
+
+def swiglu_reference(X, W_interleaved, group=128):
+    """What the fused GEMM computes, on any device: silu(gate) * up from fp32 sums, the activation in fp16."""
+    H = X.float() @ W_interleaved.float()
+    n = H.shape[1]
+    idx = torch.arange(n, device=H.device).reshape(-1, 2 * group)
+    gate, up = H[:, idx[:, :group].reshape(-1)], H[:, idx[:, group:].reshape(-1)]
+    return (F.silu(gate) * up).to(X.dtype)
+
+
 def shard_down(W2, rank, world):
     """The rank's rows of the down weight (F x hidden)."""
     f = W2.shape[0]
@@ -41,10 +66,12 @@ class TPMLP:
     """One rank's part of the block.  W1_r, W2_r: this rank's shards (fp16).  gemm(A, B) -> fp16 C = A B;
     gemm_f32(A, B) -> fp32 C = A B; reduce_scatter(out, inp) sums inp over the ranks into out (this rank's rows)."""
 
-    def __init__(self, W1_r, W2_r, rank, world, gemm, gemm_f32, reduce_scatter=None):
+    def __init__(self, W1_r, W2_r, rank, world, gemm, gemm_f32, reduce_scatter=None, gemm_swiglu=None):
+        """gemm_swiglu(A, W1_r) -> the activation directly (W1_r then in the interleaved layout of
+        shard_gateup_interleaved): the gateup GEMM with the activation in its epilogue."""
         self.W1, self.W2 = W1_r, W2_r
         self.rank, self.world = rank, world
-        self.gemm, self.gemm_f32 = gemm, gemm_f32
+        self.gemm, self.gemm_f32, self.gemm_swiglu = gemm, gemm_f32, gemm_swiglu
         self.reduce_scatter = reduce_scatter
         self.fs = W2_r.shape[0]
         if W1_r.shape[1] != 2 * self.fs:
@@ -54,8 +81,11 @@ class TPMLP:
         M = X.shape[0]
         if M % self.world:
             raise ValueError(f"{M} tokens do not split over {self.world} ranks")
-        H = self.gemm(X, self.W1)                                  # M x 2F/p, fp16
-        A = (F.silu(H[:, :self.fs].float()) * H[:, self.fs:].float()).to(X.dtype).contiguous()
+        if self.gemm_swiglu is not None:
+            A = self.gemm_swiglu(X, self.W1)                       # M x F/p, fp16, fused
+        else:
+            H = self.gemm(X, self.W1)                              # M x 2F/p, fp16
+            A = (F.silu(H[:, :self.fs].float()) * H[:, self.fs:].float()).to(X.dtype).contiguous()
         P = self.gemm_f32(A, self.W2)                              # M x hidden, fp32 partial sums
         if self.world == 1:
             return P.to(X.dtype)

@@ -57,6 +57,14 @@ int bw_gemm_f16_variant(const void* A, const void* B, void* C, int M, int N, int
  */
 int bw_gemm_f16_f32out(const void* A, const void* B, void* C, int M, int N, int K, void* stream);
 
+/*
+ * A gated MLP's activation in one GEMM: with B (K x N, N a multiple of 256) laid out so that each group of 256
+ * columns holds 128 gate columns then the 128 matching up columns, C (M x N/2 fp16) = silu(A B_gate) * (A B_up),
+ * computed from the fp32 accumulators in the epilogue (the M x N gateup result is never written).  Whole SM-pair tiles.
+ * No reference counterpart: the tensor-parallel MLP block of the B200 configs (gateup, then down).
+ */
+int bw_gemm_f16_swiglu(const void* A, const void* B, void* C, int M, int N, int K, void* stream);
+
 /* The number of variants.  Replaces: the weak `int g_nvar` (probe/probe.cu:40, hopper/verif.cu:38, hopper/step7.cu:16). */
 int bw_gemm_variant_count(void);
 

@@ -314,3 +314,48 @@ def test_tp_mlp_block_on_one_gpu():
         torch.backends.cuda.matmul.allow_tf32 = prev
     gap = ((Y.float() - ref).abs().max() / ref.abs().max()).item()
     assert gap <= 2e-3, gap
+
+
+@pytest.mark.parametrize("shape", [(512, 2048, 1024), (2048, 7168, 8192), (144, 512, 320)],
+                         ids=lambda s: "x".join(map(str, s)))
+def test_swiglu_fused_epilogue(shape):
+    """bw_gemm_f16_swiglu against silu(gate) * up computed from an fp32 GEMM (no TF32) on the interleaved layout."""
+    import tp_mlp
+
+    M, N, K = shape
+    g = torch.Generator(device="cuda")
+    g.manual_seed(M + N)
+    X = (torch.rand((M, K), generator=g, device="cuda") * 2 - 1).half()
+    W = ((torch.rand((K, N), generator=g, device="cuda") * 2 - 1) / K ** 0.5).half()
+    A = bwgemm.gemm_swiglu(X, W)
+    torch.cuda.synchronize()
+    assert bwgemm.status()[0] == 0
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        ref = tp_mlp.swiglu_reference(X, W).float()
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+    assert A.shape == (M, N // 2) and bool(torch.isfinite(A.float()).all())
+    gap = ((A.float() - ref).abs().max() / ref.abs().max()).item()
+    assert gap <= 2e-3, gap
+    assert torch.equal(bwgemm.gemm_swiglu(X, W), A), "calls differ"
+
+
+def test_tp_mlp_block_fused_on_one_gpu():
+    """The block with the activation fused into the gateup GEMM equals the unfused block within fp16 rounding."""
+    import tp_mlp
+
+    M, hidden, f = 512, 1024, 2048
+    g = torch.Generator(device="cuda")
+    g.manual_seed(10)
+    X = (torch.rand((M, hidden), generator=g, device="cuda") * 2 - 1).half()
+    W1 = ((torch.rand((hidden, 2 * f), generator=g, device="cuda") * 2 - 1) / hidden ** 0.5).half()
+    W2 = ((torch.rand((f, hidden), generator=g, device="cuda") * 2 - 1) / f ** 0.5).half()
+    fused = tp_mlp.TPMLP(tp_mlp.shard_gateup_interleaved(W1, 0, 1), tp_mlp.shard_down(W2, 0, 1), 0, 1, bwgemm.gemm,
+                         bwgemm.gemm_f32out, gemm_swiglu=bwgemm.gemm_swiglu).forward(X)
+    plain = tp_mlp.TPMLP(tp_mlp.shard_gateup(W1, 0, 1), tp_mlp.shard_down(W2, 0, 1), 0, 1, bwgemm.gemm,
+                         bwgemm.gemm_f32out).forward(X)
+    torch.cuda.synchronize()
+    gap = ((fused.float() - plain.float()).abs().max() / plain.float().abs().max()).item()
+    assert gap <= 4e-3, gap
