@@ -180,7 +180,8 @@ def dist_setup(args):
         import torch.distributed as dist
 
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
+        # a short timeout: a rank that never joins a collective ends it with an error, not a hang
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60), device_id=torch.device("cuda", local))
     else:
         torch.cuda.set_device(0)
     return rank, world, local
@@ -323,8 +324,22 @@ def run_tp_mlp(args):
                        tp_mlp.nccl_reduce_scatter if world > 1 else None,
                        gemm_swiglu=None if args.tp_unfused else bwgemm.gemm_swiglu)
     stream = torch.cuda.current_stream()
-    for _ in range(max(3, args.warmup)):
-        blk.forward(X)
+    watch = None
+    if world > 1:  # host-side failure detection at the phase boundaries (peers.py), outside the timed region
+        import peers
+
+        watch = peers.PeerWatch.from_default_group(gate_timeout_s=120.0)
+    try:
+        if watch:
+            watch.gate()
+        for _ in range(max(3, args.warmup)):
+            blk.forward(X)
+        if watch:
+            watch.gate()
+    except Exception as e:
+        if watch and not isinstance(e, (peers.PeerFailed, peers.PeerTimeout)):
+            watch.fail(f"{type(e).__name__}: {e}")
+        raise
     barrier(world)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:

@@ -84,6 +84,8 @@ def lib():
         L.bw_gemm_clear_status.restype = i
         L.bw_gemm_set_wait_limit_ns.argtypes = [ctypes.c_ulonglong]
         L.bw_gemm_set_wait_limit_ns.restype = ctypes.c_ulonglong
+        L.bw_wait_selftest.argtypes = [ctypes.c_ulonglong, vp]
+        L.bw_wait_selftest.restype = i
         L.bw_status_string.argtypes = [i]
         L.bw_status_string.restype = ctypes.c_char_p
         L.bw_last_error_string.argtypes = []
@@ -205,3 +207,10 @@ def dirty():
 
 def set_wait_limit_ns(ns):
     return lib().bw_gemm_set_wait_limit_ns(ns)
+
+
+def wait_selftest(limit_ns=0, stream=None):
+    """Runs the bounded-wait check (a wait on a barrier that nothing arrives on) and returns the C status: 3
+    (BW_ERR_TIMEOUT) is the expected outcome; the status word then holds the selftest site."""
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return lib().bw_wait_selftest(limit_ns, s.cuda_stream)

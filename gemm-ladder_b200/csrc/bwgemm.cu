@@ -384,6 +384,49 @@ BW_API unsigned long long bw_gemm_set_wait_limit_ns(unsigned long long ns)
     return old;
 }
 
+// ------------------------------------------------------------------ the bounded-wait check
+namespace bw {
+namespace {
+
+// One warp: lane 0 waits on a barrier that nothing arrives on, through the pipeline's own bounded wait, which gives
+// up after limit_ns, records the selftest site in the status word and returns.
+__global__ void wait_selftest_kernel(unsigned long long limit_ns)
+{
+    __shared__ __align__(8) uint64_t bar;
+    __shared__ int abort_flag;
+    if (threadIdx.x == 0) {
+        abort_flag = 0;
+        mbar_init(&bar, 1);
+        fence_barrier_init();
+    }
+    __syncwarp();
+    if (threadIdx.x == 0) wait_bounded(&bar, 0, &abort_flag, limit_ns, site(kSiteSelftest, 0, 0), -1);
+}
+
+}  // namespace
+}  // namespace bw
+
+BW_API int bw_wait_selftest(unsigned long long limit_ns, void* stream)
+{
+    bw::DeviceState* d = nullptr;
+    if (int st = bw::device_state(&d)) return st;
+    if (!d->supported) return BW_ERR_DEVICE;
+    if (limit_ns == 0) limit_ns = bw::g_wait_ns;
+    if (limit_ns > 10000000000ull) return BW_ERR_ARG;
+    if (int st = bw_gemm_clear_status()) return st;
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    bw::wait_selftest_kernel<<<1, 32, 0, s>>>(limit_ns);
+    cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) return bw::cuda_fail(e, "wait selftest");
+    int code = 0;
+    unsigned where = 0;
+    if (int st = bw_gemm_status(&code, &where, nullptr, nullptr)) return st;
+    if (code == BW_ERR_TIMEOUT && where == bw::site(bw::kSiteSelftest, 0, 0)) return BW_ERR_TIMEOUT;
+    snprintf(bw::g_errbuf, sizeof bw::g_errbuf, "wait selftest: status %d at site 0x%x", code, where);
+    return BW_ERR_LAUNCH;
+}
+
 BW_API const char* bw_status_string(int status)
 {
     switch (status) {

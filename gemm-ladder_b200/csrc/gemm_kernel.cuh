@@ -112,8 +112,12 @@ __device__ __forceinline__ void load_tile(void* dst, const void* tmap, int x, in
     }
 }
 
-// Where a wait gave up: role (0 producer, 1 MMA, 2 epilogue) << 16 | barrier kind << 8 | index.
-__device__ __forceinline__ uint32_t site(uint32_t role, uint32_t kind, uint32_t idx) { return role << 16 | kind << 8 | idx; }
+// Where a wait gave up: role (0 producer, 1 MMA, 2 epilogue, 7 the wait selftest) << 16 | barrier kind << 8 | index.
+enum : uint32_t { kSiteSelftest = 7u };
+__host__ __device__ __forceinline__ uint32_t site(uint32_t role, uint32_t kind, uint32_t idx)
+{
+    return role << 16 | kind << 8 | idx;
+}
 
 // A wait on a barrier that only bounds time (used to drain copies in flight after an abort).
 __device__ __forceinline__ void wait_drain(uint64_t* bar, uint32_t parity, uint64_t limit_ns)

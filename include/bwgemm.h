@@ -138,6 +138,16 @@ int bw_gemm_clear_status(void);
  * sets it at load).  Returns the previous limit. */
 unsigned long long bw_gemm_set_wait_limit_ns(unsigned long long ns);
 
+/*
+ * The bounded-wait check, for a caller's health check: one warp waits, through the same bounded wait as the GEMM's
+ * pipeline, on a shared-memory barrier that nothing arrives on, for `limit_ns` (0: the current wait limit; at most
+ * 10 s).  The wait gives up, records site 7 << 16 in the status word and the kernel returns.  Clears the status word
+ * first, synchronises `stream` (unlike the GEMM entries) and returns BW_ERR_TIMEOUT -- the expected outcome: a stall
+ * ends with a status and a usable context, not a hang.  Any other return is a failure.
+ * No reference counterpart: the reference's guarded wait traps (hopper/step2.cuh:128-145).
+ */
+int bw_wait_selftest(unsigned long long limit_ns, void* stream);
+
 /* Text of a status code, and of the last CUDA error met by the library on this thread. */
 const char* bw_status_string(int status);
 const char* bw_last_error_string(void);

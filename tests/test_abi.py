@@ -48,6 +48,12 @@ def test_bad_pointers_and_variant_are_refused_without_a_gpu():
     assert bwgemm.gemm_ptr(256, 256, 512, 16, 64, 64, variant=99) == bwgemm.BW_ERR_ARG
 
 
+def test_wait_selftest_without_a_gpu_reports_a_failure_not_a_timeout():
+    # BW_ERR_TIMEOUT means a kernel ran and its wait gave up: without a device the call must say something else
+    st = bwgemm.lib().bw_wait_selftest(1000, None)
+    assert st not in (bwgemm.BW_OK, 3)
+
+
 def test_plan_rule_on_the_judge_shapes():
     for name, M, N, K in JUDGE_B200:
         p = bwgemm.plan(M, N, K, sms=148)

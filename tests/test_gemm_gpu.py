@@ -359,3 +359,21 @@ def test_tp_mlp_block_fused_on_one_gpu():
     torch.cuda.synchronize()
     gap = ((fused.float() - plain.float()).abs().max() / plain.float().abs().max()).item()
     assert gap <= 4e-3, gap
+
+
+def test_a_wait_that_runs_out_returns_a_status_and_the_context_stays_usable(oracle_mod):
+    """The pipeline's bounded wait, on a barrier that nothing arrives on (bw_wait_selftest): it gives up after its
+    limit, the kernel returns, the host reads BW_ERR_TIMEOUT and the wait's site from the status word, and the next
+    GEMM on the same context is correct.  No fault, trap or endless loop is involved."""
+    import time
+
+    t0 = time.monotonic()
+    assert bwgemm.wait_selftest(50_000_000) == 3  # a 50 ms limit
+    assert time.monotonic() - t0 < 10
+    code, where, block, _ = bwgemm.status()
+    assert (code, where, block) == (3, 7 << 16, 0)
+    assert bwgemm.lib().bw_wait_selftest(20_000_000_000, None) == 4  # a limit over 10 s is refused
+    bwgemm.clear_status()
+    A, B, ref = lcg_case(256, 512, 1024, oracle_mod)
+    C = run(to_dev(A), to_dev(B))
+    assert_parity(bits(C), ref, 1024, oracle_mod, "256x512x1024 after the selftest")
