@@ -212,5 +212,7 @@ def set_wait_limit_ns(ns):
 def wait_selftest(limit_ns=0, stream=None):
     """Runs the bounded-wait check (a wait on a barrier that nothing arrives on) and returns the C status: 3
     (BW_ERR_TIMEOUT) is the expected outcome; the status word then holds the selftest site."""
+    import torch
+
     s = stream if stream is not None else torch.cuda.current_stream()
     return lib().bw_wait_selftest(limit_ns, s.cuda_stream)
