@@ -38,6 +38,7 @@ class Plan(ctypes.Structure):
         ("counters", ctypes.c_int),
         ("smem_bytes", ctypes.c_int),
         ("tmem_cols", ctypes.c_int),
+        ("kpair", ctypes.c_int),
     ]
 
     def as_dict(self):

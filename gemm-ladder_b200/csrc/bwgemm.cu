@@ -142,20 +142,22 @@ int ensure_workspace(DeviceState& d, const bw_plan& q, cudaStream_t st)
     return BW_OK;
 }
 
+// Clusters of two blocks for the SM pair (PAIR) and for a swap-AB plan's K halves (kpair).
 template <int BN, bool SWAP, bool PAIR>
-cudaLaunchConfig_t launch_config(int grid, cudaStream_t st, cudaLaunchAttribute* attr)
+cudaLaunchConfig_t launch_config(int grid, cudaStream_t st, cudaLaunchAttribute* attr, bool kpair = false)
 {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(kThreads);
     cfg.dynamicSmemBytes = Geom<BN, SWAP, PAIR>::kSmemBytes;
     cfg.stream = st;
+    const bool cluster = PAIR || (SWAP && kpair);
     attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = PAIR ? 2 : 1;
+    attr[0].val.clusterDim.x = cluster ? 2 : 1;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = PAIR ? 1 : 0;
+    cfg.numAttrs = cluster ? 1 : 0;
     return cfg;
 }
 
@@ -193,14 +195,15 @@ int launch_kernel(DeviceState& d, unsigned bit, const bw_plan& q, const CUtensor
                   const Params& p, cudaStream_t st)
 {
     using G = Geom<BN, SWAP, PAIR>;
-    if (q.smem_bytes != G::kSmemBytes || q.stages != G::kStages || q.tmem_cols != G::kTmemCols) {
+    if (q.smem_bytes != G::kSmemBytes || q.stages != G::kStages || q.tmem_cols != G::kTmemCols ||
+        (q.kpair && (!SWAP || q.grid % 2 || q.grid != 2 * q.tiles))) {
         snprintf(g_errbuf, sizeof g_errbuf, "plan and kernel geometry disagree (bn %d)", BN);
         return BW_ERR_LAUNCH;
     }
     int rc = set_smem_limit<BN, SWAP, PAIR, EPI>(d, bit);
     if (rc) return rc;
     cudaLaunchAttribute attr[1];
-    const cudaLaunchConfig_t cfg = launch_config<BN, SWAP, PAIR>(q.grid, st, attr);
+    const cudaLaunchConfig_t cfg = launch_config<BN, SWAP, PAIR>(q.grid, st, attr, q.kpair != 0);
     cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_kernel<BN, SWAP, PAIR, EPI>, mx, my, p);
     if (e != cudaSuccess) return cuda_fail(e, "kernel launch");
     return BW_OK;
@@ -262,6 +265,7 @@ Params make_params(const bw_plan& q, int M, int N, int K, void* C, float* work, 
     p.s.splits = q.splits;
     p.s.sk_iters = q.sk_iters;
     p.s.group_rows = q.group_rows;
+    p.s.kpair = q.kpair;
     p.C = C;
     p.work = work;
     p.counters = counters;

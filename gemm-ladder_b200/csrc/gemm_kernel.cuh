@@ -79,7 +79,8 @@ struct Geom {
     static constexpr int kStages = kRingFit < BW_MAX_STAGES ? kRingFit : BW_MAX_STAGES;
     static constexpr int kTmemCols = pow2_at_least(2 * BN < 32 ? 32 : 2 * BN, 32);  // two accumulators
     static constexpr int kBarOffset = kStages * kStageBytes;
-    static constexpr int kNumBars = 2 * kStages + 6;  // full, empty, tmem full x2, tmem empty x2, drain, reduce
+    static constexpr int kNumBars = 2 * kStages + 8;  // full, empty, tmem full x2, tmem empty x2, drain, reduce,
+                                                      // and the K halves' go / receive (kpair)
     static constexpr int kSlotBytes = 128 * BN * 4;   // one partial of this block's rows
     static constexpr int kRingSlots = kBarOffset / kSlotBytes;  // partials the idle ring holds at once
     static constexpr int kMaxSum = kRingSlots + 1 < 8 ? kRingSlots + 1 : 8;  // partials the bulk reduction sums
@@ -380,6 +381,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* tempty = tfull + 2;
     uint64_t* drain = tempty + 2;
     uint64_t* rbar = drain + 1;  // the bulk reduction's copies of partials
+    uint64_t* kgo = rbar + 1;    // kpair, second block: the first block's ring may take this block's sum
+    uint64_t* krecv = rbar + 2;  // kpair, first block: the second block's sum has arrived
     __half* cst = reinterpret_cast<__half*>(smem + G::kCStageOffset);  // swap-AB epilogue transpose buffers
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + G::kMiscOffset);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -391,6 +394,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const Sched& s = p.s;
     const int rank = PAIR ? (int)cluster_ctarank() : 0;
     const bool leader = rank == 0;
+    const bool kp = SWAP && s.kpair;                   // swap-AB K halves on the two blocks of a cluster
+    const int khalf = kp ? (int)cluster_ctarank() : 0;  // 0: the block that writes C
     const int P = gridDim.x / R, c = blockIdx.x / R;  // the two blocks of a pair share their segments
 
     if (threadIdx.x == 0) {
@@ -404,6 +409,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         mbar_init(drain, 1);
         mbar_init(rbar, 1);
+        mbar_init(kgo, 1);    // the first block's remote arrival
+        mbar_init(krecv, 1);  // the first block's arrive.expect_tx; the second block's st.async bytes complete it
         *abort_flag = 0;
         *reduce_flag = 0;
         epi_go[0] = epi_go[1] = 0;
@@ -424,7 +431,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     __syncwarp();
     tc_fence_before();
-    if (PAIR)
+    if (PAIR || kp)
         cluster_sync();  // the leader's barriers exist before the other block's loads and arrivals reach them
     else
         __syncthreads();
@@ -650,6 +657,64 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                 }
                 release_acc(acc);
+            } else if (kp) {
+                // a tile's K halves on the two blocks of this cluster (their only segment, so the first block's stage
+                // ring is idle once its accumulator is complete): the second block sends its sum into that ring, 16
+                // bytes per st.async, counted on the first block's krecv barrier; the first adds it to its own sum in
+                // a fixed order and writes C.  One thread waits (bounded) and hands the outcome to the other 127.
+                const float4* peer = reinterpret_cast<const float4*>(smem) + row;  // [col / 4][row][4]
+                if (khalf == 0) {
+                    if (threadIdx.x == kEpiThread0) {
+                        mbar_arrive_expect_tx(krecv, 128u * BN * 4u);
+                        mbar_arrive_cluster(mapa_shared(smem_u32(kgo), 1));  // the ring may take the other sum now
+                        const bool ok = wait_bounded(krecv, 0, abort_flag, p.wait_ns, site(2, 5, 0), seg);
+                        if (!ok) wait_drain(krecv, 0, p.wait_ns);  // st.async bytes still on their way land first
+                        *reduce_flag = ok ? 1 : 0;
+                    }
+                    named_bar_sync(1, 128);
+                    if (*reduce_flag) {
+                        mbar_try_wait(smem_u32(krecv), 0);  // complete: each thread acquires the bytes that arrived
+#pragma unroll 1
+                        for (int c0 = 0; c0 < BN; c0 += 16) {
+                            uint32_t r[16];
+                            tmem_ld16(tbase + (uint32_t)c0, r);
+                            tmem_wait_ld();
+                            float v[16];
+#pragma unroll
+                            for (int j = 0; j < 4; ++j) {
+                                const float4 w = peer[(c0 / 4 + j) * 128];
+                                v[4 * j] = __uint_as_float(r[4 * j]) + w.x;
+                                v[4 * j + 1] = __uint_as_float(r[4 * j + 1]) + w.y;
+                                v[4 * j + 2] = __uint_as_float(r[4 * j + 2]) + w.z;
+                                v[4 * j + 3] = __uint_as_float(r[4 * j + 3]) + w.w;
+                            }
+                            store_chunk<SWAP, EPI>(p, m0, n0, row, c0, v, cst);
+                        }
+                    }
+                } else {
+                    if (threadIdx.x == kEpiThread0) {
+                        const bool ok = wait_bounded(kgo, 0, abort_flag, p.wait_ns, site(2, 6, 0), seg);
+                        if (ok) fence_acq_rel_cluster();  // after the first block's arrival (release, cluster scope)
+                        *reduce_flag = ok ? 1 : 0;
+                    }
+                    named_bar_sync(1, 128);
+                    if (*reduce_flag) {
+                        const uint32_t dst = mapa_shared(smem_u32(smem), 0) + (uint32_t)row * 16u;
+                        const uint32_t bar = mapa_shared(smem_u32(krecv), 0);
+#pragma unroll 1
+                        for (int c0 = 0; c0 < BN; c0 += 16) {
+                            uint32_t r[16];
+                            tmem_ld16(tbase + (uint32_t)c0, r);
+                            tmem_wait_ld();
+#pragma unroll
+                            for (int j = 0; j < 4; ++j)
+                                st_async_v4(dst + (uint32_t)((c0 / 4 + j) * 128 * 16), r[4 * j], r[4 * j + 1],
+                                            r[4 * j + 2], r[4 * j + 3], bar);
+                        }
+                    }
+                }
+                release_acc(acc);
+                named_bar_sync(1, 128);  // reduce_flag is read by all before the next segment writes it
             } else if (sg.k0 == 0 && sg.k1 == s.kblocks) {
                 // a whole tile: straight to C
 #pragma unroll 1
@@ -740,7 +805,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     __syncwarp();
     tc_fence_before();
-    if (PAIR)
+    if (PAIR || kp)
         cluster_sync();  // neither block leaves while the other may still read its memory or arrive on its barriers
     else
         __syncthreads();

@@ -45,11 +45,11 @@ constexpr int kVariants = 8;
 inline const char* variant_name(int v)
 {
     switch (v) {
-    case 0: return "v0: the rule (swap-AB + stream-K at M <= 128; 256x256 pair tiles + split-K tail above)";
+    case 0: return "v0: the rule (swap-AB + cluster K halves or stream-K at M <= 128; 256x256 pair tiles + split-K tail above)";
     case 1: return "v1: without split-K / stream-K (whole tiles only, round-robin)";
     case 2: return "v2: without swap-AB (pair tiles at every M)";
     case 3: return "v3: without the serpentine order (tiles row after row)";
-    case 4: return "v4: stream-K in place of the split-K tail";
+    case 4: return "v4: stream-K in place of the split-K tail and of the cluster K halves (M <= 128)";
     case 5: return "v5: without the SM pair (128x256 tiles on single SMs)";
     case 6: return "v6: 128x64 tiles on single SMs at every M (no swap-AB, no pair)";
     case 7: return "v7: 128x128 tiles on single SMs at every M (no swap-AB, no pair)";
@@ -75,7 +75,7 @@ inline int plan_tmem_cols(int bn)
 inline int plan_smem_bytes(int bn, int ranks, bool swap)
 {
     const int st = plan_stages(bn, ranks, swap);
-    const int misc = st * plan_stage_bytes(bn, ranks) + (2 * st + 6) * 8;
+    const int misc = st * plan_stage_bytes(bn, ranks) + (2 * st + 8) * 8;
     const int cstage = (misc + 32 + 127) / 128 * 128;
     return 1024 + cstage + plan_cstage_bytes(swap);
 }
@@ -137,6 +137,22 @@ inline int make_plan(int M, int N, int K, int sms, int pairs, int variant, bw_pl
     q.tiles = q.tiles_m * q.tiles_n;
     const long long kb = q.kblocks;
     const bool stream_k = swap ? variant != 1 : variant == 4;
+    // swap-AB with every tile's two K halves at once on the SMs: clusters of two blocks, one half each, the second
+    // block's sum sent to the first through distributed shared memory (no partials in memory, no counters)
+    const int clusters = pairs > 0 ? pairs : sms / 2;  // clusters of two blocks held at once
+    const bool kpair = swap && variant != 1 && variant != 4 && q.tiles <= clusters && q.kblocks >= 2;
+    if (kpair) {
+        q.kpair = 1;
+        q.dp_tiles = 0;
+        q.sk_tiles = q.tiles;
+        q.splits = 2;
+        q.grid = 2 * q.tiles;
+        q.stages = plan_stages(q.bn, 1, true);
+        q.smem_bytes = plan_smem_bytes(q.bn, 1, true);
+        q.tmem_cols = plan_tmem_cols(q.bn);
+        *p = q;
+        return BW_OK;
+    }
     if (variant == 1 || q.tiles % units == 0) {
         q.dp_tiles = q.tiles;  // whole tiles only
     } else if (stream_k) {

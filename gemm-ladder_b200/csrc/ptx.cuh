@@ -175,6 +175,18 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr)
     asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 
+// 16 bytes into another block's shared memory (`dst`, a shared::cluster address), counted as transaction bytes on
+// that block's barrier `bar` (a shared::cluster address in the same block): the receiver waits on its barrier alone.
+__device__ __forceinline__ void st_async_v4(uint32_t dst, uint32_t a, uint32_t b, uint32_t c, uint32_t d, uint32_t bar)
+{
+    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.b32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(dst),
+                 "r"(a), "r"(b), "r"(c), "r"(d), "r"(bar)
+                 : "memory");
+}
+
+// Orders this thread's accesses after an acquire at cluster scope (after a wait on a barrier another block arrived on).
+__device__ __forceinline__ void fence_acq_rel_cluster() { asm volatile("fence.acq_rel.cluster;" ::: "memory"); }
+
 // A 2-D tiled load into this block's shared memory whose bytes complete on a barrier of either block of the pair
 // (`bar`: a shared::cluster address) -- each block of the pair loads its own halves, the leader's barrier counts both.
 // No multicast: each block reads only what it holds.

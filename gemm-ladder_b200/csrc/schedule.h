@@ -16,6 +16,9 @@
 // A tile computed by several blocks: each writes its fp32 partial to a workspace slot; the last to finish (a counter
 // per tile) sums the partials in a fixed order (split order, or block order) -- so the result is the same bits
 // whichever block finishes last -- and writes C.
+// Or (kpair, swap-AB only, every tile at once): block 2 t + r of the grid's clusters of two takes K half r of tile t,
+// its only segment; the second block of the cluster sends its sum to the first through distributed shared memory, no
+// workspace involved.
 #pragma once
 #if defined(__CUDACC__)
 #define BW_HD __host__ __device__
@@ -35,6 +38,7 @@ struct Sched {
     int splits;           // > 0: split-K into this many K ranges; 0: stream-K
     long long sk_iters;   // stream-K: sk_tiles * kblocks, split evenly over the blocks
     int group_rows;       // serpentine group height in rows of tiles; 0: row after row
+    int kpair;            // 1: each tile's K halves on the two blocks of a cluster (one segment per block)
 };
 
 // ------------------------------------------------------------------ stream-K bookkeeping
@@ -86,6 +90,16 @@ struct SegIter {
     }
     BW_HD bool next(const Sched& s, int P, Seg& seg)
     {
+        if (s.kpair) {  // block c: half c % 2 of tile c / 2's K-blocks, once
+            if (next_u < 0 || next_u >= 2 * s.tiles) return false;
+            const int h = next_u & 1;
+            seg.tile = next_u >> 1;
+            seg.k0 = h ? s.kblocks / 2 : 0;
+            seg.k1 = h ? s.kblocks : s.kblocks / 2;
+            seg.unit = h * s.tiles + seg.tile;
+            next_u = -1;
+            return true;
+        }
         // split-K units first: the reduction of a split tile then overlaps the block's next tiles (the epilogue
         // of one segment runs while the MMAs of the next fill the other accumulator), not the end of the kernel
         if (s.splits > 0 && next_u < s.sk_tiles * s.splits) {
@@ -154,7 +168,7 @@ BW_HD inline int fixup_slot(const Sched& s, int P, int tile, const Fixup& f, int
 // The number of workspace slots a schedule needs.
 BW_HD inline long long workspace_slots(const Sched& s, int P)
 {
-    if (s.sk_tiles <= 0) return 0;
+    if (s.sk_tiles <= 0 || s.kpair) return 0;
     return s.splits > 0 ? (long long)s.sk_tiles * s.splits : 2LL * P;
 }
 

@@ -115,6 +115,7 @@ typedef struct bw_plan {
     int counters;        /* one counter per split tile */
     int smem_bytes;      /* dynamic shared memory per block */
     int tmem_cols;       /* tensor-memory columns per block */
+    int kpair;           /* 1: SWAP with each tile's K halves on the two blocks of a cluster (grid = 2 tiles) */
 } bw_plan;
 
 /*

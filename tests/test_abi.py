@@ -57,7 +57,11 @@ def test_wait_selftest_without_a_gpu_reports_a_failure_not_a_timeout():
 def test_plan_rule_on_the_judge_shapes():
     for name, M, N, K in JUDGE_B200:
         p = bwgemm.plan(M, N, K, sms=148)
-        if M <= 128:
+        if M <= 128 and p["tiles"] <= 74:  # every tile's K halves at once on clusters of two SMs
+            assert p["kernel"] == bwgemm.BW_KERNEL_SWAP and p["bn"] == M and p["kpair"] == 1
+            assert p["grid"] == 2 * p["tiles"] and p["splits"] == 2 and p["workspace_bytes"] == 0
+            assert p["counters"] == 0
+        elif M <= 128:
             assert p["kernel"] == bwgemm.BW_KERNEL_SWAP and p["bn"] == M and p["dp_tiles"] == 0
             assert p["grid"] == 148 and p["sk_iters"] == p["tiles"] * (K // 64) and p["splits"] == 0
         else:
@@ -69,6 +73,8 @@ def test_plan_rule_on_the_judge_shapes():
 
 def test_plan_variants_take_out_one_mechanism():
     assert bwgemm.plan(16, 8192, 8192, variant=1)["sk_iters"] == 0          # no stream-K
+    v4s = bwgemm.plan(16, 8192, 8192, variant=4)                            # stream-K, not the cluster K halves
+    assert v4s["kpair"] == 0 and v4s["sk_iters"] == 64 * 128
     assert bwgemm.plan(16, 8192, 8192, variant=2)["kernel"] == bwgemm.BW_KERNEL_PAIR  # no swap-AB
     assert bwgemm.plan(512, 8192, 8192, variant=5)["kernel"] == bwgemm.BW_KERNEL_TILE  # no SM pair
     assert bwgemm.plan(8192, 8192, 8192, variant=3)["group_rows"] == 0      # row order
