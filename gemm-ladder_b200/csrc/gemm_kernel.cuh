@@ -716,16 +716,21 @@ __global__ void __launch_bounds__(kThreads, 1)
                 release_acc(acc);
                 named_bar_sync(1, 128);  // reduce_flag is read by all before the next segment writes it
             } else if (sg.k0 == 0 && sg.k1 == s.kblocks) {
-                // a whole tile: straight to C
+                // a whole tile: straight to C, kLdw columns per wait on the tensor-memory loads
+                constexpr int kLdw = BN % BW_EPI_LDW == 0 ? BW_EPI_LDW : 16;
 #pragma unroll 1
-                for (int c0 = 0; c0 < BN; c0 += 16) {
-                    uint32_t r[16];
-                    tmem_ld16(tbase + (uint32_t)c0, r);
-                    tmem_wait_ld();
-                    float v[16];
+                for (int c0 = 0; c0 < BN; c0 += kLdw) {
+                    uint32_t r[kLdw / 16][16];
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[j]);
-                    store_chunk<SWAP, EPI>(p, m0, n0, row, c0, v, cst);
+                    for (int h = 0; h < kLdw / 16; ++h) tmem_ld16(tbase + (uint32_t)(c0 + 16 * h), r[h]);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int h = 0; h < kLdw / 16; ++h) {
+                        float v[16];
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[h][j]);
+                        store_chunk<SWAP, EPI>(p, m0, n0, row, c0 + 16 * h, v, cst);
+                    }
                 }
                 release_acc(acc);
             } else {

@@ -39,6 +39,15 @@
 #define BW_SWAP_HINT_B 2       // swap-AB (M <= 128): the weights are read once, evict first (measured: o_m128 -11 %)
 #endif
 
+#ifndef BW_EPI_LDW
+#define BW_EPI_LDW 64          // epilogue: accumulator columns loaded from tensor memory per wait (16, 32 or 64;
+                               // measured: 64 cuts the last tile's epilogue, o_m512 -3 %)
+#endif
+#ifndef BW_SK_ONE_WAVE
+#define BW_SK_ONE_WAVE 1       // stream-K over every tile when they make one full wave and part of another (the
+                               // split-K tail's units then double a block's work: measured qkv_m512 -12 %)
+#endif
+
 namespace bw {
 
 constexpr int kVariants = 8;
@@ -136,7 +145,8 @@ inline int make_plan(int M, int N, int K, int sms, int pairs, int variant, bw_pl
     }
     q.tiles = q.tiles_m * q.tiles_n;
     const long long kb = q.kblocks;
-    const bool stream_k = swap ? variant != 1 : variant == 4;
+    const bool one_wave = BW_SK_ONE_WAVE && !swap && q.tiles > units && q.tiles < 2 * units;
+    const bool stream_k = swap ? variant != 1 : variant == 4 || (variant == 0 && one_wave);
     // swap-AB with every tile's two K halves at once on the SMs: clusters of two blocks, one half each, the second
     // block's sum sent to the first through distributed shared memory (no partials in memory, no counters)
     const int clusters = pairs > 0 ? pairs : sms / 2;  // clusters of two blocks held at once
