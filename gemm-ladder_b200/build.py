@@ -1,5 +1,6 @@
 """Build the rung's native code in-tree: gemm-ladder_b200/lib/libbwgemm.so (sm_100a, cross-compiled by nvcc; no GPU
-needed).  ``python gemm-ladder_b200/build.py [--force]``."""
+needed).  ``python gemm-ladder_b200/build.py [--force] [--trace]``; --trace builds lib/libbwgemm_trace.so, the same
+library with the per-block timeline compiled in (-DBW_TRACE, read by timeline.py)."""
 import os
 import shutil
 import subprocess
@@ -10,6 +11,7 @@ ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 LIB_DIR = os.path.join(HERE, "lib")
 LIB = os.path.join(LIB_DIR, "libbwgemm.so")
+TRACE_LIB = os.path.join(LIB_DIR, "libbwgemm_trace.so")
 INCLUDE = os.path.join(ROOT, "include")
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -32,25 +34,27 @@ def sources():
     return out
 
 
-def up_to_date():
-    if not os.path.exists(LIB):
+def up_to_date(lib=LIB):
+    if not os.path.exists(lib):
         return False
-    t = os.path.getmtime(LIB)
+    t = os.path.getmtime(lib)
     return all(os.path.getmtime(s) <= t for s in sources())
 
 
-def build(force=False, verbose=False):
-    """Compile libbwgemm.so if a source is newer than it (or force)."""
-    if not force and up_to_date():
-        return LIB
+def build(force=False, verbose=False, trace=False):
+    """Compile libbwgemm.so (trace: libbwgemm_trace.so) if a source is newer than it (or force)."""
+    lib = TRACE_LIB if trace else LIB
+    if not force and up_to_date(lib):
+        return lib
     os.makedirs(LIB_DIR, exist_ok=True)
-    cmd = [nvcc(), *NVCC_FLAGS, os.path.join(CSRC, "bwgemm.cu"), "-o", LIB + ".tmp"]
+    cmd = [nvcc(), *NVCC_FLAGS, *(["-DBW_TRACE"] if trace else []), os.path.join(CSRC, "bwgemm.cu"), "-o",
+           lib + ".tmp"]
     if verbose:
         print(" ".join(cmd))
     subprocess.check_call(cmd)
-    os.replace(LIB + ".tmp", LIB)
-    return LIB
+    os.replace(lib + ".tmp", lib)
+    return lib
 
 
 if __name__ == "__main__":
-    print(build(force="--force" in sys.argv, verbose=True))
+    print(build(force="--force" in sys.argv, verbose=True, trace="--trace" in sys.argv))

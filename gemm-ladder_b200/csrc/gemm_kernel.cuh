@@ -62,7 +62,11 @@ constexpr int kTraceSlots = 16;
 __device__ unsigned long long g_trace[1024 * kTraceSlots];
 #define BW_TRACE_AT(slot) (g_trace[blockIdx.x * kTraceSlots + (slot)] = globaltimer_ns())
 #define BW_TRACE_VAL(slot, v) (g_trace[blockIdx.x * kTraceSlots + (slot)] = (unsigned long long)(v))
+// a block's slots from an earlier launch are cleared at its entry (a slot no role of this block stamps reads 0)
+#define BW_TRACE_CLEAR() \
+    for (int i_ = 1; i_ < kTraceSlots; ++i_) g_trace[blockIdx.x * kTraceSlots + i_] = 0ull
 #else
+#define BW_TRACE_CLEAR() ((void)0)
 #define BW_TRACE_VAL(slot, v) ((void)0)
 #define BW_TRACE_AT(slot) ((void)0)
 #endif
@@ -390,7 +394,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     volatile int* epi_go = abort_flag + 2;  // two slots, alternating by segment
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    if (threadIdx.x == 0) BW_TRACE_AT(0);
+    if (threadIdx.x == 0) {
+        BW_TRACE_CLEAR();
+        BW_TRACE_AT(0);
+    }
     const Sched& s = p.s;
     const int rank = PAIR ? (int)cluster_ctarank() : 0;
     const bool leader = rank == 0;
