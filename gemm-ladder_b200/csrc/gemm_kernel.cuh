@@ -190,6 +190,68 @@ __device__ __forceinline__ void store_chunk(const Params& p, int m0, int n0, int
     }
 }
 
+// 64 columns of C from the 32 rows of one epilogue warp (TILE and PAIR; lane l holds row r0 + l, as the accumulator's
+// TMEM lanes give it), stored as whole lines.  A thread writing its own row would touch 32 rows per warp store, half a
+// sector each (measured: 16 GB/s per SM for a 128 x 256 fp16 tile); instead the 16-byte pieces are transposed within
+// groups of P lanes (P = pieces per row of 64 columns: 8 in fp16, 16 in fp32) by log2(P) rounds of shfl_xor, after
+// which lane q of a group holds piece q of the group's P rows, and each store writes 32 / P rows of 128 (256) bytes
+// (measured: 53 GB/s per SM).
+template <int P>
+__device__ __forceinline__ void transpose_pieces(uint32_t (&x)[P][4], int lane)
+{
+    const int q = lane & (P - 1);
+#pragma unroll
+    for (int m = P / 2; m >= 1; m >>= 1) {
+        const bool hi = (q & m) != 0;
+#pragma unroll
+        for (int e = 0; e < P; ++e) {
+            if (e & m) continue;
+#pragma unroll
+            for (int w = 0; w < 4; ++w) {  // the lower lane keeps piece e and takes e | m; the upper the other way
+                const uint32_t send = hi ? x[e][w] : x[e | m][w];
+                const uint32_t recv = __shfl_xor_sync(0xffffffffu, send, m);
+                if (hi)
+                    x[e][w] = recv;
+                else
+                    x[e | m][w] = recv;
+            }
+        }
+    }
+}
+
+template <int EPI>
+__device__ __forceinline__ void store_rows64(const Params& p, int r0, int n, int lane, const float (&v)[64])
+{
+    static_assert(EPI == kEpiF16 || EPI == kEpiF32, "fp16 or fp32 C");
+    constexpr int P = EPI == kEpiF32 ? 16 : 8;
+    const Sched& s = p.s;
+    uint32_t x[P][4];
+#pragma unroll
+    for (int i = 0; i < P; ++i)
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+            if (EPI == kEpiF32) {
+                x[i][w] = __float_as_uint(v[4 * i + w]);
+            } else {
+                const __half2 h = __floats2half2_rn(v[8 * i + 2 * w], v[8 * i + 2 * w + 1]);
+                x[i][w] = *reinterpret_cast<const uint32_t*>(&h);
+            }
+        }
+    transpose_pieces<P>(x, lane);
+    const int q = lane & (P - 1), g = lane / P;
+    if (n >= s.N) return;  // N % 64 == 0: the 64 columns are all in C or all outside
+#pragma unroll
+    for (int e = 0; e < P; ++e) {
+        const int m = r0 + g * P + e;
+        if (m < s.M) {
+            uint4* dst = EPI == kEpiF32
+                             ? reinterpret_cast<uint4*>(static_cast<float*>(p.C) + (size_t)m * s.N + n) + q
+                             : reinterpret_cast<uint4*>(static_cast<__half*>(p.C) + (size_t)m * s.N + n) + q;
+            *dst = make_uint4(x[e][0], x[e][1], x[e][2], x[e][3]);
+        }
+    }
+}
+
 // ------------------------------------------------------------------ the partials of a split tile
 // Slot layout: 128 rows x BN columns of fp32, interleaved by groups of 4 columns: [col / 4][row][col % 4].  TMEM lane
 // `row`'s 4-column group is one 16-byte vector, and the 32 lanes of a warp touch 512 contiguous bytes per vector
@@ -314,9 +376,9 @@ __device__ __noinline__ bool reduce_tile_bulk(const Params& p, int P, int tile, 
     if (threadIdx.x == kEpiThread0) BW_TRACE_AT(10);
     // [col / 4][row][4] within a slot: consecutive rows are consecutive 16-byte vectors
     const float4* base = reinterpret_cast<const float4*>(ring) + row;
-#pragma unroll 1
-    for (int chunk = 0; chunk < kChunks; ++chunk) {
-        float4 own[4], acc[4];
+    // the sum of 16 columns (chunk) of this row, in summation order
+    auto sum_chunk = [&](int chunk, float4 (&acc)[4]) {
+        float4 own[4];
         if (own_mine) {
             uint32_t r[16];
             tmem_ld16(tbase + (uint32_t)(chunk * 16), r);
@@ -353,15 +415,41 @@ __device__ __noinline__ bool reduce_tile_bulk(const Params& p, int P, int tile, 
                 }
             }
         }
-        float v[16];
+    };
+    if constexpr (!SWAP && BN % 64 == 0 && BW_EPI_LINES && (EPI == kEpiF16 || EPI == kEpiF32)) {
+        // 64 columns at a time, stored as whole lines of C (store_rows64)
+#pragma unroll 1
+        for (int c0 = 0; c0 < BN; c0 += 64) {
+            float v[64];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            v[4 * q] = acc[q].x;
-            v[4 * q + 1] = acc[q].y;
-            v[4 * q + 2] = acc[q].z;
-            v[4 * q + 3] = acc[q].w;
+            for (int h = 0; h < 4; ++h) {
+                float4 acc[4];
+                sum_chunk(c0 / 16 + h, acc);
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    v[16 * h + 4 * q] = acc[q].x;
+                    v[16 * h + 4 * q + 1] = acc[q].y;
+                    v[16 * h + 4 * q + 2] = acc[q].z;
+                    v[16 * h + 4 * q + 3] = acc[q].w;
+                }
+            }
+            store_rows64<EPI>(p, m0 + (row & ~31), n0 + c0, row & 31, v);
         }
-        store_chunk<SWAP, EPI>(p, m0, n0, row, chunk * 16, v, cst);
+    } else {
+#pragma unroll 1
+        for (int chunk = 0; chunk < kChunks; ++chunk) {
+            float4 acc[4];
+            sum_chunk(chunk, acc);
+            float v[16];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                v[4 * q] = acc[q].x;
+                v[4 * q + 1] = acc[q].y;
+                v[4 * q + 2] = acc[q].z;
+                v[4 * q + 3] = acc[q].w;
+            }
+            store_chunk<SWAP, EPI>(p, m0, n0, row, chunk * 16, v, cst);
+        }
     }
     if (threadIdx.x == kEpiThread0) BW_TRACE_AT(11);
     return true;
@@ -731,12 +819,19 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                     for (int h = 0; h < kLdw / 16; ++h) tmem_ld16(tbase + (uint32_t)(c0 + 16 * h), r[h]);
                     tmem_wait_ld();
+                    if (!SWAP && kLdw == 64 && BW_EPI_LINES) {  // whole lines of C (store_rows64)
+                        float v[64];
 #pragma unroll
-                    for (int h = 0; h < kLdw / 16; ++h) {
-                        float v[16];
+                        for (int j = 0; j < 64; ++j) v[j] = __uint_as_float(r[j / 16][j % 16]);
+                        store_rows64<EPI == kEpiF32 ? kEpiF32 : kEpiF16>(p, m0 + q * 32, n0 + c0, lane, v);
+                    } else {
 #pragma unroll
-                        for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[h][j]);
-                        store_chunk<SWAP, EPI>(p, m0, n0, row, c0 + 16 * h, v, cst);
+                        for (int h = 0; h < kLdw / 16; ++h) {
+                            float v[16];
+#pragma unroll
+                            for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[h][j]);
+                            store_chunk<SWAP, EPI>(p, m0, n0, row, c0 + 16 * h, v, cst);
+                        }
                     }
                 }
                 release_acc(acc);

@@ -43,6 +43,10 @@
 #define BW_EPI_LDW 64          // epilogue: accumulator columns loaded from tensor memory per wait (16, 32 or 64;
                                // measured: 64 cuts the last tile's epilogue, o_m512 -3 %)
 #endif
+#ifndef BW_EPI_LINES
+#define BW_EPI_LINES 1         // TILE / PAIR epilogue: whole-line stores of C after an in-warp transpose (0: a row
+                               // per thread)
+#endif
 #ifndef BW_SK_ONE_WAVE
 #define BW_SK_ONE_WAVE 1       // stream-K over every tile when they make one full wave and part of another (the
                                // split-K tail's units then double a block's work: measured qkv_m512 -12 %)
