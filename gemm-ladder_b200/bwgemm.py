@@ -39,6 +39,7 @@ class Plan(ctypes.Structure):
         ("smem_bytes", ctypes.c_int),
         ("tmem_cols", ctypes.c_int),
         ("kpair", ctypes.c_int),
+        ("wm", ctypes.c_int),
     ]
 
     def as_dict(self):

@@ -143,13 +143,13 @@ int ensure_workspace(DeviceState& d, const bw_plan& q, cudaStream_t st)
 }
 
 // Clusters of two blocks for the SM pair (PAIR) and for a swap-AB plan's K halves (kpair).
-template <int BN, bool SWAP, bool PAIR>
+template <int BN, bool SWAP, bool PAIR, int WM = 1>
 cudaLaunchConfig_t launch_config(int grid, cudaStream_t st, cudaLaunchAttribute* attr, bool kpair = false)
 {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = Geom<BN, SWAP, PAIR>::kSmemBytes;
+    cfg.dynamicSmemBytes = Geom<BN, SWAP, PAIR, WM>::kSmemBytes;
     cfg.stream = st;
     const bool cluster = PAIR || (SWAP && kpair);
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -161,12 +161,12 @@ cudaLaunchConfig_t launch_config(int grid, cudaStream_t st, cudaLaunchAttribute*
     return cfg;
 }
 
-template <int BN, bool SWAP, bool PAIR, int EPI = kEpiF16>
+template <int BN, bool SWAP, bool PAIR, int EPI = kEpiF16, int WM = 1>
 int set_smem_limit(DeviceState& d, unsigned bit)
 {
     if (d.attrs & bit) return BW_OK;
-    cudaError_t e = cudaFuncSetAttribute(gemm_kernel<BN, SWAP, PAIR, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         Geom<BN, SWAP, PAIR>::kSmemBytes);
+    cudaError_t e = cudaFuncSetAttribute(gemm_kernel<BN, SWAP, PAIR, EPI, WM>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, Geom<BN, SWAP, PAIR, WM>::kSmemBytes);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
     d.attrs |= bit;
     return BW_OK;
@@ -190,21 +190,22 @@ int pair_occupancy(DeviceState& d)
     return BW_OK;
 }
 
-template <int BN, bool SWAP, bool PAIR, int EPI = kEpiF16>
+template <int BN, bool SWAP, bool PAIR, int EPI = kEpiF16, int WM = 1>
 int launch_kernel(DeviceState& d, unsigned bit, const bw_plan& q, const CUtensorMap& mx, const CUtensorMap& my,
                   const Params& p, cudaStream_t st)
 {
-    using G = Geom<BN, SWAP, PAIR>;
-    if (q.smem_bytes != G::kSmemBytes || q.stages != G::kStages || q.tmem_cols != G::kTmemCols ||
-        (q.kpair && (!SWAP || q.grid % 2 || q.grid != 2 * q.tiles))) {
+    using G = Geom<BN, SWAP, PAIR, WM>;
+    // kpair: the second block's sum (128 x kAccN fp32) lands in the first block's idle stage ring
+    if (q.smem_bytes != G::kSmemBytes || q.stages != G::kStages || q.tmem_cols != G::kTmemCols || q.wm != WM ||
+        (q.kpair && (!SWAP || q.grid % 2 || q.grid != 2 * q.tiles || 128 * G::kAccN * 4 > G::kBarOffset))) {
         snprintf(g_errbuf, sizeof g_errbuf, "plan and kernel geometry disagree (bn %d)", BN);
         return BW_ERR_LAUNCH;
     }
-    int rc = set_smem_limit<BN, SWAP, PAIR, EPI>(d, bit);
+    int rc = set_smem_limit<BN, SWAP, PAIR, EPI, WM>(d, bit);
     if (rc) return rc;
     cudaLaunchAttribute attr[1];
-    const cudaLaunchConfig_t cfg = launch_config<BN, SWAP, PAIR>(q.grid, st, attr, q.kpair != 0);
-    cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_kernel<BN, SWAP, PAIR, EPI>, mx, my, p);
+    const cudaLaunchConfig_t cfg = launch_config<BN, SWAP, PAIR, WM>(q.grid, st, attr, q.kpair != 0);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_kernel<BN, SWAP, PAIR, EPI, WM>, mx, my, p);
     if (e != cudaSuccess) return cuda_fail(e, "kernel launch");
     return BW_OK;
 }
@@ -233,6 +234,19 @@ int dispatch(DeviceState& d, const bw_plan& q, const CUtensorMap& mx, const CUte
         case 64: return launch_kernel<64, false, false>(d, 1u << 10, q, mx, my, p, st);
         case 128: return launch_kernel<128, false, false>(d, 1u << 11, q, mx, my, p, st);
         case 256: return launch_kernel<256, false, false>(d, 1u << 0, q, mx, my, p, st);
+        default: return BW_ERR_ARG;
+        }
+    }
+    if (q.wm == 2) {  // swap-AB tiles of 256 weight columns
+        switch (q.bn) {
+        case 16: return launch_kernel<16, true, false, kEpiF16, 2>(d, 1u << 21, q, mx, my, p, st);
+        case 32: return launch_kernel<32, true, false, kEpiF16, 2>(d, 1u << 22, q, mx, my, p, st);
+        case 48: return launch_kernel<48, true, false, kEpiF16, 2>(d, 1u << 23, q, mx, my, p, st);
+        case 64: return launch_kernel<64, true, false, kEpiF16, 2>(d, 1u << 16, q, mx, my, p, st);
+        case 80: return launch_kernel<80, true, false, kEpiF16, 2>(d, 1u << 17, q, mx, my, p, st);
+        case 96: return launch_kernel<96, true, false, kEpiF16, 2>(d, 1u << 18, q, mx, my, p, st);
+        case 112: return launch_kernel<112, true, false, kEpiF16, 2>(d, 1u << 19, q, mx, my, p, st);
+        case 128: return launch_kernel<128, true, false, kEpiF16, 2>(d, 1u << 20, q, mx, my, p, st);
         default: return BW_ERR_ARG;
         }
     }
@@ -469,13 +483,18 @@ int noalloc_gemm(const void* A, const void* B, void* C, int M, int N, int K, cud
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
-    bw_plan q;
+    bw_plan q = {};
     void* scratch = nullptr;
     {
         std::lock_guard<std::mutex> lock(g_mu);
         if ((rc = pair_occupancy(*d))) return rc;
+        auto fits = [&] {
+            return q.workspace_bytes <= BW_NOALLOC_SCRATCH_BYTES && (unsigned)q.counters <= BW_NOALLOC_COUNTERS;
+        };
         if ((rc = make_plan(M, N, K, d->sms, d->pairs, 0, &q))) return rc;
-        if (q.workspace_bytes > BW_NOALLOC_SCRATCH_BYTES || (unsigned)q.counters > BW_NOALLOC_COUNTERS) {
+        // the 256-column swap tiles' partials are twice as large: 128-column tiles if those fit the array
+        if (!fits() && q.wm > 1 && (rc = make_plan(M, N, K, d->sms, d->pairs, 0, &q, kPlanNarrow))) return rc;
+        if (!fits()) {
             snprintf(g_errbuf, sizeof g_errbuf,
                      "%d x %d x %d needs %zu bytes of partials and %d counters; the fixed array holds %u and %u", M, N,
                      K, q.workspace_bytes, q.counters, BW_NOALLOC_SCRATCH_BYTES, BW_NOALLOC_COUNTERS);

@@ -71,21 +71,23 @@ __device__ unsigned long long g_trace[1024 * kTraceSlots];
 #define BW_TRACE_AT(slot) ((void)0)
 #endif
 
-template <int BN, bool SWAP, bool PAIR>
+template <int BN, bool SWAP, bool PAIR, int WM = 1>
 struct Geom {
     static constexpr int kRanks = PAIR ? 2 : 1;
     static constexpr int kTileM = PAIR ? 256 : 128;          // rows of C per tile (TILE, PAIR)
-    static constexpr int kXBytes = 128 * kBK * 2;            // this block's MMA-A operand: 128 rows x 64 K
+    static constexpr int kAccN = WM * BN;                    // TMEM columns of one accumulator (SWAP: WM weight
+                                                             // blocks of 128 columns, BN tokens each)
+    static constexpr int kXBytes = 128 * WM * kBK * 2;       // this block's MMA-A operand: 128 (x WM) rows x 64 K
     static constexpr int kYBytes = (BN / kRanks) * kBK * 2;  // this block's MMA-B operand: BN (PAIR: BN / 2) x 64 K
     static constexpr int kStageBytes = kXBytes + kYBytes;
     static constexpr int kCStageBytes = SWAP ? 2 * 16 * 128 * 2 : 0;  // swap-AB epilogue transpose buffers
     static constexpr int kRingFit = (BW_SMEM_LIMIT - 1024 - 512 - kCStageBytes) / kStageBytes;
     static constexpr int kStages = kRingFit < BW_MAX_STAGES ? kRingFit : BW_MAX_STAGES;
-    static constexpr int kTmemCols = pow2_at_least(2 * BN < 32 ? 32 : 2 * BN, 32);  // two accumulators
+    static constexpr int kTmemCols = pow2_at_least(2 * kAccN < 32 ? 32 : 2 * kAccN, 32);  // two accumulators
     static constexpr int kBarOffset = kStages * kStageBytes;
     static constexpr int kNumBars = 2 * kStages + 8;  // full, empty, tmem full x2, tmem empty x2, drain, reduce,
                                                       // and the K halves' go / receive (kpair)
-    static constexpr int kSlotBytes = 128 * BN * 4;   // one partial of this block's rows
+    static constexpr int kSlotBytes = 128 * kAccN * 4;  // one partial of this block's rows
     static constexpr int kRingSlots = kBarOffset / kSlotBytes;  // partials the idle ring holds at once
     static constexpr int kMaxSum = kRingSlots + 1 < 8 ? kRingSlots + 1 : 8;  // partials the bulk reduction sums
     static constexpr int kMiscOffset = kBarOffset + kNumBars * 8;
@@ -95,6 +97,7 @@ struct Geom {
     static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "MMA N: a multiple of 16 in [16, 256]");
     static_assert(SWAP || BN % (64 * kRanks) == 0, "B tiles are boxes of 64 columns (per block)");
     static_assert(!(SWAP && PAIR), "the swap-AB form runs on single blocks");
+    static_assert(WM == 1 || (SWAP && WM == 2), "two weight blocks per tile: swap-AB only");
     static_assert(kYBytes % 1024 == 0 && kXBytes % 1024 == 0, "operand tiles on 1024-byte swizzle atoms");
     static_assert(kStages >= 2 && kSmemBytes <= BW_SMEM_LIMIT, "shared memory");
     static_assert(kTmemCols <= 512, "tensor memory");
@@ -147,7 +150,7 @@ __device__ __forceinline__ uint64_t desc_mnmajor(uint32_t tile, int k) { return 
 // 16 x 128 fp16 buffers, alternating by chunk), so that C is written by 16-byte stores, a warp covering two rows of
 // 256 contiguous bytes, instead of 16 scattered 2-byte stores per thread.  One named barrier per chunk; the buffer of
 // chunk i + 2 is written only after every thread has passed the barrier of chunk i + 1, so after it read chunk i.
-template <bool SWAP, int EPI = kEpiF16>
+template <bool SWAP, int EPI = kEpiF16, int BT = 0>
 __device__ __forceinline__ void store_chunk(const Params& p, int m0, int n0, int lane, int c0, const float (&v)[16],
                                             __half* cst)
 {
@@ -178,11 +181,13 @@ __device__ __forceinline__ void store_chunk(const Params& p, int m0, int n0, int
         for (int j = 0; j < 16; ++j) buf[j * 128 + lane] = __float2half_rn(v[j]);
         named_bar_sync(1, 128);
         const int t = threadIdx.x - kEpiThread0;
+        // accumulator column c0: token c0 % BT of weight block c0 / BT (BT tokens per block; 0: one block)
+        const int wb = BT ? c0 / BT : 0, tok = c0 - wb * BT;
 #pragma unroll
         for (int k = 0; k < 2; ++k) {
             const int piece = t + 128 * k;  // 256 pieces of 8 fp16: 16 rows x 16 pieces
             const int mm = piece >> 4, nn = (piece & 15) * 8;
-            const int m = c0 + mm, n = n0 + nn;
+            const int m = tok + mm, n = n0 + wb * 128 + nn;
             if (m < s.M && n < s.N)
                 *reinterpret_cast<uint4*>(static_cast<__half*>(p.C) + (size_t)m * s.N + n) =
                     *reinterpret_cast<const uint4*>(buf + mm * 128 + nn);
@@ -268,7 +273,7 @@ __device__ __forceinline__ float4* slot_vec(const Params& p, long long slot, int
 // this block's accumulator in tensor memory when own_mine (tbase: its row's TMEM address), from its slot otherwise.
 // The loads from memory are a stream of (16-column chunk, partial) pairs in chunk order, kept kWin deep in flight:
 // with one partial in memory four chunks are on their way at once, instead of one L2 round trip per chunk.
-template <int BN, bool SWAP, int RANKS, int EPI>
+template <int BN, bool SWAP, int RANKS, int EPI, int BT = 0>
 __device__ __noinline__ void reduce_tile(const Params& p, int P, int tile, int rank, Fixup f, bool own_mine,
                                             uint32_t tbase, int row, int m0, int n0, __half* cst)
 {
@@ -340,7 +345,7 @@ __device__ __noinline__ void reduce_tile(const Params& p, int P, int tile, int r
 #pragma unroll
                         for (int e = 0; e < 16; ++e) v[e] += own[e];
                     }
-                    store_chunk<SWAP, EPI>(p, m0, n0, row, chunk * 16, v, cst);
+                    store_chunk<SWAP, EPI, BT>(p, m0, n0, row, chunk * 16, v, cst);
                 }
             }
         }
@@ -351,7 +356,7 @@ __device__ __noinline__ void reduce_tile(const Params& p, int P, int tile, int r
 // in memory are copied into the ring by the TMA engine at once (cp.async.bulk, one per partial), then summed from
 // shared memory.  The sum runs over at most kMaxSum partials, unrolled and predicated, so that everything stays in
 // registers.  Returns false if the copy did not complete within the wait limit (the block's abort flag is up).
-template <int BN, bool SWAP, int RANKS, int kMaxSum, int EPI>
+template <int BN, bool SWAP, int RANKS, int kMaxSum, int EPI, int BT = 0>
 __device__ __noinline__ bool reduce_tile_bulk(const Params& p, int P, int tile, int rank, Fixup f, bool own_mine,
                                               uint32_t tbase, int row, int m0, int n0, __half* cst, uint8_t* ring,
                                               uint64_t* rbar, volatile int* abort_flag, int seg)
@@ -448,7 +453,7 @@ __device__ __noinline__ bool reduce_tile_bulk(const Params& p, int P, int tile, 
                 v[4 * q + 2] = acc[q].z;
                 v[4 * q + 3] = acc[q].w;
             }
-            store_chunk<SWAP, EPI>(p, m0, n0, row, chunk * 16, v, cst);
+            store_chunk<SWAP, EPI, BT>(p, m0, n0, row, chunk * 16, v, cst);
         }
     }
     if (threadIdx.x == kEpiThread0) BW_TRACE_AT(11);
@@ -456,11 +461,12 @@ __device__ __noinline__ bool reduce_tile_bulk(const Params& p, int P, int tile, 
 }
 
 // ------------------------------------------------------------------ the kernel
-template <int BN, bool SWAP, bool PAIR, int EPI = kEpiF16>
+template <int BN, bool SWAP, bool PAIR, int EPI = kEpiF16, int WM = 1>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmy, const Params p)
 {
-    using G = Geom<BN, SWAP, PAIR>;
+    using G = Geom<BN, SWAP, PAIR, WM>;
+    constexpr int AN = G::kAccN;  // accumulator columns (TMEM)
     static_assert(!SWAP || EPI == kEpiF16, "fp32 and SwiGLU outputs are written by the TILE and PAIR forms");
     static_assert(EPI != kEpiSwiGLU || BN % 32 == 0, "SwiGLU pairs the two halves of a tile");
     constexpr int S = G::kStages;
@@ -573,8 +579,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                                                        &full[stage], barc, pol_b);
                     } else {
 #pragma unroll
-                        for (int j = 0; j < 2; ++j)  // B: 128 columns as two boxes of 64 columns x 64 K
-                            load_tile<false, BW_SWAP_HINT_B>(sx + j * 8192, &tmx, tn * 128 + 64 * j, kb * kBK,
+                        for (int j = 0; j < 2 * WM; ++j)  // B: 128 (x WM) columns as boxes of 64 columns x 64 K
+                            load_tile<false, BW_SWAP_HINT_B>(sx + j * 8192, &tmx, tn * 128 * WM + 64 * j, kb * kBK,
                                                              &full[stage], 0u, pol_sb);
                         load_tile<false, BW_HINT_A>(sy, &tmy, kb * kBK, 0, &full[stage], 0u, pol_a);  // A: 64 K x BN rows
                     }
@@ -618,7 +624,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 w_acc += globaltimer_ns() - ta0;
 #endif
                 tc_fence_after();
-                const uint32_t d = tmem_base + (uint32_t)(acc * BN);
+                const uint32_t d = tmem_base + (uint32_t)(acc * AN);
                 for (int kb = sg.k0; kb < sg.k1; ++kb) {
 #ifdef BW_TRACE
                     const unsigned long long tf0 = globaltimer_ns();
@@ -636,13 +642,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const uint32_t sx = smem_u32(smem + stage * G::kStageBytes), sy = sx + G::kXBytes;
 #pragma unroll
                     for (int k = 0; k < kBK / 16; ++k) {
-                        const uint64_t ad = SWAP ? desc_mnmajor(sx, k) : desc_kmajor(sx, k);
                         const uint64_t bd = SWAP ? desc_kmajor(sy, k) : desc_mnmajor(sy, k);
                         const uint32_t accumulate = (kb > sg.k0 || k > 0) ? 1u : 0u;
-                        if (PAIR)
-                            mma_f16_pair(d, ad, bd, idesc, accumulate);
-                        else
-                            mma_f16(d, ad, bd, idesc, accumulate);
+#pragma unroll
+                        for (int w = 0; w < WM; ++w) {  // SWAP: each 128-column weight block into its columns
+                            const uint64_t ad = SWAP ? desc_mnmajor(sx + (uint32_t)(w * 128 * kBK * 2), k)
+                                                     : desc_kmajor(sx, k);
+                            if (PAIR)
+                                mma_f16_pair(d, ad, bd, idesc, accumulate);
+                            else
+                                mma_f16(d + (uint32_t)(w * BN), ad, bd, idesc, accumulate);
+                        }
                     }
                     // the stage is free (in both blocks of a pair) once these MMAs have read it
                     if (PAIR) {
@@ -718,14 +728,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             int m0, n0;
             if (SWAP) {
                 m0 = 0;
-                n0 = sg.tile * 128;
+                n0 = sg.tile * 128 * WM;
             } else {
                 int tm, tn;
                 tile_coords(s, sg.tile, tm, tn);
                 m0 = tm * G::kTileM + rank * 128;
                 n0 = tn * BN;
             }
-            const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
+            const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * AN);
             if (EPI == kEpiSwiGLU) {
                 // a whole tile (the plan splits none): gate columns [0, BN/2), up columns [BN/2, BN) of the tile,
                 // silu(gate) * up to columns [n0 / 2, n0 / 2 + BN / 2) of the M x N/2 output
@@ -760,7 +770,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const float4* peer = reinterpret_cast<const float4*>(smem) + row;  // [col / 4][row][4]
                 if (khalf == 0) {
                     if (threadIdx.x == kEpiThread0) {
-                        mbar_arrive_expect_tx(krecv, 128u * BN * 4u);
+                        mbar_arrive_expect_tx(krecv, 128u * AN * 4u);
                         mbar_arrive_cluster(mapa_shared(smem_u32(kgo), 1));  // the ring may take the other sum now
                         const bool ok = wait_bounded(krecv, 0, abort_flag, p.wait_ns, site(2, 5, 0), seg);
                         if (!ok) wait_drain(krecv, 0, p.wait_ns);  // st.async bytes still on their way land first
@@ -770,7 +780,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (*reduce_flag) {
                         mbar_try_wait(smem_u32(krecv), 0);  // complete: each thread acquires the bytes that arrived
 #pragma unroll 1
-                        for (int c0 = 0; c0 < BN; c0 += 16) {
+                        for (int c0 = 0; c0 < AN; c0 += 16) {
                             uint32_t r[16];
                             tmem_ld16(tbase + (uint32_t)c0, r);
                             tmem_wait_ld();
@@ -783,7 +793,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                 v[4 * j + 2] = __uint_as_float(r[4 * j + 2]) + w.z;
                                 v[4 * j + 3] = __uint_as_float(r[4 * j + 3]) + w.w;
                             }
-                            store_chunk<SWAP, EPI>(p, m0, n0, row, c0, v, cst);
+                            store_chunk<SWAP, EPI, BN>(p, m0, n0, row, c0, v, cst);
                         }
                     }
                 } else {
@@ -797,7 +807,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const uint32_t dst = mapa_shared(smem_u32(smem), 0) + (uint32_t)row * 16u;
                         const uint32_t bar = mapa_shared(smem_u32(krecv), 0);
 #pragma unroll 1
-                        for (int c0 = 0; c0 < BN; c0 += 16) {
+                        for (int c0 = 0; c0 < AN; c0 += 16) {
                             uint32_t r[16];
                             tmem_ld16(tbase + (uint32_t)c0, r);
                             tmem_wait_ld();
@@ -812,9 +822,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 named_bar_sync(1, 128);  // reduce_flag is read by all before the next segment writes it
             } else if (sg.k0 == 0 && sg.k1 == s.kblocks) {
                 // a whole tile: straight to C, kLdw columns per wait on the tensor-memory loads
-                constexpr int kLdw = BN % BW_EPI_LDW == 0 ? BW_EPI_LDW : 16;
+                constexpr int kLdw = AN % BW_EPI_LDW == 0 ? BW_EPI_LDW : 16;
 #pragma unroll 1
-                for (int c0 = 0; c0 < BN; c0 += kLdw) {
+                for (int c0 = 0; c0 < AN; c0 += kLdw) {
                     uint32_t r[kLdw / 16][16];
 #pragma unroll
                     for (int h = 0; h < kLdw / 16; ++h) tmem_ld16(tbase + (uint32_t)(c0 + 16 * h), r[h]);
@@ -830,7 +840,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                             float v[16];
 #pragma unroll
                             for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[h][j]);
-                            store_chunk<SWAP, EPI>(p, m0, n0, row, c0 + 16 * h, v, cst);
+                            store_chunk<SWAP, EPI, BN>(p, m0, n0, row, c0 + 16 * h, v, cst);
                         }
                     }
                 }
@@ -854,23 +864,23 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 if (fast == 2) {
                     if (last_seg && f.nseg <= G::kMaxSum)
-                        reduce_tile_bulk<BN, SWAP, R, G::kMaxSum, EPI>(p, P, sg.tile, rank, f, true, tbase, row, m0, n0,
+                        reduce_tile_bulk<AN, SWAP, R, G::kMaxSum, EPI, BN>(p, P, sg.tile, rank, f, true, tbase, row, m0, n0,
                                                                   cst, smem, rbar, abort_flag, seg);
                     else
-                        reduce_tile<BN, SWAP, R, EPI>(p, P, sg.tile, rank, f, true, tbase, row, m0, n0, cst);
+                        reduce_tile<AN, SWAP, R, EPI, BN>(p, P, sg.tile, rank, f, true, tbase, row, m0, n0, cst);
                     release_acc(acc);
                     if (threadIdx.x == kEpiThread0) atomicExch(counter, 0);
                 } else {
                     // this block's partial to its slot; the last block to finish the tile sums them
                     const long long myslot = (long long)fixup_slot(s, P, sg.tile, f, f.mine) * R + rank;
 #pragma unroll 1
-                    for (int c0 = 0; c0 < BN; c0 += 16) {
+                    for (int c0 = 0; c0 < AN; c0 += 16) {
                         uint32_t r[16];
                         tmem_ld16(tbase + (uint32_t)c0, r);
                         tmem_wait_ld();
 #pragma unroll
                         for (int j = 0; j < 4; ++j)
-                            __stcg(slot_vec<BN>(p, myslot, row, c0 / 4 + j),
+                            __stcg(slot_vec<AN>(p, myslot, row, c0 / 4 + j),
                                    make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
                                                __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3])));
                     }
@@ -891,10 +901,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                             BW_TRACE_VAL(8, 1 | f.nseg << 8 | seg << 16);
                         }
                         if (last_seg && f.nseg <= G::kMaxSum)
-                            reduce_tile_bulk<BN, SWAP, R, G::kMaxSum, EPI>(p, P, sg.tile, rank, f, true, tbase, row, m0, n0,
+                            reduce_tile_bulk<AN, SWAP, R, G::kMaxSum, EPI, BN>(p, P, sg.tile, rank, f, true, tbase, row, m0, n0,
                                                                       cst, smem, rbar, abort_flag, seg);
                         else
-                            reduce_tile<BN, SWAP, R, EPI>(p, P, sg.tile, rank, f, false, tbase, row, m0, n0, cst);
+                            reduce_tile<AN, SWAP, R, EPI, BN>(p, P, sg.tile, rank, f, false, tbase, row, m0, n0, cst);
                         if (threadIdx.x == kEpiThread0) atomicExch(counter, 0);
                     }
                     if (last_seg) release_acc(acc);

@@ -47,6 +47,10 @@
 #define BW_EPI_LINES 1         // TILE / PAIR epilogue: whole-line stores of C after an in-warp transpose (0: a row
                                // per thread)
 #endif
+#ifndef BW_SWAP_WM2_MIN
+#define BW_SWAP_WM2_MIN 64     // swap-AB tiles of 256 weight columns (two MMAs on one stage of A) from this many tokens:
+                               // every 128-column tile re-reads all of A from L2 (0: never)
+#endif
 #ifndef BW_SK_ONE_WAVE
 #define BW_SK_ONE_WAVE 1       // stream-K over every tile when they make one full wave and part of another (the
                                // split-K tail's units then double a block's work: measured qkv_m512 -12 %)
@@ -62,7 +66,7 @@ inline const char* variant_name(int v)
     case 1: return "v1: without split-K / stream-K (whole tiles only, round-robin)";
     case 2: return "v2: without swap-AB (pair tiles at every M)";
     case 3: return "v3: without the serpentine order (tiles row after row)";
-    case 4: return "v4: stream-K in place of the split-K tail and of the cluster K halves (M <= 128)";
+    case 4: return "v4: stream-K in place of the split-K tail, of the cluster K halves and of 256-column swap tiles";
     case 5: return "v5: without the SM pair (128x256 tiles on single SMs)";
     case 6: return "v6: 128x64 tiles on single SMs at every M (no swap-AB, no pair)";
     case 7: return "v7: 128x128 tiles on single SMs at every M (no swap-AB, no pair)";
@@ -72,11 +76,11 @@ inline const char* variant_name(int v)
 
 // The kernels' geometry, as gemm_kernel.cuh's Geom computes it (checked against it at launch in bwgemm.cu): the ring
 // takes what the 227 KB leave after the alignment slack, the barriers and the swap-AB epilogue's transpose buffers.
-inline int plan_stage_bytes(int bn, int ranks) { return 128 * 64 * 2 + (bn / ranks) * 64 * 2; }
+inline int plan_stage_bytes(int bn, int ranks, int wm = 1) { return 128 * wm * 64 * 2 + (bn / ranks) * 64 * 2; }
 inline int plan_cstage_bytes(bool swap) { return swap ? 2 * 16 * 128 * 2 : 0; }
-inline int plan_stages(int bn, int ranks, bool swap)
+inline int plan_stages(int bn, int ranks, bool swap, int wm = 1)
 {
-    const int s = (BW_SMEM_LIMIT - 1024 - 512 - plan_cstage_bytes(swap)) / plan_stage_bytes(bn, ranks);
+    const int s = (BW_SMEM_LIMIT - 1024 - 512 - plan_cstage_bytes(swap)) / plan_stage_bytes(bn, ranks, wm);
     return s < BW_MAX_STAGES ? s : BW_MAX_STAGES;
 }
 inline int plan_tmem_cols(int bn)
@@ -85,10 +89,10 @@ inline int plan_tmem_cols(int bn)
     while (c < 2 * bn) c *= 2;
     return c;
 }
-inline int plan_smem_bytes(int bn, int ranks, bool swap)
+inline int plan_smem_bytes(int bn, int ranks, bool swap, int wm = 1)
 {
-    const int st = plan_stages(bn, ranks, swap);
-    const int misc = st * plan_stage_bytes(bn, ranks) + (2 * st + 8) * 8;
+    const int st = plan_stages(bn, ranks, swap, wm);
+    const int misc = st * plan_stage_bytes(bn, ranks, wm) + (2 * st + 8) * 8;
     const int cstage = (misc + 32 + 127) / 128 * 128;
     return 1024 + cstage + plan_cstage_bytes(swap);
 }
@@ -119,6 +123,7 @@ inline int tail_splits(int tail, int P, int kblocks, double fixup_kb)
 enum : unsigned {
     kPlanNoSwap = 1u,   // A is the MMA's A operand (fp32 and fused outputs are written by TILE and PAIR only)
     kPlanNoSplit = 2u,  // whole tiles only (a fused epilogue needs the complete sums)
+    kPlanNarrow = 4u,   // swap-AB tiles of 128 weight columns only (half the partials' scratch)
 };
 
 // sms: the SMs; pairs: the pairs of SMs the pair kernel can hold at once (its cluster occupancy).
@@ -152,20 +157,34 @@ inline int make_plan(int M, int N, int K, int sms, int pairs, int variant, bw_pl
     const bool one_wave = BW_SK_ONE_WAVE && !swap && q.tiles > units && q.tiles < 2 * units;
     const bool stream_k = swap ? variant != 1 : variant == 4 || (variant == 0 && one_wave);
     // swap-AB with every tile's two K halves at once on the SMs: clusters of two blocks, one half each, the second
-    // block's sum sent to the first through distributed shared memory (no partials in memory, no counters)
+    // block's sum sent to the first through distributed shared memory (no partials in memory, no counters).  Tiles of
+    // 128 weight columns if they all fit at once, else of 256 (two MMAs on each stage of A) if those do.
     const int clusters = pairs > 0 ? pairs : sms / 2;  // clusters of two blocks held at once
-    const bool kpair = swap && variant != 1 && variant != 4 && q.tiles <= clusters && q.kblocks >= 2;
-    if (kpair) {
+    const bool wide_ok = (variant == 0 || variant == 3) && !(flags & kPlanNarrow);
+    const int tiles256 = (N + 255) / 256;
+    const bool kpair_ok = swap && variant != 1 && variant != 4 && q.kblocks >= 2;
+    const int kpair_wm = !kpair_ok ? 0 : q.tiles <= clusters ? 1 : (wide_ok && tiles256 <= clusters) ? 2 : 0;
+    if (kpair_wm) {
         q.kpair = 1;
+        q.wm = kpair_wm;
+        q.tiles_n = (N + 128 * q.wm - 1) / (128 * q.wm);
+        q.tiles = q.tiles_n;
         q.dp_tiles = 0;
         q.sk_tiles = q.tiles;
         q.splits = 2;
         q.grid = 2 * q.tiles;
-        q.stages = plan_stages(q.bn, 1, true);
-        q.smem_bytes = plan_smem_bytes(q.bn, 1, true);
-        q.tmem_cols = plan_tmem_cols(q.bn);
+        q.stages = plan_stages(q.bn, 1, true, q.wm);
+        q.smem_bytes = plan_smem_bytes(q.bn, 1, true, q.wm);
+        q.tmem_cols = plan_tmem_cols(q.bn * q.wm);
         *p = q;
         return BW_OK;
+    }
+    // stream-K: tiles of 256 weight columns while they still outnumber the SMs (fewer, larger partials otherwise)
+    q.wm = 1;
+    if (swap && wide_ok && BW_SWAP_WM2_MIN > 0 && q.bn >= BW_SWAP_WM2_MIN && tiles256 >= sms) {
+        q.wm = 2;
+        q.tiles_n = tiles256;
+        q.tiles = q.tiles_n;
     }
     if (variant == 1 || q.tiles % units == 0) {
         q.dp_tiles = q.tiles;  // whole tiles only
@@ -198,14 +217,14 @@ inline int make_plan(int M, int N, int K, int sms, int pairs, int variant, bw_pl
         if (q.sk_iters < P) return BW_ERR_ARG;  // every block owns at least one stream-K K-block
     }
     q.grid = P * ranks;
-    q.stages = plan_stages(q.bn, ranks, swap);
-    q.smem_bytes = plan_smem_bytes(q.bn, ranks, swap);
-    q.tmem_cols = plan_tmem_cols(q.bn);
+    q.stages = plan_stages(q.bn, ranks, swap, q.wm);
+    q.smem_bytes = plan_smem_bytes(q.bn, ranks, swap, q.wm);
+    q.tmem_cols = plan_tmem_cols(q.bn * q.wm);
     q.counters = q.sk_tiles * ranks;
     Sched sc = {};
     sc.sk_tiles = q.sk_tiles;
     sc.splits = q.splits;
-    q.workspace_bytes = (size_t)workspace_slots(sc, P) * ranks * 128 * q.bn * sizeof(float);
+    q.workspace_bytes = (size_t)workspace_slots(sc, P) * ranks * 128 * q.bn * q.wm * sizeof(float);
     *p = q;
     return BW_OK;
 }

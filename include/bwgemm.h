@@ -90,7 +90,8 @@ int bw_gemm_dirty(void);
  * array of BW_NOALLOC_SCRATCH_BYTES + 4 * BW_NOALLOC_COUNTERS bytes, compiled into the library: every GPU that loads
  * the library holds it until the process exits.  The first call on a device looks up that array's device address
  * (once, with the device current); make that first call before any stream capture.  Calls never allocate or free.
- * A call whose plan needs more scratch than the array holds is refused with BW_ERR_SCRATCH before anything runs.
+ * A call whose plan needs more scratch than the array holds takes the plan with swap-AB tiles of 128 weight columns
+ * if that one fits (half the partials), and is otherwise refused with BW_ERR_SCRATCH before anything runs.
  * Every call shares the one array and clears the counters it uses on its stream first: two calls that overlap on
  * the GPU (different streams, or several host threads) race on it; order them, or use bw_gemm_f16.
  */
@@ -116,6 +117,7 @@ typedef struct bw_plan {
     int smem_bytes;      /* dynamic shared memory per block */
     int tmem_cols;       /* tensor-memory columns per block */
     int kpair;           /* 1: SWAP with each tile's K halves on the two blocks of a cluster (grid = 2 tiles) */
+    int wm;              /* SWAP: 128-column weight blocks per tile (1 or 2; 2 = two MMAs on each stage of A) */
 } bw_plan;
 
 /*

@@ -27,4 +27,7 @@ VERIF = [(16, 256, 64), (144, 256, 64), (128, 512, 128), (208, 512, 192), (272, 
 # swap path at every bn, stream-K with a block share inside one tile, data-parallel waves plus a stream-K tail.
 B200_EDGES = [(16, 64, 64), (32, 192, 128), (48, 320, 64), (64, 1088, 576), (80, 2112, 64), (96, 64, 4096),
               (112, 448, 192), (128, 128, 64), (144, 64, 64), (256, 320, 128), (272, 576, 1024), (384, 19008, 64),
-              (2048, 4864, 128), (1280, 7680, 192), (16, 128, 28672)]
+              (2048, 4864, 128), (1280, 7680, 192), (16, 128, 28672),
+              # 256-column swap tiles with the last one half outside N: K halves on clusters of two (two shapes),
+              # stream-K (the tiles outnumber the SMs)
+              (96, 9600, 512), (32, 9600, 576), (64, 38080, 128)]

@@ -57,12 +57,15 @@ def test_wait_selftest_without_a_gpu_reports_a_failure_not_a_timeout():
 def test_plan_rule_on_the_judge_shapes():
     for name, M, N, K in JUDGE_B200:
         p = bwgemm.plan(M, N, K, sms=148)
-        if M <= 128 and p["tiles"] <= 74:  # every tile's K halves at once on clusters of two SMs
-            assert p["kernel"] == bwgemm.BW_KERNEL_SWAP and p["bn"] == M and p["kpair"] == 1
+        if M <= 128 and -(-N // 256) <= 74:  # every tile's K halves at once on clusters of two SMs
+            wm = 1 if -(-N // 128) <= 74 else 2  # tiles of 128 weight columns if they fit, else of 256
+            assert p["kernel"] == bwgemm.BW_KERNEL_SWAP and p["bn"] == M and p["kpair"] == 1 and p["wm"] == wm
             assert p["grid"] == 2 * p["tiles"] and p["splits"] == 2 and p["workspace_bytes"] == 0
-            assert p["counters"] == 0
-        elif M <= 128:
-            assert p["kernel"] == bwgemm.BW_KERNEL_SWAP and p["bn"] == M and p["dp_tiles"] == 0
+            assert p["counters"] == 0 and p["tiles"] == -(-N // (128 * wm))
+        elif M <= 128:  # stream-K; tiles of 256 weight columns from 64 tokens while they outnumber the SMs
+            wm = 2 if M >= 64 and -(-N // 256) >= 148 else 1
+            assert p["kernel"] == bwgemm.BW_KERNEL_SWAP and p["bn"] == M and p["dp_tiles"] == 0 and p["wm"] == wm
+            assert p["tiles"] == -(-N // (128 * wm)) and p["tmem_cols"] >= 2 * M * wm
             assert p["grid"] == 148 and p["sk_iters"] == p["tiles"] * (K // 64) and p["splits"] == 0
         else:
             assert p["kernel"] == bwgemm.BW_KERNEL_PAIR and p["bn"] == 256 and p["grid"] % 2 == 0
@@ -75,6 +78,8 @@ def test_plan_variants_take_out_one_mechanism():
     assert bwgemm.plan(16, 8192, 8192, variant=1)["sk_iters"] == 0          # no stream-K
     v4s = bwgemm.plan(16, 8192, 8192, variant=4)                            # stream-K, not the cluster K halves
     assert v4s["kpair"] == 0 and v4s["sk_iters"] == 64 * 128
+    v4w = bwgemm.plan(128, 57344, 8192, variant=4)                          # 128-column swap tiles
+    assert v4w["wm"] == 1 and v4w["tiles"] == 448 and bwgemm.plan(128, 57344, 8192)["wm"] == 2
     assert bwgemm.plan(16, 8192, 8192, variant=2)["kernel"] == bwgemm.BW_KERNEL_PAIR  # no swap-AB
     assert bwgemm.plan(512, 8192, 8192, variant=5)["kernel"] == bwgemm.BW_KERNEL_TILE  # no SM pair
     assert bwgemm.plan(8192, 8192, 8192, variant=3)["group_rows"] == 0      # row order
