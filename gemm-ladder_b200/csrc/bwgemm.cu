@@ -64,6 +64,21 @@ bool make_map(CUtensorMap* m, const void* base, uint64_t cols, uint64_t rows, ui
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// The MN-major operand (B, K x N row-major) as {64 columns, K rows, N / 64 column blocks}: a box of `blocks` column
+// blocks is that many 64 x 64 boxes of the 2-D map, 8 KB apart in shared memory.
+bool make_map_blocks(CUtensorMap* m, const void* base, uint64_t cols, uint64_t rows, uint32_t blocks)
+{
+    EncodeTiled enc = encoder();
+    if (!enc || cols % 64 || blocks == 0 || blocks > 256) return false;
+    const cuuint64_t dims[3] = {64, rows, cols / 64};
+    const cuuint64_t strides[2] = {cols * 2, 128};
+    const cuuint32_t box[3] = {64, 64, blocks};
+    const cuuint32_t elem[3] = {1, 1, 1};
+    return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), dims, strides, box, elem,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 struct DeviceState {
     bool init = false;
     bool supported = false;
@@ -291,6 +306,12 @@ Params make_params(const bw_plan& q, int M, int N, int K, void* C, float* work, 
 // other way round.
 bool make_maps(const bw_plan& q, const void* A, const void* B, int M, int N, int K, CUtensorMap* mx, CUtensorMap* my)
 {
+    if (BW_TMA3D) {  // the stage's 64-column blocks of B in one load
+        if (q.kernel == BW_KERNEL_TILE || q.kernel == BW_KERNEL_PAIR)
+            return make_map(mx, A, K, M, 64, 128) &&
+                   make_map_blocks(my, B, N, K, (uint32_t)(q.bn / (q.kernel == BW_KERNEL_PAIR ? 128 : 64)));
+        return make_map_blocks(mx, B, N, K, (uint32_t)(2 * q.wm)) && make_map(my, A, K, M, 64, q.bn);
+    }
     if (q.kernel == BW_KERNEL_TILE || q.kernel == BW_KERNEL_PAIR)
         return make_map(mx, A, K, M, 64, 128) && make_map(my, B, N, K, 64, 64);
     return make_map(mx, B, N, K, 64, 64) && make_map(my, A, K, M, 64, q.bn);

@@ -103,6 +103,20 @@ struct Geom {
     static_assert(kTmemCols <= 512, "tensor memory");
 };
 
+// The 3-D form for the MN-major operand (BW_TMA3D): `n64` is the first 64-column block; the map's box holds the
+// stage's blocks.
+template <bool PAIR, int HINT>
+__device__ __forceinline__ void load_blocks(void* dst, const void* tmap, int n64, int k, uint64_t* bar,
+                                            uint32_t bar_cluster, uint64_t policy)
+{
+    if (PAIR)
+        tma_load_3d_pair(dst, tmap, 0, k, n64, bar_cluster);  // (the pair form takes no cache hint here)
+    else if (HINT)
+        tma_load_3d_hint(dst, tmap, 0, k, n64, bar, policy);
+    else
+        tma_load_3d(dst, tmap, 0, k, n64, bar);
+}
+
 // The L2 policy of a hint setting (0 none, 1 evict-last, 2 evict-first).
 __device__ __forceinline__ uint64_t l2_policy(int hint) { return hint == 1 ? policy_evict_last() : policy_evict_first(); }
 
@@ -573,15 +587,25 @@ __global__ void __launch_bounds__(kThreads, 1)
                         // A: 64 K x 128 rows (this block's rows of a pair tile)
                         load_tile<PAIR, BW_HINT_A>(sx, &tmx, kb * kBK, tm * G::kTileM + rank * 128, &full[stage], barc,
                                                    pol_a);
+                        if (BW_TMA3D) {  // B: this block's BN / R columns, one load
+                            load_blocks<PAIR, BW_HINT_B>(sy, &tmy, (tn * BN + rank * (BN / R)) / 64, kb * kBK,
+                                                         &full[stage], barc, pol_b);
+                        } else {
 #pragma unroll
-                        for (int j = 0; j < BN / (64 * R); ++j)  // B: this block's BN / R columns, boxes of 64 x 64 K
-                            load_tile<PAIR, BW_HINT_B>(sy + j * 8192, &tmy, tn * BN + rank * (BN / R) + 64 * j, kb * kBK,
-                                                       &full[stage], barc, pol_b);
+                            for (int j = 0; j < BN / (64 * R); ++j)  // B: this block's BN / R columns, 64 x 64 K boxes
+                                load_tile<PAIR, BW_HINT_B>(sy + j * 8192, &tmy, tn * BN + rank * (BN / R) + 64 * j,
+                                                           kb * kBK, &full[stage], barc, pol_b);
+                        }
                     } else {
+                        if (BW_TMA3D) {  // B: 128 (x WM) columns, one load
+                            load_blocks<false, BW_SWAP_HINT_B>(sx, &tmx, tn * 2 * WM, kb * kBK, &full[stage], 0u,
+                                                               pol_sb);
+                        } else {
 #pragma unroll
-                        for (int j = 0; j < 2 * WM; ++j)  // B: 128 (x WM) columns as boxes of 64 columns x 64 K
-                            load_tile<false, BW_SWAP_HINT_B>(sx + j * 8192, &tmx, tn * 128 * WM + 64 * j, kb * kBK,
-                                                             &full[stage], 0u, pol_sb);
+                            for (int j = 0; j < 2 * WM; ++j)  // B: 128 (x WM) columns as boxes of 64 columns x 64 K
+                                load_tile<false, BW_SWAP_HINT_B>(sx + j * 8192, &tmx, tn * 128 * WM + 64 * j, kb * kBK,
+                                                                 &full[stage], 0u, pol_sb);
+                        }
                         load_tile<false, BW_HINT_A>(sy, &tmy, kb * kBK, 0, &full[stage], 0u, pol_a);  // A: 64 K x BN rows
                     }
                     ++issued;

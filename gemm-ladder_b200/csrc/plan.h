@@ -51,6 +51,10 @@
 #define BW_SWAP_WM2_MIN 64     // swap-AB tiles of 256 weight columns (two MMAs on one stage of A) from this many tokens:
                                // every 128-column tile re-reads all of A from L2 (0: never)
 #endif
+#ifndef BW_TMA3D
+#define BW_TMA3D 1             // the MN-major operand's 64-column boxes of a stage in one 3-D TMA load (0: one 2-D
+                               // load per box; measured: the swap-AB shapes 0.5-3 % faster, the pair shapes even)
+#endif
 #ifndef BW_SK_ONE_WAVE
 #define BW_SK_ONE_WAVE 1       // stream-K over every tile when they make one full wave and part of another (the
                                // split-K tail's units then double a block's work: measured qkv_m512 -12 %)
