@@ -6,8 +6,9 @@
 //   warp 1      allocates tensor memory; one thread issues tcgen05.mma into one of two accumulators and commits
 //               each stage back to the producer and each finished segment to the epilogue.
 //   warps 2-5   epilogue: tcgen05.ld of the accumulator (warp w reads TMEM lanes 32 (w % 4) .. +31), fp32 -> fp16
-//               round-to-nearest, stores to C; the accumulator is released as soon as it is read, so the next tile's
-//               MMA overlaps this tile's stores.
+//               round-to-nearest, stores to C (TILE / PAIR: whole lines after an in-warp transpose; SWAP: through a
+//               shared-memory transpose); the accumulator is released as soon as it is read, so the next tile's MMA
+//               overlaps this tile's stores.
 //
 // Three operand forms (the reference's tiles and transposed bands, hopper/step7.cuh:429-631 and :671-910):
 //   TILE  (SWAP = false, PAIR = false)  MMA 128 x BN x 16: A = a 128-row tile of A (K-major), B = a BN-column tile of
@@ -18,10 +19,13 @@
 //         256 x 256 tile is that of a 128 x 128 tile.
 //   SWAP  (SWAP = true)   for M <= 128: C^T = B^T A^T.  MMA-A = 128 columns of B (MN-major), MMA-B = the M rows of A
 //         (K-major, BN = M rounded up to 16).  TMEM lane = column of C, TMEM column = row of C.  The weights fill the
-//         128-row MMA dimension whatever the number of tokens.
+//         128-row MMA dimension whatever the number of tokens.  WM = 2: tiles of 256 weight columns, two MMAs on each
+//         stage of A, accumulator columns [w * BN, (w + 1) * BN) for weight block w.
 //
 // Work (schedule.h): data-parallel whole tiles in serpentine order, then split-K or stream-K segments; a tile split
-// over several blocks is summed by the last of them in a fixed order, so results are bit-for-bit repeatable.
+// over several blocks is summed by the last of them in a fixed order, so results are bit-for-bit repeatable.  Or
+// (kpair, SWAP) each tile's two K halves on the two blocks of a cluster, the second block's sum sent into the first
+// block's idle stage ring through distributed shared memory (st.async), added there in a fixed order.
 // Every wait on a barrier is bounded (ptx.cuh, wait_bounded): a stalled pipeline ends the kernel with an error status
 // instead of hanging the GPU.
 #pragma once

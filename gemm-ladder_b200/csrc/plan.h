@@ -3,13 +3,17 @@
 // The reference picks a kernel per class of shape (step7::choose, hopper/step7.cuh:921-949; step6::choose,
 // hopper/step6.cuh:468-488; its 128 x 320 tile where waves x area are smaller, rows7c :921-933).  On the B200:
 //   M <= 128   swap-AB (BW_KERNEL_SWAP): the weights' 128 columns per tile fill the MMA's 128 rows and the M tokens its
-//              N (rounded up to 16), so small M wastes no tensor-core rows.  The shape streams B from HBM once; its
-//              K-blocks are cut evenly over the SMs (stream-K), so every SM streams the same share whatever N / 128 is.
+//              N (rounded up to 16), so small M wastes no tensor-core rows.  The shape streams B from HBM once:
+//              - if every tile's two K halves fit the SMs at once (clusters of two), each half on one block and the
+//                two sums added through distributed shared memory (kpair), with tiles of 128 weight columns, else of
+//                256 (wm = 2, two MMAs on each stage of A) if those fit;
+//              - otherwise the K-blocks of all tiles cut evenly over the SMs (stream-K), with tiles of 256 weight
+//                columns from 64 tokens while they outnumber the SMs (A is re-read from L2 once per tile).
 //   M > 128    256 x 256 tiles on pairs of SMs (BW_KERNEL_PAIR, tcgen05 cta_group::2), persistent: per SM the
 //              operand traffic of a 128 x 128 tile for the work of a 128 x 256 one.  Whole waves of tiles go
 //              round-robin (data-parallel); the tiles of the last, partial wave are split in K into `splits` ranges
 //              (split-K) when that fills the pairs better than leaving them idle, the cost of each extra partial
-//              included.
+//              included -- or, when the tiles make one wave and a part, all of them are cut evenly (stream-K).
 // Variants take one mechanism out each, for ablations (the reference's g_var, hopper/step7.cu:1-11).
 #pragma once
 #include <cstddef>
