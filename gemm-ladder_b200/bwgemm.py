@@ -67,6 +67,8 @@ def lib():
         L.bw_gemm_f16.restype = i
         L.bw_gemm_f16_variant.argtypes = [vp, vp, vp, i, i, i, vp, i]
         L.bw_gemm_f16_variant.restype = i
+        L.bw_gemm_f16_tn.argtypes = [vp, vp, vp, i, i, i, vp]
+        L.bw_gemm_f16_tn.restype = i
         L.bw_gemm_f16_f32out.argtypes = [vp, vp, vp, i, i, i, vp]
         L.bw_gemm_f16_f32out.restype = i
         L.bw_gemm_f16_swiglu.argtypes = [vp, vp, vp, i, i, i, vp]
@@ -146,6 +148,27 @@ def gemm(A, B, C=None, variant=0, stream=None):
     s = stream if stream is not None else torch.cuda.current_stream(A.device)
     with torch.cuda.device(A.device):
         check(gemm_ptr(A.data_ptr(), B.data_ptr(), C.data_ptr(), M, N, K, s.cuda_stream, variant))
+    return C
+
+
+def gemm_tn(A, Bt, C=None, stream=None):
+    """C (fp16, M x N) = A Bt^T for fp16 CUDA tensors, Bt being N x K row-major (a linear layer's weight layout)."""
+    import torch
+
+    M, K = A.shape
+    N, K2 = Bt.shape
+    if K2 != K:
+        raise ValueError(f"A is {M} x {K} but Bt is {N} x {K2}")
+    for t in (A, Bt):
+        if t.dtype != torch.float16 or not t.is_cuda or not t.is_contiguous():
+            raise ValueError("A and Bt must be contiguous fp16 CUDA tensors")
+    if C is None:
+        C = torch.empty((M, N), dtype=torch.float16, device=A.device)
+    elif C.shape != (M, N) or C.dtype != torch.float16 or not C.is_contiguous():
+        raise ValueError("C must be a contiguous fp16 M x N tensor")
+    s = stream if stream is not None else torch.cuda.current_stream(A.device)
+    with torch.cuda.device(A.device):
+        check(lib().bw_gemm_f16_tn(A.data_ptr(), Bt.data_ptr(), C.data_ptr(), M, N, K, s.cuda_stream))
     return C
 
 

@@ -279,9 +279,10 @@ int dispatch(DeviceState& d, const bw_plan& q, const CUtensorMap& mx, const CUte
 }
 
 // The kernel parameters of a plan.
-Params make_params(const bw_plan& q, int M, int N, int K, void* C, float* work, int* counters)
+Params make_params(const bw_plan& q, int M, int N, int K, void* C, float* work, int* counters, bool tn = false)
 {
     Params p;
+    p.tn = tn ? 1 : 0;
     p.s.M = M;
     p.s.N = N;
     p.s.K = K;
@@ -304,8 +305,15 @@ Params make_params(const bw_plan& q, int M, int N, int K, void* C, float* work, 
 
 // The two tensor maps of a plan: TILE and PAIR read A (K-major) and B (MN-major) in that role order; SWAP the
 // other way round.
-bool make_maps(const bw_plan& q, const void* A, const void* B, int M, int N, int K, CUtensorMap* mx, CUtensorMap* my)
+bool make_maps(const bw_plan& q, const void* A, const void* B, int M, int N, int K, CUtensorMap* mx, CUtensorMap* my,
+               bool tn = false)
 {
+    if (tn) {  // B is N x K row-major: K-major boxes of 64 K x (the rows of B one stage takes), as A's
+        if (q.kernel == BW_KERNEL_TILE || q.kernel == BW_KERNEL_PAIR)
+            return make_map(mx, A, K, M, 64, 128) &&
+                   make_map(my, B, K, N, 64, (uint32_t)(q.kernel == BW_KERNEL_PAIR ? q.bn / 2 : q.bn));
+        return make_map(mx, B, K, N, 64, (uint32_t)(128 * q.wm)) && make_map(my, A, K, M, 64, q.bn);
+    }
     if (BW_TMA3D) {  // the stage's 64-column blocks of B in one load
         if (q.kernel == BW_KERNEL_TILE || q.kernel == BW_KERNEL_PAIR)
             return make_map(mx, A, K, M, 64, 128) &&
@@ -317,7 +325,8 @@ bool make_maps(const bw_plan& q, const void* A, const void* B, int M, int N, int
     return make_map(mx, B, N, K, 64, 64) && make_map(my, A, K, M, 64, q.bn);
 }
 
-int gemm(const void* A, const void* B, void* C, int M, int N, int K, cudaStream_t st, int variant, int epi = kEpiF16)
+int gemm(const void* A, const void* B, void* C, int M, int N, int K, cudaStream_t st, int variant, int epi = kEpiF16,
+         bool tn = false)
 {
     if (variant < 0 || variant >= kVariants) return BW_ERR_ARG;
     if (!shape_ok(M, N, K)) return BW_ERR_SHAPE;
@@ -336,11 +345,11 @@ int gemm(const void* A, const void* B, void* C, int M, int N, int K, cudaStream_
         if ((rc = ensure_workspace(*d, q, st))) return rc;
     }
     CUtensorMap mx, my;
-    if (!make_maps(q, A, B, M, N, K, &mx, &my)) {
+    if (!make_maps(q, A, B, M, N, K, &mx, &my, tn)) {
         snprintf(g_errbuf, sizeof g_errbuf, "cuTensorMapEncodeTiled failed");
         return BW_ERR_LAUNCH;
     }
-    return dispatch(*d, q, mx, my, make_params(q, M, N, K, C, d->work, d->counters), st, epi);
+    return dispatch(*d, q, mx, my, make_params(q, M, N, K, C, d->work, d->counters, tn), st, epi);
 }
 
 }  // namespace
@@ -355,6 +364,11 @@ BW_API int bw_gemm_f16(const void* A, const void* B, void* C, int M, int N, int 
 BW_API int bw_gemm_f16_variant(const void* A, const void* B, void* C, int M, int N, int K, void* stream, int variant)
 {
     return bw::gemm(A, B, C, M, N, K, static_cast<cudaStream_t>(stream), variant);
+}
+
+BW_API int bw_gemm_f16_tn(const void* A, const void* B, void* C, int M, int N, int K, void* stream)
+{
+    return bw::gemm(A, B, C, M, N, K, static_cast<cudaStream_t>(stream), 0, bw::kEpiF16, true);
 }
 
 BW_API int bw_gemm_f16_f32out(const void* A, const void* B, void* C, int M, int N, int K, void* stream)

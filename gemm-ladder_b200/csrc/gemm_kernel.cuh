@@ -55,6 +55,7 @@ struct Params {
     float* work;                 // the partials: workspace_slots() x (PAIR ? 2 : 1) slots of 128 x BN fp32, row-major
     int* counters;               // one per split tile (per block of the pair), zero between calls
     unsigned long long wait_ns;  // the limit of any single wait on a barrier
+    int tn;                      // 1: B is N x K row-major (K-major for the tensor core, like A); 0: K x N
 };
 
 __host__ __device__ constexpr int pow2_at_least(int v, int p) { return p >= v ? p : pow2_at_least(v, 2 * p); }
@@ -591,7 +592,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                         // A: 64 K x 128 rows (this block's rows of a pair tile)
                         load_tile<PAIR, BW_HINT_A>(sx, &tmx, kb * kBK, tm * G::kTileM + rank * 128, &full[stage], barc,
                                                    pol_a);
-                        if (BW_TMA3D) {  // B: this block's BN / R columns, one load
+                        if (p.tn) {  // B (N x K): this block's BN / R rows of B, 64 K each, one load
+                            load_tile<PAIR, BW_HINT_B>(sy, &tmy, kb * kBK, tn * BN + rank * (BN / R), &full[stage],
+                                                       barc, pol_b);
+                        } else if (BW_TMA3D) {  // B: this block's BN / R columns, one load
                             load_blocks<PAIR, BW_HINT_B>(sy, &tmy, (tn * BN + rank * (BN / R)) / 64, kb * kBK,
                                                          &full[stage], barc, pol_b);
                         } else {
@@ -601,7 +605,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                                                            kb * kBK, &full[stage], barc, pol_b);
                         }
                     } else {
-                        if (BW_TMA3D) {  // B: 128 (x WM) columns, one load
+                        if (p.tn) {  // B (N x K): 128 (x WM) rows of B, 64 K each, one load
+                            load_tile<false, BW_SWAP_HINT_B>(sx, &tmx, kb * kBK, tn * 128 * WM, &full[stage], 0u,
+                                                             pol_sb);
+                        } else if (BW_TMA3D) {  // B: 128 (x WM) columns, one load
                             load_blocks<false, BW_SWAP_HINT_B>(sx, &tmx, tn * 2 * WM, kb * kBK, &full[stage], 0u,
                                                                pol_sb);
                         } else {
@@ -631,7 +638,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else if (warp == 1) {
         // ---------------------------------------------------------- MMA issuer (one thread; the leader of a pair)
         if (lane == 0 && leader) {
-            constexpr uint32_t idesc = idesc_f16_f32(PAIR ? 256 : 128, BN, SWAP, !SWAP);
+            // B (the MMA's A operand in swap-AB) is MN-major when K x N, K-major when N x K (p.tn)
+            constexpr uint32_t idesc_nn = idesc_f16_f32(PAIR ? 256 : 128, BN, SWAP, !SWAP);
+            constexpr uint32_t idesc_tn = idesc_f16_f32(PAIR ? 256 : 128, BN, false, false);
+            const uint32_t idesc = p.tn ? idesc_tn : idesc_nn;
+            const bool bk = p.tn != 0;
             SegIter it(s, c, P);
             Seg sg;
             int stage = 0, acc = 0, seg = 0;
@@ -670,12 +681,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const uint32_t sx = smem_u32(smem + stage * G::kStageBytes), sy = sx + G::kXBytes;
 #pragma unroll
                     for (int k = 0; k < kBK / 16; ++k) {
-                        const uint64_t bd = SWAP ? desc_kmajor(sy, k) : desc_mnmajor(sy, k);
+                        const uint64_t bd = (SWAP || bk) ? desc_kmajor(sy, k) : desc_mnmajor(sy, k);
                         const uint32_t accumulate = (kb > sg.k0 || k > 0) ? 1u : 0u;
 #pragma unroll
                         for (int w = 0; w < WM; ++w) {  // SWAP: each 128-column weight block into its columns
-                            const uint64_t ad = SWAP ? desc_mnmajor(sx + (uint32_t)(w * 128 * kBK * 2), k)
-                                                     : desc_kmajor(sx, k);
+                            const uint32_t xw = sx + (uint32_t)(w * 128 * kBK * 2);
+                            const uint64_t ad = (SWAP && !bk) ? desc_mnmajor(xw, k) : desc_kmajor(xw, k);
                             if (PAIR)
                                 mma_f16_pair(d, ad, bd, idesc, accumulate);
                             else

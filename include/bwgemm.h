@@ -50,6 +50,13 @@ int bw_gemm_f16(const void* A, const void* B, void* C, int M, int N, int K, void
 int bw_gemm_f16_variant(const void* A, const void* B, void* C, int M, int N, int K, void* stream, int variant);
 
 /*
+ * C = A B^T-stored: the same product with B given as N x K row-major (each row of B one output column's weights, the
+ * layout of a linear layer's weight matrix; K-major, the tensor core's native operand form), A M x K and C M x N as
+ * above, the same rule and plans.  Replaces nothing in the reference: its candidates take B as K x N only.
+ */
+int bw_gemm_f16_tn(const void* A, const void* B, void* C, int M, int N, int K, void* stream);
+
+/*
  * C = A B with C written in fp32 (M x N row-major, 16-byte aligned), A and B fp16 as above: the partial sums of a
  * row-parallel layer, reduced across GPUs by a reduce-scatter before they are rounded (the tensor-parallel MLP block
  * of the B200 configs: down = H_r W2_r on each rank, then an NCCL reduce-scatter of the fp32 partials).  SM-pair tiles
