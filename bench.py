@@ -17,6 +17,11 @@ B200 shapes timed against torch.matmul (cuBLAS) in CUDA graphs, with the geometr
 
 --impl reference: the reference's CPU path (its fp64 i-k-j GEMM, restated in oracle/oracle.c; the reference's GPU
 harness needs its judge, which needs CUDA 13) timed on the host cores on the same workload, in bounded row samples.
+
+--workload tp_mlp: the tensor-parallel MLP block of gemm-ladder_b200/tp_mlp.py over the ranks
+(--tp-m tokens, 8192 or 2048; --tp-unfused for the activation as separate torch ops), total work fixed: strong
+scaling.  --shape MxNxK times any shape in place of the workload.  --profile-arm {ours,cublas}: one call of either
+arm inside an NVTX range "timed" (3 warm-up calls before it), no JSON line: the command for ncu's --nvtx-include.
 """
 import argparse
 import datetime
