@@ -7,6 +7,11 @@
 #                      repository's candidate (gemm-ladder_b200/blackwell/candidate.cu, the whole rung in one
 #                      translation unit): the reference's 26 edge shapes, its fp64 CPU reference and its 8
 #                      bit-for-bit repeats of every variant, run on the B200
+#   _ref/judge_bw      the reference's judge, judge/judge.cu compiled where it lies (force-including
+#                      oracle/judge_compat.h so that CUDA 12.9 builds it) and linked with this repository's candidate,
+#                      with its inputs: _ref/shapes_b200.txt (the judge's 17 B200 shapes, written from tests/shapes.py
+#                      in the judge's "M N K label" format) and _ref/judge_reference_b200.txt (the card's cached
+#                      cuBLASLt configurations, judge/reference/b200.txt, data read by --reference)
 #
 # Nothing here is built from a copy of the reference's sources, and nothing runs the reference's own build system.
 REF ?= /root/reference
@@ -20,6 +25,7 @@ PKG := $(ROOT)/gemm-ladder_b200
 all: $(OUT)/emu_dump $(OUT)/verif_bw
 emu_dump: $(OUT)/emu_dump
 verif_bw: $(OUT)/verif_bw
+judge_bw: $(OUT)/judge_bw $(OUT)/shapes_b200.txt $(OUT)/judge_reference_b200.txt
 
 $(OUT):
 	mkdir -p $(OUT)
@@ -32,4 +38,15 @@ $(OUT)/verif_bw: $(REF)/hopper/verif.cu $(PKG)/blackwell/candidate.cu $(wildcard
 	$(NVCC) -std=c++17 -O2 -gencode arch=compute_100a,code=sm_100a -I$(ROOT)/include \
 	    $(REF)/hopper/verif.cu $(PKG)/blackwell/candidate.cu -o $@ -lcublasLt
 
-.PHONY: all emu_dump verif_bw
+$(OUT)/judge_bw: $(REF)/judge/judge.cu $(HERE)judge_compat.h $(PKG)/blackwell/candidate.cu $(wildcard $(PKG)/csrc/*) | $(OUT)
+	$(NVCC) -std=c++17 -O3 -gencode arch=compute_100a,code=sm_100a -I$(ROOT)/include -include $(HERE)judge_compat.h \
+	    $(REF)/judge/judge.cu $(PKG)/blackwell/candidate.cu -o $@ -lcublasLt -lcublas
+
+$(OUT)/shapes_b200.txt: $(ROOT)/tests/shapes.py | $(OUT)
+	cd $(ROOT)/tests && python3 -c "from shapes import JUDGE_B200; print('# M N K label'); \
+	    [print(m, n, k, name) for name, m, n, k in JUDGE_B200]" > $@
+
+$(OUT)/judge_reference_b200.txt: $(REF)/judge/reference/b200.txt | $(OUT)
+	cp $< $@
+
+.PHONY: all emu_dump verif_bw judge_bw
