@@ -22,7 +22,7 @@ CXX ?= g++
 NVCC ?= nvcc
 PKG := $(ROOT)/gemm-ladder_b200
 
-all: $(OUT)/emu_dump $(OUT)/verif_bw
+all: $(OUT)/emu_dump $(OUT)/verif_bw judge_bw
 emu_dump: $(OUT)/emu_dump
 verif_bw: $(OUT)/verif_bw
 judge_bw: $(OUT)/judge_bw $(OUT)/shapes_b200.txt $(OUT)/judge_reference_b200.txt
