@@ -427,6 +427,17 @@ BW_API int bw_gemm_clear_status(void)
     const unsigned z[4] = {0, 0, 0, 0};
     cudaError_t e = cudaMemcpyToSymbol(bw::g_status, z, sizeof z);
     if (e != cudaSuccess) return bw::cuda_fail(e, "cudaMemcpyToSymbol (status)");
+    // a call whose wait gave up may have left split-tile counters set (its reducer never came): back to zero, so that
+    // the next call's split tiles count their partials from nothing
+    bw::DeviceState* d = nullptr;
+    if (bw::device_state(&d) == BW_OK) {
+        std::lock_guard<std::mutex> lock(bw::g_mu);
+        if (d->counters) {
+            if ((e = cudaMemset(d->counters, 0, (size_t)d->n_counters * sizeof(int))) != cudaSuccess ||
+                (e = cudaDeviceSynchronize()) != cudaSuccess)
+                return bw::cuda_fail(e, "cudaMemset (counters)");
+        }
+    }
     return BW_OK;
 }
 

@@ -490,7 +490,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     static_assert(EPI != kEpiSwiGLU || BN % 32 == 0, "SwiGLU pairs the two halves of a tile");
     constexpr int S = G::kStages;
     constexpr int R = G::kRanks;
+#ifdef BW_EMULATE
+    uint8_t* smem_raw = emu::cta_smem();  // the emulated block's shared memory
+#else
     extern __shared__ uint8_t smem_raw[];
+#endif
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + G::kBarOffset);
     uint64_t* empty = full + S;

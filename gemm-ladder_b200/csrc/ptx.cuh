@@ -9,6 +9,11 @@
 #include <cstdint>
 #include <cuda_runtime.h>
 
+#ifdef BW_EMULATE
+// The host emulator (gemm-ladder_b200/emu/): the same functions, carried out on the CPU.
+#include "../emu/ptx_emu.h"
+#else
+
 namespace bw {
 
 // ------------------------------------------------------------------ addresses and timers
@@ -350,3 +355,5 @@ __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t count)
 }
 
 }  // namespace bw
+
+#endif  // BW_EMULATE

@@ -1,0 +1,230 @@
+// emu.cpp -- the host emulator of the rung's kernel (test infrastructure): gemm_kernel.cuh, unchanged, compiled as
+// host C++ with -DBW_EMULATE over emu_runtime.h / ptx_emu.h, and a launcher that plans a call exactly as the library
+// does (plan.h), builds the same tensor maps and parameters as csrc/bwgemm.cu, and runs the plan's kernel instance on
+// the CPU, cluster after cluster.
+//
+//   g++ -std=c++20 -O2 -pthread -DBW_EMULATE -fPIC -shared -I<cuda>/include -Iinclude -Igemm-ladder_b200/csrc \
+//       gemm-ladder_b200/emu/emu.cpp -o libbwemu.so        (tests/test_emulator.py builds and drives it)
+//
+// C entry (the same arguments as the library's entries, plus the emulated GPU's SM count):
+//   bw_emu_gemm(A, B, C, M, N, K, sms, variant, epi, tn, status[4], &dirty, finding, finding_len)
+//     epi: 0 fp16 C, 1 fp32 C, 2 SwiGLU (C is M x N/2);  tn: B given as N x K.
+//     Returns a BW_* status; status = the device status word, dirty = counters left non-zero, findings = the number
+//     of emulator findings and finding = the first one's text (empty if none).
+//   bw_emu_set(name, value): the knobs below.
+#include <algorithm>
+#include <functional>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "gemm_kernel.cuh"
+
+namespace bw {
+namespace {
+
+// ------------------------------------------------------------------ the library's maps and parameters, emulated
+void map2(CUtensorMap* m, const void* base, uint64_t cols, uint64_t rows, uint32_t box_cols, uint32_t box_rows)
+{
+    const uint64_t dims[2] = {cols, rows}, strides[2] = {2, cols * 2};
+    const uint32_t box[2] = {box_cols, box_rows};
+    emu::make_map(m, base, 2, dims, strides, box);
+}
+void map_blocks(CUtensorMap* m, const void* base, uint64_t cols, uint64_t rows, uint32_t blocks)
+{
+    const uint64_t dims[3] = {64, rows, cols / 64}, strides[3] = {2, cols * 2, 128};
+    const uint32_t box[3] = {64, 64, blocks};
+    emu::make_map(m, base, 3, dims, strides, box);
+}
+// the same choices as csrc/bwgemm.cu's make_maps
+void make_maps(const bw_plan& q, const void* A, const void* B, int M, int N, int K, CUtensorMap* mx, CUtensorMap* my,
+               bool tn)
+{
+    const bool ab = q.kernel == BW_KERNEL_TILE || q.kernel == BW_KERNEL_PAIR;
+    if (tn) {
+        if (ab) {
+            map2(mx, A, K, M, 64, 128);
+            map2(my, B, K, N, 64, (uint32_t)(q.kernel == BW_KERNEL_PAIR ? q.bn / 2 : q.bn));
+        } else {
+            map2(mx, B, K, N, 64, (uint32_t)(128 * q.wm));
+            map2(my, A, K, M, 64, (uint32_t)q.bn);
+        }
+        return;
+    }
+    if (BW_TMA3D) {
+        if (ab) {
+            map2(mx, A, K, M, 64, 128);
+            map_blocks(my, B, N, K, (uint32_t)(q.bn / (q.kernel == BW_KERNEL_PAIR ? 128 : 64)));
+        } else {
+            map_blocks(mx, B, N, K, (uint32_t)(2 * q.wm));
+            map2(my, A, K, M, 64, (uint32_t)q.bn);
+        }
+        return;
+    }
+    if (ab) {
+        map2(mx, A, K, M, 64, 128);
+        map2(my, B, N, K, 64, 64);
+    } else {
+        map2(mx, B, N, K, 64, 64);
+        map2(my, A, K, M, 64, (uint32_t)q.bn);
+    }
+}
+
+Params make_params(const bw_plan& q, int M, int N, int K, void* C, float* work, int* counters, bool tn)
+{
+    Params p = {};
+    p.tn = tn ? 1 : 0;
+    p.s.M = M;
+    p.s.N = N;
+    p.s.K = K;
+    p.s.tiles_m = q.tiles_m;
+    p.s.tiles_n = q.tiles_n;
+    p.s.tiles = q.tiles;
+    p.s.kblocks = q.kblocks;
+    p.s.dp_tiles = q.dp_tiles;
+    p.s.sk_tiles = q.sk_tiles;
+    p.s.splits = q.splits;
+    p.s.sk_iters = q.sk_iters;
+    p.s.group_rows = q.group_rows;
+    p.s.kpair = q.kpair;
+    p.C = C;
+    p.work = work;
+    p.counters = counters;
+    p.wait_ns = emu::g_wait_ns;  // long by default (the emulator is slow): a wait that runs out is a protocol fault
+    return p;
+}
+
+// ------------------------------------------------------------------ a launch: clusters one after another
+template <int BN, bool SWAP, bool PAIR, int EPI, int WM>
+int launch(const bw_plan& q, const CUtensorMap& mx, const CUtensorMap& my, const Params& p)
+{
+    using G = Geom<BN, SWAP, PAIR, WM>;
+    if (q.smem_bytes != G::kSmemBytes || q.stages != G::kStages || q.tmem_cols != G::kTmemCols || q.wm != WM) {
+        emu::finding("plan and kernel geometry disagree (bn %d)", BN);
+        return BW_ERR_LAUNCH;
+    }
+    const int cs = (PAIR || (SWAP && q.kpair)) ? 2 : 1;
+    if (q.grid % cs) return BW_ERR_LAUNCH;
+    for (int c0 = 0; c0 < q.grid; c0 += cs) {
+        emu::Cluster cl;
+        cl.size = cs;
+        std::vector<std::unique_ptr<emu::Cta>> ctas;
+        for (int r = 0; r < cs; ++r) {
+            ctas.emplace_back(new emu::Cta());
+            ctas[r]->rank = r;
+            ctas[r]->cluster = cs > 1 ? &cl : nullptr;
+            cl.cta[r] = ctas[r].get();
+        }
+        std::vector<std::thread> threads;
+        threads.reserve((size_t)cs * emu::kCtaThreads);
+        for (int r = 0; r < cs; ++r)
+            for (int t = 0; t < emu::kCtaThreads; ++t)
+                threads.emplace_back([&, r, t] {
+                    emu::t_cta = ctas[r].get();
+                    emu::t_tid = t;
+                    threadIdx = dim3((unsigned)t);
+                    blockIdx = dim3((unsigned)(c0 + r));
+                    gridDim = dim3((unsigned)q.grid);
+                    blockDim = dim3((unsigned)emu::kCtaThreads);
+                    gemm_kernel<BN, SWAP, PAIR, EPI, WM>(mx, my, p);
+                });
+        for (auto& th : threads) th.join();
+    }
+    return BW_OK;
+}
+
+// the plan's kernel instance (csrc/bwgemm.cu's dispatch)
+int dispatch(const bw_plan& q, const CUtensorMap& mx, const CUtensorMap& my, const Params& p, int epi)
+{
+    if (epi == kEpiF32) {
+        if (q.kernel == BW_KERNEL_PAIR) return launch<256, false, true, kEpiF32, 1>(q, mx, my, p);
+        if (q.kernel == BW_KERNEL_TILE && q.bn == 256) return launch<256, false, false, kEpiF32, 1>(q, mx, my, p);
+        return BW_ERR_ARG;
+    }
+    if (epi == kEpiSwiGLU) {
+        if (q.sk_tiles != 0) return BW_ERR_ARG;
+        if (q.kernel == BW_KERNEL_PAIR) return launch<256, false, true, kEpiSwiGLU, 1>(q, mx, my, p);
+        if (q.kernel == BW_KERNEL_TILE && q.bn == 256) return launch<256, false, false, kEpiSwiGLU, 1>(q, mx, my, p);
+        return BW_ERR_ARG;
+    }
+    if (q.kernel == BW_KERNEL_PAIR) return launch<256, false, true, kEpiF16, 1>(q, mx, my, p);
+    if (q.kernel == BW_KERNEL_TILE) {
+        switch (q.bn) {
+        case 64: return launch<64, false, false, kEpiF16, 1>(q, mx, my, p);
+        case 128: return launch<128, false, false, kEpiF16, 1>(q, mx, my, p);
+        case 256: return launch<256, false, false, kEpiF16, 1>(q, mx, my, p);
+        default: return BW_ERR_ARG;
+        }
+    }
+    if (q.wm == 2) {
+        switch (q.bn) {
+        case 16: return launch<16, true, false, kEpiF16, 2>(q, mx, my, p);
+        case 32: return launch<32, true, false, kEpiF16, 2>(q, mx, my, p);
+        case 48: return launch<48, true, false, kEpiF16, 2>(q, mx, my, p);
+        case 64: return launch<64, true, false, kEpiF16, 2>(q, mx, my, p);
+        case 80: return launch<80, true, false, kEpiF16, 2>(q, mx, my, p);
+        case 96: return launch<96, true, false, kEpiF16, 2>(q, mx, my, p);
+        case 112: return launch<112, true, false, kEpiF16, 2>(q, mx, my, p);
+        case 128: return launch<128, true, false, kEpiF16, 2>(q, mx, my, p);
+        default: return BW_ERR_ARG;
+        }
+    }
+    switch (q.bn) {
+    case 16: return launch<16, true, false, kEpiF16, 1>(q, mx, my, p);
+    case 32: return launch<32, true, false, kEpiF16, 1>(q, mx, my, p);
+    case 48: return launch<48, true, false, kEpiF16, 1>(q, mx, my, p);
+    case 64: return launch<64, true, false, kEpiF16, 1>(q, mx, my, p);
+    case 80: return launch<80, true, false, kEpiF16, 1>(q, mx, my, p);
+    case 96: return launch<96, true, false, kEpiF16, 1>(q, mx, my, p);
+    case 112: return launch<112, true, false, kEpiF16, 1>(q, mx, my, p);
+    case 128: return launch<128, true, false, kEpiF16, 1>(q, mx, my, p);
+    default: return BW_ERR_ARG;
+    }
+}
+
+}  // namespace
+}  // namespace bw
+
+// Sets a knob of the emulator: "wait_ns" (the kernel's limit of one bounded wait), "drop_tma" (the n-th TMA / bulk
+// completion of each launch never arrives, -1 none), "barrier_limit_ms" (a thread barrier never completed: a finding
+// after this long).  Returns 0, or -1 for an unknown name.
+extern "C" __attribute__((visibility("default"))) int bw_emu_set(const char* name, long long value)
+{
+    using namespace bw::emu;
+    const std::string n = name ? name : "";
+    if (n == "wait_ns") g_wait_ns = (unsigned long long)value;
+    else if (n == "drop_tma") g_drop_tma = value;
+    else if (n == "barrier_limit_ms") g_barrier_limit_ms = value;
+    else return -1;
+    return 0;
+}
+
+// Runs one call of the rung on the emulated GPU of `sms` SMs.  status[4]: the device status word after the call;
+// *dirty: split-tile counters left non-zero; *findings: the emulator's findings (the first one's text in `finding`).
+extern "C" __attribute__((visibility("default"))) int bw_emu_gemm(const void* A, const void* B, void* C, int M, int N,
+                                                                  int K, int sms, int variant, int epi, int tn,
+                                                                  unsigned* status, int* dirty, int* findings,
+                                                                  char* finding, int finding_len)
+{
+    using namespace bw;
+    emu::g_findings = 0;
+    emu::g_first_finding[0] = 0;
+    emu::g_tma_count = 0;
+    std::memset(g_status, 0, sizeof g_status);
+    bw_plan q = {};
+    const unsigned flags = epi == kEpiF32 ? kPlanNoSwap : epi == kEpiSwiGLU ? kPlanNoSwap | kPlanNoSplit : 0u;
+    if (epi == kEpiSwiGLU && N % 256) return BW_ERR_SHAPE;
+    int rc = make_plan(M, N, K, sms, sms / 2, variant, &q, flags);
+    if (rc) return rc;
+    std::vector<float> work(q.workspace_bytes / sizeof(float) + 4, 0.f);
+    std::vector<int> counters((size_t)q.counters + 1, 0);
+    CUtensorMap mx, my;
+    make_maps(q, A, B, M, N, K, &mx, &my, tn != 0);
+    const Params p = make_params(q, M, N, K, C, work.data(), counters.data(), tn != 0);
+    rc = dispatch(q, mx, my, p, epi);
+    if (status) std::memcpy(status, g_status, sizeof g_status);
+    if (dirty) *dirty = (int)std::count_if(counters.begin(), counters.begin() + q.counters, [](int v) { return v != 0; });
+    if (findings) *findings = emu::g_findings.load();
+    if (finding && finding_len > 0) snprintf(finding, (size_t)finding_len, "%s", emu::g_first_finding);
+    return rc;
+}

@@ -1,0 +1,172 @@
+// ptx_emu.h -- the host emulator's version of csrc/ptx.cuh: the same functions, carried out on the CPU by the
+// execution model of emu_runtime.h (each block's 192 threads as host threads, a cluster's blocks side by side).
+//
+// What each instruction does here:
+//   mbarrier         a table per block (arrival count, pending arrivals, transaction bytes, completed phases);
+//                    try_wait.parity(p) is true once the phase of parity p has completed.
+//   TMA tiled load   the box is copied at once, element by element from the tensor map's global array (zeros outside
+//                    it), into shared memory in the 128-byte swizzle (16-byte chunk c of 128-byte row r at c ^ (r % 8)),
+//                    then its bytes complete on the barrier (a pair's on the leader block's barrier).
+//   tcgen05.mma      the operands are read through the shared-memory descriptors (start, leading and stride byte
+//                    offsets, 128-byte swizzle; K-major or MN-major from the instruction descriptor) and multiplied in
+//                    fp32 into the block's tensor memory (128 lanes x 512 columns); the pair form takes A's rows and
+//                    B's columns from both blocks and writes each block's rows to its own tensor memory.
+//   tcgen05.commit   an arrival on the barrier (the MMAs before it are complete here).
+//   tcgen05.ld       lane (address lane + the thread's lane in its warp), 16 consecutive columns.
+//   clusters         rank, mapa (the rank in the address's top byte), barrier.cluster, remote arrivals, st.async.
+// Every access to shared or tensor memory is bounds-checked, and the checks that fail are recorded as findings
+// (emu::finding) instead of being carried out.
+#pragma once
+#include <cuda.h>
+
+#include "emu_runtime.h"
+
+namespace bw {
+
+// ------------------------------------------------------------------ addresses and timers
+inline uint32_t smem_u32(const void* p) { return emu::offset_of(p); }
+inline uint64_t globaltimer_ns() { return emu::now_ns(); }
+inline uint32_t lane_id() { return (uint32_t)(emu::t_tid & 31); }
+
+// ------------------------------------------------------------------ mbarrier
+inline void mbar_init(uint64_t* bar, uint32_t count) { emu::mb_init(emu::t_cta, emu::offset_of(bar), (int)count); }
+inline void fence_barrier_init() {}
+inline void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes)
+{
+    emu::mb_arrive(emu::t_cta, emu::offset_of(bar), (long long)bytes);
+}
+inline void mbar_arrive(uint64_t* bar) { emu::mb_arrive(emu::t_cta, emu::offset_of(bar), 0); }
+inline bool mbar_try_wait(uint32_t bar, uint32_t parity)
+{
+    return emu::mb_try_wait(emu::cta_of(bar), emu::off_of(bar), parity);
+}
+
+inline unsigned int g_status[4];
+enum : uint32_t { kStatusTimeout = 3u };
+
+// The bounded wait of ptx.cuh, with a yield in the spin so that the other emulated threads run.
+inline bool wait_slow(uint32_t bar, uint32_t parity, volatile int* abort_flag, uint64_t limit_ns, uint32_t where, int seg)
+{
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t i = 1;; ++i) {
+        if (mbar_try_wait(bar, parity)) return true;
+        std::this_thread::yield();
+        if ((i & 31u) == 0) {
+            if (*abort_flag) return false;
+            if (globaltimer_ns() - t0 > limit_ns) {
+                *abort_flag = 1;
+                unsigned expected = 0u;
+                if (__atomic_compare_exchange_n(&g_status[0], &expected, (unsigned)kStatusTimeout, false,
+                                                __ATOMIC_SEQ_CST, __ATOMIC_SEQ_CST)) {
+                    g_status[1] = where;
+                    g_status[2] = blockIdx.x;
+                    g_status[3] = (unsigned)seg;
+                }
+                return false;
+            }
+        }
+    }
+}
+
+inline bool wait_bounded(uint64_t* barp, uint32_t parity, volatile int* abort_flag, uint64_t limit_ns, uint32_t where,
+                         int seg)
+{
+    const uint32_t bar = smem_u32(barp);
+    if (mbar_try_wait(bar, parity)) return true;
+    return wait_slow(bar, parity, abort_flag, limit_ns, where, seg);
+}
+
+// ------------------------------------------------------------------ TMA
+inline void prefetch_tmap(const void*) {}
+inline void tma_load_2d(void* dst, const void* tmap, int x, int y, uint64_t* bar)
+{
+    const long long bytes = emu::tma_copy(dst, tmap, x, y, 0);
+    if (emu::keep_completion()) emu::mb_complete_tx(emu::t_cta, emu::offset_of(bar), bytes);
+}
+inline void tma_load_2d_hint(void* dst, const void* tmap, int x, int y, uint64_t* bar, uint64_t)
+{
+    tma_load_2d(dst, tmap, x, y, bar);
+}
+inline void tma_load_3d(void* dst, const void* tmap, int x, int y, int z, uint64_t* bar)
+{
+    const long long bytes = emu::tma_copy(dst, tmap, x, y, z);
+    if (emu::keep_completion()) emu::mb_complete_tx(emu::t_cta, emu::offset_of(bar), bytes);
+}
+inline void tma_load_3d_hint(void* dst, const void* tmap, int x, int y, int z, uint64_t* bar, uint64_t)
+{
+    tma_load_3d(dst, tmap, x, y, z, bar);
+}
+inline uint64_t policy_evict_first() { return 0; }
+inline uint64_t policy_evict_last() { return 0; }
+inline void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar)
+{
+    emu::bulk_copy(dst, src, bytes);
+    if (emu::keep_completion()) emu::mb_complete_tx(emu::t_cta, emu::offset_of(bar), bytes);
+}
+
+// ------------------------------------------------------------------ clusters
+inline uint32_t cluster_ctarank() { return (uint32_t)emu::t_cta->rank; }
+inline uint32_t mapa_shared(uint32_t saddr, uint32_t rank) { return emu::mapa(saddr, rank); }
+inline void cluster_sync() { emu::cluster_sync(); }
+inline void mbar_arrive_cluster(uint32_t cluster_addr) { emu::mb_arrive(emu::cta_of(cluster_addr), emu::off_of(cluster_addr), 0); }
+inline void st_async_v4(uint32_t dst, uint32_t a, uint32_t b, uint32_t c, uint32_t d, uint32_t bar)
+{
+    const uint32_t v[4] = {a, b, c, d};
+    emu::remote_store(dst, v, 16);
+    emu::mb_complete_tx(emu::cta_of(bar), emu::off_of(bar), 16);
+}
+inline void fence_acq_rel_cluster() { std::atomic_thread_fence(std::memory_order_seq_cst); }
+inline void tma_load_2d_pair(void* dst, const void* tmap, int x, int y, uint32_t bar)
+{
+    const long long bytes = emu::tma_copy(dst, tmap, x, y, 0);
+    if (emu::keep_completion()) emu::mb_complete_tx(emu::cta_of(bar), emu::off_of(bar), bytes);
+}
+inline void tma_load_3d_pair(void* dst, const void* tmap, int x, int y, int z, uint32_t bar)
+{
+    const long long bytes = emu::tma_copy(dst, tmap, x, y, z);
+    if (emu::keep_completion()) emu::mb_complete_tx(emu::cta_of(bar), emu::off_of(bar), bytes);
+}
+inline void tma_load_2d_pair_hint(void* dst, const void* tmap, int x, int y, uint32_t bar, uint64_t)
+{
+    tma_load_2d_pair(dst, tmap, x, y, bar);
+}
+
+// ------------------------------------------------------------------ tensor memory and the tensor core
+inline void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) { emu::tmem_alloc(dst_smem, ncols); }
+inline void tmem_relinquish() {}
+inline void tmem_dealloc(uint32_t taddr, uint32_t ncols) { emu::tmem_dealloc(taddr, ncols); }
+inline void tmem_alloc_pair(uint32_t* dst_smem, uint32_t ncols) { emu::tmem_alloc(dst_smem, ncols); }
+inline void tmem_relinquish_pair() {}
+inline void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) { emu::tmem_dealloc(taddr, ncols); }
+inline void tc_fence_before() {}
+inline void tc_fence_after() {}
+inline void mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate)
+{
+    emu::mma(d_tmem, adesc, bdesc, idesc, accumulate != 0, false);
+}
+inline void mma_f16_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate)
+{
+    emu::mma(d_tmem, adesc, bdesc, idesc, accumulate != 0, true);
+}
+inline void mma_commit_pair(uint32_t bar) { emu::mb_arrive(emu::cta_of(bar), emu::off_of(bar), 0); }
+inline void mma_commit(uint64_t* bar) { emu::mb_arrive(emu::t_cta, emu::offset_of(bar), 0); }
+inline void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) { emu::tmem_ld(taddr, r); }
+inline void tmem_wait_ld() {}
+
+// ------------------------------------------------------------------ descriptors (the same encodings as ptx.cuh)
+inline uint64_t smem_desc_sw128(uint32_t saddr, uint32_t lbo, uint32_t sbo)
+{
+    return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
+           ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46) | (2ull << 61);
+}
+constexpr uint32_t idesc_f16_f32(int m, int n, bool a_mn_major, bool b_mn_major)
+{
+    return (1u << 4) | ((a_mn_major ? 1u : 0u) << 15) | ((b_mn_major ? 1u : 0u) << 16) | ((uint32_t)(n >> 3) << 17) |
+           ((uint32_t)(m >> 4) << 24);
+}
+
+// ------------------------------------------------------------------ global memory ordering, named barriers
+inline int ld_acquire_gpu(const int* p) { return __atomic_load_n(p, __ATOMIC_ACQUIRE); }
+inline void named_bar_sync(uint32_t id, uint32_t count) { emu::named_sync((int)id, (int)count); }
+
+}  // namespace bw

@@ -142,6 +142,10 @@ int bw_gemm_plan(int M, int N, int K, int sms, int variant, bw_plan* out);
  * rung's waits return instead and leave the context usable.
  */
 int bw_gemm_status(int* code, unsigned* site, unsigned* block, unsigned* segment);
+
+/* Clears the status word and puts back to zero the split-tile counters of the current device that a call whose wait
+ * gave up may have left set (call it after handling BW_ERR_TIMEOUT, with the device idle; it synchronises the
+ * device).  No reference counterpart. */
 int bw_gemm_clear_status(void);
 
 /* The limit of any single wait on a barrier, in nanoseconds (default 1 s; the BWGEMM_WAIT_NS environment variable

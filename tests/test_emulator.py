@@ -1,0 +1,134 @@
+"""The host emulator (gemm-ladder_b200/emu/): the rung's kernel source, unchanged, compiled for the CPU with the sm_100a
+instructions it uses carried out by the emulator (mbarriers, TMA with the 128-byte swizzle, tcgen05 MMA through the
+same shared-memory descriptors, tensor memory, clusters and distributed shared memory), one host thread per GPU thread.
+
+Each plan form the rule makes, on a small emulated GPU (8 to 16 SMs): the result against the fp64 oracle under the
+GPU tests' gates, the device status word clear, the split tiles' counters back at zero, and no emulator finding
+(every shared- and tensor-memory access in bounds, every mbarrier initialised before use and never over-arrived,
+every TMA box within the swizzle's rules).  Then a stall made on purpose (a TMA completion that never arrives): the
+kernel's bounded waits give up, the status word names the wait, and every thread leaves -- no deadlock in the abort
+path, which no GPU test may provoke."""
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+import pytest
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(HERE)
+PKG = os.path.join(ROOT, "gemm-ladder_b200")
+CUDA_INCLUDE = os.path.join(os.environ.get("CUDA_HOME", "/usr/local/cuda"), "include")
+
+
+@pytest.fixture(scope="module")
+def emu(tmp_path_factory):
+    if not os.path.isdir(CUDA_INCLUDE):
+        pytest.skip("no CUDA headers")
+    lib = str(tmp_path_factory.mktemp("emu") / "libbwemu.so")
+    subprocess.check_call(["g++", "-std=c++20", "-O2", "-pthread", "-DBW_EMULATE", "-fPIC", "-shared", "-w",
+                           f"-I{CUDA_INCLUDE}", f"-I{os.path.join(ROOT, 'include')}", f"-I{os.path.join(PKG, 'csrc')}",
+                           os.path.join(PKG, "emu", "emu.cpp"), "-o", lib])
+    L = ctypes.CDLL(lib)
+    vp, i = ctypes.c_void_p, ctypes.c_int
+    L.bw_emu_gemm.argtypes = [vp, vp, vp, i, i, i, i, i, i, i, ctypes.POINTER(ctypes.c_uint),
+                              ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int), ctypes.c_char_p, i]
+    L.bw_emu_gemm.restype = i
+    L.bw_emu_set.argtypes = [ctypes.c_char_p, ctypes.c_longlong]
+    L.bw_emu_set.restype = i
+    return L
+
+
+def emulate(L, A, B, M, N, K, sms, variant=0, epi=0, tn=False):
+    """One call on the emulated GPU; A, B fp16 bits (B K x N, or N x K if tn). Returns (rc, C, status, dirty, findings,
+    first finding)."""
+    Bx = np.ascontiguousarray(np.asarray(B).reshape(K, N).T) if tn else np.ascontiguousarray(B)
+    if epi == 1:
+        C = np.full((M, N), np.nan, np.float32)
+    else:
+        C = np.full((M, N // 2 if epi == 2 else N), 0xFFFF, np.uint16)  # fp16 NaN: an unwritten element shows
+    st = (ctypes.c_uint * 4)()
+    dirty, nf = ctypes.c_int(), ctypes.c_int()
+    msg = ctypes.create_string_buffer(512)
+    rc = L.bw_emu_gemm(np.ascontiguousarray(A).ctypes.data, Bx.ctypes.data, C.ctypes.data, M, N, K, sms, variant, epi,
+                       int(tn), st, ctypes.byref(dirty), ctypes.byref(nf), msg, 512)
+    return rc, C, list(st), dirty.value, nf.value, msg.value.decode()
+
+
+# (M, N, K, emulated SMs, what the rule takes there on that GPU)
+FORMS = [
+    (256, 256, 128, 8, "pair tile"),
+    (512, 1280, 512, 8, "pair tiles, several per pair (double-buffered accumulators)"),
+    (512, 1280, 4096, 8, "pair tiles with a split-K tail"),
+    (256, 1280, 256, 8, "pair tiles: stream-K over one wave and a part"),
+    (144, 320, 192, 8, "pair tile, rows and columns beyond C, odd K-blocks"),
+    (16, 256, 128, 8, "swap-AB, K halves on a cluster of two (kpair)"),
+    (96, 448, 320, 8, "swap-AB kpair, bn 96, odd K-blocks"),
+    (16, 1024, 384, 8, "swap-AB kpair with 256-column tiles"),
+    (16, 1280, 256, 8, "swap-AB stream-K"),
+    (64, 2304, 256, 8, "swap-AB stream-K with 256-column tiles"),
+    (128, 2112, 128, 8, "swap-AB stream-K, bn 128, 256-column tiles, the last one ragged"),
+    (128, 2176, 128, 16, "swap-AB stream-K, bn 128, 128-column tiles, ragged N"),
+]
+
+
+@pytest.mark.parametrize("form", FORMS, ids=lambda f: f"{f[0]}x{f[1]}x{f[2]}")
+@pytest.mark.parametrize("tn", [False, True], ids=["KxN", "NxK"])
+def test_every_plan_form_on_the_emulator(emu, oracle_mod, form, tn):
+    M, N, K, sms, _ = form
+    A, B = oracle_mod.lcg_inputs(M, N, K)
+    rc, C, status, dirty, nf, msg = emulate(emu, A, B, M, N, K, sms, tn=tn)
+    assert rc == 0 and nf == 0, f"rc {rc}, {nf} findings, first: {msg}"
+    assert status[0] == 0 and dirty == 0, (status, dirty)
+    r = oracle_mod.check(C, oracle_mod.gemm_f64(A, B), K)
+    assert r["nonfinite"] == 0 and r["violations"] == 0 and r["normwise"] <= 2e-3, r
+
+
+@pytest.mark.parametrize("variant", range(1, 8))
+def test_every_variant_on_the_emulator(emu, oracle_mod, variant):
+    for M, N, K in ((256, 512, 256), (16, 512, 256)):
+        A, B = oracle_mod.lcg_inputs(M, N, K)
+        rc, C, status, dirty, nf, msg = emulate(emu, A, B, M, N, K, 8, variant=variant)
+        assert rc == 0 and nf == 0 and status[0] == 0 and dirty == 0, (rc, nf, msg, status, dirty)
+        r = oracle_mod.check(C, oracle_mod.gemm_f64(A, B), K)
+        assert r["nonfinite"] == 0 and r["violations"] == 0, (M, N, K, r)
+
+
+def test_fp32_and_swiglu_outputs_on_the_emulator(emu, oracle_mod):
+    M, N, K = 512, 1024, 256
+    A, B = oracle_mod.lcg_inputs(M, N, K)
+    ref = oracle_mod.gemm_f64(A, B)
+    rc, C, status, dirty, nf, msg = emulate(emu, A, B, M, N, K, 8, epi=1)
+    assert rc == 0 and nf == 0 and status[0] == 0, (rc, nf, msg, status)
+    assert np.abs(C - ref).max() <= 1e-5 * np.abs(ref).max()  # fp32 sums of the same products
+    rc, C, status, dirty, nf, msg = emulate(emu, A, B, M, N, K, 8, epi=2)
+    assert rc == 0 and nf == 0 and status[0] == 0, (rc, nf, msg, status)
+    g = ref.reshape(M, -1, 2, 128)
+    gate, up = g[:, :, 0, :].reshape(M, -1), g[:, :, 1, :].reshape(M, -1)
+    act = gate / (1.0 + np.exp(-gate)) * up
+    got = C.view(np.float16).astype(np.float64)
+    assert np.isfinite(got).all() and np.abs(got - act).max() <= 2e-3 * np.abs(act).max()
+
+
+@pytest.mark.parametrize("shape", [(256, 512, 256), (16, 256, 128), (16, 1280, 256), (512, 1280, 4096)],
+                         ids=lambda s: "x".join(map(str, s)))
+@pytest.mark.parametrize("drop", [0, 3])
+def test_a_stalled_pipeline_ends_with_a_status_not_a_hang(emu, shape, drop):
+    """The drop-th TMA completion never arrives: a bounded wait gives up after its limit, the status word holds
+    BW_ERR_TIMEOUT and the site of the wait (the MMA issuer's wait for a full stage, or the epilogue's for the
+    accumulator), and every thread of every block leaves: no thread barrier is left waiting."""
+    M, N, K = shape
+    A = np.full((M, K), 0x3C00, np.uint16)  # 1.0
+    B = np.full((K, N), 0x3C00, np.uint16)
+    emu.bw_emu_set(b"wait_ns", 300_000_000)
+    emu.bw_emu_set(b"barrier_limit_ms", 30_000)
+    emu.bw_emu_set(b"drop_tma", drop)
+    try:
+        rc, C, status, dirty, nf, msg = emulate(emu, A, B, M, N, K, 8)
+    finally:
+        emu.bw_emu_set(b"drop_tma", -1)
+        emu.bw_emu_set(b"wait_ns", 60_000_000_000)
+        emu.bw_emu_set(b"barrier_limit_ms", 120_000)
+    assert rc == 0 and nf == 0, f"{nf} findings, first: {msg}"
+    role, kind = status[1] >> 16, (status[1] >> 8) & 0xFF
+    assert status[0] == 3 and (role, kind) in ((1, 0), (2, 2), (0, 1)), status
