@@ -38,7 +38,7 @@ class Plan(ctypes.Structure):
         ("counters", ctypes.c_int),
         ("smem_bytes", ctypes.c_int),
         ("tmem_cols", ctypes.c_int),
-        ("kpair", ctypes.c_int),
+        ("ksplit", ctypes.c_int),
         ("wm", ctypes.c_int),
     ]
 

@@ -89,6 +89,7 @@ struct DeviceState {
     int n_counters = 0;
     unsigned attrs = 0;  // kernels whose shared-memory limit is set, one bit each
     int pairs = -1;      // pairs of SMs the pair kernel holds at once (its cluster occupancy); -1: not asked yet
+    int held[9] = {};    // BW_KSPLIT 1: clusters of c swap-AB blocks held at once, c = 2 .. 8 (asked with pairs)
 };
 constexpr int kMaxDevices = 64;
 DeviceState g_dev[kMaxDevices];
@@ -157,18 +158,19 @@ int ensure_workspace(DeviceState& d, const bw_plan& q, cudaStream_t st)
     return BW_OK;
 }
 
-// Clusters of two blocks for the SM pair (PAIR) and for a swap-AB plan's K halves (kpair).
+// Clusters of two blocks for the SM pair (PAIR), of `ksplit` blocks for a swap-AB plan's K split.
 template <int BN, bool SWAP, bool PAIR, int WM = 1>
-cudaLaunchConfig_t launch_config(int grid, cudaStream_t st, cudaLaunchAttribute* attr, bool kpair = false)
+cudaLaunchConfig_t launch_config(int grid, cudaStream_t st, cudaLaunchAttribute* attr, int ksplit = 0)
 {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(kThreads);
     cfg.dynamicSmemBytes = Geom<BN, SWAP, PAIR, WM>::kSmemBytes;
     cfg.stream = st;
-    const bool cluster = PAIR || (SWAP && kpair);
+    const int size = PAIR ? 2 : (SWAP && ksplit > 1) ? ksplit : 1;
+    const bool cluster = size > 1;
     attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = cluster ? 2 : 1;
+    attr[0].val.clusterDim.x = (unsigned)size;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
@@ -201,25 +203,40 @@ int pair_occupancy(DeviceState& d)
     int n = 0;
     cudaError_t e = cudaOccupancyMaxActiveClusters(&n, gemm_kernel<256, false, true>, &cfg);
     if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveClusters");
+#if BW_KSPLIT
+    // clusters of 2 .. 8 swap-AB blocks (one block per SM, as every instance's shared memory makes it)
+    if ((rc = set_smem_limit<16, true, false>(d, 1u << 1))) return rc;
+    for (int c = 2; c <= 8; ++c) {
+        const cudaLaunchConfig_t cc = launch_config<16, true, false>(c, 0, attr, c);
+        int h = 0;
+        if ((e = cudaOccupancyMaxActiveClusters(&h, gemm_kernel<16, true, false>, &cc)) != cudaSuccess)
+            return cuda_fail(e, "cudaOccupancyMaxActiveClusters (K split)");
+        d.held[c] = h;
+    }
+#endif
     d.pairs = n;
     return BW_OK;
 }
+
+// The clusters of each size the device holds at once, for the K-split rule (BW_KSPLIT 1; null: the rule's default).
+const int* held_of(const DeviceState& d) { return BW_KSPLIT ? d.held : nullptr; }
 
 template <int BN, bool SWAP, bool PAIR, int EPI = kEpiF16, int WM = 1>
 int launch_kernel(DeviceState& d, unsigned bit, const bw_plan& q, const CUtensorMap& mx, const CUtensorMap& my,
                   const Params& p, cudaStream_t st)
 {
     using G = Geom<BN, SWAP, PAIR, WM>;
-    // kpair: the second block's sum (128 x kAccN fp32) lands in the first block's idle stage ring
+    // K split: what a block receives from the others of its cluster lands in its idle stage ring
     if (q.smem_bytes != G::kSmemBytes || q.stages != G::kStages || q.tmem_cols != G::kTmemCols || q.wm != WM ||
-        (q.kpair && (!SWAP || q.grid % 2 || q.grid != 2 * q.tiles || 128 * G::kAccN * 4 > G::kBarOffset))) {
+        (q.ksplit && (!SWAP || q.ksplit < 2 || q.ksplit > 8 || q.grid != q.ksplit * q.tiles ||
+                      plan_ksplit_recv_bytes(BN, WM, q.ksplit) > G::kBarOffset))) {
         snprintf(g_errbuf, sizeof g_errbuf, "plan and kernel geometry disagree (bn %d)", BN);
         return BW_ERR_LAUNCH;
     }
     int rc = set_smem_limit<BN, SWAP, PAIR, EPI, WM>(d, bit);
     if (rc) return rc;
     cudaLaunchAttribute attr[1];
-    const cudaLaunchConfig_t cfg = launch_config<BN, SWAP, PAIR, WM>(q.grid, st, attr, q.kpair != 0);
+    const cudaLaunchConfig_t cfg = launch_config<BN, SWAP, PAIR, WM>(q.grid, st, attr, q.ksplit);
     cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_kernel<BN, SWAP, PAIR, EPI, WM>, mx, my, p);
     if (e != cudaSuccess) return cuda_fail(e, "kernel launch");
     return BW_OK;
@@ -295,7 +312,7 @@ Params make_params(const bw_plan& q, int M, int N, int K, void* C, float* work, 
     p.s.splits = q.splits;
     p.s.sk_iters = q.sk_iters;
     p.s.group_rows = q.group_rows;
-    p.s.kpair = q.kpair;
+    p.s.ksplit = q.ksplit;
     p.C = C;
     p.work = work;
     p.counters = counters;
@@ -341,7 +358,7 @@ int gemm(const void* A, const void* B, void* C, int M, int N, int K, cudaStream_
         std::lock_guard<std::mutex> lock(g_mu);
         if ((rc = pair_occupancy(*d))) return rc;
         const unsigned flags = epi == kEpiF32 ? kPlanNoSwap : epi == kEpiSwiGLU ? kPlanNoSwap | kPlanNoSplit : 0u;
-        if ((rc = make_plan(M, N, K, d->sms, d->pairs, variant, &q, flags))) return rc;
+        if ((rc = make_plan(M, N, K, d->sms, d->pairs, variant, &q, flags, held_of(*d)))) return rc;
         if ((rc = ensure_workspace(*d, q, st))) return rc;
     }
     CUtensorMap mx, my;
@@ -537,9 +554,9 @@ int noalloc_gemm(const void* A, const void* B, void* C, int M, int N, int K, cud
         auto fits = [&] {
             return q.workspace_bytes <= BW_NOALLOC_SCRATCH_BYTES && (unsigned)q.counters <= BW_NOALLOC_COUNTERS;
         };
-        if ((rc = make_plan(M, N, K, d->sms, d->pairs, 0, &q))) return rc;
+        if ((rc = make_plan(M, N, K, d->sms, d->pairs, 0, &q, 0u, held_of(*d)))) return rc;
         // the 256-column swap tiles' partials are twice as large: 128-column tiles if those fit the array
-        if (!fits() && q.wm > 1 && (rc = make_plan(M, N, K, d->sms, d->pairs, 0, &q, kPlanNarrow))) return rc;
+        if (!fits() && q.wm > 1 && (rc = make_plan(M, N, K, d->sms, d->pairs, 0, &q, kPlanNarrow, held_of(*d)))) return rc;
         if (!fits()) {
             snprintf(g_errbuf, sizeof g_errbuf,
                      "%d x %d x %d needs %zu bytes of partials and %d counters; the fixed array holds %u and %u", M, N,

@@ -24,8 +24,10 @@
 //
 // Work (schedule.h): data-parallel whole tiles in serpentine order, then split-K or stream-K segments; a tile split
 // over several blocks is summed by the last of them in a fixed order, so results are bit-for-bit repeatable.  Or
-// (kpair, SWAP) each tile's two K halves on the two blocks of a cluster, the second block's sum sent into the first
-// block's idle stage ring through distributed shared memory (st.async), added there in a fixed order.
+// (ksplit, SWAP) each tile's K ranges on the blocks of a cluster, their sums exchanged through distributed shared
+// memory (st.async into idle stage rings) and added in a fixed order: BW_KSPLIT 0, halves on clusters of two, the
+// second block's sum added by the first; BW_KSPLIT 1, clusters of 2 to 8, each block summing its own run of the
+// accumulator's 16-column chunks.
 // Every wait on a barrier is bounded (ptx.cuh, wait_bounded): a stalled pipeline ends the kernel with an error status
 // instead of hanging the GPU.
 #pragma once
@@ -91,7 +93,7 @@ struct Geom {
     static constexpr int kTmemCols = pow2_at_least(2 * kAccN < 32 ? 32 : 2 * kAccN, 32);  // two accumulators
     static constexpr int kBarOffset = kStages * kStageBytes;
     static constexpr int kNumBars = 2 * kStages + 8;  // full, empty, tmem full x2, tmem empty x2, drain, reduce,
-                                                      // and the K halves' go / receive (kpair)
+                                                      // and the K split's go / receive
     static constexpr int kSlotBytes = 128 * kAccN * 4;  // one partial of this block's rows
     static constexpr int kRingSlots = kBarOffset / kSlotBytes;  // partials the idle ring holds at once
     static constexpr int kMaxSum = kRingSlots + 1 < 8 ? kRingSlots + 1 : 8;  // partials the bulk reduction sums
@@ -502,13 +504,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* tempty = tfull + 2;
     uint64_t* drain = tempty + 2;
     uint64_t* rbar = drain + 1;  // the bulk reduction's copies of partials
-    uint64_t* kgo = rbar + 1;    // kpair, second block: the first block's ring may take this block's sum
-    uint64_t* krecv = rbar + 2;  // kpair, first block: the second block's sum has arrived
+    uint64_t* kgo = rbar + 1;    // K split: the other blocks' rings may take this block's sums
+    uint64_t* krecv = rbar + 2;  // K split: the other blocks' sums for this block have arrived
     __half* cst = reinterpret_cast<__half*>(smem + G::kCStageOffset);  // swap-AB epilogue transpose buffers
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + G::kMiscOffset);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
     volatile int* reduce_flag = abort_flag + 1;
     volatile int* epi_go = abort_flag + 2;  // two slots, alternating by segment
+    volatile int* recv_flag = abort_flag + 4;  // K split: the other blocks' parts arrived
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
@@ -518,8 +521,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const Sched& s = p.s;
     const int rank = PAIR ? (int)cluster_ctarank() : 0;
     const bool leader = rank == 0;
-    const bool kp = SWAP && s.kpair;                   // swap-AB K halves on the two blocks of a cluster
-    const int khalf = kp ? (int)cluster_ctarank() : 0;  // 0: the block that writes C
+    const bool kp = SWAP && s.ksplit;                // swap-AB K ranges on the blocks of a cluster
+    const int kr = kp ? (int)cluster_ctarank() : 0;  // this block's K range (0: the first)
     const int P = gridDim.x / R, c = blockIdx.x / R;  // the two blocks of a pair share their segments
 
     if (threadIdx.x == 0) {
@@ -533,11 +536,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         mbar_init(drain, 1);
         mbar_init(rbar, 1);
-        mbar_init(kgo, 1);    // the first block's remote arrival
-        mbar_init(krecv, 1);  // the first block's arrive.expect_tx; the second block's st.async bytes complete it
+        mbar_init(kgo, kp ? s.ksplit - 1 : 1);  // a remote arrival from each other block of the cluster
+        mbar_init(krecv, 1);  // this block's arrive.expect_tx; the other blocks' st.async bytes complete it
         *abort_flag = 0;
         *reduce_flag = 0;
         epi_go[0] = epi_go[1] = 0;
+        *recv_flag = 0;
         fence_barrier_init();
     }
     if (warp == 0 && lane == 0) {
@@ -806,12 +810,101 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 release_acc(acc);
             } else if (kp) {
+#if BW_KSPLIT
+                // a tile's K ranges on the kc blocks of this cluster (their only segment, so every block's stage ring
+                // is idle once its accumulator is complete).  The accumulator's 16-column chunks are dealt out in
+                // runs, block o owning [ksplit_run(o), ksplit_run(o + 1)).  Each block sends every chunk it does not
+                // own into the owner's idle ring (16 bytes per st.async, counted on the owner's krecv barrier), as
+                // piece (source block, chunk of the run) of 8 KB laid out [col / 4][row][4]; then sums the kc partials
+                // of its own chunks in block order (its own from tensor memory) and writes them to C.  A block sends
+                // once every other block has arrived on its kgo barrier (their rings are idle and they expect the
+                // bytes).  One thread waits (bounded) and hands each outcome to the other 127.
+                constexpr int kChunks = AN / 16;
+                const int kc = s.ksplit;
+                const int own0 = ksplit_run(kr, kChunks, kc), own1 = ksplit_run(kr + 1, kChunks, kc);
+                const uint32_t recv_bytes = (uint32_t)((kc - 1) * (own1 - own0)) * 8192u;
+                if (threadIdx.x == kEpiThread0) {
+                    if (recv_bytes) mbar_arrive_expect_tx(krecv, recv_bytes);
+                    for (int o = 0; o < kc; ++o)
+                        if (o != kr) mbar_arrive_cluster(mapa_shared(smem_u32(kgo), (uint32_t)o));
+                    const bool ok = wait_bounded(kgo, 0, abort_flag, p.wait_ns, site(2, 6, 0), seg);
+                    if (ok) fence_acq_rel_cluster();  // after the others' arrivals (release, cluster scope)
+                    *reduce_flag = ok ? 1 : 0;
+                }
+                named_bar_sync(1, 128);
+                const bool go = *reduce_flag != 0;
+                if (go) {
+#pragma unroll 1
+                    for (int ch = 0; ch < kChunks; ++ch) {
+                        if (ch >= own0 && ch < own1) continue;
+                        const int o = ksplit_owner(ch, kChunks, kc);
+                        const int r0 = ksplit_run(o, kChunks, kc), len = ksplit_run(o + 1, kChunks, kc) - r0;
+                        const int piece = (kr < o ? kr : kr - 1) * len + (ch - r0);
+                        const uint32_t dst = mapa_shared(smem_u32(smem), (uint32_t)o) + (uint32_t)piece * 8192u +
+                                             (uint32_t)row * 16u;
+                        const uint32_t bar = mapa_shared(smem_u32(krecv), (uint32_t)o);
+                        uint32_t r[16];
+                        tmem_ld16(tbase + (uint32_t)(ch * 16), r);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int j = 0; j < 4; ++j)
+                            st_async_v4(dst + (uint32_t)(j * 128 * 16), r[4 * j], r[4 * j + 1], r[4 * j + 2],
+                                        r[4 * j + 3], bar);
+                    }
+                }
+                bool have = go;
+                if (recv_bytes) {
+                    // the others' parts of this block's chunks (after a failure, bytes still on their way land first)
+                    if (threadIdx.x == kEpiThread0) {
+                        const bool ok = go && wait_bounded(krecv, 0, abort_flag, p.wait_ns, site(2, 5, 0), seg);
+                        if (!ok) wait_drain(krecv, 0, p.wait_ns);
+                        *recv_flag = ok ? 1 : 0;
+                    }
+                    named_bar_sync(1, 128);
+                    have = *recv_flag != 0;
+                    if (have) mbar_try_wait(smem_u32(krecv), 0);  // complete: each thread acquires the bytes
+                }
+                if (have) {
+                    const float4* ring = reinterpret_cast<const float4*>(smem) + row;  // [piece][col / 4][row][4]
+#pragma unroll 1
+                    for (int ch = own0; ch < own1; ++ch) {
+                        float v[16];
+#pragma unroll 1
+                        for (int sb = 0; sb < kc; ++sb) {
+                            float x[16];
+                            if (sb == kr) {
+                                uint32_t r[16];
+                                tmem_ld16(tbase + (uint32_t)(ch * 16), r);
+                                tmem_wait_ld();
+#pragma unroll
+                                for (int e = 0; e < 16; ++e) x[e] = __uint_as_float(r[e]);
+                            } else {
+                                const float4* src = ring + (size_t)((sb < kr ? sb : sb - 1) * (own1 - own0) +
+                                                                    (ch - own0)) * 512;
+#pragma unroll
+                                for (int j = 0; j < 4; ++j) {
+                                    const float4 w = src[j * 128];
+                                    x[4 * j] = w.x;
+                                    x[4 * j + 1] = w.y;
+                                    x[4 * j + 2] = w.z;
+                                    x[4 * j + 3] = w.w;
+                                }
+                            }
+#pragma unroll
+                            for (int e = 0; e < 16; ++e) v[e] = sb == 0 ? x[e] : v[e] + x[e];
+                        }
+                        store_chunk<SWAP, EPI, BN>(p, m0, n0, row, ch * 16, v, cst);
+                    }
+                }
+                release_acc(acc);
+                named_bar_sync(1, 128);  // the flags are read by all before the block goes on
+#else
                 // a tile's K halves on the two blocks of this cluster (their only segment, so the first block's stage
                 // ring is idle once its accumulator is complete): the second block sends its sum into that ring, 16
                 // bytes per st.async, counted on the first block's krecv barrier; the first adds it to its own sum in
                 // a fixed order and writes C.  One thread waits (bounded) and hands the outcome to the other 127.
                 const float4* peer = reinterpret_cast<const float4*>(smem) + row;  // [col / 4][row][4]
-                if (khalf == 0) {
+                if (kr == 0) {
                     if (threadIdx.x == kEpiThread0) {
                         mbar_arrive_expect_tx(krecv, 128u * AN * 4u);
                         mbar_arrive_cluster(mapa_shared(smem_u32(kgo), 1));  // the ring may take the other sum now
@@ -863,6 +956,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 release_acc(acc);
                 named_bar_sync(1, 128);  // reduce_flag is read by all before the next segment writes it
+#endif
             } else if (sg.k0 == 0 && sg.k1 == s.kblocks) {
                 // a whole tile: straight to C, kLdw columns per wait on the tensor-memory loads
                 constexpr int kLdw = AN % BW_EPI_LDW == 0 ? BW_EPI_LDW : 16;

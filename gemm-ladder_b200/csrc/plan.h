@@ -5,8 +5,9 @@
 //   M <= 128   swap-AB (BW_KERNEL_SWAP): the weights' 128 columns per tile fill the MMA's 128 rows and the M tokens its
 //              N (rounded up to 16), so small M wastes no tensor-core rows.  The shape streams B from HBM once:
 //              - if every tile's two K halves fit the SMs at once (clusters of two), each half on one block and the
-//                two sums added through distributed shared memory (kpair), with tiles of 128 weight columns, else of
-//                256 (wm = 2, two MMAs on each stage of A) if those fit;
+//                two sums added through distributed shared memory (ksplit = 2), with tiles of 128 weight columns,
+//                else of 256 (wm = 2, two MMAs on each stage of A) if those fit (BW_KSPLIT 1: K cut over clusters
+//                of 2 to 8 blocks, the cluster size and tile width that stream on the most SMs);
 //              - otherwise the K-blocks of all tiles cut evenly over the SMs (stream-K), with tiles of 256 weight
 //                columns from 64 tokens while they outnumber the SMs (A is re-read from L2 once per tile).
 //   M > 128    256 x 256 tiles on pairs of SMs (BW_KERNEL_PAIR, tcgen05 cta_group::2), persistent: per SM the
@@ -59,6 +60,15 @@
 #define BW_TMA3D 1             // the MN-major operand's 64-column boxes of a stage in one 3-D TMA load (0: one 2-D
                                // load per box; measured: the swap-AB shapes 0.5-3 % faster, the pair shapes even)
 #endif
+#ifndef BW_KSPLIT
+#define BW_KSPLIT 0            // swap-AB K cut over the blocks of a cluster: 0, halves on clusters of two, the second
+                               // block's sum added by the first (measured on the B200); 1, clusters of 2 to
+                               // BW_KSPLIT_MAX blocks, each summing the cluster's partials of its own run of the
+                               // accumulator's 16-column chunks (run on the host emulator; not yet measured)
+#endif
+#ifndef BW_KSPLIT_MAX
+#define BW_KSPLIT_MAX 8        // BW_KSPLIT 1: the largest cluster (8, the portable limit)
+#endif
 #ifndef BW_SK_ONE_WAVE
 #define BW_SK_ONE_WAVE 1       // stream-K over every tile when they make one full wave and part of another (the
                                // split-K tail's units then double a block's work: measured qkv_m512 -12 %)
@@ -105,6 +115,20 @@ inline int plan_smem_bytes(int bn, int ranks, bool swap, int wm = 1)
     return 1024 + cstage + plan_cstage_bytes(swap);
 }
 
+// A K-split cluster of c blocks (swap-AB): the bytes one block receives into its idle stage ring.  BW_KSPLIT 0: the
+// second block's whole accumulator (128 x bn x wm fp32) at the first.  BW_KSPLIT 1: the other c - 1 blocks' parts
+// of the longest run of 16-column chunks (8 KB each) that one block owns (runs of floor or ceil(chunks / c)).
+inline int plan_ksplit_recv_bytes(int bn, int wm, int c)
+{
+    if (!BW_KSPLIT) return 128 * bn * wm * 4;
+    const int chunks = bn * wm / 16;
+    return (c - 1) * ((chunks + c - 1) / c) * 8192;
+}
+inline bool plan_ksplit_fits(int bn, int wm, int c)
+{
+    return plan_ksplit_recv_bytes(bn, wm, c) <= plan_stages(bn, 1, true, wm) * plan_stage_bytes(bn, 1, wm);
+}
+
 inline bool shape_ok(int M, int N, int K)
 {
     return M > 0 && N > 0 && K > 0 && M % 16 == 0 && N % 64 == 0 && K % 64 == 0;
@@ -134,8 +158,10 @@ enum : unsigned {
     kPlanNarrow = 4u,   // swap-AB tiles of 128 weight columns only (half the partials' scratch)
 };
 
-// sms: the SMs; pairs: the pairs of SMs the pair kernel can hold at once (its cluster occupancy).
-inline int make_plan(int M, int N, int K, int sms, int pairs, int variant, bw_plan* p, unsigned flags = 0)
+// sms: the SMs; pairs: the pairs of SMs the pair kernel can hold at once (its cluster occupancy); held (BW_KSPLIT 1,
+// may be null): held[c], c = 2 .. 8, the clusters of c swap-AB blocks the device holds at once (null: sms / c).
+inline int make_plan(int M, int N, int K, int sms, int pairs, int variant, bw_plan* p, unsigned flags = 0,
+                     const int* held = nullptr)
 {
     if (!p || variant < 0 || variant >= kVariants || sms <= 0) return BW_ERR_ARG;
     if (!shape_ok(M, N, K)) return BW_ERR_SHAPE;
@@ -164,23 +190,45 @@ inline int make_plan(int M, int N, int K, int sms, int pairs, int variant, bw_pl
     const long long kb = q.kblocks;
     const bool one_wave = BW_SK_ONE_WAVE && !swap && q.tiles > units && q.tiles < 2 * units;
     const bool stream_k = swap ? variant != 1 : variant == 4 || (variant == 0 && one_wave);
-    // swap-AB with every tile's two K halves at once on the SMs: clusters of two blocks, one half each, the second
-    // block's sum sent to the first through distributed shared memory (no partials in memory, no counters).  Tiles of
-    // 128 weight columns if they all fit at once, else of 256 (two MMAs on each stage of A) if those do.
-    const int clusters = pairs > 0 ? pairs : sms / 2;  // clusters of two blocks held at once
+    // swap-AB with every tile at once on clusters of blocks, each block one equal K range of its tile, the blocks'
+    // sums added through distributed shared memory (no partials in memory, no counters).  BW_KSPLIT 0: clusters of
+    // two, tiles of 128 weight columns if they all fit at once, else of 256 (two MMAs on each stage of A) if those do.
+    // BW_KSPLIT 1: clusters of c = 2 .. BW_KSPLIT_MAX, the (c, tile width) that streams on the most SMs, ties to the
+    // smaller c (fewer partials), then to the narrower tile; c > 2 wants 4 K-blocks per block at least.
     const bool wide_ok = (variant == 0 || variant == 3) && !(flags & kPlanNarrow);
     const int tiles256 = (N + 255) / 256;
-    const bool kpair_ok = swap && variant != 1 && variant != 4 && q.kblocks >= 2;
-    const int kpair_wm = !kpair_ok ? 0 : q.tiles <= clusters ? 1 : (wide_ok && tiles256 <= clusters) ? 2 : 0;
-    if (kpair_wm) {
-        q.kpair = 1;
-        q.wm = kpair_wm;
+    int ks = 0, ks_wm = 0;
+    if (swap && variant != 1 && variant != 4 && q.kblocks >= 2) {
+#if BW_KSPLIT
+        int best = 0;
+        for (int wm = 1; wm <= (wide_ok ? 2 : 1); ++wm) {
+            const int tiles = (N + 128 * wm - 1) / (128 * wm);
+            for (int c = 2; c <= BW_KSPLIT_MAX && c <= 8; ++c) {
+                const int at_once = held ? held[c] : (c == 2 && pairs > 0) ? pairs : sms / c;
+                if (tiles > at_once || (c > 2 && q.kblocks < 4 * c) || !plan_ksplit_fits(q.bn, wm, c)) continue;
+                if (tiles * c > best) {
+                    best = tiles * c;
+                    ks = c;
+                    ks_wm = wm;
+                }
+            }
+        }
+#else
+        (void)held;
+        const int clusters = pairs > 0 ? pairs : sms / 2;  // clusters of two blocks held at once
+        ks_wm = q.tiles <= clusters ? 1 : (wide_ok && tiles256 <= clusters) ? 2 : 0;
+        ks = ks_wm ? 2 : 0;
+#endif
+    }
+    if (ks) {
+        q.ksplit = ks;
+        q.wm = ks_wm;
         q.tiles_n = (N + 128 * q.wm - 1) / (128 * q.wm);
         q.tiles = q.tiles_n;
         q.dp_tiles = 0;
         q.sk_tiles = q.tiles;
-        q.splits = 2;
-        q.grid = 2 * q.tiles;
+        q.splits = ks;
+        q.grid = ks * q.tiles;
         q.stages = plan_stages(q.bn, 1, true, q.wm);
         q.smem_bytes = plan_smem_bytes(q.bn, 1, true, q.wm);
         q.tmem_cols = plan_tmem_cols(q.bn * q.wm);

@@ -16,9 +16,9 @@
 // A tile computed by several blocks: each writes its fp32 partial to a workspace slot; the last to finish (a counter
 // per tile) sums the partials in a fixed order (split order, or block order) -- so the result is the same bits
 // whichever block finishes last -- and writes C.
-// Or (kpair, swap-AB only, every tile at once): block 2 t + r of the grid's clusters of two takes K half r of tile t,
-// its only segment; the second block of the cluster sends its sum to the first through distributed shared memory, no
-// workspace involved.
+// Or (ksplit = c > 0, swap-AB only, every tile at once): block c t + r of the grid's clusters of c blocks takes K
+// range r of tile t (of c equal ranges), its only segment; the blocks of the cluster add their sums through
+// distributed shared memory, no workspace involved.
 #pragma once
 #if defined(__CUDACC__)
 #define BW_HD __host__ __device__
@@ -38,7 +38,8 @@ struct Sched {
     int splits;           // > 0: split-K into this many K ranges; 0: stream-K
     long long sk_iters;   // stream-K: sk_tiles * kblocks, split evenly over the blocks
     int group_rows;       // serpentine group height in rows of tiles; 0: row after row
-    int kpair;            // 1: each tile's K halves on the two blocks of a cluster (one segment per block)
+    int ksplit;           // > 0: each tile's K cut in ksplit ranges on the blocks of a cluster of ksplit (one
+                          // segment per block); 0: none
 };
 
 // ------------------------------------------------------------------ stream-K bookkeeping
@@ -90,13 +91,13 @@ struct SegIter {
     }
     BW_HD bool next(const Sched& s, int P, Seg& seg)
     {
-        if (s.kpair) {  // block c: half c % 2 of tile c / 2's K-blocks, once
-            if (next_u < 0 || next_u >= 2 * s.tiles) return false;
-            const int h = next_u & 1;
-            seg.tile = next_u >> 1;
-            seg.k0 = h ? s.kblocks / 2 : 0;
-            seg.k1 = h ? s.kblocks : s.kblocks / 2;
-            seg.unit = h * s.tiles + seg.tile;
+        if (s.ksplit) {  // block c: K range c % ksplit of tile c / ksplit, once
+            if (next_u < 0 || next_u >= s.ksplit * s.tiles) return false;
+            const int r = next_u % s.ksplit;
+            seg.tile = next_u / s.ksplit;
+            seg.k0 = (int)((long long)r * s.kblocks / s.ksplit);
+            seg.k1 = (int)((long long)(r + 1) * s.kblocks / s.ksplit);
+            seg.unit = r * s.tiles + seg.tile;
             next_u = -1;
             return true;
         }
@@ -165,10 +166,17 @@ BW_HD inline int fixup_slot(const Sched& s, int P, int tile, const Fixup& f, int
     return sk_slot(s, f.first + i, P, tile);
 }
 
+// ------------------------------------------------------------------ the chunks of a K-split cluster (BW_KSPLIT 1)
+// The accumulator's n 16-column chunks in runs, block o of a cluster of c owning [ksplit_run(o), ksplit_run(o + 1))
+// (runs of floor or ceil(n / c) chunks, empty ones where n < c).  The owner of chunk ch is the largest o whose run
+// starts at or before it: o n / c < ch + 1, so o = ceil((ch + 1) c / n) - 1.
+BW_HD inline int ksplit_run(int o, int n, int c) { return o * n / c; }
+BW_HD inline int ksplit_owner(int ch, int n, int c) { return ((ch + 1) * c + n - 1) / n - 1; }
+
 // The number of workspace slots a schedule needs.
 BW_HD inline long long workspace_slots(const Sched& s, int P)
 {
-    if (s.sk_tiles <= 0 || s.kpair) return 0;
+    if (s.sk_tiles <= 0 || s.ksplit) return 0;
     return s.splits > 0 ? (long long)s.sk_tiles * s.splits : 2LL * P;
 }
 

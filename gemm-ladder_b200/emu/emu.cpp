@@ -12,6 +12,8 @@
 //     Returns a BW_* status; status = the device status word, dirty = counters left non-zero, findings = the number
 //     of emulator findings and finding = the first one's text (empty if none).
 //   bw_emu_set(name, value): the knobs below.
+//   bw_emu_plan(M, N, K, sms, variant, &plan): the plan a call takes.
+// Built with -DBW_KSPLIT=1 it runs the K split over clusters of 2 to 8 blocks (plan.h) in place of the halves.
 #include <algorithm>
 #include <functional>
 #include <string>
@@ -86,7 +88,7 @@ Params make_params(const bw_plan& q, int M, int N, int K, void* C, float* work, 
     p.s.splits = q.splits;
     p.s.sk_iters = q.sk_iters;
     p.s.group_rows = q.group_rows;
-    p.s.kpair = q.kpair;
+    p.s.ksplit = q.ksplit;
     p.C = C;
     p.work = work;
     p.counters = counters;
@@ -103,8 +105,14 @@ int launch(const bw_plan& q, const CUtensorMap& mx, const CUtensorMap& my, const
         emu::finding("plan and kernel geometry disagree (bn %d)", BN);
         return BW_ERR_LAUNCH;
     }
-    const int cs = (PAIR || (SWAP && q.kpair)) ? 2 : 1;
-    if (q.grid % cs) return BW_ERR_LAUNCH;
+    const int cs = PAIR ? 2 : (SWAP && q.ksplit) ? q.ksplit : 1;
+    if (q.grid % cs || cs > emu::kMaxCluster ||
+        (q.ksplit && (!SWAP || q.grid != q.ksplit * q.tiles ||
+                      plan_ksplit_recv_bytes(BN, WM, q.ksplit) > G::kBarOffset))) {
+        emu::finding("a launch the library would refuse (cluster %d, grid %d)", cs, q.grid);
+        return BW_ERR_LAUNCH;
+    }
+    emu::g_smem_limit = q.smem_bytes - 1024;
     for (int c0 = 0; c0 < q.grid; c0 += cs) {
         emu::Cluster cl;
         cl.size = cs;
@@ -197,6 +205,13 @@ extern "C" __attribute__((visibility("default"))) int bw_emu_set(const char* nam
     else if (n == "barrier_limit_ms") g_barrier_limit_ms = value;
     else return -1;
     return 0;
+}
+
+// The plan the launcher takes for a call on the emulated GPU of `sms` SMs (the rule of this build).
+extern "C" __attribute__((visibility("default"))) int bw_emu_plan(int M, int N, int K, int sms, int variant,
+                                                                  bw_plan* out)
+{
+    return bw::make_plan(M, N, K, sms, sms / 2, variant, out);
 }
 
 // Runs one call of the rung on the emulated GPU of `sms` SMs.  status[4]: the device status word after the call;

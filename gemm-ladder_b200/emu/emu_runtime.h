@@ -116,11 +116,17 @@ struct Cta {
     }
 };
 
+constexpr int kMaxCluster = 8;  // the portable cluster limit
+
 struct Cluster {
     int size = 1;
-    Cta* cta[2] = {nullptr, nullptr};
+    Cta* cta[kMaxCluster] = {};
     Barrier all;
 };
+
+// The shared memory a launch's layout may use: its dynamic size less the 1024 bytes of slack the kernel keeps for
+// aligning its base (on the GPU the slack is spent on alignment; here the base is aligned already).
+inline int g_smem_limit = kSmemBytes;
 
 inline thread_local Cta* t_cta = nullptr;
 inline thread_local int t_tid = 0;
@@ -141,8 +147,8 @@ inline uint8_t* cta_smem() { return t_cta->smem; }
 inline uint32_t offset_of(const void* p)
 {
     const std::ptrdiff_t o = static_cast<const uint8_t*>(p) - t_cta->smem;
-    if (o < 0 || o >= kSmemBytes) {
-        finding("a shared-memory address outside the block's shared memory (offset %td)", o);
+    if (o < 0 || o >= g_smem_limit) {
+        finding("a shared-memory address outside the launch's shared memory (offset %td)", o);
         return 0;
     }
     return (uint32_t)o;
@@ -165,6 +171,16 @@ inline uint32_t mapa(uint32_t a, uint32_t rank)
 }
 
 // ------------------------------------------------------------------ mbarrier
+constexpr long long kTxLimit = (1 << 20) - 1;  // an mbarrier's pending transaction bytes, either way
+
+// A copy into [off, off + bytes) of block c's shared memory that would overwrite one of its mbarriers.
+inline bool over_mbar(Cta* c, uint32_t off, uint32_t bytes)
+{
+    std::lock_guard<std::mutex> l(g_mb);
+    auto it = c->mbars.lower_bound(off >= 7 ? off - 7 : 0);
+    return it != c->mbars.end() && it->first < off + bytes;
+}
+
 inline void mb_settle(MBar& b)
 {
     if (b.pending == 0 && b.tx == 0) {
@@ -198,6 +214,7 @@ inline void mb_arrive(Cta* c, uint32_t off, long long tx_add)
         return;
     }
     b->tx += tx_add;
+    if (b->tx > kTxLimit || b->tx < -kTxLimit) finding("an mbarrier transaction count of %lld bytes", b->tx);
     --b->pending;
     mb_settle(*b);
 }
@@ -207,6 +224,7 @@ inline void mb_complete_tx(Cta* c, uint32_t off, long long bytes)
     MBar* b = mb_find(c, off, "transaction bytes");
     if (!b) return;
     b->tx -= bytes;
+    if (b->tx > kTxLimit || b->tx < -kTxLimit) finding("an mbarrier transaction count of %lld bytes", b->tx);
     mb_settle(*b);
 }
 inline bool mb_try_wait(Cta* c, uint32_t off, uint32_t parity)
@@ -274,6 +292,10 @@ inline long long tma_copy(void* dst, const void* tmap, int x, int y, int z)
     if (((long long)x * 2) % 16) finding("a TMA load at x = %d, not on a 16-byte boundary", x);
     if (base % 1024) finding("a TMA destination not on a 1024-byte swizzle atom (offset %u)", base);
     const long long bytes = (long long)m.box[0] * m.box[1] * m.box[2] * 2;
+    if (base + bytes > (long long)g_smem_limit || over_mbar(c, base, (uint32_t)bytes)) {
+        finding("a TMA load past the launch's shared memory or over an mbarrier (offset %u, %lld bytes)", base, bytes);
+        return bytes;
+    }
     for (uint32_t zz = 0; zz < m.box[2]; ++zz)
         for (uint32_t rr = 0; rr < m.box[1]; ++rr)
             for (uint32_t cc = 0; cc < m.box[0]; ++cc) {
@@ -298,8 +320,8 @@ inline void bulk_copy(void* dst, const void* src, uint32_t bytes)
     const uint32_t off = offset_of(dst);
     if (off % 16 || bytes % 16 || reinterpret_cast<uintptr_t>(src) % 16)
         finding("a bulk copy not on 16-byte boundaries");
-    if (off + bytes > (uint32_t)kSmemBytes) {
-        finding("a bulk copy past the end of shared memory");
+    if (off + bytes > (uint32_t)g_smem_limit || over_mbar(t_cta, off, bytes)) {
+        finding("a bulk copy past the launch's shared memory or over an mbarrier");
         return;
     }
     std::memcpy(t_cta->smem + off, src, bytes);
@@ -309,8 +331,8 @@ inline void remote_store(uint32_t dst, const uint32_t* v, uint32_t bytes)
 {
     Cta* c = cta_of(dst);
     const uint32_t off = off_of(dst);
-    if (off + bytes > (uint32_t)kSmemBytes || off % bytes) {
-        finding("an st.async outside the destination block's shared memory or unaligned");
+    if (off + bytes > (uint32_t)g_smem_limit || off % bytes || over_mbar(c, off, bytes)) {
+        finding("an st.async outside the destination block's shared memory, unaligned or over an mbarrier");
         return;
     }
     std::memcpy(c->smem + off, v, bytes);

@@ -66,7 +66,7 @@ def timeline(lib, M, N, K, variant=0, dump=False):
     rel = lambda k: (raw[:, k].astype(np.float64) - t0) / 1e3  # noqa: E731  us after the first entry
     print(f"{M}x{N}x{K} v{variant}: event {e0.elapsed_time(e1) * 1e3:.1f} us, grid {g}, kernel {plan['kernel']}, "
           f"bn {plan['bn']}, whole tiles {plan['dp_tiles']}, split tiles {plan['sk_tiles']} "
-          f"(splits {plan['splits']}, kpair {plan['kpair']})")
+          f"(splits {plan['splits']}, ksplit {plan['ksplit']})")
     kind = raw[:, 8] & 0xFF
     for kd, name in KINDS.items():
         sel = kind == kd

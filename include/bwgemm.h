@@ -123,7 +123,8 @@ typedef struct bw_plan {
     int counters;        /* one counter per split tile */
     int smem_bytes;      /* dynamic shared memory per block */
     int tmem_cols;       /* tensor-memory columns per block */
-    int kpair;           /* 1: SWAP with each tile's K halves on the two blocks of a cluster (grid = 2 tiles) */
+    int ksplit;          /* > 0: SWAP with each tile's K cut in ksplit ranges on the blocks of a cluster of ksplit
+                            (grid = ksplit x tiles); 0: none */
     int wm;              /* SWAP: 128-column weight blocks per tile (1 or 2; 2 = two MMAs on each stage of A) */
 } bw_plan;
 

@@ -25,7 +25,7 @@ int main(void)
     CHECK(p.kernel == BW_KERNEL_PAIR && p.bn == 256 && p.tiles == 18 * 22 && p.kblocks == 128);
     /* M = 16: swap-AB, K halves on clusters of two */
     CHECK(bw_gemm_plan(16, 8192, 8192, 148, 0, &p) == BW_OK);
-    CHECK(p.kernel == BW_KERNEL_SWAP && p.bn == 16 && p.kpair == 1 && p.grid == 128);
+    CHECK(p.kernel == BW_KERNEL_SWAP && p.bn == 16 && p.ksplit == 2 && p.grid == 128);
     /* the reference's shape rule and bad arguments, refused before any GPU work */
     CHECK(bw_gemm_plan(15, 64, 64, 148, 0, &p) == BW_ERR_SHAPE);
     CHECK(bw_gemm_plan(16, 64, 64, 148, bw_gemm_variant_count(), &p) == BW_ERR_ARG);
@@ -36,13 +36,13 @@ int main(void)
     CHECK(strlen(bw_status_string(BW_ERR_TIMEOUT)) > 0);
     printf("bw_plan size %zu kernel %zu bn %zu stages %zu tiles_m %zu tiles_n %zu tiles %zu kblocks %zu grid %zu "
            "dp_tiles %zu sk_tiles %zu splits %zu sk_iters %zu group_rows %zu workspace_bytes %zu counters %zu "
-           "smem_bytes %zu tmem_cols %zu kpair %zu wm %zu\n",
+           "smem_bytes %zu tmem_cols %zu ksplit %zu wm %zu\n",
            sizeof(bw_plan), offsetof(bw_plan, kernel), offsetof(bw_plan, bn), offsetof(bw_plan, stages),
            offsetof(bw_plan, tiles_m), offsetof(bw_plan, tiles_n), offsetof(bw_plan, tiles), offsetof(bw_plan, kblocks),
            offsetof(bw_plan, grid), offsetof(bw_plan, dp_tiles), offsetof(bw_plan, sk_tiles),
            offsetof(bw_plan, splits), offsetof(bw_plan, sk_iters), offsetof(bw_plan, group_rows),
            offsetof(bw_plan, workspace_bytes), offsetof(bw_plan, counters), offsetof(bw_plan, smem_bytes),
-           offsetof(bw_plan, tmem_cols), offsetof(bw_plan, kpair), offsetof(bw_plan, wm));
+           offsetof(bw_plan, tmem_cols), offsetof(bw_plan, ksplit), offsetof(bw_plan, wm));
     printf("OK\n");
     return 0;
 }

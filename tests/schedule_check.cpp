@@ -24,7 +24,7 @@ static int check(int M, int N, int K, int sms, int variant)
     bw::Sched s;
     s.M = M, s.N = N, s.K = K, s.tiles_m = q.tiles_m, s.tiles_n = q.tiles_n, s.tiles = q.tiles;
     s.kblocks = q.kblocks, s.dp_tiles = q.dp_tiles, s.sk_tiles = q.sk_tiles, s.splits = q.splits;
-    s.sk_iters = q.sk_iters, s.group_rows = q.group_rows, s.kpair = q.kpair;
+    s.sk_iters = q.sk_iters, s.group_rows = q.group_rows, s.ksplit = q.ksplit;
     if (q.dp_tiles + q.sk_tiles != q.tiles || (q.splits > 0) == (q.sk_iters > 0) && q.sk_tiles > 0) {
         printf("FAULT %dx%dx%d v%d: inconsistent plan\n", M, N, K, variant);
         return 1;
@@ -62,13 +62,14 @@ static int check(int M, int N, int K, int sms, int variant)
             }
             for (int k = sg.k0; k < sg.k1; ++k) cover[(size_t)sg.tile * q.kblocks + k]++;
             const bool whole = sg.k0 == 0 && sg.k1 == q.kblocks;
-            if (q.kpair) {
-                // the two K halves of tile t on blocks 2 t (the first K-blocks, it writes C) and 2 t + 1 of one
-                // cluster of two, no workspace
-                const bool first = sg.k0 == 0;
-                if (q.kernel != BW_KERNEL_SWAP || q.workspace_bytes || q.counters || sg.tile != c / 2 ||
-                    first != (c % 2 == 0) || q.grid != 2 * q.tiles) {
-                    printf("FAULT %dx%dx%d v%d: kpair block %d tile %d k %d..%d\n", M, N, K, variant, c, sg.tile, sg.k0,
+            if (q.ksplit) {
+                // K range r of tile t on block c t + r of one cluster of c = ksplit blocks (block r of the cluster),
+                // the ranges in block order, no workspace
+                const int ks = q.ksplit, r = c % ks;
+                if (q.kernel != BW_KERNEL_SWAP || q.workspace_bytes || q.counters || sg.tile != c / ks || ks < 2 ||
+                    ks > 8 || sg.k0 != (int)((long long)r * q.kblocks / ks) ||
+                    sg.k1 != (int)((long long)(r + 1) * q.kblocks / ks) || q.grid != ks * q.tiles) {
+                    printf("FAULT %dx%dx%d v%d: ksplit block %d tile %d k %d..%d\n", M, N, K, variant, c, sg.tile, sg.k0,
                            sg.k1);
                     return 1;
                 }

@@ -59,7 +59,7 @@ def test_plan_rule_on_the_judge_shapes():
         p = bwgemm.plan(M, N, K, sms=148)
         if M <= 128 and -(-N // 256) <= 74:  # every tile's K halves at once on clusters of two SMs
             wm = 1 if -(-N // 128) <= 74 else 2  # tiles of 128 weight columns if they fit, else of 256
-            assert p["kernel"] == bwgemm.BW_KERNEL_SWAP and p["bn"] == M and p["kpair"] == 1 and p["wm"] == wm
+            assert p["kernel"] == bwgemm.BW_KERNEL_SWAP and p["bn"] == M and p["ksplit"] == 2 and p["wm"] == wm
             assert p["grid"] == 2 * p["tiles"] and p["splits"] == 2 and p["workspace_bytes"] == 0
             assert p["counters"] == 0 and p["tiles"] == -(-N // (128 * wm))
         elif M <= 128:  # stream-K; tiles of 256 weight columns from 64 tokens while they outnumber the SMs
@@ -77,7 +77,7 @@ def test_plan_rule_on_the_judge_shapes():
 def test_plan_variants_take_out_one_mechanism():
     assert bwgemm.plan(16, 8192, 8192, variant=1)["sk_iters"] == 0          # no stream-K
     v4s = bwgemm.plan(16, 8192, 8192, variant=4)                            # stream-K, not the cluster K halves
-    assert v4s["kpair"] == 0 and v4s["sk_iters"] == 64 * 128
+    assert v4s["ksplit"] == 0 and v4s["sk_iters"] == 64 * 128
     v4w = bwgemm.plan(128, 57344, 8192, variant=4)                          # 128-column swap tiles
     assert v4w["wm"] == 1 and v4w["tiles"] == 448 and bwgemm.plan(128, 57344, 8192)["wm"] == 2
     assert bwgemm.plan(16, 8192, 8192, variant=2)["kernel"] == bwgemm.BW_KERNEL_PAIR  # no swap-AB

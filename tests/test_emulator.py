@@ -21,14 +21,13 @@ PKG = os.path.join(ROOT, "gemm-ladder_b200")
 CUDA_INCLUDE = os.path.join(os.environ.get("CUDA_HOME", "/usr/local/cuda"), "include")
 
 
-@pytest.fixture(scope="module")
-def emu(tmp_path_factory):
+def build_emulator(tmp_path_factory, ksplit):
     if not os.path.isdir(CUDA_INCLUDE):
         pytest.skip("no CUDA headers")
-    lib = str(tmp_path_factory.mktemp("emu") / "libbwemu.so")
-    subprocess.check_call(["g++", "-std=c++20", "-O2", "-pthread", "-DBW_EMULATE", "-fPIC", "-shared", "-w",
-                           f"-I{CUDA_INCLUDE}", f"-I{os.path.join(ROOT, 'include')}", f"-I{os.path.join(PKG, 'csrc')}",
-                           os.path.join(PKG, "emu", "emu.cpp"), "-o", lib])
+    lib = str(tmp_path_factory.mktemp("emu") / f"libbwemu{ksplit}.so")
+    subprocess.check_call(["g++", "-std=c++20", "-O2", "-pthread", "-DBW_EMULATE", f"-DBW_KSPLIT={ksplit}", "-fPIC",
+                           "-shared", "-w", f"-I{CUDA_INCLUDE}", f"-I{os.path.join(ROOT, 'include')}",
+                           f"-I{os.path.join(PKG, 'csrc')}", os.path.join(PKG, "emu", "emu.cpp"), "-o", lib])
     L = ctypes.CDLL(lib)
     vp, i = ctypes.c_void_p, ctypes.c_int
     L.bw_emu_gemm.argtypes = [vp, vp, vp, i, i, i, i, i, i, i, ctypes.POINTER(ctypes.c_uint),
@@ -37,6 +36,27 @@ def emu(tmp_path_factory):
     L.bw_emu_set.argtypes = [ctypes.c_char_p, ctypes.c_longlong]
     L.bw_emu_set.restype = i
     return L
+
+
+@pytest.fixture(scope="module")
+def emu(tmp_path_factory):
+    """The kernel as the library builds it."""
+    return build_emulator(tmp_path_factory, 0)
+
+
+@pytest.fixture(scope="module")
+def emu_ksplit(tmp_path_factory):
+    """The kernel with the K split over clusters of 2 to 8 blocks (BW_KSPLIT 1)."""
+    return build_emulator(tmp_path_factory, 1)
+
+
+def plan_of(L, M, N, K, sms, variant=0):
+    import bwgemm  # the ctypes layout of bw_plan
+
+    q = bwgemm.Plan()
+    L.bw_emu_plan.argtypes = [ctypes.c_int] * 5 + [ctypes.POINTER(bwgemm.Plan)]
+    assert L.bw_emu_plan(M, N, K, sms, variant, ctypes.byref(q)) == 0
+    return q.as_dict()
 
 
 def emulate(L, A, B, M, N, K, sms, variant=0, epi=0, tn=False):
@@ -132,3 +152,65 @@ def test_a_stalled_pipeline_ends_with_a_status_not_a_hang(emu, shape, drop):
     assert rc == 0 and nf == 0, f"{nf} findings, first: {msg}"
     role, kind = status[1] >> 16, (status[1] >> 8) & 0xFF
     assert status[0] == 3 and (role, kind) in ((1, 0), (2, 2), (0, 1)), status
+
+
+# (M, N, K, emulated SMs, cluster size and tile width the BW_KSPLIT 1 rule takes there)
+KSPLIT_FORMS = [
+    (128, 512, 256, 8, 2, 1),    # bn 128: 8 chunks, 4 owned by each block, each receives the other's 4
+    (16, 1280, 1024, 16, 3, 2),  # 2 chunks over 3 blocks: one block owns none (sends only)
+    (96, 640, 1024, 16, 3, 1),   # 6 chunks, 2 per block; ragged last tile
+    (16, 512, 2048, 16, 4, 1),   # 1 chunk, the last block owns it and receives 3 pieces
+    (64, 512, 2048, 16, 4, 1),   # 4 chunks, one per block
+    (16, 256, 2048, 16, 8, 1),   # clusters of 8
+    (112, 256, 4096, 16, 8, 1),  # 7 chunks over 8 blocks (one owns none), 8 K-blocks per block
+    (48, 320, 1600, 16, 5, 1),   # clusters of 5, 25 K-blocks in ranges of 5, a last tile of 64 columns
+]
+
+
+@pytest.mark.parametrize("form", KSPLIT_FORMS, ids=lambda f: f"{f[0]}x{f[1]}x{f[2]}_c{f[4]}")
+@pytest.mark.parametrize("tn", [False, True], ids=["KxN", "NxK"])
+def test_k_split_over_clusters_of_2_to_8(emu_ksplit, oracle_mod, form, tn):
+    """BW_KSPLIT 1: each tile's K over a cluster of c blocks, every block summing its own run of the accumulator's
+    chunks from the others' pieces in its idle ring."""
+    M, N, K, sms, c, wm = form
+    q = plan_of(emu_ksplit, M, N, K, sms)
+    assert (q["ksplit"], q["wm"], q["grid"]) == (c, wm, c * q["tiles"]), q
+    A, B = oracle_mod.lcg_inputs(M, N, K)
+    rc, C, status, dirty, nf, msg = emulate(emu_ksplit, A, B, M, N, K, sms, tn=tn)
+    assert rc == 0 and nf == 0, f"rc {rc}, {nf} findings, first: {msg}"
+    assert status[0] == 0 and dirty == 0, (status, dirty)
+    r = oracle_mod.check(C, oracle_mod.gemm_f64(A, B), K)
+    assert r["nonfinite"] == 0 and r["violations"] == 0 and r["normwise"] <= 2e-3, r
+
+
+def test_k_split_in_halves_is_the_same_bits_either_way(emu, emu_ksplit, oracle_mod):
+    """At c = 2 both protocols add block 0's sum and block 1's in that order: the same bits."""
+    M, N, K = 128, 512, 256
+    assert plan_of(emu, M, N, K, 8)["ksplit"] == 2 and plan_of(emu_ksplit, M, N, K, 8)["ksplit"] == 2
+    A, B = oracle_mod.lcg_inputs(M, N, K)
+    C0 = emulate(emu, A, B, M, N, K, 8)[1]
+    C1 = emulate(emu_ksplit, A, B, M, N, K, 8)[1]
+    assert np.array_equal(C0, C1)
+
+
+@pytest.mark.parametrize("shape", [(16, 512, 2048), (96, 640, 1024)], ids=lambda s: "x".join(map(str, s)))
+@pytest.mark.parametrize("drop", [0, 5])
+def test_a_stalled_k_split_cluster_ends_with_a_status(emu_ksplit, shape, drop):
+    """A TMA completion that never arrives in one block of a K-split cluster: that block's MMA issuer (or its epilogue,
+    waiting for the accumulator) gives up, the others give up on the go barrier or on their pieces, and every block
+    leaves.  The status word keeps the first wait to give up."""
+    M, N, K = shape
+    A = np.full((M, K), 0x3C00, np.uint16)
+    B = np.full((K, N), 0x3C00, np.uint16)
+    emu_ksplit.bw_emu_set(b"wait_ns", 300_000_000)
+    emu_ksplit.bw_emu_set(b"barrier_limit_ms", 30_000)
+    emu_ksplit.bw_emu_set(b"drop_tma", drop)
+    try:
+        rc, C, status, dirty, nf, msg = emulate(emu_ksplit, A, B, M, N, K, 16)
+    finally:
+        emu_ksplit.bw_emu_set(b"drop_tma", -1)
+        emu_ksplit.bw_emu_set(b"wait_ns", 60_000_000_000)
+        emu_ksplit.bw_emu_set(b"barrier_limit_ms", 120_000)
+    assert rc == 0 and nf == 0, f"{nf} findings, first: {msg}"
+    role, kind = status[1] >> 16, (status[1] >> 8) & 0xFF
+    assert status[0] == 3 and (role, kind) in ((1, 0), (2, 2), (2, 5), (2, 6), (0, 1)), status

@@ -11,11 +11,12 @@ ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(ROOT, "gemm-ladder_b200", "csrc")
 
 
-@pytest.fixture(scope="module")
-def checker(tmp_path_factory):
+@pytest.fixture(scope="module", params=[0, 1], ids=["ksplit2", "ksplit2to8"])
+def checker(request, tmp_path_factory):
+    """The checker over the library's rule (BW_KSPLIT 0) and over the K split on clusters of 2 to 8 (BW_KSPLIT 1)."""
     exe = str(tmp_path_factory.mktemp("sched") / "schedule_check")
-    subprocess.check_call(["g++", "-std=c++17", "-O2", "-Wall", f"-I{CSRC}", f"-I{os.path.join(ROOT, 'include')}",
-                           os.path.join(HERE, "schedule_check.cpp"), "-o", exe])
+    subprocess.check_call(["g++", "-std=c++17", "-O2", "-Wall", f"-DBW_KSPLIT={request.param}", f"-I{CSRC}",
+                           f"-I{os.path.join(ROOT, 'include')}", os.path.join(HERE, "schedule_check.cpp"), "-o", exe])
     return exe
 
 
