@@ -69,6 +69,17 @@
 #ifndef BW_KSPLIT_MAX
 #define BW_KSPLIT_MAX 8        // BW_KSPLIT 1: the largest cluster (8, the portable limit)
 #endif
+// BW_KSPLIT 1's choice of cluster size and tile width: the estimated time of a call (plan.h, ksplit_cost)
+#ifndef BW_HBM_GBS
+#define BW_HBM_GBS 6450.0      // HBM copy bandwidth (measured on this pool's B200s)
+#endif
+#ifndef BW_SM_INGEST_GBS
+#define BW_SM_INGEST_GBS 80.0  // operand bytes one SM takes in from L2 per second (measured: the pair kernel's mainloop,
+                               // 32 KB per K-block in ~400 ns)
+#endif
+#ifndef BW_DSMEM_GBS
+#define BW_DSMEM_GBS 100.0     // distributed-shared-memory bytes one SM sends per second (an estimate, not measured)
+#endif
 #ifndef BW_SK_ONE_WAVE
 #define BW_SK_ONE_WAVE 1       // stream-K over every tile when they make one full wave and part of another (the
                                // split-K tail's units then double a block's work: measured qkv_m512 -12 %)
@@ -127,6 +138,22 @@ inline int plan_ksplit_recv_bytes(int bn, int wm, int c)
 inline bool plan_ksplit_fits(int bn, int wm, int c)
 {
     return plan_ksplit_recv_bytes(bn, wm, c) <= plan_stages(bn, 1, true, wm) * plan_stage_bytes(bn, 1, wm);
+}
+
+// The estimated time (us) of a K-split plan with clusters of c blocks and tiles of 128 wm weight columns: the larger
+// of the weights' HBM time and the busiest block's operand intake (its K range of 128 wm weight columns and of the bn
+// tokens, both re-read per block), plus that block's hand-over of the chunks it does not own.  Every K-split plan
+// streams the weights once, so the intake decides between them where it exceeds the HBM time: at M = 128 the tokens
+// cost as much intake per block as the weights of a 128-column tile.
+inline double ksplit_cost(int M, int N, int K, int bn, int wm, int c)
+{
+    const double kb = (double)((K / 64 + c - 1) / c);                      // the longest K range, in K-blocks
+    const double intake = (128.0 * wm + bn) * 64 * 2 * kb;                  // bytes into the busiest block
+    const double hbm = ((double)N * K + (double)M * K + (double)M * N) * 2;  // bytes from / to HBM
+    const int chunks = bn * wm / 16;
+    const double sent = (double)(chunks - chunks / c) * 8192;               // the busiest sender's pieces
+    const double t_hbm = hbm / (BW_HBM_GBS * 1e3), t_in = intake / (BW_SM_INGEST_GBS * 1e3);
+    return (t_hbm > t_in ? t_hbm : t_in) + sent / (BW_DSMEM_GBS * 1e3);
 }
 
 inline bool shape_ok(int M, int N, int K)
@@ -193,21 +220,23 @@ inline int make_plan(int M, int N, int K, int sms, int pairs, int variant, bw_pl
     // swap-AB with every tile at once on clusters of blocks, each block one equal K range of its tile, the blocks'
     // sums added through distributed shared memory (no partials in memory, no counters).  BW_KSPLIT 0: clusters of
     // two, tiles of 128 weight columns if they all fit at once, else of 256 (two MMAs on each stage of A) if those do.
-    // BW_KSPLIT 1: clusters of c = 2 .. BW_KSPLIT_MAX, the (c, tile width) that streams on the most SMs, ties to the
-    // smaller c (fewer partials), then to the narrower tile; c > 2 wants 4 K-blocks per block at least.
+    // BW_KSPLIT 1: clusters of c = 2 .. BW_KSPLIT_MAX, the (c, tile width) of the least estimated time (ksplit_cost),
+    // one within 1 % of another going to the smaller c (fewer partials), then to the narrower tile; c > 2 wants 4
+    // K-blocks per block at least.
     const bool wide_ok = (variant == 0 || variant == 3) && !(flags & kPlanNarrow);
     const int tiles256 = (N + 255) / 256;
     int ks = 0, ks_wm = 0;
     if (swap && variant != 1 && variant != 4 && q.kblocks >= 2) {
 #if BW_KSPLIT
-        int best = 0;
-        for (int wm = 1; wm <= (wide_ok ? 2 : 1); ++wm) {
-            const int tiles = (N + 128 * wm - 1) / (128 * wm);
-            for (int c = 2; c <= BW_KSPLIT_MAX && c <= 8; ++c) {
+        double best = 0.0;
+        for (int c = 2; c <= BW_KSPLIT_MAX && c <= 8; ++c) {
+            for (int wm = 1; wm <= (wide_ok ? 2 : 1); ++wm) {
+                const int tiles = (N + 128 * wm - 1) / (128 * wm);
                 const int at_once = held ? held[c] : (c == 2 && pairs > 0) ? pairs : sms / c;
                 if (tiles > at_once || (c > 2 && q.kblocks < 4 * c) || !plan_ksplit_fits(q.bn, wm, c)) continue;
-                if (tiles * c > best) {
-                    best = tiles * c;
+                const double t = ksplit_cost(M, N, K, q.bn, wm, c);
+                if (!ks || t < 0.99 * best) {
+                    best = t;
                     ks = c;
                     ks_wm = wm;
                 }

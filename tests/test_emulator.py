@@ -158,12 +158,14 @@ def test_a_stalled_pipeline_ends_with_a_status_not_a_hang(emu, shape, drop):
 KSPLIT_FORMS = [
     (128, 512, 256, 8, 2, 1),    # bn 128: 8 chunks, 4 owned by each block, each receives the other's 4
     (16, 1280, 1024, 16, 3, 2),  # 2 chunks over 3 blocks: one block owns none (sends only)
-    (96, 640, 1024, 16, 3, 1),   # 6 chunks, 2 per block; ragged last tile
-    (16, 512, 2048, 16, 4, 1),   # 1 chunk, the last block owns it and receives 3 pieces
-    (64, 512, 2048, 16, 4, 1),   # 4 chunks, one per block
-    (16, 256, 2048, 16, 8, 1),   # clusters of 8
-    (112, 256, 4096, 16, 8, 1),  # 7 chunks over 8 blocks (one owns none), 8 K-blocks per block
+    (96, 640, 1024, 16, 3, 1),   # 6 chunks, 2 per block
+    (16, 128, 1024, 16, 4, 1),   # 1 chunk: the last block owns it and receives 3 pieces
+    (64, 512, 1024, 16, 4, 1),   # 4 chunks, one per block
+    (64, 704, 1024, 16, 4, 2),   # 8 chunks of 256-column tiles, 2 per block; the last tile 192 columns wide
     (48, 320, 1600, 16, 5, 1),   # clusters of 5, 25 K-blocks in ranges of 5, a last tile of 64 columns
+    (32, 128, 1536, 16, 6, 1),   # 2 chunks over 6 blocks
+    (96, 448, 2624, 16, 7, 2),   # 12 chunks over 7 (runs of 1 and 2), 41 K-blocks in ranges of 5 and 6
+    (112, 256, 4096, 16, 8, 1),  # 7 chunks over 8 blocks (one owns none), 8 K-blocks per block
 ]
 
 
@@ -214,3 +216,20 @@ def test_a_stalled_k_split_cluster_ends_with_a_status(emu_ksplit, shape, drop):
     assert rc == 0 and nf == 0, f"{nf} findings, first: {msg}"
     role, kind = status[1] >> 16, (status[1] >> 8) & 0xFF
     assert status[0] == 3 and (role, kind) in ((1, 0), (2, 2), (2, 5), (2, 6), (0, 1)), status
+
+
+def test_k_split_rule_on_the_judge_shapes(emu_ksplit):
+    """BW_KSPLIT 1 on 148 SMs: the cluster size and tile width of the least estimated time.  qkv (40 tiles of 256
+    columns) on clusters of 3; at M = 128 the o and down shapes take 256-column tiles on clusters of 4, which halves
+    each block's intake of the tokens against 128-column tiles on pairs; at M = 16 the weights' HBM time decides and
+    pairs stay."""
+    from shapes import JUDGE_B200
+
+    want = {"qkv_m16": (3, 2), "qkv_m128": (3, 2), "o_m16": (2, 1), "o_m128": (4, 2), "down_m16": (2, 1),
+            "down_m128": (4, 2), "gateup_m16": (0, 1), "gateup_m128": (0, 2)}
+    for name, M, N, K in JUDGE_B200:
+        if M > 128:
+            continue
+        q = plan_of(emu_ksplit, M, N, K, 148)
+        assert (q["ksplit"], q["wm"]) == want[name], (name, q)
+        assert q["grid"] <= 148 and (q["ksplit"] == 0 or q["grid"] == q["ksplit"] * q["tiles"])
