@@ -21,8 +21,8 @@ B200 shapes timed against torch.matmul (cuBLAS) in CUDA graphs, with the geometr
 harness needs its judge, which needs CUDA 13) timed on the host cores on the same workload, in bounded row samples.
 
 --workload tp_mlp: the tensor-parallel MLP block of gemm-ladder_b200/tp_mlp.py over the ranks
-(--tp-m tokens, 8192 or 2048; --tp-unfused for the activation as separate torch ops), total work fixed: strong
-scaling.  --shape MxNxK times any shape in place of the workload.  --profile-arm {ours,cublas}: one call of either
+(--tp-m tokens, 8192 or 2048; --tp-unfused for the activation as separate torch ops; --tp-fused-rs for down and the
+reduce-scatter in one kernel per rank, bw_gemm_f16_rs), total work fixed: strong scaling.  --shape MxNxK times any shape in place of the workload.  --profile-arm {ours,cublas}: one call of either
 arm inside an NVTX range "timed" (3 warm-up calls before it), no JSON line: the command for ncu's --nvtx-include.
 """
 import argparse
@@ -62,6 +62,8 @@ def parse():
     ap.add_argument("--variant", type=int, default=0)
     ap.add_argument("--tp-m", type=int, default=8192, help="tokens of the tp_mlp workload (2048 or 8192)")
     ap.add_argument("--tp-unfused", action="store_true", help="tp_mlp: the activation as separate torch ops")
+    ap.add_argument("--tp-fused-rs", action="store_true",
+                    help="tp_mlp: down and the reduce-scatter in one kernel per rank (bw_gemm_f16_rs), no NCCL call")
     ap.add_argument("--sweep", action="store_true", help="also time the judge's 17 shapes against cuBLAS")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
@@ -327,9 +329,10 @@ def run_tp_mlp(args):
     W1 = ((torch.rand((hidden, 2 * f // world), generator=gw, device="cuda") * 2 - 1) / hidden ** 0.5).half()
     W2 = ((torch.rand((f // world, hidden), generator=gw, device="cuda") * 2 - 1) / f ** 0.5).half()
     # (random shards: the interleaved gate / up layout of the fused activation needs no permutation here)
+    rs = bwgemm.ReduceScatterGemm(M, hidden) if args.tp_fused_rs and world > 1 else None
     blk = tp_mlp.TPMLP(W1, W2, rank, world, bwgemm.gemm, bwgemm.gemm_f32out,
                        tp_mlp.nccl_reduce_scatter if world > 1 else None,
-                       gemm_swiglu=None if args.tp_unfused else bwgemm.gemm_swiglu)
+                       gemm_swiglu=None if args.tp_unfused else bwgemm.gemm_swiglu, gemm_rs=rs)
     stream = torch.cuda.current_stream()
     watch = None
     if world > 1:  # host-side failure detection at the phase boundaries (peers.py), outside the timed region
@@ -377,6 +380,10 @@ def run_tp_mlp(args):
         import torch.distributed as dist
 
         dist.barrier()
+        if rs is not None:
+            torch.cuda.synchronize()
+            rs.close()
+            dist.barrier()
         dist.destroy_process_group()
     if rank == 0:
         print(json.dumps({
@@ -387,7 +394,9 @@ def run_tp_mlp(args):
             "data": "synthetic: seeded uniform tokens and weights",
             "config": {"workload": f"tp_mlp M={M} hidden={hidden} mlp={f}", "M": M, "parallelism": f"tp{world}",
                        "activation": "separate torch ops" if args.tp_unfused else "fused in the gateup epilogue",
-                       "collective": "NCCL reduce-scatter of fp32 partials" if world > 1 else "none"},
+                       "collective": ("fused: partial tiles pushed into the owners' memory in the down GEMM's kernel"
+                                      if rs is not None else "NCCL reduce-scatter of fp32 partials")
+                       if world > 1 else "none"},
             "clocks": clk.summary(), "gpu_launches": 2 * args.steps, "device_status": code,
             "e2e": {"value": round(flops * steps_e2e / te / 1e12, 2), "unit": "TFLOP/s",
                     "h2d_bytes_per_step": M * hidden * 2, "d2h_bytes_per_step": M // world * hidden * 2},

@@ -90,6 +90,18 @@ def lib():
         L.bw_gemm_set_wait_limit_ns.restype = ctypes.c_ulonglong
         L.bw_wait_selftest.argtypes = [ctypes.c_ulonglong, vp]
         L.bw_wait_selftest.restype = i
+        L.bw_rs_create.argtypes = [i, i, i, i, ctypes.POINTER(vp)]
+        L.bw_rs_create.restype = i
+        L.bw_rs_region_bytes.argtypes = [vp]
+        L.bw_rs_region_bytes.restype = ctypes.c_size_t
+        L.bw_rs_handle.argtypes = [vp, ctypes.c_char_p]
+        L.bw_rs_handle.restype = i
+        L.bw_rs_connect.argtypes = [vp, ctypes.c_char_p]
+        L.bw_rs_connect.restype = i
+        L.bw_gemm_f16_rs.argtypes = [vp, vp, vp, vp, i, vp]
+        L.bw_gemm_f16_rs.restype = i
+        L.bw_rs_destroy.argtypes = [vp]
+        L.bw_rs_destroy.restype = i
         L.bw_status_string.argtypes = [i]
         L.bw_status_string.restype = ctypes.c_char_p
         L.bw_last_error_string.argtypes = []
@@ -241,3 +253,64 @@ def wait_selftest(limit_ns=0, stream=None):
 
     s = stream if stream is not None else torch.cuda.current_stream()
     return lib().bw_wait_selftest(limit_ns, s.cuda_stream)
+
+
+RS_HANDLE_BYTES = 64
+
+
+class ReduceScatterGemm:
+    """The fused reduce-scatter of a row-parallel layer on this rank (bw_rs_* of bwgemm.h): for fp16 A_r (M x K) and
+    B_r (K x N), C_r = this rank's rows [r M/world, (r+1) M/world) of sum_r A_r B_r in fp16, one kernel per rank that
+    pushes the partial tiles of the other ranks' rows into their memory and sums its own rows' partials in rank order.
+
+    Every rank of `group` constructs it with the same M and N (its receive region's CUDA IPC handle is exchanged with
+    all_gather_object, then every rank opens the others' and a barrier follows), and calls it with the same shapes in
+    the same order.  Not capturable in a CUDA graph.  After a BW_ERR_TIMEOUT (another rank never came), close it and
+    make a new one."""
+
+    def __init__(self, M, N, group=None):
+        import torch.distributed as dist
+
+        L = lib()
+        self.M, self.N = M, N
+        self.world, self.rank = dist.get_world_size(group), dist.get_rank(group)
+        self._ctx = ctypes.c_void_p()
+        check(L.bw_rs_create(M, N, self.world, self.rank, ctypes.byref(self._ctx)))
+        try:
+            h = ctypes.create_string_buffer(RS_HANDLE_BYTES)
+            check(L.bw_rs_handle(self._ctx, h))
+            handles = [None] * self.world
+            dist.all_gather_object(handles, h.raw, group=group)
+            check(L.bw_rs_connect(self._ctx, b"".join(handles)))
+            dist.barrier(group=group)
+        except Exception:
+            self.close()
+            raise
+
+    def region_bytes(self):
+        return lib().bw_rs_region_bytes(self._ctx)
+
+    def __call__(self, A, B, C=None, stream=None):
+        import torch
+
+        M, K = A.shape
+        K2, N = B.shape
+        if (M, N) != (self.M, self.N) or K2 != K:
+            raise ValueError(f"A {tuple(A.shape)} and B {tuple(B.shape)} do not make the context's {self.M} x {self.N}")
+        for t in (A, B):
+            if t.dtype != torch.float16 or not t.is_cuda or not t.is_contiguous():
+                raise ValueError("A and B must be contiguous fp16 CUDA tensors")
+        rows = M // self.world
+        if C is None:
+            C = torch.empty((rows, N), dtype=torch.float16, device=A.device)
+        elif C.shape != (rows, N) or C.dtype != torch.float16 or not C.is_contiguous():
+            raise ValueError(f"C must be a contiguous fp16 {rows} x {N} tensor")
+        s = stream if stream is not None else torch.cuda.current_stream(A.device)
+        with torch.cuda.device(A.device):
+            check(lib().bw_gemm_f16_rs(self._ctx, A.data_ptr(), B.data_ptr(), C.data_ptr(), K, s.cuda_stream))
+        return C
+
+    def close(self):
+        if self._ctx:
+            lib().bw_rs_destroy(self._ctx)
+            self._ctx = ctypes.c_void_p()

@@ -298,7 +298,7 @@ int dispatch(DeviceState& d, const bw_plan& q, const CUtensorMap& mx, const CUte
 // The kernel parameters of a plan.
 Params make_params(const bw_plan& q, int M, int N, int K, void* C, float* work, int* counters, bool tn = false)
 {
-    Params p;
+    Params p = {};  // row_shift 0 (the rule's order), no reduce-scatter
     p.tn = tn ? 1 : 0;
     p.s.M = M;
     p.s.N = N;
@@ -601,3 +601,165 @@ BW_API int bw_trace_read(unsigned long long* dst, int blocks)
     return e == cudaSuccess ? BW_OK : BW_ERR_LAUNCH;
 }
 #endif
+
+// ------------------------------------------------------------------ the fused reduce-scatter (kEpiRS)
+// One context per rank: this rank's region (the slots, flags, ack and count of gemm_kernel.cuh's RsTable, and the
+// table itself; one cudaMalloc so that one CUDA IPC handle exports it) and the other ranks' regions opened from their
+// handles.
+struct bw_rs {
+    int dev, M, N, world, rank;
+    int tiles_block;                     // pair tiles in one owner's rows
+    size_t flags_off, ack_off, table_off, bytes;  // offsets in a region; its size
+    uint8_t* region;                     // this rank's
+    uint8_t* peer[bw::kRsMaxWorld];      // every rank's region in this process (this rank's own: region)
+    unsigned epoch;                      // calls made
+    bool connected;                      // the table is written
+};
+
+static_assert(sizeof(cudaIpcMemHandle_t) == BW_RS_HANDLE_BYTES, "the IPC handle size of bwgemm.h");
+
+namespace bw {
+namespace {
+
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+int rs_gemm(bw_rs* rs, const void* A, const void* B, void* C, int K, cudaStream_t st)
+{
+    if (!rs) return BW_ERR_ARG;
+    const int M = rs->M, N = rs->N;
+    if (!shape_ok(M, N, K)) return BW_ERR_SHAPE;
+    if (!A || !B || !C || (reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(B) |
+                           reinterpret_cast<uintptr_t>(C)) % 16)
+        return BW_ERR_ARG;
+    if (!rs->connected) {
+        snprintf(g_errbuf, sizeof g_errbuf, "the reduce-scatter context is not connected (bw_rs_connect)");
+        return BW_ERR_ARG;
+    }
+    int dev = -1;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+    if (dev != rs->dev) {
+        snprintf(g_errbuf, sizeof g_errbuf, "the reduce-scatter context belongs to device %d", rs->dev);
+        return BW_ERR_ARG;
+    }
+    DeviceState* d = nullptr;
+    int rc = device_state(&d);
+    if (rc) return rc;
+    bw_plan q;
+    {
+        std::lock_guard<std::mutex> lock(g_mu);
+        if ((rc = pair_occupancy(*d))) return rc;
+        if ((rc = make_plan(M, N, K, d->sms, d->pairs, 0, &q, kPlanNoSwap | kPlanNoSplit, held_of(*d)))) return rc;
+    }
+    if (q.kernel != BW_KERNEL_PAIR || q.sk_tiles != 0 || q.bn != 256) {
+        snprintf(g_errbuf, sizeof g_errbuf, "the fused reduce-scatter needs whole pair tiles");
+        return BW_ERR_LAUNCH;
+    }
+    CUtensorMap mx, my;
+    if (!make_maps(q, A, B, M, N, K, &mx, &my)) {
+        snprintf(g_errbuf, sizeof g_errbuf, "cuTensorMapEncodeTiled failed");
+        return BW_ERR_LAUNCH;
+    }
+    Params p = make_params(q, M, N, K, C, nullptr, nullptr);
+    p.s.row_shift = ((rs->rank + 1) * (rs->M / rs->world / 256)) % q.tiles_m;  // this rank's own rows last
+    p.rs = reinterpret_cast<const RsTable*>(rs->region + rs->table_off);
+    p.rs_epoch = rs->epoch + 1u;
+    rc = launch_kernel<256, false, true, kEpiRS>(*d, 1u << 24, q, mx, my, p, st);
+    if (rc == BW_OK) rs->epoch = p.rs_epoch;
+    return rc;
+}
+
+}  // namespace
+}  // namespace bw
+
+BW_API int bw_rs_create(int M, int N, int world, int rank, bw_rs** out)
+{
+    using namespace bw;
+    if (!out) return BW_ERR_ARG;
+    *out = nullptr;
+    if (world < 2 || world > kRsMaxWorld || rank < 0 || rank >= world) return BW_ERR_ARG;
+    if (!shape_ok(M, N, 64) || M % (256 * world)) return BW_ERR_SHAPE;
+    DeviceState* d = nullptr;
+    int rc = device_state(&d);
+    if (rc) return rc;
+    bw_rs* rs = static_cast<bw_rs*>(calloc(1, sizeof(bw_rs)));
+    if (!rs) return BW_ERR_ARG;
+    cudaError_t e = cudaGetDevice(&rs->dev);
+    if (e != cudaSuccess) {
+        free(rs);
+        return cuda_fail(e, "cudaGetDevice");
+    }
+    rs->M = M, rs->N = N, rs->world = world, rs->rank = rank;
+    rs->tiles_block = (M / world / 256) * ((N + 255) / 256);
+    const size_t nslots = (size_t)rs->tiles_block * (world - 1) * 2;
+    rs->flags_off = align_up(nslots * 128 * 256 * sizeof(float), 256);
+    rs->ack_off = align_up(rs->flags_off + nslots * sizeof(unsigned), 256);
+    rs->table_off = rs->ack_off + 256;  // the ack word, then the count; then the table
+    rs->bytes = align_up(rs->table_off + sizeof(RsTable), 256);
+    if ((e = cudaMalloc(reinterpret_cast<void**>(&rs->region), rs->bytes)) != cudaSuccess ||
+        (e = cudaMemset(rs->region, 0, rs->bytes)) != cudaSuccess) {
+        if (rs->region) cudaFree(rs->region);
+        free(rs);
+        return cuda_fail(e, "cudaMalloc (reduce-scatter region)");
+    }
+    rs->peer[rank] = rs->region;
+    *out = rs;
+    return BW_OK;
+}
+
+BW_API size_t bw_rs_region_bytes(const bw_rs* rs) { return rs ? rs->bytes : 0; }
+
+BW_API int bw_rs_handle(const bw_rs* rs, void* handle)
+{
+    if (!rs || !handle) return BW_ERR_ARG;
+    cudaIpcMemHandle_t h;
+    cudaError_t e = cudaIpcGetMemHandle(&h, rs->region);
+    if (e != cudaSuccess) return bw::cuda_fail(e, "cudaIpcGetMemHandle");
+    memcpy(handle, &h, sizeof h);
+    return BW_OK;
+}
+
+BW_API int bw_rs_connect(bw_rs* rs, const void* handles)
+{
+    if (!rs || !handles) return BW_ERR_ARG;
+    for (int o = 0; o < rs->world; ++o) {
+        if (o == rs->rank || rs->peer[o]) continue;
+        cudaIpcMemHandle_t h;
+        memcpy(&h, static_cast<const uint8_t*>(handles) + (size_t)o * BW_RS_HANDLE_BYTES, sizeof h);
+        void* ptr = nullptr;
+        cudaError_t e = cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) return bw::cuda_fail(e, "cudaIpcOpenMemHandle");
+        rs->peer[o] = static_cast<uint8_t*>(ptr);
+    }
+    // this rank's view of every region, into its own region's table
+    bw::RsTable t = {};
+    t.world = rs->world;
+    t.rank = rs->rank;
+    t.rows = rs->M / rs->world;
+    for (int o = 0; o < rs->world; ++o) {
+        t.slots[o] = reinterpret_cast<float*>(rs->peer[o]);
+        t.flags[o] = reinterpret_cast<unsigned*>(rs->peer[o] + rs->flags_off);
+        t.ack[o] = reinterpret_cast<unsigned*>(rs->peer[o] + rs->ack_off);
+    }
+    t.count = reinterpret_cast<unsigned*>(rs->region + rs->ack_off) + 1;
+    cudaError_t e = cudaMemcpy(rs->region + rs->table_off, &t, sizeof t, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) return bw::cuda_fail(e, "cudaMemcpy (reduce-scatter table)");
+    rs->connected = true;
+    return BW_OK;
+}
+
+BW_API int bw_gemm_f16_rs(bw_rs* rs, const void* A, const void* B, void* C, int K, void* stream)
+{
+    return bw::rs_gemm(rs, A, B, C, K, static_cast<cudaStream_t>(stream));
+}
+
+BW_API int bw_rs_destroy(bw_rs* rs)
+{
+    if (!rs) return BW_OK;
+    int rc = BW_OK;
+    for (int o = 0; o < rs->world; ++o)
+        if (o != rs->rank && rs->peer[o] && cudaIpcCloseMemHandle(rs->peer[o]) != cudaSuccess) rc = BW_ERR_LAUNCH;
+    if (rs->region && cudaFree(rs->region) != cudaSuccess) rc = BW_ERR_LAUNCH;
+    free(rs);
+    return rc;
+}

@@ -49,6 +49,29 @@ enum : int {
     kEpiF32 = 1,     // C = A B in fp32 (row-parallel partial sums)
     kEpiSwiGLU = 2,  // B's tiles of BN columns hold BN/2 gate then BN/2 up columns: C = silu(gate) * up in fp16,
                      // M x N/2 (a gated MLP's activation, from the accumulators: the gateup result never exists)
+    kEpiRS = 3,      // the fused reduce-scatter: C (fp16, this rank's M / world rows) = the sum over the ranks of
+                     // their A_r B_r, the partials exchanged tile by tile through the ranks' memory (RsTable)
+};
+
+constexpr int kRsMaxWorld = 8;
+
+// The fused reduce-scatter of a row-parallel layer (kEpiRS, pair tiles of 256 x 256, whole tiles): every rank computes
+// every tile of its partial A_r B_r; owner o = the rank whose rows [o rows, (o + 1) rows) hold the tile.  Owner o's
+// region (one allocation, mapped into the other ranks' address spaces):
+//   slots  [tile of o's rows][sender j: the other ranks in rank order][block of the pair] x 128 x 256 fp32, each
+//          laid out [col / 4][row][4] (a warp's 16-byte stores contiguous)
+//   flags  one per slot: the epoch of the call whose partial it holds
+//   ack    the last epoch whose slots o has consumed (a sender waits for epoch - 1 before writing)
+//   count  tile halves o has consumed in this call
+// The table lives in this rank's device memory (written once, when the ranks connect); a call passes its address
+// and its epoch.
+struct RsTable {
+    int world, rank;                 // ranks; this one
+    int rows;                        // rows of C per owner (M / world, a multiple of 256)
+    float* slots[kRsMaxWorld];       // owner o's slots, as this rank addresses them
+    unsigned* flags[kRsMaxWorld];    // owner o's flags
+    unsigned* ack[kRsMaxWorld];      // owner o's ack word
+    unsigned* count;                 // this rank's count
 };
 
 struct Params {
@@ -58,6 +81,8 @@ struct Params {
     int* counters;               // one per split tile (per block of the pair), zero between calls
     unsigned long long wait_ns;  // the limit of any single wait on a barrier
     int tn;                      // 1: B is N x K row-major (K-major for the tensor core, like A); 0: K x N
+    const RsTable* rs;           // kEpiRS only: the ranks' regions
+    unsigned rs_epoch;           // kEpiRS only: this call's number (from 1)
 };
 
 __host__ __device__ constexpr int pow2_at_least(int v, int p) { return p >= v ? p : pow2_at_least(v, 2 * p); }
@@ -481,6 +506,110 @@ __device__ __noinline__ bool reduce_tile_bulk(const Params& p, int P, int tile, 
     return true;
 }
 
+// ------------------------------------------------------------------ the fused reduce-scatter's epilogue
+// One pair tile's half (this block's 128 rows x 256 columns, accumulator at tbase) under kEpiRS.  Not this rank's
+// rows: the partial goes into the owner's slot by 16-byte stores (over NVLink), then the slot's flag takes the epoch
+// (each thread's stores ordered before it by a system-scope fence).  The first time a block sends to an owner in a
+// call it waits for the owner's ack of the previous call (the slot is free).  This rank's rows: the other ranks'
+// flags for the tile, then the sum in rank order (this rank's own partial from tensor memory) rounded to fp16 into C,
+// then a count; the block that consumes the call's last tile half acks the epoch.  Every wait is bounded; one thread
+// waits and hands the outcome to the other 127 through `go`.  Returns false after a wait gave up.
+__device__ __noinline__ bool rs_tile(const Params& p, int tm, int tn, int pr, uint32_t tbase, int row, int lane,
+                                     int q, volatile int* abort_flag, volatile int* go, unsigned& acked, int seg)
+{
+    const RsTable& rs = *p.rs;
+    const unsigned epoch = p.rs_epoch;
+    const Sched& s = p.s;
+    const int o = tm * 256 / rs.rows;                        // the owner of the tile's rows
+    const int tl = (tm - o * (rs.rows / 256)) * s.tiles_n + tn;  // the tile among the owner's
+    if (o != rs.rank) {
+        if (!(acked >> o & 1u)) {
+            if (threadIdx.x == kEpiThread0)
+                *go = wait_flag(rs.ack[o], epoch - 1u, abort_flag, p.wait_ns, site(2, 8, (uint32_t)o), seg) ? 1 : 0;
+            named_bar_sync(1, 128);
+            const bool ok = *go != 0;
+            named_bar_sync(1, 128);  // `go` is read by all before it is written again
+            if (!ok) return false;
+            acked |= 1u << o;
+        }
+        const int j = rs.rank < o ? rs.rank : rs.rank - 1;
+        const size_t idx = ((size_t)tl * (rs.world - 1) + j) * 2 + pr;
+        float4* slot = reinterpret_cast<float4*>(rs.slots[o] + idx * 128 * 256);
+#pragma unroll 1
+        for (int c0 = 0; c0 < 256; c0 += 16) {
+            uint32_t r[16];
+            tmem_ld16(tbase + (uint32_t)c0, r);
+            tmem_wait_ld();
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+                slot[(size_t)(c0 / 4 + k) * 128 + row] =
+                    make_float4(__uint_as_float(r[4 * k]), __uint_as_float(r[4 * k + 1]), __uint_as_float(r[4 * k + 2]),
+                                __uint_as_float(r[4 * k + 3]));
+        }
+        fence_sys();
+        named_bar_sync(1, 128);
+        if (threadIdx.x == kEpiThread0) st_release_sys(rs.flags[o] + idx, epoch);
+        return true;
+    }
+    // this rank's rows: the others' partials of the tile
+    if (threadIdx.x == kEpiThread0) {
+        bool ok = true;
+        for (int j = 0; j < rs.world - 1 && ok; ++j)
+            ok = wait_flag(rs.flags[o] + ((size_t)tl * (rs.world - 1) + j) * 2 + pr, epoch, abort_flag, p.wait_ns,
+                           site(2, 7, (uint32_t)j), seg);
+        *go = ok ? 1 : 0;
+    }
+    named_bar_sync(1, 128);
+    const bool ok = *go != 0;
+    named_bar_sync(1, 128);
+    if (!ok) return false;
+    const int m_local = tm * 256 + pr * 128 - o * rs.rows;  // the block's first row in this rank's C
+#pragma unroll 1
+    for (int c0 = 0; c0 < 256; c0 += 64) {
+        float v[64];
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+            uint32_t r[16];
+            tmem_ld16(tbase + (uint32_t)(c0 + 16 * h), r);
+            tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 16; ++e) v[16 * h + e] = __uint_as_float(r[e]);
+        }
+        // the sum in rank order: rank 0's partial first, this rank's (v) at its place
+        float acc[64];
+        for (int src = 0; src < rs.world; ++src) {
+            if (src == rs.rank) {
+#pragma unroll
+                for (int e = 0; e < 64; ++e) acc[e] = src == 0 ? v[e] : acc[e] + v[e];
+                continue;
+            }
+            const int j = src < rs.rank ? src : src - 1;
+            const float4* slot = reinterpret_cast<const float4*>(
+                rs.slots[o] + (((size_t)tl * (rs.world - 1) + j) * 2 + pr) * 128 * 256);
+#pragma unroll
+            for (int k = 0; k < 16; ++k) {
+                const float4 w = __ldcg(slot + (size_t)(c0 / 4 + k) * 128 + row);
+                const float x[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) acc[4 * k + e] = src == 0 ? x[e] : acc[4 * k + e] + x[e];
+            }
+        }
+        store_rows64<kEpiF16>(p, m_local + q * 32, tn * 256 + c0, lane, acc);
+    }
+    named_bar_sync(1, 128);
+    if (threadIdx.x == kEpiThread0) {
+        // every rank's tile halves of this rank's rows: 2 per tile
+        const unsigned total = 2u * (unsigned)((rs.rows / 256) * s.tiles_n);
+        __threadfence();
+        if (atomicAdd(rs.count, 1u) == total - 1u) {
+            *rs.count = 0u;
+            __threadfence();
+            st_release_sys(rs.ack[rs.rank], epoch);
+        }
+    }
+    return true;
+}
+
 // ------------------------------------------------------------------ the kernel
 template <int BN, bool SWAP, bool PAIR, int EPI = kEpiF16, int WM = 1>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -490,6 +619,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     constexpr int AN = G::kAccN;  // accumulator columns (TMEM)
     static_assert(!SWAP || EPI == kEpiF16, "fp32 and SwiGLU outputs are written by the TILE and PAIR forms");
     static_assert(EPI != kEpiSwiGLU || BN % 32 == 0, "SwiGLU pairs the two halves of a tile");
+    static_assert(EPI != kEpiRS || (PAIR && BN == 256 && WM == 1), "the fused reduce-scatter runs on pair tiles");
     constexpr int S = G::kStages;
     constexpr int R = G::kRanks;
 #ifdef BW_EMULATE
@@ -749,6 +879,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         Seg sg;
         int acc = 0, seg = 0;
         uint32_t aph = 0;
+        unsigned rs_acked = 0;  // kEpiRS: owners whose ack of the previous call this block has seen
         // the accumulator is read: one arrival per warp on the (leader's) tmem-empty barrier
         auto release_acc = [&](int a) {
             tc_fence_before();
@@ -783,7 +914,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                 n0 = tn * BN;
             }
             const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * AN);
-            if (EPI == kEpiSwiGLU) {
+            if constexpr (EPI == kEpiRS) {
+                int tm, tn;
+                tile_coords(s, sg.tile, tm, tn);
+                rs_tile(p, tm, tn, rank, tbase, row, lane, q, abort_flag, recv_flag, rs_acked, seg);
+                release_acc(acc);
+            } else if (EPI == kEpiSwiGLU) {
                 // a whole tile (the plan splits none): gate columns [0, BN/2), up columns [BN/2, BN) of the tile,
                 // silu(gate) * up to columns [n0 / 2, n0 / 2 + BN / 2) of the M x N/2 output
 #pragma unroll 1

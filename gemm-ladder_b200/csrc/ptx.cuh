@@ -69,6 +69,19 @@ __device__ unsigned int g_status[4];
 
 enum : uint32_t { kStatusTimeout = 3u };
 
+// A wait that gave up: the first one since the host cleared the status word records `where`, the block's abort flag
+// rises.
+__device__ __forceinline__ void record_timeout(volatile int* abort_flag, uint32_t where, int seg)
+{
+    *abort_flag = 1;
+    if (atomicCAS(&g_status[0], 0u, kStatusTimeout) == 0u) {
+        g_status[1] = where;
+        g_status[2] = blockIdx.x;
+        g_status[3] = (unsigned)seg;
+    }
+    __threadfence();
+}
+
 // Spins on (bar, parity) until the phase completes, the block's abort flag rises, or `limit_ns` pass. On a timeout it
 // records `where` and raises the abort flag; returns false on timeout or abort.
 __device__ __noinline__ bool wait_slow(uint32_t bar, uint32_t parity, volatile int* abort_flag, uint64_t limit_ns,
@@ -80,13 +93,7 @@ __device__ __noinline__ bool wait_slow(uint32_t bar, uint32_t parity, volatile i
         if ((i & 31u) == 0) {
             if (*abort_flag) return false;
             if (globaltimer_ns() - t0 > limit_ns) {
-                *abort_flag = 1;
-                if (atomicCAS(&g_status[0], 0u, kStatusTimeout) == 0u) {
-                    g_status[1] = where;
-                    g_status[2] = blockIdx.x;
-                    g_status[3] = (unsigned)seg;
-                }
-                __threadfence();
+                record_timeout(abort_flag, where, seg);
                 return false;
             }
         }
@@ -346,6 +353,40 @@ __device__ __forceinline__ int ld_acquire_gpu(const int* p)
     int v;
     asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
+}
+
+// ------------------------------------------------------------------ system scope: flags in another GPU's memory
+// (reached through a CUDA IPC mapping over NVLink) or in this GPU's memory written by another GPU
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p)
+{
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v)
+{
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+// Orders this thread's earlier stores (to any GPU's memory) before its later ones, at system scope.
+__device__ __forceinline__ void fence_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+
+// Spins until the flag at p reaches `want` (epochs count up from 1; compared modulo 2^32), the block's abort flag
+// rises, or `limit_ns` pass; a timeout is recorded like wait_slow's.  One thread calls it.
+__device__ __noinline__ bool wait_flag(const unsigned* p, unsigned want, volatile int* abort_flag, uint64_t limit_ns,
+                                       uint32_t where, int seg)
+{
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t i = 1;; ++i) {
+        if ((int)(ld_acquire_sys(p) - want) >= 0) return true;
+        if ((i & 15u) == 0) {
+            if (*abort_flag) return false;
+            if (globaltimer_ns() - t0 > limit_ns) {
+                record_timeout(abort_flag, where, seg);
+                return false;
+            }
+            __nanosleep(256);
+        }
+    }
 }
 
 // ------------------------------------------------------------------ named barriers

@@ -40,6 +40,7 @@ struct Sched {
     int group_rows;       // serpentine group height in rows of tiles; 0: row after row
     int ksplit;           // > 0: each tile's K cut in ksplit ranges on the blocks of a cluster of ksplit (one
                           // segment per block); 0: none
+    int row_shift;        // rows of tiles the order is rotated by (the fused reduce-scatter: a rank's own rows last)
 };
 
 // ------------------------------------------------------------------ stream-K bookkeeping
@@ -59,21 +60,22 @@ BW_HD inline int sk_slot(const Sched& s, int cc, int P, int tile)
 
 // ------------------------------------------------------------------ tile order
 // Serpentine order of hopper/step5.cuh:149-163: groups of group_rows rows of tiles, column after column within a
-// group, the odd groups from the last column back.
+// group, the odd groups from the last column back; then the rows rotated by row_shift.
 BW_HD inline void tile_coords(const Sched& s, int t, int& tm, int& tn)
 {
     if (s.group_rows <= 0) {
         tm = t / s.tiles_n;
         tn = t - tm * s.tiles_n;
-        return;
+    } else {
+        const int per = s.group_rows * s.tiles_n;
+        const int g = t / per, r = t - g * per;
+        const int left = s.tiles_m - g * s.group_rows;
+        const int rows = left < s.group_rows ? left : s.group_rows;
+        tm = g * s.group_rows + r % rows;
+        tn = r / rows;
+        if (g & 1) tn = s.tiles_n - 1 - tn;
     }
-    const int per = s.group_rows * s.tiles_n;
-    const int g = t / per, r = t - g * per;
-    const int left = s.tiles_m - g * s.group_rows;
-    const int rows = left < s.group_rows ? left : s.group_rows;
-    tm = g * s.group_rows + r % rows;
-    tn = r / rows;
-    if (g & 1) tn = s.tiles_n - 1 - tn;
+    if (s.row_shift) tm = (tm + s.row_shift) % s.tiles_m;
 }
 
 // ------------------------------------------------------------------ one block's segments

@@ -243,3 +243,124 @@ extern "C" __attribute__((visibility("default"))) int bw_emu_gemm(const void* A,
     if (finding && finding_len > 0) snprintf(finding, (size_t)finding_len, "%s", emu::g_first_finding);
     return rc;
 }
+
+// ------------------------------------------------------------------ the fused reduce-scatter over emulated GPUs
+// `world` emulated GPUs in one process, each with its own region (the layout of csrc/bwgemm.cu's bw_rs) and status
+// word.  Every block of every rank runs at once: an owner's blocks wait for other ranks' blocks.
+namespace bw {
+namespace {
+
+struct EmuRank {
+    std::vector<uint8_t> raw;
+    uint8_t* region = nullptr;
+    RsTable table = {};
+    unsigned status[4] = {0, 0, 0, 0};
+};
+
+size_t align256(size_t v) { return (v + 255) / 256 * 256; }
+
+int launch_rs(const bw_plan& q, int world, std::vector<EmuRank>& ranks, const std::vector<CUtensorMap>& mx,
+              const std::vector<CUtensorMap>& my, const std::vector<Params>& p, int absent)
+{
+    using G = Geom<256, false, true, 1>;
+    if (q.smem_bytes != G::kSmemBytes || q.stages != G::kStages || q.tmem_cols != G::kTmemCols || q.grid % 2) {
+        emu::finding("plan and kernel geometry disagree (reduce-scatter)");
+        return BW_ERR_LAUNCH;
+    }
+    emu::g_smem_limit = q.smem_bytes - 1024;
+    std::vector<std::unique_ptr<emu::Cluster>> clusters;
+    std::vector<std::unique_ptr<emu::Cta>> ctas;
+    std::vector<std::thread> threads;
+    for (int r = 0; r < world; ++r) {
+        if (r == absent) continue;
+        for (int c0 = 0; c0 < q.grid; c0 += 2) {
+            clusters.emplace_back(new emu::Cluster());
+            emu::Cluster* cl = clusters.back().get();
+            cl->size = 2;
+            for (int k = 0; k < 2; ++k) {
+                ctas.emplace_back(new emu::Cta());
+                ctas.back()->rank = k;
+                ctas.back()->cluster = cl;
+                cl->cta[k] = ctas.back().get();
+            }
+            for (int k = 0; k < 2; ++k)
+                for (int t = 0; t < emu::kCtaThreads; ++t)
+                    threads.emplace_back([&, r, c0, k, t, cl] {
+                        emu::t_cta = cl->cta[k];
+                        emu::t_tid = t;
+                        t_status = ranks[r].status;
+                        threadIdx = dim3((unsigned)t);
+                        blockIdx = dim3((unsigned)(c0 + k));
+                        gridDim = dim3((unsigned)q.grid);
+                        blockDim = dim3((unsigned)emu::kCtaThreads);
+                        gemm_kernel<256, false, true, kEpiRS, 1>(mx[r], my[r], p[r]);
+                    });
+        }
+    }
+    for (auto& th : threads) th.join();
+    return BW_OK;
+}
+
+}  // namespace
+}  // namespace bw
+
+// The fused reduce-scatter on `world` emulated GPUs of `sms` SMs each: rank r's C[r] (M / world x N fp16) = its rows
+// of sum_r A[r] B[r], `calls` calls in a row (the epochs and acks of call-to-call reuse); in the last call rank
+// `absent` (-1: none) does not run, as a rank that died between calls.  status: world x 4 words (each rank's status
+// word after the last call).  Returns a BW_* status.
+extern "C" __attribute__((visibility("default"))) int bw_emu_gemm_rs(int world, const void* const* A,
+                                                                     const void* const* B, void* const* C, int M,
+                                                                     int N, int K, int sms, int calls, int absent,
+                                                                     unsigned* status, int* findings, char* finding,
+                                                                     int finding_len)
+{
+    using namespace bw;
+    emu::g_findings = 0;
+    emu::g_first_finding[0] = 0;
+    emu::g_tma_count = 0;
+    if (world < 2 || world > kRsMaxWorld || M % (256 * world) || !shape_ok(M, N, K)) return BW_ERR_SHAPE;
+    bw_plan q = {};
+    int rc = make_plan(M, N, K, sms, sms / 2, 0, &q, kPlanNoSwap | kPlanNoSplit);
+    if (rc) return rc;
+    if (q.kernel != BW_KERNEL_PAIR || q.sk_tiles != 0 || q.bn != 256) return BW_ERR_LAUNCH;
+    // the regions, laid out as bwgemm.cu's bw_rs_create does
+    const int tiles_block = (M / world / 256) * ((N + 255) / 256);
+    const size_t nslots = (size_t)tiles_block * (world - 1) * 2;
+    const size_t flags_off = align256(nslots * 128 * 256 * sizeof(float));
+    const size_t ack_off = align256(flags_off + nslots * sizeof(unsigned));
+    const size_t bytes = ack_off + 256;
+    std::vector<EmuRank> ranks((size_t)world);
+    for (auto& r : ranks) {
+        r.raw.assign(bytes + 256, 0);
+        r.region = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(r.raw.data()) + 255) & ~uintptr_t(255));
+    }
+    for (int r = 0; r < world; ++r) {
+        RsTable& t = ranks[r].table;
+        t.world = world;
+        t.rank = r;
+        t.rows = M / world;
+        for (int o = 0; o < world; ++o) {
+            t.slots[o] = reinterpret_cast<float*>(ranks[o].region);
+            t.flags[o] = reinterpret_cast<unsigned*>(ranks[o].region + flags_off);
+            t.ack[o] = reinterpret_cast<unsigned*>(ranks[o].region + ack_off);
+        }
+        t.count = reinterpret_cast<unsigned*>(ranks[r].region + ack_off) + 1;
+    }
+    std::vector<CUtensorMap> mx((size_t)world), my((size_t)world);
+    std::vector<Params> p((size_t)world);
+    for (int e = 1; e <= calls && rc == BW_OK; ++e) {
+        for (int r = 0; r < world; ++r) {
+            make_maps(q, A[r], B[r], M, N, K, &mx[r], &my[r], false);
+            p[r] = make_params(q, M, N, K, C[r], nullptr, nullptr, false);
+            p[r].s.row_shift = ((r + 1) * (M / world / 256)) % q.tiles_m;
+            p[r].rs = &ranks[r].table;
+            p[r].rs_epoch = (unsigned)e;
+        }
+        rc = launch_rs(q, world, ranks, mx, my, p, e == calls ? absent : -1);
+    }
+    if (status)
+        for (int r = 0; r < world; ++r) std::memcpy(status + 4 * r, ranks[r].status, sizeof ranks[r].status);
+    if (findings) *findings = emu::g_findings.load();
+    if (finding && finding_len > 0) snprintf(finding, (size_t)finding_len, "%s", emu::g_first_finding);
+    return rc;
+}

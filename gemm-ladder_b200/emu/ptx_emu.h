@@ -42,7 +42,20 @@ inline bool mbar_try_wait(uint32_t bar, uint32_t parity)
 }
 
 inline unsigned int g_status[4];
+inline thread_local unsigned int* t_status = g_status;  // the status word of the emulated GPU this thread runs on
 enum : uint32_t { kStatusTimeout = 3u };
+
+inline void record_timeout(volatile int* abort_flag, uint32_t where, int seg)
+{
+    *abort_flag = 1;
+    unsigned expected = 0u;
+    if (__atomic_compare_exchange_n(&t_status[0], &expected, (unsigned)kStatusTimeout, false, __ATOMIC_SEQ_CST,
+                                    __ATOMIC_SEQ_CST)) {
+        t_status[1] = where;
+        t_status[2] = blockIdx.x;
+        t_status[3] = (unsigned)seg;
+    }
+}
 
 // The bounded wait of ptx.cuh, with a yield in the spin so that the other emulated threads run.
 inline bool wait_slow(uint32_t bar, uint32_t parity, volatile int* abort_flag, uint64_t limit_ns, uint32_t where, int seg)
@@ -54,14 +67,28 @@ inline bool wait_slow(uint32_t bar, uint32_t parity, volatile int* abort_flag, u
         if ((i & 31u) == 0) {
             if (*abort_flag) return false;
             if (globaltimer_ns() - t0 > limit_ns) {
-                *abort_flag = 1;
-                unsigned expected = 0u;
-                if (__atomic_compare_exchange_n(&g_status[0], &expected, (unsigned)kStatusTimeout, false,
-                                                __ATOMIC_SEQ_CST, __ATOMIC_SEQ_CST)) {
-                    g_status[1] = where;
-                    g_status[2] = blockIdx.x;
-                    g_status[3] = (unsigned)seg;
-                }
+                record_timeout(abort_flag, where, seg);
+                return false;
+            }
+        }
+    }
+}
+
+// ------------------------------------------------------------------ system scope (the emulated GPUs of one process)
+inline unsigned ld_acquire_sys(const unsigned* p) { return __atomic_load_n(p, __ATOMIC_ACQUIRE); }
+inline void st_release_sys(unsigned* p, unsigned v) { __atomic_store_n(p, v, __ATOMIC_RELEASE); }
+inline void fence_sys() { std::atomic_thread_fence(std::memory_order_seq_cst); }
+inline bool wait_flag(const unsigned* p, unsigned want, volatile int* abort_flag, uint64_t limit_ns, uint32_t where,
+                      int seg)
+{
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t i = 1;; ++i) {
+        if ((int)(ld_acquire_sys(p) - want) >= 0) return true;
+        std::this_thread::yield();
+        if ((i & 15u) == 0) {
+            if (*abort_flag) return false;
+            if (globaltimer_ns() - t0 > limit_ns) {
+                record_timeout(abort_flag, where, seg);
                 return false;
             }
         }

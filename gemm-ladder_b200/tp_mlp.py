@@ -9,7 +9,9 @@ Megatron-style, one rank per GPU, p ranks:
       then H_r is never written;
   down (row-parallel): P_r = A_r W2_r with W2_r = rows [r F/p, (r+1) F/p) of W2 (F x hidden), in fp32 through the
       rung's fp32-output GEMM (bw_gemm_f16_f32out);
-  reduce-scatter (NCCL, sum, fp32): rank r receives rows [r M/p, (r+1) M/p) of Y = sum_r P_r, then rounds them to fp16.
+  reduce-scatter (NCCL, sum, fp32): rank r receives rows [r M/p, (r+1) M/p) of Y = sum_r P_r, then rounds them to fp16;
+      or down and the reduce-scatter in one kernel per rank (bwgemm.ReduceScatterGemm: the partial tiles of the other
+      ranks' rows pushed into their memory, each rank summing its own rows' partials in rank order), no NCCL call.
 
 The GEMMs are parameters so that the sharding and the collective can be tested on CPU ranks (gloo) with a CPU matmul
 in their place; on the GPU they are the rung's (bwgemm.gemm, bwgemm.gemm_f32out).
@@ -66,12 +68,15 @@ class TPMLP:
     """One rank's part of the block.  W1_r, W2_r: this rank's shards (fp16).  gemm(A, B) -> fp16 C = A B;
     gemm_f32(A, B) -> fp32 C = A B; reduce_scatter(out, inp) sums inp over the ranks into out (this rank's rows)."""
 
-    def __init__(self, W1_r, W2_r, rank, world, gemm, gemm_f32, reduce_scatter=None, gemm_swiglu=None):
+    def __init__(self, W1_r, W2_r, rank, world, gemm, gemm_f32, reduce_scatter=None, gemm_swiglu=None,
+                 gemm_rs=None):
         """gemm_swiglu(A, W1_r) -> the activation directly (W1_r then in the interleaved layout of
-        shard_gateup_interleaved): the gateup GEMM with the activation in its epilogue."""
+        shard_gateup_interleaved): the gateup GEMM with the activation in its epilogue.  gemm_rs(A, W2_r) -> this
+        rank's rows of the block's output in fp16: down and the reduce-scatter fused (in place of gemm_f32 and
+        reduce_scatter)."""
         self.W1, self.W2 = W1_r, W2_r
         self.rank, self.world = rank, world
-        self.gemm, self.gemm_f32, self.gemm_swiglu = gemm, gemm_f32, gemm_swiglu
+        self.gemm, self.gemm_f32, self.gemm_swiglu, self.gemm_rs = gemm, gemm_f32, gemm_swiglu, gemm_rs
         self.reduce_scatter = reduce_scatter
         self.fs = W2_r.shape[0]
         if W1_r.shape[1] != 2 * self.fs:
@@ -86,6 +91,8 @@ class TPMLP:
         else:
             H = self.gemm(X, self.W1)                              # M x 2F/p, fp16
             A = (F.silu(H[:, :self.fs].float()) * H[:, self.fs:].float()).to(X.dtype).contiguous()
+        if self.gemm_rs is not None and self.world > 1:
+            return self.gemm_rs(A, self.W2)                        # M/p x hidden, fp16, reduced across the ranks
         P = self.gemm_f32(A, self.W2)                              # M x hidden, fp32 partial sums
         if self.world == 1:
             return P.to(X.dtype)

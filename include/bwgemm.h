@@ -106,6 +106,36 @@ int bw_gemm_dirty(void);
 #define BW_NOALLOC_COUNTERS 4096u            /* split-tile counters */
 int bw_gemm_f16_noalloc(const void* A, const void* B, void* C, int M, int N, int K, void* stream);
 
+/*
+ * The fused reduce-scatter of a row-parallel layer, on `world` GPUs of one node (2 to 8, one process each, the same
+ * M and N everywhere): rank r holds A_r (M x K) and B_r (K x N) and receives C_r, rows [r M/world, (r+1) M/world) of
+ * the sum over the ranks of A_r B_r, in fp16 (M/world x N row-major).  One kernel per rank computes its pair tiles;
+ * a tile of another rank's rows goes as fp32 into that rank's memory over NVLink (its receive slots, reached through
+ * CUDA IPC), and each rank sums the ranks' partials of its own tiles in rank order (bit-for-bit the same on every
+ * run) as they arrive.  No NCCL call: it replaces the fp32-output GEMM + reduce-scatter collective of the tensor-
+ * parallel MLP block (gemm-ladder_b200/tp_mlp.py).  No reference counterpart (the reference runs on one GPU).
+ *
+ *   bw_rs_create     this rank's context and receive region (M % (256 world) == 0), on the current device; the
+ *                    region holds (world - 1) fp32 partials of this rank's rows (bw_rs_region_bytes)
+ *   bw_rs_handle     the region's CUDA IPC handle (BW_RS_HANDLE_BYTES bytes), for the other ranks
+ *   bw_rs_connect    opens the other ranks' regions from all ranks' handles (world x BW_RS_HANDLE_BYTES bytes, in
+ *                    rank order); every rank connects before any rank calls bw_gemm_f16_rs
+ *   bw_gemm_f16_rs   C_r as above, on `stream`; every rank makes the same calls in the same order.  A call waits
+ *                    (bounded) for the other ranks' partials and, before reusing a rank's slots, for that rank to
+ *                    have consumed the previous call's; a rank that never comes ends the others' calls with
+ *                    BW_ERR_TIMEOUT in the status word (site kinds 7 and 8).  Not capturable in a CUDA graph (each
+ *                    call carries its own number).  After a BW_ERR_TIMEOUT destroy the contexts and create new ones.
+ *   bw_rs_destroy    closes the peers' regions and frees this rank's
+ */
+#define BW_RS_HANDLE_BYTES 64
+typedef struct bw_rs bw_rs;
+int bw_rs_create(int M, int N, int world, int rank, bw_rs** out);
+size_t bw_rs_region_bytes(const bw_rs* rs);
+int bw_rs_handle(const bw_rs* rs, void* handle);
+int bw_rs_connect(bw_rs* rs, const void* handles);
+int bw_gemm_f16_rs(bw_rs* rs, const void* A, const void* B, void* C, int K, void* stream);
+int bw_rs_destroy(bw_rs* rs);
+
 /* The plan of one call: the kernel, its tile and its schedule (host only, no GPU needed). */
 typedef struct bw_plan {
     int kernel;          /* BW_KERNEL_TILE or BW_KERNEL_SWAP */
@@ -138,7 +168,9 @@ int bw_gemm_plan(int M, int N, int K, int sms, int variant, bw_plan* out);
 /*
  * The device status word of the current device, after the caller has synchronised: *code = 0, or BW_ERR_TIMEOUT if
  * a bounded wait gave up since the last clear; *site = role << 16 | barrier kind << 8 | index of the first wait that
- * gave up, *block its block, *segment the segment that block was on.  Returns a CUDA error as BW_ERR_LAUNCH.
+ * gave up, *block its block, *segment the segment that block was on.  Kinds: 0 a full stage, 1 an empty stage, 2 a
+ * finished accumulator, 3 a free accumulator, 4 partials copied in, 5 and 6 a K-split cluster's pieces and go signal,
+ * 7 another rank's partial of the fused reduce-scatter (index: the sender), 8 a rank's ack of the previous call.  Returns a CUDA error as BW_ERR_LAUNCH.
  * No reference counterpart as a function: the reference traps in its guarded wait (hopper/step2.cuh:128-145); this
  * rung's waits return instead and leave the context usable.
  */

@@ -21,7 +21,7 @@ static int check(int M, int N, int K, int sms, int variant)
         printf("FAULT %d %d %d sms %d v%d: plan status %d\n", M, N, K, sms, variant, rc);
         return 1;
     }
-    bw::Sched s;
+    bw::Sched s = {};
     s.M = M, s.N = N, s.K = K, s.tiles_m = q.tiles_m, s.tiles_n = q.tiles_n, s.tiles = q.tiles;
     s.kblocks = q.kblocks, s.dp_tiles = q.dp_tiles, s.sk_tiles = q.sk_tiles, s.splits = q.splits;
     s.sk_iters = q.sk_iters, s.group_rows = q.group_rows, s.ksplit = q.ksplit;

@@ -35,6 +35,10 @@ def build_emulator(tmp_path_factory, ksplit):
     L.bw_emu_gemm.restype = i
     L.bw_emu_set.argtypes = [ctypes.c_char_p, ctypes.c_longlong]
     L.bw_emu_set.restype = i
+    pp = ctypes.POINTER(vp)
+    L.bw_emu_gemm_rs.argtypes = [i, pp, pp, pp, i, i, i, i, i, i, ctypes.POINTER(ctypes.c_uint),
+                                 ctypes.POINTER(ctypes.c_int), ctypes.c_char_p, i]
+    L.bw_emu_gemm_rs.restype = i
     return L
 
 
@@ -233,3 +237,76 @@ def test_k_split_rule_on_the_judge_shapes(emu_ksplit):
         q = plan_of(emu_ksplit, M, N, K, 148)
         assert (q["ksplit"], q["wm"]) == want[name], (name, q)
         assert q["grid"] <= 148 and (q["ksplit"] == 0 or q["grid"] == q["ksplit"] * q["tiles"])
+
+
+
+def emulate_rs(L, As, Bs, M, N, K, sms, calls=1, absent=-1):
+    """The fused reduce-scatter on len(As) emulated GPUs: returns (rc, [C_r], statuses, findings, first finding)."""
+    world = len(As)
+    vp = ctypes.c_void_p
+    Cs = [np.full((M // world, N), 0xFFFF, np.uint16) for _ in range(world)]  # fp16 NaN: an unwritten element shows
+    arr = lambda xs: (vp * world)(*[x.ctypes.data for x in xs])  # noqa: E731
+    st = (ctypes.c_uint * (4 * world))()
+    nf = ctypes.c_int()
+    msg = ctypes.create_string_buffer(512)
+    rc = L.bw_emu_gemm_rs(world, arr(As), arr(Bs), arr(Cs), M, N, K, sms, calls, absent, st, ctypes.byref(nf), msg,
+                          512)
+    return rc, Cs, [list(st[4 * r:4 * r + 4]) for r in range(world)], nf.value, msg.value.decode()
+
+
+def rs_inputs(world, M, N, K):
+    As, Bs = [], []
+    for r in range(world):
+        rng = np.random.default_rng(100 + r)
+        As.append(np.ascontiguousarray(rng.uniform(-1, 1, (M, K)).astype(np.float16).view(np.uint16)))
+        Bs.append(np.ascontiguousarray(rng.uniform(-1, 1, (K, N)).astype(np.float16).view(np.uint16)))
+    return As, Bs
+
+
+# (ranks, M, N, K, emulated SMs per GPU, calls in a row)
+RS_FORMS = [
+    (2, 512, 512, 256, 8, 1),   # 2 x 2 pair tiles, each rank owning one row of them
+    (2, 512, 640, 320, 8, 3),   # a last tile of 128 columns; three calls reuse the slots (epochs, acks)
+    (4, 1024, 384, 192, 4, 2),  # four ranks on two pairs of SMs each
+]
+
+
+@pytest.mark.parametrize("form", RS_FORMS, ids=lambda f: f"w{f[0]}_{f[1]}x{f[2]}x{f[3]}_calls{f[5]}")
+def test_fused_reduce_scatter_over_emulated_gpus(emu, oracle_mod, form):
+    """Each rank's C is its rows of the sum over the ranks of A_r B_r: partials pushed into the owners' slots, summed
+    there in rank order, within the GPU tests' gates of the fp64 sum; every status word clear."""
+    world, M, N, K, sms, calls = form
+    As, Bs = rs_inputs(world, M, N, K)
+    rc, Cs, status, nf, msg = emulate_rs(emu, As, Bs, M, N, K, sms, calls)
+    assert rc == 0 and nf == 0, f"rc {rc}, {nf} findings, first: {msg}"
+    assert all(s_[0] == 0 for s_ in status), status
+    ref = sum(oracle_mod.gemm_f64(As[r], Bs[r]) for r in range(world))
+    rows = M // world
+    for r in range(world):
+        res = oracle_mod.check(Cs[r], ref[r * rows:(r + 1) * rows], world * K)
+        assert res["nonfinite"] == 0 and res["violations"] == 0 and res["normwise"] <= 2e-3, (r, res)
+
+
+def test_fused_reduce_scatter_is_the_same_bits_every_call(emu):
+    world, M, N, K = 2, 512, 512, 256
+    As, Bs = rs_inputs(world, M, N, K)
+    once = emulate_rs(emu, As, Bs, M, N, K, 8, calls=1)[1]
+    thrice = emulate_rs(emu, As, Bs, M, N, K, 8, calls=3)[1]
+    assert all(np.array_equal(a, b) for a, b in zip(once, thrice))
+
+
+@pytest.mark.parametrize("absent", [0, 1])
+def test_fused_reduce_scatter_without_a_rank_ends_with_a_status(emu, absent):
+    """A rank that does not come to the second call: the others' bounded waits for its partials (kind 7) give up, their
+    status words say so, and every block of every other rank leaves."""
+    world, M, N, K = 2, 512, 512, 256
+    As, Bs = rs_inputs(world, M, N, K)
+    emu.bw_emu_set(b"wait_ns", 300_000_000)
+    try:
+        rc, Cs, status, nf, msg = emulate_rs(emu, As, Bs, M, N, K, 8, calls=2, absent=absent)
+    finally:
+        emu.bw_emu_set(b"wait_ns", 60_000_000_000)
+    assert rc == 0 and nf == 0, f"{nf} findings, first: {msg}"
+    other = 1 - absent
+    code, where = status[other][0], status[other][1]
+    assert code == 3 and where >> 16 == 2 and (where >> 8) & 0xFF in (7, 8), status

@@ -33,6 +33,14 @@ def _reduce_scatter_gloo(out, inp):
     out.copy_(full[dist.get_rank() * rows:(dist.get_rank() + 1) * rows])
 
 
+def _gemm_rs_gloo(A, B):
+    """A CPU stand-in for the fused down + reduce-scatter (bw_gemm_f16_rs): this rank's rows of sum_r A_r B_r, fp16."""
+    P = A.float() @ B.float()
+    out = torch.empty((P.shape[0] // dist.get_world_size(), P.shape[1]), dtype=torch.float32)
+    _reduce_scatter_gloo(out, P)
+    return out.to(A.dtype)
+
+
 def _reference(X, W1, W2):
     f = W2.shape[0]
     H = _gemm(X, W1)
@@ -40,7 +48,7 @@ def _reference(X, W1, W2):
     return (A.float() @ W2.float())
 
 
-def _worker(rank, world, port, M, hidden, f, q, fused=False):
+def _worker(rank, world, port, M, hidden, f, q, mode="unfused"):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
@@ -48,11 +56,13 @@ def _worker(rank, world, port, M, hidden, f, q, fused=False):
         X = (torch.rand(M, hidden, generator=g) * 2 - 1).half()
         W1 = ((torch.rand(hidden, 2 * f, generator=g) * 2 - 1) / hidden ** 0.5).half()
         W2 = ((torch.rand(f, hidden, generator=g) * 2 - 1) / f ** 0.5).half()
-        if fused:  # the interleaved layout, a CPU stand-in for the fused GEMM
+        if mode != "unfused":  # the interleaved layout, a CPU stand-in for the fused GEMM
             blk = tp_mlp.TPMLP(tp_mlp.shard_gateup_interleaved(W1, rank, world, group=16),
-                               tp_mlp.shard_down(W2, rank, world), rank, world, _gemm, _gemm_f32,
-                               _reduce_scatter_gloo,
-                               gemm_swiglu=lambda A, W: tp_mlp.swiglu_reference(A, W, group=16))
+                               tp_mlp.shard_down(W2, rank, world), rank, world, _gemm,
+                               None if mode == "fused_rs" else _gemm_f32,
+                               None if mode == "fused_rs" else _reduce_scatter_gloo,
+                               gemm_swiglu=lambda A, W: tp_mlp.swiglu_reference(A, W, group=16),
+                               gemm_rs=_gemm_rs_gloo if mode == "fused_rs" else None)
         else:
             blk = tp_mlp.TPMLP(tp_mlp.shard_gateup(W1, rank, world), tp_mlp.shard_down(W2, rank, world), rank,
                                world, _gemm, _gemm_f32, _reduce_scatter_gloo)
@@ -64,14 +74,16 @@ def _worker(rank, world, port, M, hidden, f, q, fused=False):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("fused", [False, True], ids=["unfused", "fused"])
+@pytest.mark.parametrize("mode", ["unfused", "fused", "fused_rs"])
 @pytest.mark.parametrize("world", [2])
-def test_tp_mlp_over_two_cpu_ranks_equals_the_whole_block(world, fused):
+def test_tp_mlp_over_two_cpu_ranks_equals_the_whole_block(world, mode):
+    """unfused: gateup, the activation, down in fp32 and a reduce-scatter; fused: the activation in the gateup GEMM;
+    fused_rs: also down and the reduce-scatter in one call (no separate collective)."""
     M, hidden, f = 32, 64, 96
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, M, hidden, f, q, fused)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, M, hidden, f, q, mode)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
