@@ -60,6 +60,11 @@
 #define BW_TMA3D 1             // the MN-major operand's 64-column boxes of a stage in one 3-D TMA load (0: one 2-D
                                // load per box; measured: the swap-AB shapes 0.5-3 % faster, the pair shapes even)
 #endif
+#ifndef BW_SK_PART_WAVE
+#define BW_SK_PART_WAVE 0      // stream-K over every pair when the tiles make more than half a wave but not a whole one
+                               // (o and down at M = 512: 64 tiles on 74 pairs leave 10 idle; run on the host emulator,
+                               // not yet measured)
+#endif
 #ifndef BW_KSPLIT
 #define BW_KSPLIT 0            // swap-AB K cut over the blocks of a cluster: 0, halves on clusters of two, the second
                                // block's sum added by the first (measured on the B200); 1, clusters of 2 to
@@ -215,7 +220,8 @@ inline int make_plan(int M, int N, int K, int sms, int pairs, int variant, bw_pl
     }
     q.tiles = q.tiles_m * q.tiles_n;
     const long long kb = q.kblocks;
-    const bool one_wave = BW_SK_ONE_WAVE && !swap && q.tiles > units && q.tiles < 2 * units;
+    const bool one_wave = (BW_SK_ONE_WAVE && !swap && q.tiles > units && q.tiles < 2 * units) ||
+                          (BW_SK_PART_WAVE && !swap && 2 * q.tiles > units && q.tiles < units);
     const bool stream_k = swap ? variant != 1 : variant == 4 || (variant == 0 && one_wave);
     // swap-AB with every tile at once on clusters of blocks, each block one equal K range of its tile, the blocks'
     // sums added through distributed shared memory (no partials in memory, no counters).  BW_KSPLIT 0: clusters of

@@ -21,12 +21,12 @@ PKG = os.path.join(ROOT, "gemm-ladder_b200")
 CUDA_INCLUDE = os.path.join(os.environ.get("CUDA_HOME", "/usr/local/cuda"), "include")
 
 
-def build_emulator(tmp_path_factory, ksplit):
+def build_emulator(tmp_path_factory, defines=()):
     if not os.path.isdir(CUDA_INCLUDE):
         pytest.skip("no CUDA headers")
-    lib = str(tmp_path_factory.mktemp("emu") / f"libbwemu{ksplit}.so")
-    subprocess.check_call(["g++", "-std=c++20", "-O2", "-pthread", "-DBW_EMULATE", f"-DBW_KSPLIT={ksplit}", "-fPIC",
-                           "-shared", "-w", f"-I{CUDA_INCLUDE}", f"-I{os.path.join(ROOT, 'include')}",
+    lib = str(tmp_path_factory.mktemp("emu") / "libbwemu.so")
+    subprocess.check_call(["g++", "-std=c++20", "-O2", "-pthread", "-DBW_EMULATE", *[f"-D{d}" for d in defines],
+                           "-fPIC", "-shared", "-w", f"-I{CUDA_INCLUDE}", f"-I{os.path.join(ROOT, 'include')}",
                            f"-I{os.path.join(PKG, 'csrc')}", os.path.join(PKG, "emu", "emu.cpp"), "-o", lib])
     L = ctypes.CDLL(lib)
     vp, i = ctypes.c_void_p, ctypes.c_int
@@ -45,13 +45,14 @@ def build_emulator(tmp_path_factory, ksplit):
 @pytest.fixture(scope="module")
 def emu(tmp_path_factory):
     """The kernel as the library builds it."""
-    return build_emulator(tmp_path_factory, 0)
+    return build_emulator(tmp_path_factory)
 
 
 @pytest.fixture(scope="module")
 def emu_ksplit(tmp_path_factory):
-    """The kernel with the K split over clusters of 2 to 8 blocks (BW_KSPLIT 1)."""
-    return build_emulator(tmp_path_factory, 1)
+    """The kernel and rule with the options built but not yet measured on a B200: the K split over clusters of 2 to 8
+    blocks (BW_KSPLIT 1) and stream-K over a part wave of pair tiles (BW_SK_PART_WAVE 1)."""
+    return build_emulator(tmp_path_factory, ("BW_KSPLIT=1", "BW_SK_PART_WAVE=1"))
 
 
 def plan_of(L, M, N, K, sms, variant=0):
@@ -310,3 +311,23 @@ def test_fused_reduce_scatter_without_a_rank_ends_with_a_status(emu, absent):
     other = 1 - absent
     code, where = status[other][0], status[other][1]
     assert code == 3 and where >> 16 == 2 and (where >> 8) & 0xFF in (7, 8), status
+
+
+
+@pytest.mark.parametrize("shape", [(512, 768, 512, 16), (256, 768, 640, 8), (384, 704, 320, 16)],
+                         ids=lambda s: "x".join(map(str, s[:3])))
+@pytest.mark.parametrize("tn", [False, True], ids=["KxN", "NxK"])
+def test_stream_k_over_a_part_wave_of_pair_tiles(emu_ksplit, oracle_mod, shape, tn):
+    """BW_SK_PART_WAVE 1: pair tiles that fill more than half of the pairs but not all of them are cut evenly over every
+    pair (stream-K, dp_tiles 0) instead of leaving pairs idle."""
+    M, N, K, sms = shape
+    q = plan_of(emu_ksplit, M, N, K, sms)
+    pairs = sms // 2
+    assert q["kernel"] == 2 and pairs < 2 * q["tiles"] and q["tiles"] < pairs, q
+    assert q["dp_tiles"] == 0 and q["sk_tiles"] == q["tiles"] and q["grid"] == sms, q
+    A, B = oracle_mod.lcg_inputs(M, N, K)
+    rc, C, status, dirty, nf, msg = emulate(emu_ksplit, A, B, M, N, K, sms, tn=tn)
+    assert rc == 0 and nf == 0, f"rc {rc}, {nf} findings, first: {msg}"
+    assert status[0] == 0 and dirty == 0, (status, dirty)
+    r = oracle_mod.check(C, oracle_mod.gemm_f64(A, B), K)
+    assert r["nonfinite"] == 0 and r["violations"] == 0 and r["normwise"] <= 2e-3, r

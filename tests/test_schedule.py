@@ -11,11 +11,12 @@ ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(ROOT, "gemm-ladder_b200", "csrc")
 
 
-@pytest.fixture(scope="module", params=[0, 1], ids=["ksplit2", "ksplit2to8"])
+@pytest.fixture(scope="module", params=[(), ("BW_KSPLIT=1", "BW_SK_PART_WAVE=1")], ids=["library", "not_yet_measured"])
 def checker(request, tmp_path_factory):
-    """The checker over the library's rule (BW_KSPLIT 0) and over the K split on clusters of 2 to 8 (BW_KSPLIT 1)."""
+    """The checker over the library's rule, and over the rule with the options built but not yet measured (the K split
+    on clusters of 2 to 8, stream-K over a part wave of pair tiles)."""
     exe = str(tmp_path_factory.mktemp("sched") / "schedule_check")
-    subprocess.check_call(["g++", "-std=c++17", "-O2", "-Wall", f"-DBW_KSPLIT={request.param}", f"-I{CSRC}",
+    subprocess.check_call(["g++", "-std=c++17", "-O2", "-Wall", *[f"-D{d}" for d in request.param], f"-I{CSRC}",
                            f"-I{os.path.join(ROOT, 'include')}", os.path.join(HERE, "schedule_check.cpp"), "-o", exe])
     return exe
 
