@@ -1,6 +1,8 @@
 """Build the rung's native code in-tree: gemm-ladder_b200/lib/libbwgemm.so (sm_100a, cross-compiled by nvcc; no GPU
-needed).  ``python gemm-ladder_b200/build.py [--force] [--trace]``; --trace builds lib/libbwgemm_trace.so, the same
-library with the per-block timeline compiled in (-DBW_TRACE, read by timeline.py)."""
+needed).  ``python gemm-ladder_b200/build.py [--force] [--trace] [--next]``; --trace builds lib/libbwgemm_trace.so,
+the same library with the per-block timeline compiled in (-DBW_TRACE, read by timeline.py); --next builds
+lib/libbwgemm_next.so, the library with the options built but not yet measured on a B200 (the K split over clusters
+of 2 to 8, stream-K over a part wave of pair tiles), for A/B runs: BWGEMM_LIB=libbwgemm_next.so selects it."""
 import os
 import shutil
 import subprocess
@@ -12,6 +14,8 @@ CSRC = os.path.join(HERE, "csrc")
 LIB_DIR = os.path.join(HERE, "lib")
 LIB = os.path.join(LIB_DIR, "libbwgemm.so")
 TRACE_LIB = os.path.join(LIB_DIR, "libbwgemm_trace.so")
+NEXT_LIB = os.path.join(LIB_DIR, "libbwgemm_next.so")
+NEXT_DEFINES = ["-DBW_KSPLIT=1", "-DBW_SK_PART_WAVE=1"]
 INCLUDE = os.path.join(ROOT, "include")
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -41,14 +45,15 @@ def up_to_date(lib=LIB):
     return all(os.path.getmtime(s) <= t for s in sources())
 
 
-def build(force=False, verbose=False, trace=False):
-    """Compile libbwgemm.so (trace: libbwgemm_trace.so) if a source is newer than it (or force)."""
-    lib = TRACE_LIB if trace else LIB
+def build(force=False, verbose=False, trace=False, next_options=False):
+    """Compile libbwgemm.so (trace: libbwgemm_trace.so; next_options: libbwgemm_next.so) if a source is newer than it
+    (or force)."""
+    lib = TRACE_LIB if trace else NEXT_LIB if next_options else LIB
     if not force and up_to_date(lib):
         return lib
     os.makedirs(LIB_DIR, exist_ok=True)
-    cmd = [nvcc(), *NVCC_FLAGS, *(["-DBW_TRACE"] if trace else []), os.path.join(CSRC, "bwgemm.cu"), "-o",
-           lib + ".tmp"]
+    defines = (["-DBW_TRACE"] if trace else []) + (NEXT_DEFINES if next_options else [])
+    cmd = [nvcc(), *NVCC_FLAGS, *defines, os.path.join(CSRC, "bwgemm.cu"), "-o", lib + ".tmp"]
     if verbose:
         print(" ".join(cmd))
     subprocess.check_call(cmd)
@@ -57,4 +62,5 @@ def build(force=False, verbose=False, trace=False):
 
 
 if __name__ == "__main__":
-    print(build(force="--force" in sys.argv, verbose=True, trace="--trace" in sys.argv))
+    print(build(force="--force" in sys.argv, verbose=True, trace="--trace" in sys.argv,
+                next_options="--next" in sys.argv))

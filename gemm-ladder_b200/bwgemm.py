@@ -12,7 +12,8 @@ import os
 import re
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(HERE, "lib", "libbwgemm.so")
+# BWGEMM_LIB picks another build of the library in lib/ (e.g. libbwgemm_next.so from build.py --next), or a path
+LIB_PATH = os.path.join(HERE, "lib", os.environ.get("BWGEMM_LIB") or "libbwgemm.so")
 HEADER = os.path.join(os.path.dirname(HERE), "include", "bwgemm.h")
 
 BW_OK, BW_ERR_SHAPE, BW_ERR_LAUNCH, BW_ERR_TIMEOUT, BW_ERR_ARG, BW_ERR_DEVICE = 0, 1, 2, 3, 4, 5
