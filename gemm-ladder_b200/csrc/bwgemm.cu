@@ -260,6 +260,9 @@ int dispatch(DeviceState& d, const bw_plan& q, const CUtensorMap& mx, const CUte
             return launch_kernel<256, false, false, kEpiSwiGLU>(d, 1u << 15, q, mx, my, p, st);
         return BW_ERR_ARG;
     }
+#if BW_PAIR_WIDE
+    if (q.kernel == BW_KERNEL_PAIR && q.bn == 512) return launch_kernel<512, false, true>(d, 1u << 25, q, mx, my, p, st);
+#endif
     if (q.kernel == BW_KERNEL_PAIR) return launch_kernel<256, false, true>(d, kBitPair, q, mx, my, p, st);
     if (q.kernel == BW_KERNEL_TILE) {
         switch (q.bn) {
@@ -326,15 +329,15 @@ bool make_maps(const bw_plan& q, const void* A, const void* B, int M, int N, int
                bool tn = false)
 {
     if (tn) {  // B is N x K row-major: K-major boxes of 64 K x (the rows of B one stage takes), as A's
-        if (q.kernel == BW_KERNEL_TILE || q.kernel == BW_KERNEL_PAIR)
+        if (q.kernel == BW_KERNEL_TILE || q.kernel == BW_KERNEL_PAIR)  // a pair block loads 128 rows per MMA
             return make_map(mx, A, K, M, 64, 128) &&
-                   make_map(my, B, K, N, 64, (uint32_t)(q.kernel == BW_KERNEL_PAIR ? q.bn / 2 : q.bn));
+                   make_map(my, B, K, N, 64, (uint32_t)(q.kernel == BW_KERNEL_PAIR ? 128 : q.bn));
         return make_map(mx, B, K, N, 64, (uint32_t)(128 * q.wm)) && make_map(my, A, K, M, 64, q.bn);
     }
     if (BW_TMA3D) {  // the stage's 64-column blocks of B in one load
         if (q.kernel == BW_KERNEL_TILE || q.kernel == BW_KERNEL_PAIR)
             return make_map(mx, A, K, M, 64, 128) &&
-                   make_map_blocks(my, B, N, K, (uint32_t)(q.bn / (q.kernel == BW_KERNEL_PAIR ? 128 : 64)));
+                   make_map_blocks(my, B, N, K, (uint32_t)(q.kernel == BW_KERNEL_PAIR ? 2 : q.bn / 64));
         return make_map_blocks(mx, B, N, K, (uint32_t)(2 * q.wm)) && make_map(my, A, K, M, 64, q.bn);
     }
     if (q.kernel == BW_KERNEL_TILE || q.kernel == BW_KERNEL_PAIR)
@@ -555,8 +558,11 @@ int noalloc_gemm(const void* A, const void* B, void* C, int M, int N, int K, cud
             return q.workspace_bytes <= BW_NOALLOC_SCRATCH_BYTES && (unsigned)q.counters <= BW_NOALLOC_COUNTERS;
         };
         if ((rc = make_plan(M, N, K, d->sms, d->pairs, 0, &q, 0u, held_of(*d)))) return rc;
-        // the 256-column swap tiles' partials are twice as large: 128-column tiles if those fit the array
-        if (!fits() && q.wm > 1 && (rc = make_plan(M, N, K, d->sms, d->pairs, 0, &q, kPlanNarrow, held_of(*d)))) return rc;
+        // 256-column swap tiles' (and 512-column pair tiles') partials are twice as large: the narrower tiles if
+        // those fit the array
+        if (!fits() && (q.wm > 1 || q.bn > 256) &&
+            (rc = make_plan(M, N, K, d->sms, d->pairs, 0, &q, kPlanNarrow, held_of(*d))))
+            return rc;
         if (!fits()) {
             snprintf(g_errbuf, sizeof g_errbuf,
                      "%d x %d x %d needs %zu bytes of partials and %d counters; the fixed array holds %u and %u", M, N,

@@ -109,13 +109,17 @@ struct Geom {
     static constexpr int kTileM = PAIR ? 256 : 128;          // rows of C per tile (TILE, PAIR)
     static constexpr int kAccN = WM * BN;                    // TMEM columns of one accumulator (SWAP: WM weight
                                                              // blocks of 128 columns, BN tokens each)
+    static constexpr int kWN = PAIR && BN > 256 ? BN / 256 : 1;  // PAIR: MMAs of N = 256 across a 512-column tile
+    static constexpr int kMmaN = BN / kWN;                       // N of one MMA
+    static constexpr int kBPart = BN / kRanks / kWN;             // this block's B columns per MMA (PAIR: 128)
     static constexpr int kXBytes = 128 * WM * kBK * 2;       // this block's MMA-A operand: 128 (x WM) rows x 64 K
     static constexpr int kYBytes = (BN / kRanks) * kBK * 2;  // this block's MMA-B operand: BN (PAIR: BN / 2) x 64 K
     static constexpr int kStageBytes = kXBytes + kYBytes;
     static constexpr int kCStageBytes = SWAP ? 2 * 16 * 128 * 2 : 0;  // swap-AB epilogue transpose buffers
     static constexpr int kRingFit = (BW_SMEM_LIMIT - 1024 - 512 - kCStageBytes) / kStageBytes;
     static constexpr int kStages = kRingFit < BW_MAX_STAGES ? kRingFit : BW_MAX_STAGES;
-    static constexpr int kTmemCols = pow2_at_least(2 * kAccN < 32 ? 32 : 2 * kAccN, 32);  // two accumulators
+    static constexpr int kAccBufs = 2 * kAccN <= 512 ? 2 : 1;  // two accumulators, or one of 512 columns
+    static constexpr int kTmemCols = pow2_at_least(kAccBufs * kAccN < 32 ? 32 : kAccBufs * kAccN, 32);
     static constexpr int kBarOffset = kStages * kStageBytes;
     static constexpr int kNumBars = 2 * kStages + 8;  // full, empty, tmem full x2, tmem empty x2, drain, reduce,
                                                       // and the K split's go / receive
@@ -126,7 +130,8 @@ struct Geom {
     // swap-AB: the epilogue transposes each 16-column chunk through two 16 x 128 fp16 buffers
     static constexpr int kCStageOffset = (kMiscOffset + 32 + 127) / 128 * 128;
     static constexpr int kSmemBytes = 1024 + kCStageOffset + kCStageBytes;  // + slack to align the stages to 1024 B
-    static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "MMA N: a multiple of 16 in [16, 256]");
+    static_assert(BN % 16 == 0 && BN >= 16 && (BN <= 256 || (PAIR && BN == 512 && WM == 1)),
+                  "MMA N: a multiple of 16 in [16, 256] (pair tiles of 512 columns: two MMAs of 256)");
     static_assert(SWAP || BN % (64 * kRanks) == 0, "B tiles are boxes of 64 columns (per block)");
     static_assert(!(SWAP && PAIR), "the swap-AB form runs on single blocks");
     static_assert(WM == 1 || (SWAP && WM == 2), "two weight blocks per tile: swap-AB only");
@@ -730,17 +735,22 @@ __global__ void __launch_bounds__(kThreads, 1)
                         // A: 64 K x 128 rows (this block's rows of a pair tile)
                         load_tile<PAIR, BW_HINT_A>(sx, &tmx, kb * kBK, tm * G::kTileM + rank * 128, &full[stage], barc,
                                                    pol_a);
-                        if (p.tn) {  // B (N x K): this block's BN / R rows of B, 64 K each, one load
-                            load_tile<PAIR, BW_HINT_B>(sy, &tmy, kb * kBK, tn * BN + rank * (BN / R), &full[stage],
-                                                       barc, pol_b);
-                        } else if (BW_TMA3D) {  // B: this block's BN / R columns, one load
-                            load_blocks<PAIR, BW_HINT_B>(sy, &tmy, (tn * BN + rank * (BN / R)) / 64, kb * kBK,
-                                                         &full[stage], barc, pol_b);
-                        } else {
+                        // B: this block's kBPart columns of each MMA's 256 (w: a wide pair tile's MMA), so that
+                        // accumulator column c is tile column c
 #pragma unroll
-                            for (int j = 0; j < BN / (64 * R); ++j)  // B: this block's BN / R columns, 64 x 64 K boxes
-                                load_tile<PAIR, BW_HINT_B>(sy + j * 8192, &tmy, tn * BN + rank * (BN / R) + 64 * j,
-                                                           kb * kBK, &full[stage], barc, pol_b);
+                        for (int w = 0; w < G::kWN; ++w) {
+                            uint8_t* syw = sy + w * G::kBPart * kBK * 2;
+                            const int n = tn * BN + w * 256 + rank * G::kBPart;
+                            if (p.tn) {  // B (N x K): kBPart rows of B, 64 K each, one load
+                                load_tile<PAIR, BW_HINT_B>(syw, &tmy, kb * kBK, n, &full[stage], barc, pol_b);
+                            } else if (BW_TMA3D) {  // B: kBPart columns, one load
+                                load_blocks<PAIR, BW_HINT_B>(syw, &tmy, n / 64, kb * kBK, &full[stage], barc, pol_b);
+                            } else {
+#pragma unroll
+                                for (int j = 0; j < G::kBPart / 64; ++j)  // B: kBPart columns, 64 x 64 K boxes
+                                    load_tile<PAIR, BW_HINT_B>(syw + j * 8192, &tmy, n + 64 * j, kb * kBK,
+                                                               &full[stage], barc, pol_b);
+                            }
                         }
                     } else {
                         if (p.tn) {  // B (N x K): 128 (x WM) rows of B, 64 K each, one load
@@ -777,8 +787,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         // ---------------------------------------------------------- MMA issuer (one thread; the leader of a pair)
         if (lane == 0 && leader) {
             // B (the MMA's A operand in swap-AB) is MN-major when K x N, K-major when N x K (p.tn)
-            constexpr uint32_t idesc_nn = idesc_f16_f32(PAIR ? 256 : 128, BN, SWAP, !SWAP);
-            constexpr uint32_t idesc_tn = idesc_f16_f32(PAIR ? 256 : 128, BN, false, false);
+            constexpr uint32_t idesc_nn = idesc_f16_f32(PAIR ? 256 : 128, G::kMmaN, SWAP, !SWAP);
+            constexpr uint32_t idesc_tn = idesc_f16_f32(PAIR ? 256 : 128, G::kMmaN, false, false);
             const uint32_t idesc = p.tn ? idesc_tn : idesc_nn;
             const bool bk = p.tn != 0;
             SegIter it(s, c, P);
@@ -819,16 +829,20 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const uint32_t sx = smem_u32(smem + stage * G::kStageBytes), sy = sx + G::kXBytes;
 #pragma unroll
                     for (int k = 0; k < kBK / 16; ++k) {
-                        const uint64_t bd = (SWAP || bk) ? desc_kmajor(sy, k) : desc_mnmajor(sy, k);
                         const uint32_t accumulate = (kb > sg.k0 || k > 0) ? 1u : 0u;
+                        // SWAP: each 128-column weight block of A into its BN columns; a wide pair tile: each
+                        // 256-column part of B into its columns
 #pragma unroll
-                        for (int w = 0; w < WM; ++w) {  // SWAP: each 128-column weight block into its columns
-                            const uint32_t xw = sx + (uint32_t)(w * 128 * kBK * 2);
+                        for (int w = 0; w < WM * G::kWN; ++w) {
+                            const uint32_t xw = sx + (uint32_t)((SWAP ? w : 0) * 128 * kBK * 2);
+                            const uint32_t yw = sy + (uint32_t)((SWAP ? 0 : w) * G::kBPart * kBK * 2);
                             const uint64_t ad = (SWAP && !bk) ? desc_mnmajor(xw, k) : desc_kmajor(xw, k);
+                            const uint64_t bd = (SWAP || bk) ? desc_kmajor(yw, k) : desc_mnmajor(yw, k);
+                            const uint32_t dw = d + (uint32_t)(w * (SWAP ? BN : G::kMmaN));
                             if (PAIR)
-                                mma_f16_pair(d, ad, bd, idesc, accumulate);
+                                mma_f16_pair(dw, ad, bd, idesc, accumulate);
                             else
-                                mma_f16(d + (uint32_t)(w * BN), ad, bd, idesc, accumulate);
+                                mma_f16(dw, ad, bd, idesc, accumulate);
                         }
                     }
                     // the stage is free (in both blocks of a pair) once these MMAs have read it
@@ -851,7 +865,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 } else {
                     mma_commit(&tfull[acc]);
                 }
-                if (++acc == 2) {
+                if (++acc == G::kAccBufs) {
                     acc = 0;
                     aph ^= 1u;
                 }
@@ -1184,7 +1198,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 named_bar_sync(1, 128);  // reduce_flag is read by all before the next segment writes it
             }
-            if (++acc == 2) {
+            if (++acc == G::kAccBufs) {
                 acc = 0;
                 aph ^= 1u;
             }

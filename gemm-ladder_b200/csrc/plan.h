@@ -60,6 +60,12 @@
 #define BW_TMA3D 1             // the MN-major operand's 64-column boxes of a stage in one 3-D TMA load (0: one 2-D
                                // load per box; measured: the swap-AB shapes 0.5-3 % faster, the pair shapes even)
 #endif
+#ifndef BW_PAIR_WIDE
+#define BW_PAIR_WIDE 0         // pair tiles of 256 x 512 (two MMAs of N = 256 per K step into one 512-column accumulator)
+                               // where they make a whole wave at least: a block takes in 48 KB per K-block for twice
+                               // the math of the 32 KB of a 256 x 256 tile; its epilogue is no longer hidden (run on the
+                               // host emulator; not yet measured)
+#endif
 #ifndef BW_SK_PART_WAVE
 #define BW_SK_PART_WAVE 0      // stream-K over every pair when the tiles make more than half a wave but not a whole one
                                // (o and down at M = 512: 64 tiles on 74 pairs leave 10 idle; run on the host emulator,
@@ -117,10 +123,12 @@ inline int plan_stages(int bn, int ranks, bool swap, int wm = 1)
     const int s = (BW_SMEM_LIMIT - 1024 - 512 - plan_cstage_bytes(swap)) / plan_stage_bytes(bn, ranks, wm);
     return s < BW_MAX_STAGES ? s : BW_MAX_STAGES;
 }
-inline int plan_tmem_cols(int bn)
+// Tensor-memory columns for accumulators of acc_n columns: two of them, or one of 512.
+inline int plan_tmem_cols(int acc_n)
 {
+    const int need = 2 * acc_n <= 512 ? 2 * acc_n : acc_n;
     int c = 32;
-    while (c < 2 * bn) c *= 2;
+    while (c < need) c *= 2;
     return c;
 }
 inline int plan_smem_bytes(int bn, int ranks, bool swap, int wm = 1)
@@ -187,7 +195,7 @@ inline int tail_splits(int tail, int P, int kblocks, double fixup_kb)
 enum : unsigned {
     kPlanNoSwap = 1u,   // A is the MMA's A operand (fp32 and fused outputs are written by TILE and PAIR only)
     kPlanNoSplit = 2u,  // whole tiles only (a fused epilogue needs the complete sums)
-    kPlanNarrow = 4u,   // swap-AB tiles of 128 weight columns only (half the partials' scratch)
+    kPlanNarrow = 4u,   // swap-AB tiles of 128 weight columns, pair tiles of 256 (half the partials' scratch)
 };
 
 // sms: the SMs; pairs: the pairs of SMs the pair kernel can hold at once (its cluster occupancy); held (BW_KSPLIT 1,
@@ -215,6 +223,10 @@ inline int make_plan(int M, int N, int K, int sms, int pairs, int variant, bw_pl
         ranks = pair ? 2 : 1;
         units = pair ? pairs : sms;
         q.tiles_m = (M + 128 * ranks - 1) / (128 * ranks);
+        // pair tiles of 512 columns for the fp16 entries, where they still make a whole wave
+        if (BW_PAIR_WIDE && pair && (variant == 0 || variant == 3) && !(flags & (kPlanNoSwap | kPlanNarrow)) &&
+            N > 256 && q.tiles_m * ((N + 511) / 512) >= units)
+            q.bn = 512;
         q.tiles_n = (N + q.bn - 1) / q.bn;
         q.group_rows = variant == 3 ? 0 : BW_GROUP_ROWS;
     }

@@ -46,7 +46,7 @@ void make_maps(const bw_plan& q, const void* A, const void* B, int M, int N, int
     if (tn) {
         if (ab) {
             map2(mx, A, K, M, 64, 128);
-            map2(my, B, K, N, 64, (uint32_t)(q.kernel == BW_KERNEL_PAIR ? q.bn / 2 : q.bn));
+            map2(my, B, K, N, 64, (uint32_t)(q.kernel == BW_KERNEL_PAIR ? 128 : q.bn));
         } else {
             map2(mx, B, K, N, 64, (uint32_t)(128 * q.wm));
             map2(my, A, K, M, 64, (uint32_t)q.bn);
@@ -56,7 +56,7 @@ void make_maps(const bw_plan& q, const void* A, const void* B, int M, int N, int
     if (BW_TMA3D) {
         if (ab) {
             map2(mx, A, K, M, 64, 128);
-            map_blocks(my, B, N, K, (uint32_t)(q.bn / (q.kernel == BW_KERNEL_PAIR ? 128 : 64)));
+            map_blocks(my, B, N, K, (uint32_t)(q.kernel == BW_KERNEL_PAIR ? 2 : q.bn / 64));
         } else {
             map_blocks(mx, B, N, K, (uint32_t)(2 * q.wm));
             map2(my, A, K, M, 64, (uint32_t)q.bn);
@@ -155,6 +155,9 @@ int dispatch(const bw_plan& q, const CUtensorMap& mx, const CUtensorMap& my, con
         if (q.kernel == BW_KERNEL_TILE && q.bn == 256) return launch<256, false, false, kEpiSwiGLU, 1>(q, mx, my, p);
         return BW_ERR_ARG;
     }
+#if BW_PAIR_WIDE
+    if (q.kernel == BW_KERNEL_PAIR && q.bn == 512) return launch<512, false, true, kEpiF16, 1>(q, mx, my, p);
+#endif
     if (q.kernel == BW_KERNEL_PAIR) return launch<256, false, true, kEpiF16, 1>(q, mx, my, p);
     if (q.kernel == BW_KERNEL_TILE) {
         switch (q.bn) {

@@ -50,9 +50,10 @@ def emu(tmp_path_factory):
 
 @pytest.fixture(scope="module")
 def emu_ksplit(tmp_path_factory):
-    """The kernel and rule with the options built but not yet measured on a B200: the K split over clusters of 2 to 8
-    blocks (BW_KSPLIT 1) and stream-K over a part wave of pair tiles (BW_SK_PART_WAVE 1)."""
-    return build_emulator(tmp_path_factory, ("BW_KSPLIT=1", "BW_SK_PART_WAVE=1"))
+    """The kernel and rule with the options built but not yet measured on a B200 (build.py --next): the K split over
+    clusters of 2 to 8 blocks (BW_KSPLIT 1), stream-K over a part wave of pair tiles (BW_SK_PART_WAVE 1), pair tiles of
+    256 x 512 (BW_PAIR_WIDE 1)."""
+    return build_emulator(tmp_path_factory, ("BW_KSPLIT=1", "BW_SK_PART_WAVE=1", "BW_PAIR_WIDE=1"))
 
 
 def plan_of(L, M, N, K, sms, variant=0):
@@ -325,6 +326,32 @@ def test_stream_k_over_a_part_wave_of_pair_tiles(emu_ksplit, oracle_mod, shape, 
     pairs = sms // 2
     assert q["kernel"] == 2 and pairs < 2 * q["tiles"] and q["tiles"] < pairs, q
     assert q["dp_tiles"] == 0 and q["sk_tiles"] == q["tiles"] and q["grid"] == sms, q
+    A, B = oracle_mod.lcg_inputs(M, N, K)
+    rc, C, status, dirty, nf, msg = emulate(emu_ksplit, A, B, M, N, K, sms, tn=tn)
+    assert rc == 0 and nf == 0, f"rc {rc}, {nf} findings, first: {msg}"
+    assert status[0] == 0 and dirty == 0, (status, dirty)
+    r = oracle_mod.check(C, oracle_mod.gemm_f64(A, B), K)
+    assert r["nonfinite"] == 0 and r["violations"] == 0 and r["normwise"] <= 2e-3, r
+
+
+
+# (M, N, K, emulated SMs, what the BW_PAIR_WIDE 1 rule takes there)
+WIDE_FORMS = [
+    (512, 1024, 512, 8, "2 x 2 tiles of 256 x 512 on 4 pairs, one wave"),
+    (256, 2048, 256, 8, "1 x 4 wide tiles"),
+    (768, 1536, 512, 8, "3 x 3 wide tiles: two waves and a part, the accumulator reused tile after tile"),
+    (384, 1280, 320, 8, "2 x 3 wide tiles, the last rows and 256 columns beyond C: stream-K over one wave and a part"),
+]
+
+
+@pytest.mark.parametrize("form", WIDE_FORMS, ids=lambda f: f"{f[0]}x{f[1]}x{f[2]}")
+@pytest.mark.parametrize("tn", [False, True], ids=["KxN", "NxK"])
+def test_pair_tiles_of_512_columns(emu_ksplit, oracle_mod, form, tn):
+    """BW_PAIR_WIDE 1: two MMAs of N = 256 per K step on each stage (this block's 128 columns of each), one
+    512-column accumulator whose column c is the tile's column c."""
+    M, N, K, sms, _ = form
+    q = plan_of(emu_ksplit, M, N, K, sms)
+    assert q["kernel"] == 2 and q["bn"] == 512 and q["tmem_cols"] == 512, q
     A, B = oracle_mod.lcg_inputs(M, N, K)
     rc, C, status, dirty, nf, msg = emulate(emu_ksplit, A, B, M, N, K, sms, tn=tn)
     assert rc == 0 and nf == 0, f"rc {rc}, {nf} findings, first: {msg}"

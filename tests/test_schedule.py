@@ -11,7 +11,8 @@ ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(ROOT, "gemm-ladder_b200", "csrc")
 
 
-@pytest.fixture(scope="module", params=[(), ("BW_KSPLIT=1", "BW_SK_PART_WAVE=1")], ids=["library", "not_yet_measured"])
+@pytest.fixture(scope="module", params=[(), ("BW_KSPLIT=1", "BW_SK_PART_WAVE=1", "BW_PAIR_WIDE=1")],
+                ids=["library", "not_yet_measured"])
 def checker(request, tmp_path_factory):
     """The checker over the library's rule, and over the rule with the options built but not yet measured (the K split
     on clusters of 2 to 8, stream-K over a part wave of pair tiles)."""
