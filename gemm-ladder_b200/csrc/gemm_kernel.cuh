@@ -3,8 +3,9 @@
 //
 // One persistent block per SM (PAIR: one block pair per two SMs), 6 warps with fixed roles:
 //   warp 0      TMA producer: fills a ring of shared-memory stages (full / empty mbarriers).
-//   warp 1      allocates tensor memory; one thread issues tcgen05.mma into one of two accumulators and commits
-//               each stage back to the producer and each finished segment to the epilogue.
+//   warp 1      allocates tensor memory; one thread issues tcgen05.mma into one of two accumulators (one, for a
+//               512-column pair tile) and commits each stage back to the producer and each finished segment to the
+//               epilogue.
 //   warps 2-5   epilogue: tcgen05.ld of the accumulator (warp w reads TMEM lanes 32 (w % 4) .. +31), fp32 -> fp16
 //               round-to-nearest, stores to C (TILE / PAIR: whole lines after an in-warp transpose; SWAP: through a
 //               shared-memory transpose); the accumulator is released as soon as it is read, so the next tile's MMA
@@ -16,7 +17,8 @@
 //   PAIR  (SWAP = false, PAIR = true)   MMA 256 x BN x 16 on a cluster of two blocks (cta_group::2): each block loads
 //         its own 128 rows of A and BN / 2 columns of B, the leader block issues the MMA that reads both blocks'
 //         shared memory, each block's tensor memory holds its 128 rows x BN.  Per SM the operand traffic of a
-//         256 x 256 tile is that of a 128 x 128 tile.
+//         256 x 256 tile is that of a 128 x 128 tile.  BN = 512 (BW_PAIR_WIDE): two MMAs of N = 256 per K step, each
+//         block holding 128 columns of each, so that accumulator column c is tile column c.
 //   SWAP  (SWAP = true)   for M <= 128: C^T = B^T A^T.  MMA-A = 128 columns of B (MN-major), MMA-B = the M rows of A
 //         (K-major, BN = M rounded up to 16).  TMEM lane = column of C, TMEM column = row of C.  The weights fill the
 //         128-row MMA dimension whatever the number of tokens.  WM = 2: tiles of 256 weight columns, two MMAs on each
@@ -28,6 +30,8 @@
 // memory (st.async into idle stage rings) and added in a fixed order: BW_KSPLIT 0, halves on clusters of two, the
 // second block's sum added by the first; BW_KSPLIT 1, clusters of 2 to 8, each block summing its own run of the
 // accumulator's 16-column chunks.
+// Outputs (EPI): fp16 C; fp32 C; the SwiGLU activation of a gate / up tile; or the fused reduce-scatter of a
+// row-parallel layer (kEpiRS: partial tiles of other ranks' rows pushed into their memory, this rank's rows summed).
 // Every wait on a barrier is bounded (ptx.cuh, wait_bounded): a stalled pipeline ends the kernel with an error status
 // instead of hanging the GPU.
 #pragma once
