@@ -34,6 +34,21 @@ int main(void)
     CHECK(bw_gemm_variant_count() >= 1 && bw_gemm_variant_name(0) != NULL);
     CHECK(bw_gemm_variant_name(-1) == NULL);
     CHECK(strlen(bw_status_string(BW_ERR_TIMEOUT)) > 0);
+    /* the fused reduce-scatter's context: bad ranks and shapes refused first; without a GPU no context is made */
+    {
+        bw_rs* rs = (bw_rs*)&p; /* not NULL: a refused create must set it to NULL */
+        unsigned char handle[BW_RS_HANDLE_BYTES];
+        CHECK(bw_rs_create(512, 512, 1, 0, &rs) == BW_ERR_ARG && rs == NULL);
+        CHECK(bw_rs_create(512, 512, 2, 2, &rs) == BW_ERR_ARG && rs == NULL);
+        CHECK(bw_rs_create(512, 512, 9, 0, &rs) == BW_ERR_ARG);
+        CHECK(bw_rs_create(768, 512, 2, 0, &rs) == BW_ERR_SHAPE); /* M % (256 world) != 0 */
+        CHECK(bw_rs_create(512, 500, 2, 0, &rs) == BW_ERR_SHAPE);
+        CHECK(bw_rs_create(512, 512, 2, 0, NULL) == BW_ERR_ARG);
+        CHECK(bw_rs_create(512, 512, 2, 0, &rs) != BW_OK && rs == NULL); /* no device here */
+        CHECK(bw_gemm_f16_rs(NULL, (const void*)16, (const void*)16, (void*)16, 64, NULL) == BW_ERR_ARG);
+        CHECK(bw_rs_handle(NULL, handle) == BW_ERR_ARG && bw_rs_connect(NULL, handle) == BW_ERR_ARG);
+        CHECK(bw_rs_region_bytes(NULL) == 0 && bw_rs_destroy(NULL) == BW_OK);
+    }
     printf("bw_plan size %zu kernel %zu bn %zu stages %zu tiles_m %zu tiles_n %zu tiles %zu kblocks %zu grid %zu "
            "dp_tiles %zu sk_tiles %zu splits %zu sk_iters %zu group_rows %zu workspace_bytes %zu counters %zu "
            "smem_bytes %zu tmem_cols %zu ksplit %zu wm %zu\n",
