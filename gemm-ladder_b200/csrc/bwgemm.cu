@@ -641,8 +641,15 @@ int rs_gemm(bw_rs* rs, const void* A, const void* B, void* C, int K, cudaStream_
         snprintf(g_errbuf, sizeof g_errbuf, "the reduce-scatter context is not connected (bw_rs_connect)");
         return BW_ERR_ARG;
     }
+    cudaStreamCaptureStatus capture = cudaStreamCaptureStatusNone;
+    cudaError_t e = cudaStreamIsCapturing(st, &capture);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaStreamIsCapturing");
+    if (capture != cudaStreamCaptureStatusNone) {  // a replay would reuse this call's epoch
+        snprintf(g_errbuf, sizeof g_errbuf, "the fused reduce-scatter cannot be captured in a CUDA graph");
+        return BW_ERR_ARG;
+    }
     int dev = -1;
-    cudaError_t e = cudaGetDevice(&dev);
+    e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
     if (dev != rs->dev) {
         snprintf(g_errbuf, sizeof g_errbuf, "the reduce-scatter context belongs to device %d", rs->dev);
