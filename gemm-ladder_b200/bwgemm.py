@@ -266,8 +266,8 @@ class ReduceScatterGemm:
 
     Every rank of `group` constructs it with the same M and N (its receive region's CUDA IPC handle is exchanged with
     all_gather_object, then every rank opens the others' and a barrier follows), and calls it with the same shapes in
-    the same order.  Not capturable in a CUDA graph.  After a BW_ERR_TIMEOUT (another rank never came), close it and
-    make a new one."""
+    the same order.  Capturable in a CUDA graph (every rank then replays the same graphs).  After a BW_ERR_TIMEOUT
+    (another rank never came), close it and make a new one."""
 
     def __init__(self, M, N, group=None):
         import torch.distributed as dist

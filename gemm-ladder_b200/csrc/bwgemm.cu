@@ -618,7 +618,6 @@ struct bw_rs {
     size_t flags_off, ack_off, table_off, bytes;  // offsets in a region; its size
     uint8_t* region;                     // this rank's
     uint8_t* peer[bw::kRsMaxWorld];      // every rank's region in this process (this rank's own: region)
-    unsigned epoch;                      // calls made
     bool connected;                      // the table is written
 };
 
@@ -641,15 +640,8 @@ int rs_gemm(bw_rs* rs, const void* A, const void* B, void* C, int K, cudaStream_
         snprintf(g_errbuf, sizeof g_errbuf, "the reduce-scatter context is not connected (bw_rs_connect)");
         return BW_ERR_ARG;
     }
-    cudaStreamCaptureStatus capture = cudaStreamCaptureStatusNone;
-    cudaError_t e = cudaStreamIsCapturing(st, &capture);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaStreamIsCapturing");
-    if (capture != cudaStreamCaptureStatusNone) {  // a replay would reuse this call's epoch
-        snprintf(g_errbuf, sizeof g_errbuf, "the fused reduce-scatter cannot be captured in a CUDA graph");
-        return BW_ERR_ARG;
-    }
     int dev = -1;
-    e = cudaGetDevice(&dev);
+    cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
     if (dev != rs->dev) {
         snprintf(g_errbuf, sizeof g_errbuf, "the reduce-scatter context belongs to device %d", rs->dev);
@@ -676,10 +668,7 @@ int rs_gemm(bw_rs* rs, const void* A, const void* B, void* C, int K, cudaStream_
     Params p = make_params(q, M, N, K, C, nullptr, nullptr);
     p.s.row_shift = ((rs->rank + 1) * (rs->M / rs->world / 256)) % q.tiles_m;  // this rank's own rows last
     p.rs = reinterpret_cast<const RsTable*>(rs->region + rs->table_off);
-    p.rs_epoch = rs->epoch + 1u;
-    rc = launch_kernel<256, false, true, kEpiRS>(*d, 1u << 24, q, mx, my, p, st);
-    if (rc == BW_OK) rs->epoch = p.rs_epoch;
-    return rc;
+    return launch_kernel<256, false, true, kEpiRS>(*d, 1u << 24, q, mx, my, p, st);
 }
 
 }  // namespace
@@ -707,7 +696,7 @@ BW_API int bw_rs_create(int M, int N, int world, int rank, bw_rs** out)
     const size_t nslots = (size_t)rs->tiles_block * (world - 1) * 2;
     rs->flags_off = align_up(nslots * 128 * 256 * sizeof(float), 256);
     rs->ack_off = align_up(rs->flags_off + nslots * sizeof(unsigned), 256);
-    rs->table_off = rs->ack_off + 256;  // the ack word, then the count; then the table
+    rs->table_off = rs->ack_off + 256;  // the ack, count, epoch and done words; then the table
     rs->bytes = align_up(rs->table_off + sizeof(RsTable), 256);
     if ((e = cudaMalloc(reinterpret_cast<void**>(&rs->region), rs->bytes)) != cudaSuccess ||
         (e = cudaMemset(rs->region, 0, rs->bytes)) != cudaSuccess) {
@@ -755,6 +744,8 @@ BW_API int bw_rs_connect(bw_rs* rs, const void* handles)
         t.ack[o] = reinterpret_cast<unsigned*>(rs->peer[o] + rs->ack_off);
     }
     t.count = reinterpret_cast<unsigned*>(rs->region + rs->ack_off) + 1;
+    t.epoch = reinterpret_cast<unsigned*>(rs->region + rs->ack_off) + 2;
+    t.done = reinterpret_cast<unsigned*>(rs->region + rs->ack_off) + 3;
     cudaError_t e = cudaMemcpy(rs->region + rs->table_off, &t, sizeof t, cudaMemcpyHostToDevice);
     if (e != cudaSuccess) return bw::cuda_fail(e, "cudaMemcpy (reduce-scatter table)");
     rs->connected = true;

@@ -67,8 +67,10 @@ constexpr int kRsMaxWorld = 8;
 //   flags  one per slot: the epoch of the call whose partial it holds
 //   ack    the last epoch whose slots o has consumed (a sender waits for epoch - 1 before writing)
 //   count  tile halves o has consumed in this call
-// The table lives in this rank's device memory (written once, when the ranks connect); a call passes its address
-// and its epoch.
+//   epoch  o's calls so far: every block of a call reads it at entry (the call's epoch is one more), the call's last
+//          block to finish advances it, so a call replayed from a CUDA graph carries a new epoch each time
+//   done   blocks of the current call that have finished
+// The table lives in this rank's device memory (written once, when the ranks connect); a call passes its address.
 struct RsTable {
     int world, rank;                 // ranks; this one
     int rows;                        // rows of C per owner (M / world, a multiple of 256)
@@ -76,6 +78,8 @@ struct RsTable {
     unsigned* flags[kRsMaxWorld];    // owner o's flags
     unsigned* ack[kRsMaxWorld];      // owner o's ack word
     unsigned* count;                 // this rank's count
+    unsigned* epoch;                 // this rank's epoch word
+    unsigned* done;                  // this rank's finished-block count
 };
 
 struct Params {
@@ -86,7 +90,6 @@ struct Params {
     unsigned long long wait_ns;  // the limit of any single wait on a barrier
     int tn;                      // 1: B is N x K row-major (K-major for the tensor core, like A); 0: K x N
     const RsTable* rs;           // kEpiRS only: the ranks' regions
-    unsigned rs_epoch;           // kEpiRS only: this call's number (from 1)
 };
 
 __host__ __device__ constexpr int pow2_at_least(int v, int p) { return p >= v ? p : pow2_at_least(v, 2 * p); }
@@ -523,11 +526,11 @@ __device__ __noinline__ bool reduce_tile_bulk(const Params& p, int P, int tile, 
 // flags for the tile, then the sum in rank order (this rank's own partial from tensor memory) rounded to fp16 into C,
 // then a count; the block that consumes the call's last tile half acks the epoch.  Every wait is bounded; one thread
 // waits and hands the outcome to the other 127 through `go`.  Returns false after a wait gave up.
-__device__ __noinline__ bool rs_tile(const Params& p, int tm, int tn, int pr, uint32_t tbase, int row, int lane,
-                                     int q, volatile int* abort_flag, volatile int* go, unsigned& acked, int seg)
+__device__ __noinline__ bool rs_tile(const Params& p, unsigned epoch, int tm, int tn, int pr, uint32_t tbase, int row,
+                                     int lane, int q, volatile int* abort_flag, volatile int* go, unsigned& acked,
+                                     int seg)
 {
     const RsTable& rs = *p.rs;
-    const unsigned epoch = p.rs_epoch;
     const Sched& s = p.s;
     const int o = tm * 256 / rs.rows;                        // the owner of the tile's rows
     const int tl = (tm - o * (rs.rows / 256)) * s.tiles_n + tn;  // the tile among the owner's
@@ -898,6 +901,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         int acc = 0, seg = 0;
         uint32_t aph = 0;
         unsigned rs_acked = 0;  // kEpiRS: owners whose ack of the previous call this block has seen
+        // kEpiRS: this call's epoch (the rank's epoch word moves on only once every block has finished, below)
+        unsigned rs_epoch = 0u;
+        if constexpr (EPI == kEpiRS) rs_epoch = *static_cast<volatile unsigned*>(p.rs->epoch) + 1u;
         // the accumulator is read: one arrival per warp on the (leader's) tmem-empty barrier
         auto release_acc = [&](int a) {
             tc_fence_before();
@@ -935,7 +941,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             if constexpr (EPI == kEpiRS) {
                 int tm, tn;
                 tile_coords(s, sg.tile, tm, tn);
-                rs_tile(p, tm, tn, rank, tbase, row, lane, q, abort_flag, recv_flag, rs_acked, seg);
+                rs_tile(p, rs_epoch, tm, tn, rank, tbase, row, lane, q, abort_flag, recv_flag, rs_acked, seg);
                 release_acc(acc);
             } else if (EPI == kEpiSwiGLU) {
                 // a whole tile (the plan splits none): gate columns [0, BN/2), up columns [BN/2, BN) of the tile,
@@ -1207,6 +1213,19 @@ __global__ void __launch_bounds__(kThreads, 1)
                 aph ^= 1u;
             }
             ++seg;
+        }
+        if constexpr (EPI == kEpiRS) {
+            // the call's last block to finish moves the rank's epoch word on; every block read it at entry (this
+            // block's 128 threads have all passed that read at this barrier)
+            named_bar_sync(1, 128);
+            if (threadIdx.x == kEpiThread0) {
+                __threadfence();
+                if (atomicAdd(p.rs->done, 1u) == gridDim.x - 1u) {
+                    *p.rs->done = 0u;
+                    __threadfence();
+                    *static_cast<volatile unsigned*>(p.rs->epoch) = rs_epoch;
+                }
+            }
         }
         if (threadIdx.x == kEpiThread0) BW_TRACE_AT(4);
     }

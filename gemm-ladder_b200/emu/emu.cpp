@@ -348,6 +348,8 @@ extern "C" __attribute__((visibility("default"))) int bw_emu_gemm_rs(int world, 
             t.ack[o] = reinterpret_cast<unsigned*>(ranks[o].region + ack_off);
         }
         t.count = reinterpret_cast<unsigned*>(ranks[r].region + ack_off) + 1;
+        t.epoch = reinterpret_cast<unsigned*>(ranks[r].region + ack_off) + 2;
+        t.done = reinterpret_cast<unsigned*>(ranks[r].region + ack_off) + 3;
     }
     std::vector<CUtensorMap> mx((size_t)world), my((size_t)world);
     std::vector<Params> p((size_t)world);
@@ -357,7 +359,6 @@ extern "C" __attribute__((visibility("default"))) int bw_emu_gemm_rs(int world, 
             p[r] = make_params(q, M, N, K, C[r], nullptr, nullptr, false);
             p[r].s.row_shift = ((r + 1) * (M / world / 256)) % q.tiles_m;
             p[r].rs = &ranks[r].table;
-            p[r].rs_epoch = (unsigned)e;
         }
         rc = launch_rs(q, world, ranks, mx, my, p, e == calls ? absent : -1);
     }

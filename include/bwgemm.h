@@ -123,8 +123,9 @@ int bw_gemm_f16_noalloc(const void* A, const void* B, void* C, int M, int N, int
  *   bw_gemm_f16_rs   C_r as above, on `stream`; every rank makes the same calls in the same order.  A call waits
  *                    (bounded) for the other ranks' partials and, before reusing a rank's slots, for that rank to
  *                    have consumed the previous call's; a rank that never comes ends the others' calls with
- *                    BW_ERR_TIMEOUT in the status word (site kinds 7 and 8).  Not capturable in a CUDA graph (each
- *                    call carries its own number).  After a BW_ERR_TIMEOUT destroy the contexts and create new ones.
+ *                    BW_ERR_TIMEOUT in the status word (site kinds 7 and 8).  Capturable in a CUDA graph (each call
+ *                    takes its number from the device, so every replay is a new call); every rank replays the same
+ *                    calls.  After a BW_ERR_TIMEOUT destroy the contexts and create new ones.
  *   bw_rs_destroy    closes the peers' regions and frees this rank's
  */
 #define BW_RS_HANDLE_BYTES 64

@@ -1,7 +1,8 @@
 """The fused reduce-scatter (bw_gemm_f16_rs, bwgemm.ReduceScatterGemm) on two or four GPUs, one child process per
 rank, NVLS off: each rank's rows of sum_r A_r B_r against an fp32 reference (torch matmul per rank, an NCCL all-reduce),
 under the judge's tolerance; three calls in a row give the same bits (the receive slots reused through the epochs and
-acks); every rank's status word clear.
+acks); the call captured in a CUDA graph and replayed twice gives the same bits again (its epoch comes from the
+device); every rank's status word clear.
 
 The fused kernel has run on the host emulator only so far (tests/test_emulator.py); until it has run on B200s these
 tests also want BW_TEST_FUSED_RS=1.  Skipped with fewer GPUs than ranks."""
@@ -42,6 +43,16 @@ def _worker(rank, world, port, M, N, K, q):
         for _ in range(3):
             outs.append(rs(A, B).clone())
         torch.cuda.synchronize()
+        C = torch.empty_like(outs[0])
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            rs(A, B, C)
+        for _ in range(2):  # every rank replays the same calls
+            C.fill_(float("nan"))
+            graph.replay()
+            torch.cuda.synchronize()
+            outs.append(C.clone())
+        del graph
         code = bwgemm.status()[0]
         ref = A.float() @ B.float()
         dist.all_reduce(ref)
