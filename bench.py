@@ -22,8 +22,11 @@ harness needs its judge, which needs CUDA 13) timed on the host cores on the sam
 
 --workload tp_mlp: the tensor-parallel MLP block of gemm-ladder_b200/tp_mlp.py over the ranks
 (--tp-m tokens, 8192 or 2048; --tp-unfused for the activation as separate torch ops; --tp-fused-rs for down and the
-reduce-scatter in one kernel per rank, bw_gemm_f16_rs), total work fixed: strong scaling.  --shape MxNxK times any shape in place of the workload.  --profile-arm {ours,cublas}: one call of either
-arm inside an NVTX range "timed" (3 warm-up calls before it), no JSON line: the command for ncu's --nvtx-include.
+reduce-scatter in one kernel per rank, bw_gemm_f16_rs), total work fixed: strong scaling.  --shape MxNxK times any
+shape in place of the workload.  --profile-arm {ours,cublas}: one call of either arm inside an NVTX range "timed" (3
+warm-up calls before it), no JSON line: the command for ncu's --nvtx-include.  BWGEMM_LIB=libbwgemm_next.so runs any
+of these on the library with the options not yet measured (gemm-ladder_b200/build.py --next); config.library says
+which library a line comes from.
 """
 import argparse
 import datetime
@@ -394,6 +397,7 @@ def run_tp_mlp(args):
             "data": "synthetic: seeded uniform tokens and weights",
             "config": {"workload": f"tp_mlp M={M} hidden={hidden} mlp={f}", "M": M, "parallelism": f"tp{world}",
                        "activation": "separate torch ops" if args.tp_unfused else "fused in the gateup epilogue",
+                       "library": os.path.basename(bwgemm.LIB_PATH),
                        "collective": ("fused: partial tiles pushed into the owners' memory in the down GEMM's kernel"
                                       if rs is not None else "NCCL reduce-scatter of fp32 partials")
                        if world > 1 else "none"},
@@ -547,7 +551,7 @@ def run_ours(args):
         "dtype": "fp16 (fp32 accumulate)", "data": "synthetic: seeded uniform [-1, 1) fp16",
         "config": {"workload": f"{args.workload} {M}x{N}x{K}" + (f" per rank (column shards, N total {N * world})"
                                                                   if world > 1 else ""),
-                   "M": M, "N": N, "K": K, "variant": args.variant,
+                   "M": M, "N": N, "K": K, "variant": args.variant, "library": os.path.basename(bwgemm.LIB_PATH),
                    "l2": "3 rotating input sets (%.0f MB) > 126 MB L2, no flush" % (3 * (M * K + K * N) * 2 / 1e6),
                    "parallelism": f"column shards x{world}, no collective" if world > 1 else "1 GPU"},
         "clocks": clk.summary(), "gpu_launches": args.steps, "device_status": code,
