@@ -62,9 +62,18 @@
 #endif
 #ifndef BW_PAIR_WIDE
 #define BW_PAIR_WIDE 0         // pair tiles of 256 x 512 (two MMAs of N = 256 per K step into one 512-column accumulator)
-                               // where they make a whole wave at least: a block takes in 48 KB per K-block for twice
-                               // the math of the 32 KB of a 256 x 256 tile; its epilogue is no longer hidden (run on the
-                               // host emulator; not yet measured)
+                               // where their estimated time beats the 256 x 256 tiles' (pair_time): a block takes in
+                               // 48 KB per K-block for twice the math of the 32 KB of a 256 x 256 tile; its epilogue is
+                               // no longer hidden (run on the host emulator; not yet measured)
+#endif
+#ifndef BW_PAIR_KB_NS
+#define BW_PAIR_KB_NS 409.0        // a 256 x 256 pair tile's K-block (measured: its intake-bound mainloop at 1965 MHz)
+#endif
+#ifndef BW_PAIR_WIDE_KB_NS
+#define BW_PAIR_WIDE_KB_NS 748.0   // a 256 x 512 one's: twice the MMA time of the measured cuBLAS peak (an estimate)
+#endif
+#ifndef BW_PAIR_WIDE_EPI_NS
+#define BW_PAIR_WIDE_EPI_NS 2000.0 // the 256 x 512 tile's epilogue, exposed once per wave (an estimate)
 #endif
 #ifndef BW_SK_PART_WAVE
 #define BW_SK_PART_WAVE 0      // stream-K over every pair when the tiles make more than half a wave but not a whole one
@@ -176,7 +185,7 @@ inline bool shape_ok(int M, int N, int K)
 
 // The split-K factor for a tail of `tail` tiles on P blocks: minimises the tail's time in tile-times,
 // ceil(tail s / P) / s, plus the reduction of s partials (each about fixup_kb K-blocks of work for the last block).
-inline int tail_splits(int tail, int P, int kblocks, double fixup_kb)
+inline int tail_splits(int tail, int P, int kblocks, double fixup_kb, double* cost_out = nullptr)
 {
     int best = 1;
     double best_cost = 1.0;
@@ -188,7 +197,31 @@ inline int tail_splits(int tail, int P, int kblocks, double fixup_kb)
             best = sp;
         }
     }
+    if (cost_out) *cost_out = best_cost;
     return best;
+}
+
+// BW_PAIR_WIDE: the estimated time (ns) of `tiles` pair tiles of `bn` columns on `units` pairs, as the rule below
+// schedules them: whole waves, then stream-K over one wave and a part (even shares plus one fix-up) or the split-K tail
+// at tail_splits' cost; each wave at kblocks K-blocks of the tile's measured or estimated time, and the 512-column
+// tile's exposed epilogue once per wave.
+inline double pair_time(int tiles, int units, int kblocks, int bn)
+{
+    const double fixup_kb = BW_FIXUP_KB * bn / 256;
+    double waves;
+    if (tiles % units == 0) {
+        waves = tiles / units;
+    } else if ((BW_SK_ONE_WAVE && tiles > units && tiles < 2 * units) ||
+               (BW_SK_PART_WAVE && 2 * tiles > units && tiles < units)) {
+        waves = (double)tiles / units + fixup_kb / kblocks;
+    } else {
+        double tail = 1.0;
+        tail_splits(tiles % units, units, kblocks, fixup_kb, &tail);
+        waves = tiles / units + tail;
+    }
+    const bool wide = bn > 256;
+    return waves * kblocks * (wide ? BW_PAIR_WIDE_KB_NS : BW_PAIR_KB_NS) +
+           (wide ? (double)((tiles + units - 1) / units) * BW_PAIR_WIDE_EPI_NS : 0.0);
 }
 
 // Plan constraints of the entries that need them (on top of the variant).
@@ -223,9 +256,11 @@ inline int make_plan(int M, int N, int K, int sms, int pairs, int variant, bw_pl
         ranks = pair ? 2 : 1;
         units = pair ? pairs : sms;
         q.tiles_m = (M + 128 * ranks - 1) / (128 * ranks);
-        // pair tiles of 512 columns for the fp16 entries, where they still make a whole wave
+        // pair tiles of 512 columns for the fp16 entries, where their estimated time is 2 % below the 256-column ones'
         if (BW_PAIR_WIDE && pair && (variant == 0 || variant == 3) && !(flags & (kPlanNoSwap | kPlanNarrow)) &&
-            N > 256 && q.tiles_m * ((N + 511) / 512) >= units)
+            N > 256 && units > 0 &&
+            pair_time(q.tiles_m * ((N + 511) / 512), units, q.kblocks, 512) <
+                0.98 * pair_time(q.tiles_m * ((N + 255) / 256), units, q.kblocks, 256))
             q.bn = 512;
         q.tiles_n = (N + q.bn - 1) / q.bn;
         q.group_rows = variant == 3 ? 0 : BW_GROUP_ROWS;
