@@ -7,7 +7,7 @@
 //              - if every tile's two K halves fit the SMs at once (clusters of two), each half on one block and the
 //                two sums added through distributed shared memory (ksplit = 2), with tiles of 128 weight columns,
 //                else of 256 (wm = 2, two MMAs on each stage of A) if those fit (BW_KSPLIT 1: K cut over clusters
-//                of 2 to 8 blocks, the cluster size and tile width that stream on the most SMs);
+//                of 2 to 8 blocks, the cluster size and tile width of the least estimated time, ksplit_cost);
 //              - otherwise the K-blocks of all tiles cut evenly over the SMs (stream-K), with tiles of 256 weight
 //                columns from 64 tokens while they outnumber the SMs (A is re-read from L2 once per tile).
 //   M > 128    256 x 256 tiles on pairs of SMs (BW_KERNEL_PAIR, tcgen05 cta_group::2), persistent: per SM the
@@ -15,13 +15,15 @@
 //              round-robin (data-parallel); the tiles of the last, partial wave are split in K into `splits` ranges
 //              (split-K) when that fills the pairs better than leaving them idle, the cost of each extra partial
 //              included -- or, when the tiles make one wave and a part, all of them are cut evenly (stream-K).
+//              Options built but not yet measured: stream-K also over a part wave (BW_SK_PART_WAVE 1), and pair tiles
+//              of 256 x 512 where their estimated time is lower (BW_PAIR_WIDE 1, pair_time).
 // Variants take one mechanism out each, for ablations (the reference's g_var, hopper/step7.cu:1-11).
 #pragma once
 #include <cstddef>
 #include "bwgemm.h"
 #include "schedule.h"
 
-// Tuning constants (compile-time; measured on the B200, see the profiles).
+// Tuning constants (compile-time; measured on the B200 unless marked as estimates).
 #ifndef BW_GROUP_ROWS
 #define BW_GROUP_ROWS 8        // rows of tiles per serpentine group (8 vs 16: -20 % DRAM reads at 8192^3)
 #endif
