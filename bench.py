@@ -249,9 +249,16 @@ def cpu_baseline(M, N, K, seconds):
     t0 = time.perf_counter()
     oracle.gemm_f64(A, B, threads=threads)
     t = time.perf_counter() - t0
+    # the loop as the reference runs it, one thread, on its own CPU case (its LCG inputs)
+    A0, B0 = oracle.lcg_inputs(256, 256, 512)
+    t1 = time.perf_counter()
+    oracle.gemm_f64(A0, B0, threads=1)
+    t1 = time.perf_counter() - t1
     del np
     return {"value": 2.0 * rows * N * K / t / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "port",
-            "sample": f"{rows} of {M} rows of {M}x{N}x{K}, fp64 i-k-j oracle (oracle/oracle.c), {t:.1f} s"}
+            "sample": f"{rows} of {M} rows of {M}x{N}x{K}, fp64 i-k-j oracle (oracle/oracle.c), {t:.1f} s",
+            "single_thread_config0": {"gflops": round(2.0 * 256 * 256 * 512 / t1 / 1e9, 3), "seconds": round(t1, 4),
+                                      "shape": "256x256x512", "cores": 1}}
 
 
 def sweep(args, stream_runs=3):
