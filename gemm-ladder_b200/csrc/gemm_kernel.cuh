@@ -126,6 +126,8 @@ struct Geom {
     static constexpr int kRingFit = (BW_SMEM_LIMIT - 1024 - 512 - kCStageBytes) / kStageBytes;
     static constexpr int kStages = kRingFit < BW_MAX_STAGES ? kRingFit : BW_MAX_STAGES;
     static constexpr int kAccBufs = 2 * kAccN <= 512 ? 2 : 1;  // two accumulators, or one of 512 columns
+    // one accumulator of two 256-column halves (a wide pair tile): the halves are released and refilled separately
+    static constexpr bool kHalves = kAccBufs == 1 && kWN == 2;
     static constexpr int kTmemCols = pow2_at_least(kAccBufs * kAccN < 32 ? 32 : kAccBufs * kAccN, 32);
     static constexpr int kBarOffset = kStages * kStageBytes;
     static constexpr int kNumBars = 2 * kStages + 8;  // full, empty, tmem full x2, tmem empty x2, drain, reduce,
@@ -819,6 +821,54 @@ __global__ void __launch_bounds__(kThreads, 1)
 #endif
                 tc_fence_after();
                 const uint32_t d = tmem_base + (uint32_t)(acc * AN);
+                // the MMAs of stage st (K-block kb) into parts [w0, w1) of the accumulator: SWAP, each 128-column
+                // weight block of A into its BN columns; a wide pair tile, each 256-column part of B into its columns
+                auto issue = [&](int st, int kb, int w0, int w1) {
+                    const uint32_t sx = smem_u32(smem + st * G::kStageBytes), sy = sx + G::kXBytes;
+#pragma unroll
+                    for (int k = 0; k < kBK / 16; ++k) {
+                        const uint32_t accumulate = (kb > sg.k0 || k > 0) ? 1u : 0u;
+#pragma unroll
+                        for (int w = 0; w < WM * G::kWN; ++w) {
+                            if (w < w0 || w >= w1) continue;
+                            const uint32_t xw = sx + (uint32_t)((SWAP ? w : 0) * 128 * kBK * 2);
+                            const uint32_t yw = sy + (uint32_t)((SWAP ? 0 : w) * G::kBPart * kBK * 2);
+                            const uint64_t ad = (SWAP && !bk) ? desc_mnmajor(xw, k) : desc_kmajor(xw, k);
+                            const uint64_t bd = (SWAP || bk) ? desc_kmajor(yw, k) : desc_mnmajor(yw, k);
+                            const uint32_t dw = d + (uint32_t)(w * (SWAP ? BN : G::kMmaN));
+                            if (PAIR)
+                                mma_f16_pair(dw, ad, bd, idesc, accumulate);
+                            else
+                                mma_f16(dw, ad, bd, idesc, accumulate);
+                        }
+                    }
+                };
+                // the stage is free (in both blocks of a pair) once the MMAs so far have read it
+                auto free_stage = [&](int st) {
+                    if (PAIR) {
+                        mma_commit_pair(mapa_shared(smem_u32(&empty[st]), 0));
+                        mma_commit_pair(mapa_shared(smem_u32(&empty[st]), 1));
+                    } else {
+                        mma_commit(&empty[st]);
+                    }
+                };
+                // kHalves: the epilogue has released the accumulator's first half (tempty[0]); until it releases the
+                // second (tempty[1]) the stages get their first-half MMAs only and are held, at most S - 1 of them,
+                // then get their second-half MMAs in K order and are freed
+                int held = 0, held_stage = 0, held_kb = 0;
+                bool half1 = !G::kHalves;
+                auto catch_up = [&]() -> bool {
+                    if (!wait_bounded(&tempty[1], aph ^ 1u, abort_flag, p.wait_ns, site(1, 3, 1), seg)) return false;
+                    tc_fence_after();
+                    for (int i = 0; i < held; ++i) {
+                        const int st = (held_stage + i) % S;
+                        issue(st, held_kb + i, 1, 2);
+                        free_stage(st);
+                    }
+                    held = 0;
+                    half1 = true;
+                    return true;
+                };
                 for (int kb = sg.k0; kb < sg.k1; ++kb) {
 #ifdef BW_TRACE
                     const unsigned long long tf0 = globaltimer_ns();
@@ -833,37 +883,26 @@ __global__ void __launch_bounds__(kThreads, 1)
                     ++n_kb;
 #endif
                     tc_fence_after();
-                    const uint32_t sx = smem_u32(smem + stage * G::kStageBytes), sy = sx + G::kXBytes;
-#pragma unroll
-                    for (int k = 0; k < kBK / 16; ++k) {
-                        const uint32_t accumulate = (kb > sg.k0 || k > 0) ? 1u : 0u;
-                        // SWAP: each 128-column weight block of A into its BN columns; a wide pair tile: each
-                        // 256-column part of B into its columns
-#pragma unroll
-                        for (int w = 0; w < WM * G::kWN; ++w) {
-                            const uint32_t xw = sx + (uint32_t)((SWAP ? w : 0) * 128 * kBK * 2);
-                            const uint32_t yw = sy + (uint32_t)((SWAP ? 0 : w) * G::kBPart * kBK * 2);
-                            const uint64_t ad = (SWAP && !bk) ? desc_mnmajor(xw, k) : desc_kmajor(xw, k);
-                            const uint64_t bd = (SWAP || bk) ? desc_kmajor(yw, k) : desc_mnmajor(yw, k);
-                            const uint32_t dw = d + (uint32_t)(w * (SWAP ? BN : G::kMmaN));
-                            if (PAIR)
-                                mma_f16_pair(dw, ad, bd, idesc, accumulate);
-                            else
-                                mma_f16(dw, ad, bd, idesc, accumulate);
+                    if (G::kHalves && !half1) {
+                        issue(stage, kb, 0, 1);
+                        if (held++ == 0) {
+                            held_stage = stage;
+                            held_kb = kb;
                         }
-                    }
-                    // the stage is free (in both blocks of a pair) once these MMAs have read it
-                    if (PAIR) {
-                        mma_commit_pair(mapa_shared(smem_u32(&empty[stage]), 0));
-                        mma_commit_pair(mapa_shared(smem_u32(&empty[stage]), 1));
+                        if ((mbar_try_wait(smem_u32(&tempty[1]), aph ^ 1u) || held == S - 1) && !catch_up()) {
+                            ok = false;
+                            break;
+                        }
                     } else {
-                        mma_commit(&empty[stage]);
+                        issue(stage, kb, 0, WM * G::kWN);
+                        free_stage(stage);
                     }
                     if (++stage == S) {
                         stage = 0;
                         ph ^= 1u;
                     }
                 }
+                if (ok && !half1 && !catch_up()) ok = false;  // a segment shorter than the held stages
                 if (!ok) break;
                 // the accumulator (both blocks' halves) is complete once every MMA so far has finished
                 if (PAIR) {
@@ -915,6 +954,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                     mbar_arrive(&tempty[a]);
             }
         };
+        // the whole accumulator (kHalves: its two halves, tempty[0] and tempty[1])
+        auto release_all = [&](int a) {
+            if constexpr (G::kHalves) {
+                release_acc(0);
+                release_acc(1);
+            } else {
+                release_acc(a);
+            }
+        };
         while (it.next(s, P, sg)) {
             // one thread waits (bounded); a named barrier hands its outcome to the other 127, so that an abort
             // takes the whole group out together and no thread is left at a later barrier
@@ -942,7 +990,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 int tm, tn;
                 tile_coords(s, sg.tile, tm, tn);
                 rs_tile(p, rs_epoch, tm, tn, rank, tbase, row, lane, q, abort_flag, recv_flag, rs_acked, seg);
-                release_acc(acc);
+                release_all(acc);
             } else if (EPI == kEpiSwiGLU) {
                 // a whole tile (the plan splits none): gate columns [0, BN/2), up columns [BN/2, BN) of the tile,
                 // silu(gate) * up to columns [n0 / 2, n0 / 2 + BN / 2) of the M x N/2 output
@@ -968,7 +1016,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         dst[1] = make_uint4(h[4], h[5], h[6], h[7]);
                     }
                 }
-                release_acc(acc);
+                release_all(acc);
             } else if (kp) {
 #if BW_KSPLIT
                 // a tile's K ranges on the kc blocks of this cluster (their only segment, so every block's stage ring
@@ -1056,7 +1104,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         store_chunk<SWAP, EPI, BN>(p, m0, n0, row, ch * 16, v, cst);
                     }
                 }
-                release_acc(acc);
+                release_all(acc);
                 named_bar_sync(1, 128);  // the flags are read by all before the block goes on
 #else
                 // a tile's K halves on the two blocks of this cluster (their only segment, so the first block's stage
@@ -1114,7 +1162,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         }
                     }
                 }
-                release_acc(acc);
+                release_all(acc);
                 named_bar_sync(1, 128);  // reduce_flag is read by all before the next segment writes it
 #endif
             } else if (sg.k0 == 0 && sg.k1 == s.kblocks) {
@@ -1126,6 +1174,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                     for (int h = 0; h < kLdw / 16; ++h) tmem_ld16(tbase + (uint32_t)(c0 + 16 * h), r[h]);
                     tmem_wait_ld();
+                    if (G::kHalves && c0 + kLdw == AN / 2) release_acc(0);  // the first half is read
                     if (!SWAP && kLdw == 64 && BW_EPI_LINES) {  // whole lines of C (store_rows64)
                         float v[64];
 #pragma unroll
@@ -1141,7 +1190,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                         }
                     }
                 }
-                release_acc(acc);
+                if constexpr (G::kHalves)
+                    release_acc(1);  // the first half went at the middle
+                else
+                    release_acc(acc);
             } else {
                 // part of a split tile
                 const Fixup f = fixup_of(s, c, P, sg);
@@ -1165,7 +1217,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                                                   cst, smem, rbar, abort_flag, seg);
                     else
                         reduce_tile<AN, SWAP, R, EPI, BN>(p, P, sg.tile, rank, f, true, tbase, row, m0, n0, cst);
-                    release_acc(acc);
+                    release_all(acc);
                     if (threadIdx.x == kEpiThread0) atomicExch(counter, 0);
                 } else {
                     // this block's partial to its slot; the last block to finish the tile sums them
@@ -1183,7 +1235,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                     // at the last segment the accumulator stays (no later MMA needs it): the reduction reads this
                     // block's own partial from tensor memory
-                    if (!last_seg) release_acc(acc);
+                    if (!last_seg) release_all(acc);
                     __threadfence();
                     named_bar_sync(1, 128);
                     if (threadIdx.x == kEpiThread0) {
@@ -1204,7 +1256,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                             reduce_tile<AN, SWAP, R, EPI, BN>(p, P, sg.tile, rank, f, false, tbase, row, m0, n0, cst);
                         if (threadIdx.x == kEpiThread0) atomicExch(counter, 0);
                     }
-                    if (last_seg) release_acc(acc);
+                    if (last_seg) release_all(acc);
                 }
                 named_bar_sync(1, 128);  // reduce_flag is read by all before the next segment writes it
             }

@@ -75,7 +75,8 @@
 #define BW_PAIR_WIDE_KB_NS 748.0   // a 256 x 512 one's: twice the MMA time of the measured cuBLAS peak (an estimate)
 #endif
 #ifndef BW_PAIR_WIDE_EPI_NS
-#define BW_PAIR_WIDE_EPI_NS 2000.0 // the 256 x 512 tile's epilogue, exposed once per wave (an estimate)
+#define BW_PAIR_WIDE_EPI_NS 1200.0 // the 256 x 512 tile's exposed epilogue, once per wave: the first half's drain (the
+                                   // next tile's first-half MMAs overlap the second's) and the catch-up (an estimate)
 #endif
 #ifndef BW_SK_PART_WAVE
 #define BW_SK_PART_WAVE 0      // stream-K over every pair when the tiles make more than half a wave but not a whole one

@@ -57,6 +57,12 @@ def emu_ksplit(tmp_path_factory):
 
 
 @pytest.fixture(scope="module")
+def emu_part(tmp_path_factory):
+    """Stream-K over a part wave of pair tiles alone (BW_SK_PART_WAVE 1), its tiles 256 x 256."""
+    return build_emulator(tmp_path_factory, ("BW_SK_PART_WAVE=1",))
+
+
+@pytest.fixture(scope="module")
 def emu_wide(tmp_path_factory):
     """The 256 x 512 pair tile forced wherever the rule allows it (its estimated costs set so that it always wins), to
     run the wide kernel on shapes small enough to emulate."""
@@ -325,16 +331,16 @@ def test_fused_reduce_scatter_without_a_rank_ends_with_a_status(emu, absent):
 @pytest.mark.parametrize("shape", [(512, 768, 512, 16), (256, 768, 640, 8), (384, 704, 1280, 16)],
                          ids=lambda s: "x".join(map(str, s[:3])))
 @pytest.mark.parametrize("tn", [False, True], ids=["KxN", "NxK"])
-def test_stream_k_over_a_part_wave_of_pair_tiles(emu_ksplit, oracle_mod, shape, tn):
+def test_stream_k_over_a_part_wave_of_pair_tiles(emu_part, oracle_mod, shape, tn):
     """BW_SK_PART_WAVE 1: pair tiles that fill more than half of the pairs but not all of them are cut evenly over every
     pair (stream-K, dp_tiles 0) instead of leaving pairs idle."""
     M, N, K, sms = shape
-    q = plan_of(emu_ksplit, M, N, K, sms)
+    q = plan_of(emu_part, M, N, K, sms)
     pairs = sms // 2
     assert q["kernel"] == 2 and pairs < 2 * q["tiles"] and q["tiles"] < pairs, q
     assert q["dp_tiles"] == 0 and q["sk_tiles"] == q["tiles"] and q["grid"] == sms, q
     A, B = oracle_mod.lcg_inputs(M, N, K)
-    rc, C, status, dirty, nf, msg = emulate(emu_ksplit, A, B, M, N, K, sms, tn=tn)
+    rc, C, status, dirty, nf, msg = emulate(emu_part, A, B, M, N, K, sms, tn=tn)
     assert rc == 0 and nf == 0, f"rc {rc}, {nf} findings, first: {msg}"
     assert status[0] == 0 and dirty == 0, (status, dirty)
     r = oracle_mod.check(C, oracle_mod.gemm_f64(A, B), K)
@@ -370,9 +376,9 @@ def test_pair_tiles_of_512_columns(emu_wide, oracle_mod, form, tn):
 
 def test_wide_pair_tile_rule_on_the_judge_shapes(emu_ksplit):
     """BW_PAIR_WIDE 1 on 148 SMs: 256 x 512 pair tiles where their estimated time (plan.h, pair_time) is 2 % below the
-    256 x 256 tiles' -- the m2048 shapes of o, gateup and down and the ladder -- and not where the wide tiles quantise
-    worse (qkv_m2048: 160 wide tiles are 2.2 waves) or make less than a wave (M = 512); BASELINE config 1 (198 wide
-    tiles, 2.7 waves, against 5.35) keeps 256 x 256."""
+    256 x 256 tiles' -- the m2048 shapes of o, gateup and down, the ladder and BASELINE config 1 (198 wide tiles, 2.7
+    waves, against 5.35) -- and not where the wide tiles quantise worse (qkv_m2048: 160 wide tiles are 2.2 waves) or
+    make less than a wave (M = 512)."""
     from shapes import JUDGE_B200
 
     wide = {"o_m2048", "gateup_m2048", "down_m2048", "ladder"}
@@ -381,4 +387,4 @@ def test_wide_pair_tile_rule_on_the_judge_shapes(emu_ksplit):
             continue
         q = plan_of(emu_ksplit, M, N, K, 148)
         assert q["bn"] == (512 if name in wide else 256), (name, q["bn"])
-    assert plan_of(emu_ksplit, 4608, 5632, 8192, 148)["bn"] == 256
+    assert plan_of(emu_ksplit, 4608, 5632, 8192, 148)["bn"] == 512
