@@ -388,3 +388,24 @@ def test_wide_pair_tile_rule_on_the_judge_shapes(emu_ksplit):
         q = plan_of(emu_ksplit, M, N, K, 148)
         assert q["bn"] == (512 if name in wide else 256), (name, q["bn"])
     assert plan_of(emu_ksplit, 4608, 5632, 8192, 148)["bn"] == 512
+
+
+@pytest.mark.parametrize("drop", [0, 2, 5])
+def test_a_stalled_wide_pair_tile_ends_with_a_status(emu_wide, drop):
+    """A TMA completion that never arrives under 256 x 512 pair tiles, whose MMA issuer may hold stages while it waits
+    for the accumulator's second half: the bounded waits give up, the status word names one, every thread leaves."""
+    M, N, K = 768, 2048, 192  # 12 wide tiles on 4 pairs: three tiles per pair, each refilling the one accumulator
+    A = np.full((M, K), 0x3C00, np.uint16)
+    B = np.full((K, N), 0x3C00, np.uint16)
+    emu_wide.bw_emu_set(b"wait_ns", 300_000_000)
+    emu_wide.bw_emu_set(b"barrier_limit_ms", 30_000)
+    emu_wide.bw_emu_set(b"drop_tma", drop)
+    try:
+        rc, C, status, dirty, nf, msg = emulate(emu_wide, A, B, M, N, K, 8)
+    finally:
+        emu_wide.bw_emu_set(b"drop_tma", -1)
+        emu_wide.bw_emu_set(b"wait_ns", 60_000_000_000)
+        emu_wide.bw_emu_set(b"barrier_limit_ms", 120_000)
+    assert rc == 0 and nf == 0, f"{nf} findings, first: {msg}"
+    role, kind = status[1] >> 16, (status[1] >> 8) & 0xFF
+    assert status[0] == 3 and (role, kind) in ((1, 0), (1, 3), (2, 2), (0, 1)), status
