@@ -283,6 +283,8 @@ RS_FORMS = [
     (2, 512, 512, 256, 8, 1),   # 2 x 2 pair tiles, each rank owning one row of them
     (2, 512, 640, 320, 8, 3),   # a last tile of 128 columns; three calls reuse the slots (epochs, acks)
     (4, 1024, 384, 192, 4, 2),  # four ranks on two pairs of SMs each
+    (3, 768, 256, 128, 4, 2),   # an odd number of ranks
+    (8, 2048, 256, 64, 4, 2),   # eight ranks, the most a context takes
 ]
 
 
