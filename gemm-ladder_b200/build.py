@@ -2,7 +2,7 @@
 needed).  ``python gemm-ladder_b200/build.py [--force] [--trace] [--next]``; --trace builds lib/libbwgemm_trace.so,
 the same library with the per-block timeline compiled in (-DBW_TRACE, read by timeline.py); --next builds
 lib/libbwgemm_next.so, the library with the options built but not yet measured on a B200 (the K split over clusters
-of 2 to 8, stream-K over a part wave of pair tiles, pair tiles of 256 x 512), for A/B runs: BWGEMM_LIB=libbwgemm_next.so selects it."""
+of 2 to 8, stream-K over a part wave of pair tiles, pair tiles of 256 x 512, swap-AB on SM pairs), for A/B runs: BWGEMM_LIB=libbwgemm_next.so selects it."""
 import os
 import shutil
 import subprocess
@@ -15,7 +15,7 @@ LIB_DIR = os.path.join(HERE, "lib")
 LIB = os.path.join(LIB_DIR, "libbwgemm.so")
 TRACE_LIB = os.path.join(LIB_DIR, "libbwgemm_trace.so")
 NEXT_LIB = os.path.join(LIB_DIR, "libbwgemm_next.so")
-NEXT_DEFINES = ["-DBW_KSPLIT=1", "-DBW_SK_PART_WAVE=1", "-DBW_PAIR_WIDE=1"]
+NEXT_DEFINES = ["-DBW_KSPLIT=1", "-DBW_SK_PART_WAVE=1", "-DBW_PAIR_WIDE=1", "-DBW_SWAP_PAIR=1"]
 INCLUDE = os.path.join(ROOT, "include")
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

@@ -87,7 +87,7 @@ struct DeviceState {
     size_t work_bytes = 0;
     int* counters = nullptr;
     int n_counters = 0;
-    unsigned attrs = 0;  // kernels whose shared-memory limit is set, one bit each
+    unsigned long long attrs = 0;  // kernels whose shared-memory limit is set, one bit each
     int pairs = -1;      // pairs of SMs the pair kernel holds at once (its cluster occupancy); -1: not asked yet
     int held[9] = {};    // BW_KSPLIT 1: clusters of c swap-AB blocks held at once, c = 2 .. 8 (asked with pairs)
 };
@@ -179,7 +179,7 @@ cudaLaunchConfig_t launch_config(int grid, cudaStream_t st, cudaLaunchAttribute*
 }
 
 template <int BN, bool SWAP, bool PAIR, int EPI = kEpiF16, int WM = 1>
-int set_smem_limit(DeviceState& d, unsigned bit)
+int set_smem_limit(DeviceState& d, unsigned long long bit)
 {
     if (d.attrs & bit) return BW_OK;
     cudaError_t e = cudaFuncSetAttribute(gemm_kernel<BN, SWAP, PAIR, EPI, WM>,
@@ -222,7 +222,7 @@ int pair_occupancy(DeviceState& d)
 const int* held_of(const DeviceState& d) { return BW_KSPLIT ? d.held : nullptr; }
 
 template <int BN, bool SWAP, bool PAIR, int EPI = kEpiF16, int WM = 1>
-int launch_kernel(DeviceState& d, unsigned bit, const bw_plan& q, const CUtensorMap& mx, const CUtensorMap& my,
+int launch_kernel(DeviceState& d, unsigned long long bit, const bw_plan& q, const CUtensorMap& mx, const CUtensorMap& my,
                   const Params& p, cudaStream_t st)
 {
     using G = Geom<BN, SWAP, PAIR, WM>;
@@ -272,6 +272,20 @@ int dispatch(DeviceState& d, const bw_plan& q, const CUtensorMap& mx, const CUte
         default: return BW_ERR_ARG;
         }
     }
+#if BW_SWAP_PAIR
+    if (q.kernel == BW_KERNEL_SWAP_PAIR) {  // swap-AB on SM pairs
+        switch (q.bn * 4 + q.wm) {
+        case 32 * 4 + 1: return launch_kernel<32, true, true, kEpiF16, 1>(d, 1ull << 26, q, mx, my, p, st);
+        case 64 * 4 + 1: return launch_kernel<64, true, true, kEpiF16, 1>(d, 1ull << 27, q, mx, my, p, st);
+        case 96 * 4 + 1: return launch_kernel<96, true, true, kEpiF16, 1>(d, 1ull << 28, q, mx, my, p, st);
+        case 128 * 4 + 1: return launch_kernel<128, true, true, kEpiF16, 1>(d, 1ull << 29, q, mx, my, p, st);
+        case 64 * 4 + 2: return launch_kernel<64, true, true, kEpiF16, 2>(d, 1ull << 30, q, mx, my, p, st);
+        case 96 * 4 + 2: return launch_kernel<96, true, true, kEpiF16, 2>(d, 1ull << 31, q, mx, my, p, st);
+        case 128 * 4 + 2: return launch_kernel<128, true, true, kEpiF16, 2>(d, 1ull << 32, q, mx, my, p, st);
+        default: return BW_ERR_ARG;
+        }
+    }
+#endif
     if (q.wm == 2) {  // swap-AB tiles of 256 weight columns
         switch (q.bn) {
         case 16: return launch_kernel<16, true, false, kEpiF16, 2>(d, 1u << 21, q, mx, my, p, st);
@@ -323,6 +337,9 @@ Params make_params(const bw_plan& q, int M, int N, int K, void* C, float* work, 
     return p;
 }
 
+// The rows of A one swap-AB block loads per stage: the tokens (a pair: half of them each).
+uint32_t swap_rows(const bw_plan& q) { return (uint32_t)(q.kernel == BW_KERNEL_SWAP_PAIR ? q.bn / 2 : q.bn); }
+
 // The two tensor maps of a plan: TILE and PAIR read A (K-major) and B (MN-major) in that role order; SWAP the
 // other way round.
 bool make_maps(const bw_plan& q, const void* A, const void* B, int M, int N, int K, CUtensorMap* mx, CUtensorMap* my,
@@ -332,17 +349,17 @@ bool make_maps(const bw_plan& q, const void* A, const void* B, int M, int N, int
         if (q.kernel == BW_KERNEL_TILE || q.kernel == BW_KERNEL_PAIR)  // a pair block loads 128 rows per MMA
             return make_map(mx, A, K, M, 64, 128) &&
                    make_map(my, B, K, N, 64, (uint32_t)(q.kernel == BW_KERNEL_PAIR ? 128 : q.bn));
-        return make_map(mx, B, K, N, 64, (uint32_t)(128 * q.wm)) && make_map(my, A, K, M, 64, q.bn);
+        return make_map(mx, B, K, N, 64, (uint32_t)(128 * q.wm)) && make_map(my, A, K, M, 64, swap_rows(q));
     }
     if (BW_TMA3D) {  // the stage's 64-column blocks of B in one load
         if (q.kernel == BW_KERNEL_TILE || q.kernel == BW_KERNEL_PAIR)
             return make_map(mx, A, K, M, 64, 128) &&
                    make_map_blocks(my, B, N, K, (uint32_t)(q.kernel == BW_KERNEL_PAIR ? 2 : q.bn / 64));
-        return make_map_blocks(mx, B, N, K, (uint32_t)(2 * q.wm)) && make_map(my, A, K, M, 64, q.bn);
+        return make_map_blocks(mx, B, N, K, (uint32_t)(2 * q.wm)) && make_map(my, A, K, M, 64, swap_rows(q));
     }
     if (q.kernel == BW_KERNEL_TILE || q.kernel == BW_KERNEL_PAIR)
         return make_map(mx, A, K, M, 64, 128) && make_map(my, B, N, K, 64, 64);
-    return make_map(mx, B, N, K, 64, 64) && make_map(my, A, K, M, 64, q.bn);
+    return make_map(mx, B, N, K, 64, 64) && make_map(my, A, K, M, 64, swap_rows(q));
 }
 
 int gemm(const void* A, const void* B, void* C, int M, int N, int K, cudaStream_t st, int variant, int epi = kEpiF16,
@@ -558,9 +575,9 @@ int noalloc_gemm(const void* A, const void* B, void* C, int M, int N, int K, cud
             return q.workspace_bytes <= BW_NOALLOC_SCRATCH_BYTES && (unsigned)q.counters <= BW_NOALLOC_COUNTERS;
         };
         if ((rc = make_plan(M, N, K, d->sms, d->pairs, 0, &q, 0u, held_of(*d)))) return rc;
-        // 256-column swap tiles' (and 512-column pair tiles') partials are twice as large: the narrower tiles if
-        // those fit the array
-        if (!fits() && (q.wm > 1 || q.bn > 256) &&
+        // 256-column swap tiles', 512-column pair tiles' and swap-AB pairs' partials are twice as large: the
+        // narrower tiles on single SMs if those fit the array
+        if (!fits() && (q.wm > 1 || q.bn > 256 || q.kernel == BW_KERNEL_SWAP_PAIR) &&
             (rc = make_plan(M, N, K, d->sms, d->pairs, 0, &q, kPlanNarrow, held_of(*d))))
             return rc;
         if (!fits()) {

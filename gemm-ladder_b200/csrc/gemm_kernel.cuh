@@ -142,7 +142,7 @@ struct Geom {
     static_assert(BN % 16 == 0 && BN >= 16 && (BN <= 256 || (PAIR && BN == 512 && WM == 1)),
                   "MMA N: a multiple of 16 in [16, 256] (pair tiles of 512 columns: two MMAs of 256)");
     static_assert(SWAP || BN % (64 * kRanks) == 0, "B tiles are boxes of 64 columns (per block)");
-    static_assert(!(SWAP && PAIR), "the swap-AB form runs on single blocks");
+    static_assert(!(SWAP && PAIR) || BN % 32 == 0, "swap-AB on a pair: MMA N a multiple of 32, half per block");
     static_assert(WM == 1 || (SWAP && WM == 2), "two weight blocks per tile: swap-AB only");
     static_assert(kYBytes % 1024 == 0 && kXBytes % 1024 == 0, "operand tiles on 1024-byte swizzle atoms");
     static_assert(kStages >= 2 && kSmemBytes <= BW_SMEM_LIMIT, "shared memory");
@@ -762,19 +762,21 @@ __global__ void __launch_bounds__(kThreads, 1)
                             }
                         }
                     } else {
+                        // this block's weight columns (a pair: block r holds the tile's r-th run of 128 x WM), and
+                        // its tokens (a pair: block r the r-th half of the BN, the MMA's N split over the pair)
+                        const int wcol = (tn * R + rank) * 128 * WM;
                         if (p.tn) {  // B (N x K): 128 (x WM) rows of B, 64 K each, one load
-                            load_tile<false, BW_SWAP_HINT_B>(sx, &tmx, kb * kBK, tn * 128 * WM, &full[stage], 0u,
-                                                             pol_sb);
+                            load_tile<PAIR, BW_SWAP_HINT_B>(sx, &tmx, kb * kBK, wcol, &full[stage], barc, pol_sb);
                         } else if (BW_TMA3D) {  // B: 128 (x WM) columns, one load
-                            load_blocks<false, BW_SWAP_HINT_B>(sx, &tmx, tn * 2 * WM, kb * kBK, &full[stage], 0u,
-                                                               pol_sb);
+                            load_blocks<PAIR, BW_SWAP_HINT_B>(sx, &tmx, wcol / 64, kb * kBK, &full[stage], barc, pol_sb);
                         } else {
 #pragma unroll
                             for (int j = 0; j < 2 * WM; ++j)  // B: 128 (x WM) columns as boxes of 64 columns x 64 K
-                                load_tile<false, BW_SWAP_HINT_B>(sx + j * 8192, &tmx, tn * 128 * WM + 64 * j, kb * kBK,
-                                                                 &full[stage], 0u, pol_sb);
+                                load_tile<PAIR, BW_SWAP_HINT_B>(sx + j * 8192, &tmx, wcol + 64 * j, kb * kBK,
+                                                                &full[stage], barc, pol_sb);
                         }
-                        load_tile<false, BW_HINT_A>(sy, &tmy, kb * kBK, 0, &full[stage], 0u, pol_a);  // A: 64 K x BN rows
+                        // A: 64 K x BN (a pair: BN / 2) rows
+                        load_tile<PAIR, BW_HINT_A>(sy, &tmy, kb * kBK, rank * (BN / R), &full[stage], barc, pol_a);
                     }
                     ++issued;
                     if (++stage == S) {
@@ -978,7 +980,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             int m0, n0;
             if (SWAP) {
                 m0 = 0;
-                n0 = sg.tile * 128 * WM;
+                n0 = (sg.tile * R + rank) * 128 * WM;  // this block's weight columns (a pair: its run of the tile)
             } else {
                 int tm, tn;
                 tile_coords(s, sg.tile, tm, tn);

@@ -16,7 +16,8 @@
 //              (split-K) when that fills the pairs better than leaving them idle, the cost of each extra partial
 //              included -- or, when the tiles make one wave and a part, all of them are cut evenly (stream-K).
 //              Options built but not yet measured: stream-K also over a part wave (BW_SK_PART_WAVE 1), and pair tiles
-//              of 256 x 512 where their estimated time is lower (BW_PAIR_WIDE 1, pair_time).
+//              of 256 x 512 where their estimated time is lower (BW_PAIR_WIDE 1, pair_time); at M <= 128, the
+//              stream-K swap-AB tiles on SM pairs (BW_SWAP_PAIR 1).
 // Variants take one mechanism out each, for ablations (the reference's g_var, hopper/step7.cu:1-11).
 #pragma once
 #include <cstddef>
@@ -77,6 +78,11 @@
 #ifndef BW_PAIR_WIDE_EPI_NS
 #define BW_PAIR_WIDE_EPI_NS 1200.0 // the 256 x 512 tile's exposed epilogue, once per wave: the first half's drain (the
                                    // next tile's first-half MMAs overlap the second's) and the catch-up (an estimate)
+#endif
+#ifndef BW_SWAP_PAIR
+#define BW_SWAP_PAIR 0         // swap-AB on SM pairs (cta_group::2, M = 256: each block 128 x wm weight columns, the
+                               // tokens split over the pair) where the swap-AB tiles go to stream-K: each block takes
+                               // in half the tokens (run on the host emulator; not yet measured)
 #endif
 #ifndef BW_SK_PART_WAVE
 #define BW_SK_PART_WAVE 0      // stream-K over every pair when the tiles make more than half a wave but not a whole one
@@ -325,6 +331,18 @@ inline int make_plan(int M, int N, int K, int sms, int pairs, int variant, bw_pl
     if (swap && wide_ok && BW_SWAP_WM2_MIN > 0 && q.bn >= BW_SWAP_WM2_MIN && tiles256 >= sms) {
         q.wm = 2;
         q.tiles_n = tiles256;
+        q.tiles = q.tiles_n;
+    }
+    // BW_SWAP_PAIR: the stream-K swap-AB tiles on SM pairs instead, N rounded up to 32 (half per block); tiles of 2 x
+    // 128 weight columns, or 2 x 256 while those still outnumber the pairs
+    if (BW_SWAP_PAIR && swap && wide_ok && pairs > 0 && q.bn >= 32 && variant != 1) {
+        q.kernel = BW_KERNEL_SWAP_PAIR;
+        q.bn = (q.bn + 31) / 32 * 32;
+        ranks = 2;
+        units = pairs;
+        const int tiles512 = (N + 511) / 512;
+        q.wm = BW_SWAP_WM2_MIN > 0 && q.bn >= BW_SWAP_WM2_MIN && tiles512 >= pairs ? 2 : 1;
+        q.tiles_n = (N + 256 * q.wm - 1) / (256 * q.wm);
         q.tiles = q.tiles_n;
     }
     if (variant == 1 || q.tiles % units == 0) {

@@ -38,6 +38,7 @@ void map_blocks(CUtensorMap* m, const void* base, uint64_t cols, uint64_t rows, 
     const uint32_t box[3] = {64, 64, blocks};
     emu::make_map(m, base, 3, dims, strides, box);
 }
+uint32_t swap_rows(const bw_plan& q) { return (uint32_t)(q.kernel == BW_KERNEL_SWAP_PAIR ? q.bn / 2 : q.bn); }
 // the same choices as csrc/bwgemm.cu's make_maps
 void make_maps(const bw_plan& q, const void* A, const void* B, int M, int N, int K, CUtensorMap* mx, CUtensorMap* my,
                bool tn)
@@ -49,7 +50,7 @@ void make_maps(const bw_plan& q, const void* A, const void* B, int M, int N, int
             map2(my, B, K, N, 64, (uint32_t)(q.kernel == BW_KERNEL_PAIR ? 128 : q.bn));
         } else {
             map2(mx, B, K, N, 64, (uint32_t)(128 * q.wm));
-            map2(my, A, K, M, 64, (uint32_t)q.bn);
+            map2(my, A, K, M, 64, swap_rows(q));
         }
         return;
     }
@@ -59,7 +60,7 @@ void make_maps(const bw_plan& q, const void* A, const void* B, int M, int N, int
             map_blocks(my, B, N, K, (uint32_t)(q.kernel == BW_KERNEL_PAIR ? 2 : q.bn / 64));
         } else {
             map_blocks(mx, B, N, K, (uint32_t)(2 * q.wm));
-            map2(my, A, K, M, 64, (uint32_t)q.bn);
+            map2(my, A, K, M, 64, swap_rows(q));
         }
         return;
     }
@@ -68,7 +69,7 @@ void make_maps(const bw_plan& q, const void* A, const void* B, int M, int N, int
         map2(my, B, N, K, 64, 64);
     } else {
         map2(mx, B, N, K, 64, 64);
-        map2(my, A, K, M, 64, (uint32_t)q.bn);
+        map2(my, A, K, M, 64, swap_rows(q));
     }
 }
 
@@ -167,6 +168,20 @@ int dispatch(const bw_plan& q, const CUtensorMap& mx, const CUtensorMap& my, con
         default: return BW_ERR_ARG;
         }
     }
+#if BW_SWAP_PAIR
+    if (q.kernel == BW_KERNEL_SWAP_PAIR) {
+        switch (q.bn * 4 + q.wm) {
+        case 32 * 4 + 1: return launch<32, true, true, kEpiF16, 1>(q, mx, my, p);
+        case 64 * 4 + 1: return launch<64, true, true, kEpiF16, 1>(q, mx, my, p);
+        case 96 * 4 + 1: return launch<96, true, true, kEpiF16, 1>(q, mx, my, p);
+        case 128 * 4 + 1: return launch<128, true, true, kEpiF16, 1>(q, mx, my, p);
+        case 64 * 4 + 2: return launch<64, true, true, kEpiF16, 2>(q, mx, my, p);
+        case 96 * 4 + 2: return launch<96, true, true, kEpiF16, 2>(q, mx, my, p);
+        case 128 * 4 + 2: return launch<128, true, true, kEpiF16, 2>(q, mx, my, p);
+        default: return BW_ERR_ARG;
+        }
+    }
+#endif
     if (q.wm == 2) {
         switch (q.bn) {
         case 16: return launch<16, true, false, kEpiF16, 2>(q, mx, my, p);

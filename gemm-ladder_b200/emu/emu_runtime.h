@@ -379,7 +379,8 @@ inline void mma(uint32_t d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, bool
     const int N = (int)((idesc >> 17) & 0x3Fu) << 3, M = (int)((idesc >> 24) & 0x1Fu) << 4;
     if (((idesc >> 4) & 3u) != 1u) finding("an MMA whose accumulator is not fp32");
     const int ranks = pair ? 2 : 1;
-    if (M != 128 * ranks || N < 16 || N > 256 || N % 16) {
+    // cta_group::1 with M = 128: N in 16 .. 256 by 16; cta_group::2 (M = 256): N in 32 .. 256 by 32, half per block
+    if (M != 128 * ranks || N < 16 * ranks || N > 256 || N % (16 * ranks)) {
         finding("an MMA of M %d N %d (cta_group::%d)", M, N, ranks);
         return;
     }

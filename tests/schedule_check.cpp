@@ -29,7 +29,7 @@ static int check(int M, int N, int K, int sms, int variant)
         printf("FAULT %dx%dx%d v%d: inconsistent plan\n", M, N, K, variant);
         return 1;
     }
-    const int R = q.kernel == BW_KERNEL_PAIR ? 2 : 1;
+    const int R = q.kernel == BW_KERNEL_PAIR || q.kernel == BW_KERNEL_SWAP_PAIR ? 2 : 1;
     const int P = q.grid / R;
     if (P < 1 || q.grid > sms || q.grid % R) {
         printf("FAULT %dx%dx%d v%d: grid %d\n", M, N, K, variant, P);

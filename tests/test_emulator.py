@@ -49,11 +49,11 @@ def emu(tmp_path_factory):
 
 
 @pytest.fixture(scope="module")
-def emu_ksplit(tmp_path_factory):
+def emu_next(tmp_path_factory):
     """The kernel and rule with the options built but not yet measured on a B200 (build.py --next): the K split over
     clusters of 2 to 8 blocks (BW_KSPLIT 1), stream-K over a part wave of pair tiles (BW_SK_PART_WAVE 1), pair tiles of
-    256 x 512 (BW_PAIR_WIDE 1)."""
-    return build_emulator(tmp_path_factory, ("BW_KSPLIT=1", "BW_SK_PART_WAVE=1", "BW_PAIR_WIDE=1"))
+    256 x 512 (BW_PAIR_WIDE 1), swap-AB on SM pairs (BW_SWAP_PAIR 1)."""
+    return build_emulator(tmp_path_factory, ("BW_KSPLIT=1", "BW_SK_PART_WAVE=1", "BW_PAIR_WIDE=1", "BW_SWAP_PAIR=1"))
 
 
 @pytest.fixture(scope="module")
@@ -190,54 +190,54 @@ KSPLIT_FORMS = [
 
 @pytest.mark.parametrize("form", KSPLIT_FORMS, ids=lambda f: f"{f[0]}x{f[1]}x{f[2]}_c{f[4]}")
 @pytest.mark.parametrize("tn", [False, True], ids=["KxN", "NxK"])
-def test_k_split_over_clusters_of_2_to_8(emu_ksplit, oracle_mod, form, tn):
+def test_k_split_over_clusters_of_2_to_8(emu_next, oracle_mod, form, tn):
     """BW_KSPLIT 1: each tile's K over a cluster of c blocks, every block summing its own run of the accumulator's
     chunks from the others' pieces in its idle ring."""
     M, N, K, sms, c, wm = form
-    q = plan_of(emu_ksplit, M, N, K, sms)
+    q = plan_of(emu_next, M, N, K, sms)
     assert (q["ksplit"], q["wm"], q["grid"]) == (c, wm, c * q["tiles"]), q
     A, B = oracle_mod.lcg_inputs(M, N, K)
-    rc, C, status, dirty, nf, msg = emulate(emu_ksplit, A, B, M, N, K, sms, tn=tn)
+    rc, C, status, dirty, nf, msg = emulate(emu_next, A, B, M, N, K, sms, tn=tn)
     assert rc == 0 and nf == 0, f"rc {rc}, {nf} findings, first: {msg}"
     assert status[0] == 0 and dirty == 0, (status, dirty)
     r = oracle_mod.check(C, oracle_mod.gemm_f64(A, B), K)
     assert r["nonfinite"] == 0 and r["violations"] == 0 and r["normwise"] <= 2e-3, r
 
 
-def test_k_split_in_halves_is_the_same_bits_either_way(emu, emu_ksplit, oracle_mod):
+def test_k_split_in_halves_is_the_same_bits_either_way(emu, emu_next, oracle_mod):
     """At c = 2 both protocols add block 0's sum and block 1's in that order: the same bits."""
     M, N, K = 128, 512, 256
-    assert plan_of(emu, M, N, K, 8)["ksplit"] == 2 and plan_of(emu_ksplit, M, N, K, 8)["ksplit"] == 2
+    assert plan_of(emu, M, N, K, 8)["ksplit"] == 2 and plan_of(emu_next, M, N, K, 8)["ksplit"] == 2
     A, B = oracle_mod.lcg_inputs(M, N, K)
     C0 = emulate(emu, A, B, M, N, K, 8)[1]
-    C1 = emulate(emu_ksplit, A, B, M, N, K, 8)[1]
+    C1 = emulate(emu_next, A, B, M, N, K, 8)[1]
     assert np.array_equal(C0, C1)
 
 
 @pytest.mark.parametrize("shape", [(16, 512, 2048), (96, 640, 1024)], ids=lambda s: "x".join(map(str, s)))
 @pytest.mark.parametrize("drop", [0, 5])
-def test_a_stalled_k_split_cluster_ends_with_a_status(emu_ksplit, shape, drop):
+def test_a_stalled_k_split_cluster_ends_with_a_status(emu_next, shape, drop):
     """A TMA completion that never arrives in one block of a K-split cluster: that block's MMA issuer (or its epilogue,
     waiting for the accumulator) gives up, the others give up on the go barrier or on their pieces, and every block
     leaves.  The status word keeps the first wait to give up."""
     M, N, K = shape
     A = np.full((M, K), 0x3C00, np.uint16)
     B = np.full((K, N), 0x3C00, np.uint16)
-    emu_ksplit.bw_emu_set(b"wait_ns", 300_000_000)
-    emu_ksplit.bw_emu_set(b"barrier_limit_ms", 30_000)
-    emu_ksplit.bw_emu_set(b"drop_tma", drop)
+    emu_next.bw_emu_set(b"wait_ns", 300_000_000)
+    emu_next.bw_emu_set(b"barrier_limit_ms", 30_000)
+    emu_next.bw_emu_set(b"drop_tma", drop)
     try:
-        rc, C, status, dirty, nf, msg = emulate(emu_ksplit, A, B, M, N, K, 16)
+        rc, C, status, dirty, nf, msg = emulate(emu_next, A, B, M, N, K, 16)
     finally:
-        emu_ksplit.bw_emu_set(b"drop_tma", -1)
-        emu_ksplit.bw_emu_set(b"wait_ns", 60_000_000_000)
-        emu_ksplit.bw_emu_set(b"barrier_limit_ms", 120_000)
+        emu_next.bw_emu_set(b"drop_tma", -1)
+        emu_next.bw_emu_set(b"wait_ns", 60_000_000_000)
+        emu_next.bw_emu_set(b"barrier_limit_ms", 120_000)
     assert rc == 0 and nf == 0, f"{nf} findings, first: {msg}"
     role, kind = status[1] >> 16, (status[1] >> 8) & 0xFF
     assert status[0] == 3 and (role, kind) in ((1, 0), (2, 2), (2, 5), (2, 6), (0, 1)), status
 
 
-def test_k_split_rule_on_the_judge_shapes(emu_ksplit):
+def test_k_split_rule_on_the_judge_shapes(emu_next):
     """BW_KSPLIT 1 on 148 SMs: the cluster size and tile width of the least estimated time.  qkv (40 tiles of 256
     columns) on clusters of 3; at M = 128 the o and down shapes take 256-column tiles on clusters of 4, which halves
     each block's intake of the tokens against 128-column tiles on pairs; at M = 16 the weights' HBM time decides and
@@ -249,7 +249,7 @@ def test_k_split_rule_on_the_judge_shapes(emu_ksplit):
     for name, M, N, K in JUDGE_B200:
         if M > 128:
             continue
-        q = plan_of(emu_ksplit, M, N, K, 148)
+        q = plan_of(emu_next, M, N, K, 148)
         assert (q["ksplit"], q["wm"]) == want[name], (name, q)
         assert q["grid"] <= 148 and (q["ksplit"] == 0 or q["grid"] == q["ksplit"] * q["tiles"])
 
@@ -376,7 +376,7 @@ def test_pair_tiles_of_512_columns(emu_wide, oracle_mod, form, tn):
 
 
 
-def test_wide_pair_tile_rule_on_the_judge_shapes(emu_ksplit):
+def test_wide_pair_tile_rule_on_the_judge_shapes(emu_next):
     """BW_PAIR_WIDE 1 on 148 SMs: 256 x 512 pair tiles where their estimated time (plan.h, pair_time) is 2 % below the
     256 x 256 tiles' -- the m2048 shapes of o, gateup and down, the ladder and BASELINE config 1 (198 wide tiles, 2.7
     waves, against 5.35) -- and not where the wide tiles quantise worse (qkv_m2048: 160 wide tiles are 2.2 waves) or
@@ -387,9 +387,9 @@ def test_wide_pair_tile_rule_on_the_judge_shapes(emu_ksplit):
     for name, M, N, K in JUDGE_B200:
         if M <= 128:
             continue
-        q = plan_of(emu_ksplit, M, N, K, 148)
+        q = plan_of(emu_next, M, N, K, 148)
         assert q["bn"] == (512 if name in wide else 256), (name, q["bn"])
-    assert plan_of(emu_ksplit, 4608, 5632, 8192, 148)["bn"] == 512
+    assert plan_of(emu_next, 4608, 5632, 8192, 148)["bn"] == 512
 
 
 @pytest.mark.parametrize("drop", [0, 2, 5])
@@ -411,3 +411,49 @@ def test_a_stalled_wide_pair_tile_ends_with_a_status(emu_wide, drop):
     assert rc == 0 and nf == 0, f"{nf} findings, first: {msg}"
     role, kind = status[1] >> 16, (status[1] >> 8) & 0xFF
     assert status[0] == 3 and (role, kind) in ((1, 0), (1, 3), (2, 2), (0, 1)), status
+
+
+
+# (M, N, K, emulated SMs, weight blocks per block): swap-AB tiles that outnumber the clusters, on SM pairs
+SWAP_PAIR_FORMS = [
+    (64, 2560, 256, 16, 1),    # 10 tiles of 2 x 128 weight columns on 8 pairs, stream-K
+    (128, 4608, 256, 16, 2),   # 9 tiles of 2 x 256 (two MMAs per stage of A)
+    (32, 2560, 256, 16, 1),    # 16 tokens per block
+    (80, 2624, 192, 16, 1),    # 80 tokens in an MMA N of 96 (48 per block, the last 16 beyond A), a last tile of 64
+]
+
+
+@pytest.mark.parametrize("form", SWAP_PAIR_FORMS, ids=lambda f: f"{f[0]}x{f[1]}x{f[2]}")
+@pytest.mark.parametrize("tn", [False, True], ids=["KxN", "NxK"])
+def test_swap_ab_on_sm_pairs(emu_next, oracle_mod, form, tn):
+    """BW_SWAP_PAIR 1: cta_group::2 MMAs of M = 256 over the pair's weight columns (each block its own run of 128 x
+    wm), N = the tokens rounded up to 32, half of them loaded by each block; stream-K over the pairs."""
+    M, N, K, sms, wm = form
+    q = plan_of(emu_next, M, N, K, sms)
+    assert q["kernel"] == 3 and q["wm"] == wm and q["bn"] % 32 == 0 and q["grid"] == sms, q
+    assert q["tiles"] == -(-N // (256 * wm)), q
+    A, B = oracle_mod.lcg_inputs(M, N, K)
+    rc, C, status, dirty, nf, msg = emulate(emu_next, A, B, M, N, K, sms, tn=tn)
+    assert rc == 0 and nf == 0, f"rc {rc}, {nf} findings, first: {msg}"
+    assert status[0] == 0 and dirty == 0, (status, dirty)
+    r = oracle_mod.check(C, oracle_mod.gemm_f64(A, B), K)
+    assert r["nonfinite"] == 0 and r["violations"] == 0 and r["normwise"] <= 2e-3, r
+
+
+@pytest.mark.parametrize("drop", [0, 4])
+def test_a_stalled_swap_ab_pair_ends_with_a_status(emu_next, drop):
+    M, N, K = 64, 2560, 256
+    A = np.full((M, K), 0x3C00, np.uint16)
+    B = np.full((K, N), 0x3C00, np.uint16)
+    emu_next.bw_emu_set(b"wait_ns", 300_000_000)
+    emu_next.bw_emu_set(b"barrier_limit_ms", 30_000)
+    emu_next.bw_emu_set(b"drop_tma", drop)
+    try:
+        rc, C, status, dirty, nf, msg = emulate(emu_next, A, B, M, N, K, 16)
+    finally:
+        emu_next.bw_emu_set(b"drop_tma", -1)
+        emu_next.bw_emu_set(b"wait_ns", 60_000_000_000)
+        emu_next.bw_emu_set(b"barrier_limit_ms", 120_000)
+    assert rc == 0 and nf == 0, f"{nf} findings, first: {msg}"
+    role, kind = status[1] >> 16, (status[1] >> 8) & 0xFF
+    assert status[0] == 3 and (role, kind) in ((1, 0), (2, 2), (0, 1), (2, 4)), status

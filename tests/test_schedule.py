@@ -11,7 +11,7 @@ ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(ROOT, "gemm-ladder_b200", "csrc")
 
 
-@pytest.fixture(scope="module", params=[(), ("BW_KSPLIT=1", "BW_SK_PART_WAVE=1", "BW_PAIR_WIDE=1")],
+@pytest.fixture(scope="module", params=[(), ("BW_KSPLIT=1", "BW_SK_PART_WAVE=1", "BW_PAIR_WIDE=1", "BW_SWAP_PAIR=1")],
                 ids=["library", "not_yet_measured"])
 def checker(request, tmp_path_factory):
     """The checker over the library's rule, and over the rule with the options built but not yet measured (the K split
