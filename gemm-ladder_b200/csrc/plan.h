@@ -194,7 +194,7 @@ inline bool shape_ok(int M, int N, int K)
 
 // The split-K factor for a tail of `tail` tiles on P blocks: minimises the tail's time in tile-times,
 // ceil(tail s / P) / s, plus the reduction of s partials (each about fixup_kb K-blocks of work for the last block).
-inline int tail_splits(int tail, int P, int kblocks, double fixup_kb, double* cost_out = nullptr)
+inline int tail_splits(int tail, int P, int kblocks, double fixup_kb)
 {
     int best = 1;
     double best_cost = 1.0;
@@ -206,31 +206,33 @@ inline int tail_splits(int tail, int P, int kblocks, double fixup_kb, double* co
             best = sp;
         }
     }
-    if (cost_out) *cost_out = best_cost;
     return best;
 }
 
 // BW_PAIR_WIDE: the estimated time (ns) of `tiles` pair tiles of `bn` columns on `units` pairs, as the rule below
 // schedules them: whole waves, then stream-K over one wave and a part (even shares plus one fix-up) or the split-K tail
-// at tail_splits' cost; each wave at kblocks K-blocks of the tile's measured or estimated time, and the 512-column
-// tile's exposed epilogue once per wave.
+// tail_splits picks; each wave at kblocks K-blocks of the tile's measured or estimated time, each partial's fix-up at
+// BW_FIXUP_KB K-blocks of the 256-column tile per 256 columns (its bytes), and the 512-column tile's exposed epilogue
+// once per wave.
 inline double pair_time(int tiles, int units, int kblocks, int bn)
 {
-    const double fixup_kb = BW_FIXUP_KB * bn / 256;
-    double waves;
+    const bool wide = bn > 256;
+    const double kb_ns = wide ? BW_PAIR_WIDE_KB_NS : BW_PAIR_KB_NS;
+    const double fixup_kb = BW_FIXUP_KB * bn / 256;                // as the rule weighs a partial
+    const double fixup_ns = BW_FIXUP_KB * bn / 256 * BW_PAIR_KB_NS;  // a partial's write and read
+    double t;
     if (tiles % units == 0) {
-        waves = tiles / units;
+        t = (double)(tiles / units) * kblocks * kb_ns;
     } else if ((BW_SK_ONE_WAVE && tiles > units && tiles < 2 * units) ||
                (BW_SK_PART_WAVE && 2 * tiles > units && tiles < units)) {
-        waves = (double)tiles / units + fixup_kb / kblocks;
+        t = (double)tiles / units * kblocks * kb_ns + fixup_ns;
     } else {
-        double tail = 1.0;
-        tail_splits(tiles % units, units, kblocks, fixup_kb, &tail);
-        waves = tiles / units + tail;
+        const int tail = tiles % units;
+        const int sp = tail_splits(tail, units, kblocks, fixup_kb);
+        const double tail_waves = (double)((tail * sp + units - 1) / units) / sp;
+        t = (tiles / units + tail_waves) * kblocks * kb_ns + (sp > 1 ? sp * fixup_ns : 0.0);
     }
-    const bool wide = bn > 256;
-    return waves * kblocks * (wide ? BW_PAIR_WIDE_KB_NS : BW_PAIR_KB_NS) +
-           (wide ? (double)((tiles + units - 1) / units) * BW_PAIR_WIDE_EPI_NS : 0.0);
+    return t + (wide ? (double)((tiles + units - 1) / units) * BW_PAIR_WIDE_EPI_NS : 0.0);
 }
 
 // Plan constraints of the entries that need them (on top of the variant).
