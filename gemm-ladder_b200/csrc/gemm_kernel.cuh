@@ -35,594 +35,9 @@
 // Every wait on a barrier is bounded (ptx.cuh, wait_bounded): a stalled pipeline ends the kernel with an error status
 // instead of hanging the GPU.
 #pragma once
-#include <cuda.h>
-#include <cuda_fp16.h>
-#include "plan.h"
-#include "ptx.cuh"
-#include "schedule.h"
+#include "epilogue.cuh"
 
 namespace bw {
-
-constexpr int kThreads = 192;    // 6 warps
-constexpr int kEpiThread0 = 64;  // the first epilogue thread
-constexpr int kBK = 64;          // K per stage: one 128-byte swizzle row of fp16
-
-// Epilogue modes: what the kernel writes.
-enum : int {
-    kEpiF16 = 0,     // C = A B in fp16
-    kEpiF32 = 1,     // C = A B in fp32 (row-parallel partial sums)
-    kEpiSwiGLU = 2,  // B's tiles of BN columns hold BN/2 gate then BN/2 up columns: C = silu(gate) * up in fp16,
-                     // M x N/2 (a gated MLP's activation, from the accumulators: the gateup result never exists)
-    kEpiRS = 3,      // the fused reduce-scatter: C (fp16, this rank's M / world rows) = the sum over the ranks of
-                     // their A_r B_r, the partials exchanged tile by tile through the ranks' memory (RsTable)
-};
-
-constexpr int kRsMaxWorld = 8;
-
-// The fused reduce-scatter of a row-parallel layer (kEpiRS, pair tiles of 256 x 256, whole tiles): every rank computes
-// every tile of its partial A_r B_r; owner o = the rank whose rows [o rows, (o + 1) rows) hold the tile.  Owner o's
-// region (one allocation, mapped into the other ranks' address spaces):
-//   slots  [tile of o's rows][sender j: the other ranks in rank order][block of the pair] x 128 x 256 fp32, each
-//          laid out [col / 4][row][4] (a warp's 16-byte stores contiguous)
-//   flags  one per slot: the epoch of the call whose partial it holds
-//   ack    the last epoch whose slots o has consumed (a sender waits for epoch - 1 before writing)
-//   count  tile halves o has consumed in this call
-//   epoch  o's calls so far: every block of a call reads it at entry (the call's epoch is one more), the call's last
-//          block to finish advances it, so a call replayed from a CUDA graph carries a new epoch each time
-//   done   blocks of the current call that have finished
-// The table lives in this rank's device memory (written once, when the ranks connect); a call passes its address.
-struct RsTable {
-    int world, rank;                 // ranks; this one
-    int rows;                        // rows of C per owner (M / world, a multiple of 256)
-    float* slots[kRsMaxWorld];       // owner o's slots, as this rank addresses them
-    unsigned* flags[kRsMaxWorld];    // owner o's flags
-    unsigned* ack[kRsMaxWorld];      // owner o's ack word
-    unsigned* count;                 // this rank's count
-    unsigned* epoch;                 // this rank's epoch word
-    unsigned* done;                  // this rank's finished-block count
-};
-
-struct Params {
-    Sched s;
-    void* C;                     // fp16; fp32 for kEpiF32; M x N/2 fp16 for kEpiSwiGLU
-    float* work;                 // the partials: workspace_slots() x (PAIR ? 2 : 1) slots of 128 x BN fp32, row-major
-    int* counters;               // one per split tile (per block of the pair), zero between calls
-    unsigned long long wait_ns;  // the limit of any single wait on a barrier
-    int tn;                      // 1: B is N x K row-major (K-major for the tensor core, like A); 0: K x N
-    const RsTable* rs;           // kEpiRS only: the ranks' regions
-};
-
-__host__ __device__ constexpr int pow2_at_least(int v, int p) { return p >= v ? p : pow2_at_least(v, 2 * p); }
-
-// Optional timeline (compiled in with -DBW_TRACE only): per block, %globaltimer at kernel entry, after set-up, the
-// MMA's first full stage, its last commit, the epilogue's end, and the exit.
-#ifdef BW_TRACE
-constexpr int kTraceSlots = 16;
-__device__ unsigned long long g_trace[1024 * kTraceSlots];
-#define BW_TRACE_AT(slot) (g_trace[blockIdx.x * kTraceSlots + (slot)] = globaltimer_ns())
-#define BW_TRACE_VAL(slot, v) (g_trace[blockIdx.x * kTraceSlots + (slot)] = (unsigned long long)(v))
-// a block's slots from an earlier launch are cleared at its entry (a slot no role of this block stamps reads 0)
-#define BW_TRACE_CLEAR() \
-    for (int i_ = 1; i_ < kTraceSlots; ++i_) g_trace[blockIdx.x * kTraceSlots + i_] = 0ull
-#else
-#define BW_TRACE_CLEAR() ((void)0)
-#define BW_TRACE_VAL(slot, v) ((void)0)
-#define BW_TRACE_AT(slot) ((void)0)
-#endif
-
-template <int BN, bool SWAP, bool PAIR, int WM = 1>
-struct Geom {
-    static constexpr int kRanks = PAIR ? 2 : 1;
-    static constexpr int kTileM = PAIR ? 256 : 128;          // rows of C per tile (TILE, PAIR)
-    static constexpr int kAccN = WM * BN;                    // TMEM columns of one accumulator (SWAP: WM weight
-                                                             // blocks of 128 columns, BN tokens each)
-    static constexpr int kWN = PAIR && BN > 256 ? BN / 256 : 1;  // PAIR: MMAs of N = 256 across a 512-column tile
-    static constexpr int kMmaN = BN / kWN;                       // N of one MMA
-    static constexpr int kBPart = BN / kRanks / kWN;             // this block's B columns per MMA (PAIR: 128)
-    static constexpr int kXBytes = 128 * WM * kBK * 2;       // this block's MMA-A operand: 128 (x WM) rows x 64 K
-    static constexpr int kYBytes = (BN / kRanks) * kBK * 2;  // this block's MMA-B operand: BN (PAIR: BN / 2) x 64 K
-    static constexpr int kStageBytes = kXBytes + kYBytes;
-    static constexpr int kCStageBytes = SWAP ? 2 * 16 * 128 * 2 : 0;  // swap-AB epilogue transpose buffers
-    static constexpr int kRingFit = (BW_SMEM_LIMIT - 1024 - 512 - kCStageBytes) / kStageBytes;
-    static constexpr int kStages = kRingFit < BW_MAX_STAGES ? kRingFit : BW_MAX_STAGES;
-    static constexpr int kAccBufs = 2 * kAccN <= 512 ? 2 : 1;  // two accumulators, or one of 512 columns
-    // one accumulator of two 256-column halves (a wide pair tile): the halves are released and refilled separately
-    static constexpr bool kHalves = kAccBufs == 1 && kWN == 2;
-    static constexpr int kTmemCols = pow2_at_least(kAccBufs * kAccN < 32 ? 32 : kAccBufs * kAccN, 32);
-    static constexpr int kBarOffset = kStages * kStageBytes;
-    static constexpr int kNumBars = 2 * kStages + 8;  // full, empty, tmem full x2, tmem empty x2, drain, reduce,
-                                                      // and the K split's go / receive
-    static constexpr int kSlotBytes = 128 * kAccN * 4;  // one partial of this block's rows
-    static constexpr int kRingSlots = kBarOffset / kSlotBytes;  // partials the idle ring holds at once
-    static constexpr int kMaxSum = kRingSlots + 1 < 8 ? kRingSlots + 1 : 8;  // partials the bulk reduction sums
-    static constexpr int kMiscOffset = kBarOffset + kNumBars * 8;
-    // swap-AB: the epilogue transposes each 16-column chunk through two 16 x 128 fp16 buffers
-    static constexpr int kCStageOffset = (kMiscOffset + 32 + 127) / 128 * 128;
-    static constexpr int kSmemBytes = 1024 + kCStageOffset + kCStageBytes;  // + slack to align the stages to 1024 B
-    static_assert(BN % 16 == 0 && BN >= 16 && (BN <= 256 || (PAIR && BN == 512 && WM == 1)),
-                  "MMA N: a multiple of 16 in [16, 256] (pair tiles of 512 columns: two MMAs of 256)");
-    static_assert(SWAP || BN % (64 * kRanks) == 0, "B tiles are boxes of 64 columns (per block)");
-    static_assert(!(SWAP && PAIR) || BN % 32 == 0, "swap-AB on a pair: MMA N a multiple of 32, half per block");
-    static_assert(WM == 1 || (SWAP && WM == 2), "two weight blocks per tile: swap-AB only");
-    static_assert(kYBytes % 1024 == 0 && kXBytes % 1024 == 0, "operand tiles on 1024-byte swizzle atoms");
-    static_assert(kStages >= 2 && kSmemBytes <= BW_SMEM_LIMIT, "shared memory");
-    static_assert(kTmemCols <= 512, "tensor memory");
-};
-
-// The 3-D form for the MN-major operand (BW_TMA3D): `n64` is the first 64-column block; the map's box holds the
-// stage's blocks.
-template <bool PAIR, int HINT>
-__device__ __forceinline__ void load_blocks(void* dst, const void* tmap, int n64, int k, uint64_t* bar,
-                                            uint32_t bar_cluster, uint64_t policy)
-{
-    if (PAIR)
-        tma_load_3d_pair(dst, tmap, 0, k, n64, bar_cluster);  // (the pair form takes no cache hint here)
-    else if (HINT)
-        tma_load_3d_hint(dst, tmap, 0, k, n64, bar, policy);
-    else
-        tma_load_3d(dst, tmap, 0, k, n64, bar);
-}
-
-// The L2 policy of a hint setting (0 none, 1 evict-last, 2 evict-first).
-__device__ __forceinline__ uint64_t l2_policy(int hint) { return hint == 1 ? policy_evict_last() : policy_evict_first(); }
-
-// A tile load with an optional L2 policy; `bar` is this block's barrier (or, PAIR, the leader's shared::cluster one).
-template <bool PAIR, int HINT>
-__device__ __forceinline__ void load_tile(void* dst, const void* tmap, int x, int y, uint64_t* bar, uint32_t bar_cluster,
-                                          uint64_t policy)
-{
-    if (PAIR) {
-        if (HINT) tma_load_2d_pair_hint(dst, tmap, x, y, bar_cluster, policy);
-        else tma_load_2d_pair(dst, tmap, x, y, bar_cluster);
-    } else {
-        if (HINT) tma_load_2d_hint(dst, tmap, x, y, bar, policy);
-        else tma_load_2d(dst, tmap, x, y, bar);
-    }
-}
-
-// Where a wait gave up: role (0 producer, 1 MMA, 2 epilogue, 7 the wait selftest) << 16 | barrier kind << 8 | index.
-enum : uint32_t { kSiteSelftest = 7u };
-__host__ __device__ __forceinline__ uint32_t site(uint32_t role, uint32_t kind, uint32_t idx)
-{
-    return role << 16 | kind << 8 | idx;
-}
-
-// A wait on a barrier that only bounds time (used to drain copies in flight after an abort).
-__device__ __forceinline__ void wait_drain(uint64_t* bar, uint32_t parity, uint64_t limit_ns)
-{
-    const uint32_t b = smem_u32(bar);
-    const uint64_t t0 = globaltimer_ns();
-    while (!mbar_try_wait(b, parity))
-        if (globaltimer_ns() - t0 > limit_ns) return;
-}
-
-// ------------------------------------------------------------------ descriptors of the stage tiles
-// K-major tile (rows of 64 fp16 = 128 bytes, 8-row swizzle atoms of 1024 bytes): the k-th K16 slice starts 32 bytes in.
-__device__ __forceinline__ uint64_t desc_kmajor(uint32_t tile, int k) { return smem_desc_sw128(tile + 32u * k, 16u, 1024u); }
-// MN-major tile (boxes of 64 MN x 64 K, 8 KB each; within a box K-row r at 128 r): the k-th K16 slice is 16 rows on;
-// leading byte offset = the next 64 MN (8192), stride byte offset = the next 8 K-rows (1024).
-__device__ __forceinline__ uint64_t desc_mnmajor(uint32_t tile, int k) { return smem_desc_sw128(tile + 2048u * k, 8192u, 1024u); }
-
-// ------------------------------------------------------------------ the epilogue's stores
-// 16 accumulator columns of TMEM lane `lane` (v) -> C, by all 128 epilogue threads together.
-// Not swapped: C[m0 + lane][n0 + c0 .. +15], two 16-byte stores per thread.
-// Swapped: the values are column n0 + lane of rows c0 .. c0 + 15 of C.  They go through shared memory (cst: two
-// 16 x 128 fp16 buffers, alternating by chunk), so that C is written by 16-byte stores, a warp covering two rows of
-// 256 contiguous bytes, instead of 16 scattered 2-byte stores per thread.  One named barrier per chunk; the buffer of
-// chunk i + 2 is written only after every thread has passed the barrier of chunk i + 1, so after it read chunk i.
-template <bool SWAP, int EPI = kEpiF16, int BT = 0>
-__device__ __forceinline__ void store_chunk(const Params& p, int m0, int n0, int lane, int c0, const float (&v)[16],
-                                            __half* cst)
-{
-    const Sched& s = p.s;
-    if (EPI == kEpiF32) {  // fp32 C (not swapped): four 16-byte stores
-        const int m = m0 + lane, n = n0 + c0;
-        if (m >= s.M || n >= s.N) return;
-        float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.C) + (size_t)m * s.N + n);
-#pragma unroll
-        for (int q = 0; q < 4; ++q) dst[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-        return;
-    }
-    if (!SWAP) {
-        const int m = m0 + lane, n = n0 + c0;
-        if (m >= s.M || n >= s.N) return;
-        uint32_t h[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const __half2 x = __floats2half2_rn(v[2 * j], v[2 * j + 1]);
-            h[j] = *reinterpret_cast<const uint32_t*>(&x);
-        }
-        uint4* dst = reinterpret_cast<uint4*>(static_cast<__half*>(p.C) + (size_t)m * s.N + n);
-        dst[0] = make_uint4(h[0], h[1], h[2], h[3]);
-        dst[1] = make_uint4(h[4], h[5], h[6], h[7]);
-    } else {
-        __half* buf = cst + ((c0 >> 4) & 1) * (16 * 128);
-#pragma unroll
-        for (int j = 0; j < 16; ++j) buf[j * 128 + lane] = __float2half_rn(v[j]);
-        named_bar_sync(1, 128);
-        const int t = threadIdx.x - kEpiThread0;
-        // accumulator column c0: token c0 % BT of weight block c0 / BT (BT tokens per block; 0: one block)
-        const int wb = BT ? c0 / BT : 0, tok = c0 - wb * BT;
-#pragma unroll
-        for (int k = 0; k < 2; ++k) {
-            const int piece = t + 128 * k;  // 256 pieces of 8 fp16: 16 rows x 16 pieces
-            const int mm = piece >> 4, nn = (piece & 15) * 8;
-            const int m = tok + mm, n = n0 + wb * 128 + nn;
-            if (m < s.M && n < s.N)
-                *reinterpret_cast<uint4*>(static_cast<__half*>(p.C) + (size_t)m * s.N + n) =
-                    *reinterpret_cast<const uint4*>(buf + mm * 128 + nn);
-        }
-    }
-}
-
-// 64 columns of C from the 32 rows of one epilogue warp (TILE and PAIR; lane l holds row r0 + l, as the accumulator's
-// TMEM lanes give it), stored as whole lines.  A thread writing its own row would touch 32 rows per warp store, half a
-// sector each (measured: 16 GB/s per SM for a 128 x 256 fp16 tile); instead the 16-byte pieces are transposed within
-// groups of P lanes (P = pieces per row of 64 columns: 8 in fp16, 16 in fp32) by log2(P) rounds of shfl_xor, after
-// which lane q of a group holds piece q of the group's P rows, and each store writes 32 / P rows of 128 (256) bytes
-// (measured: 53 GB/s per SM).
-template <int P>
-__device__ __forceinline__ void transpose_pieces(uint32_t (&x)[P][4], int lane)
-{
-    const int q = lane & (P - 1);
-#pragma unroll
-    for (int m = P / 2; m >= 1; m >>= 1) {
-        const bool hi = (q & m) != 0;
-#pragma unroll
-        for (int e = 0; e < P; ++e) {
-            if (e & m) continue;
-#pragma unroll
-            for (int w = 0; w < 4; ++w) {  // the lower lane keeps piece e and takes e | m; the upper the other way
-                const uint32_t send = hi ? x[e][w] : x[e | m][w];
-                const uint32_t recv = __shfl_xor_sync(0xffffffffu, send, m);
-                if (hi)
-                    x[e][w] = recv;
-                else
-                    x[e | m][w] = recv;
-            }
-        }
-    }
-}
-
-template <int EPI>
-__device__ __forceinline__ void store_rows64(const Params& p, int r0, int n, int lane, const float (&v)[64])
-{
-    static_assert(EPI == kEpiF16 || EPI == kEpiF32, "fp16 or fp32 C");
-    constexpr int P = EPI == kEpiF32 ? 16 : 8;
-    const Sched& s = p.s;
-    uint32_t x[P][4];
-#pragma unroll
-    for (int i = 0; i < P; ++i)
-#pragma unroll
-        for (int w = 0; w < 4; ++w) {
-            if (EPI == kEpiF32) {
-                x[i][w] = __float_as_uint(v[4 * i + w]);
-            } else {
-                const __half2 h = __floats2half2_rn(v[8 * i + 2 * w], v[8 * i + 2 * w + 1]);
-                x[i][w] = *reinterpret_cast<const uint32_t*>(&h);
-            }
-        }
-    transpose_pieces<P>(x, lane);
-    const int q = lane & (P - 1), g = lane / P;
-    if (n >= s.N) return;  // N % 64 == 0: the 64 columns are all in C or all outside
-#pragma unroll
-    for (int e = 0; e < P; ++e) {
-        const int m = r0 + g * P + e;
-        if (m < s.M) {
-            uint4* dst = EPI == kEpiF32
-                             ? reinterpret_cast<uint4*>(static_cast<float*>(p.C) + (size_t)m * s.N + n) + q
-                             : reinterpret_cast<uint4*>(static_cast<__half*>(p.C) + (size_t)m * s.N + n) + q;
-            *dst = make_uint4(x[e][0], x[e][1], x[e][2], x[e][3]);
-        }
-    }
-}
-
-// ------------------------------------------------------------------ the partials of a split tile
-// Slot layout: 128 rows x BN columns of fp32, interleaved by groups of 4 columns: [col / 4][row][col % 4].  TMEM lane
-// `row`'s 4-column group is one 16-byte vector, and the 32 lanes of a warp touch 512 contiguous bytes per vector
-// access (stores of a partial and loads of the reduction alike).  A block of a pair keeps its half in slot
-// 2 s + rank.
-template <int BN>
-__device__ __forceinline__ float4* slot_vec(const Params& p, long long slot, int row, int col4)
-{
-    return reinterpret_cast<float4*>(p.work + (size_t)slot * 128 * BN) + (size_t)col4 * 128 + row;
-}
-
-// The last block of a split tile: for its row of the tile, sums the tile's nseg partials in their fixed order
-// (p_0 + p_1 + ... : the same bits whichever block is last) and stores the result to C.  Partial f.mine comes from
-// this block's accumulator in tensor memory when own_mine (tbase: its row's TMEM address), from its slot otherwise.
-// The loads from memory are a stream of (16-column chunk, partial) pairs in chunk order, kept kWin deep in flight:
-// with one partial in memory four chunks are on their way at once, instead of one L2 round trip per chunk.
-template <int BN, bool SWAP, int RANKS, int EPI, int BT = 0>
-__device__ __noinline__ void reduce_tile(const Params& p, int P, int tile, int rank, Fixup f, bool own_mine,
-                                            uint32_t tbase, int row, int m0, int n0, __half* cst)
-{
-    constexpr int kWin = 4;
-    constexpr int kChunks = BN / 16;
-    const Sched& s = p.s;
-    const int L = f.nseg - (own_mine ? 1 : 0);  // partials read from memory
-    const int total = kChunks * L;
-    // the memory partial j (in order) is partial index i: j, or j + 1 past this block's own
-    auto index_of = [&](int j) { return (own_mine && j >= f.mine) ? j + 1 : j; };
-    auto issue = [&](int idx, float4 (&w)[4]) {
-        const int chunk = idx / L, j = idx - chunk * L;
-        const long long slot = (long long)fixup_slot(s, P, tile, f, index_of(j)) * RANKS + rank;
-#pragma unroll
-        for (int q = 0; q < 4; ++q) w[q] = __ldcg(slot_vec<BN>(p, slot, row, chunk * 4 + q));
-    };
-    float4 win[kWin][4];
-#pragma unroll
-    for (int q = 0; q < kWin; ++q)
-        if (q < total) issue(q, win[q]);
-    float v[16], own[16];
-    bool own_added = false;
-    for (int base = 0; base < total; base += kWin) {
-#pragma unroll
-        for (int q = 0; q < kWin; ++q) {
-            const int idx = base + q;
-            if (idx < total) {
-                const int chunk = idx / L, j = idx - chunk * L;
-                const int i = index_of(j);
-                if (j == 0) {
-                    own_added = false;
-                    if (own_mine) {
-                        uint32_t r[16];
-                        tmem_ld16(tbase + (uint32_t)(chunk * 16), r);
-                        tmem_wait_ld();
-#pragma unroll
-                        for (int e = 0; e < 16; ++e) own[e] = __uint_as_float(r[e]);
-                    }
-                }
-                // this block's own partial goes in at its place in the order
-                if (own_mine && !own_added && f.mine < i) {
-                    if (f.mine == 0) {
-#pragma unroll
-                        for (int e = 0; e < 16; ++e) v[e] = own[e];
-                    } else {
-#pragma unroll
-                        for (int e = 0; e < 16; ++e) v[e] += own[e];
-                    }
-                    own_added = true;
-                }
-                float x[16];
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    x[4 * e] = win[q][e].x;
-                    x[4 * e + 1] = win[q][e].y;
-                    x[4 * e + 2] = win[q][e].z;
-                    x[4 * e + 3] = win[q][e].w;
-                }
-                if (idx + kWin < total) issue(idx + kWin, win[q]);  // refill this window slot
-                if (i == 0) {
-#pragma unroll
-                    for (int e = 0; e < 16; ++e) v[e] = x[e];
-                } else {
-#pragma unroll
-                    for (int e = 0; e < 16; ++e) v[e] += x[e];
-                }
-                if (j == L - 1) {  // the chunk is complete
-                    if (own_mine && !own_added) {
-#pragma unroll
-                        for (int e = 0; e < 16; ++e) v[e] += own[e];
-                    }
-                    store_chunk<SWAP, EPI, BT>(p, m0, n0, row, chunk * 16, v, cst);
-                }
-            }
-        }
-    }
-}
-
-// The same at a block's last segment, when its stage ring is idle (every load consumed, none to come): the partials
-// in memory are copied into the ring by the TMA engine at once (cp.async.bulk, one per partial), then summed from
-// shared memory.  The sum runs over at most kMaxSum partials, unrolled and predicated, so that everything stays in
-// registers.  Returns false if the copy did not complete within the wait limit (the block's abort flag is up).
-template <int BN, bool SWAP, int RANKS, int kMaxSum, int EPI, int BT = 0>
-__device__ __noinline__ bool reduce_tile_bulk(const Params& p, int P, int tile, int rank, Fixup f, bool own_mine,
-                                              uint32_t tbase, int row, int m0, int n0, __half* cst, uint8_t* ring,
-                                              uint64_t* rbar, volatile int* abort_flag, int seg)
-{
-    constexpr int kSlotBytes = 128 * BN * 4;
-    constexpr int kChunks = BN / 16;
-    const Sched& s = p.s;
-    const int L = f.nseg - (own_mine ? 1 : 0);
-    if (threadIdx.x == kEpiThread0) {
-        mbar_arrive_expect_tx(rbar, (uint32_t)(L * kSlotBytes));
-        for (int j = 0; j < L; ++j) {
-            const int i = (own_mine && j >= f.mine) ? j + 1 : j;
-            const long long slot = (long long)fixup_slot(s, P, tile, f, i) * RANKS + rank;
-            const uint8_t* src = reinterpret_cast<const uint8_t*>(p.work + (size_t)slot * 128 * BN);
-            for (int off = 0; off < kSlotBytes; off += 32768) {
-                const int n = kSlotBytes - off < 32768 ? kSlotBytes - off : 32768;
-                bulk_load(ring + (size_t)j * kSlotBytes + off, src + off, (uint32_t)n, rbar);
-            }
-        }
-    }
-    if (!wait_bounded(rbar, 0, abort_flag, p.wait_ns, site(2, 4, 0), seg)) return false;
-    if (threadIdx.x == kEpiThread0) BW_TRACE_AT(10);
-    // [col / 4][row][4] within a slot: consecutive rows are consecutive 16-byte vectors
-    const float4* base = reinterpret_cast<const float4*>(ring) + row;
-    // the sum of 16 columns (chunk) of this row, in summation order
-    auto sum_chunk = [&](int chunk, float4 (&acc)[4]) {
-        float4 own[4];
-        if (own_mine) {
-            uint32_t r[16];
-            tmem_ld16(tbase + (uint32_t)(chunk * 16), r);
-            tmem_wait_ld();
-#pragma unroll
-            for (int q = 0; q < 4; ++q)
-                own[q] = make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]),
-                                     __uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3]));
-        }
-#pragma unroll
-        for (int i = 0; i < kMaxSum; ++i) {
-            if (i < f.nseg) {
-                float4 w[4];
-                if (own_mine && i == f.mine) {
-#pragma unroll
-                    for (int q = 0; q < 4; ++q) w[q] = own[q];
-                } else {
-                    const int j = (own_mine && i > f.mine) ? i - 1 : i;  // its place in the ring
-                    const float4* src = base + (size_t)j * (kSlotBytes / 16) + (size_t)chunk * 4 * 128;
-#pragma unroll
-                    for (int q = 0; q < 4; ++q) w[q] = src[q * 128];
-                }
-                if (i == 0) {
-#pragma unroll
-                    for (int q = 0; q < 4; ++q) acc[q] = w[q];
-                } else {
-#pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-                        acc[q].x += w[q].x;
-                        acc[q].y += w[q].y;
-                        acc[q].z += w[q].z;
-                        acc[q].w += w[q].w;
-                    }
-                }
-            }
-        }
-    };
-    if constexpr (!SWAP && BN % 64 == 0 && BW_EPI_LINES && (EPI == kEpiF16 || EPI == kEpiF32)) {
-        // 64 columns at a time, stored as whole lines of C (store_rows64)
-#pragma unroll 1
-        for (int c0 = 0; c0 < BN; c0 += 64) {
-            float v[64];
-#pragma unroll
-            for (int h = 0; h < 4; ++h) {
-                float4 acc[4];
-                sum_chunk(c0 / 16 + h, acc);
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    v[16 * h + 4 * q] = acc[q].x;
-                    v[16 * h + 4 * q + 1] = acc[q].y;
-                    v[16 * h + 4 * q + 2] = acc[q].z;
-                    v[16 * h + 4 * q + 3] = acc[q].w;
-                }
-            }
-            store_rows64<EPI>(p, m0 + (row & ~31), n0 + c0, row & 31, v);
-        }
-    } else {
-#pragma unroll 1
-        for (int chunk = 0; chunk < kChunks; ++chunk) {
-            float4 acc[4];
-            sum_chunk(chunk, acc);
-            float v[16];
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                v[4 * q] = acc[q].x;
-                v[4 * q + 1] = acc[q].y;
-                v[4 * q + 2] = acc[q].z;
-                v[4 * q + 3] = acc[q].w;
-            }
-            store_chunk<SWAP, EPI, BT>(p, m0, n0, row, chunk * 16, v, cst);
-        }
-    }
-    if (threadIdx.x == kEpiThread0) BW_TRACE_AT(11);
-    return true;
-}
-
-// ------------------------------------------------------------------ the fused reduce-scatter's epilogue
-// One pair tile's half (this block's 128 rows x 256 columns, accumulator at tbase) under kEpiRS.  Not this rank's
-// rows: the partial goes into the owner's slot by 16-byte stores (over NVLink), then the slot's flag takes the epoch
-// (each thread's stores ordered before it by a system-scope fence).  The first time a block sends to an owner in a
-// call it waits for the owner's ack of the previous call (the slot is free).  This rank's rows: the other ranks'
-// flags for the tile, then the sum in rank order (this rank's own partial from tensor memory) rounded to fp16 into C,
-// then a count; the block that consumes the call's last tile half acks the epoch.  Every wait is bounded; one thread
-// waits and hands the outcome to the other 127 through `go`.  Returns false after a wait gave up.
-__device__ __noinline__ bool rs_tile(const Params& p, unsigned epoch, int tm, int tn, int pr, uint32_t tbase, int row,
-                                     int lane, int q, volatile int* abort_flag, volatile int* go, unsigned& acked,
-                                     int seg)
-{
-    const RsTable& rs = *p.rs;
-    const Sched& s = p.s;
-    const int o = tm * 256 / rs.rows;                        // the owner of the tile's rows
-    const int tl = (tm - o * (rs.rows / 256)) * s.tiles_n + tn;  // the tile among the owner's
-    if (o != rs.rank) {
-        if (!(acked >> o & 1u)) {
-            if (threadIdx.x == kEpiThread0)
-                *go = wait_flag(rs.ack[o], epoch - 1u, abort_flag, p.wait_ns, site(2, 8, (uint32_t)o), seg) ? 1 : 0;
-            named_bar_sync(1, 128);
-            const bool ok = *go != 0;
-            named_bar_sync(1, 128);  // `go` is read by all before it is written again
-            if (!ok) return false;
-            acked |= 1u << o;
-        }
-        const int j = rs.rank < o ? rs.rank : rs.rank - 1;
-        const size_t idx = ((size_t)tl * (rs.world - 1) + j) * 2 + pr;
-        float4* slot = reinterpret_cast<float4*>(rs.slots[o] + idx * 128 * 256);
-#pragma unroll 1
-        for (int c0 = 0; c0 < 256; c0 += 16) {
-            uint32_t r[16];
-            tmem_ld16(tbase + (uint32_t)c0, r);
-            tmem_wait_ld();
-#pragma unroll
-            for (int k = 0; k < 4; ++k)
-                slot[(size_t)(c0 / 4 + k) * 128 + row] =
-                    make_float4(__uint_as_float(r[4 * k]), __uint_as_float(r[4 * k + 1]), __uint_as_float(r[4 * k + 2]),
-                                __uint_as_float(r[4 * k + 3]));
-        }
-        fence_sys();
-        named_bar_sync(1, 128);
-        if (threadIdx.x == kEpiThread0) st_release_sys(rs.flags[o] + idx, epoch);
-        return true;
-    }
-    // this rank's rows: the others' partials of the tile
-    if (threadIdx.x == kEpiThread0) {
-        bool ok = true;
-        for (int j = 0; j < rs.world - 1 && ok; ++j)
-            ok = wait_flag(rs.flags[o] + ((size_t)tl * (rs.world - 1) + j) * 2 + pr, epoch, abort_flag, p.wait_ns,
-                           site(2, 7, (uint32_t)j), seg);
-        *go = ok ? 1 : 0;
-    }
-    named_bar_sync(1, 128);
-    const bool ok = *go != 0;
-    named_bar_sync(1, 128);
-    if (!ok) return false;
-    const int m_local = tm * 256 + pr * 128 - o * rs.rows;  // the block's first row in this rank's C
-#pragma unroll 1
-    for (int c0 = 0; c0 < 256; c0 += 64) {
-        float v[64];
-#pragma unroll
-        for (int h = 0; h < 4; ++h) {
-            uint32_t r[16];
-            tmem_ld16(tbase + (uint32_t)(c0 + 16 * h), r);
-            tmem_wait_ld();
-#pragma unroll
-            for (int e = 0; e < 16; ++e) v[16 * h + e] = __uint_as_float(r[e]);
-        }
-        // the sum in rank order: rank 0's partial first, this rank's (v) at its place
-        float acc[64];
-        for (int src = 0; src < rs.world; ++src) {
-            if (src == rs.rank) {
-#pragma unroll
-                for (int e = 0; e < 64; ++e) acc[e] = src == 0 ? v[e] : acc[e] + v[e];
-                continue;
-            }
-            const int j = src < rs.rank ? src : src - 1;
-            const float4* slot = reinterpret_cast<const float4*>(
-                rs.slots[o] + (((size_t)tl * (rs.world - 1) + j) * 2 + pr) * 128 * 256);
-#pragma unroll
-            for (int k = 0; k < 16; ++k) {
-                const float4 w = __ldcg(slot + (size_t)(c0 / 4 + k) * 128 + row);
-                const float x[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-                for (int e = 0; e < 4; ++e) acc[4 * k + e] = src == 0 ? x[e] : acc[4 * k + e] + x[e];
-            }
-        }
-        store_rows64<kEpiF16>(p, m_local + q * 32, tn * 256 + c0, lane, acc);
-    }
-    named_bar_sync(1, 128);
-    if (threadIdx.x == kEpiThread0) {
-        // every rank's tile halves of this rank's rows: 2 per tile
-        const unsigned total = 2u * (unsigned)((rs.rows / 256) * s.tiles_n);
-        __threadfence();
-        if (atomicAdd(rs.count, 1u) == total - 1u) {
-            *rs.count = 0u;
-            __threadfence();
-            st_release_sys(rs.ack[rs.rank], epoch);
-        }
-    }
-    return true;
-}
 
 // ------------------------------------------------------------------ the kernel
 template <int BN, bool SWAP, bool PAIR, int EPI = kEpiF16, int WM = 1>

@@ -64,9 +64,10 @@ def emu_part(tmp_path_factory):
 
 @pytest.fixture(scope="module")
 def emu_wide(tmp_path_factory):
-    """The 256 x 512 pair tile forced wherever the rule allows it (its estimated costs set so that it always wins), to
-    run the wide kernel on shapes small enough to emulate."""
-    return build_emulator(tmp_path_factory, ("BW_PAIR_WIDE=1", "BW_PAIR_WIDE_KB_NS=1", "BW_PAIR_WIDE_EPI_NS=0"))
+    """The 256 x 512 pair tile forced wherever the rule allows it (its estimated costs, and the fix-ups', set so that it
+    always wins), to run the wide kernel on shapes small enough to emulate."""
+    return build_emulator(tmp_path_factory, ("BW_PAIR_WIDE=1", "BW_PAIR_WIDE_KB_NS=1", "BW_PAIR_WIDE_EPI_NS=0",
+                                             "BW_FIXUP_KB=0"))
 
 
 def plan_of(L, M, N, K, sms, variant=0):
