@@ -15,7 +15,8 @@ with host buffers: pinned host -> device copies of A and B and the device -> hos
 everything in order on one stream),
 roofline (the kernel against the measured cuBLAS peak), cpu_baseline (the fp64 oracle on a bounded sample of rows,
 all host threads), clocks sampled through NVML during the timed region, gpu_launches.  --sweep adds the judge's 17
-B200 shapes timed against torch.matmul (cuBLAS) in CUDA graphs, with the geometric mean of the time ratios.
+B200 shapes timed against torch.matmul (cuBLAS) in CUDA graphs, with the geometric mean of the time ratios
+(--ab-lib libbwgemm_next.so adds a third arm, another build of the library, interleaved with the other two).
 
 --impl reference: the reference's CPU path (its fp64 i-k-j GEMM, restated in oracle/oracle.c; the reference's GPU
 harness needs its judge, which needs CUDA 13) timed on the host cores on the same workload, in bounded row samples.
@@ -68,6 +69,9 @@ def parse():
     ap.add_argument("--tp-fused-rs", action="store_true",
                     help="tp_mlp: down and the reduce-scatter in one kernel per rank (bw_gemm_f16_rs), no NCCL call")
     ap.add_argument("--sweep", action="store_true", help="also time the judge's 17 shapes against cuBLAS")
+    ap.add_argument("--ab-lib", default=None,
+                    help="--sweep: also time another build of the library, from gemm-ladder_b200/lib/ (e.g. "
+                         "libbwgemm_next.so), interleaved with the two arms in the same process")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
@@ -264,11 +268,28 @@ def cpu_baseline(M, N, K, seconds):
 def sweep(args, stream_runs=3):
     """The judge's 17 shapes (+ BASELINE's ladder variants): ours and torch.matmul (cuBLAS), CUDA graphs of G calls
     on 3 rotating input sets, interleaved rounds, median; ratio = cuBLAS time / ours (the judge's ratio)."""
+    import ctypes
+
     import torch
 
     import bwgemm
     from shapes import CONFIG1, JUDGE_B200, LADDER_4096
 
+    other = None  # the other build of the library (--ab-lib), bound on its own
+    if args.ab_lib:
+        other = ctypes.CDLL(os.path.join(PKG, "lib", args.ab_lib))
+        other.bw_gemm_f16_variant.argtypes = [ctypes.c_void_p] * 3 + [ctypes.c_int] * 3 + [ctypes.c_void_p, ctypes.c_int]
+        other.bw_gemm_f16_variant.restype = ctypes.c_int
+
+    def call_other(A, B, C):
+        M, K = A.shape
+        N = B.shape[1]
+        rc = other.bw_gemm_f16_variant(A.data_ptr(), B.data_ptr(), C.data_ptr(), M, N, K,
+                                       torch.cuda.current_stream().cuda_stream, args.variant)
+        if rc:
+            raise RuntimeError(f"{args.ab_lib}: status {rc}")
+
+    arms = ("ours", "cublas") + (("other",) if other else ())
     out = {}
     ratios = []
     for name, M, N, K in list(JUDGE_B200) + [LADDER_4096, CONFIG1]:
@@ -278,9 +299,11 @@ def sweep(args, stream_runs=3):
         G = max(3, min(60, int(20e-3 / max(flops / 1.2e15, 5e-6))))
         bwgemm.gemm(A[0], B[0], C, variant=args.variant)  # the first call of a shape (workspace)
         torch.matmul(A[0], B[0], out=C)
+        if other:
+            call_other(A[0], B[0], C)
         torch.cuda.synchronize()
         graphs = {}
-        for arm in ("ours", "cublas"):
+        for arm in arms:
             g = torch.cuda.CUDAGraph()
             s = torch.cuda.Stream()
             s.wait_stream(torch.cuda.current_stream())
@@ -289,13 +312,15 @@ def sweep(args, stream_runs=3):
                     for i in range(G):
                         if arm == "ours":
                             bwgemm.gemm(A[i % 3], B[i % 3], C, variant=args.variant)
+                        elif arm == "other":
+                            call_other(A[i % 3], B[i % 3], C)
                         else:
                             torch.matmul(A[i % 3], B[i % 3], out=C)
             torch.cuda.synchronize()
             graphs[arm] = g
-        times = {"ours": [], "cublas": []}
+        times = {arm: [] for arm in arms}
         for rnd in range(stream_runs):
-            for arm in (("ours", "cublas") if rnd % 2 == 0 else ("cublas", "ours")):
+            for arm in (arms if rnd % 2 == 0 else arms[::-1]):
                 g = graphs[arm]
                 g.replay()  # warm-up
                 e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -313,11 +338,19 @@ def sweep(args, stream_runs=3):
         out[name] = {"M": M, "N": N, "K": K, "us": round(t_ours * 1e6, 2), "cublas_us": round(t_cub * 1e6, 2),
                      "ratio": round(ratio, 4), "tflops": round(flops / t_ours / 1e12, 1),
                      "gbs": round(bytes_alg / t_ours / 1e9, 1)}
+        if other:
+            t_other = statistics.median(times["other"])
+            out[name].update({"other_us": round(t_other * 1e6, 2), "other_ratio": round(t_cub / t_other, 4)})
         del graphs, A, B, C
         torch.cuda.empty_cache()
     judge = [out[n]["ratio"] for n, *_ in JUDGE_B200]
-    return {"shapes": out, "geomean_ratio_vs_cublas_17": round(math.exp(sum(map(math.log, judge)) / len(judge)), 4),
-            "reference": "torch.matmul fp16 (cuBLAS heuristic), CUDA graphs, 3 rotating input sets"}
+    res = {"shapes": out, "geomean_ratio_vs_cublas_17": round(math.exp(sum(map(math.log, judge)) / len(judge)), 4),
+           "reference": "torch.matmul fp16 (cuBLAS heuristic), CUDA graphs, 3 rotating input sets"}
+    if other:
+        judge_o = [out[n]["other_ratio"] for n, *_ in JUDGE_B200]
+        res.update({"other_library": args.ab_lib,
+                    "other_geomean_ratio_vs_cublas_17": round(math.exp(sum(map(math.log, judge_o)) / len(judge_o)), 4)})
+    return res
 
 
 def run_tp_mlp(args):
