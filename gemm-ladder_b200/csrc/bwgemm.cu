@@ -275,12 +275,9 @@ int dispatch(DeviceState& d, const bw_plan& q, const CUtensorMap& mx, const CUte
 #if BW_SWAP_PAIR
     if (q.kernel == BW_KERNEL_SWAP_PAIR) {  // swap-AB on SM pairs
         switch (q.bn * 4 + q.wm) {
-        case 32 * 4 + 1: return launch_kernel<32, true, true, kEpiF16, 1>(d, 1ull << 26, q, mx, my, p, st);
         case 64 * 4 + 1: return launch_kernel<64, true, true, kEpiF16, 1>(d, 1ull << 27, q, mx, my, p, st);
-        case 96 * 4 + 1: return launch_kernel<96, true, true, kEpiF16, 1>(d, 1ull << 28, q, mx, my, p, st);
         case 128 * 4 + 1: return launch_kernel<128, true, true, kEpiF16, 1>(d, 1ull << 29, q, mx, my, p, st);
         case 64 * 4 + 2: return launch_kernel<64, true, true, kEpiF16, 2>(d, 1ull << 30, q, mx, my, p, st);
-        case 96 * 4 + 2: return launch_kernel<96, true, true, kEpiF16, 2>(d, 1ull << 31, q, mx, my, p, st);
         case 128 * 4 + 2: return launch_kernel<128, true, true, kEpiF16, 2>(d, 1ull << 32, q, mx, my, p, st);
         default: return BW_ERR_ARG;
         }

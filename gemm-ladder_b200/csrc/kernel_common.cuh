@@ -109,7 +109,7 @@ struct Geom {
     static_assert(BN % 16 == 0 && BN >= 16 && (BN <= 256 || (PAIR && BN == 512 && WM == 1)),
                   "MMA N: a multiple of 16 in [16, 256] (pair tiles of 512 columns: two MMAs of 256)");
     static_assert(SWAP || BN % (64 * kRanks) == 0, "B tiles are boxes of 64 columns (per block)");
-    static_assert(!(SWAP && PAIR) || BN % 32 == 0, "swap-AB on a pair: MMA N a multiple of 32, half per block");
+    static_assert(!(SWAP && PAIR) || BN == 64 || BN == 128, "swap-AB on a pair: MMA N of 64 or 128, half per block");
     static_assert(WM == 1 || (SWAP && WM == 2), "two weight blocks per tile: swap-AB only");
     static_assert(kYBytes % 1024 == 0 && kXBytes % 1024 == 0, "operand tiles on 1024-byte swizzle atoms");
     static_assert(kStages >= 2 && kSmemBytes <= BW_SMEM_LIMIT, "shared memory");

@@ -81,8 +81,9 @@
 #endif
 #ifndef BW_SWAP_PAIR
 #define BW_SWAP_PAIR 0         // swap-AB on SM pairs (cta_group::2, M = 256: each block 128 x wm weight columns, the
-                               // tokens split over the pair) where the swap-AB tiles go to stream-K: each block takes
-                               // in half the tokens (run on the host emulator; not yet measured)
+                               // tokens, 33 to 128 of them as N = 64 or 128, split over the pair) where the swap-AB
+                               // tiles go to stream-K: each block takes in half the tokens (run on the host emulator;
+                               // not yet measured)
 #endif
 #ifndef BW_SK_PART_WAVE
 #define BW_SK_PART_WAVE 0      // stream-K over every pair when the tiles make more than half a wave but not a whole one
@@ -335,11 +336,12 @@ inline int make_plan(int M, int N, int K, int sms, int pairs, int variant, bw_pl
         q.tiles_n = tiles256;
         q.tiles = q.tiles_n;
     }
-    // BW_SWAP_PAIR: the stream-K swap-AB tiles on SM pairs instead, N rounded up to 32 (half per block); tiles of 2 x
-    // 128 weight columns, or 2 x 256 while those still outnumber the pairs
-    if (BW_SWAP_PAIR && swap && wide_ok && pairs > 0 && q.bn >= 32 && variant != 1) {
+    // BW_SWAP_PAIR: the stream-K swap-AB tiles on SM pairs instead, from 33 tokens, the MMA's N rounded up to 64 or
+    // 128 (half per block; the pair MMA's N kept to those two); tiles of 2 x 128 weight columns, or 2 x 256 while those
+    // still outnumber the pairs
+    if (BW_SWAP_PAIR && swap && wide_ok && pairs > 0 && q.bn > 32 && variant != 1) {
         q.kernel = BW_KERNEL_SWAP_PAIR;
-        q.bn = (q.bn + 31) / 32 * 32;
+        q.bn = q.bn <= 64 ? 64 : 128;
         ranks = 2;
         units = pairs;
         const int tiles512 = (N + 511) / 512;

@@ -171,12 +171,9 @@ int dispatch(const bw_plan& q, const CUtensorMap& mx, const CUtensorMap& my, con
 #if BW_SWAP_PAIR
     if (q.kernel == BW_KERNEL_SWAP_PAIR) {
         switch (q.bn * 4 + q.wm) {
-        case 32 * 4 + 1: return launch<32, true, true, kEpiF16, 1>(q, mx, my, p);
         case 64 * 4 + 1: return launch<64, true, true, kEpiF16, 1>(q, mx, my, p);
-        case 96 * 4 + 1: return launch<96, true, true, kEpiF16, 1>(q, mx, my, p);
         case 128 * 4 + 1: return launch<128, true, true, kEpiF16, 1>(q, mx, my, p);
         case 64 * 4 + 2: return launch<64, true, true, kEpiF16, 2>(q, mx, my, p);
-        case 96 * 4 + 2: return launch<96, true, true, kEpiF16, 2>(q, mx, my, p);
         case 128 * 4 + 2: return launch<128, true, true, kEpiF16, 2>(q, mx, my, p);
         default: return BW_ERR_ARG;
         }

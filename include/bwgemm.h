@@ -31,8 +31,8 @@ extern "C" {
 #define BW_KERNEL_TILE 0   /* 128 x bn tiles of C, A as the MMA's A operand */
 #define BW_KERNEL_SWAP 1   /* M <= 128: C^T = B^T A^T, 128 columns of B as the MMA's A operand, bn = M rounded to 16 */
 #define BW_KERNEL_PAIR 2   /* 256 x bn tiles on a pair of SMs (tcgen05 cta_group::2) */
-#define BW_KERNEL_SWAP_PAIR 3 /* swap-AB on a pair of SMs: 128 (x wm) weight columns per SM, the tokens split over the
-                                pair (built with BW_SWAP_PAIR 1 only) */
+#define BW_KERNEL_SWAP_PAIR 3 /* swap-AB on a pair of SMs: 128 (x wm) weight columns per SM, the tokens (bn 64 or 128)
+                                split over the pair (built with BW_SWAP_PAIR 1 only) */
 
 /*
  * C = A B on `stream` (a cudaStream_t, 0 for the legacy default stream), with the current device.

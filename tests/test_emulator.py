@@ -419,8 +419,8 @@ def test_a_stalled_wide_pair_tile_ends_with_a_status(emu_wide, drop):
 SWAP_PAIR_FORMS = [
     (64, 2560, 256, 16, 1),    # 10 tiles of 2 x 128 weight columns on 8 pairs, stream-K
     (128, 4608, 256, 16, 2),   # 9 tiles of 2 x 256 (two MMAs per stage of A)
-    (32, 2560, 256, 16, 1),    # 16 tokens per block
-    (80, 2624, 192, 16, 1),    # 80 tokens in an MMA N of 96 (48 per block, the last 16 beyond A), a last tile of 64
+    (48, 2560, 256, 16, 1),    # 48 tokens in an MMA N of 64 (32 per block, the last 16 beyond A)
+    (80, 2624, 192, 16, 1),    # 80 tokens in an MMA N of 128 (64 per block, the last 48 beyond A), a last tile of 64
 ]
 
 
@@ -428,10 +428,10 @@ SWAP_PAIR_FORMS = [
 @pytest.mark.parametrize("tn", [False, True], ids=["KxN", "NxK"])
 def test_swap_ab_on_sm_pairs(emu_next, oracle_mod, form, tn):
     """BW_SWAP_PAIR 1: cta_group::2 MMAs of M = 256 over the pair's weight columns (each block its own run of 128 x
-    wm), N = the tokens rounded up to 32, half of them loaded by each block; stream-K over the pairs."""
+    wm), N = the tokens rounded up to 64 or 128, half of them loaded by each block; stream-K over the pairs."""
     M, N, K, sms, wm = form
     q = plan_of(emu_next, M, N, K, sms)
-    assert q["kernel"] == 3 and q["wm"] == wm and q["bn"] % 32 == 0 and q["grid"] == sms, q
+    assert q["kernel"] == 3 and q["wm"] == wm and q["bn"] in (64, 128) and q["grid"] == sms, q
     assert q["tiles"] == -(-N // (256 * wm)), q
     A, B = oracle_mod.lcg_inputs(M, N, K)
     rc, C, status, dirty, nf, msg = emulate(emu_next, A, B, M, N, K, sms, tn=tn)
