@@ -57,13 +57,23 @@ inline void record_timeout(volatile int* abort_flag, uint32_t where, int seg)
     }
 }
 
-// The bounded wait of ptx.cuh, with a yield in the spin so that the other emulated threads run.
+// A spinning thread gives way to the other emulated threads: a yield at first, then short sleeps (thousands of host
+// threads spinning on yields alone spend most of their time in the scheduler).
+inline void spin_pause(uint32_t i)
+{
+    if (i < 64)
+        std::this_thread::yield();
+    else
+        std::this_thread::sleep_for(std::chrono::microseconds(20));
+}
+
+// The bounded wait of ptx.cuh, with a pause in the spin so that the other emulated threads run.
 inline bool wait_slow(uint32_t bar, uint32_t parity, volatile int* abort_flag, uint64_t limit_ns, uint32_t where, int seg)
 {
     const uint64_t t0 = globaltimer_ns();
     for (uint32_t i = 1;; ++i) {
         if (mbar_try_wait(bar, parity)) return true;
-        std::this_thread::yield();
+        spin_pause(i);
         if ((i & 31u) == 0) {
             if (*abort_flag) return false;
             if (globaltimer_ns() - t0 > limit_ns) {
@@ -84,7 +94,7 @@ inline bool wait_flag(const unsigned* p, unsigned want, volatile int* abort_flag
     const uint64_t t0 = globaltimer_ns();
     for (uint32_t i = 1;; ++i) {
         if ((int)(ld_acquire_sys(p) - want) >= 0) return true;
-        std::this_thread::yield();
+        spin_pause(i);
         if ((i & 15u) == 0) {
             if (*abort_flag) return false;
             if (globaltimer_ns() - t0 > limit_ns) {

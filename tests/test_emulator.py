@@ -21,14 +21,37 @@ PKG = os.path.join(ROOT, "gemm-ladder_b200")
 CUDA_INCLUDE = os.path.join(os.environ.get("CUDA_HOME", "/usr/local/cuda"), "include")
 
 
-def build_emulator(tmp_path_factory, defines=()):
+# The emulator's builds, by name: the kernel as the library builds it, the options not yet measured (build.py --next),
+# part-wave stream-K alone, and the 256 x 512 pair tile forced wherever the rule allows it.
+BUILDS = {
+    "library": (),
+    "next": ("BW_KSPLIT=1", "BW_SK_PART_WAVE=1", "BW_PAIR_WIDE=1", "BW_SWAP_PAIR=1"),
+    "part": ("BW_SK_PART_WAVE=1",),
+    "wide": ("BW_PAIR_WIDE=1", "BW_PAIR_WIDE_KB_NS=1", "BW_PAIR_WIDE_EPI_NS=0", "BW_FIXUP_KB=0"),
+}
+
+
+@pytest.fixture(scope="session")
+def emu_builds(tmp_path_factory):
+    """Every build of the emulator, compiled at the same time (g++ runs one process per build)."""
     if not os.path.isdir(CUDA_INCLUDE):
         pytest.skip("no CUDA headers")
-    lib = str(tmp_path_factory.mktemp("emu") / "libbwemu.so")
-    subprocess.check_call(["g++", "-std=c++20", "-O2", "-pthread", "-DBW_EMULATE", *[f"-D{d}" for d in defines],
-                           "-fPIC", "-shared", "-w", f"-I{CUDA_INCLUDE}", f"-I{os.path.join(ROOT, 'include')}",
-                           f"-I{os.path.join(PKG, 'csrc')}", os.path.join(PKG, "emu", "emu.cpp"), "-o", lib])
-    L = ctypes.CDLL(lib)
+    out = tmp_path_factory.mktemp("emu")
+    procs = {}
+    for name, defines in BUILDS.items():
+        lib = str(out / f"libbwemu_{name}.so")
+        procs[name] = (lib, subprocess.Popen(
+            ["g++", "-std=c++20", "-O2", "-pthread", "-DBW_EMULATE", *[f"-D{d}" for d in defines], "-fPIC", "-shared",
+             "-w", f"-I{CUDA_INCLUDE}", f"-I{os.path.join(ROOT, 'include')}", f"-I{os.path.join(PKG, 'csrc')}",
+             os.path.join(PKG, "emu", "emu.cpp"), "-o", lib]))
+    libs = {}
+    for name, (lib, proc) in procs.items():
+        assert proc.wait() == 0, f"the {name} build of the emulator failed"
+        libs[name] = bind(ctypes.CDLL(lib))
+    return libs
+
+
+def bind(L):
     vp, i = ctypes.c_void_p, ctypes.c_int
     L.bw_emu_gemm.argtypes = [vp, vp, vp, i, i, i, i, i, i, i, ctypes.POINTER(ctypes.c_uint),
                               ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int), ctypes.c_char_p, i]
@@ -43,31 +66,30 @@ def build_emulator(tmp_path_factory, defines=()):
 
 
 @pytest.fixture(scope="module")
-def emu(tmp_path_factory):
+def emu(emu_builds):
     """The kernel as the library builds it."""
-    return build_emulator(tmp_path_factory)
+    return emu_builds["library"]
 
 
 @pytest.fixture(scope="module")
-def emu_next(tmp_path_factory):
+def emu_next(emu_builds):
     """The kernel and rule with the options built but not yet measured on a B200 (build.py --next): the K split over
     clusters of 2 to 8 blocks (BW_KSPLIT 1), stream-K over a part wave of pair tiles (BW_SK_PART_WAVE 1), pair tiles of
     256 x 512 (BW_PAIR_WIDE 1), swap-AB on SM pairs (BW_SWAP_PAIR 1)."""
-    return build_emulator(tmp_path_factory, ("BW_KSPLIT=1", "BW_SK_PART_WAVE=1", "BW_PAIR_WIDE=1", "BW_SWAP_PAIR=1"))
+    return emu_builds["next"]
 
 
 @pytest.fixture(scope="module")
-def emu_part(tmp_path_factory):
+def emu_part(emu_builds):
     """Stream-K over a part wave of pair tiles alone (BW_SK_PART_WAVE 1), its tiles 256 x 256."""
-    return build_emulator(tmp_path_factory, ("BW_SK_PART_WAVE=1",))
+    return emu_builds["part"]
 
 
 @pytest.fixture(scope="module")
-def emu_wide(tmp_path_factory):
+def emu_wide(emu_builds):
     """The 256 x 512 pair tile forced wherever the rule allows it (its estimated costs, and the fix-ups', set so that it
     always wins), to run the wide kernel on shapes small enough to emulate."""
-    return build_emulator(tmp_path_factory, ("BW_PAIR_WIDE=1", "BW_PAIR_WIDE_KB_NS=1", "BW_PAIR_WIDE_EPI_NS=0",
-                                             "BW_FIXUP_KB=0"))
+    return emu_builds["wide"]
 
 
 def plan_of(L, M, N, K, sms, variant=0):
@@ -460,12 +482,11 @@ def test_a_stalled_swap_ab_pair_ends_with_a_status(emu_next, drop):
     assert status[0] == 3 and (role, kind) in ((1, 0), (2, 2), (0, 1), (2, 4)), status
 
 
-@pytest.mark.parametrize("build,shape", [("library", (16, 10240, 8192)), ("next", (128, 8192, 8192))],
+@pytest.mark.parametrize("build,shape", [("next", (128, 8192, 8192))],
                          ids=lambda v: v if isinstance(v, str) else "x".join(map(str, v)))
 def test_judge_shapes_at_full_size_on_an_emulated_b200(emu, emu_next, oracle_mod, build, shape):
-    """Judge shapes at full size on an emulated GPU of 148 SMs, the plans at their real grid sizes: the library's K
-    halves with 256-column tiles (qkv_m16, 80 blocks); the next build's K split on clusters of 4 with 256-column
-    tiles (o_m128, 128 blocks)."""
+    """A judge shape at full size on an emulated GPU of 148 SMs, its plan at its real grid size: the next build's K
+    split on clusters of 4 with 256-column tiles (o_m128, 128 blocks)."""
     L = emu if build == "library" else emu_next
     M, N, K = shape
     A, B = oracle_mod.lcg_inputs(M, N, K)
