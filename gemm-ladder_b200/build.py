@@ -46,9 +46,10 @@ def up_to_date(lib=LIB):
 
 
 def build(force=False, verbose=False, trace=False, next_options=False):
-    """Compile libbwgemm.so (trace: libbwgemm_trace.so; next_options: libbwgemm_next.so) if a source is newer than it
-    (or force)."""
-    lib = TRACE_LIB if trace else NEXT_LIB if next_options else LIB
+    """Compile libbwgemm.so (trace: libbwgemm_trace.so; next_options: libbwgemm_next.so; both:
+    libbwgemm_next_trace.so) if a source is newer than it (or force)."""
+    lib = (os.path.join(LIB_DIR, "libbwgemm_next_trace.so") if trace and next_options else TRACE_LIB if trace
+           else NEXT_LIB if next_options else LIB)
     if not force and up_to_date(lib):
         return lib
     os.makedirs(LIB_DIR, exist_ok=True)

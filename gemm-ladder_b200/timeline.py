@@ -1,14 +1,15 @@
 """Per-block timeline of one launch of the rung's kernel, from the library built with the timeline compiled in
 (``python gemm-ladder_b200/build.py --trace`` -> lib/libbwgemm_trace.so).  Needs a GPU.
 
-    python gemm-ladder_b200/timeline.py MxNxK[:variant] [...]   [--dump]
+    python gemm-ladder_b200/timeline.py MxNxK[:variant] [...]   [--dump] [--next]
 
 For each shape: 5 calls, then one timed call whose per-block %globaltimer stamps are read back (bw_trace_read).
 Printed, relative to the earliest block's entry: set-up done, the MMA issuer's first full stage and last commit, the
 epilogue's end, the exit (min / p10 / median / p90 / max over the blocks); the MMA issuer's waits for full stages and
 for a free accumulator; and, by kind of each block's last segment (a whole tile, a split tile's writer, or its
 reducer), when its accumulator was ready, when it decided, and when its reduction copied and summed the partials.
---dump adds the raw stamps of the 8 slowest blocks.
+--dump adds the raw stamps of the 8 slowest blocks.  --next times the library with the options not yet measured
+(build.py --next), the timeline compiled in (lib/libbwgemm_next_trace.so).
 
 The stamps (csrc/gemm_kernel.cuh, BW_TRACE_AT / BW_TRACE_VAL), per block:
   0 entry, 1 set-up done, 2 first full stage, 3 last MMA commit, 4 epilogue done, 5 exit, 6 the last segment's
@@ -32,9 +33,11 @@ SLOTS = 16
 KINDS = {0: "whole", 1: "reducer", 2: "reducer (fast)", 3: "writer"}
 
 
-def load():
-    lib = ctypes.CDLL(build.build(trace=True))
+def load(next_options=False):
+    lib = ctypes.CDLL(build.build(trace=True, next_options=next_options))
     vp, i = ctypes.c_void_p, ctypes.c_int
+    lib.bw_gemm_plan.argtypes = [i, i, i, i, i, ctypes.POINTER(bwgemm.Plan)]
+    lib.bw_gemm_plan.restype = i
     lib.bw_gemm_f16_variant.argtypes = [vp, vp, vp, i, i, i, vp, i]
     lib.bw_gemm_f16_variant.restype = i
     lib.bw_trace_read.argtypes = [ctypes.POINTER(ctypes.c_ulonglong), i]
@@ -46,7 +49,10 @@ def timeline(lib, M, N, K, variant=0, dump=False):
     A = (torch.rand(M, K, device="cuda") * 2 - 1).half()
     B = (torch.rand(K, N, device="cuda") * 2 - 1).half()
     C = torch.empty(M, N, device="cuda", dtype=torch.float16)
-    plan = bwgemm.plan(M, N, K, sms=torch.cuda.get_device_properties(0).multi_processor_count, variant=variant)
+    q = bwgemm.Plan()  # the rule of the library being timed
+    bwgemm.check(lib.bw_gemm_plan(M, N, K, torch.cuda.get_device_properties(0).multi_processor_count, variant,
+                                  ctypes.byref(q)))
+    plan = q.as_dict()
     call = lambda: lib.bw_gemm_f16_variant(A.data_ptr(), B.data_ptr(), C.data_ptr(), M, N, K, None, variant)  # noqa
     for _ in range(5):
         if call():
@@ -105,7 +111,7 @@ def main(argv):
         print(__doc__)
         return 2
     torch.cuda.set_device(0)
-    lib = load()
+    lib = load("--next" in argv)
     for spec in specs:
         shape, _, var = spec.partition(":")
         M, N, K = (int(x) for x in shape.lower().split("x"))
