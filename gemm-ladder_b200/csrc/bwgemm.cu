@@ -159,13 +159,13 @@ int ensure_workspace(DeviceState& d, const bw_plan& q, cudaStream_t st)
 }
 
 // Clusters of two blocks for the SM pair (PAIR), of `ksplit` blocks for a swap-AB plan's K split.
-template <int BN, bool SWAP, bool PAIR, int WM = 1>
+template <int BN, bool SWAP, bool PAIR, int WM = 1, int EPI = kEpiF16>
 cudaLaunchConfig_t launch_config(int grid, cudaStream_t st, cudaLaunchAttribute* attr, int ksplit = 0)
 {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = Geom<BN, SWAP, PAIR, WM>::kSmemBytes;
+    cfg.dynamicSmemBytes = KGeom<BN, SWAP, PAIR, EPI, WM>::kSmemBytes;
     cfg.stream = st;
     const int size = PAIR ? 2 : (SWAP && ksplit > 1) ? ksplit : 1;
     const bool cluster = size > 1;
@@ -183,7 +183,8 @@ int set_smem_limit(DeviceState& d, unsigned long long bit)
 {
     if (d.attrs & bit) return BW_OK;
     cudaError_t e = cudaFuncSetAttribute(gemm_kernel<BN, SWAP, PAIR, EPI, WM>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, Geom<BN, SWAP, PAIR, WM>::kSmemBytes);
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         KGeom<BN, SWAP, PAIR, EPI, WM>::kSmemBytes);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
     d.attrs |= bit;
     return BW_OK;
@@ -225,7 +226,7 @@ template <int BN, bool SWAP, bool PAIR, int EPI = kEpiF16, int WM = 1>
 int launch_kernel(DeviceState& d, unsigned long long bit, const bw_plan& q, const CUtensorMap& mx, const CUtensorMap& my,
                   const Params& p, cudaStream_t st)
 {
-    using G = Geom<BN, SWAP, PAIR, WM>;
+    using G = KGeom<BN, SWAP, PAIR, EPI, WM>;
     // K split: what a block receives from the others of its cluster lands in its idle stage ring
     if (q.smem_bytes != G::kSmemBytes || q.stages != G::kStages || q.tmem_cols != G::kTmemCols || q.wm != WM ||
         (q.ksplit && (!SWAP || q.ksplit < 2 || q.ksplit > 8 || q.grid != q.ksplit * q.tiles ||
@@ -236,7 +237,7 @@ int launch_kernel(DeviceState& d, unsigned long long bit, const bw_plan& q, cons
     int rc = set_smem_limit<BN, SWAP, PAIR, EPI, WM>(d, bit);
     if (rc) return rc;
     cudaLaunchAttribute attr[1];
-    const cudaLaunchConfig_t cfg = launch_config<BN, SWAP, PAIR, WM>(q.grid, st, attr, q.ksplit);
+    const cudaLaunchConfig_t cfg = launch_config<BN, SWAP, PAIR, WM, EPI>(q.grid, st, attr, q.ksplit);
     cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_kernel<BN, SWAP, PAIR, EPI, WM>, mx, my, p);
     if (e != cudaSuccess) return cuda_fail(e, "kernel launch");
     return BW_OK;
@@ -668,7 +669,9 @@ int rs_gemm(bw_rs* rs, const void* A, const void* B, void* C, int K, cudaStream_
     {
         std::lock_guard<std::mutex> lock(g_mu);
         if ((rc = pair_occupancy(*d))) return rc;
-        if ((rc = make_plan(M, N, K, d->sms, d->pairs, 0, &q, kPlanNoSwap | kPlanNoSplit, held_of(*d)))) return rc;
+        if ((rc = make_plan(M, N, K, d->sms, d->pairs, 0, &q, kPlanNoSwap | kPlanNoSplit | kPlanRsWindow,
+                            held_of(*d))))
+            return rc;
     }
     if (q.kernel != BW_KERNEL_PAIR || q.sk_tiles != 0 || q.bn != 256) {
         snprintf(g_errbuf, sizeof g_errbuf, "the fused reduce-scatter needs whole pair tiles");

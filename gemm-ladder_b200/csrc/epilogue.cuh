@@ -328,12 +328,18 @@ __device__ __noinline__ bool reduce_tile_bulk(const Params& p, int P, int tile, 
 // rows: the partial goes into the owner's slot by 16-byte stores (over NVLink), then the slot's flag takes the epoch
 // (each thread's stores ordered before it by a system-scope fence).  The first time a block sends to an owner in a
 // call it waits for the owner's ack of the previous call (the slot is free).  This rank's rows: the other ranks'
-// flags for the tile, then the sum in rank order (this rank's own partial from tensor memory) rounded to fp16 into C,
-// then a count; the block that consumes the call's last tile half acks the epoch.  Every wait is bounded; one thread
-// waits and hands the outcome to the other 127 through `go`.  Returns false after a wait gave up.
+// flags for the tile, then, 64 columns at a time, the sum in rank order (this rank's own partial from tensor memory)
+// rounded to fp16 into C, then a count; the block that consumes the call's last tile half acks the epoch.  The other
+// ranks' partials reach the sum through the window (two 32 KB buffers of shared memory after the ring): each 64-column
+// piece of a partial (32 KB, contiguous in the slot layout) is copied in by the TMA engine (cp.async.bulk, measured
+// 90-98 GB/s per SM against ~35 for 16-byte loads) while the one before it is summed.  win_bar: the buffers' barriers;
+// win_ph: the parity each waits for next (bit b); win_next: the buffer the next copy goes to.  Every wait is bounded;
+// one thread waits and hands the outcome to the other 127 through `go` (two slots, alternating).  Returns false after
+// a wait gave up.
 __device__ __noinline__ bool rs_tile(const Params& p, unsigned epoch, int tm, int tn, int pr, uint32_t tbase, int row,
-                                     int lane, int q, volatile int* abort_flag, volatile int* go, unsigned& acked,
-                                     int seg)
+                                     int lane, int q, volatile int* abort_flag, volatile int* go, volatile int* go2,
+                                     unsigned& acked, uint8_t* window, uint64_t* win_bar0, uint64_t* win_bar1,
+                                     uint32_t& win_ph, int& win_next, int seg)
 {
     const RsTable& rs = *p.rs;
     const Sched& s = p.s;
@@ -381,6 +387,19 @@ __device__ __noinline__ bool rs_tile(const Params& p, unsigned epoch, int tm, in
     named_bar_sync(1, 128);
     if (!ok) return false;
     const int m_local = tm * 256 + pr * 128 - o * rs.rows;  // the block's first row in this rank's C
+    const int others = rs.world - 1;
+    uint64_t* const wbar[2] = {win_bar0, win_bar1};
+    // the 64-column piece c0 of the j-th other rank's partial (j in rank order), into buffer b of the window
+    auto fetch = [&](int j, int c0, int b) {
+        if (threadIdx.x == kEpiThread0) {
+            const uint8_t* src = reinterpret_cast<const uint8_t*>(
+                                     rs.slots[o] + (((size_t)tl * others + j) * 2 + pr) * 128 * 256) +
+                                 (size_t)(c0 / 4) * 128 * 16;
+            mbar_arrive_expect_tx(wbar[b], 32768u);
+            bulk_load(window + b * 32768, src, 32768u, wbar[b]);
+        }
+    };
+    int turn = 0;  // alternates the `go` slots
 #pragma unroll 1
     for (int c0 = 0; c0 < 256; c0 += 64) {
         float v[64];
@@ -394,22 +413,43 @@ __device__ __noinline__ bool rs_tile(const Params& p, unsigned epoch, int tm, in
         }
         // the sum in rank order: rank 0's partial first, this rank's (v) at its place
         float acc[64];
-        for (int src = 0; src < rs.world; ++src) {
-            if (src == rs.rank) {
-#pragma unroll
-                for (int e = 0; e < 64; ++e) acc[e] = src == 0 ? v[e] : acc[e] + v[e];
-                continue;
+        bool own_in = false;
+        fetch(0, c0, win_next);
+#pragma unroll 1
+        for (int j = 0; j < others; ++j) {
+            const int b = win_next;
+            const int src = j < rs.rank ? j : j + 1;
+            if (j + 1 < others) fetch(j + 1, c0, b ^ 1);  // the other buffer was read by every thread before
+            volatile int* slot = (turn++ & 1) ? go2 : go;
+            if (threadIdx.x == kEpiThread0) {
+                const bool okw = wait_bounded(wbar[b], (win_ph >> b) & 1u, abort_flag, p.wait_ns, site(2, 4, b), seg);
+                if (!okw && j + 1 < others)  // the next piece is on its way: let it land before giving up
+                    wait_drain(wbar[b ^ 1], (win_ph >> (b ^ 1)) & 1u, p.wait_ns);
+                *slot = okw ? 1 : 0;
             }
-            const int j = src < rs.rank ? src : src - 1;
-            const float4* slot = reinterpret_cast<const float4*>(
-                rs.slots[o] + (((size_t)tl * (rs.world - 1) + j) * 2 + pr) * 128 * 256);
+            named_bar_sync(1, 128);
+            if (!*slot) return false;
+            mbar_try_wait(smem_u32(wbar[b]), (win_ph >> b) & 1u);  // complete: each thread acquires the bytes
+            win_ph ^= 1u << b;
+            win_next = b ^ 1;
+            if (!own_in && rs.rank < src) {
+#pragma unroll
+                for (int e = 0; e < 64; ++e) acc[e] = rs.rank == 0 ? v[e] : acc[e] + v[e];
+                own_in = true;
+            }
+            const float4* w4 = reinterpret_cast<const float4*>(window + b * 32768) + row;  // [col / 4][row][4]
 #pragma unroll
             for (int k = 0; k < 16; ++k) {
-                const float4 w = __ldcg(slot + (size_t)(c0 / 4 + k) * 128 + row);
+                const float4 w = w4[k * 128];
                 const float x[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
                 for (int e = 0; e < 4; ++e) acc[4 * k + e] = src == 0 ? x[e] : acc[4 * k + e] + x[e];
             }
+            named_bar_sync(1, 128);  // buffer b read by every thread: it may be refilled
+        }
+        if (!own_in) {  // this rank is the last
+#pragma unroll
+            for (int e = 0; e < 64; ++e) acc[e] = acc[e] + v[e];
         }
         store_rows64<kEpiF16>(p, m_local + q * 32, tn * 256 + c0, lane, acc);
     }

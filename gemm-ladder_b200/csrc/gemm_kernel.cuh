@@ -44,7 +44,7 @@ template <int BN, bool SWAP, bool PAIR, int EPI = kEpiF16, int WM = 1>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmy, const Params p)
 {
-    using G = Geom<BN, SWAP, PAIR, WM>;
+    using G = KGeom<BN, SWAP, PAIR, EPI, WM>;
     constexpr int AN = G::kAccN;  // accumulator columns (TMEM)
     static_assert(!SWAP || EPI == kEpiF16, "fp32 and SwiGLU outputs are written by the TILE and PAIR forms");
     static_assert(EPI != kEpiSwiGLU || BN % 32 == 0, "SwiGLU pairs the two halves of a tile");
@@ -357,6 +357,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         int acc = 0, seg = 0;
         uint32_t aph = 0;
         unsigned rs_acked = 0;  // kEpiRS: owners whose ack of the previous call this block has seen
+        uint32_t win_ph = 0;    // kEpiRS: the window's buffers (rbar, krecv): the parity each waits for next
+        int win_next = 0;       // kEpiRS: the buffer the next copy into the window goes to
         // kEpiRS: this call's epoch (the rank's epoch word moves on only once every block has finished, below)
         unsigned rs_epoch = 0u;
         if constexpr (EPI == kEpiRS) rs_epoch = *static_cast<volatile unsigned*>(p.rs->epoch) + 1u;
@@ -406,7 +408,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             if constexpr (EPI == kEpiRS) {
                 int tm, tn;
                 tile_coords(s, sg.tile, tm, tn);
-                rs_tile(p, rs_epoch, tm, tn, rank, tbase, row, lane, q, abort_flag, recv_flag, rs_acked, seg);
+                rs_tile(p, rs_epoch, tm, tn, rank, tbase, row, lane, q, abort_flag, recv_flag, reduce_flag, rs_acked,
+                        smem + G::kWindowOffset, rbar, krecv, win_ph, win_next, seg);
                 release_all(acc);
             } else if (EPI == kEpiSwiGLU) {
                 // a whole tile (the plan splits none): gate columns [0, BN/2), up columns [BN/2, BN) of the tile,

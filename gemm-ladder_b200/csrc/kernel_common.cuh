@@ -77,7 +77,8 @@ __device__ unsigned long long g_trace[1024 * kTraceSlots];
 #define BW_TRACE_AT(slot) ((void)0)
 #endif
 
-template <int BN, bool SWAP, bool PAIR, int WM = 1>
+// RSV: bytes of shared memory reserved after the stage ring (the fused reduce-scatter's window).
+template <int BN, bool SWAP, bool PAIR, int WM = 1, int RSV = 0>
 struct Geom {
     static constexpr int kRanks = PAIR ? 2 : 1;
     static constexpr int kTileM = PAIR ? 256 : 128;          // rows of C per tile (TILE, PAIR)
@@ -90,17 +91,19 @@ struct Geom {
     static constexpr int kYBytes = (BN / kRanks) * kBK * 2;  // this block's MMA-B operand: BN (PAIR: BN / 2) x 64 K
     static constexpr int kStageBytes = kXBytes + kYBytes;
     static constexpr int kCStageBytes = SWAP ? 2 * 16 * 128 * 2 : 0;  // swap-AB epilogue transpose buffers
-    static constexpr int kRingFit = (BW_SMEM_LIMIT - 1024 - 512 - kCStageBytes) / kStageBytes;
+    static constexpr int kRingFit = (BW_SMEM_LIMIT - 1024 - 512 - kCStageBytes - RSV) / kStageBytes;
     static constexpr int kStages = kRingFit < BW_MAX_STAGES ? kRingFit : BW_MAX_STAGES;
     static constexpr int kAccBufs = 2 * kAccN <= 512 ? 2 : 1;  // two accumulators, or one of 512 columns
     // one accumulator of two 256-column halves (a wide pair tile): the halves are released and refilled separately
     static constexpr bool kHalves = kAccBufs == 1 && kWN == 2;
     static constexpr int kTmemCols = pow2_at_least(kAccBufs * kAccN < 32 ? 32 : kAccBufs * kAccN, 32);
-    static constexpr int kBarOffset = kStages * kStageBytes;
+    static constexpr int kRingBytes = kStages * kStageBytes;
+    static constexpr int kWindowOffset = kRingBytes;         // RSV bytes (kEpiRS: the owner's window)
+    static constexpr int kBarOffset = kRingBytes + RSV;
     static constexpr int kNumBars = 2 * kStages + 8;  // full, empty, tmem full x2, tmem empty x2, drain, reduce,
                                                       // and the K split's go / receive
     static constexpr int kSlotBytes = 128 * kAccN * 4;  // one partial of this block's rows
-    static constexpr int kRingSlots = kBarOffset / kSlotBytes;  // partials the idle ring holds at once
+    static constexpr int kRingSlots = kRingBytes / kSlotBytes;  // partials the idle ring holds at once
     static constexpr int kMaxSum = kRingSlots + 1 < 8 ? kRingSlots + 1 : 8;  // partials the bulk reduction sums
     static constexpr int kMiscOffset = kBarOffset + kNumBars * 8;
     // swap-AB: the epilogue transposes each 16-column chunk through two 16 x 128 fp16 buffers
@@ -115,6 +118,10 @@ struct Geom {
     static_assert(kStages >= 2 && kSmemBytes <= BW_SMEM_LIMIT, "shared memory");
     static_assert(kTmemCols <= 512, "tensor memory");
 };
+
+// The geometry of a kernel instance: the fused reduce-scatter's reserves its window.
+template <int BN, bool SWAP, bool PAIR, int EPI, int WM = 1>
+using KGeom = Geom<BN, SWAP, PAIR, WM, EPI == kEpiRS ? kPlanRsWindowBytes : 0>;
 
 // The 3-D form for the MN-major operand (BW_TMA3D): `n64` is the first 64-column block; the map's box holds the
 // stage's blocks.

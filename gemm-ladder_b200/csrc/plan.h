@@ -137,9 +137,11 @@ inline const char* variant_name(int v)
 // takes what the 227 KB leave after the alignment slack, the barriers and the swap-AB epilogue's transpose buffers.
 inline int plan_stage_bytes(int bn, int ranks, int wm = 1) { return 128 * wm * 64 * 2 + (bn / ranks) * 64 * 2; }
 inline int plan_cstage_bytes(bool swap) { return swap ? 2 * 16 * 128 * 2 : 0; }
-inline int plan_stages(int bn, int ranks, bool swap, int wm = 1)
+// The fused reduce-scatter's window (two 32 KB buffers) for the owner's partials, after the stage ring.
+constexpr int kPlanRsWindowBytes = 2 * 32768;
+inline int plan_stages(int bn, int ranks, bool swap, int wm = 1, int reserve = 0)
 {
-    const int s = (BW_SMEM_LIMIT - 1024 - 512 - plan_cstage_bytes(swap)) / plan_stage_bytes(bn, ranks, wm);
+    const int s = (BW_SMEM_LIMIT - 1024 - 512 - plan_cstage_bytes(swap) - reserve) / plan_stage_bytes(bn, ranks, wm);
     return s < BW_MAX_STAGES ? s : BW_MAX_STAGES;
 }
 // Tensor-memory columns for accumulators of acc_n columns: two of them, or one of 512.
@@ -150,10 +152,10 @@ inline int plan_tmem_cols(int acc_n)
     while (c < need) c *= 2;
     return c;
 }
-inline int plan_smem_bytes(int bn, int ranks, bool swap, int wm = 1)
+inline int plan_smem_bytes(int bn, int ranks, bool swap, int wm = 1, int reserve = 0)
 {
-    const int st = plan_stages(bn, ranks, swap, wm);
-    const int misc = st * plan_stage_bytes(bn, ranks, wm) + (2 * st + 8) * 8;
+    const int st = plan_stages(bn, ranks, swap, wm, reserve);
+    const int misc = st * plan_stage_bytes(bn, ranks, wm) + reserve + (2 * st + 8) * 8;
     const int cstage = (misc + 32 + 127) / 128 * 128;
     return 1024 + cstage + plan_cstage_bytes(swap);
 }
@@ -241,6 +243,7 @@ enum : unsigned {
     kPlanNoSwap = 1u,   // A is the MMA's A operand (fp32 and fused outputs are written by TILE and PAIR only)
     kPlanNoSplit = 2u,  // whole tiles only (a fused epilogue needs the complete sums)
     kPlanNarrow = 4u,   // swap-AB tiles of 128 weight columns, pair tiles of 256 (half the partials' scratch)
+    kPlanRsWindow = 8u, // shared memory for the fused reduce-scatter's window (kPlanRsWindowBytes), fewer stages
 };
 
 // sms: the SMs; pairs: the pairs of SMs the pair kernel can hold at once (its cluster occupancy); held (BW_KSPLIT 1,
@@ -380,8 +383,9 @@ inline int make_plan(int M, int N, int K, int sms, int pairs, int variant, bw_pl
         if (q.sk_iters < P) return BW_ERR_ARG;  // every block owns at least one stream-K K-block
     }
     q.grid = P * ranks;
-    q.stages = plan_stages(q.bn, ranks, swap, q.wm);
-    q.smem_bytes = plan_smem_bytes(q.bn, ranks, swap, q.wm);
+    const int reserve = (flags & kPlanRsWindow) ? kPlanRsWindowBytes : 0;
+    q.stages = plan_stages(q.bn, ranks, swap, q.wm, reserve);
+    q.smem_bytes = plan_smem_bytes(q.bn, ranks, swap, q.wm, reserve);
     q.tmem_cols = plan_tmem_cols(q.bn * q.wm);
     q.counters = q.sk_tiles * ranks;
     Sched sc = {};

@@ -101,7 +101,7 @@ Params make_params(const bw_plan& q, int M, int N, int K, void* C, float* work, 
 template <int BN, bool SWAP, bool PAIR, int EPI, int WM>
 int launch(const bw_plan& q, const CUtensorMap& mx, const CUtensorMap& my, const Params& p)
 {
-    using G = Geom<BN, SWAP, PAIR, WM>;
+    using G = KGeom<BN, SWAP, PAIR, EPI, WM>;
     if (q.smem_bytes != G::kSmemBytes || q.stages != G::kStages || q.tmem_cols != G::kTmemCols || q.wm != WM) {
         emu::finding("plan and kernel geometry disagree (bn %d)", BN);
         return BW_ERR_LAUNCH;
@@ -277,7 +277,7 @@ size_t align256(size_t v) { return (v + 255) / 256 * 256; }
 int launch_rs(const bw_plan& q, int world, std::vector<EmuRank>& ranks, const std::vector<CUtensorMap>& mx,
               const std::vector<CUtensorMap>& my, const std::vector<Params>& p, int absent)
 {
-    using G = Geom<256, false, true, 1>;
+    using G = KGeom<256, false, true, kEpiRS, 1>;
     if (q.smem_bytes != G::kSmemBytes || q.stages != G::kStages || q.tmem_cols != G::kTmemCols || q.grid % 2) {
         emu::finding("plan and kernel geometry disagree (reduce-scatter)");
         return BW_ERR_LAUNCH;
@@ -335,7 +335,7 @@ extern "C" __attribute__((visibility("default"))) int bw_emu_gemm_rs(int world, 
     emu::g_tma_count = 0;
     if (world < 2 || world > kRsMaxWorld || M % (256 * world) || !shape_ok(M, N, K)) return BW_ERR_SHAPE;
     bw_plan q = {};
-    int rc = make_plan(M, N, K, sms, sms / 2, 0, &q, kPlanNoSwap | kPlanNoSplit);
+    int rc = make_plan(M, N, K, sms, sms / 2, 0, &q, kPlanNoSwap | kPlanNoSplit | kPlanRsWindow);
     if (rc) return rc;
     if (q.kernel != BW_KERNEL_PAIR || q.sk_tiles != 0 || q.bn != 256) return BW_ERR_LAUNCH;
     // the regions, laid out as bwgemm.cu's bw_rs_create does
