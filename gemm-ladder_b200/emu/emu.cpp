@@ -1,7 +1,7 @@
 // emu.cpp -- the host emulator of the rung's kernel (test infrastructure): gemm_kernel.cuh, unchanged, compiled as
 // host C++ with -DBW_EMULATE over emu_runtime.h / ptx_emu.h, and a launcher that plans a call exactly as the library
 // does (plan.h), builds the same tensor maps and parameters as csrc/bwgemm.cu, and runs the plan's kernel instance on
-// the CPU, cluster after cluster.
+// the CPU, clusters in concurrent batches.
 //
 //   g++ -std=c++20 -O2 -pthread -DBW_EMULATE -fPIC -shared -I<cuda>/include -Iinclude -Igemm-ladder_b200/csrc \
 //       gemm-ladder_b200/emu/emu.cpp -o libbwemu.so        (tests/test_emulator.py builds and drives it)
@@ -97,7 +97,12 @@ Params make_params(const bw_plan& q, int M, int N, int K, void* C, float* work, 
     return p;
 }
 
-// ------------------------------------------------------------------ a launch: clusters one after another
+// ------------------------------------------------------------------ a launch: clusters in batches
+// Blocks of different clusters never wait on one another in a launch (a split tile is summed by whichever block
+// finishes it last), so clusters run in concurrent batches across the host's cores, as many at once as keeps the
+// host threads to a few thousand (g_cluster_batch, 0: that many; 1: one after another).
+inline long long g_cluster_batch = 0;
+
 template <int BN, bool SWAP, bool PAIR, int EPI, int WM>
 int launch(const bw_plan& q, const CUtensorMap& mx, const CUtensorMap& my, const Params& p)
 {
@@ -114,25 +119,33 @@ int launch(const bw_plan& q, const CUtensorMap& mx, const CUtensorMap& my, const
         return BW_ERR_LAUNCH;
     }
     emu::g_smem_limit = q.smem_bytes - 1024;
-    for (int c0 = 0; c0 < q.grid; c0 += cs) {
-        emu::Cluster cl;
-        cl.size = cs;
+    const int cores = (int)std::max(1u, std::thread::hardware_concurrency());
+    const int batch = g_cluster_batch > 0 ? (int)g_cluster_batch
+                                          : std::max(1, std::min(cores, 4096 / (cs * emu::kCtaThreads)));
+    for (int b0 = 0; b0 < q.grid; b0 += batch * cs) {
+        const int b1 = std::min(q.grid, b0 + batch * cs);
+        std::vector<std::unique_ptr<emu::Cluster>> clusters;
         std::vector<std::unique_ptr<emu::Cta>> ctas;
-        for (int r = 0; r < cs; ++r) {
-            ctas.emplace_back(new emu::Cta());
-            ctas[r]->rank = r;
-            ctas[r]->cluster = cs > 1 ? &cl : nullptr;
-            cl.cta[r] = ctas[r].get();
+        for (int c0 = b0; c0 < b1; c0 += cs) {
+            clusters.emplace_back(new emu::Cluster());
+            emu::Cluster* cl = clusters.back().get();
+            cl->size = cs;
+            for (int r = 0; r < cs; ++r) {
+                ctas.emplace_back(new emu::Cta());
+                ctas.back()->rank = r;
+                ctas.back()->cluster = cs > 1 ? cl : nullptr;
+                cl->cta[r] = ctas.back().get();
+            }
         }
         std::vector<std::thread> threads;
-        threads.reserve((size_t)cs * emu::kCtaThreads);
-        for (int r = 0; r < cs; ++r)
+        threads.reserve((size_t)(b1 - b0) * emu::kCtaThreads);
+        for (int blk = b0; blk < b1; ++blk)
             for (int t = 0; t < emu::kCtaThreads; ++t)
-                threads.emplace_back([&, r, t] {
-                    emu::t_cta = ctas[r].get();
+                threads.emplace_back([&, blk, t] {
+                    emu::t_cta = ctas[(size_t)(blk - b0)].get();
                     emu::t_tid = t;
                     threadIdx = dim3((unsigned)t);
-                    blockIdx = dim3((unsigned)(c0 + r));
+                    blockIdx = dim3((unsigned)blk);
                     gridDim = dim3((unsigned)q.grid);
                     blockDim = dim3((unsigned)emu::kCtaThreads);
                     gemm_kernel<BN, SWAP, PAIR, EPI, WM>(mx, my, p);
@@ -210,12 +223,13 @@ int dispatch(const bw_plan& q, const CUtensorMap& mx, const CUtensorMap& my, con
 
 // Sets a knob of the emulator: "wait_ns" (the kernel's limit of one bounded wait), "drop_tma" (the n-th TMA / bulk
 // completion of each launch never arrives, -1 none), "barrier_limit_ms" (a thread barrier never completed: a finding
-// after this long).  Returns 0, or -1 for an unknown name.
+// after this long), "cluster_batch" (clusters run at once; 0: as many as the host's cores take).  Returns 0, or -1 for an unknown name.
 extern "C" __attribute__((visibility("default"))) int bw_emu_set(const char* name, long long value)
 {
     using namespace bw::emu;
     const std::string n = name ? name : "";
     if (n == "wait_ns") g_wait_ns = (unsigned long long)value;
+    else if (n == "cluster_batch") bw::g_cluster_batch = value;
     else if (n == "drop_tma") g_drop_tma = value;
     else if (n == "barrier_limit_ms") g_barrier_limit_ms = value;
     else return -1;

@@ -1,8 +1,9 @@
 // emu_runtime.h -- the host emulator's execution model for the rung's kernel (gemm_kernel.cuh compiled as host C++
 // with -DBW_EMULATE; test infrastructure, never part of the library).
 //
-// A launch runs its clusters one after another (blocks of different clusters meet only through global memory: the
-// split tiles' counters and partials, which the kernel orders with atomics and fences).  Inside a cluster every thread
+// A launch runs its clusters in concurrent batches (blocks of different clusters meet only through global memory:
+// the split tiles' counters and partials, which the kernel orders with atomics and fences; none waits on another).
+// The fused reduce-scatter runs every block of every emulated GPU at once.  Inside a cluster every thread
 // of every block is a host thread, so the kernel's own barriers, mbarrier waits and warp-synchronous code run as they
 // are written.  State per block: its shared memory, its tensor memory (128 lanes x 512 fp32 columns), its mbarriers,
 // named barriers, warp barriers and shuffle slots.
