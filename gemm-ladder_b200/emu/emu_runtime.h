@@ -269,6 +269,15 @@ inline void make_map(CUtensorMap* m, const void* base, int rank, const uint64_t*
                      const uint32_t* box)
 {
     std::memset(m, 0, sizeof *m);
+    // what cuTensorMapEncodeTiled refuses (the library's maps are encoded by the driver, which checks these): a base
+    // not on 16 bytes, row strides not multiples of 16 bytes, boxes outside 1 .. 256, or (128-byte swizzle) an inner
+    // box wider than 128 bytes
+    if (reinterpret_cast<uintptr_t>(base) % 16) finding("a tensor map whose base is not on 16 bytes");
+    for (int i = 0; i < rank; ++i) {
+        if (box[i] < 1 || box[i] > 256) finding("a tensor map box of %u in dimension %d", box[i], i);
+        if (i > 0 && strides[i] % 16) finding("a tensor map stride of %llu bytes", (unsigned long long)strides[i]);
+    }
+    if (box[0] * 2 > 128) finding("a 128-byte-swizzled tensor map box %u elements wide", box[0]);
     Map e;
     e.base = static_cast<const uint8_t*>(base);
     e.rank = rank;
