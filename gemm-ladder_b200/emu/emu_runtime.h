@@ -239,8 +239,8 @@ inline bool mb_try_wait(Cta* c, uint32_t off, uint32_t parity)
 // ------------------------------------------------------------------ thread barriers, shuffles
 inline void named_sync(int id, int count)
 {
-    if (id < 0 || id >= 16) {
-        finding("named barrier %d", id);
+    if (id < 0 || id >= 16 || count <= 0 || count % 32 || count > kCtaThreads) {  // bar.sync: whole warps, ids 0..15
+        finding("named barrier %d of %d threads", id, count);
         return;
     }
     t_cta->named[id].sync(count);
