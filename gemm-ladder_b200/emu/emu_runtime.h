@@ -20,9 +20,12 @@
 #include <cstdint>
 #include <cstdio>
 #include <cstring>
+#include <deque>
+#include <functional>
 #include <map>
 #include <memory>
 #include <mutex>
+#include <random>
 #include <thread>
 #include <vector>
 
@@ -98,6 +101,41 @@ struct MBar {
 };
 
 struct Cluster;
+struct Cta;
+
+// The longest delay (microseconds) before an asynchronous unit carries out an item of work.
+inline int g_engine_delay_us = 20;
+
+// One of a block's asynchronous units (its TMA engine, or its tensor core): work issued to it runs later, in issue
+// order, on a host thread of its own, each item after a random delay of up to g_engine_delay_us -- so the kernel sees
+// its copies land and its MMAs finish only when their barriers say so, as on the GPU, and a read that does not wait
+// for them finds stale data.
+struct Engine {
+    Cta* owner = nullptr;
+    std::mutex m;
+    std::condition_variable cv;
+    std::deque<std::function<void()>> q;
+    bool stop = false;
+    std::thread th;
+    void start(Cta* c);
+    void post(std::function<void()> f)
+    {
+        {
+            std::lock_guard<std::mutex> l(m);
+            q.push_back(std::move(f));
+        }
+        cv.notify_one();
+    }
+    void finish()  // carries out what is queued, then ends
+    {
+        {
+            std::lock_guard<std::mutex> l(m);
+            stop = true;
+        }
+        cv.notify_one();
+        if (th.joinable()) th.join();
+    }
+};
 
 struct Cta {
     std::unique_ptr<uint8_t[]> raw;
@@ -110,10 +148,18 @@ struct Cta {
     Barrier warp[kCtaThreads / 32];
     uint32_t shfl[kCtaThreads / 32][32];
     int tmem_cols = 0;  // allocated columns (0: none)
+    Engine tma, tc;     // the TMA engine (tiled loads, bulk copies) and the tensor core (MMAs, their commits)
     Cta() : raw(new uint8_t[kSmemBytes + 1024]), tmem((size_t)kTmemLanes * kTmemCols, 0u)
     {
         smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(raw.get()) + 1023) & ~uintptr_t(1023));
         std::memset(smem, 0xA5, kSmemBytes);  // not zero: a read of shared memory nothing wrote shows in the result
+        tma.start(this);
+        tc.start(this);
+    }
+    ~Cta()
+    {
+        tma.finish();
+        tc.finish();
     }
 };
 
@@ -132,6 +178,28 @@ inline int g_smem_limit = kSmemBytes;
 inline thread_local Cta* t_cta = nullptr;
 inline thread_local int t_tid = 0;
 inline std::mutex g_mb;  // every mbarrier operation
+
+inline void Engine::start(Cta* c)
+{
+    owner = c;
+    th = std::thread([this] {
+        t_cta = owner;  // the work runs as its block's
+        std::minstd_rand rng((unsigned)reinterpret_cast<uintptr_t>(this));
+        for (;;) {
+            std::function<void()> f;
+            {
+                std::unique_lock<std::mutex> l(m);
+                cv.wait(l, [&] { return stop || !q.empty(); });
+                if (q.empty()) return;
+                f = std::move(q.front());
+                q.pop_front();
+            }
+            const int d = g_engine_delay_us > 0 ? (int)(rng() % (unsigned)(g_engine_delay_us + 1)) : 0;
+            if (d > 0) std::this_thread::sleep_for(std::chrono::microseconds(d));
+            f();
+        }
+    });
+}
 
 inline uint64_t now_ns()
 {

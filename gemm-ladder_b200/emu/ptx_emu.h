@@ -4,14 +4,16 @@
 // What each instruction does here:
 //   mbarrier         a table per block (arrival count, pending arrivals, transaction bytes, completed phases);
 //                    try_wait.parity(p) is true once the phase of parity p has completed.
-//   TMA tiled load   the box is copied at once, element by element from the tensor map's global array (zeros outside
-//                    it), into shared memory in the 128-byte swizzle (16-byte chunk c of 128-byte row r at c ^ (r % 8)),
-//                    then its bytes complete on the barrier (a pair's on the leader block's barrier).
-//   tcgen05.mma      the operands are read through the shared-memory descriptors (start, leading and stride byte
-//                    offsets, 128-byte swizzle; K-major or MN-major from the instruction descriptor) and multiplied in
-//                    fp32 into the block's tensor memory (128 lanes x 512 columns); the pair form takes A's rows and
-//                    B's columns from both blocks and writes each block's rows to its own tensor memory.
-//   tcgen05.commit   an arrival on the barrier (the MMAs before it are complete here).
+//   TMA tiled load   queued to the block's TMA engine (emu_runtime.h, Engine), which later copies the box element by
+//                    element from the tensor map's global array (zeros outside it) into shared memory in the 128-byte
+//                    swizzle (16-byte chunk c of 128-byte row r at c ^ (r % 8)), then completes its bytes on the
+//                    barrier (a pair's on the leader block's barrier).  Bulk copies likewise.
+//   tcgen05.mma      queued to the block's tensor core, which later reads the operands through the shared-memory
+//                    descriptors (start, leading and stride byte offsets, 128-byte swizzle; K-major or MN-major from the
+//                    instruction descriptor) and multiplies them in fp32 into the block's tensor memory (128 lanes x 512
+//                    columns); the pair form takes A's rows and B's columns from both blocks and writes each block's
+//                    rows to its own tensor memory.
+//   tcgen05.commit   queued behind the MMAs: an arrival on the barrier once they have run.
 //   tcgen05.ld       lane (address lane + the thread's lane in its warp), 16 consecutive columns.
 //   clusters         rank, mapa (the rank in the address's top byte), barrier.cluster, remote arrivals, st.async.
 // Every access to shared or tensor memory is bounds-checked, and the checks that fail are recorded as findings
@@ -115,10 +117,22 @@ inline bool wait_bounded(uint64_t* barp, uint32_t parity, volatile int* abort_fl
 
 // ------------------------------------------------------------------ TMA
 inline void prefetch_tmap(const void*) {}
+// A tiled load into this block's shared memory, carried out later by its TMA engine; its bytes complete on `bar`
+// (a shared::cluster address: possibly the pair leader's) when it lands.
+inline void tma_post(void* dst, const void* tmap, int x, int y, int z, uint32_t bar)
+{
+    emu::Cta* c = emu::t_cta;
+    const bool keep = emu::keep_completion();
+    CUtensorMap map;
+    std::memcpy(&map, tmap, sizeof map);  // the map lives in the kernel's parameters: copied as the TMA unit would
+    c->tma.post([=] {
+        const long long bytes = emu::tma_copy(dst, &map, x, y, z);
+        if (keep) emu::mb_complete_tx(emu::cta_of(bar), emu::off_of(bar), bytes);
+    });
+}
 inline void tma_load_2d(void* dst, const void* tmap, int x, int y, uint64_t* bar)
 {
-    const long long bytes = emu::tma_copy(dst, tmap, x, y, 0);
-    if (emu::keep_completion()) emu::mb_complete_tx(emu::t_cta, emu::offset_of(bar), bytes);
+    tma_post(dst, tmap, x, y, 0, emu::offset_of(bar));
 }
 inline void tma_load_2d_hint(void* dst, const void* tmap, int x, int y, uint64_t* bar, uint64_t)
 {
@@ -126,8 +140,7 @@ inline void tma_load_2d_hint(void* dst, const void* tmap, int x, int y, uint64_t
 }
 inline void tma_load_3d(void* dst, const void* tmap, int x, int y, int z, uint64_t* bar)
 {
-    const long long bytes = emu::tma_copy(dst, tmap, x, y, z);
-    if (emu::keep_completion()) emu::mb_complete_tx(emu::t_cta, emu::offset_of(bar), bytes);
+    tma_post(dst, tmap, x, y, z, emu::offset_of(bar));
 }
 inline void tma_load_3d_hint(void* dst, const void* tmap, int x, int y, int z, uint64_t* bar, uint64_t)
 {
@@ -137,8 +150,13 @@ inline uint64_t policy_evict_first() { return 0; }
 inline uint64_t policy_evict_last() { return 0; }
 inline void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar)
 {
-    emu::bulk_copy(dst, src, bytes);
-    if (emu::keep_completion()) emu::mb_complete_tx(emu::t_cta, emu::offset_of(bar), bytes);
+    emu::Cta* c = emu::t_cta;
+    const bool keep = emu::keep_completion();
+    const uint32_t boff = emu::offset_of(bar);
+    c->tma.post([=] {
+        emu::bulk_copy(dst, src, bytes);
+        if (keep) emu::mb_complete_tx(c, boff, bytes);
+    });
 }
 
 // ------------------------------------------------------------------ clusters
@@ -155,13 +173,11 @@ inline void st_async_v4(uint32_t dst, uint32_t a, uint32_t b, uint32_t c, uint32
 inline void fence_acq_rel_cluster() { std::atomic_thread_fence(std::memory_order_seq_cst); }
 inline void tma_load_2d_pair(void* dst, const void* tmap, int x, int y, uint32_t bar)
 {
-    const long long bytes = emu::tma_copy(dst, tmap, x, y, 0);
-    if (emu::keep_completion()) emu::mb_complete_tx(emu::cta_of(bar), emu::off_of(bar), bytes);
+    tma_post(dst, tmap, x, y, 0, bar);
 }
 inline void tma_load_3d_pair(void* dst, const void* tmap, int x, int y, int z, uint32_t bar)
 {
-    const long long bytes = emu::tma_copy(dst, tmap, x, y, z);
-    if (emu::keep_completion()) emu::mb_complete_tx(emu::cta_of(bar), emu::off_of(bar), bytes);
+    tma_post(dst, tmap, x, y, z, bar);
 }
 inline void tma_load_2d_pair_hint(void* dst, const void* tmap, int x, int y, uint32_t bar, uint64_t)
 {
@@ -177,16 +193,26 @@ inline void tmem_relinquish_pair() {}
 inline void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) { emu::tmem_dealloc(taddr, ncols); }
 inline void tc_fence_before() {}
 inline void tc_fence_after() {}
+// MMAs and their commits go to the block's tensor core, which carries them out later and in order: a commit arrives
+// once the MMAs issued before it have run.
 inline void mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate)
 {
-    emu::mma(d_tmem, adesc, bdesc, idesc, accumulate != 0, false);
+    emu::t_cta->tc.post([=] { emu::mma(d_tmem, adesc, bdesc, idesc, accumulate != 0, false); });
 }
 inline void mma_f16_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate)
 {
-    emu::mma(d_tmem, adesc, bdesc, idesc, accumulate != 0, true);
+    emu::t_cta->tc.post([=] { emu::mma(d_tmem, adesc, bdesc, idesc, accumulate != 0, true); });
 }
-inline void mma_commit_pair(uint32_t bar) { emu::mb_arrive(emu::cta_of(bar), emu::off_of(bar), 0); }
-inline void mma_commit(uint64_t* bar) { emu::mb_arrive(emu::t_cta, emu::offset_of(bar), 0); }
+inline void mma_commit_pair(uint32_t bar)
+{
+    emu::t_cta->tc.post([=] { emu::mb_arrive(emu::cta_of(bar), emu::off_of(bar), 0); });
+}
+inline void mma_commit(uint64_t* bar)
+{
+    const uint32_t off = emu::offset_of(bar);
+    emu::Cta* c = emu::t_cta;
+    c->tc.post([=] { emu::mb_arrive(c, off, 0); });
+}
 inline void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) { emu::tmem_ld(taddr, r); }
 inline void tmem_wait_ld() {}
 
