@@ -151,6 +151,11 @@ int launch(const bw_plan& q, const CUtensorMap& mx, const CUtensorMap& my, const
                     gemm_kernel<BN, SWAP, PAIR, EPI, WM>(mx, my, p);
                 });
         for (auto& th : threads) th.join();
+        // every block's queued work (an st.async into another block among it) done before any block goes away
+        for (auto& c : ctas) {
+            c->tma.finish();
+            c->tc.finish();
+        }
     }
     return BW_OK;
 }
@@ -327,6 +332,10 @@ int launch_rs(const bw_plan& q, int world, std::vector<EmuRank>& ranks, const st
         }
     }
     for (auto& th : threads) th.join();
+    for (auto& c : ctas) {
+        c->tma.finish();
+        c->tc.finish();
+    }
     return BW_OK;
 }
 

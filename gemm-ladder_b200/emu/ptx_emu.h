@@ -15,7 +15,8 @@
 //                    rows to its own tensor memory.
 //   tcgen05.commit   queued behind the MMAs: an arrival on the barrier once they have run.
 //   tcgen05.ld       lane (address lane + the thread's lane in its warp), 16 consecutive columns.
-//   clusters         rank, mapa (the rank in the address's top byte), barrier.cluster, remote arrivals, st.async.
+//   clusters         rank, mapa (the rank in the address's top byte), barrier.cluster, remote arrivals, st.async (queued
+//                    like a copy: its bytes land in the other block, and complete on its barrier, later).
 // Every access to shared or tensor memory is bounds-checked, and the checks that fail are recorded as findings
 // (emu::finding) instead of being carried out.
 #pragma once
@@ -164,11 +165,15 @@ inline uint32_t cluster_ctarank() { return (uint32_t)emu::t_cta->rank; }
 inline uint32_t mapa_shared(uint32_t saddr, uint32_t rank) { return emu::mapa(saddr, rank); }
 inline void cluster_sync() { emu::cluster_sync(); }
 inline void mbar_arrive_cluster(uint32_t cluster_addr) { emu::mb_arrive(emu::cta_of(cluster_addr), emu::off_of(cluster_addr), 0); }
+// st.async: the 16 bytes land in the other block later (queued to this block's TMA engine, standing for the path
+// between the blocks), then complete on that block's barrier.
 inline void st_async_v4(uint32_t dst, uint32_t a, uint32_t b, uint32_t c, uint32_t d, uint32_t bar)
 {
-    const uint32_t v[4] = {a, b, c, d};
-    emu::remote_store(dst, v, 16);
-    emu::mb_complete_tx(emu::cta_of(bar), emu::off_of(bar), 16);
+    emu::t_cta->tma.post([=] {
+        const uint32_t v[4] = {a, b, c, d};
+        emu::remote_store(dst, v, 16);
+        emu::mb_complete_tx(emu::cta_of(bar), emu::off_of(bar), 16);
+    });
 }
 inline void fence_acq_rel_cluster() { std::atomic_thread_fence(std::memory_order_seq_cst); }
 inline void tma_load_2d_pair(void* dst, const void* tmap, int x, int y, uint32_t bar)
