@@ -102,6 +102,7 @@ Params make_params(const bw_plan& q, int M, int N, int K, void* C, float* work, 
 // finishes it last), so clusters run in concurrent batches across the host's cores, as many at once as keeps the
 // host threads to a few thousand (g_cluster_batch, 0: that many; 1: one after another).
 inline long long g_cluster_batch = 0;
+inline bool g_dry_run = false;  // dispatch and check a plan's instance and geometry, launch nothing
 
 template <int BN, bool SWAP, bool PAIR, int EPI, int WM>
 int launch(const bw_plan& q, const CUtensorMap& mx, const CUtensorMap& my, const Params& p)
@@ -118,6 +119,7 @@ int launch(const bw_plan& q, const CUtensorMap& mx, const CUtensorMap& my, const
         emu::finding("a launch the library would refuse (cluster %d, grid %d)", cs, q.grid);
         return BW_ERR_LAUNCH;
     }
+    if (g_dry_run) return BW_OK;
     emu::g_smem_limit = q.smem_bytes - 1024;
     const int cores = (int)std::max(1u, std::thread::hardware_concurrency());
     const int batch = g_cluster_batch > 0 ? (int)g_cluster_batch
@@ -239,6 +241,27 @@ extern "C" __attribute__((visibility("default"))) int bw_emu_set(const char* nam
     else if (n == "barrier_limit_ms") g_barrier_limit_ms = value;
     else return -1;
     return 0;
+}
+
+// Plans a call as bw_emu_gemm does and dispatches the plan to its kernel instance without running it: BW_OK if an
+// instance exists whose geometry is the plan's (BW_ERR_ARG / BW_ERR_LAUNCH otherwise), or the plan's own status.
+extern "C" __attribute__((visibility("default"))) int bw_emu_check_plan(int M, int N, int K, int sms, int variant,
+                                                                        int epi, int tn)
+{
+    using namespace bw;
+    bw_plan q = {};
+    const unsigned flags = epi == kEpiF32 ? kPlanNoSwap : epi == kEpiSwiGLU ? kPlanNoSwap | kPlanNoSplit : 0u;
+    if (epi == kEpiSwiGLU && N % 256) return BW_ERR_SHAPE;
+    int rc = make_plan(M, N, K, sms, sms / 2, variant, &q, flags);
+    if (rc) return rc;
+    alignas(64) static const unsigned char dummy[64] = {};
+    CUtensorMap mx, my;
+    make_maps(q, dummy, dummy, M, N, K, &mx, &my, tn != 0);
+    const Params p = make_params(q, M, N, K, nullptr, nullptr, nullptr, tn != 0);
+    g_dry_run = true;
+    rc = dispatch(q, mx, my, p, epi);
+    g_dry_run = false;
+    return rc;
 }
 
 // The plan the launcher takes for a call on the emulated GPU of `sms` SMs (the rule of this build).

@@ -497,3 +497,29 @@ def test_judge_shapes_at_full_size_on_an_emulated_b200(emu, emu_next, oracle_mod
     assert status[0] == 0 and dirty == 0, (status, dirty)
     r = oracle_mod.check(C, oracle_mod.gemm_f64(A, B), K)
     assert r["nonfinite"] == 0 and r["violations"] == 0 and r["normwise"] <= 2e-3, r
+
+
+@pytest.mark.parametrize("build", ["library", "next"])
+def test_every_plan_has_a_kernel_instance(emu_builds, build):
+    """Every plan the rule makes -- over M, N, K, SM counts, variants and outputs -- dispatches to a kernel instance
+    whose geometry (stages, shared and tensor memory, cluster size) is the plan's; a plan with none would fail only on
+    the GPU.  Nothing is launched."""
+    L = emu_builds[build]
+    L.bw_emu_check_plan.argtypes = [ctypes.c_int] * 7
+    L.bw_emu_check_plan.restype = ctypes.c_int
+    Ms = list(range(16, 129, 16)) + [144, 256, 384, 512, 2048, 8192]
+    Ns = [64, 192, 256, 320, 1024, 2176, 5632, 8192, 10240, 28672, 57344]
+    Ks = [64, 576, 8192, 28672]
+    bad = []
+    for sms in (148, 132, 16):
+        for variant in range(8):
+            for epi in (0, 1, 2):
+                if epi and variant:
+                    continue
+                for M in Ms:
+                    for N in Ns:
+                        for K in Ks:
+                            rc = L.bw_emu_check_plan(M, N, K, sms, variant, epi, 0)
+                            if rc and not (epi == 2 and N % 256 and rc == 1):
+                                bad.append((M, N, K, sms, variant, epi, rc))
+    assert not bad, bad[:10]
