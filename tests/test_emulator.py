@@ -523,3 +523,36 @@ def test_every_plan_has_a_kernel_instance(emu_builds, build):
                             if rc and not (epi == 2 and N % 256 and rc == 1):
                                 bad.append((M, N, K, sms, variant, epi, rc))
     assert not bad, bad[:10]
+
+
+def _dispatch_table(path, func):
+    """The plan -> kernel-instance table of a dispatch function, read from its source: for each launch in order, the
+    enclosing #if, the case label or if-condition, and the template arguments with the defaults filled in."""
+    import re
+    src = open(path).read()
+    body = src[src.index(func):]
+    body = body[:body.index("\n}\n")]
+    rows, cond, pending = [], None, ""
+    for line in body.splitlines():
+        s = pending + " " + line.split("//")[0].strip() if pending else line.split("//")[0].strip()
+        pending = s if s.startswith("if (") and "return" not in s and not s.endswith("{") else ""
+        if s.startswith("#if"):
+            cond = s
+        elif s.startswith("#endif"):
+            cond = None
+        m = re.search(r"(case [^:]+:|if \((.*)\))?\s*return launch(?:_kernel)?<([^>]*)>", s)
+        if m:
+            args = [a.strip() for a in m.group(3).split(",")]
+            args += ["kEpiF16", "1"][len(args) - 3:]
+            label = (m.group(1) or "").replace(" ", "")
+            rows.append((cond, label, tuple(args)))
+    return rows
+
+
+def test_the_emulator_dispatches_as_the_library_does():
+    """The emulator's dispatch is the library's plan -> instance table (bwgemm.cu), so the dry run above speaks for
+    the library too."""
+    lib = _dispatch_table(os.path.join(PKG, "csrc", "bwgemm.cu"), "int dispatch(DeviceState& d")
+    emu = _dispatch_table(os.path.join(PKG, "emu", "emu.cpp"), "int dispatch(const bw_plan& q")
+    assert len(lib) == 29  # 4 fp32 / SwiGLU, 2 pair, 3 tile, 4 swap pair, 8 + 8 swap
+    assert lib == emu
