@@ -243,23 +243,30 @@ extern "C" __attribute__((visibility("default"))) int bw_emu_set(const char* nam
     return 0;
 }
 
-// Plans a call as bw_emu_gemm does and dispatches the plan to its kernel instance without running it: BW_OK if an
-// instance exists whose geometry is the plan's (BW_ERR_ARG / BW_ERR_LAUNCH otherwise), or the plan's own status.
+// Plans a call as bw_emu_gemm does (epi kEpiRS: as bw_emu_gemm_rs does, variant and tn unused) and dispatches the plan
+// to its kernel instance without running it: BW_OK if an instance exists whose geometry is the plan's (BW_ERR_ARG /
+// BW_ERR_LAUNCH otherwise; for kEpiRS, BW_ERR_LAUNCH also for a plan of other than whole 256 x 256 pair tiles), or
+// the plan's own status.
 extern "C" __attribute__((visibility("default"))) int bw_emu_check_plan(int M, int N, int K, int sms, int variant,
                                                                         int epi, int tn)
 {
     using namespace bw;
     bw_plan q = {};
-    const unsigned flags = epi == kEpiF32 ? kPlanNoSwap : epi == kEpiSwiGLU ? kPlanNoSwap | kPlanNoSplit : 0u;
+    const unsigned flags = epi == kEpiF32      ? kPlanNoSwap
+                           : epi == kEpiSwiGLU ? kPlanNoSwap | kPlanNoSplit
+                           : epi == kEpiRS     ? kPlanNoSwap | kPlanNoSplit | kPlanRsWindow
+                                               : 0u;
     if (epi == kEpiSwiGLU && N % 256) return BW_ERR_SHAPE;
+    if (epi == kEpiRS) variant = 0, tn = 0;
     int rc = make_plan(M, N, K, sms, sms / 2, variant, &q, flags);
     if (rc) return rc;
+    if (epi == kEpiRS && (q.kernel != BW_KERNEL_PAIR || q.sk_tiles != 0 || q.bn != 256)) return BW_ERR_LAUNCH;
     alignas(64) static const unsigned char dummy[64] = {};
     CUtensorMap mx, my;
     make_maps(q, dummy, dummy, M, N, K, &mx, &my, tn != 0);
     const Params p = make_params(q, M, N, K, nullptr, nullptr, nullptr, tn != 0);
     g_dry_run = true;
-    rc = dispatch(q, mx, my, p, epi);
+    rc = epi == kEpiRS ? launch<256, false, true, kEpiRS, 1>(q, mx, my, p) : dispatch(q, mx, my, p, epi);
     g_dry_run = false;
     return rc;
 }

@@ -522,6 +522,14 @@ def test_every_plan_has_a_kernel_instance(emu_builds, build):
                             rc = L.bw_emu_check_plan(M, N, K, sms, variant, epi, 0)
                             if rc and not (epi == 2 and N % 256 and rc == 1):
                                 bad.append((M, N, K, sms, variant, epi, rc))
+    # the fused reduce-scatter: M a multiple of 256 x world (world 2 .. 8), its plan whole 256 x 256 pair tiles
+    for sms in (148, 132, 16):
+        for M in (512, 768, 1024, 1536, 2048, 3072, 4096, 6144, 8192, 16384):
+            for N in Ns:
+                for K in Ks:
+                    rc = L.bw_emu_check_plan(M, N, K, sms, 0, 3, 0)
+                    if rc:
+                        bad.append((M, N, K, sms, "rs", rc))
     assert not bad, bad[:10]
 
 
@@ -556,3 +564,24 @@ def test_the_emulator_dispatches_as_the_library_does():
     emu = _dispatch_table(os.path.join(PKG, "emu", "emu.cpp"), "int dispatch(const bw_plan& q")
     assert len(lib) == 29  # 4 fp32 / SwiGLU, 2 pair, 3 tile, 4 swap pair, 8 + 8 swap
     assert lib == emu
+
+
+def test_each_kernel_instance_has_its_own_attribute_bit():
+    """The library sets each instance's shared-memory limit once per device, remembered by one bit of a 64-bit word
+    (bwgemm.cu, set_smem_limit): two instances on one bit would leave the second without its limit, a launch failure
+    seen only on a GPU.  Each instance keeps one bit wherever it is named, and no bit serves two instances."""
+    import re
+    src = open(os.path.join(PKG, "csrc", "bwgemm.cu")).read()
+    consts = {m.group(1): int(m.group(2)) for m in re.finditer(r"constexpr unsigned (\w+) = 1u << (\d+);", src)}
+    by_inst, by_bit = {}, {}
+    for m in re.finditer(r"(?:launch_kernel|set_smem_limit)<([^>]*)>\(\*?d, ([^,)]+)", src):
+        if m.group(2).strip() == "bit":
+            continue
+        args = [a.strip() for a in m.group(1).split(",")]
+        inst = tuple(args + ["kEpiF16", "1"][len(args) - 3:])
+        b = m.group(2).strip()
+        bit = consts[b] if b in consts else int(re.fullmatch(r"1u?l?l? << (\d+)", b).group(1))
+        assert 0 <= bit < 64
+        assert by_inst.setdefault(inst, bit) == bit, (inst, bit)
+        assert by_bit.setdefault(bit, inst) == inst, (bit, inst)
+    assert len(by_inst) >= 30
