@@ -569,21 +569,15 @@ int noalloc_gemm(const void* A, const void* B, void* C, int M, int N, int K, cud
     {
         std::lock_guard<std::mutex> lock(g_mu);
         if ((rc = pair_occupancy(*d))) return rc;
-        auto fits = [&] {
-            return q.workspace_bytes <= BW_NOALLOC_SCRATCH_BYTES && (unsigned)q.counters <= BW_NOALLOC_COUNTERS;
-        };
-        if ((rc = make_plan(M, N, K, d->sms, d->pairs, 0, &q, 0u, held_of(*d)))) return rc;
-        // 256-column swap tiles', 512-column pair tiles' and swap-AB pairs' partials are twice as large: the
-        // narrower tiles on single SMs if those fit the array
-        if (!fits() && (q.wm > 1 || q.bn > 256 || q.kernel == BW_KERNEL_SWAP_PAIR) &&
-            (rc = make_plan(M, N, K, d->sms, d->pairs, 0, &q, kPlanNarrow, held_of(*d))))
-            return rc;
-        if (!fits()) {
+        rc = make_plan_capped(M, N, K, d->sms, d->pairs, &q, BW_NOALLOC_SCRATCH_BYTES, BW_NOALLOC_COUNTERS,
+                              held_of(*d));
+        if (rc == BW_ERR_SCRATCH) {
             snprintf(g_errbuf, sizeof g_errbuf,
                      "%d x %d x %d needs %zu bytes of partials and %d counters; the fixed array holds %u and %u", M, N,
                      K, q.workspace_bytes, q.counters, BW_NOALLOC_SCRATCH_BYTES, BW_NOALLOC_COUNTERS);
             return BW_ERR_SCRATCH;
         }
+        if (rc) return rc;
         if (!g_noalloc_addr[dev]) {  // once per device, this device current
             void* ptr = nullptr;
             if ((e = cudaGetSymbolAddress(&ptr, g_bw_noalloc_scratch)) != cudaSuccess)

@@ -197,11 +197,11 @@ inline bool shape_ok(int M, int N, int K)
 
 // The split-K factor for a tail of `tail` tiles on P blocks: minimises the tail's time in tile-times,
 // ceil(tail s / P) / s, plus the reduction of s partials (each about fixup_kb K-blocks of work for the last block).
-inline int tail_splits(int tail, int P, int kblocks, double fixup_kb)
+inline int tail_splits(int tail, int P, int kblocks, double fixup_kb, int max_sp = 16)
 {
     int best = 1;
     double best_cost = 1.0;
-    for (int sp = 2; sp <= 16 && sp <= kblocks; ++sp) {
+    for (int sp = 2; sp <= 16 && sp <= max_sp && sp <= kblocks; ++sp) {
         const double waves = (double)((tail * sp + P - 1) / P);
         const double cost = waves / sp + sp * fixup_kb / kblocks;
         if (cost < best_cost - 1e-9) {
@@ -249,7 +249,7 @@ enum : unsigned {
 // sms: the SMs; pairs: the pairs of SMs the pair kernel can hold at once (its cluster occupancy); held (BW_KSPLIT 1,
 // may be null): held[c], c = 2 .. 8, the clusters of c swap-AB blocks the device holds at once (null: sms / c).
 inline int make_plan(int M, int N, int K, int sms, int pairs, int variant, bw_plan* p, unsigned flags = 0,
-                     const int* held = nullptr)
+                     const int* held = nullptr, size_t work_cap = 0)
 {
     if (!p || variant < 0 || variant >= kVariants || sms <= 0) return BW_ERR_ARG;
     if (!shape_ok(M, N, K)) return BW_ERR_SHAPE;
@@ -363,7 +363,13 @@ inline int make_plan(int M, int N, int K, int sms, int pairs, int variant, bw_pl
     } else {
         // split-K over the partial wave, if it pays
         const int tail = q.tiles % units;
-        const int sp = tail_splits(tail, units, q.kblocks, /*fixup_kb=*/BW_FIXUP_KB * q.bn / 256);
+        // a fixed scratch of work_cap bytes (0: none) holds at most work_cap / (tail x one partial) splits of the tail
+        int max_sp = 16;
+        if (work_cap) {
+            const size_t per = (size_t)tail * ranks * 128 * q.bn * q.wm * sizeof(float);
+            max_sp = work_cap / per < 16 ? (int)(work_cap / per) : 16;
+        }
+        const int sp = tail_splits(tail, units, q.kblocks, /*fixup_kb=*/BW_FIXUP_KB * q.bn / 256, max_sp);
         if (sp > 1) {
             q.dp_tiles = q.tiles - tail;
             q.sk_tiles = tail;
@@ -394,6 +400,25 @@ inline int make_plan(int M, int N, int K, int sms, int pairs, int variant, bw_pl
     q.workspace_bytes = (size_t)workspace_slots(sc, P) * ranks * 128 * q.bn * q.wm * sizeof(float);
     *p = q;
     return BW_OK;
+}
+
+// The plan of a call whose split-tile scratch is a fixed array of `work_cap` bytes of partials and `counter_cap`
+// counters (bw_gemm_f16_noalloc), the first of these that fits: the rule's plan (variant 0); where the rule's partials
+// are twice as large (256-column swap tiles, 512-column pair tiles, swap-AB pairs), the plan on the narrower tiles
+// (kPlanNarrow); that plan with its split-K tail cut to the splits the array holds; whole tiles (kPlanNoSplit), which
+// keep no partials.  BW_ERR_SCRATCH, with *p the last plan tried, if none fits (whole tiles always do).
+inline int make_plan_capped(int M, int N, int K, int sms, int pairs, bw_plan* p, size_t work_cap,
+                            unsigned counter_cap, const int* held = nullptr)
+{
+    auto fits = [&] { return p->workspace_bytes <= work_cap && (unsigned)p->counters <= counter_cap; };
+    int rc = make_plan(M, N, K, sms, pairs, 0, p, 0u, held);
+    if (rc || fits()) return rc;
+    if ((p->wm > 1 || p->bn > 256 || p->kernel == BW_KERNEL_SWAP_PAIR) &&
+        ((rc = make_plan(M, N, K, sms, pairs, 0, p, kPlanNarrow, held)) || fits()))
+        return rc;
+    if ((rc = make_plan(M, N, K, sms, pairs, 0, p, kPlanNarrow, held, work_cap ? work_cap : 1)) || fits()) return rc;
+    if ((rc = make_plan(M, N, K, sms, pairs, 0, p, kPlanNoSplit, held))) return rc;
+    return fits() ? BW_OK : BW_ERR_SCRATCH;
 }
 
 }  // namespace bw

@@ -103,6 +103,7 @@ Params make_params(const bw_plan& q, int M, int N, int K, void* C, float* work, 
 // host threads to a few thousand (g_cluster_batch, 0: that many; 1: one after another).
 inline long long g_cluster_batch = 0;
 inline bool g_dry_run = false;  // dispatch and check a plan's instance and geometry, launch nothing
+inline long long g_noalloc_cap = -1;  // >= 0: bw_emu_gemm plans as bw_gemm_f16_noalloc does, with this many bytes
 
 template <int BN, bool SWAP, bool PAIR, int EPI, int WM>
 int launch(const bw_plan& q, const CUtensorMap& mx, const CUtensorMap& my, const Params& p)
@@ -230,7 +231,8 @@ int dispatch(const bw_plan& q, const CUtensorMap& mx, const CUtensorMap& my, con
 
 // Sets a knob of the emulator: "wait_ns" (the kernel's limit of one bounded wait), "drop_tma" (the n-th TMA / bulk
 // completion of each launch never arrives, -1 none), "barrier_limit_ms" (a thread barrier never completed: a finding
-// after this long), "cluster_batch" (clusters run at once; 0: as many as the host's cores take).  Returns 0, or -1 for an unknown name.
+// after this long), "cluster_batch" (clusters run at once; 0: as many as the host's cores take), "noalloc_cap"
+// (>= 0: fp16 calls of variant 0 plan as bw_gemm_f16_noalloc does, its array this many bytes; -1: the rule).  Returns 0, or -1 for an unknown name.
 extern "C" __attribute__((visibility("default"))) int bw_emu_set(const char* name, long long value)
 {
     using namespace bw::emu;
@@ -239,6 +241,7 @@ extern "C" __attribute__((visibility("default"))) int bw_emu_set(const char* nam
     else if (n == "cluster_batch") bw::g_cluster_batch = value;
     else if (n == "drop_tma") g_drop_tma = value;
     else if (n == "barrier_limit_ms") g_barrier_limit_ms = value;
+    else if (n == "noalloc_cap") bw::g_noalloc_cap = value;
     else return -1;
     return 0;
 }
@@ -271,6 +274,16 @@ extern "C" __attribute__((visibility("default"))) int bw_emu_check_plan(int M, i
     return rc;
 }
 
+// The plan bw_gemm_f16_noalloc takes on the emulated GPU of `sms` SMs, its scratch a fixed array of `work_cap` bytes
+// of partials and `counter_cap` counters (the library's: BW_NOALLOC_SCRATCH_BYTES, BW_NOALLOC_COUNTERS): BW_OK, or
+// BW_ERR_SCRATCH if no plan fits.
+extern "C" __attribute__((visibility("default"))) int bw_emu_noalloc_plan(int M, int N, int K, int sms,
+                                                                          long long work_cap, int counter_cap,
+                                                                          bw_plan* out)
+{
+    return bw::make_plan_capped(M, N, K, sms, sms / 2, out, (size_t)work_cap, (unsigned)counter_cap);
+}
+
 // The plan the launcher takes for a call on the emulated GPU of `sms` SMs (the rule of this build).
 extern "C" __attribute__((visibility("default"))) int bw_emu_plan(int M, int N, int K, int sms, int variant,
                                                                   bw_plan* out)
@@ -293,7 +306,9 @@ extern "C" __attribute__((visibility("default"))) int bw_emu_gemm(const void* A,
     bw_plan q = {};
     const unsigned flags = epi == kEpiF32 ? kPlanNoSwap : epi == kEpiSwiGLU ? kPlanNoSwap | kPlanNoSplit : 0u;
     if (epi == kEpiSwiGLU && N % 256) return BW_ERR_SHAPE;
-    int rc = make_plan(M, N, K, sms, sms / 2, variant, &q, flags);
+    int rc = g_noalloc_cap >= 0 && epi == kEpiF16 && variant == 0
+                 ? make_plan_capped(M, N, K, sms, sms / 2, &q, (size_t)g_noalloc_cap, BW_NOALLOC_COUNTERS)
+                 : make_plan(M, N, K, sms, sms / 2, variant, &q, flags);
     if (rc) return rc;
     std::vector<float> work(q.workspace_bytes / sizeof(float) + 4, 0.f);
     std::vector<int> counters((size_t)q.counters + 1, 0);

@@ -25,7 +25,7 @@ extern "C" {
 #define BW_ERR_TIMEOUT 3   /* a kernel's bounded wait on a barrier gave up; see bw_gemm_status */
 #define BW_ERR_ARG 4       /* null or misaligned pointer, unknown variant */
 #define BW_ERR_DEVICE 5    /* the current device is not an sm_100 (B200-class) GPU */
-#define BW_ERR_SCRATCH 6   /* bw_gemm_f16_noalloc: the call needs more scratch than its fixed array holds */
+#define BW_ERR_SCRATCH 6   /* bw_gemm_f16_noalloc: no plan's scratch fits its fixed array (whole tiles always do) */
 
 /* Kernels of the rule (bw_plan.kernel). */
 #define BW_KERNEL_TILE 0   /* 128 x bn tiles of C, A as the MMA's A operand */
@@ -99,12 +99,16 @@ int bw_gemm_dirty(void);
  * array of BW_NOALLOC_SCRATCH_BYTES + 4 * BW_NOALLOC_COUNTERS bytes, compiled into the library: every GPU that loads
  * the library holds it until the process exits.  The first call on a device looks up that array's device address
  * (once, with the device current); make that first call before any stream capture.  Calls never allocate or free.
- * A call whose plan needs more scratch than the array holds takes the plan with swap-AB tiles of 128 weight columns
- * if that one fits (half the partials), and is otherwise refused with BW_ERR_SCRATCH before anything runs.
+ * The array holds the stream-K partials of any plan on a GPU of up to 160 SMs (two 256 x 256 fp32 slots per SM pair,
+ * 37 MiB on a B200), so every judge, ladder and decode shape takes the rule's own plan.  A call whose plan needs more
+ * than the array holds takes the first of these that fits: the narrower tiles (where the rule's are 256-column swap
+ * tiles, 512-column pair tiles or swap-AB pairs), the same plan with its split-K tail cut to the splits the array
+ * holds, whole tiles (no partials).  So no call is refused for scratch; BW_ERR_SCRATCH is kept for a plan that
+ * somehow still does not fit.
  * Every call shares the one array and clears the counters it uses on its stream first: two calls that overlap on
  * the GPU (different streams, or several host threads) race on it; order them, or use bw_gemm_f16.
  */
-#define BW_NOALLOC_SCRATCH_BYTES (20u << 20) /* fp32 partials: 20 MiB */
+#define BW_NOALLOC_SCRATCH_BYTES (40u << 20) /* fp32 partials: 40 MiB */
 #define BW_NOALLOC_COUNTERS 4096u            /* split-tile counters */
 int bw_gemm_f16_noalloc(const void* A, const void* B, void* C, int M, int N, int K, void* stream);
 

@@ -585,3 +585,75 @@ def test_each_kernel_instance_has_its_own_attribute_bit():
         assert by_inst.setdefault(inst, bit) == bit, (inst, bit)
         assert by_bit.setdefault(bit, inst) == inst, (bit, inst)
     assert len(by_inst) >= 30
+
+
+def header_constant(name):
+    """A #define of include/bwgemm.h: `(a u << b)`, `a u` or `a`."""
+    import re
+    with open(os.path.join(ROOT, "include", "bwgemm.h")) as f:
+        m = re.search(r"#define\s+%s\s+(?:\((\d+)u\s*<<\s*(\d+)\)|(\d+)u?\b)" % name, f.read())
+    return int(m.group(1)) << int(m.group(2)) if m.group(1) else int(m.group(3))
+
+
+@pytest.mark.parametrize("build", ["library", "next"])
+def test_the_no_allocation_plan_fits_its_array(emu_builds, build):
+    """bw_gemm_f16_noalloc's plan (plan.h, make_plan_capped) on a 148-SM B200.  With the library's fixed array every
+    judge, ladder, verif, edge and decode shape takes the library rule's own plan, and a sweep up to 16384 x 131072 x 57344
+    gets plans whose partials and counters fit.  With a quarter of the array (and none at all) no call is refused
+    either: the largest plans fall back to narrower tiles, fewer splits of the tail, or whole tiles."""
+    import bwgemm
+    from shapes import B200_EDGES, CONFIG1, DECODE_M, DECODE_WEIGHTS, JUDGE_B200, LADDER_4096, VERIF
+
+    L = emu_builds[build]
+    L.bw_emu_noalloc_plan.argtypes = [ctypes.c_int] * 4 + [ctypes.c_longlong, ctypes.c_int,
+                                                            ctypes.POINTER(bwgemm.Plan)]
+    L.bw_emu_noalloc_plan.restype = ctypes.c_int
+    cap = header_constant("BW_NOALLOC_SCRATCH_BYTES")
+    counters = header_constant("BW_NOALLOC_COUNTERS")
+    named = [(m, n, k) for _, m, n, k in JUDGE_B200] + [LADDER_4096[1:], CONFIG1[1:]] + list(VERIF)
+    named += list(B200_EDGES) + [(m, n, k) for m in DECODE_M for (_, n, k) in DECODE_WEIGHTS]
+    for M, N, K in named:
+        q = bwgemm.Plan()
+        assert L.bw_emu_noalloc_plan(M, N, K, 148, cap, counters, ctypes.byref(q)) == 0, (M, N, K)
+        if build == "library":  # the next build's 512-column stream-K tiles keep 74 MiB: narrower tiles there
+            assert q.as_dict() == plan_of(L, M, N, K, 148), (M, N, K)
+    sweep = [(m, n, k) for m in (16, 64, 128, 256, 512, 1024, 4096, 16384) for n in (256, 4096, 10240, 28672, 131072)
+             for k in (64, 4096, 57344)]
+    seen = set()
+    for limit in (cap, cap // 4, 0):
+        for M, N, K in named + sweep:
+            rule, q = plan_of(L, M, N, K, 148), bwgemm.Plan()
+            assert L.bw_emu_noalloc_plan(M, N, K, 148, limit, counters, ctypes.byref(q)) == 0, (M, N, K, limit)
+            assert q.workspace_bytes <= limit and q.counters <= counters, (M, N, K, limit)
+            if q.as_dict() != rule:
+                seen.add("whole tiles" if q.sk_tiles == 0 else "fewer splits" if 0 < q.splits < rule["splits"]
+                         else "narrower" if q.bn < rule["bn"] or q.wm < rule["wm"] else "other")
+    assert {"whole tiles", "fewer splits"} <= seen, seen
+
+
+def test_the_no_allocation_fallbacks_run(emu, oracle_mod):
+    """The plans bw_gemm_f16_noalloc falls back to when its array is short (plan.h, make_plan_capped) run right:
+    a split-K tail cut to fewer splits, and whole tiles, each against the fp64 oracle with the counters left clear."""
+    import bwgemm
+
+    M, N, K, sms = 144, 256, 4672, 8  # one pair tile, split three ways, ragged rows
+    rule = plan_of(emu, M, N, K, sms)
+    assert rule["splits"] >= 3
+    emu.bw_emu_noalloc_plan.argtypes = [ctypes.c_int] * 4 + [ctypes.c_longlong, ctypes.c_int,
+                                                              ctypes.POINTER(bwgemm.Plan)]
+    A, B = oracle_mod.lcg_inputs(M, N, K)
+    ref = oracle_mod.gemm_f64(A, B)
+    kinds = []
+    for cap in (rule["workspace_bytes"] - 1, 0):
+        q = bwgemm.Plan()
+        assert emu.bw_emu_noalloc_plan(M, N, K, sms, cap, 4096, ctypes.byref(q)) == 0
+        kinds.append("fewer splits" if 1 < q.splits < rule["splits"] else "whole tiles" if q.sk_tiles == 0 else "?")
+        assert emu.bw_emu_set(b"noalloc_cap", cap) == 0
+        try:
+            rc, C, status, dirty, nf, msg = emulate(emu, A, B, M, N, K, sms)
+        finally:
+            emu.bw_emu_set(b"noalloc_cap", -1)
+        assert rc == 0 and nf == 0 and status[0] == 0 and dirty == 0, (cap, rc, nf, msg, status, dirty)
+        r = oracle_mod.check(C, ref, K)
+        assert r["nonfinite"] == 0 and r["violations"] == 0 and r["normwise"] <= 2e-3, (cap, r)
+    assert kinds == ["fewer splits", "whole tiles"], kinds

@@ -4,8 +4,9 @@ Callers such as a serving process whose device memory is all owned by its own al
 else's process, may not call cudaMalloc; this entry point keeps the scratch of split tiles in a fixed array compiled
 into the library.  Checked here: two calls in a row give the same C as bw_gemm_f16 within the per-element bound the
 other tests use (2 ulp16 of the reference value + 1e-3 sqrt(K)), on shapes whose plan splits tiles (stream-K at
-M <= 128, a split-K tail on the SM pairs) and on one that splits none; and a call needing more scratch than the array
-holds is refused with BW_ERR_SCRATCH.  This file is collected last, and passes alone in a fresh process too.
+M <= 128 and on the SM pairs, a split-K tail on the SM pairs) and on one that splits none; and a call whose rule plan
+needs more scratch than the array holds runs on a plan that fits (fewer splits of the tail) instead of being refused.
+This file is collected last, and passes alone in a fresh process too.
 """
 import ctypes
 import os
@@ -18,8 +19,6 @@ torch = pytest.importorskip("torch")
 import bwgemm  # noqa: E402
 
 pytestmark = pytest.mark.gpu
-
-BW_ERR_SCRATCH = 6
 
 
 def header_constant(name):
@@ -57,9 +56,11 @@ def within_bound(C, ref, K):
     return bool(torch.isfinite(C.float()).all()) and bool((diff <= bound).all())
 
 
-# stream-K on the swap-AB kernel (bn 16 and bn 128, the largest scratch of the judge's shapes), a split-K tail on
-# the SM pairs, whole tiles only (no scratch used)
-SHAPES = [(16, 8192, 8192), (128, 10240, 8192), (4608, 5632, 8192), (512, 8192, 8192), (272, 5376, 128)]
+# stream-K on the swap-AB kernel (bn 16 and bn 128), stream-K over the SM pairs (the judge's qkv_m512: 37 MiB, the
+# largest scratch of the judge's shapes), a split-K tail on the SM pairs, whole tiles only
+# (no scratch used)
+SHAPES = [(16, 8192, 8192), (128, 10240, 8192), (512, 10240, 8192), (4608, 5632, 8192), (512, 8192, 8192),
+          (272, 5376, 128)]
 
 
 @pytest.mark.parametrize("shape", SHAPES, ids=lambda s: "x".join(map(str, s)))
@@ -80,22 +81,27 @@ def test_noalloc_agrees_with_the_allocating_entry(lib, shape):
         assert within_bound(C, ref, K), f"call {call}: C differs from bw_gemm_f16's beyond the bound"
 
 
-def test_noalloc_refuses_a_call_beyond_its_array(lib):
+def test_noalloc_runs_a_call_beyond_its_array(lib):
+    """A call whose rule plan keeps more partials than the array holds (a split-K tail of 7 splits at K = 57344) runs
+    on a plan that fits: the tail cut to fewer splits (plan.h, make_plan_capped).  Its C agrees with bw_gemm_f16's."""
     limit = header_constant("BW_NOALLOC_SCRATCH_BYTES")
     sms = torch.cuda.get_device_properties(0).multi_processor_count
     big = None
-    for M in (256, 512):
-        for N in range(256, 16385, 256):
-            if bwgemm.plan(M, N, 8192, sms=sms)["workspace_bytes"] > limit:
-                big = (M, N, 8192)
-                break
-        if big:
+    for N in range(256, 16385, 256):
+        if bwgemm.plan(256, N, 57344, sms=sms)["workspace_bytes"] > limit:
+            big = (256, N, 57344)
             break
-    assert big, "no shape found whose plan needs more scratch than the array"
+    assert big, "no shape found whose rule plan needs more scratch than the array"
     M, N, K = big
     A, B = inputs(M, N, K, seed=1)
-    C = torch.empty((M, N), dtype=torch.float16, device="cuda")
-    rc = lib.bw_gemm_f16_noalloc(A.data_ptr(), B.data_ptr(), C.data_ptr(), M, N, K,
-                                 torch.cuda.current_stream().cuda_stream)
-    assert rc == BW_ERR_SCRATCH
-    assert "fixed array" in lib.bw_last_error_string().decode()
+    stream = torch.cuda.current_stream().cuda_stream
+    ref = torch.empty((M, N), dtype=torch.float16, device="cuda")
+    assert bwgemm.gemm_ptr(A.data_ptr(), B.data_ptr(), ref.data_ptr(), M, N, K, stream) == 0
+    for call in range(2):
+        C = torch.empty((M, N), dtype=torch.float16, device="cuda")
+        C.view(torch.int16).fill_(-1)
+        rc = lib.bw_gemm_f16_noalloc(A.data_ptr(), B.data_ptr(), C.data_ptr(), M, N, K, stream)
+        torch.cuda.synchronize()
+        assert rc == 0, f"call {call}: {lib.bw_status_string(rc).decode()}: {lib.bw_last_error_string().decode()}"
+        assert bwgemm.status()[0] == 0
+        assert within_bound(C, ref, K), f"call {call}: C differs from bw_gemm_f16's beyond the bound"
