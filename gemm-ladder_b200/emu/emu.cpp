@@ -246,10 +246,10 @@ extern "C" __attribute__((visibility("default"))) int bw_emu_set(const char* nam
     return 0;
 }
 
-// Plans a call as bw_emu_gemm does (epi kEpiRS: as bw_emu_gemm_rs does, variant and tn unused) and dispatches the plan
-// to its kernel instance without running it: BW_OK if an instance exists whose geometry is the plan's (BW_ERR_ARG /
-// BW_ERR_LAUNCH otherwise; for kEpiRS, BW_ERR_LAUNCH also for a plan of other than whole 256 x 256 pair tiles), or
-// the plan's own status.
+// Plans a call as bw_emu_gemm does (epi kEpiRS: as bw_emu_gemm_rs does, variant and tn unused), makes its tensor maps
+// and dispatches the plan to its kernel instance without running it: BW_OK if the maps are within the driver's limits
+// and an instance exists whose geometry is the plan's (BW_ERR_ARG / BW_ERR_LAUNCH otherwise; for kEpiRS,
+// BW_ERR_LAUNCH also for a plan of other than whole 256 x 256 pair tiles), or the plan's own status.
 extern "C" __attribute__((visibility("default"))) int bw_emu_check_plan(int M, int N, int K, int sms, int variant,
                                                                         int epi, int tn)
 {
@@ -266,12 +266,13 @@ extern "C" __attribute__((visibility("default"))) int bw_emu_check_plan(int M, i
     if (epi == kEpiRS && (q.kernel != BW_KERNEL_PAIR || q.sk_tiles != 0 || q.bn != 256)) return BW_ERR_LAUNCH;
     alignas(64) static const unsigned char dummy[64] = {};
     CUtensorMap mx, my;
-    make_maps(q, dummy, dummy, M, N, K, &mx, &my, tn != 0);
+    emu::g_findings = 0;
+    make_maps(q, dummy, dummy, M, N, K, &mx, &my, tn != 0);  // the driver's limits on a tensor map: findings
     const Params p = make_params(q, M, N, K, nullptr, nullptr, nullptr, tn != 0);
     g_dry_run = true;
     rc = epi == kEpiRS ? launch<256, false, true, kEpiRS, 1>(q, mx, my, p) : dispatch(q, mx, my, p, epi);
     g_dry_run = false;
-    return rc;
+    return rc ? rc : emu::g_findings ? BW_ERR_LAUNCH : BW_OK;
 }
 
 // The plan bw_gemm_f16_noalloc takes on the emulated GPU of `sms` SMs, its scratch a fixed array of `work_cap` bytes

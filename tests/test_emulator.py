@@ -501,9 +501,9 @@ def test_judge_shapes_at_full_size_on_an_emulated_b200(emu, emu_next, oracle_mod
 
 @pytest.mark.parametrize("build", ["library", "next"])
 def test_every_plan_has_a_kernel_instance(emu_builds, build):
-    """Every plan the rule makes -- over M, N, K, SM counts, variants and outputs -- dispatches to a kernel instance
-    whose geometry (stages, shared and tensor memory, cluster size) is the plan's; a plan with none would fail only on
-    the GPU.  Nothing is launched."""
+    """Every plan the rule makes -- over M, N, K, SM counts, variants, outputs and both B layouts -- has tensor maps
+    within the driver's limits and dispatches to a kernel instance whose geometry (stages, shared and tensor memory,
+    cluster size) is the plan's; a plan without would fail only on the GPU.  Nothing is launched."""
     L = emu_builds[build]
     L.bw_emu_check_plan.argtypes = [ctypes.c_int] * 7
     L.bw_emu_check_plan.restype = ctypes.c_int
@@ -519,9 +519,10 @@ def test_every_plan_has_a_kernel_instance(emu_builds, build):
                 for M in Ms:
                     for N in Ns:
                         for K in Ks:
-                            rc = L.bw_emu_check_plan(M, N, K, sms, variant, epi, 0)
-                            if rc and not (epi == 2 and N % 256 and rc == 1):
-                                bad.append((M, N, K, sms, variant, epi, rc))
+                            for tn in (0, 1):
+                                rc = L.bw_emu_check_plan(M, N, K, sms, variant, epi, tn)
+                                if rc and not (epi == 2 and N % 256 and rc == 1):
+                                    bad.append((M, N, K, sms, variant, epi, tn, rc))
     # the fused reduce-scatter: M a multiple of 256 x world (world 2 .. 8), its plan whole 256 x 256 pair tiles
     for sms in (148, 132, 16):
         for M in (512, 768, 1024, 1536, 2048, 3072, 4096, 6144, 8192, 16384):
@@ -657,3 +658,35 @@ def test_the_no_allocation_fallbacks_run(emu, oracle_mod):
         r = oracle_mod.check(C, ref, K)
         assert r["nonfinite"] == 0 and r["violations"] == 0 and r["normwise"] <= 2e-3, (cap, r)
     assert kinds == ["fewer splits", "whole tiles"], kinds
+
+
+def _calls(path, func, names):
+    """The calls of `names` in a function's body, in order, with their arguments, whitespace removed."""
+    src = open(path).read()
+    body = src[src.index(func):]
+    body = body[body.index("{"):body.index("\n}\n")]
+    out, i = [], 0
+    while True:
+        hits = [(body.find(n + "(", i), n) for n in names]
+        hits = [h for h in hits if h[0] >= 0 and (h[0] == 0 or not (body[h[0] - 1].isalnum() or body[h[0] - 1] == "_"))]
+        if not hits:
+            return out
+        at, n = min(hits)
+        j, depth = at + len(n), 0
+        while True:
+            depth += {"(": 1, ")": -1}.get(body[j], 0)
+            j += 1
+            if depth == 0:
+                break
+        out.append((n, "".join(body[at + len(n) + 1:j - 1].split())))
+        i = j
+
+
+def test_the_emulator_makes_the_library_maps():
+    """The emulator's tensor maps (emu.cpp, make_maps) are the library's (bwgemm.cu, make_maps): the same maps, boxes
+    and B layouts, in the same branches, so the dry run's check of the driver's limits speaks for the library."""
+    lib = _calls(os.path.join(PKG, "csrc", "bwgemm.cu"), "bool make_maps(const bw_plan& q", ["make_map", "make_map_blocks"])
+    emu = _calls(os.path.join(PKG, "emu", "emu.cpp"), "void make_maps(const bw_plan& q", ["map2", "map_blocks"])
+    rename = {"make_map": "map2", "make_map_blocks": "map_blocks"}
+    assert len(lib) == 12
+    assert [(rename[n], a) for n, a in lib] == emu
