@@ -136,3 +136,34 @@ def test_the_pipelined_loop_orders_every_reuse_of_a_slot(monkeypatch):
     start = [r for r in records if r[1] < gemms[2][1]][-1]
     timed_first_copy = ops(cs, "copy", "A0")[1]
     assert happens_before(start, timed_first_copy)
+
+
+def _bench(*argv, env=None):
+    import subprocess
+    e = dict(os.environ, **(env or {}))
+    return subprocess.run([sys.executable, os.path.join(os.path.dirname(HERE), "bench.py"), *argv], env=e,
+                          capture_output=True, text=True, timeout=600)
+
+
+def test_the_reference_arm_prints_its_line_on_the_cpu():
+    """bench.py --impl reference times the reference's CPU path (the oracle's restatement) on the host cores and
+    prints one JSON line with the contract's keys; it needs no GPU."""
+    import json
+    r = _bench("--impl", "reference", "--shape", "64x256x128", "--steps", "2", "--warmup", "1",
+               env={"RANK": "0", "WORLD_SIZE": "1"})
+    assert r.returncode == 0, r.stderr[-2000:]
+    lines = [l for l in r.stdout.splitlines() if l.startswith("{")]
+    assert len(lines) == 1, r.stdout
+    out = json.loads(lines[0])
+    for key in ("metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step", "higher_is_better", "scaling",
+                "vs_baseline", "dtype", "data", "config", "cpu_baseline", "e2e"):
+        assert key in out, key
+    assert out["impl"] == "reference" and out["steps"] == 2 and out["warmup"] == 1 and out["value"] > 0
+    assert out["cpu_baseline"]["value"] == out["value"] and out["cpu_baseline"]["kind"] in ("port", "reference")
+    assert out["e2e"] == {"value": out["value"], "unit": out["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
+
+
+def test_the_reference_arm_runs_on_rank_0_only():
+    r = _bench("--impl", "reference", "--shape", "64x256x128", "--steps", "1", "--warmup", "1",
+               env={"RANK": "1", "WORLD_SIZE": "2"})
+    assert r.returncode == 0 and r.stdout.strip() == "", (r.stdout, r.stderr[-2000:])
