@@ -690,3 +690,37 @@ def test_the_emulator_makes_the_library_maps():
     rename = {"make_map": "map2", "make_map_blocks": "map_blocks"}
     assert len(lib) == 12
     assert [(rename[n], a) for n, a in lib] == emu
+
+
+def _random_cases(seed, n):
+    """Seeded random calls: M a multiple of 16 (ragged against the tiles), N of 64, K of 64, 2 to 16 SMs, any variant,
+    either B layout; sized so the oracle and the emulator finish each in well under a second."""
+    rng = np.random.default_rng(seed)
+    out = []
+    while len(out) < n:
+        M = int(rng.integers(1, 25)) * 16
+        N = int(rng.integers(1, 21)) * 64
+        K = int(rng.integers(1, 25)) * 64
+        if M * N * K > 120_000_000:
+            continue
+        out.append((M, N, K, int(rng.choice([2, 3, 4, 6, 8, 10, 12, 16])), int(rng.integers(0, 8)),
+                    bool(rng.integers(0, 2))))
+    return out
+
+
+@pytest.mark.parametrize("build", ["library", "next"])
+def test_random_calls_on_the_emulator(emu_builds, oracle_mod, build):
+    """24 seeded random calls per build (shapes, SM counts, variants, B layouts) against the fp64 oracle, with no
+    finding, the status word clear and the counters at zero."""
+    L = emu_builds[build]
+    bad = []
+    for M, N, K, sms, variant, tn in _random_cases(11 if build == "library" else 12, 24):
+        A, B = oracle_mod.lcg_inputs(M, N, K)
+        rc, C, status, dirty, nf, msg = emulate(L, A, B, M, N, K, sms, variant=variant, tn=tn)
+        if rc or nf or status[0] or dirty:
+            bad.append((M, N, K, sms, variant, tn, rc, nf, msg, status[0], dirty))
+            continue
+        r = oracle_mod.check(C, oracle_mod.gemm_f64(A, B), K)
+        if r["nonfinite"] or r["violations"] or r["normwise"] > 2e-3:
+            bad.append((M, N, K, sms, variant, tn, r))
+    assert not bad, bad
