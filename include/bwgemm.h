@@ -100,10 +100,11 @@ int bw_gemm_dirty(void);
  * the library holds it until the process exits.  The first call on a device looks up that array's device address
  * (once, with the device current); make that first call before any stream capture.  Calls never allocate or free.
  * The array holds the stream-K partials of any plan on a GPU of up to 160 SMs (two 256 x 256 fp32 slots per SM pair,
- * 37 MiB on a B200), so every judge, ladder and decode shape takes the rule's own plan.  A call whose plan needs more
- * than the array holds takes the first of these that fits: the narrower tiles (where the rule's are 256-column swap
- * tiles, 512-column pair tiles or swap-AB pairs), the same plan with its split-K tail cut to the splits the array
- * holds, whole tiles (no partials).  So no call is refused for scratch; BW_ERR_SCRATCH is kept for a plan that
+ * 37 MiB on a B200), so on a B200's 74 pairs every judge, ladder and decode shape takes the rule's own plan (on a
+ * device that holds fewer pairs at once, down_m2048's split-K tail can take fewer splits).  A call whose plan needs
+ * more than the array holds takes the first of these that fits: the narrower tiles (where the rule's are 256-column
+ * swap tiles, 512-column pair tiles or swap-AB pairs), the same plan with its split-K tail cut to the splits the
+ * array holds, whole tiles (no partials).  So no call is refused for scratch; BW_ERR_SCRATCH is kept for a plan that
  * somehow still does not fit.
  * Every call shares the one array and clears the counters it uses on its stream first: two calls that overlap on
  * the GPU (different streams, or several host threads) race on it; order them, or use bw_gemm_f16.
