@@ -618,6 +618,11 @@ def test_the_no_allocation_plan_fits_its_array(emu_builds, build):
         assert L.bw_emu_noalloc_plan(M, N, K, 148, cap, counters, ctypes.byref(q)) == 0, (M, N, K)
         if build == "library":  # the next build's 512-column stream-K tiles keep 74 MiB: narrower tiles there
             assert q.as_dict() == plan_of(L, M, N, K, 148), (M, N, K)
+    for sms in (140, 142, 144, 146):  # a device that holds 70 to 73 pairs at once: fitting plans, the rule's or not
+        for M, N, K in named:
+            q = bwgemm.Plan()
+            assert L.bw_emu_noalloc_plan(M, N, K, sms, cap, counters, ctypes.byref(q)) == 0, (M, N, K, sms)
+            assert q.workspace_bytes <= cap and q.counters <= counters, (M, N, K, sms)
     sweep = [(m, n, k) for m in (16, 64, 128, 256, 512, 1024, 4096, 16384) for n in (256, 4096, 10240, 28672, 131072)
              for k in (64, 4096, 57344)]
     seen = set()
