@@ -74,7 +74,8 @@ int bw_gemm_f16_f32out(const void* A, const void* B, void* C, int M, int N, int 
  */
 int bw_gemm_f16_swiglu(const void* A, const void* B, void* C, int M, int N, int K, void* stream);
 
-/* The number of variants.  Replaces: the weak `int g_nvar` (probe/probe.cu:40, hopper/verif.cu:38, hopper/step7.cu:16). */
+/* The number of variants.  Replaces: the weak `int g_nvar` (probe/probe.cu:40, hopper/verif.cu:38,
+ * hopper/step7.cu:16). */
 int bw_gemm_variant_count(void);
 
 /* A one-line description of variant v (NULL if v is out of range).  Replaces: the variant list in the header comment
@@ -178,7 +179,8 @@ int bw_gemm_plan(int M, int N, int K, int sms, int variant, bw_plan* out);
  * a bounded wait gave up since the last clear; *site = role << 16 | barrier kind << 8 | index of the first wait that
  * gave up, *block its block, *segment the segment that block was on.  Kinds: 0 a full stage, 1 an empty stage, 2 a
  * finished accumulator, 3 a free accumulator, 4 partials copied in, 5 and 6 a K-split cluster's pieces and go signal,
- * 7 another rank's partial of the fused reduce-scatter (index: the sender), 8 a rank's ack of the previous call.  Returns a CUDA error as BW_ERR_LAUNCH.
+ * 7 another rank's partial of the fused reduce-scatter (index: the sender), 8 a rank's ack of the previous call.
+ * Returns a CUDA error as BW_ERR_LAUNCH.
  * No reference counterpart as a function: the reference traps in its guarded wait (hopper/step2.cuh:128-145); this
  * rung's waits return instead and leave the context usable.
  */
