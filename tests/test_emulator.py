@@ -482,17 +482,18 @@ def test_a_stalled_swap_ab_pair_ends_with_a_status(emu_next, drop):
     assert status[0] == 3 and (role, kind) in ((1, 0), (2, 2), (0, 1), (2, 4)), status
 
 
-@pytest.mark.parametrize("build,shape", [("library", (16, 10240, 8192)), ("next", (128, 8192, 8192)),
-                                         ("next", (128, 10240, 8192))],
-                         ids=lambda v: v if isinstance(v, str) else "x".join(map(str, v)))
-def test_judge_shapes_at_full_size_on_an_emulated_b200(emu, emu_next, oracle_mod, build, shape):
+@pytest.mark.parametrize("build,shape,tn", [("library", (16, 10240, 8192), False), ("next", (128, 8192, 8192), False),
+                                            ("next", (128, 10240, 8192), False), ("next", (128, 8192, 8192), True)],
+                         ids=lambda v: v if isinstance(v, str) else ("NxK" if v else "KxN") if isinstance(v, bool)
+                         else "x".join(map(str, v)))
+def test_judge_shapes_at_full_size_on_an_emulated_b200(emu, emu_next, oracle_mod, build, shape, tn):
     """Judge shapes at full size on an emulated GPU of 148 SMs, their plans at their real grid sizes: the library's K
     halves with 256-column tiles (qkv_m16, 80 blocks); the next build's K split on clusters of 4 with 256-column tiles
-    (o_m128, 128 blocks) and on clusters of 3 (qkv_m128, 120 blocks)."""
+    (o_m128, 128 blocks, B as K x N and as N x K) and on clusters of 3 (qkv_m128, 120 blocks)."""
     L = emu if build == "library" else emu_next
     M, N, K = shape
     A, B = oracle_mod.lcg_inputs(M, N, K)
-    rc, C, status, dirty, nf, msg = emulate(L, A, B, M, N, K, 148)
+    rc, C, status, dirty, nf, msg = emulate(L, A, B, M, N, K, 148, tn=tn)
     assert rc == 0 and nf == 0, f"rc {rc}, {nf} findings, first: {msg}"
     assert status[0] == 0 and dirty == 0, (status, dirty)
     r = oracle_mod.check(C, oracle_mod.gemm_f64(A, B), K)
