@@ -1,8 +1,9 @@
 """Build the rung's native code in-tree: gemm-ladder_b200/lib/libbwgemm.so (sm_100a, cross-compiled by nvcc; no GPU
 needed).  ``python gemm-ladder_b200/build.py [--force] [--trace] [--next]``; --trace builds lib/libbwgemm_trace.so,
-the same library with the per-block timeline compiled in (-DBW_TRACE, read by timeline.py); --next builds
-lib/libbwgemm_next.so, the library with the options built but not yet measured on a B200 (the K split over clusters
-of 2 to 8, stream-K over a part wave of pair tiles, pair tiles of 256 x 512, swap-AB on SM pairs), for A/B runs: BWGEMM_LIB=libbwgemm_next.so selects it."""
+the same library with the per-block timeline compiled in (-DBW_TRACE: per block, %globaltimer stamps of its phases,
+read back with bw_trace_read); --next builds lib/libbwgemm_next.so, the library with the options built but not yet
+measured on a B200 (the K split over clusters of 2 to 8, stream-K over a part wave of pair tiles, pair tiles of
+256 x 512, swap-AB on SM pairs), for A/B runs: BWGEMM_LIB=libbwgemm_next.so selects it."""
 import os
 import shutil
 import subprocess

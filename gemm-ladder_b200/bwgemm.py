@@ -82,6 +82,10 @@ def lib():
         L.bw_gemm_dirty.restype = i
         L.bw_gemm_plan.argtypes = [i, i, i, i, i, ctypes.POINTER(Plan)]
         L.bw_gemm_plan.restype = i
+        L.bw_gemm_device_plan.argtypes = [i, i, i, i, i, ctypes.POINTER(Plan)]
+        L.bw_gemm_device_plan.restype = i
+        L.bw_gemm_f16_noalloc.argtypes = [vp, vp, vp, i, i, i, vp]
+        L.bw_gemm_f16_noalloc.restype = i
         u = ctypes.POINTER(ctypes.c_uint)
         L.bw_gemm_status.argtypes = [ctypes.POINTER(ctypes.c_int), u, u, u]
         L.bw_gemm_status.restype = i
@@ -135,6 +139,14 @@ def variants():
 def plan(M, N, K, sms=148, variant=0):
     p = Plan()
     check(lib().bw_gemm_plan(M, N, K, sms, variant, ctypes.byref(p)))
+    return p.as_dict()
+
+
+def device_plan(M, N, K, variant=0, noalloc=False):
+    """The plan a call takes on the current device (bw_gemm_device_plan): the rule on the device's own pair count, or
+    the no-allocation entry's plan (the rule's, or the fallback that fits its fixed array)."""
+    p = Plan()
+    check(lib().bw_gemm_device_plan(M, N, K, variant, 1 if noalloc else 0, ctypes.byref(p)))
     return p.as_dict()
 
 

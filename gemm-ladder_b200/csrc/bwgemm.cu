@@ -106,6 +106,21 @@ unsigned long long initial_wait_ns()
 }
 unsigned long long g_wait_ns = initial_wait_ns();
 
+// The fused reduce-scatter's waits on other ranks (their partials, their ack of the previous call): the ranks'
+// processes reach a call out of step by host-side work (a first call's module loading and plan, a slow rank's launch
+// queue), so these waits get a longer limit than the pipeline's own barriers.  BWGEMM_RANK_WAIT_NS sets it (default
+// 10 s; never below the barrier limit).
+unsigned long long initial_rank_wait_ns()
+{
+    const char* e = getenv("BWGEMM_RANK_WAIT_NS");
+    if (e) {
+        const unsigned long long v = strtoull(e, nullptr, 10);
+        if (v > 0) return v;
+    }
+    return 10000000000ull;  // 10 s
+}
+unsigned long long g_rank_wait_ns = initial_rank_wait_ns();
+
 int device_state(DeviceState** out)
 {
     int dev = 0;
@@ -332,6 +347,7 @@ Params make_params(const bw_plan& q, int M, int N, int K, void* C, float* work, 
     p.work = work;
     p.counters = counters;
     p.wait_ns = g_wait_ns;
+    p.rank_wait_ns = g_rank_wait_ns > g_wait_ns ? g_rank_wait_ns : g_wait_ns;
     return p;
 }
 
@@ -530,7 +546,7 @@ BW_API const char* bw_status_string(int status)
 {
     switch (status) {
     case BW_OK: return "ok";
-    case BW_ERR_SHAPE: return "shape not supported (M % 16, N % 64 and K % 64 must be 0, all positive)";
+    case BW_ERR_SHAPE: return "shape not supported (M, N, K positive; N % 64 and K % 64 must be 0)";
     case BW_ERR_LAUNCH: return "CUDA error (see bw_last_error_string)";
     case BW_ERR_TIMEOUT: return "a bounded wait on a barrier gave up (see bw_gemm_status)";
     case BW_ERR_ARG: return "bad argument (null or misaligned pointer, unknown variant)";
@@ -564,17 +580,18 @@ int noalloc_gemm(const void* A, const void* B, void* C, int M, int N, int K, cud
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
-    bw_plan q = {};
+    bw_plan q = {}, rule = {};
     void* scratch = nullptr;
     {
         std::lock_guard<std::mutex> lock(g_mu);
         if ((rc = pair_occupancy(*d))) return rc;
         rc = make_plan_capped(M, N, K, d->sms, d->pairs, &q, BW_NOALLOC_SCRATCH_BYTES, BW_NOALLOC_COUNTERS,
-                              held_of(*d));
+                              held_of(*d), &rule);
         if (rc == BW_ERR_SCRATCH) {
             snprintf(g_errbuf, sizeof g_errbuf,
-                     "%d x %d x %d needs %zu bytes of partials and %d counters; the fixed array holds %u and %u", M, N,
-                     K, q.workspace_bytes, q.counters, BW_NOALLOC_SCRATCH_BYTES, BW_NOALLOC_COUNTERS);
+                     "%d x %d x %d: the rule's plan needs %zu bytes of partials and %d counters and no fallback fits; "
+                     "the fixed array holds %u and %u", M, N, K, rule.workspace_bytes, rule.counters,
+                     BW_NOALLOC_SCRATCH_BYTES, BW_NOALLOC_COUNTERS);
             return BW_ERR_SCRATCH;
         }
         if (rc) return rc;
@@ -606,6 +623,20 @@ int noalloc_gemm(const void* A, const void* B, void* C, int M, int N, int K, cud
 BW_API int bw_gemm_f16_noalloc(const void* A, const void* B, void* C, int M, int N, int K, void* stream)
 {
     return bw::noalloc_gemm(A, B, C, M, N, K, static_cast<cudaStream_t>(stream));
+}
+
+BW_API int bw_gemm_device_plan(int M, int N, int K, int variant, int noalloc, bw_plan* out)
+{
+    if (!out || variant < 0 || variant >= bw::kVariants || (noalloc && variant != 0)) return BW_ERR_ARG;
+    bw::DeviceState* d = nullptr;
+    int rc = bw::device_state(&d);
+    if (rc) return rc;
+    std::lock_guard<std::mutex> lock(bw::g_mu);
+    if ((rc = bw::pair_occupancy(*d))) return rc;
+    if (noalloc)
+        return bw::make_plan_capped(M, N, K, d->sms, d->pairs, out, BW_NOALLOC_SCRATCH_BYTES, BW_NOALLOC_COUNTERS,
+                                    bw::held_of(*d));
+    return bw::make_plan(M, N, K, d->sms, d->pairs, variant, out, 0u, bw::held_of(*d));
 }
 
 #ifdef BW_TRACE

@@ -229,6 +229,9 @@ __device__ __noinline__ bool reduce_tile_bulk(const Params& p, int P, int tile, 
     const Sched& s = p.s;
     const int L = f.nseg - (own_mine ? 1 : 0);
     if (threadIdx.x == kEpiThread0) {
+        // the other blocks' partials were written by ordinary stores, made visible to this thread by its acquire of
+        // the tile's counter; the bulk copies below read through the async proxy, so order them after that view
+        fence_proxy_async_global();
         mbar_arrive_expect_tx(rbar, (uint32_t)(L * kSlotBytes));
         for (int j = 0; j < L; ++j) {
             const int i = (own_mine && j >= f.mine) ? j + 1 : j;
@@ -348,7 +351,7 @@ __device__ __noinline__ bool rs_tile(const Params& p, unsigned epoch, int tm, in
     if (o != rs.rank) {
         if (!(acked >> o & 1u)) {
             if (threadIdx.x == kEpiThread0)
-                *go = wait_flag(rs.ack[o], epoch - 1u, abort_flag, p.wait_ns, site(2, 8, (uint32_t)o), seg) ? 1 : 0;
+                *go = wait_flag(rs.ack[o], epoch - 1u, abort_flag, p.rank_wait_ns, site(2, 8, (uint32_t)o), seg) ? 1 : 0;
             named_bar_sync(1, 128);
             const bool ok = *go != 0;
             named_bar_sync(1, 128);  // `go` is read by all before it is written again
@@ -378,8 +381,11 @@ __device__ __noinline__ bool rs_tile(const Params& p, unsigned epoch, int tm, in
     if (threadIdx.x == kEpiThread0) {
         bool ok = true;
         for (int j = 0; j < rs.world - 1 && ok; ++j)
-            ok = wait_flag(rs.flags[o] + ((size_t)tl * (rs.world - 1) + j) * 2 + pr, epoch, abort_flag, p.wait_ns,
-                           site(2, 7, (uint32_t)j), seg);
+            ok = wait_flag(rs.flags[o] + ((size_t)tl * (rs.world - 1) + j) * 2 + pr, epoch, abort_flag,
+                           p.rank_wait_ns, site(2, 7, (uint32_t)j), seg);
+        // the peers' partials came by ordinary stores over NVLink, visible to this thread after its acquires of their
+        // flags; this thread's bulk copies of them (fetch) go through the async proxy, so order them after that view
+        if (ok) fence_proxy_async_global();
         *go = ok ? 1 : 0;
     }
     named_bar_sync(1, 128);

@@ -55,6 +55,8 @@ struct Params {
     float* work;                 // the partials: workspace_slots() x (PAIR ? 2 : 1) slots of 128 x BN fp32, row-major
     int* counters;               // one per split tile (per block of the pair), zero between calls
     unsigned long long wait_ns;  // the limit of any single wait on a barrier
+    unsigned long long rank_wait_ns;  // kEpiRS: the limit of a wait on another rank (its partials, its ack), longer
+                                      // than wait_ns: the ranks' processes reach their first call out of step
     int tn;                      // 1: B is N x K row-major (K-major for the tensor core, like A); 0: K x N
     const RsTable* rs;           // kEpiRS only: the ranks' regions
 };

@@ -190,10 +190,14 @@ inline double ksplit_cost(int M, int N, int K, int bn, int wm, int c)
     return (t_hbm > t_in ? t_hbm : t_in) + sent / (BW_DSMEM_GBS * 1e3);
 }
 
-inline bool shape_ok(int M, int N, int K)
-{
-    return M > 0 && N > 0 && K > 0 && M % 16 == 0 && N % 64 == 0 && K % 64 == 0;
-}
+// The shapes the library serves: N and K multiples of 64 (the TMA boxes' widths), any M >= 1.  Rows of A past M
+// reach the tensor core as the TMA engine's zero fill and rows of C past M are never stored, so the tokens of a decode
+// step (M = 1, 8, ...) need no padding in the caller's memory.
+inline bool shape_ok(int M, int N, int K) { return M > 0 && N > 0 && K > 0 && N % 64 == 0 && K % 64 == 0; }
+
+// The reference's candidate rule (hopper/step7.cu:358-361): M % 16 too.  candidate.cu keeps it, so the reference's
+// harnesses see the reference's behaviour.
+inline bool reference_shape_ok(int M, int N, int K) { return shape_ok(M, N, K) && M % 16 == 0; }
 
 // The split-K factor for a tail of `tail` tiles on P blocks: minimises the tail's time in tile-times,
 // ceil(tail s / P) / s, plus the reduction of s partials (each about fixup_kb K-blocks of work for the last block).
@@ -405,18 +409,22 @@ inline int make_plan(int M, int N, int K, int sms, int pairs, int variant, bw_pl
 // The plan of a call whose split-tile scratch is a fixed array of `work_cap` bytes of partials and `counter_cap`
 // counters (bw_gemm_f16_noalloc), the first of these that fits: the rule's plan (variant 0); where the rule's partials
 // are twice as large (256-column swap tiles, 512-column pair tiles, swap-AB pairs), the plan on the narrower tiles
-// (kPlanNarrow); that plan with its split-K tail cut to the splits the array holds; whole tiles (kPlanNoSplit), which
-// keep no partials.  BW_ERR_SCRATCH, with *p the last plan tried, if none fits (whole tiles always do).
+// (kPlanNarrow); the plan so far with its split-K tail cut to the splits the array holds; whole tiles (kPlanNoSplit),
+// which keep no partials.  BW_ERR_SCRATCH if none fits (whole tiles always do); *rule, if given, receives the rule's
+// own plan (what the call would have taken with scratch enough, for the error text and for callers comparing them).
 inline int make_plan_capped(int M, int N, int K, int sms, int pairs, bw_plan* p, size_t work_cap,
-                            unsigned counter_cap, const int* held = nullptr)
+                            unsigned counter_cap, const int* held = nullptr, bw_plan* rule = nullptr)
 {
     auto fits = [&] { return p->workspace_bytes <= work_cap && (unsigned)p->counters <= counter_cap; };
     int rc = make_plan(M, N, K, sms, pairs, 0, p, 0u, held);
+    if (rule) *rule = *p;
     if (rc || fits()) return rc;
-    if ((p->wm > 1 || p->bn > 256 || p->kernel == BW_KERNEL_SWAP_PAIR) &&
-        ((rc = make_plan(M, N, K, sms, pairs, 0, p, kPlanNarrow, held)) || fits()))
-        return rc;
-    if ((rc = make_plan(M, N, K, sms, pairs, 0, p, kPlanNarrow, held, work_cap ? work_cap : 1)) || fits()) return rc;
+    unsigned narrow = 0u;  // kPlanNarrow once the rule's double-width tiles have been given up
+    if (p->wm > 1 || p->bn > 256 || p->kernel == BW_KERNEL_SWAP_PAIR) {
+        narrow = kPlanNarrow;
+        if ((rc = make_plan(M, N, K, sms, pairs, 0, p, narrow, held)) || fits()) return rc;
+    }
+    if ((rc = make_plan(M, N, K, sms, pairs, 0, p, narrow, held, work_cap ? work_cap : 1)) || fits()) return rc;
     if ((rc = make_plan(M, N, K, sms, pairs, 0, p, kPlanNoSplit, held))) return rc;
     return fits() ? BW_OK : BW_ERR_SCRATCH;
 }

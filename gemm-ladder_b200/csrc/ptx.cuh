@@ -170,6 +170,11 @@ __device__ __forceinline__ uint64_t policy_evict_last()
     return p;
 }
 
+// Orders this thread's generic-proxy view of global memory before its later async-proxy operations (TMA, bulk copies):
+// after an acquire that made other threads' ordinary stores visible to this thread, a bulk copy it issues next reads
+// those stores, not older data.
+__device__ __forceinline__ void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
+
 // A contiguous copy of `bytes` (a multiple of 16) from global to this block's shared memory by the TMA engine,
 // completing on `bar` (both addresses 16-byte aligned).
 __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar)

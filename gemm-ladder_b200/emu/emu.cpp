@@ -94,6 +94,7 @@ Params make_params(const bw_plan& q, int M, int N, int K, void* C, float* work, 
     p.work = work;
     p.counters = counters;
     p.wait_ns = emu::g_wait_ns;  // long by default (the emulator is slow): a wait that runs out is a protocol fault
+    p.rank_wait_ns = emu::g_wait_ns;
     return p;
 }
 

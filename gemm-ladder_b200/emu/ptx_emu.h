@@ -147,6 +147,8 @@ inline void tma_load_3d_hint(void* dst, const void* tmap, int x, int y, int z, u
 {
     tma_load_3d(dst, tmap, x, y, z, bar);
 }
+// One memory model for every access here: the proxy fence is an ordinary full fence.
+inline void fence_proxy_async_global() { std::atomic_thread_fence(std::memory_order_seq_cst); }
 inline uint64_t policy_evict_first() { return 0; }
 inline uint64_t policy_evict_last() { return 0; }
 inline void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar)

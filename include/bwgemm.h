@@ -18,9 +18,12 @@ extern "C" {
 #endif
 
 /* Status codes.  The reference prints and aborts on an unsupported shape (hopper/step7.cu:358-361); the C ABI returns
- * a code instead and candidate.cu turns a non-zero code into that print-and-abort. */
+ * a code instead and candidate.cu turns a non-zero code into that print-and-abort.  The reference's candidates also
+ * want M % 16 == 0; this library serves any M >= 1 (the tokens of a decode step, M = 1 or 8, included: rows past M
+ * are the TMA engine's zero fill inside the kernel, never padding in the caller's memory), and candidate.cu keeps the
+ * reference's M % 16 rule for the reference's harnesses. */
 #define BW_OK 0
-#define BW_ERR_SHAPE 1     /* M, N, K not positive, or M % 16, N % 64, K % 64 not 0 (the reference's rule) */
+#define BW_ERR_SHAPE 1     /* M, N, K not positive, or N % 64, K % 64 not 0 (any M >= 1 is served) */
 #define BW_ERR_LAUNCH 2    /* a CUDA call failed (the CUDA error string: bw_last_error_string) */
 #define BW_ERR_TIMEOUT 3   /* a kernel's bounded wait on a barrier gave up; see bw_gemm_status */
 #define BW_ERR_ARG 4       /* null or misaligned pointer, unknown variant */
@@ -173,6 +176,14 @@ typedef struct bw_plan {
  * Replaces: step7::choose / step6::choose / rows7c (hopper/step7.cuh:921-949, hopper/step6.cuh:468-488).
  */
 int bw_gemm_plan(int M, int N, int K, int sms, int variant, bw_plan* out);
+
+/*
+ * The plan a call on the current device takes: bw_gemm_f16_variant's with `variant` (noalloc 0), or
+ * bw_gemm_f16_noalloc's (noalloc 1, variant 0) -- the rule on the pairs of SMs the device holds at once (its cluster
+ * occupancy, asked once), and for the no-allocation entry the fallback that fits its fixed array, if the rule's plan
+ * does not.  Host work only (no launch), but it needs the device.  No reference counterpart.
+ */
+int bw_gemm_device_plan(int M, int N, int K, int variant, int noalloc, bw_plan* out);
 
 /*
  * The device status word of the current device, after the caller has synchronised: *code = 0, or BW_ERR_TIMEOUT if

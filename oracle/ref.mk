@@ -12,19 +12,24 @@
 #                      with its inputs: _ref/shapes_b200.txt (the judge's 17 B200 shapes, written from tests/shapes.py
 #                      in the judge's "M N K label" format) and _ref/judge_reference_b200.txt (the card's cached
 #                      cuBLASLt configurations, judge/reference/b200.txt, data read by --reference)
+#   _ref/probe_bw      the reference's probe, probe/probe.cu compiled where it lies (force-including
+#                      oracle/judge_compat.h: it takes the same four CUDA 13 graph calls, probe/probe.cu:162-177) and
+#                      linked with this repository's candidate: interleaved timing of the arms v<i>, twin and x:<hex>
 #
 # Nothing here is built from a copy of the reference's sources, and nothing runs the reference's own build system.
-REF ?= /root/reference
 HERE := $(dir $(abspath $(lastword $(MAKEFILE_LIST))))
 ROOT := $(abspath $(HERE)..)
+# the reference project's tree: REF=<path>, else a checkout named "reference" beside this repository
+REF ?= $(abspath $(ROOT)/../reference)
 OUT := $(HERE)_ref
 CXX ?= g++
 NVCC ?= nvcc
 PKG := $(ROOT)/gemm-ladder_b200
 
-all: $(OUT)/emu_dump $(OUT)/verif_bw judge_bw
+all: $(OUT)/emu_dump $(OUT)/verif_bw judge_bw $(OUT)/probe_bw
 emu_dump: $(OUT)/emu_dump
 verif_bw: $(OUT)/verif_bw
+probe_bw: $(OUT)/probe_bw
 judge_bw: $(OUT)/judge_bw $(OUT)/shapes_b200.txt $(OUT)/judge_reference_b200.txt
 
 $(OUT):
@@ -42,6 +47,10 @@ $(OUT)/judge_bw: $(REF)/judge/judge.cu $(HERE)judge_compat.h $(PKG)/blackwell/ca
 	$(NVCC) -std=c++17 -O3 -gencode arch=compute_100a,code=sm_100a -I$(ROOT)/include -include $(HERE)judge_compat.h \
 	    $(REF)/judge/judge.cu $(PKG)/blackwell/candidate.cu -o $@ -lcublasLt -lcublas
 
+$(OUT)/probe_bw: $(REF)/probe/probe.cu $(HERE)judge_compat.h $(PKG)/blackwell/candidate.cu $(wildcard $(PKG)/csrc/*) | $(OUT)
+	$(NVCC) -std=c++17 -O3 -gencode arch=compute_100a,code=sm_100a -I$(ROOT)/include -include $(HERE)judge_compat.h \
+	    $(REF)/probe/probe.cu $(PKG)/blackwell/candidate.cu -o $@ -lcublasLt -lcublas
+
 $(OUT)/shapes_b200.txt: $(ROOT)/tests/shapes.py | $(OUT)
 	cd $(ROOT)/tests && python3 -c "from shapes import JUDGE_B200; print('# M N K label'); \
 	    [print(m, n, k, name) for name, m, n, k in JUDGE_B200]" > $@
@@ -49,4 +58,4 @@ $(OUT)/shapes_b200.txt: $(ROOT)/tests/shapes.py | $(OUT)
 $(OUT)/judge_reference_b200.txt: $(REF)/judge/reference/b200.txt | $(OUT)
 	cp $< $@
 
-.PHONY: all emu_dump verif_bw judge_bw
+.PHONY: all emu_dump verif_bw judge_bw probe_bw

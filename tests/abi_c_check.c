@@ -26,8 +26,10 @@ int main(void)
     /* M = 16: swap-AB, K halves on clusters of two */
     CHECK(bw_gemm_plan(16, 8192, 8192, 148, 0, &p) == BW_OK);
     CHECK(p.kernel == BW_KERNEL_SWAP && p.bn == 16 && p.ksplit == 2 && p.grid == 128);
-    /* the reference's shape rule and bad arguments, refused before any GPU work */
-    CHECK(bw_gemm_plan(15, 64, 64, 148, 0, &p) == BW_ERR_SHAPE);
+    /* any M >= 1 (M = 1: the tokens rounded up to 16 inside the kernel); N % 64, K % 64 and bad arguments refused
+     * before any GPU work */
+    CHECK(bw_gemm_plan(1, 8192, 8192, 148, 0, &p) == BW_OK && p.kernel == BW_KERNEL_SWAP && p.bn == 16);
+    CHECK(bw_gemm_plan(16, 96, 64, 148, 0, &p) == BW_ERR_SHAPE);
     CHECK(bw_gemm_plan(16, 64, 64, 148, bw_gemm_variant_count(), &p) == BW_ERR_ARG);
     CHECK(bw_gemm_f16((const void*)16, (const void*)16, (void*)16, 16, 32, 64, NULL) == BW_ERR_SHAPE);
     CHECK(bw_gemm_f16(NULL, (const void*)16, (void*)16, 16, 64, 64, NULL) == BW_ERR_ARG);

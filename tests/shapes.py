@@ -12,9 +12,17 @@ JUDGE_B200 = [
 # BASELINE's 17th shape variant and its config 1 (the H100 ladder shape).
 LADDER_4096 = ("ladder_4096", 4096, 6144, 8192)
 CONFIG1 = ("config1", 4608, 5632, 8192)
-# The decode regime: the four weights at M = 1, 8, 16, 32, 64 (M rounded up to the ABI's multiple of 16).
+# The decode regime: the four weights at M = 1, 8, 16, 32, 64 tokens (M = 1 and 8 served as they
+# are: the kernel rounds the tokens up to 16 with the TMA engine's zero fill).
 DECODE_WEIGHTS = [("qkv", 10240, 8192), ("o", 8192, 8192), ("gateup", 57344, 8192), ("down", 8192, 28672)]
-DECODE_M = [16, 32, 64]
+DECODE_M = [1, 8, 16, 32, 64]
+
+# M not a multiple of 16 (the library serves any M >= 1; the reference's candidates refuse these): swap-AB with the
+# tokens' last group part-filled (K halves on clusters of two, stream-K), pair tiles with ragged last rows (whole
+# tiles, a split-K tail, stream-K), M below a pair tile's 256 rows.
+RAGGED_M = [(1, 256, 64), (1, 9600, 576), (8, 1024, 1024), (8, 38080, 128), (3, 64, 4096), (24, 320, 192),
+            (100, 10240, 448), (127, 576, 64), (129, 256, 128), (130, 5376, 128), (200, 512, 1024),
+            (1001, 2304, 320), (2049, 4864, 128), (4599, 5632, 192)]
 
 # hopper/verif.cu:158-163: the reference's 26 edge shapes.
 VERIF = [(16, 256, 64), (144, 256, 64), (128, 512, 128), (208, 512, 192), (272, 5376, 128), (1168, 512, 64),

@@ -36,10 +36,20 @@ def test_status_strings_and_variants():
     assert L.bw_gemm_variant_name(L.bw_gemm_variant_count()) is None
 
 
-@pytest.mark.parametrize("shape", [(0, 64, 64), (15, 64, 64), (16, 32, 64), (16, 64, 32), (16, 64, -64), (-16, 64, 64)])
+@pytest.mark.parametrize("shape", [(0, 64, 64), (16, 32, 64), (16, 64, 32), (16, 64, -64), (-16, 64, 64), (1, 64, 100)])
 def test_bad_shape_is_refused_without_a_gpu(shape):
     M, N, K = shape
     assert bwgemm.gemm_ptr(16, 16, 16, M, N, K) == bwgemm.BW_ERR_SHAPE
+
+
+@pytest.mark.parametrize("M", [1, 8, 15, 100, 130, 1001])
+def test_any_m_is_served(M):
+    """The library serves any M >= 1 (the reference's candidates want M % 16; candidate.cu keeps that rule): the
+    plan of a decode step's tokens (M = 1, 8) is swap-AB with the tokens rounded up to 16 inside the kernel."""
+    p = bwgemm.plan(M, 8192, 8192, sms=148)
+    assert p["bn"] == (-(-M // 16) * 16 if p["kernel"] == bwgemm.BW_KERNEL_SWAP else p["bn"])
+    assert p["kernel"] == (bwgemm.BW_KERNEL_SWAP if M <= 128 else bwgemm.BW_KERNEL_PAIR)
+    assert bwgemm.gemm_ptr(16, 16, 16, M, 8192, 8192) != bwgemm.BW_ERR_SHAPE  # no device here: some other status
 
 
 def test_bad_pointers_and_variant_are_refused_without_a_gpu():

@@ -105,16 +105,19 @@ def emulate(L, A, B, M, N, K, sms, variant=0, epi=0, tn=False):
     """One call on the emulated GPU; A, B fp16 bits (B K x N, or N x K if tn). Returns (rc, C, status, dirty, findings,
     first finding)."""
     Bx = np.ascontiguousarray(np.asarray(B).reshape(K, N).T) if tn else np.ascontiguousarray(B)
+    # C with 16 rows of padding after row M (NaN): the kernel must write every element of C and none past it
     if epi == 1:
-        C = np.full((M, N), np.nan, np.float32)
+        Cp = np.full((M + 16, N), np.nan, np.float32)
     else:
-        C = np.full((M, N // 2 if epi == 2 else N), 0xFFFF, np.uint16)  # fp16 NaN: an unwritten element shows
+        Cp = np.full((M + 16, N // 2 if epi == 2 else N), 0xFFFF, np.uint16)  # fp16 NaN: an unwritten element shows
     st = (ctypes.c_uint * 4)()
     dirty, nf = ctypes.c_int(), ctypes.c_int()
     msg = ctypes.create_string_buffer(512)
-    rc = L.bw_emu_gemm(np.ascontiguousarray(A).ctypes.data, Bx.ctypes.data, C.ctypes.data, M, N, K, sms, variant, epi,
+    rc = L.bw_emu_gemm(np.ascontiguousarray(A).ctypes.data, Bx.ctypes.data, Cp.ctypes.data, M, N, K, sms, variant, epi,
                        int(tn), st, ctypes.byref(dirty), ctypes.byref(nf), msg, 512)
-    return rc, C, list(st), dirty.value, nf.value, msg.value.decode()
+    pad = Cp[M:]
+    assert (np.isnan(pad).all() if epi == 1 else (pad == 0xFFFF).all()), f"{M}x{N}x{K}: rows past M written"
+    return rc, Cp[:M], list(st), dirty.value, nf.value, msg.value.decode()
 
 
 # (M, N, K, emulated SMs, what the rule takes there on that GPU)
@@ -146,9 +149,34 @@ def test_every_plan_form_on_the_emulator(emu, oracle_mod, form, tn):
     assert r["nonfinite"] == 0 and r["violations"] == 0 and r["normwise"] <= 2e-3, r
 
 
+# M not a multiple of 16 (the library serves any M >= 1): decode steps of 1 and 8 tokens, ragged last tiles
+RAGGED = [
+    (1, 256, 128, 8, "swap-AB kpair, one token (15 rows of zero fill)"),
+    (8, 1280, 256, 8, "swap-AB stream-K, 8 tokens"),
+    (24, 1024, 384, 8, "swap-AB kpair with 256-column tiles, 24 tokens in bn 32"),
+    (100, 448, 320, 8, "swap-AB kpair, bn 112, odd K-blocks"),
+    (130, 320, 192, 8, "pair tile, 130 rows"),
+    (200, 1280, 512, 8, "pair tiles, 200 rows, stream-K"),
+    (300, 1280, 4096, 8, "pair tiles with a split-K tail, ragged second row of tiles"),
+]
+
+
+@pytest.mark.parametrize("form", RAGGED, ids=lambda f: f"{f[0]}x{f[1]}x{f[2]}")
+@pytest.mark.parametrize("tn", [False, True], ids=["KxN", "NxK"])
+@pytest.mark.parametrize("build", ["library", "next"])
+def test_ragged_m_on_the_emulator(emu_builds, oracle_mod, form, tn, build):
+    M, N, K, sms, _ = form
+    A, B = oracle_mod.lcg_inputs(M, N, K)
+    rc, C, status, dirty, nf, msg = emulate(emu_builds[build], A, B, M, N, K, sms, tn=tn)
+    assert rc == 0 and nf == 0, f"rc {rc}, {nf} findings, first: {msg}"
+    assert status[0] == 0 and dirty == 0, (status, dirty)
+    r = oracle_mod.check(C, oracle_mod.gemm_f64(A, B), K)
+    assert r["nonfinite"] == 0 and r["violations"] == 0 and r["normwise"] <= 2e-3, r
+
+
 @pytest.mark.parametrize("variant", range(1, 8))
 def test_every_variant_on_the_emulator(emu, oracle_mod, variant):
-    for M, N, K in ((256, 512, 256), (16, 512, 256)):
+    for M, N, K in ((256, 512, 256), (16, 512, 256), (24, 512, 256), (130, 512, 256)):
         A, B = oracle_mod.lcg_inputs(M, N, K)
         rc, C, status, dirty, nf, msg = emulate(emu, A, B, M, N, K, 8, variant=variant)
         assert rc == 0 and nf == 0 and status[0] == 0 and dirty == 0, (rc, nf, msg, status, dirty)

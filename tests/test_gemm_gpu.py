@@ -18,7 +18,7 @@ import pytest
 torch = pytest.importorskip("torch")
 
 import bwgemm  # noqa: E402
-from shapes import B200_EDGES, CONFIG1, DECODE_M, DECODE_WEIGHTS, JUDGE_B200, LADDER_4096, VERIF  # noqa: E402
+from shapes import B200_EDGES, CONFIG1, DECODE_M, DECODE_WEIGHTS, JUDGE_B200, LADDER_4096, RAGGED_M, VERIF  # noqa: E402
 
 pytestmark = pytest.mark.gpu
 
@@ -141,6 +141,23 @@ def test_b200_edges(shape, oracle_mod):
         first = bits(run(dA, dB, variant=v))
         assert_parity(first, ref, K, oracle_mod, f"{shape} v{v}")
         assert np.array_equal(bits(run(dA, dB, variant=v)), first)
+    assert bwgemm.dirty() == 0
+
+
+@pytest.mark.parametrize("shape", RAGGED_M, ids=lambda s: "x".join(map(str, s)))
+def test_ragged_m_every_variant(shape, oracle_mod):
+    """M not a multiple of 16 (decode steps of 1 or 8 tokens, ragged last tiles): every variant against the fp64
+    oracle under both gates, 2 calls bit for bit, nothing written past row M (C's padding rows keep their NaN)."""
+    M, N, K = shape
+    A, B, ref = lcg_case(M, N, K, oracle_mod)
+    dA, dB = to_dev(A), to_dev(B)
+    pad = torch.empty((M + 16, N), dtype=torch.float16, device="cuda")
+    for v in range(bwgemm.lib().bw_gemm_variant_count()):
+        pad.view(torch.int16).fill_(-1)
+        first = bits(run(dA, dB, variant=v, C=pad[:M]))
+        assert_parity(first, ref, K, oracle_mod, f"{shape} v{v}")
+        assert np.all(bits(pad[M:]) == NAN16), f"{shape} v{v}: rows past M written"
+        assert np.array_equal(bits(run(dA, dB, variant=v)), first), f"{shape} v{v}: calls differ"
     assert bwgemm.dirty() == 0
 
 

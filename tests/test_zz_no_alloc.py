@@ -2,14 +2,13 @@
 
 Callers such as a serving process whose device memory is all owned by its own allocator, or a plugin inside someone
 else's process, may not call cudaMalloc; this entry point keeps the scratch of split tiles in a fixed array compiled
-into the library.  Checked here: two calls in a row give the same C as bw_gemm_f16 within the per-element bound the
-other tests use (2 ulp16 of the reference value + 1e-3 sqrt(K)), on shapes whose plan splits tiles (stream-K at
-M <= 128 and on the SM pairs, a split-K tail on the SM pairs) and on one that splits none; and a call whose rule plan
-needs more scratch than the array holds runs on a plan that fits (fewer splits of the tail) instead of being refused.
-This file is collected last, and passes alone in a fresh process too.
+into the library.  Checked here: two calls in a row give the same C as bw_gemm_f16 -- bit for bit where the device
+takes the same plan for both entries (the partials are summed in the same fixed order), and within the per-element
+bound the other tests use (2 ulp16 of the reference value + 1e-3 sqrt(K)) everywhere -- on shapes whose plan splits
+tiles (stream-K at M <= 128 and on the SM pairs, a split-K tail on the SM pairs) and on one that splits none; and a
+call whose rule plan needs more scratch than the array holds runs on a different plan that fits (fewer splits of the
+tail) instead of being refused.  This file is collected last, and passes alone in a fresh process too.
 """
-import ctypes
-import os
 import re
 
 import pytest
@@ -32,10 +31,7 @@ def lib():
     if not torch.cuda.is_available():
         pytest.skip("no CUDA device")
     torch.cuda.set_device(0)
-    L = bwgemm.lib()
-    L.bw_gemm_f16_noalloc.argtypes = [ctypes.c_void_p] * 3 + [ctypes.c_int] * 3 + [ctypes.c_void_p]
-    L.bw_gemm_f16_noalloc.restype = ctypes.c_int
-    return L
+    return bwgemm.lib()
 
 
 def inputs(M, N, K, seed):
@@ -71,6 +67,7 @@ def test_noalloc_agrees_with_the_allocating_entry(lib, shape):
     ref = torch.empty((M, N), dtype=torch.float16, device="cuda")
     assert bwgemm.gemm_ptr(A.data_ptr(), B.data_ptr(), ref.data_ptr(), M, N, K, stream) == 0
     torch.cuda.synchronize()
+    same_plan = bwgemm.device_plan(M, N, K, noalloc=True) == bwgemm.device_plan(M, N, K)
     for call in range(2):  # two calls in a row: the second finds what the first left in the shared array
         C = torch.empty((M, N), dtype=torch.float16, device="cuda")
         C.view(torch.int16).fill_(-1)  # NaN: an element left unwritten shows
@@ -79,6 +76,8 @@ def test_noalloc_agrees_with_the_allocating_entry(lib, shape):
         assert rc == 0, f"call {call}: {lib.bw_status_string(rc).decode()}: {lib.bw_last_error_string().decode()}"
         assert bwgemm.status()[0] == 0
         assert within_bound(C, ref, K), f"call {call}: C differs from bw_gemm_f16's beyond the bound"
+        if same_plan:  # the same plan sums the same partials in the same order
+            assert torch.equal(C, ref), f"call {call}: the same plan as bw_gemm_f16 but not the same bits"
 
 
 def test_noalloc_runs_a_call_beyond_its_array(lib):
@@ -93,6 +92,9 @@ def test_noalloc_runs_a_call_beyond_its_array(lib):
             break
     assert big, "no shape found whose rule plan needs more scratch than the array"
     M, N, K = big
+    rule, capped = bwgemm.device_plan(M, N, K), bwgemm.device_plan(M, N, K, noalloc=True)
+    assert rule["workspace_bytes"] > limit, "the device's own rule plan fits the array: no fallback exercised"
+    assert capped != rule and capped["workspace_bytes"] <= limit, (rule, capped)
     A, B = inputs(M, N, K, seed=1)
     stream = torch.cuda.current_stream().cuda_stream
     ref = torch.empty((M, N), dtype=torch.float16, device="cuda")
