@@ -68,7 +68,13 @@ def parse():
     ap.add_argument("--tp-unfused", action="store_true", help="tp_mlp: the activation as separate torch ops")
     ap.add_argument("--tp-fused-rs", action="store_true",
                     help="tp_mlp: down and the reduce-scatter in one kernel per rank (bw_gemm_f16_rs), no NCCL call")
-    ap.add_argument("--sweep", action="store_true", help="also time the judge's 17 shapes against cuBLAS")
+    ap.add_argument("--sweep", action="store_true",
+                    help="time the judge's 17 shapes against cuBLAS (on by default for the 1-GPU config1 run)")
+    ap.add_argument("--no-sweep", action="store_true", help="leave the 17-shape sweep out of the default run")
+    ap.add_argument("--no-decode", action="store_true", help="leave the decode block (config 3) out")
+    ap.add_argument("--no-sustained", action="store_true", help="leave the sustained config-1 run out")
+    ap.add_argument("--no-tp", action="store_true", help="leave the tensor-parallel MLP sub-record (config 4) out")
+    ap.add_argument("--sustained-seconds", type=float, default=3.0)
     ap.add_argument("--ab-lib", default=None,
                     help="--sweep: also time another build of the library, from gemm-ladder_b200/lib/ (e.g. "
                          "libbwgemm_next.so), interleaved with the two arms in the same process")
@@ -353,17 +359,18 @@ def sweep(args, stream_runs=3):
     return res
 
 
-def run_tp_mlp(args):
-    """BASELINE config 4: the MLP block of a Llama-3-70B layer (hidden 8192, MLP 28672) over the GPUs, Megatron
-    tensor parallelism: gateup column-parallel and down row-parallel through the rung's GEMMs, the fp32 partials of
-    down reduced by an NCCL reduce-scatter (tp_mlp.py).  Total work fixed: strong scaling."""
+def tp_mlp_measure(args, rank, world, local, fused_rs=False, steps=None, warmup=None, e2e=True, tp_m=None):
+    """BASELINE config 4 on the process group's ranks (tp_mlp.py): the block's device time per step (max over ranks),
+    the same block without its collective (gateup + down's fp32 partials only, this rank's compute: max over ranks),
+    and the collective's exposed time, the difference.  Every rank calls it; returns rank 0's record (others: None)."""
     import torch
 
     import bwgemm
     import tp_mlp
 
-    rank, world, local = dist_setup(args)
-    M, hidden, f = args.tp_m, 8192, 28672
+    steps = args.steps if steps is None else steps
+    warmup = max(3, args.warmup if warmup is None else warmup)
+    M, hidden, f = (args.tp_m if tp_m is None else tp_m), 8192, 28672
     gx = torch.Generator(device="cuda")
     gx.manual_seed(7)  # the same tokens on every rank
     X = (torch.rand((M, hidden), generator=gx, device="cuda") * 2 - 1).half()
@@ -372,7 +379,7 @@ def run_tp_mlp(args):
     W1 = ((torch.rand((hidden, 2 * f // world), generator=gw, device="cuda") * 2 - 1) / hidden ** 0.5).half()
     W2 = ((torch.rand((f // world, hidden), generator=gw, device="cuda") * 2 - 1) / f ** 0.5).half()
     # (random shards: the interleaved gate / up layout of the fused activation needs no permutation here)
-    rs = bwgemm.ReduceScatterGemm(M, hidden) if args.tp_fused_rs and world > 1 else None
+    rs = bwgemm.ReduceScatterGemm(M, hidden) if fused_rs and world > 1 else None
     blk = tp_mlp.TPMLP(W1, W2, rank, world, bwgemm.gemm, bwgemm.gemm_f32out,
                        tp_mlp.nccl_reduce_scatter if world > 1 else None,
                        gemm_swiglu=None if args.tp_unfused else bwgemm.gemm_swiglu, gemm_rs=rs)
@@ -385,7 +392,7 @@ def run_tp_mlp(args):
     try:
         if watch:
             watch.gate()
-        for _ in range(max(3, args.warmup)):
+        for _ in range(warmup):
             blk.forward(X)
         if watch:
             watch.gate()
@@ -398,26 +405,46 @@ def run_tp_mlp(args):
     with ClockSampler(local) as clk:
         barrier(world)
         e0.record(stream)
-        for _ in range(args.steps):
+        for _ in range(steps):
             Y = blk.forward(X)
         e1.record(stream)
         barrier(world)
     t = dist_max(e0.elapsed_time(e1) / 1e3, world)
+    del Y
+    # the same block without its collective: this rank's GEMMs alone (the activation fused or not, as above)
+    def local_step():
+        Act = bwgemm.gemm_swiglu(X, blk.W1) if not args.tp_unfused else None
+        if Act is None:
+            H = bwgemm.gemm(X, blk.W1)
+            Act = (torch.nn.functional.silu(H[:, :blk.fs].float()) * H[:, blk.fs:].float()).half()
+        return bwgemm.gemm_f32out(Act, blk.W2)
+
+    for _ in range(2):
+        local_step()
+    barrier(world)
+    g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    g0.record(stream)
+    for _ in range(steps):
+        local_step()
+    g1.record(stream)
+    barrier(world)
+    t_local = dist_max(g0.elapsed_time(g1) / 1e3, world)
     flops = tp_mlp.TPMLP.flops(M, hidden, f)
-    # end to end: the tokens from pinned host memory, this rank's rows of the result back
-    hX = torch.empty((M, hidden), dtype=torch.float16, pin_memory=True)
-    hX.copy_(X)
-    hY = torch.empty((M // world, hidden), dtype=torch.float16, pin_memory=True)
-    steps_e2e = max(3, min(args.steps, 10))
-    barrier(world)
-    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    f0.record(stream)
-    for _ in range(steps_e2e):
-        X.copy_(hX, non_blocking=True)
-        hY.copy_(blk.forward(X), non_blocking=True)
-    f1.record(stream)
-    barrier(world)
-    te = dist_max(f0.elapsed_time(f1) / 1e3, world)
+    te = None
+    if e2e:  # end to end: the tokens from pinned host memory, this rank's rows of the result back
+        hX = torch.empty((M, hidden), dtype=torch.float16, pin_memory=True)
+        hX.copy_(X)
+        hY = torch.empty((M // world, hidden), dtype=torch.float16, pin_memory=True)
+        steps_e2e = max(3, min(steps, 10))
+        barrier(world)
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record(stream)
+        for _ in range(steps_e2e):
+            X.copy_(hX, non_blocking=True)
+            hY.copy_(blk.forward(X), non_blocking=True)
+        f1.record(stream)
+        barrier(world)
+        te = dist_max(f0.elapsed_time(f1) / 1e3, world)
     code = bwgemm.status()[0]
     if world > 1:
         import torch.distributed as dist
@@ -427,23 +454,150 @@ def run_tp_mlp(args):
             torch.cuda.synchronize()
             rs.close()
             dist.barrier()
+    del blk, X, W1, W2
+    torch.cuda.empty_cache()
+    if rank != 0:
+        return None
+    step_ms, local_ms = t / steps * 1e3, t_local / steps * 1e3
+    rec = {"M": M, "hidden": hidden, "mlp": f, "parallelism": f"tp{world}", "tflops": round(flops * steps / t / 1e12, 2),
+           "ms_per_step": round(step_ms, 4), "steps": steps,
+           "local_ms_per_step": round(local_ms, 4),
+           "exposed_collective_ms": round(step_ms - local_ms, 4) if world > 1 else 0.0,
+           "exposed_share": round((step_ms - local_ms) / step_ms, 4) if world > 1 else 0.0,
+           "activation": "separate torch ops" if args.tp_unfused else "fused in the gateup epilogue",
+           "collective": ("fused: partial tiles pushed into the owners' memory in the down GEMM's kernel"
+                          if rs is not None else "NCCL reduce-scatter of fp32 partials") if world > 1 else "none",
+           "clocks": clk.summary(), "device_status": code}
+    if te is not None:
+        rec["e2e"] = {"value": round(flops * steps_e2e / te / 1e12, 2), "unit": "TFLOP/s",
+                      "h2d_bytes_per_step": M * hidden * 2, "d2h_bytes_per_step": M // world * hidden * 2}
+    return rec
+
+
+def graph_time(calls, G, seconds=0.1, rounds=3):
+    """Seconds per call of `calls(i)` (i = 0 .. G-1), captured in a CUDA graph of G calls on a side stream and replayed
+    for about `seconds` per round; the median of `rounds`, on CUDA events."""
+    import torch
+
+    g = torch.cuda.CUDAGraph()
+    st = torch.cuda.Stream()
+    st.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(st):
+        with torch.cuda.graph(g, stream=st):
+            for i in range(G):
+                calls(i)
+    torch.cuda.synchronize()
+    g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    one = max(e0.elapsed_time(e1) / 1e3, 1e-6)
+    reps = max(1, int(seconds / one))
+    times = []
+    for _ in range(rounds):
+        e0.record()
+        for _ in range(reps):
+            g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        times.append(e0.elapsed_time(e1) / 1e3 / (reps * G))
+    del g
+    return statistics.median(times)
+
+
+def decode(args, hbm_gbs):
+    """the four weights of a Llama-3-70B layer at M = 1, 8, 16, 32, 64 tokens, through the rung
+    (bw_gemm_f16 serves any M), against torch.matmul (cuBLAS); CUDA graphs on 3 rotating input sets (every weight's
+    three copies exceed the 126 MB L2).  Bound by HBM: GB/s = 2 (MK + KN + MN) bytes per call over its time, and the
+    fraction of the measured copy bandwidth."""
+    import torch
+
+    import bwgemm
+    from shapes import DECODE_M, DECODE_WEIGHTS
+
+    out = {}
+    for wname, N, K in DECODE_WEIGHTS:
+        Bs = make_sets(1, N, K, seed=N + K)[1]
+        for M in DECODE_M:
+            As = make_sets(M, 1, K, seed=M)[0]
+            C = torch.empty((M, N), dtype=torch.float16, device="cuda")
+            bwgemm.gemm(As[0], Bs[0], C)
+            torch.matmul(As[0], Bs[0], out=C)
+            torch.cuda.synchronize()
+            G = 30
+            t = graph_time(lambda i: bwgemm.gemm(As[i % 3], Bs[i % 3], C), G)
+            tc = graph_time(lambda i: torch.matmul(As[i % 3], Bs[i % 3], out=C), G)
+            gbs = 2.0 * (M * K + K * N + M * N) / t / 1e9
+            out[f"{wname}_m{M}"] = {"M": M, "N": N, "K": K, "us": round(t * 1e6, 2), "gbs": round(gbs, 1),
+                                    "frac_hbm": round(gbs / hbm_gbs, 4), "cublas_us": round(tc * 1e6, 2),
+                                    "ratio_vs_cublas": round(tc / t, 4)}
+            del As, C
+        del Bs
+        torch.cuda.empty_cache()
+    fr = [v["frac_hbm"] for v in out.values()]
+    return {"shapes": out, "hbm_gbs_peak": hbm_gbs, "min_frac_hbm": min(fr),
+            "geomean_frac_hbm": round(math.exp(sum(map(math.log, fr)) / len(fr)), 4),
+            "reference": "torch.matmul fp16 (cuBLAS heuristic); CUDA graphs of 30 calls, 3 rotating input sets"}
+
+
+def sustained(args, A, B, C, local, seconds):
+    """Config 1 back to back for `seconds` (the step of a long run under the 1 kW power cap, not the driver's short
+    burst): TFLOP/s on CUDA events over the whole window, with the SM clock sampled during it."""
+    import torch
+
+    import bwgemm
+
+    M, K = A[0].shape
+    N = B[0].shape[1]
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for i in range(20):
+        bwgemm.gemm(A[i % 3], B[i % 3], C)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    n = max(20, int(seconds / (e0.elapsed_time(e1) / 1e3 / 20)))
+    with ClockSampler(local) as clk:
+        e0.record(stream)
+        for i in range(n):
+            bwgemm.gemm(A[i % 3], B[i % 3], C)
+        e1.record(stream)
+        torch.cuda.synchronize()
+    t = e0.elapsed_time(e1) / 1e3
+    return {"value": round(2.0 * M * N * K * n / t / 1e12, 2), "unit": "TFLOP/s", "calls": n,
+            "seconds": round(t, 3), "ms_per_call": round(t / n * 1e3, 5), "clocks": clk.summary()}
+
+
+def run_tp_mlp(args):
+    """BASELINE config 4: the MLP block of a Llama-3-70B layer (hidden 8192, MLP 28672) over the GPUs, Megatron
+    tensor parallelism: gateup column-parallel and down row-parallel through the rung's GEMMs, the fp32 partials of
+    down reduced by an NCCL reduce-scatter (tp_mlp.py), or down and the reduce-scatter fused (--tp-fused-rs).  Total
+    work fixed: strong scaling."""
+    import bwgemm
+
+    rank, world, local = dist_setup(args)
+    rec = tp_mlp_measure(args, rank, world, local, fused_rs=args.tp_fused_rs)
+    if world > 1:
+        import torch.distributed as dist
+
         dist.destroy_process_group()
     if rank == 0:
         print(json.dumps({
             "metric": "TFLOP/s of the tensor-parallel MLP block (gateup + down + reduce-scatter), BASELINE config 4",
-            "value": round(flops * args.steps / t / 1e12, 2), "unit": "TFLOP/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(t / args.steps * 1e3, 4),
+            "value": rec["tflops"], "unit": "TFLOP/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": rec["ms_per_step"],
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp16 (fp32 accumulate)",
             "data": "synthetic: seeded uniform tokens and weights",
-            "config": {"workload": f"tp_mlp M={M} hidden={hidden} mlp={f}", "M": M, "parallelism": f"tp{world}",
-                       "activation": "separate torch ops" if args.tp_unfused else "fused in the gateup epilogue",
-                       "library": os.path.basename(bwgemm.LIB_PATH),
-                       "collective": ("fused: partial tiles pushed into the owners' memory in the down GEMM's kernel"
-                                      if rs is not None else "NCCL reduce-scatter of fp32 partials")
-                       if world > 1 else "none"},
-            "clocks": clk.summary(), "gpu_launches": 2 * args.steps, "device_status": code,
-            "e2e": {"value": round(flops * steps_e2e / te / 1e12, 2), "unit": "TFLOP/s",
-                    "h2d_bytes_per_step": M * hidden * 2, "d2h_bytes_per_step": M // world * hidden * 2},
+            "config": {"workload": f"tp_mlp M={rec['M']} hidden={rec['hidden']} mlp={rec['mlp']}", "M": rec["M"],
+                       "parallelism": f"tp{world}", "activation": rec["activation"],
+                       "library": os.path.basename(bwgemm.LIB_PATH), "collective": rec["collective"]},
+            "clocks": rec["clocks"], "gpu_launches": 2 * args.steps, "device_status": rec["device_status"],
+            "local_ms_per_step": rec["local_ms_per_step"], "exposed_collective_ms": rec["exposed_collective_ms"],
+            "e2e": rec.get("e2e"),
         }), flush=True)
 
 
@@ -597,10 +751,33 @@ def run_ours(args):
         "clocks": clk.summary(), "gpu_launches": args.steps, "device_status": code,
         "roofline": roofline, "e2e": e2e,
     }
+    default_run = args.workload == "config1" and args.variant == 0
+    if world == 1 and default_run and not args.no_sustained:
+        result["sustained"] = sustained(args, A, B, C, local, args.sustained_seconds)
     if rank == 0 and world == 1 and not args.no_cpu:
         result["cpu_baseline"] = cpu_baseline(M, N, K, args.cpu_seconds)
-    if rank == 0 and args.sweep and world == 1:
+    del A, B
+    torch.cuda.empty_cache()
+    if world == 1 and (args.sweep or (default_run and not args.no_sweep)):
         result["sweep"] = sweep(args)
+    if world == 1 and default_run and not args.no_decode:
+        result["decode"] = decode(args, pk["hbm_gbs"])
+    if default_run and not args.no_tp:
+        # BASELINE config 4 at every N: the row-parallel collective the column shards above never exercise
+        tp = tp_mlp_measure(args, rank, world, local, fused_rs=False, steps=min(args.steps, 20), e2e=False)
+        if rank == 0:
+            result["tp_mlp"] = tp
+    if rank == 0:
+        head = {}
+        if "sweep" in result:
+            head["geomean_ratio_vs_cublas_17"] = result["sweep"]["geomean_ratio_vs_cublas_17"]
+        if "sustained" in result:
+            head["sustained_tflops"] = result["sustained"]["value"]
+        if "decode" in result:
+            head["decode_min_frac_hbm"] = result["decode"]["min_frac_hbm"]
+        if "tp_mlp" in result:
+            head["tp_mlp_tflops"] = result["tp_mlp"]["tflops"]
+        result["headline"] = head
     if world > 1:
         import torch.distributed as dist
 

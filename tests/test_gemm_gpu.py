@@ -286,8 +286,9 @@ def test_graph_survives_a_later_workspace_growth(oracle_mod):
 @pytest.mark.parametrize("shape", [(256, 512, 1024), (2048, 8192, 28672 // 8), (4608, 5632, 8192), (144, 640, 320)],
                          ids=lambda s: "x".join(map(str, s)))
 def test_f32out_partials(shape, oracle_mod):
-    """bw_gemm_f16_f32out: fp32 C within fp32 accumulation error of the fp64 oracle, and (same plan as the fp16 entry
-    above M = 128) rounded to fp16 it is the fp16 entry's result bit for bit."""
+    """bw_gemm_f16_f32out: fp32 C within fp32 accumulation error of the fp64 oracle, and, where the fp16 entry takes the
+    same plan (above M = 128 on 256-column pair tiles: the fp32 entry never takes the 512-column ones), rounded to fp16
+    it is the fp16 entry's result bit for bit."""
     M, N, K = shape
     A, B = oracle_mod.judge_inputs(M, N, K)
     dA, dB = to_dev(A), to_dev(B)
@@ -302,7 +303,7 @@ def test_f32out_partials(shape, oracle_mod):
         ref = oracle_mod.dot_f64(A, B, int(i), int(j))
         assert abs(got[i, j] - ref) <= 1e-4 * K ** 0.5, (i, j, got[i, j], ref)
     C16 = run(dA, dB)
-    if M > 128:
+    if M > 128 and bwgemm.device_plan(M, N, K)["bn"] == 256:
         assert torch.equal(C32.half(), C16), "fp32 partials rounded differ from the fp16 entry's result"
     assert bwgemm.dirty() == 0
 
