@@ -152,6 +152,7 @@ int launch(const bw_plan& q, const CUtensorMap& mx, const CUtensorMap& my, const
                     blockIdx = dim3((unsigned)blk);
                     gridDim = dim3((unsigned)q.grid);
                     blockDim = dim3((unsigned)emu::kCtaThreads);
+                    emu::start_jitter((unsigned)blk);
                     gemm_kernel<BN, SWAP, PAIR, EPI, WM>(mx, my, p);
                 });
         for (auto& th : threads) th.join();
@@ -233,7 +234,10 @@ int dispatch(const bw_plan& q, const CUtensorMap& mx, const CUtensorMap& my, con
 // Sets a knob of the emulator: "wait_ns" (the kernel's limit of one bounded wait), "drop_tma" (the n-th TMA / bulk
 // completion of each launch never arrives, -1 none), "barrier_limit_ms" (a thread barrier never completed: a finding
 // after this long), "cluster_batch" (clusters run at once; 0: as many as the host's cores take), "noalloc_cap"
-// (>= 0: fp16 calls of variant 0 plan as bw_gemm_f16_noalloc does, its array this many bytes; -1: the rule).  Returns 0, or -1 for an unknown name.
+// (>= 0: fp16 calls of variant 0 plan as bw_gemm_f16_noalloc does, its array this many bytes; -1: the rule),
+// "ld_delay_us" (a random pause of up to this long before each tensor-memory load), "start_jitter_us" (each block starts
+// up to this much later), "engine_delay_us" (the asynchronous units' longest delay).  Returns 0, or -1 for an unknown
+// name.
 extern "C" __attribute__((visibility("default"))) int bw_emu_set(const char* name, long long value)
 {
     using namespace bw::emu;
@@ -243,6 +247,9 @@ extern "C" __attribute__((visibility("default"))) int bw_emu_set(const char* nam
     else if (n == "drop_tma") g_drop_tma = value;
     else if (n == "barrier_limit_ms") g_barrier_limit_ms = value;
     else if (n == "noalloc_cap") bw::g_noalloc_cap = value;
+    else if (n == "ld_delay_us") g_ld_delay_us = (int)value;
+    else if (n == "start_jitter_us") g_start_jitter_us = (int)value;
+    else if (n == "engine_delay_us") g_engine_delay_us = (int)value;
     else return -1;
     return 0;
 }
@@ -374,6 +381,7 @@ int launch_rs(const bw_plan& q, int world, std::vector<EmuRank>& ranks, const st
                         blockIdx = dim3((unsigned)(c0 + k));
                         gridDim = dim3((unsigned)q.grid);
                         blockDim = dim3((unsigned)emu::kCtaThreads);
+                        emu::start_jitter((unsigned)(r * q.grid + c0 + k));
                         gemm_kernel<256, false, true, kEpiRS, 1>(mx[r], my[r], p[r]);
                     });
         }

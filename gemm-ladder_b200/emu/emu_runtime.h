@@ -105,6 +105,12 @@ struct Cta;
 
 // The longest delay (microseconds) before an asynchronous unit carries out an item of work.
 inline int g_engine_delay_us = 20;
+// The longest random pause (microseconds) a thread takes before each tensor-memory load (0: none): an epilogue that
+// reads its accumulator slowly, so that an MMA that does not wait for the accumulator to be released overwrites it.
+inline int g_ld_delay_us = 0;
+// The longest random delay (microseconds) before a block's threads start the kernel (0: none; each block its own),
+// so that a block whose cluster peer has not yet set up its barriers or tensor memory meets them unset.
+inline int g_start_jitter_us = 0;
 
 // One of a block's asynchronous units (its TMA engine, or its tensor core): work issued to it runs later, in issue
 // order, on a host thread of its own, each item after a random delay of up to g_engine_delay_us -- so the kernel sees
@@ -117,6 +123,7 @@ struct Engine {
     std::deque<std::function<void()>> q;
     bool stop = false;
     std::thread th;
+    std::atomic<int> mmas{0};  // the tensor core: MMAs issued and not yet carried out
     void start(Cta* c);
     void post(std::function<void()> f)
     {
@@ -199,6 +206,16 @@ inline void Engine::start(Cta* c)
             f();
         }
     });
+}
+
+// A block's start delay under g_start_jitter_us: the same for every thread of the block (from its index), plus a few
+// microseconds per thread.
+inline void start_jitter(unsigned block)
+{
+    if (g_start_jitter_us <= 0) return;
+    std::minstd_rand rng(block * 2654435761u + 1u);
+    const unsigned d = rng() % (unsigned)(g_start_jitter_us + 1) + (unsigned)(t_tid % 8);
+    std::this_thread::sleep_for(std::chrono::microseconds(d));
 }
 
 inline uint64_t now_ns()
@@ -417,15 +434,23 @@ inline void remote_store(uint32_t dst, const uint32_t* v, uint32_t bytes)
 }
 
 // ------------------------------------------------------------------ tensor memory and the MMA
+// A fresh allocation holds what earlier kernels left, not zeros: here a NaN in every column, so that an MMA chain
+// that accumulates onto an accumulator it never cleared (accumulate set on its first MMA) shows in the result.
+constexpr uint32_t kTmemStale = 0x7FC0DEADu;
 inline void tmem_alloc(uint32_t* slot, uint32_t ncols)
 {
     if (ncols < 32 || ncols > (uint32_t)kTmemCols || (ncols & (ncols - 1))) finding("tcgen05.alloc of %u columns", ncols);
     t_cta->tmem_cols = (int)ncols;
+    std::fill(t_cta->tmem.begin(), t_cta->tmem.end(), kTmemStale);
     *slot = 0u;  // lane 0, column 0
 }
 inline void tmem_dealloc(uint32_t taddr, uint32_t ncols)
 {
     if (taddr != 0u || (int)ncols != t_cta->tmem_cols) finding("tcgen05.dealloc of %u columns at %#x", ncols, taddr);
+    // the MMAs that write this block's tensor memory: its own, and its pair leader's (cta_group::2)
+    const Cta* writers[2] = {t_cta, t_cta->cluster && t_cta->rank ? t_cta->cluster->cta[0] : t_cta};
+    for (const Cta* w : writers)
+        if (w->tc.mmas.load() > 0) finding("tensor memory freed while %d MMAs are still in flight", w->tc.mmas.load());
 }
 
 // operand element (row, k) of a K16 slice through a 128-byte-swizzled shared-memory descriptor
@@ -504,6 +529,10 @@ inline void mma(uint32_t d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, bool
 // tcgen05.ld 32x32b.x16: lane = the address's lane + the thread's lane in its warp, 16 columns
 inline void tmem_ld(uint32_t taddr, uint32_t (&r)[16])
 {
+    if (g_ld_delay_us > 0) {
+        thread_local std::minstd_rand rng((unsigned)(t_tid * 7919 + 17));
+        std::this_thread::sleep_for(std::chrono::microseconds(rng() % (unsigned)(g_ld_delay_us + 1)));
+    }
     const uint32_t lane = (taddr >> 16) + (uint32_t)(t_tid & 31), col = taddr & 0xFFFFu;
     if (lane >= (uint32_t)kTmemLanes || col + 16 > (uint32_t)t_cta->tmem_cols) {
         finding("tcgen05.ld of lane %u column %u outside the allocation", lane, col);

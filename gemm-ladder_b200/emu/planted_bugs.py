@@ -120,8 +120,9 @@ MUTATIONS = [
     ("mma_stage_phase_never_flips", GK, "ph ^= 1u;", "(void)0;", 1, "library"),
     ("mma_one_accumulator", GK, "const uint32_t d = tmem_base + (uint32_t)(acc * AN);", "const uint32_t d = tmem_base;", 0,
      "library"),
-    ("mma_no_drain_wait", GK, "mma_commit(drain);\n                wait_drain(drain, 0, p.wait_ns);",
-     "mma_commit(drain);", 0, "library"),
+    ("sched_block_index", GK, "const int P = gridDim.x / R, c = blockIdx.x / R;",
+     "const int P = gridDim.x / R, c = blockIdx.x / R + (blockIdx.x >= (unsigned)R && blockIdx.x + R < gridDim.x);", 0,
+     "library"),
     # ---------------------------------------------------------------- barrier set-up
     ("init_acc_free_count", GK, "mbar_init(&tempty[i], 4 * R);", "mbar_init(&tempty[i], 4 * R + 1);", 0, "library"),
     ("init_acc_free_count_low", GK, "mbar_init(&tempty[i], 4 * R);", "mbar_init(&tempty[i], 4 * R - 1);", 0, "library"),
@@ -139,7 +140,7 @@ MUTATIONS = [
     ("epi_release_other_acc", GK, "mbar_arrive(&tempty[a]);", "mbar_arrive(&tempty[a ^ 1]);", 0, "library"),
     ("epi_release_other_acc_pair", GK, "mbar_arrive_cluster(tempty_leader0 + 8u * (uint32_t)a);",
      "mbar_arrive_cluster(tempty_leader0 + 8u * (uint32_t)(a ^ 1));", 0, "library"),
-    ("epi_release_twice", GK, "if (!last_seg) release_all(acc);", "release_all(acc);", 0, "library"),
+    ("epi_split_acc_kept", GK, "if (!last_seg) release_all(acc);", "if (false) release_all(acc);", 0, "library"),
     ("epi_lane_quarter", GK, "const int q = warp & 3;         // the TMEM lane quarter this warp may access",
      "const int q = (warp + 1) & 3;", 0, "library"),
     ("epi_tmem_acc_column", GK, "((uint32_t)(q * 32) << 16) + (uint32_t)(acc * AN)",
@@ -316,6 +317,7 @@ MUTATIONS = [
 CASES = {
     "library": [
         (256, 256, 128, 8, 0, 0, False),    # one pair tile
+        (512, 2048, 128, 8, 0, 0, False),   # four pair tiles per pair: both accumulators reused twice
         (512, 1280, 4096, 8, 0, 0, False),  # pair tiles, a split-K tail (bulk and plain reductions)
         (256, 1280, 256, 8, 0, 0, False),   # pair tiles, stream-K over one wave and a part
         (16, 256, 128, 8, 0, 0, False),     # swap-AB, K halves on a cluster of two
@@ -335,6 +337,14 @@ CASES = {
         (256, 512, 256, 8, 5, 0, False),    # 128 x 256 single-SM tiles
         (256, 512, 256, 8, 6, 0, False),    # 128 x 64 tiles
         (256, 512, 256, 8, 1, 0, False),    # whole pair tiles only
+        (2304, 512, 128, 8, 0, 0, False),   # nine rows of pair tiles: a second, reversed serpentine group
+        (768, 1280, 4096, 8, 0, 0, False),  # more split-K units than pairs
+        (16, 256, 2048, 8, 0, 0, False),    # K halves deeper than the stage ring
+        (256, 512, 1024, 8, 5, 0, False),   # single-SM tiles deeper than the stage ring
+        (64, 2304, 1024, 8, 0, 0, False),   # swap-AB stream-K, 256-column tiles, several tiles per block
+        (128, 2112, 128, 16, 0, 0, False),  # swap-AB stream-K, N not a multiple of 128
+        (300, 1024, 256, 8, 0, 2, False),   # SwiGLU output, ragged rows
+        (300, 1280, 4096, 8, 0, 1, False),  # fp32 output, ragged rows, a split-K tail
     ],
     "next": [
         (16, 1280, 256, 8, 0, 0, False),    # the K split over clusters of 2 to 8
@@ -432,6 +442,8 @@ def check(lib_path, build_name, cluster_batch):
     L.bw_emu_set(b"wait_ns", 4_000_000_000)        # a wait that gives up is a report, so no need to wait long
     L.bw_emu_set(b"barrier_limit_ms", 8000)
     L.bw_emu_set(b"cluster_batch", cluster_batch)
+    L.bw_emu_set(b"ld_delay_us", 30)               # a slow epilogue: an MMA that does not wait for it overwrites
+    L.bw_emu_set(b"start_jitter_us", 2000)         # blocks start apart: a peer's barriers unset show
 
     def call(A, B, M, N, K, sms, variant, epi, tn):
         Bx = np.ascontiguousarray(np.asarray(B).reshape(K, N).T) if tn else np.ascontiguousarray(B)

@@ -204,11 +204,21 @@ inline void tc_fence_after() {}
 // once the MMAs issued before it have run.
 inline void mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate)
 {
-    emu::t_cta->tc.post([=] { emu::mma(d_tmem, adesc, bdesc, idesc, accumulate != 0, false); });
+    emu::Engine& tc = emu::t_cta->tc;
+    ++tc.mmas;
+    tc.post([=, &tc] {
+        emu::mma(d_tmem, adesc, bdesc, idesc, accumulate != 0, false);
+        --tc.mmas;
+    });
 }
 inline void mma_f16_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate)
 {
-    emu::t_cta->tc.post([=] { emu::mma(d_tmem, adesc, bdesc, idesc, accumulate != 0, true); });
+    emu::Engine& tc = emu::t_cta->tc;
+    ++tc.mmas;
+    tc.post([=, &tc] {
+        emu::mma(d_tmem, adesc, bdesc, idesc, accumulate != 0, true);
+        --tc.mmas;
+    });
 }
 inline void mma_commit_pair(uint32_t bar)
 {
