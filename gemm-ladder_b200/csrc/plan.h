@@ -64,16 +64,20 @@
                                // load per box; measured: the swap-AB shapes 0.5-3 % faster, the pair shapes even)
 #endif
 #ifndef BW_PAIR_WIDE
-#define BW_PAIR_WIDE 0         // pair tiles of 256 x 512 (two MMAs of N = 256 per K step into one 512-column accumulator)
-                               // where their estimated time beats the 256 x 256 tiles' (pair_time): a block takes in
-                               // 48 KB per K-block for twice the math of the 32 KB of a 256 x 256 tile; its epilogue is
-                               // no longer hidden (run on the host emulator; not yet measured)
+#define BW_PAIR_WIDE 1         // pair tiles of 256 x 512 (two MMAs of N = 256 per K step into one 512-column accumulator)
+                               // where their estimated time beats the 256 x 256 tiles' (pair_time) and their schedule
+                               // needs no stream-K: a block takes in 48 KB per K-block for twice the math of the 32 KB of
+                               // a 256 x 256 tile (measured in back-to-back CUDA graphs under the power cap: config 1
+                               // -7 %, 8192^3 -5 %, gateup_m2048 -5 %; stream-K over 512-column tiles, whose partials
+                               // are 256 KB per block, +37 % at o_m2048)
 #endif
 #ifndef BW_PAIR_KB_NS
 #define BW_PAIR_KB_NS 409.0        // a 256 x 256 pair tile's K-block (measured: its intake-bound mainloop at 1965 MHz)
 #endif
 #ifndef BW_PAIR_WIDE_KB_NS
-#define BW_PAIR_WIDE_KB_NS 748.0   // a 256 x 512 one's: twice the MMA time of the measured cuBLAS peak (an estimate)
+#define BW_PAIR_WIDE_KB_NS 748.0   // a 256 x 512 one's: twice the MMA time of the measured cuBLAS peak (an estimate; with
+                                   // it the rule takes the wide tile where it measured faster -- config 1, 8192^3,
+                                   // gateup_m2048 -- and not at qkv_m2048 (1 % slower wide) or 4096 x 6144 (even))
 #endif
 #ifndef BW_PAIR_WIDE_EPI_NS
 #define BW_PAIR_WIDE_EPI_NS 1200.0 // the 256 x 512 tile's exposed epilogue, once per wave: the first half's drain (the
@@ -276,10 +280,13 @@ inline int make_plan(int M, int N, int K, int sms, int pairs, int variant, bw_pl
         units = pair ? pairs : sms;
         q.tiles_m = (M + 128 * ranks - 1) / (128 * ranks);
         // pair tiles of 512 columns for the fp16 entries, where their estimated time is 2 % below the 256-column ones'
+        // and they make no stream-K schedule (whose partials would be 256 KB per block)
+        const int tw = q.tiles_m * ((N + 511) / 512);
+        const bool wide_sk = (BW_SK_ONE_WAVE && tw > units && tw < 2 * units) ||
+                             (BW_SK_PART_WAVE && 2 * tw > units && tw < units);
         if (BW_PAIR_WIDE && pair && (variant == 0 || variant == 3) && !(flags & (kPlanNoSwap | kPlanNarrow)) &&
-            N > 256 && units > 0 &&
-            pair_time(q.tiles_m * ((N + 511) / 512), units, q.kblocks, 512) <
-                0.98 * pair_time(q.tiles_m * ((N + 255) / 256), units, q.kblocks, 256))
+            N > 256 && units > 0 && !wide_sk &&
+            pair_time(tw, units, q.kblocks, 512) < 0.98 * pair_time(q.tiles_m * ((N + 255) / 256), units, q.kblocks, 256))
             q.bn = 512;
         q.tiles_n = (N + q.bn - 1) / q.bn;
         q.group_rows = variant == 3 ? 0 : BW_GROUP_ROWS;

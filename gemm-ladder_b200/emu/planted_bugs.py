@@ -391,16 +391,22 @@ def build(tree, build_name, out):
     return r.returncode == 0, r.stderr[-2000:]
 
 
-def run_one(mutation, build_name, timeout_s, cluster_batch):
-    """Compile the sources with `mutation` (None: unmodified) and run the build's calls in a child process.  Returns a
-    dict: name, build, reported (bool), why."""
+def snapshot(dst):
+    """The sources every mutant starts from, copied once when a run starts (later edits of the tree do not reach it)."""
+    os.makedirs(os.path.join(dst, "gemm-ladder_b200"))
+    shutil.copytree(os.path.join(PKG, "csrc"), os.path.join(dst, "gemm-ladder_b200", "csrc"))
+    shutil.copytree(os.path.join(PKG, "emu"), os.path.join(dst, "gemm-ladder_b200", "emu"),
+                    ignore=shutil.ignore_patterns("*.py", "__pycache__"))
+    shutil.copytree(os.path.join(ROOT, "include"), os.path.join(dst, "include"))
+
+
+def run_one(mutation, build_name, timeout_s, cluster_batch, base):
+    """Compile the sources of `base` (a snapshot) with `mutation` (None: unmodified) and run the build's calls in a
+    child process.  Returns a dict: name, build, reported (bool), why."""
     name = mutation[0] if mutation else "unmodified"
     with tempfile.TemporaryDirectory(prefix="bwpb_") as tmp:
-        os.makedirs(os.path.join(tmp, "gemm-ladder_b200"))
-        shutil.copytree(os.path.join(PKG, "csrc"), os.path.join(tmp, "gemm-ladder_b200", "csrc"))
-        shutil.copytree(os.path.join(PKG, "emu"), os.path.join(tmp, "gemm-ladder_b200", "emu"),
-                        ignore=shutil.ignore_patterns("*.py", "__pycache__"))
-        shutil.copytree(os.path.join(ROOT, "include"), os.path.join(tmp, "include"))
+        os.rmdir(tmp)
+        shutil.copytree(base, tmp)
         if mutation:
             apply(tmp, mutation)
         lib = os.path.join(tmp, "libbwemu.so")
@@ -534,9 +540,12 @@ def main():
     t0 = time.time()
     results = []
     builds = sorted({m[5] for m in todo})
+    base_dir = tempfile.mkdtemp(prefix="bwpb_base_")
+    base = os.path.join(base_dir, "src")
+    snapshot(base)
     with concurrent.futures.ThreadPoolExecutor(max_workers=a.jobs) as ex:
-        futs = [ex.submit(run_one, None, b, a.timeout, a.cluster_batch) for b in builds]
-        futs += [ex.submit(run_one, m, m[5], a.timeout, a.cluster_batch) for m in todo]
+        futs = [ex.submit(run_one, None, b, a.timeout, a.cluster_batch, base) for b in builds]
+        futs += [ex.submit(run_one, m, m[5], a.timeout, a.cluster_batch, base) for m in todo]
         for f in concurrent.futures.as_completed(futs):
             r = f.result()
             results.append(r)
@@ -544,6 +553,7 @@ def main():
             if r["name"] == "unmodified":
                 mark = "CLEAN   " if not r["reported"] else "BROKEN  "
             print(f"{mark} {r['name']:34s} [{r['build']}] {r['why']}", flush=True)
+    shutil.rmtree(base_dir, ignore_errors=True)
     clean = [r for r in results if r["name"] == "unmodified"]
     muts = [r for r in results if r["name"] != "unmodified"]
     caught = sum(r["reported"] for r in muts)

@@ -20,9 +20,9 @@ int main(void)
 {
     bw_plan p;
     memset(&p, 0, sizeof p);
-    /* the rule, host only: BASELINE config 1 on 148 SMs takes SM-pair tiles of 256 x 256 */
+    /* the rule, host only: BASELINE config 1 on 148 SMs takes SM-pair tiles of 256 x 512 (198 tiles, 2.7 waves) */
     CHECK(bw_gemm_plan(4608, 5632, 8192, 148, 0, &p) == BW_OK);
-    CHECK(p.kernel == BW_KERNEL_PAIR && p.bn == 256 && p.tiles == 18 * 22 && p.kblocks == 128);
+    CHECK(p.kernel == BW_KERNEL_PAIR && p.bn == 512 && p.tiles == 18 * 11 && p.kblocks == 128);
     /* M = 16: swap-AB, K halves on clusters of two */
     CHECK(bw_gemm_plan(16, 8192, 8192, 148, 0, &p) == BW_OK);
     CHECK(p.kernel == BW_KERNEL_SWAP && p.bn == 16 && p.ksplit == 2 && p.grid == 128);
