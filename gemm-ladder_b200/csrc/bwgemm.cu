@@ -239,7 +239,7 @@ const int* held_of(const DeviceState& d) { return BW_KSPLIT ? d.held : nullptr; 
 
 template <int BN, bool SWAP, bool PAIR, int EPI = kEpiF16, int WM = 1>
 int launch_kernel(DeviceState& d, unsigned long long bit, const bw_plan& q, const CUtensorMap& mx, const CUtensorMap& my,
-                  const Params& p, cudaStream_t st)
+                  const CUtensorMap& mc, const Params& p, cudaStream_t st)
 {
     using G = KGeom<BN, SWAP, PAIR, EPI, WM>;
     // K split: what a block receives from the others of its cluster lands in its idle stage ring
@@ -253,74 +253,74 @@ int launch_kernel(DeviceState& d, unsigned long long bit, const bw_plan& q, cons
     if (rc) return rc;
     cudaLaunchAttribute attr[1];
     const cudaLaunchConfig_t cfg = launch_config<BN, SWAP, PAIR, WM, EPI>(q.grid, st, attr, q.ksplit);
-    cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_kernel<BN, SWAP, PAIR, EPI, WM>, mx, my, p);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_kernel<BN, SWAP, PAIR, EPI, WM>, mx, my, mc, p);
     if (e != cudaSuccess) return cuda_fail(e, "kernel launch");
     return BW_OK;
 }
 
 // The plan's kernel instance, launched.
-int dispatch(DeviceState& d, const bw_plan& q, const CUtensorMap& mx, const CUtensorMap& my, const Params& p,
-             cudaStream_t st, int epi = kEpiF16)
+int dispatch(DeviceState& d, const bw_plan& q, const CUtensorMap& mx, const CUtensorMap& my, const CUtensorMap& mc,
+             const Params& p, cudaStream_t st, int epi = kEpiF16)
 {
     if (epi == kEpiF32) {  // fp32 C: the plan is a TILE or PAIR one (no swap-AB)
-        if (q.kernel == BW_KERNEL_PAIR) return launch_kernel<256, false, true, kEpiF32>(d, 1u << 12, q, mx, my, p, st);
+        if (q.kernel == BW_KERNEL_PAIR) return launch_kernel<256, false, true, kEpiF32>(d, 1u << 12, q, mx, my, mc, p, st);
         if (q.kernel == BW_KERNEL_TILE && q.bn == 256)
-            return launch_kernel<256, false, false, kEpiF32>(d, 1u << 13, q, mx, my, p, st);
+            return launch_kernel<256, false, false, kEpiF32>(d, 1u << 13, q, mx, my, mc, p, st);
         return BW_ERR_ARG;
     }
     if (epi == kEpiSwiGLU) {  // fused activation: TILE or PAIR, whole tiles only
         if (q.sk_tiles != 0) return BW_ERR_ARG;
         if (q.kernel == BW_KERNEL_PAIR)
-            return launch_kernel<256, false, true, kEpiSwiGLU>(d, 1u << 14, q, mx, my, p, st);
+            return launch_kernel<256, false, true, kEpiSwiGLU>(d, 1u << 14, q, mx, my, mc, p, st);
         if (q.kernel == BW_KERNEL_TILE && q.bn == 256)
-            return launch_kernel<256, false, false, kEpiSwiGLU>(d, 1u << 15, q, mx, my, p, st);
+            return launch_kernel<256, false, false, kEpiSwiGLU>(d, 1u << 15, q, mx, my, mc, p, st);
         return BW_ERR_ARG;
     }
 #if BW_PAIR_WIDE
-    if (q.kernel == BW_KERNEL_PAIR && q.bn == 512) return launch_kernel<512, false, true>(d, 1u << 25, q, mx, my, p, st);
+    if (q.kernel == BW_KERNEL_PAIR && q.bn == 512) return launch_kernel<512, false, true>(d, 1u << 25, q, mx, my, mc, p, st);
 #endif
-    if (q.kernel == BW_KERNEL_PAIR) return launch_kernel<256, false, true>(d, kBitPair, q, mx, my, p, st);
+    if (q.kernel == BW_KERNEL_PAIR) return launch_kernel<256, false, true>(d, kBitPair, q, mx, my, mc, p, st);
     if (q.kernel == BW_KERNEL_TILE) {
         switch (q.bn) {
-        case 64: return launch_kernel<64, false, false>(d, 1u << 10, q, mx, my, p, st);
-        case 128: return launch_kernel<128, false, false>(d, 1u << 11, q, mx, my, p, st);
-        case 256: return launch_kernel<256, false, false>(d, 1u << 0, q, mx, my, p, st);
+        case 64: return launch_kernel<64, false, false>(d, 1u << 10, q, mx, my, mc, p, st);
+        case 128: return launch_kernel<128, false, false>(d, 1u << 11, q, mx, my, mc, p, st);
+        case 256: return launch_kernel<256, false, false>(d, 1u << 0, q, mx, my, mc, p, st);
         default: return BW_ERR_ARG;
         }
     }
 #if BW_SWAP_PAIR
     if (q.kernel == BW_KERNEL_SWAP_PAIR) {  // swap-AB on SM pairs
         switch (q.bn * 4 + q.wm) {
-        case 64 * 4 + 1: return launch_kernel<64, true, true, kEpiF16, 1>(d, 1ull << 27, q, mx, my, p, st);
-        case 128 * 4 + 1: return launch_kernel<128, true, true, kEpiF16, 1>(d, 1ull << 29, q, mx, my, p, st);
-        case 64 * 4 + 2: return launch_kernel<64, true, true, kEpiF16, 2>(d, 1ull << 30, q, mx, my, p, st);
-        case 128 * 4 + 2: return launch_kernel<128, true, true, kEpiF16, 2>(d, 1ull << 32, q, mx, my, p, st);
+        case 64 * 4 + 1: return launch_kernel<64, true, true, kEpiF16, 1>(d, 1ull << 27, q, mx, my, mc, p, st);
+        case 128 * 4 + 1: return launch_kernel<128, true, true, kEpiF16, 1>(d, 1ull << 29, q, mx, my, mc, p, st);
+        case 64 * 4 + 2: return launch_kernel<64, true, true, kEpiF16, 2>(d, 1ull << 30, q, mx, my, mc, p, st);
+        case 128 * 4 + 2: return launch_kernel<128, true, true, kEpiF16, 2>(d, 1ull << 32, q, mx, my, mc, p, st);
         default: return BW_ERR_ARG;
         }
     }
 #endif
     if (q.wm == 2) {  // swap-AB tiles of 256 weight columns
         switch (q.bn) {
-        case 16: return launch_kernel<16, true, false, kEpiF16, 2>(d, 1u << 21, q, mx, my, p, st);
-        case 32: return launch_kernel<32, true, false, kEpiF16, 2>(d, 1u << 22, q, mx, my, p, st);
-        case 48: return launch_kernel<48, true, false, kEpiF16, 2>(d, 1u << 23, q, mx, my, p, st);
-        case 64: return launch_kernel<64, true, false, kEpiF16, 2>(d, 1u << 16, q, mx, my, p, st);
-        case 80: return launch_kernel<80, true, false, kEpiF16, 2>(d, 1u << 17, q, mx, my, p, st);
-        case 96: return launch_kernel<96, true, false, kEpiF16, 2>(d, 1u << 18, q, mx, my, p, st);
-        case 112: return launch_kernel<112, true, false, kEpiF16, 2>(d, 1u << 19, q, mx, my, p, st);
-        case 128: return launch_kernel<128, true, false, kEpiF16, 2>(d, 1u << 20, q, mx, my, p, st);
+        case 16: return launch_kernel<16, true, false, kEpiF16, 2>(d, 1u << 21, q, mx, my, mc, p, st);
+        case 32: return launch_kernel<32, true, false, kEpiF16, 2>(d, 1u << 22, q, mx, my, mc, p, st);
+        case 48: return launch_kernel<48, true, false, kEpiF16, 2>(d, 1u << 23, q, mx, my, mc, p, st);
+        case 64: return launch_kernel<64, true, false, kEpiF16, 2>(d, 1u << 16, q, mx, my, mc, p, st);
+        case 80: return launch_kernel<80, true, false, kEpiF16, 2>(d, 1u << 17, q, mx, my, mc, p, st);
+        case 96: return launch_kernel<96, true, false, kEpiF16, 2>(d, 1u << 18, q, mx, my, mc, p, st);
+        case 112: return launch_kernel<112, true, false, kEpiF16, 2>(d, 1u << 19, q, mx, my, mc, p, st);
+        case 128: return launch_kernel<128, true, false, kEpiF16, 2>(d, 1u << 20, q, mx, my, mc, p, st);
         default: return BW_ERR_ARG;
         }
     }
     switch (q.bn) {
-    case 16: return launch_kernel<16, true, false>(d, 1u << 1, q, mx, my, p, st);
-    case 32: return launch_kernel<32, true, false>(d, 1u << 2, q, mx, my, p, st);
-    case 48: return launch_kernel<48, true, false>(d, 1u << 3, q, mx, my, p, st);
-    case 64: return launch_kernel<64, true, false>(d, 1u << 4, q, mx, my, p, st);
-    case 80: return launch_kernel<80, true, false>(d, 1u << 5, q, mx, my, p, st);
-    case 96: return launch_kernel<96, true, false>(d, 1u << 6, q, mx, my, p, st);
-    case 112: return launch_kernel<112, true, false>(d, 1u << 7, q, mx, my, p, st);
-    case 128: return launch_kernel<128, true, false>(d, 1u << 8, q, mx, my, p, st);
+    case 16: return launch_kernel<16, true, false>(d, 1u << 1, q, mx, my, mc, p, st);
+    case 32: return launch_kernel<32, true, false>(d, 1u << 2, q, mx, my, mc, p, st);
+    case 48: return launch_kernel<48, true, false>(d, 1u << 3, q, mx, my, mc, p, st);
+    case 64: return launch_kernel<64, true, false>(d, 1u << 4, q, mx, my, mc, p, st);
+    case 80: return launch_kernel<80, true, false>(d, 1u << 5, q, mx, my, mc, p, st);
+    case 96: return launch_kernel<96, true, false>(d, 1u << 6, q, mx, my, mc, p, st);
+    case 112: return launch_kernel<112, true, false>(d, 1u << 7, q, mx, my, mc, p, st);
+    case 128: return launch_kernel<128, true, false>(d, 1u << 8, q, mx, my, mc, p, st);
     default: return BW_ERR_ARG;
     }
 }
@@ -376,6 +376,16 @@ bool make_maps(const bw_plan& q, const void* A, const void* B, int M, int N, int
     return make_map(mx, B, N, K, 64, 64) && make_map(my, A, K, M, 64, swap_rows(q));
 }
 
+// The map of C for the TMA-store epilogue (BW_EPI_TMA: fp16 C of a TILE or PAIR plan): boxes of 64 columns x 32 rows
+// (one epilogue warp's rows), 128-byte swizzle.  Other plans store C from registers; they get a copy of `mx`.
+bool make_c_map(const bw_plan& q, void* C, int M, int N, int epi, const CUtensorMap& mx, CUtensorMap* mc)
+{
+    if (BW_EPI_TMA && epi == kEpiF16 && (q.kernel == BW_KERNEL_TILE || q.kernel == BW_KERNEL_PAIR))
+        return make_map(mc, C, N, M, 64, 32);
+    *mc = mx;
+    return true;
+}
+
 int gemm(const void* A, const void* B, void* C, int M, int N, int K, cudaStream_t st, int variant, int epi = kEpiF16,
          bool tn = false)
 {
@@ -395,12 +405,12 @@ int gemm(const void* A, const void* B, void* C, int M, int N, int K, cudaStream_
         if ((rc = make_plan(M, N, K, d->sms, d->pairs, variant, &q, flags, held_of(*d)))) return rc;
         if ((rc = ensure_workspace(*d, q, st))) return rc;
     }
-    CUtensorMap mx, my;
-    if (!make_maps(q, A, B, M, N, K, &mx, &my, tn)) {
+    CUtensorMap mx, my, mc;
+    if (!make_maps(q, A, B, M, N, K, &mx, &my, tn) || !make_c_map(q, C, M, N, epi, mx, &mc)) {
         snprintf(g_errbuf, sizeof g_errbuf, "cuTensorMapEncodeTiled failed");
         return BW_ERR_LAUNCH;
     }
-    return dispatch(*d, q, mx, my, make_params(q, M, N, K, C, d->work, d->counters, tn), st, epi);
+    return dispatch(*d, q, mx, my, mc, make_params(q, M, N, K, C, d->work, d->counters, tn), st, epi);
 }
 
 }  // namespace
@@ -609,12 +619,12 @@ int noalloc_gemm(const void* A, const void* B, void* C, int M, int N, int K, cud
     // may leave some set)
     if (q.counters > 0 && (e = cudaMemsetAsync(counters, 0, (size_t)q.counters * sizeof(int), st)) != cudaSuccess)
         return cuda_fail(e, "cudaMemsetAsync (no-allocation counters)");
-    CUtensorMap mx, my;
-    if (!make_maps(q, A, B, M, N, K, &mx, &my)) {
+    CUtensorMap mx, my, mc;
+    if (!make_maps(q, A, B, M, N, K, &mx, &my) || !make_c_map(q, C, M, N, kEpiF16, mx, &mc)) {
         snprintf(g_errbuf, sizeof g_errbuf, "cuTensorMapEncodeTiled failed");
         return BW_ERR_LAUNCH;
     }
-    return dispatch(*d, q, mx, my, make_params(q, M, N, K, C, work, counters), st);
+    return dispatch(*d, q, mx, my, mc, make_params(q, M, N, K, C, work, counters), st);
 }
 
 }  // namespace
@@ -710,7 +720,7 @@ int rs_gemm(bw_rs* rs, const void* A, const void* B, void* C, int K, cudaStream_
     Params p = make_params(q, M, N, K, C, nullptr, nullptr);
     p.s.row_shift = ((rs->rank + 1) * (rs->M / rs->world / 256)) % q.tiles_m;  // this rank's own rows last
     p.rs = reinterpret_cast<const RsTable*>(rs->region + rs->table_off);
-    return launch_kernel<256, false, true, kEpiRS>(*d, 1u << 24, q, mx, my, p, st);
+    return launch_kernel<256, false, true, kEpiRS>(*d, 1u << 24, q, mx, my, mx, p, st);
 }
 
 }  // namespace

@@ -120,6 +120,37 @@ __device__ __forceinline__ void store_rows64(const Params& p, int r0, int n, int
     }
 }
 
+// The same 64 columns of C from one warp's 32 rows by a TMA store (TILE and PAIR, fp16, BW_EPI_TMA): the warp writes
+// its rows into `quarter`, its 4 KB of a staging buffer (128-byte rows; the 16-byte pieces of row l at piece
+// j ^ (l % 8), the map's 128-byte swizzle, so that the 8 rows a quarter-warp writes at once fall in distinct banks),
+// makes them visible to the async proxy, and lane 0 stores the box of 64 columns x 32 rows at (n, r0) -- the map
+// clips the rows past M.  The buffer was last read by this warp's store of two chunks before: lane 0 first waits until
+// at most one of its stores (the previous chunk's, from the other buffer) is still reading shared memory.
+__device__ __forceinline__ void store_rows64_tma(const CUtensorMap* tmc, uint8_t* quarter, int r0, int n, int M,
+                                                 int N, int lane, const float (&v)[64])
+{
+    if (n >= N || r0 >= M) return;  // the whole box outside C (warp-uniform): nothing to store
+    if (lane == 0) bulk_wait_read<1>();
+    __syncwarp();
+    uint4* row = reinterpret_cast<uint4*>(quarter + lane * 128);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        uint32_t h[4];
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+            const __half2 x = __floats2half2_rn(v[8 * j + 2 * w], v[8 * j + 2 * w + 1]);
+            h[w] = *reinterpret_cast<const uint32_t*>(&x);
+        }
+        row[j ^ (lane & 7)] = make_uint4(h[0], h[1], h[2], h[3]);
+    }
+    fence_proxy_async_shared();
+    __syncwarp();
+    if (lane == 0) {
+        tma_store_2d(tmc, quarter, n, r0);
+        bulk_commit();
+    }
+}
+
 // ------------------------------------------------------------------ the partials of a split tile
 // Slot layout: 128 rows x BN columns of fp32, interleaved by groups of 4 columns: [col / 4][row][col % 4].  TMEM lane
 // `row`'s 4-column group is one 16-byte vector, and the 32 lanes of a warp touch 512 contiguous bytes per vector

@@ -42,7 +42,8 @@ namespace bw {
 // ------------------------------------------------------------------ the kernel
 template <int BN, bool SWAP, bool PAIR, int EPI = kEpiF16, int WM = 1>
 __global__ void __launch_bounds__(kThreads, 1)
-    gemm_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmy, const Params p)
+    gemm_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmy,
+                const __grid_constant__ CUtensorMap tmc, const Params p)
 {
     using G = KGeom<BN, SWAP, PAIR, EPI, WM>;
     constexpr int AN = G::kAccN;  // accumulator columns (TMEM)
@@ -106,6 +107,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp == 0 && lane == 0) {
         prefetch_tmap(&tmx);
         prefetch_tmap(&tmy);
+        if (kEpiTma<BN, SWAP, PAIR, EPI>) prefetch_tmap(&tmc);
     }
     if (warp == 1) {
         if (PAIR) {
@@ -356,6 +358,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         Seg sg;
         int acc = 0, seg = 0;
         uint32_t aph = 0;
+        unsigned epi_chunks = 0;  // BW_EPI_TMA: 64-column chunks this warp has stored (the staging buffer alternates)
         unsigned rs_acked = 0;  // kEpiRS: owners whose ack of the previous call this block has seen
         uint32_t win_ph = 0;    // kEpiRS: the window's buffers (rbar, krecv): the parity each waits for next
         int win_next = 0;       // kEpiRS: the buffer the next copy into the window goes to
@@ -595,7 +598,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                     for (int h = 0; h < kLdw / 16; ++h) tmem_ld16(tbase + (uint32_t)(c0 + 16 * h), r[h]);
                     tmem_wait_ld();
                     if (G::kHalves && c0 + kLdw == AN / 2) release_acc(0);  // the first half is read
-                    if (!SWAP && kLdw == 64 && BW_EPI_LINES) {  // whole lines of C (store_rows64)
+                    if (kEpiTma<BN, SWAP, PAIR, EPI> && kLdw == 64) {  // a TMA store per warp (store_rows64_tma)
+                        float v[64];
+#pragma unroll
+                        for (int j = 0; j < 64; ++j) v[j] = __uint_as_float(r[j / 16][j % 16]);
+                        uint8_t* quarter = smem + G::kWindowOffset + (epi_chunks++ & 1u) * 16384u + q * 4096;
+                        store_rows64_tma(&tmc, quarter, m0 + q * 32, n0 + c0, s.M, s.N, lane, v);
+                    } else if (!SWAP && kLdw == 64 && BW_EPI_LINES) {  // whole lines of C (store_rows64)
                         float v[64];
 #pragma unroll
                         for (int j = 0; j < 64; ++j) v[j] = __uint_as_float(r[j / 16][j % 16]);
@@ -699,6 +708,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
             }
         }
+        // the TMA stores of C complete before the block leaves (their sources are this block's shared memory)
+        if (kEpiTma<BN, SWAP, PAIR, EPI> && lane == 0) bulk_wait<0>();
         if (threadIdx.x == kEpiThread0) BW_TRACE_AT(4);
     }
 

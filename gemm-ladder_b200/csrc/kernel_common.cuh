@@ -121,9 +121,13 @@ struct Geom {
     static_assert(kTmemCols <= 512, "tensor memory");
 };
 
-// The geometry of a kernel instance: the fused reduce-scatter's reserves its window.
+// The geometry of a kernel instance: the fused reduce-scatter's reserves its window, the fp16 TILE / PAIR epilogue its
+// staging buffers for TMA stores of C (BW_EPI_TMA).
+template <int BN, bool SWAP, bool PAIR, int EPI>
+constexpr bool kEpiTma = BW_EPI_TMA && !SWAP && EPI == kEpiF16;
 template <int BN, bool SWAP, bool PAIR, int EPI, int WM = 1>
-using KGeom = Geom<BN, SWAP, PAIR, WM, EPI == kEpiRS ? kPlanRsWindowBytes : 0>;
+using KGeom = Geom<BN, SWAP, PAIR, WM,
+                   EPI == kEpiRS ? kPlanRsWindowBytes : kEpiTma<BN, SWAP, PAIR, EPI> ? kPlanEpiStageBytes : 0>;
 
 // The 3-D form for the MN-major operand (BW_TMA3D): `n64` is the first 64-column block; the map's box holds the
 // stage's blocks.

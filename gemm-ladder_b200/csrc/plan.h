@@ -114,6 +114,12 @@
 #ifndef BW_DSMEM_GBS
 #define BW_DSMEM_GBS 100.0     // distributed-shared-memory bytes one SM sends per second (an estimate, not measured)
 #endif
+#ifndef BW_EPI_TMA
+#define BW_EPI_TMA 0           // TILE / PAIR fp16 epilogue: each warp's 32 rows x 64 columns of C through a swizzled 4 KB
+                               // quarter of a shared-memory staging buffer (two buffers of 16 KB after the stage ring,
+                               // alternating by 64-column chunk) and one TMA store per warp and chunk, in place of
+                               // whole-line stores from registers (0); the ring loses what the buffers take
+#endif
 #ifndef BW_SK_ONE_WAVE
 #define BW_SK_ONE_WAVE 1       // stream-K over every tile when they make one full wave and part of another (the
                                // split-K tail's units then double a block's work: measured qkv_m512 -12 %)
@@ -143,6 +149,8 @@ inline int plan_stage_bytes(int bn, int ranks, int wm = 1) { return 128 * wm * 6
 inline int plan_cstage_bytes(bool swap) { return swap ? 2 * 16 * 128 * 2 : 0; }
 // The fused reduce-scatter's window (two 32 KB buffers) for the owner's partials, after the stage ring.
 constexpr int kPlanRsWindowBytes = 2 * 32768;
+// The TMA-store epilogue's staging (BW_EPI_TMA): two buffers of 128 rows x 64 fp16 columns, after the stage ring.
+constexpr int kPlanEpiStageBytes = 2 * 16384;
 inline int plan_stages(int bn, int ranks, bool swap, int wm = 1, int reserve = 0)
 {
     const int s = (BW_SMEM_LIMIT - 1024 - 512 - plan_cstage_bytes(swap) - reserve) / plan_stage_bytes(bn, ranks, wm);
@@ -400,7 +408,9 @@ inline int make_plan(int M, int N, int K, int sms, int pairs, int variant, bw_pl
         if (q.sk_iters < P) return BW_ERR_ARG;  // every block owns at least one stream-K K-block
     }
     q.grid = P * ranks;
-    const int reserve = (flags & kPlanRsWindow) ? kPlanRsWindowBytes : 0;
+    // shared memory after the ring: the fused reduce-scatter's window, or the fp16 TILE / PAIR epilogue's staging
+    const bool epi_tma = BW_EPI_TMA && !swap && !(flags & (kPlanNoSwap | kPlanRsWindow));
+    const int reserve = (flags & kPlanRsWindow) ? kPlanRsWindowBytes : epi_tma ? kPlanEpiStageBytes : 0;
     q.stages = plan_stages(q.bn, ranks, swap, q.wm, reserve);
     q.smem_bytes = plan_smem_bytes(q.bn, ranks, swap, q.wm, reserve);
     q.tmem_cols = plan_tmem_cols(q.bn * q.wm);

@@ -185,6 +185,34 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
                  : "memory");
 }
 
+// ------------------------------------------------------------------ TMA stores (the epilogue's C tiles)
+// A 2-D tiled store of one box from this block's shared memory (in the map's swizzle) to global memory; the map's
+// bounds clip the box (rows or columns past the tensor are not written).  It joins the thread's open bulk-async group.
+__device__ __forceinline__ void tma_store_2d(const void* tmap, const void* src, int x, int y)
+{
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                     reinterpret_cast<uint64_t>(tmap)),
+                 "r"(x), "r"(y), "r"(smem_u32(src))
+                 : "memory");
+}
+// Closes the thread's open bulk-async group.
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Waits until at most N of the thread's committed groups are still reading their shared-memory sources (the sources of
+// the others may be overwritten).  A store's read of shared memory always completes; it depends on no other agent.
+template <int N>
+__device__ __forceinline__ void bulk_wait_read()
+{
+    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+// Waits until at most N of the thread's committed groups are incomplete (their writes to global memory done).
+template <int N>
+__device__ __forceinline__ void bulk_wait()
+{
+    asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
+}
+// Makes this thread's ordinary writes to shared memory visible to the async proxy (a TMA store that reads them next).
+__device__ __forceinline__ void fence_proxy_async_shared() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
 // ------------------------------------------------------------------ clusters (the CTA pair of cta_group::2)
 __device__ __forceinline__ uint32_t cluster_ctarank()
 {

@@ -16,6 +16,7 @@
 // Built with -DBW_KSPLIT=1 it runs the K split over clusters of 2 to 8 blocks (plan.h) in place of the halves.
 #include <algorithm>
 #include <functional>
+#include <future>
 #include <string>
 #include <thread>
 #include <vector>
@@ -39,6 +40,14 @@ void map_blocks(CUtensorMap* m, const void* base, uint64_t cols, uint64_t rows, 
     emu::make_map(m, base, 3, dims, strides, box);
 }
 uint32_t swap_rows(const bw_plan& q) { return (uint32_t)(q.kernel == BW_KERNEL_SWAP_PAIR ? q.bn / 2 : q.bn); }
+// the same choice as csrc/bwgemm.cu's make_c_map: C's map for the TMA-store epilogue (fp16 TILE / PAIR plans)
+void make_c_map(const bw_plan& q, void* C, int M, int N, int epi, const CUtensorMap& mx, CUtensorMap* mc)
+{
+    if (BW_EPI_TMA && epi == kEpiF16 && (q.kernel == BW_KERNEL_TILE || q.kernel == BW_KERNEL_PAIR))
+        map2(mc, C, N, M, 64, 32);
+    else
+        *mc = mx;
+}
 // the same choices as csrc/bwgemm.cu's make_maps
 void make_maps(const bw_plan& q, const void* A, const void* B, int M, int N, int K, CUtensorMap* mx, CUtensorMap* my,
                bool tn)
@@ -107,7 +116,7 @@ inline bool g_dry_run = false;  // dispatch and check a plan's instance and geom
 inline long long g_noalloc_cap = -1;  // >= 0: bw_emu_gemm plans as bw_gemm_f16_noalloc does, with this many bytes
 
 template <int BN, bool SWAP, bool PAIR, int EPI, int WM>
-int launch(const bw_plan& q, const CUtensorMap& mx, const CUtensorMap& my, const Params& p)
+int launch(const bw_plan& q, const CUtensorMap& mx, const CUtensorMap& my, const CUtensorMap& mc, const Params& p)
 {
     using G = KGeom<BN, SWAP, PAIR, EPI, WM>;
     if (q.smem_bytes != G::kSmemBytes || q.stages != G::kStages || q.tmem_cols != G::kTmemCols || q.wm != WM) {
@@ -123,6 +132,7 @@ int launch(const bw_plan& q, const CUtensorMap& mx, const CUtensorMap& my, const
     }
     if (g_dry_run) return BW_OK;
     emu::g_smem_limit = q.smem_bytes - 1024;
+    const unsigned seq = emu::g_launch_seq++;
     const int cores = (int)std::max(1u, std::thread::hardware_concurrency());
     const int batch = g_cluster_batch > 0 ? (int)g_cluster_batch
                                           : std::max(1, std::min(cores, 4096 / (cs * emu::kCtaThreads)));
@@ -143,18 +153,24 @@ int launch(const bw_plan& q, const CUtensorMap& mx, const CUtensorMap& my, const
         }
         std::vector<std::thread> threads;
         threads.reserve((size_t)(b1 - b0) * emu::kCtaThreads);
+        // every thread of the batch waits at a gate until all exist, so that the blocks start together (the order of
+        // thread creation gives no block a head start), then by its block's start jitter
+        std::promise<void> gate;
+        std::shared_future<void> open = gate.get_future().share();
         for (int blk = b0; blk < b1; ++blk)
             for (int t = 0; t < emu::kCtaThreads; ++t)
-                threads.emplace_back([&, blk, t] {
+                threads.emplace_back([&, blk, t, open] {
+                    open.wait();
                     emu::t_cta = ctas[(size_t)(blk - b0)].get();
                     emu::t_tid = t;
                     threadIdx = dim3((unsigned)t);
                     blockIdx = dim3((unsigned)blk);
                     gridDim = dim3((unsigned)q.grid);
                     blockDim = dim3((unsigned)emu::kCtaThreads);
-                    emu::start_jitter((unsigned)blk);
-                    gemm_kernel<BN, SWAP, PAIR, EPI, WM>(mx, my, p);
+                    emu::start_jitter((unsigned)blk, seq);
+                    gemm_kernel<BN, SWAP, PAIR, EPI, WM>(mx, my, mc, p);
                 });
+        gate.set_value();
         for (auto& th : threads) th.join();
         // every block's queued work (an st.async into another block among it) done before any block goes away
         for (auto& c : ctas) {
@@ -166,64 +182,65 @@ int launch(const bw_plan& q, const CUtensorMap& mx, const CUtensorMap& my, const
 }
 
 // the plan's kernel instance (csrc/bwgemm.cu's dispatch)
-int dispatch(const bw_plan& q, const CUtensorMap& mx, const CUtensorMap& my, const Params& p, int epi)
+int dispatch(const bw_plan& q, const CUtensorMap& mx, const CUtensorMap& my, const CUtensorMap& mc, const Params& p,
+             int epi)
 {
     if (epi == kEpiF32) {
-        if (q.kernel == BW_KERNEL_PAIR) return launch<256, false, true, kEpiF32, 1>(q, mx, my, p);
-        if (q.kernel == BW_KERNEL_TILE && q.bn == 256) return launch<256, false, false, kEpiF32, 1>(q, mx, my, p);
+        if (q.kernel == BW_KERNEL_PAIR) return launch<256, false, true, kEpiF32, 1>(q, mx, my, mc, p);
+        if (q.kernel == BW_KERNEL_TILE && q.bn == 256) return launch<256, false, false, kEpiF32, 1>(q, mx, my, mc, p);
         return BW_ERR_ARG;
     }
     if (epi == kEpiSwiGLU) {
         if (q.sk_tiles != 0) return BW_ERR_ARG;
-        if (q.kernel == BW_KERNEL_PAIR) return launch<256, false, true, kEpiSwiGLU, 1>(q, mx, my, p);
-        if (q.kernel == BW_KERNEL_TILE && q.bn == 256) return launch<256, false, false, kEpiSwiGLU, 1>(q, mx, my, p);
+        if (q.kernel == BW_KERNEL_PAIR) return launch<256, false, true, kEpiSwiGLU, 1>(q, mx, my, mc, p);
+        if (q.kernel == BW_KERNEL_TILE && q.bn == 256) return launch<256, false, false, kEpiSwiGLU, 1>(q, mx, my, mc, p);
         return BW_ERR_ARG;
     }
 #if BW_PAIR_WIDE
-    if (q.kernel == BW_KERNEL_PAIR && q.bn == 512) return launch<512, false, true, kEpiF16, 1>(q, mx, my, p);
+    if (q.kernel == BW_KERNEL_PAIR && q.bn == 512) return launch<512, false, true, kEpiF16, 1>(q, mx, my, mc, p);
 #endif
-    if (q.kernel == BW_KERNEL_PAIR) return launch<256, false, true, kEpiF16, 1>(q, mx, my, p);
+    if (q.kernel == BW_KERNEL_PAIR) return launch<256, false, true, kEpiF16, 1>(q, mx, my, mc, p);
     if (q.kernel == BW_KERNEL_TILE) {
         switch (q.bn) {
-        case 64: return launch<64, false, false, kEpiF16, 1>(q, mx, my, p);
-        case 128: return launch<128, false, false, kEpiF16, 1>(q, mx, my, p);
-        case 256: return launch<256, false, false, kEpiF16, 1>(q, mx, my, p);
+        case 64: return launch<64, false, false, kEpiF16, 1>(q, mx, my, mc, p);
+        case 128: return launch<128, false, false, kEpiF16, 1>(q, mx, my, mc, p);
+        case 256: return launch<256, false, false, kEpiF16, 1>(q, mx, my, mc, p);
         default: return BW_ERR_ARG;
         }
     }
 #if BW_SWAP_PAIR
     if (q.kernel == BW_KERNEL_SWAP_PAIR) {
         switch (q.bn * 4 + q.wm) {
-        case 64 * 4 + 1: return launch<64, true, true, kEpiF16, 1>(q, mx, my, p);
-        case 128 * 4 + 1: return launch<128, true, true, kEpiF16, 1>(q, mx, my, p);
-        case 64 * 4 + 2: return launch<64, true, true, kEpiF16, 2>(q, mx, my, p);
-        case 128 * 4 + 2: return launch<128, true, true, kEpiF16, 2>(q, mx, my, p);
+        case 64 * 4 + 1: return launch<64, true, true, kEpiF16, 1>(q, mx, my, mc, p);
+        case 128 * 4 + 1: return launch<128, true, true, kEpiF16, 1>(q, mx, my, mc, p);
+        case 64 * 4 + 2: return launch<64, true, true, kEpiF16, 2>(q, mx, my, mc, p);
+        case 128 * 4 + 2: return launch<128, true, true, kEpiF16, 2>(q, mx, my, mc, p);
         default: return BW_ERR_ARG;
         }
     }
 #endif
     if (q.wm == 2) {
         switch (q.bn) {
-        case 16: return launch<16, true, false, kEpiF16, 2>(q, mx, my, p);
-        case 32: return launch<32, true, false, kEpiF16, 2>(q, mx, my, p);
-        case 48: return launch<48, true, false, kEpiF16, 2>(q, mx, my, p);
-        case 64: return launch<64, true, false, kEpiF16, 2>(q, mx, my, p);
-        case 80: return launch<80, true, false, kEpiF16, 2>(q, mx, my, p);
-        case 96: return launch<96, true, false, kEpiF16, 2>(q, mx, my, p);
-        case 112: return launch<112, true, false, kEpiF16, 2>(q, mx, my, p);
-        case 128: return launch<128, true, false, kEpiF16, 2>(q, mx, my, p);
+        case 16: return launch<16, true, false, kEpiF16, 2>(q, mx, my, mc, p);
+        case 32: return launch<32, true, false, kEpiF16, 2>(q, mx, my, mc, p);
+        case 48: return launch<48, true, false, kEpiF16, 2>(q, mx, my, mc, p);
+        case 64: return launch<64, true, false, kEpiF16, 2>(q, mx, my, mc, p);
+        case 80: return launch<80, true, false, kEpiF16, 2>(q, mx, my, mc, p);
+        case 96: return launch<96, true, false, kEpiF16, 2>(q, mx, my, mc, p);
+        case 112: return launch<112, true, false, kEpiF16, 2>(q, mx, my, mc, p);
+        case 128: return launch<128, true, false, kEpiF16, 2>(q, mx, my, mc, p);
         default: return BW_ERR_ARG;
         }
     }
     switch (q.bn) {
-    case 16: return launch<16, true, false, kEpiF16, 1>(q, mx, my, p);
-    case 32: return launch<32, true, false, kEpiF16, 1>(q, mx, my, p);
-    case 48: return launch<48, true, false, kEpiF16, 1>(q, mx, my, p);
-    case 64: return launch<64, true, false, kEpiF16, 1>(q, mx, my, p);
-    case 80: return launch<80, true, false, kEpiF16, 1>(q, mx, my, p);
-    case 96: return launch<96, true, false, kEpiF16, 1>(q, mx, my, p);
-    case 112: return launch<112, true, false, kEpiF16, 1>(q, mx, my, p);
-    case 128: return launch<128, true, false, kEpiF16, 1>(q, mx, my, p);
+    case 16: return launch<16, true, false, kEpiF16, 1>(q, mx, my, mc, p);
+    case 32: return launch<32, true, false, kEpiF16, 1>(q, mx, my, mc, p);
+    case 48: return launch<48, true, false, kEpiF16, 1>(q, mx, my, mc, p);
+    case 64: return launch<64, true, false, kEpiF16, 1>(q, mx, my, mc, p);
+    case 80: return launch<80, true, false, kEpiF16, 1>(q, mx, my, mc, p);
+    case 96: return launch<96, true, false, kEpiF16, 1>(q, mx, my, mc, p);
+    case 112: return launch<112, true, false, kEpiF16, 1>(q, mx, my, mc, p);
+    case 128: return launch<128, true, false, kEpiF16, 1>(q, mx, my, mc, p);
     default: return BW_ERR_ARG;
     }
 }
@@ -278,7 +295,9 @@ extern "C" __attribute__((visibility("default"))) int bw_emu_check_plan(int M, i
     make_maps(q, dummy, dummy, M, N, K, &mx, &my, tn != 0);  // the driver's limits on a tensor map: findings
     const Params p = make_params(q, M, N, K, nullptr, nullptr, nullptr, tn != 0);
     g_dry_run = true;
-    rc = epi == kEpiRS ? launch<256, false, true, kEpiRS, 1>(q, mx, my, p) : dispatch(q, mx, my, p, epi);
+    CUtensorMap mc;
+    make_c_map(q, const_cast<unsigned char*>(dummy), M, N, epi, mx, &mc);
+    rc = epi == kEpiRS ? launch<256, false, true, kEpiRS, 1>(q, mx, my, mx, p) : dispatch(q, mx, my, mc, p, epi);
     g_dry_run = false;
     return rc ? rc : emu::g_findings ? BW_ERR_LAUNCH : BW_OK;
 }
@@ -324,7 +343,9 @@ extern "C" __attribute__((visibility("default"))) int bw_emu_gemm(const void* A,
     CUtensorMap mx, my;
     make_maps(q, A, B, M, N, K, &mx, &my, tn != 0);
     const Params p = make_params(q, M, N, K, C, work.data(), counters.data(), tn != 0);
-    rc = dispatch(q, mx, my, p, epi);
+    CUtensorMap mc;
+    make_c_map(q, C, M, N, epi, mx, &mc);
+    rc = dispatch(q, mx, my, mc, p, epi);
     if (status) std::memcpy(status, g_status, sizeof g_status);
     if (dirty) *dirty = (int)std::count_if(counters.begin(), counters.begin() + q.counters, [](int v) { return v != 0; });
     if (findings) *findings = emu::g_findings.load();
@@ -356,9 +377,12 @@ int launch_rs(const bw_plan& q, int world, std::vector<EmuRank>& ranks, const st
         return BW_ERR_LAUNCH;
     }
     emu::g_smem_limit = q.smem_bytes - 1024;
+    const unsigned seq = emu::g_launch_seq++;
     std::vector<std::unique_ptr<emu::Cluster>> clusters;
     std::vector<std::unique_ptr<emu::Cta>> ctas;
     std::vector<std::thread> threads;
+    std::promise<void> gate;  // as in launch: the threads start together once all exist
+    std::shared_future<void> open = gate.get_future().share();
     for (int r = 0; r < world; ++r) {
         if (r == absent) continue;
         for (int c0 = 0; c0 < q.grid; c0 += 2) {
@@ -373,7 +397,8 @@ int launch_rs(const bw_plan& q, int world, std::vector<EmuRank>& ranks, const st
             }
             for (int k = 0; k < 2; ++k)
                 for (int t = 0; t < emu::kCtaThreads; ++t)
-                    threads.emplace_back([&, r, c0, k, t, cl] {
+                    threads.emplace_back([&, r, c0, k, t, cl, open] {
+                        open.wait();
                         emu::t_cta = cl->cta[k];
                         emu::t_tid = t;
                         t_status = ranks[r].status;
@@ -381,11 +406,12 @@ int launch_rs(const bw_plan& q, int world, std::vector<EmuRank>& ranks, const st
                         blockIdx = dim3((unsigned)(c0 + k));
                         gridDim = dim3((unsigned)q.grid);
                         blockDim = dim3((unsigned)emu::kCtaThreads);
-                        emu::start_jitter((unsigned)(r * q.grid + c0 + k));
-                        gemm_kernel<256, false, true, kEpiRS, 1>(mx[r], my[r], p[r]);
+                        emu::start_jitter((unsigned)(r * q.grid + c0 + k), seq);
+                        gemm_kernel<256, false, true, kEpiRS, 1>(mx[r], my[r], mx[r], p[r]);
                     });
         }
     }
+    gate.set_value();
     for (auto& th : threads) th.join();
     for (auto& c : ctas) {
         c->tma.finish();

@@ -208,13 +208,17 @@ inline void Engine::start(Cta* c)
     });
 }
 
-// A block's start delay under g_start_jitter_us: the same for every thread of the block (from its index), plus a few
-// microseconds per thread.
-inline void start_jitter(unsigned block)
+// A block's start delay under g_start_jitter_us: the same for every thread of the block, drawn from the block's index
+// and the launch's sequence number (so the blocks of a cluster start in another order on each launch): none for about
+// half the blocks, up to g_start_jitter_us for the others; plus a few microseconds per thread.
+inline std::atomic<unsigned> g_launch_seq{0};
+inline void start_jitter(unsigned block, unsigned seq)
 {
     if (g_start_jitter_us <= 0) return;
-    std::minstd_rand rng(block * 2654435761u + 1u);
-    const unsigned d = rng() % (unsigned)(g_start_jitter_us + 1) + (unsigned)(t_tid % 8);
+    std::minstd_rand rng((block + 1u) * 2654435761u ^ (seq * 40503u + 1u));
+    rng.discard(3);
+    const unsigned r = rng();
+    const unsigned d = ((r >> 7) & 1u ? r % (unsigned)(g_start_jitter_us + 1) : 0u) + (unsigned)(t_tid % 8);
     std::this_thread::sleep_for(std::chrono::microseconds(d));
 }
 
@@ -408,6 +412,56 @@ inline long long tma_copy(void* dst, const void* tmap, int x, int y, int z)
                 std::memcpy(c->smem + off, &v, 2);
             }
     return bytes;
+}
+
+// TMA stores: each issued store is queued to the block's TMA engine, which later reads the box out of shared memory
+// (through the 128-byte swizzle, as the map says) and writes the part of it inside the tensor to global memory -- so a
+// kernel that overwrites a store's source before waiting for the store's read sends the new data, as on the GPU.  A
+// thread's stores join its open group until it commits; a wait for the groups counts the committed ones still pending.
+using StoreFlag = std::shared_ptr<std::atomic<bool>>;
+inline thread_local std::vector<StoreFlag> t_open_stores;
+inline thread_local std::deque<std::vector<StoreFlag>> t_store_groups;
+
+inline void tma_store(const void* tmap, const void* src, int x, int y)
+{
+    Map m;
+    std::memcpy(&m, tmap, sizeof m);
+    Cta* c = t_cta;
+    const uint32_t base = offset_of(src);
+    if (m.rank != 2 || m.box[0] * 2 != 128) finding("a TMA store through a map that is not 2-D with 128-byte rows");
+    if (((long long)x * 2) % 16 || x < 0 || y < 0) finding("a TMA store at (%d, %d): not on 16 bytes, or negative", x, y);
+    if (base % 1024) finding("a TMA store source not on a 1024-byte swizzle atom (offset %u)", base);
+    const uint32_t bytes = m.box[0] * m.box[1] * 2;
+    if (base + bytes > (uint32_t)g_smem_limit || over_mbar(c, base, bytes)) {
+        finding("a TMA store source past the launch's shared memory or over an mbarrier (offset %u)", base);
+        return;
+    }
+    StoreFlag done = std::make_shared<std::atomic<bool>>(false);
+    t_open_stores.push_back(done);
+    c->tma.post([=] {
+        uint8_t* g = const_cast<uint8_t*>(m.base);
+        for (uint32_t rr = 0; rr < m.box[1]; ++rr)
+            for (uint32_t cc = 0; cc < m.box[0]; ++cc) {
+                const long long gx = (long long)x + cc, gy = (long long)y + rr;
+                if (gx >= (long long)m.dims[0] || gy >= (long long)m.dims[1]) continue;  // clipped
+                std::memcpy(g + gy * m.strides[1] + gx * 2, c->smem + swizzle128(base + (rr * m.box[0] + cc) * 2), 2);
+            }
+        done->store(true);
+    });
+}
+inline void store_commit()
+{
+    t_store_groups.push_back(std::move(t_open_stores));
+    t_open_stores.clear();
+}
+// Waits until at most n committed groups are pending (reads and writes alike: here a store is done when both are).
+inline void store_wait(int n)
+{
+    while ((int)t_store_groups.size() > n) {
+        for (const StoreFlag& f : t_store_groups.front())
+            while (!f->load()) std::this_thread::sleep_for(std::chrono::microseconds(5));
+        t_store_groups.pop_front();
+    }
 }
 
 inline void bulk_copy(void* dst, const void* src, uint32_t bytes)

@@ -40,6 +40,8 @@ BUILDS = {
     "next": ("BW_KSPLIT=1", "BW_SK_PART_WAVE=1", "BW_PAIR_WIDE=1", "BW_SWAP_PAIR=1"),
     # the 256 x 512 pair tile wherever the rule allows it, so that small emulated shapes run the wide kernel
     "wide": ("BW_PAIR_WIDE=1", "BW_PAIR_WIDE_KB_NS=1", "BW_PAIR_WIDE_EPI_NS=0", "BW_FIXUP_KB=0"),
+    # the TMA-store epilogue
+    "tma": ("BW_EPI_TMA=1",),
 }
 
 GK, EP, KC, SC, PL = "csrc/gemm_kernel.cuh", "csrc/epilogue.cuh", "csrc/kernel_common.cuh", "csrc/schedule.h", "csrc/plan.h"
@@ -137,9 +139,10 @@ MUTATIONS = [
      "epi_go[seg & 1] = wait_bounded(&tfull[acc], aph, abort_flag, p.wait_ns, site(2, 2, acc), seg) ? 1 : 0;",
      "epi_go[seg & 1] = 1;", 0, "library"),
     ("epi_acc_parity", GK, "wait_bounded(&tfull[acc], aph,", "wait_bounded(&tfull[acc], aph ^ 1u,", 0, "library"),
-    ("epi_release_other_acc", GK, "mbar_arrive(&tempty[a]);", "mbar_arrive(&tempty[a ^ 1]);", 0, "library"),
-    ("epi_release_other_acc_pair", GK, "mbar_arrive_cluster(tempty_leader0 + 8u * (uint32_t)a);",
-     "mbar_arrive_cluster(tempty_leader0 + 8u * (uint32_t)(a ^ 1));", 0, "library"),
+    ("epi_whole_tile_kept", GK, "                else\n                    release_acc(acc);\n",
+     "                else\n                    (void)acc;\n", 0, "library"),
+    ("epi_release_early", GK, "if (G::kHalves && c0 + kLdw == AN / 2) release_acc(0);  // the first half is read",
+     "if (G::kHalves ? c0 + kLdw == AN / 2 : c0 == 0) release_acc(G::kHalves ? 0 : acc);", 0, "library"),
     ("epi_split_acc_kept", GK, "if (!last_seg) release_all(acc);", "if (false) release_all(acc);", 0, "library"),
     ("epi_lane_quarter", GK, "const int q = warp & 3;         // the TMEM lane quarter this warp may access",
      "const int q = (warp + 1) & 3;", 0, "library"),
@@ -306,6 +309,18 @@ MUTATIONS = [
      "const uint32_t yw = sy;", 0, "wide"),
     ("wide_catch_up_wait", GK, "if (!wait_bounded(&tempty[1], aph ^ 1u, abort_flag, p.wait_ns, site(1, 3, 1), seg)) return false;",
      "(void)0;", 0, "wide"),
+    # ---------------------------------------------------------------- the TMA-store epilogue (BW_EPI_TMA)
+    ("tma_no_read_wait", EP, "if (lane == 0) bulk_wait_read<1>();", "(void)0;", 0, "tma"),
+    ("tma_one_buffer", GK, "(epi_chunks++ & 1u) * 16384u", "(epi_chunks++ & 0u) * 16384u", 0, "tma"),
+    ("tma_swizzle_off", EP, "row[j ^ (lane & 7)] = make_uint4(h[0], h[1], h[2], h[3]);",
+     "row[j] = make_uint4(h[0], h[1], h[2], h[3]);", 0, "tma"),
+    ("tma_box_rows", EP, "tma_store_2d(tmc, quarter, n, r0);", "tma_store_2d(tmc, quarter, n, r0 + 8);", 0, "tma"),
+    ("tma_quarter_overlap", GK, "(epi_chunks++ & 1u) * 16384u + q * 4096", "(epi_chunks++ & 1u) * 16384u + q * 2048", 0,
+     "tma"),
+    ("tma_uncommitted", EP, "tma_store_2d(tmc, quarter, n, r0);\n        bulk_commit();",
+     "tma_store_2d(tmc, quarter, n, r0);", 0, "tma"),
+    ("tma_pair_order", EP, "const __half2 x = __floats2half2_rn(v[8 * j + 2 * w], v[8 * j + 2 * w + 1]);",
+     "const __half2 x = __floats2half2_rn(v[8 * j + 2 * w + 1], v[8 * j + 2 * w]);", 0, "tma"),
     ("swap_pair_weights", GK, "const int wcol = (tn * R + rank) * 128 * WM;", "const int wcol = (tn * R) * 128 * WM;", 0,
      "next"),
     ("swap_pair_tokens", GK, "load_tile<PAIR, BW_HINT_A>(sy, &tmy, kb * kBK, rank * (BN / R),",
@@ -338,7 +353,7 @@ CASES = {
         (256, 512, 256, 8, 6, 0, False),    # 128 x 64 tiles
         (256, 512, 256, 8, 1, 0, False),    # whole pair tiles only
         (2304, 512, 128, 8, 0, 0, False),   # nine rows of pair tiles: a second, reversed serpentine group
-        (768, 1280, 4096, 8, 0, 0, False),  # more split-K units than pairs
+        (512, 2560, 4096, 16, 0, 0, False), # four two-way split tiles, each pair's unit before its whole tiles
         (16, 256, 2048, 8, 0, 0, False),    # K halves deeper than the stage ring
         (256, 512, 1024, 8, 5, 0, False),   # single-SM tiles deeper than the stage ring
         (64, 2304, 1024, 8, 0, 0, False),   # swap-AB stream-K, 256-column tiles, several tiles per block
@@ -356,6 +371,14 @@ CASES = {
         (128, 4096, 256, 8, 0, 0, False),
         (16, 1280, 256, 8, 0, 0, True),
         (80, 2304, 256, 8, 0, 0, True),
+    ],
+    "tma": [
+        (256, 256, 128, 8, 0, 0, False),    # one pair tile
+        (512, 2048, 128, 8, 0, 0, False),   # four pair tiles per pair
+        (130, 320, 192, 8, 0, 0, False),    # ragged rows (the map clips them)
+        (256, 512, 1024, 8, 5, 0, False),   # single-SM tiles
+        (256, 512, 256, 8, 6, 0, False),    # 128 x 64 tiles
+        (256, 256, 128, 8, 0, 0, True),     # B as N x K
     ],
     "wide": [
         (256, 1024, 256, 8, 0, 0, False),   # 256 x 512 pair tiles, whole waves
@@ -449,7 +472,7 @@ def check(lib_path, build_name, cluster_batch):
     L.bw_emu_set(b"barrier_limit_ms", 8000)
     L.bw_emu_set(b"cluster_batch", cluster_batch)
     L.bw_emu_set(b"ld_delay_us", 30)               # a slow epilogue: an MMA that does not wait for it overwrites
-    L.bw_emu_set(b"start_jitter_us", 2000)         # blocks start apart: a peer's barriers unset show
+    L.bw_emu_set(b"start_jitter_us", 50000)        # blocks start apart: a peer's barriers unset show
 
     def call(A, B, M, N, K, sms, variant, epi, tn):
         Bx = np.ascontiguousarray(np.asarray(B).reshape(K, N).T) if tn else np.ascontiguousarray(B)

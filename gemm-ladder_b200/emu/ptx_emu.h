@@ -147,8 +147,15 @@ inline void tma_load_3d_hint(void* dst, const void* tmap, int x, int y, int z, u
 {
     tma_load_3d(dst, tmap, x, y, z, bar);
 }
-// One memory model for every access here: the proxy fence is an ordinary full fence.
+// One memory model for every access here: the proxy fences are ordinary full fences.
 inline void fence_proxy_async_global() { std::atomic_thread_fence(std::memory_order_seq_cst); }
+inline void fence_proxy_async_shared() { std::atomic_thread_fence(std::memory_order_seq_cst); }
+inline void tma_store_2d(const void* tmap, const void* src, int x, int y) { emu::tma_store(tmap, src, x, y); }
+inline void bulk_commit() { emu::store_commit(); }
+template <int N>
+inline void bulk_wait_read() { emu::store_wait(N); }
+template <int N>
+inline void bulk_wait() { emu::store_wait(N); }
 inline uint64_t policy_evict_first() { return 0; }
 inline uint64_t policy_evict_last() { return 0; }
 inline void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar)
