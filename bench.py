@@ -724,10 +724,15 @@ def run_ours(args):
             err = f"{type(exc).__name__}: {exc}"[:200]
         tp = dist_max(tp_rank, world)  # every rank joins, whatever happened on it
         if math.isfinite(tp):
+            h2d_gbs = (M * K + K * N) * 2 * steps_e2e / tp / 1e9  # each rank's host -> device rate over the steps
             e2e.update({"value": round(flops_rank * world * steps_e2e / tp / 1e12, 2), "serial_value": serial,
                         "path": "bwgemm.gemm (ctypes -> bw_gemm_f16) with pinned host buffers; step i + 1's "
                                 "host -> device copies and step i - 1's device -> host copy overlap step i's GEMM "
-                                "(three streams, two device slots)"})
+                                "(three streams, two device slots)",
+                        "h2d_gbs_per_rank": round(h2d_gbs, 1),
+                        "bound": ("host -> device copies (the GEMM takes %.0f%% of a step): the ranks share the host's "
+                                  "pinned-memory bandwidth" % (100.0 * t / args.steps / (tp / steps_e2e)))
+                                 if t / args.steps < 0.8 * tp / steps_e2e else "the GEMM"})
         else:
             e2e["pipelined_error"] = err
 

@@ -1,9 +1,10 @@
 """Build the rung's native code in-tree: gemm-ladder_b200/lib/libbwgemm.so (sm_100a, cross-compiled by nvcc; no GPU
 needed).  ``python gemm-ladder_b200/build.py [--force] [--trace] [--next]``; --trace builds lib/libbwgemm_trace.so,
 the same library with the per-block timeline compiled in (-DBW_TRACE: per block, %globaltimer stamps of its phases,
-read back with bw_trace_read); --next builds lib/libbwgemm_next.so, the library with the options built but not yet
-measured on a B200 (the K split over clusters of 2 to 8, stream-K over a part wave of pair tiles, pair tiles of
-256 x 512, swap-AB on SM pairs), for A/B runs: BWGEMM_LIB=libbwgemm_next.so selects it."""
+read back with bw_trace_read); --next builds lib/libbwgemm_next.so, the library with the options built but not on by
+default (the K split over clusters of 2 to 8 blocks, the TMA-store epilogue), for A/B runs: BWGEMM_LIB=libbwgemm_next.so
+selects it.  (Stream-K over a part wave of pair tiles and swap-AB on SM pairs were measured slower and stay off; the
+host emulator still builds and checks them.)"""
 import os
 import shutil
 import subprocess
@@ -16,7 +17,7 @@ LIB_DIR = os.path.join(HERE, "lib")
 LIB = os.path.join(LIB_DIR, "libbwgemm.so")
 TRACE_LIB = os.path.join(LIB_DIR, "libbwgemm_trace.so")
 NEXT_LIB = os.path.join(LIB_DIR, "libbwgemm_next.so")
-NEXT_DEFINES = ["-DBW_KSPLIT=1", "-DBW_SK_PART_WAVE=1", "-DBW_PAIR_WIDE=1", "-DBW_SWAP_PAIR=1"]
+NEXT_DEFINES = ["-DBW_KSPLIT=1", "-DBW_EPI_TMA=1"]
 INCLUDE = os.path.join(ROOT, "include")
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

@@ -95,24 +95,35 @@
                                // not yet measured)
 #endif
 #ifndef BW_KSPLIT
-#define BW_KSPLIT 0            // swap-AB K cut over the blocks of a cluster: 0, halves on clusters of two, the second
-                               // block's sum added by the first (measured on the B200); 1, clusters of 2 to
-                               // BW_KSPLIT_MAX blocks, each summing the cluster's partials of its own run of the
-                               // accumulator's 16-column chunks (run on the host emulator; not yet measured)
+#define BW_KSPLIT 1            // swap-AB K cut over the blocks of a cluster: 1, clusters of 2 to BW_KSPLIT_MAX blocks,
+                               // each summing the cluster's partials of its own run of the accumulator's 16-column
+                               // chunks, the cluster size and tile width of the least estimated time (ksplit_cost;
+                               // measured against the halves: qkv_m128 -9 %, down_m128 -9 %, o_m16 -5 %); 0, halves
+                               // on clusters of two, the second block's sum added by the first
 #endif
 #ifndef BW_KSPLIT_MAX
 #define BW_KSPLIT_MAX 8        // BW_KSPLIT 1: the largest cluster (8, the portable limit)
 #endif
-// BW_KSPLIT 1's choice of cluster size and tile width: the estimated time of a call (plan.h, ksplit_cost)
+// BW_KSPLIT 1's choice of cluster size and tile width: the estimated time of a call (plan.h, ksplit_cost).  The five
+// constants were fitted to the times of every valid (cluster size, tile width) of the qkv, o and down weights at
+// M = 1 .. 128 on a B200 (back-to-back CUDA graphs): with them the rule's choice is within 1 % of the fastest on 13 of
+// the 18 shapes and within 4 % on all (0.55 % slower than the fastest on average).
 #ifndef BW_HBM_GBS
 #define BW_HBM_GBS 6450.0      // HBM copy bandwidth (measured on this pool's B200s)
 #endif
 #ifndef BW_SM_INGEST_GBS
-#define BW_SM_INGEST_GBS 80.0  // operand bytes one SM takes in from L2 per second (measured: the pair kernel's mainloop,
-                               // 32 KB per K-block in ~400 ns)
+#define BW_SM_INGEST_GBS 70.0  // operand bytes one swap-AB block takes in from L2 per second (fitted; the pair kernel's
+                               // mainloop measured ~80: 32 KB per K-block in ~400 ns)
 #endif
 #ifndef BW_DSMEM_GBS
-#define BW_DSMEM_GBS 100.0     // distributed-shared-memory bytes one SM sends per second (an estimate, not measured)
+#define BW_DSMEM_GBS 10.0      // bytes one block hands over to the others of its cluster per second (fitted: the whole
+                               // hand-over, st.async into their rings and the wait for it)
+#endif
+#ifndef BW_KS_BLOCK_US
+#define BW_KS_BLOCK_US 0.1     // per block of the grid (fitted: more blocks streaming the weights at once cost time)
+#endif
+#ifndef BW_KS_CLUSTER_US
+#define BW_KS_CLUSTER_US 0.5   // per block of a cluster beyond two (fitted: the larger clusters' longer hand-over)
 #endif
 #ifndef BW_EPI_TMA
 #define BW_EPI_TMA 0           // TILE / PAIR fp16 epilogue: each warp's 32 rows x 64 columns of C through a swizzled 4 KB
@@ -126,6 +137,12 @@
 #endif
 
 namespace bw {
+
+#ifdef BW_EMULATE
+// The host emulator's test knob (emu.cpp, bw_emu_set "force_ksplit"): c * 16 + wm restricts the BW_KSPLIT 1 choice to
+// that cluster size and tile width where they fit (0: the rule).  Not compiled into the library.
+inline int g_emu_force_ksplit = 0;
+#endif
 
 constexpr int kVariants = 8;
 inline const char* variant_name(int v)
@@ -188,9 +205,10 @@ inline bool plan_ksplit_fits(int bn, int wm, int c)
 
 // The estimated time (us) of a K-split plan with clusters of c blocks and tiles of 128 wm weight columns: the larger
 // of the weights' HBM time and the busiest block's operand intake (its K range of 128 wm weight columns and of the bn
-// tokens, both re-read per block), plus that block's hand-over of the chunks it does not own.  Every K-split plan
-// streams the weights once, so the intake decides between them where it exceeds the HBM time: at M = 128 the tokens
-// cost as much intake per block as the weights of a 128-column tile.
+// tokens, both re-read per block), plus that block's hand-over of the chunks it does not own, plus a cost per block of
+// the grid and per block of a cluster beyond two.  Every K-split plan streams the weights once, so the intake decides
+// between them where it exceeds the HBM time: at M = 128 the tokens cost as much intake per block as the weights of a
+// 128-column tile.
 inline double ksplit_cost(int M, int N, int K, int bn, int wm, int c)
 {
     const double kb = (double)((K / 64 + c - 1) / c);                      // the longest K range, in K-blocks
@@ -198,8 +216,10 @@ inline double ksplit_cost(int M, int N, int K, int bn, int wm, int c)
     const double hbm = ((double)N * K + (double)M * K + (double)M * N) * 2;  // bytes from / to HBM
     const int chunks = bn * wm / 16;
     const double sent = (double)(chunks - chunks / c) * 8192;               // the busiest sender's pieces
+    const int blocks = (N + 128 * wm - 1) / (128 * wm) * c;
     const double t_hbm = hbm / (BW_HBM_GBS * 1e3), t_in = intake / (BW_SM_INGEST_GBS * 1e3);
-    return (t_hbm > t_in ? t_hbm : t_in) + sent / (BW_DSMEM_GBS * 1e3);
+    return (t_hbm > t_in ? t_hbm : t_in) + sent / (BW_DSMEM_GBS * 1e3) + BW_KS_BLOCK_US * blocks +
+           BW_KS_CLUSTER_US * (c - 2);
 }
 
 // The shapes the library serves: N and K multiples of 64 (the TMA boxes' widths), any M >= 1.  Rows of A past M
@@ -307,9 +327,8 @@ inline int make_plan(int M, int N, int K, int sms, int pairs, int variant, bw_pl
     // swap-AB with every tile at once on clusters of blocks, each block one equal K range of its tile, the blocks'
     // sums added through distributed shared memory (no partials in memory, no counters).  BW_KSPLIT 0: clusters of
     // two, tiles of 128 weight columns if they all fit at once, else of 256 (two MMAs on each stage of A) if those do.
-    // BW_KSPLIT 1: clusters of c = 2 .. BW_KSPLIT_MAX, the (c, tile width) of the least estimated time (ksplit_cost),
-    // one within 1 % of another going to the smaller c (fewer partials), then to the narrower tile; c > 2 wants 4
-    // K-blocks per block at least.
+    // BW_KSPLIT 1: clusters of c = 2 .. BW_KSPLIT_MAX, the (c, tile width) of the least estimated time (ksplit_cost;
+    // an exact tie goes to the smaller c, then to the narrower tile); c > 2 wants 4 K-blocks per block at least.
     const bool wide_ok = (variant == 0 || variant == 3) && !(flags & kPlanNarrow);
     const int tiles256 = (N + 255) / 256;
     int ks = 0, ks_wm = 0;
@@ -318,11 +337,14 @@ inline int make_plan(int M, int N, int K, int sms, int pairs, int variant, bw_pl
         double best = 0.0;
         for (int c = 2; c <= BW_KSPLIT_MAX && c <= 8; ++c) {
             for (int wm = 1; wm <= (wide_ok ? 2 : 1); ++wm) {
+#ifdef BW_EMULATE
+                if (g_emu_force_ksplit && (c != g_emu_force_ksplit / 16 || wm != g_emu_force_ksplit % 16)) continue;
+#endif
                 const int tiles = (N + 128 * wm - 1) / (128 * wm);
                 const int at_once = held ? held[c] : (c == 2 && pairs > 0) ? pairs : sms / c;
                 if (tiles > at_once || (c > 2 && q.kblocks < 4 * c) || !plan_ksplit_fits(q.bn, wm, c)) continue;
                 const double t = ksplit_cost(M, N, K, q.bn, wm, c);
-                if (!ks || t < 0.99 * best) {
+                if (!ks || t < best) {
                     best = t;
                     ks = c;
                     ks_wm = wm;

@@ -253,7 +253,8 @@ int dispatch(const bw_plan& q, const CUtensorMap& mx, const CUtensorMap& my, con
 // after this long), "cluster_batch" (clusters run at once; 0: as many as the host's cores take), "noalloc_cap"
 // (>= 0: fp16 calls of variant 0 plan as bw_gemm_f16_noalloc does, its array this many bytes; -1: the rule),
 // "ld_delay_us" (a random pause of up to this long before each tensor-memory load), "start_jitter_us" (each block starts
-// up to this much later), "engine_delay_us" (the asynchronous units' longest delay).  Returns 0, or -1 for an unknown
+// up to this much later), "engine_delay_us" (the asynchronous units' longest delay), "force_ksplit" (c * 16 + wm: the K
+// split takes clusters of c and tiles of 128 wm columns where they fit; 0: the rule).  Returns 0, or -1 for an unknown
 // name.
 extern "C" __attribute__((visibility("default"))) int bw_emu_set(const char* name, long long value)
 {
@@ -267,6 +268,7 @@ extern "C" __attribute__((visibility("default"))) int bw_emu_set(const char* nam
     else if (n == "ld_delay_us") g_ld_delay_us = (int)value;
     else if (n == "start_jitter_us") g_start_jitter_us = (int)value;
     else if (n == "engine_delay_us") g_engine_delay_us = (int)value;
+    else if (n == "force_ksplit") bw::g_emu_force_ksplit = (int)value;
     else return -1;
     return 0;
 }

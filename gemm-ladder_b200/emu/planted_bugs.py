@@ -17,8 +17,8 @@ every one of its mutations reported, the unmodified copy clean).
 
     python gemm-ladder_b200/emu/planted_bugs.py [--jobs 8] [--only name,...] [--list] [--out FILE]
 
-Each mutation names the build it needs ("library": the kernel as the library builds it; "next": with the options built
-for A/B runs, build.py --next), so that code compiled only there is mutated where it runs.
+Each mutation names the build it needs ("library": the kernel as the library builds it; the others: BUILDS, below), so
+that code compiled only there is mutated where it runs.
 """
 import argparse
 import concurrent.futures
@@ -37,7 +37,10 @@ ROOT = os.path.dirname(PKG)
 CUDA_INCLUDE = os.path.join(os.environ.get("CUDA_HOME", "/usr/local/cuda"), "include")
 BUILDS = {
     "library": (),
-    "next": ("BW_KSPLIT=1", "BW_SK_PART_WAVE=1", "BW_PAIR_WIDE=1", "BW_SWAP_PAIR=1"),
+    # the options built but off by default (stream-K over a part wave of pair tiles, swap-AB on SM pairs)
+    "next": ("BW_SK_PART_WAVE=1", "BW_SWAP_PAIR=1"),
+    # the swap-AB K halves on clusters of two (BW_KSPLIT 0, the rule's form before the K split over 2 to 8 blocks)
+    "halves": ("BW_KSPLIT=0",),
     # the 256 x 512 pair tile wherever the rule allows it, so that small emulated shapes run the wide kernel
     "wide": ("BW_PAIR_WIDE=1", "BW_PAIR_WIDE_KB_NS=1", "BW_PAIR_WIDE_EPI_NS=0", "BW_FIXUP_KB=0"),
     # the TMA-store epilogue
@@ -156,7 +159,9 @@ MUTATIONS = [
     ("epi_lines_column", GK, "store_rows64<EPI == kEpiF32 ? kEpiF32 : kEpiF16>(p, m0 + q * 32, n0 + c0, lane, v);",
      "store_rows64<EPI == kEpiF32 ? kEpiF32 : kEpiF16>(p, m0 + q * 32, n0, lane, v);", 0, "library"),
     ("epi_lines_order", GK, "for (int j = 0; j < 64; ++j) v[j] = __uint_as_float(r[j / 16][j % 16]);",
-     "for (int j = 0; j < 64; ++j) v[j] = __uint_as_float(r[j % 4][j / 4]);", 0, "library"),
+     "for (int j = 0; j < 64; ++j) v[j] = __uint_as_float(r[j % 4][j / 4]);", 1, "library"),
+    ("tma_lines_order", GK, "for (int j = 0; j < 64; ++j) v[j] = __uint_as_float(r[j / 16][j % 16]);",
+     "for (int j = 0; j < 64; ++j) v[j] = __uint_as_float(r[j % 4][j / 4]);", 0, "tma"),
     ("epi_chunk_column", GK, "store_chunk<SWAP, EPI, BN>(p, m0, n0, row, c0 + 16 * h, v, cst);",
      "store_chunk<SWAP, EPI, BN>(p, m0, n0, row, c0, v, cst);", 0, "library"),
     ("epi_swiglu_up_half", GK, "tmem_ld16(tbase + (uint32_t)(BN / 2 + c0), ur);", "tmem_ld16(tbase + (uint32_t)(c0), ur);", 0,
@@ -187,19 +192,19 @@ MUTATIONS = [
     ("split_bulk_not_last_slow", GK, "if (last_seg && f.nseg <= G::kMaxSum)", "if (f.nseg <= G::kMaxSum)", 1, "library"),
     # ---------------------------------------------------------------- K halves on clusters of two (swap-AB)
     ("khalf_expect_half", GK, "mbar_arrive_expect_tx(krecv, 128u * AN * 4u);", "mbar_arrive_expect_tx(krecv, 128u * AN * 2u);",
-     0, "library"),
+     0, "halves"),
     ("khalf_go_to_self", GK, "mbar_arrive_cluster(mapa_shared(smem_u32(kgo), 1));  // the ring may take the other sum now",
-     "mbar_arrive_cluster(mapa_shared(smem_u32(kgo), 0));", 0, "library"),
+     "mbar_arrive_cluster(mapa_shared(smem_u32(kgo), 0));", 0, "halves"),
     ("khalf_recv_wait_gone", GK, "const bool ok = wait_bounded(krecv, 0, abort_flag, p.wait_ns, site(2, 5, 0), seg);\n                        if (!ok) wait_drain(krecv, 0, p.wait_ns);  // st.async",
-     "const bool ok = true;\n                        if (!ok) wait_drain(krecv, 0, p.wait_ns);  // st.async", 0, "library"),
+     "const bool ok = true;\n                        if (!ok) wait_drain(krecv, 0, p.wait_ns);  // st.async", 0, "halves"),
     ("khalf_other_half_dropped", GK, "v[4 * j] = __uint_as_float(r[4 * j]) + w.x;", "v[4 * j] = __uint_as_float(r[4 * j]);",
-     0, "library"),
+     0, "halves"),
     ("khalf_send_stride", GK, "st_async_v4(dst + (uint32_t)((c0 / 4 + j) * 128 * 16), r[4 * j], r[4 * j + 1],",
-     "st_async_v4(dst + (uint32_t)((c0 / 4 + j) * 128 * 8), r[4 * j], r[4 * j + 1],", 0, "library"),
+     "st_async_v4(dst + (uint32_t)((c0 / 4 + j) * 128 * 8), r[4 * j], r[4 * j + 1],", 0, "halves"),
     ("khalf_peer_row", GK, "const float4* peer = reinterpret_cast<const float4*>(smem) + row;  // [col / 4][row][4]",
-     "const float4* peer = reinterpret_cast<const float4*>(smem) + (row ^ 1);", 0, "library"),
+     "const float4* peer = reinterpret_cast<const float4*>(smem) + (row ^ 1);", 0, "halves"),
     ("khalf_send_before_go", GK, "const bool ok = wait_bounded(kgo, 0, abort_flag, p.wait_ns, site(2, 6, 0), seg);\n                        if (ok) fence_acq_rel_cluster();  // after the first block's arrival",
-     "const bool ok = true;\n                        if (ok) fence_acq_rel_cluster();  // after the first block's arrival", 0, "library"),
+     "const bool ok = true;\n                        if (ok) fence_acq_rel_cluster();  // after the first block's arrival", 0, "halves"),
     # ---------------------------------------------------------------- descriptors and loads (kernel_common.cuh)
     ("desc_kmajor_k_step", KC, "smem_desc_sw128(tile + 32u * k, 16u, 1024u)", "smem_desc_sw128(tile + 16u * k, 16u, 1024u)", 0,
      "library"),
@@ -295,13 +300,13 @@ MUTATIONS = [
     ("plan_sk_tiles", PL, "q.sk_tiles = q.tiles - q.dp_tiles;", "q.sk_tiles = q.tiles - q.dp_tiles - 1;", 0, "library"),
     # ---------------------------------------------------------------- options of the next build
     ("ksplit_recv_bytes", GK, "const uint32_t recv_bytes = (uint32_t)((kc - 1) * (own1 - own0)) * 8192u;",
-     "const uint32_t recv_bytes = (uint32_t)((kc - 1) * (own1 - own0)) * 4096u;", 0, "next"),
+     "const uint32_t recv_bytes = (uint32_t)((kc - 1) * (own1 - own0)) * 4096u;", 0, "library"),
     ("ksplit_piece", GK, "const int piece = (kr < o ? kr : kr - 1) * len + (ch - r0);", "const int piece = (kr < o ? kr : kr - 1) * len;",
-     0, "next"),
+     0, "library"),
     ("ksplit_sum_order", GK, "const float4* src = ring + (size_t)((sb < kr ? sb : sb - 1) * (own1 - own0) +",
-     "const float4* src = ring + (size_t)((sb < kr ? sb : sb) * (own1 - own0) +", 0, "next"),
+     "const float4* src = ring + (size_t)((sb < kr ? sb : sb) * (own1 - own0) +", 0, "library"),
     ("ksplit_owner_run", SC, "BW_HD inline int ksplit_run(int o, int n, int c) { return o * n / c; }",
-     "BW_HD inline int ksplit_run(int o, int n, int c) { return o * n / c + (o == 1); }", 0, "next"),
+     "BW_HD inline int ksplit_run(int o, int n, int c) { return o * n / c + (o == 1); }", 0, "library"),
     ("wide_first_half_early", GK, "if (G::kHalves && c0 + kLdw == AN / 2) release_acc(0);  // the first half is read",
      "if (G::kHalves && c0 == 0) release_acc(0);", 0, "wide"),
     ("wide_catch_up_k", GK, "issue(st, held_kb + i, 1, 2);", "issue(st, held_kb, 1, 2);", 0, "wide"),
@@ -328,7 +333,8 @@ MUTATIONS = [
 ]
 
 # The calls each build's mutants run, in order; a mutant stops at its first reported call.  (M, N, K, emulated SMs,
-# variant, epi: 0 fp16 / 1 fp32 / 2 SwiGLU, B as N x K)
+# variant, epi: 0 fp16 / 1 fp32 / 2 SwiGLU, B as N x K[, the K split forced to clusters of c and tiles of 128 wm
+# columns: c * 16 + wm])
 CASES = {
     "library": [
         (256, 256, 128, 8, 0, 0, False),    # one pair tile
@@ -354,6 +360,13 @@ CASES = {
         (256, 512, 256, 8, 1, 0, False),    # whole pair tiles only
         (2304, 512, 128, 8, 0, 0, False),   # nine rows of pair tiles: a second, reversed serpentine group
         (512, 2560, 4096, 16, 0, 0, False), # four two-way split tiles, each pair's unit before its whole tiles
+        (512, 256, 4096, 8, 0, 0, False),   # two two-way split tiles, no whole tiles: the reductions by bulk copies
+        (256, 1280, 8192, 16, 0, 0, False), # five three-way split tiles, 15 units on 8 pairs
+        (128, 1024, 1024, 8, 0, 0, False),  # the K split over clusters of 2 to 8 (the rule's, then forced sizes)
+        (96, 640, 1024, 16, 0, 0, False, 3 * 16 + 1),
+        (64, 704, 1024, 16, 0, 0, False, 4 * 16 + 2),
+        (112, 256, 4096, 16, 0, 0, False, 8 * 16 + 1),
+        (96, 448, 2624, 16, 0, 0, True, 7 * 16 + 2),
         (16, 256, 2048, 8, 0, 0, False),    # K halves deeper than the stage ring
         (256, 512, 1024, 8, 5, 0, False),   # single-SM tiles deeper than the stage ring
         (64, 2304, 1024, 8, 0, 0, False),   # swap-AB stream-K, 256-column tiles, several tiles per block
@@ -362,15 +375,19 @@ CASES = {
         (300, 1280, 4096, 8, 0, 1, False),  # fp32 output, ragged rows, a split-K tail
     ],
     "next": [
-        (16, 1280, 256, 8, 0, 0, False),    # the K split over clusters of 2 to 8
-        (128, 1024, 1024, 8, 0, 0, False),
-        (96, 448, 320, 8, 0, 0, False),
-        (16, 1024, 2048, 16, 0, 0, False),
         (48, 2304, 256, 8, 0, 0, False),    # swap-AB on SM pairs (stream-K swap shapes from 33 tokens)
         (80, 2304, 256, 8, 0, 0, False),
         (128, 4096, 256, 8, 0, 0, False),
         (16, 1280, 256, 8, 0, 0, True),
         (80, 2304, 256, 8, 0, 0, True),
+    ],
+    "halves": [
+        (16, 256, 128, 8, 0, 0, False),     # K halves on a cluster of two
+        (16, 256, 2048, 8, 0, 0, False),    # deeper than the stage ring
+        (16, 1024, 384, 8, 0, 0, False),    # 256-column tiles
+        (96, 448, 320, 8, 0, 0, False),     # bn 96, odd K-blocks
+        (1, 256, 128, 8, 0, 0, False),      # one token
+        (16, 256, 128, 8, 0, 0, True),      # B as N x K
     ],
     "tma": [
         (256, 256, 128, 8, 0, 0, False),    # one pair tile
@@ -488,7 +505,9 @@ def check(lib_path, build_name, cluster_batch):
     def report(why):
         print(json.dumps({"reported": True, "why": why}), flush=True)
 
-    for M, N, K, sms, variant, epi, tn in CASES[build_name]:
+    for case in CASES[build_name]:
+        M, N, K, sms, variant, epi, tn = case[:7]
+        L.bw_emu_set(b"force_ksplit", case[7] if len(case) > 7 else 0)
         tag = f"{M}x{N}x{K} on {sms} SMs, v{variant}, epi {epi}{', B as N x K' if tn else ''}"
         A, B = oracle.lcg_inputs(M, N, K)
         ref = oracle.gemm_f64(A, B)

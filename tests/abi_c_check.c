@@ -23,9 +23,9 @@ int main(void)
     /* the rule, host only: BASELINE config 1 on 148 SMs takes SM-pair tiles of 256 x 512 (198 tiles, 2.7 waves) */
     CHECK(bw_gemm_plan(4608, 5632, 8192, 148, 0, &p) == BW_OK);
     CHECK(p.kernel == BW_KERNEL_PAIR && p.bn == 512 && p.tiles == 18 * 11 && p.kblocks == 128);
-    /* M = 16: swap-AB, K halves on clusters of two */
+    /* M = 16: swap-AB, 256-column tiles with their K cut in three on clusters of three SMs */
     CHECK(bw_gemm_plan(16, 8192, 8192, 148, 0, &p) == BW_OK);
-    CHECK(p.kernel == BW_KERNEL_SWAP && p.bn == 16 && p.ksplit == 2 && p.grid == 128);
+    CHECK(p.kernel == BW_KERNEL_SWAP && p.bn == 16 && p.ksplit == 3 && p.wm == 2 && p.grid == 96);
     /* any M >= 1 (M = 1: the tokens rounded up to 16 inside the kernel); N % 64, K % 64 and bad arguments refused
      * before any GPU work */
     CHECK(bw_gemm_plan(1, 8192, 8192, 148, 0, &p) == BW_OK && p.kernel == BW_KERNEL_SWAP && p.bn == 16);

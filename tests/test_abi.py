@@ -65,12 +65,14 @@ def test_wait_selftest_without_a_gpu_reports_a_failure_not_a_timeout():
 
 
 def test_plan_rule_on_the_judge_shapes():
+    ksplit = {"qkv_m16": (3, 2), "qkv_m128": (3, 2), "o_m16": (3, 2), "o_m128": (2, 1), "down_m16": (3, 2),
+              "down_m128": (4, 2)}  # (cluster size, 128-column weight blocks per tile): ksplit_cost's choices
     for name, M, N, K in JUDGE_B200:
         p = bwgemm.plan(M, N, K, sms=148)
-        if M <= 128 and -(-N // 256) <= 74:  # every tile's K halves at once on clusters of two SMs
-            wm = 1 if -(-N // 128) <= 74 else 2  # tiles of 128 weight columns if they fit, else of 256
-            assert p["kernel"] == bwgemm.BW_KERNEL_SWAP and p["bn"] == M and p["ksplit"] == 2 and p["wm"] == wm
-            assert p["grid"] == 2 * p["tiles"] and p["splits"] == 2 and p["workspace_bytes"] == 0
+        if name in ksplit:  # every tile's K ranges at once on clusters of c SMs, the sums added through DSMEM
+            c, wm = ksplit[name]
+            assert p["kernel"] == bwgemm.BW_KERNEL_SWAP and p["bn"] == M and p["ksplit"] == c and p["wm"] == wm
+            assert p["grid"] == c * p["tiles"] <= 148 and p["splits"] == c and p["workspace_bytes"] == 0
             assert p["counters"] == 0 and p["tiles"] == -(-N // (128 * wm))
         elif M <= 128:  # stream-K; tiles of 256 weight columns from 64 tokens while they outnumber the SMs
             wm = 2 if M >= 64 and -(-N // 256) >= 148 else 1

@@ -21,13 +21,17 @@ PKG = os.path.join(ROOT, "gemm-ladder_b200")
 CUDA_INCLUDE = os.path.join(os.environ.get("CUDA_HOME", "/usr/local/cuda"), "include")
 
 
-# The emulator's builds, by name: the kernel as the library builds it, the options not yet measured (build.py --next),
-# part-wave stream-K alone, and the 256 x 512 pair tile forced wherever the rule allows it.
+# The emulator's builds, by name: the kernel as the library builds it; the options built but off by default (stream-K
+# over a part wave of pair tiles and swap-AB on SM pairs, both measured slower, and the TMA-store epilogue); the swap-AB
+# K split in halves on clusters of two (the rule before the K split over clusters of 2 to 8); part-wave stream-K alone;
+# the 256 x 512 pair tile forced wherever the rule allows it; the TMA-store epilogue alone.
 BUILDS = {
     "library": (),
-    "next": ("BW_KSPLIT=1", "BW_SK_PART_WAVE=1", "BW_PAIR_WIDE=1", "BW_SWAP_PAIR=1"),
-    "part": ("BW_SK_PART_WAVE=1",),
+    "next": ("BW_SK_PART_WAVE=1", "BW_SWAP_PAIR=1", "BW_EPI_TMA=1"),
+    "halves": ("BW_KSPLIT=0",),
+    "part": ("BW_SK_PART_WAVE=1", "BW_PAIR_WIDE=0"),
     "wide": ("BW_PAIR_WIDE=1", "BW_PAIR_WIDE_KB_NS=1", "BW_PAIR_WIDE_EPI_NS=0", "BW_FIXUP_KB=0"),
+    "tma": ("BW_EPI_TMA=1",),
 }
 
 
@@ -73,9 +77,9 @@ def emu(emu_builds):
 
 @pytest.fixture(scope="module")
 def emu_next(emu_builds):
-    """The kernel and rule with the options built but not yet measured on a B200 (build.py --next): the K split over
-    clusters of 2 to 8 blocks (BW_KSPLIT 1), stream-K over a part wave of pair tiles (BW_SK_PART_WAVE 1), pair tiles of
-    256 x 512 (BW_PAIR_WIDE 1), swap-AB on SM pairs (BW_SWAP_PAIR 1)."""
+    """The kernel and rule with the options built but off by default: stream-K over a part wave of pair tiles
+    (BW_SK_PART_WAVE 1) and swap-AB on SM pairs (BW_SWAP_PAIR 1), both measured slower on a B200, and the TMA-store
+    epilogue (BW_EPI_TMA 1)."""
     return emu_builds["next"]
 
 
@@ -147,6 +151,30 @@ def test_every_plan_form_on_the_emulator(emu, oracle_mod, form, tn):
     assert status[0] == 0 and dirty == 0, (status, dirty)
     r = oracle_mod.check(C, oracle_mod.gemm_f64(A, B), K)
     assert r["nonfinite"] == 0 and r["violations"] == 0 and r["normwise"] <= 2e-3, r
+
+
+@pytest.mark.parametrize("form", [f for f in FORMS if f[0] > 128] + [(300, 1280, 4096, 8, ""), (512, 2048, 128, 8, "")],
+                         ids=lambda f: f"{f[0]}x{f[1]}x{f[2]}")
+@pytest.mark.parametrize("tn", [False, True], ids=["KxN", "NxK"])
+def test_tma_store_epilogue(emu_builds, oracle_mod, form, tn):
+    """BW_EPI_TMA 1: the fp16 TILE / PAIR epilogue stores C by TMA from a swizzled staging buffer (two buffers,
+    alternating by chunk, each store's read waited for before its buffer is rewritten), on every pair-tile form and the
+    single-SM variants; ragged rows clipped by the map, none written past M.  A slow epilogue (random pauses before the
+    tensor-memory loads) and the TMA engine's own delays vary the timing."""
+    L = emu_builds["tma"]
+    M, N, K, sms, _ = form
+    A, B = oracle_mod.lcg_inputs(M, N, K)
+    ref = oracle_mod.gemm_f64(A, B)
+    L.bw_emu_set(b"ld_delay_us", 10)
+    try:
+        for variant in (0, 5, 6):
+            rc, C, status, dirty, nf, msg = emulate(L, A, B, M, N, K, sms, variant=variant, tn=tn)
+            assert rc == 0 and nf == 0, f"v{variant}: rc {rc}, {nf} findings, first: {msg}"
+            assert status[0] == 0 and dirty == 0, (status, dirty)
+            r = oracle_mod.check(C, ref, K)
+            assert r["nonfinite"] == 0 and r["violations"] == 0 and r["normwise"] <= 2e-3, (variant, r)
+    finally:
+        L.bw_emu_set(b"ld_delay_us", 0)
 
 
 # M not a multiple of 16 (the library serves any M >= 1): decode steps of 1 and 8 tokens, ragged last tiles
@@ -224,7 +252,8 @@ def test_a_stalled_pipeline_ends_with_a_status_not_a_hang(emu, shape, drop):
     assert status[0] == 3 and (role, kind) in ((1, 0), (2, 2), (0, 1)), status
 
 
-# (M, N, K, emulated SMs, cluster size and tile width the BW_KSPLIT 1 rule takes there)
+# (M, N, K, emulated SMs, cluster size and tile width, forced through the emulator's "force_ksplit" knob so that every
+# cluster size and ownership pattern runs whatever the rule's cost model prefers)
 KSPLIT_FORMS = [
     (128, 512, 256, 8, 2, 1),    # bn 128: 8 chunks, 4 owned by each block, each receives the other's 4
     (16, 1280, 1024, 16, 3, 2),  # 2 chunks over 3 blocks: one block owns none (sends only)
@@ -241,39 +270,60 @@ KSPLIT_FORMS = [
 
 @pytest.mark.parametrize("form", KSPLIT_FORMS, ids=lambda f: f"{f[0]}x{f[1]}x{f[2]}_c{f[4]}")
 @pytest.mark.parametrize("tn", [False, True], ids=["KxN", "NxK"])
-def test_k_split_over_clusters_of_2_to_8(emu_next, oracle_mod, form, tn):
+def test_k_split_over_clusters_of_2_to_8(emu, oracle_mod, form, tn):
     """BW_KSPLIT 1: each tile's K over a cluster of c blocks, every block summing its own run of the accumulator's
     chunks from the others' pieces in its idle ring."""
     M, N, K, sms, c, wm = form
-    q = plan_of(emu_next, M, N, K, sms)
-    assert (q["ksplit"], q["wm"], q["grid"]) == (c, wm, c * q["tiles"]), q
-    A, B = oracle_mod.lcg_inputs(M, N, K)
-    rc, C, status, dirty, nf, msg = emulate(emu_next, A, B, M, N, K, sms, tn=tn)
+    emu.bw_emu_set(b"force_ksplit", c * 16 + wm)
+    try:
+        q = plan_of(emu, M, N, K, sms)
+        assert (q["ksplit"], q["wm"], q["grid"]) == (c, wm, c * q["tiles"]), q
+        A, B = oracle_mod.lcg_inputs(M, N, K)
+        rc, C, status, dirty, nf, msg = emulate(emu, A, B, M, N, K, sms, tn=tn)
+    finally:
+        emu.bw_emu_set(b"force_ksplit", 0)
     assert rc == 0 and nf == 0, f"rc {rc}, {nf} findings, first: {msg}"
     assert status[0] == 0 and dirty == 0, (status, dirty)
     r = oracle_mod.check(C, oracle_mod.gemm_f64(A, B), K)
     assert r["nonfinite"] == 0 and r["violations"] == 0 and r["normwise"] <= 2e-3, r
 
 
-def test_k_split_in_halves_is_the_same_bits_either_way(emu, emu_next, oracle_mod):
-    """At c = 2 both protocols add block 0's sum and block 1's in that order: the same bits."""
+def test_k_split_in_halves_is_the_same_bits_either_way(emu, emu_builds, oracle_mod):
+    """At c = 2 both protocols (the K split over clusters of 2 to 8, and the halves of BW_KSPLIT 0) add block 0's sum
+    and block 1's in that order: the same bits."""
     M, N, K = 128, 512, 256
-    assert plan_of(emu, M, N, K, 8)["ksplit"] == 2 and plan_of(emu_next, M, N, K, 8)["ksplit"] == 2
+    halves = emu_builds["halves"]
+    assert plan_of(emu, M, N, K, 8)["ksplit"] == 2 and plan_of(halves, M, N, K, 8)["ksplit"] == 2
     A, B = oracle_mod.lcg_inputs(M, N, K)
-    C0 = emulate(emu, A, B, M, N, K, 8)[1]
-    C1 = emulate(emu_next, A, B, M, N, K, 8)[1]
+    C0 = emulate(halves, A, B, M, N, K, 8)[1]
+    C1 = emulate(emu, A, B, M, N, K, 8)[1]
     assert np.array_equal(C0, C1)
 
 
-@pytest.mark.parametrize("shape", [(16, 512, 2048), (96, 640, 1024)], ids=lambda s: "x".join(map(str, s)))
+@pytest.mark.parametrize("form", [f for f in FORMS if f[0] <= 128], ids=lambda f: f"{f[0]}x{f[1]}x{f[2]}")
+def test_k_halves_on_clusters_of_two(emu_builds, oracle_mod, form):
+    """BW_KSPLIT 0 (kept as a build option): the swap-AB K halves on clusters of two, the second block's sum added by
+    the first, on every swap-AB form."""
+    L = emu_builds["halves"]
+    M, N, K, sms, _ = form
+    A, B = oracle_mod.lcg_inputs(M, N, K)
+    rc, C, status, dirty, nf, msg = emulate(L, A, B, M, N, K, sms)
+    assert rc == 0 and nf == 0 and status[0] == 0 and dirty == 0, (rc, nf, msg, status, dirty)
+    r = oracle_mod.check(C, oracle_mod.gemm_f64(A, B), K)
+    assert r["nonfinite"] == 0 and r["violations"] == 0 and r["normwise"] <= 2e-3, r
+
+
+@pytest.mark.parametrize("shape", [(16, 512, 2048, 4 * 16 + 1), (96, 640, 1024, 3 * 16 + 1)],
+                         ids=lambda s: "x".join(map(str, s[:3])))
 @pytest.mark.parametrize("drop", [0, 5])
 def test_a_stalled_k_split_cluster_ends_with_a_status(emu_next, shape, drop):
     """A TMA completion that never arrives in one block of a K-split cluster: that block's MMA issuer (or its epilogue,
     waiting for the accumulator) gives up, the others give up on the go barrier or on their pieces, and every block
     leaves.  The status word keeps the first wait to give up."""
-    M, N, K = shape
+    M, N, K, force = shape
     A = np.full((M, K), 0x3C00, np.uint16)
     B = np.full((K, N), 0x3C00, np.uint16)
+    emu_next.bw_emu_set(b"force_ksplit", force)  # clusters of 4 and of 3
     emu_next.bw_emu_set(b"wait_ns", 300_000_000)
     emu_next.bw_emu_set(b"barrier_limit_ms", 30_000)
     emu_next.bw_emu_set(b"drop_tma", drop)
@@ -283,25 +333,27 @@ def test_a_stalled_k_split_cluster_ends_with_a_status(emu_next, shape, drop):
         emu_next.bw_emu_set(b"drop_tma", -1)
         emu_next.bw_emu_set(b"wait_ns", 60_000_000_000)
         emu_next.bw_emu_set(b"barrier_limit_ms", 120_000)
+        emu_next.bw_emu_set(b"force_ksplit", 0)
     assert rc == 0 and nf == 0, f"{nf} findings, first: {msg}"
     role, kind = status[1] >> 16, (status[1] >> 8) & 0xFF
     assert status[0] == 3 and (role, kind) in ((1, 0), (2, 2), (2, 5), (2, 6), (0, 1)), status
 
 
-def test_k_split_rule_on_the_judge_shapes(emu_next):
-    """BW_KSPLIT 1 on 148 SMs: the cluster size and tile width of the least estimated time.  qkv (40 tiles of 256
-    columns) on clusters of 3; at M = 128 the o and down shapes take 256-column tiles on clusters of 4, which halves
-    each block's intake of the tokens against 128-column tiles on pairs; at M = 16 the weights' HBM time decides and
-    pairs stay."""
-    from shapes import JUDGE_B200
-
-    want = {"qkv_m16": (3, 2), "qkv_m128": (3, 2), "o_m16": (2, 1), "o_m128": (4, 2), "down_m16": (2, 1),
-            "down_m128": (4, 2), "gateup_m16": (0, 1), "gateup_m128": (0, 2)}
-    for name, M, N, K in JUDGE_B200:
-        if M > 128:
-            continue
-        q = plan_of(emu_next, M, N, K, 148)
-        assert (q["ksplit"], q["wm"]) == want[name], (name, q)
+def test_k_split_rule_on_the_judge_shapes(emu):
+    """BW_KSPLIT 1 (the library's rule) on 148 SMs: the cluster size and tile width of the least estimated time
+    (ksplit_cost, fitted to the measured times of every valid choice), which the B200 measured fastest or within 4 %
+    of it: 256-column tiles on clusters of 3 for qkv (120 blocks) and for o and down up to 16 tokens (96 blocks);
+    128-column tiles on pairs for o from 32 tokens and down at 32; 256-column tiles on clusters of 4 for down from 64
+    tokens.  gateup's tiles outnumber the clusters: stream-K."""
+    want = {("qkv", m): (3, 2) for m in (1, 8, 16, 32, 64, 128)}
+    want.update({("o", m): (3, 2) if m <= 16 else (2, 1) for m in (1, 8, 16, 32, 64, 128)})
+    want.update({("down", m): (3, 2) if m <= 16 else (2, 1) if m == 32 else (4, 2) for m in (1, 8, 16, 32, 64, 128)})
+    want.update({("gateup", m): (0, 2 if m >= 64 else 1) for m in (1, 8, 16, 32, 64, 128)})
+    shapes = {"qkv": (10240, 8192), "o": (8192, 8192), "down": (8192, 28672), "gateup": (57344, 8192)}
+    for (name, M), (c, wm) in want.items():
+        N, K = shapes[name]
+        q = plan_of(emu, M, N, K, 148)
+        assert (q["ksplit"], q["wm"]) == (c, wm), (name, M, q)
         assert q["grid"] <= 148 and (q["ksplit"] == 0 or q["grid"] == q["ksplit"] * q["tiles"])
 
 
@@ -406,7 +458,7 @@ WIDE_FORMS = [
     (512, 1024, 512, 8, "2 x 2 tiles of 256 x 512 on 4 pairs, one wave"),
     (256, 2048, 256, 8, "1 x 4 wide tiles"),
     (768, 1536, 512, 8, "3 x 3 wide tiles: two waves and a part, the accumulator reused tile after tile"),
-    (384, 1280, 320, 8, "2 x 3 wide tiles, the last rows and 256 columns beyond C: stream-K over one wave and a part"),
+    (640, 1280, 320, 8, "3 x 3 wide tiles, the last rows and 256 columns beyond C: two waves and a split-K tail"),
 ]
 
 
@@ -418,6 +470,7 @@ def test_pair_tiles_of_512_columns(emu_wide, oracle_mod, form, tn):
     M, N, K, sms, _ = form
     q = plan_of(emu_wide, M, N, K, sms)
     assert q["kernel"] == 2 and q["bn"] == 512 and q["tmem_cols"] == 512, q
+    assert q["splits"] > 0 or q["sk_tiles"] == 0, q  # never stream-K on wide tiles
     A, B = oracle_mod.lcg_inputs(M, N, K)
     rc, C, status, dirty, nf, msg = emulate(emu_wide, A, B, M, N, K, sms, tn=tn)
     assert rc == 0 and nf == 0, f"rc {rc}, {nf} findings, first: {msg}"
@@ -531,7 +584,7 @@ def test_judge_shapes_at_full_size_on_an_emulated_b200(emu, emu_next, oracle_mod
     assert r["nonfinite"] == 0 and r["violations"] == 0 and r["normwise"] <= 2e-3, r
 
 
-@pytest.mark.parametrize("build", ["library", "next"])
+@pytest.mark.parametrize("build", ["library", "next", "halves"])
 def test_every_plan_has_a_kernel_instance(emu_builds, build):
     """Every plan the rule makes -- over M, N, K, SM counts, variants, outputs and both B layouts -- has tensor maps
     within the driver's limits and dispatches to a kernel instance whose geometry (stages, shared and tensor memory,
@@ -539,7 +592,7 @@ def test_every_plan_has_a_kernel_instance(emu_builds, build):
     L = emu_builds[build]
     L.bw_emu_check_plan.argtypes = [ctypes.c_int] * 7
     L.bw_emu_check_plan.restype = ctypes.c_int
-    Ms = list(range(16, 129, 16)) + [144, 256, 384, 512, 2048, 8192]
+    Ms = [1, 8, 24, 100] + list(range(16, 129, 16)) + [130, 144, 256, 384, 512, 2048, 8192]
     Ns = [64, 192, 256, 320, 1024, 2176, 5632, 8192, 10240, 28672, 57344]
     Ks = [64, 576, 8192, 28672]
     bad = []
@@ -720,22 +773,26 @@ def _calls(path, func, names):
 
 
 def test_the_emulator_makes_the_library_maps():
-    """The emulator's tensor maps (emu.cpp, make_maps) are the library's (bwgemm.cu, make_maps): the same maps, boxes
-    and B layouts, in the same branches, so the dry run's check of the driver's limits speaks for the library."""
+    """The emulator's tensor maps (emu.cpp, make_maps and make_c_map) are the library's (bwgemm.cu): the same maps,
+    boxes and B layouts, in the same branches, so the dry run's check of the driver's limits speaks for the library."""
     lib = _calls(os.path.join(PKG, "csrc", "bwgemm.cu"), "bool make_maps(const bw_plan& q", ["make_map", "make_map_blocks"])
     emu = _calls(os.path.join(PKG, "emu", "emu.cpp"), "void make_maps(const bw_plan& q", ["map2", "map_blocks"])
     rename = {"make_map": "map2", "make_map_blocks": "map_blocks"}
     assert len(lib) == 12
     assert [(rename[n], a) for n, a in lib] == emu
+    lib_c = _calls(os.path.join(PKG, "csrc", "bwgemm.cu"), "bool make_c_map(const bw_plan& q", ["make_map"])
+    emu_c = _calls(os.path.join(PKG, "emu", "emu.cpp"), "void make_c_map(const bw_plan& q", ["map2"])
+    assert len(lib_c) == 1 and [(rename[n], a) for n, a in lib_c] == emu_c
 
 
 def _random_cases(seed, n):
-    """Seeded random calls: M a multiple of 16 (ragged against the tiles), N of 64, K of 64, 2 to 16 SMs, any variant,
-    either B layout; sized so the oracle and the emulator finish each in well under a second."""
+    """Seeded random calls: any M from 1 to 384 (ragged against the tiles and the token groups of 16), N a multiple of
+    64, K of 64, 2 to 16 SMs, any variant, either B layout; sized so the oracle and the emulator finish each in well
+    under a second."""
     rng = np.random.default_rng(seed)
     out = []
     while len(out) < n:
-        M = int(rng.integers(1, 25)) * 16
+        M = int(rng.integers(1, 385))
         N = int(rng.integers(1, 21)) * 64
         K = int(rng.integers(1, 25)) * 64
         if M * N * K > 120_000_000:
@@ -745,7 +802,7 @@ def _random_cases(seed, n):
     return out
 
 
-@pytest.mark.parametrize("build", ["library", "next"])
+@pytest.mark.parametrize("build", ["library", "next", "halves"])
 def test_random_calls_on_the_emulator(emu_builds, oracle_mod, build):
     """24 seeded random calls per build (shapes, SM counts, variants, B layouts) against the fp64 oracle, with no
     finding, the status word clear and the counters at zero."""
