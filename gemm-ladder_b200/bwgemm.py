@@ -41,6 +41,7 @@ class Plan(ctypes.Structure):
         ("tmem_cols", ctypes.c_int),
         ("ksplit", ctypes.c_int),
         ("wm", ctypes.c_int),
+        ("dyn", ctypes.c_int),
     ]
 
     def as_dict(self):

@@ -343,6 +343,7 @@ Params make_params(const bw_plan& q, int M, int N, int K, void* C, float* work, 
     p.s.sk_iters = q.sk_iters;
     p.s.group_rows = q.group_rows;
     p.s.ksplit = q.ksplit;
+    p.s.dyn = q.dyn;
     p.C = C;
     p.work = work;
     p.counters = counters;

@@ -66,12 +66,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* rbar = drain + 1;  // the bulk reduction's copies of partials
     uint64_t* kgo = rbar + 1;    // K split: the other blocks' rings may take this block's sums
     uint64_t* krecv = rbar + 2;  // K split: the other blocks' sums for this block have arrived
+    uint64_t* uq_full = rbar + 3;             // s.dyn: the unit queue's entries, filled by the producer
+    uint64_t* uq_empty = uq_full + kPlanUnitQ;  // and read by the MMA issuer and the epilogue
     __half* cst = reinterpret_cast<__half*>(smem + G::kCStageOffset);  // swap-AB epilogue transpose buffers
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + G::kMiscOffset);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
     volatile int* reduce_flag = abort_flag + 1;
     volatile int* epi_go = abort_flag + 2;  // two slots, alternating by segment
     volatile int* recv_flag = abort_flag + 4;  // K split: the other blocks' parts arrived
+    volatile int* epi_unit = abort_flag + 5;   // s.dyn: two slots, alternating by segment, beside epi_go
+    volatile int* uq = abort_flag + 7;         // s.dyn: the unit queue (kPlanUnitQ entries; -1: no unit left)
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
@@ -96,6 +100,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         mbar_init(drain, 1);
         mbar_init(rbar, 1);
+        for (int i = 0; i < kPlanUnitQ; ++i) {
+            mbar_init(&uq_full[i], 1);   // the producer's arrival once the entry is written
+            mbar_init(&uq_empty[i], 2);  // the MMA issuer's and the epilogue's, once they have read it
+        }
         mbar_init(kgo, kp ? s.ksplit - 1 : 1);  // a remote arrival from each other block of the cluster
         mbar_init(krecv, 1);  // this block's arrive.expect_tx; the other blocks' st.async bytes complete it
         *abort_flag = 0;
@@ -136,10 +144,29 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint64_t pol_a = BW_HINT_A ? l2_policy(BW_HINT_A) : 0ull;
             const uint64_t pol_b = BW_HINT_B ? l2_policy(BW_HINT_B) : 0ull;
             const uint64_t pol_sb = BW_SWAP_HINT_B ? l2_policy(BW_SWAP_HINT_B) : 0ull;
-            int stage = 0, issued = 0, seg = 0;
+            int stage = 0, issued = 0, seg = 0, qi = 0;
             uint32_t ph = 0;
             bool ok = true;
-            while (ok && it.next(s, P, sg)) {
+            // s.dyn: the next unit from the call's counter, passed on through the queue (-1 once none is left)
+            auto next = [&](Seg& g) -> bool {
+                if (!s.dyn) return it.next(s, P, g);
+                const int qs = qi % kPlanUnitQ;
+                if (!wait_bounded(&uq_empty[qs], (uint32_t)((qi / kPlanUnitQ) & 1) ^ 1u, abort_flag, p.wait_ns,
+                                  site(0, 9, (uint32_t)qs), seg)) {
+                    ok = false;
+                    return false;
+                }
+                int u = atomicAdd(p.counters + s.sk_tiles * R, 1);
+                if (u >= s.sk_tiles * s.splits) u = -1;
+                uq[qs] = u;
+                mbar_arrive(&uq_full[qs]);  // release: the readers see the entry after their wait
+                ++qi;
+                if (u < 0) return false;
+                unit_seg(s, u, g.tile, g.k0, g.k1);
+                g.unit = u;
+                return true;
+            };
+            while (ok && next(sg)) {
                 int tm, tn;
                 if (SWAP) {
                     tm = 0;
@@ -221,13 +248,30 @@ __global__ void __launch_bounds__(kThreads, 1)
             const bool bk = p.tn != 0;
             SegIter it(s, c, P);
             Seg sg;
-            int stage = 0, acc = 0, seg = 0;
+            int stage = 0, acc = 0, seg = 0, qi = 0;
             uint32_t ph = 0, aph = 0;
             bool ok = true;
 #ifdef BW_TRACE
             unsigned long long w_full = 0, w_acc = 0, n_kb = 0;
 #endif
-            while (ok && it.next(s, P, sg)) {
+            // s.dyn: the producer's next unit from the queue
+            auto next = [&](Seg& g) -> bool {
+                if (!s.dyn) return it.next(s, P, g);
+                const int qs = qi % kPlanUnitQ;
+                if (!wait_bounded(&uq_full[qs], (uint32_t)((qi / kPlanUnitQ) & 1), abort_flag, p.wait_ns,
+                                  site(1, 9, (uint32_t)qs), seg)) {
+                    ok = false;
+                    return false;
+                }
+                const int u = uq[qs];
+                mbar_arrive(&uq_empty[qs]);
+                ++qi;
+                if (u < 0) return false;
+                unit_seg(s, u, g.tile, g.k0, g.k1);
+                g.unit = u;
+                return true;
+            };
+            while (ok && next(sg)) {
 #ifdef BW_TRACE
                 const unsigned long long ta0 = globaltimer_ns();
 #endif
@@ -356,7 +400,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t tempty_leader0 = PAIR ? mapa_shared(smem_u32(&tempty[0]), 0) : smem_u32(&tempty[0]);
         SegIter it(s, c, P);
         Seg sg;
-        int acc = 0, seg = 0;
+        int acc = 0, seg = 0, qi = 0;
         uint32_t aph = 0;
         unsigned epi_chunks = 0;  // BW_EPI_TMA: 64-column chunks this warp has stored (the staging buffer alternates)
         unsigned rs_acked = 0;  // kEpiRS: owners whose ack of the previous call this block has seen
@@ -385,13 +429,35 @@ __global__ void __launch_bounds__(kThreads, 1)
                 release_acc(a);
             }
         };
-        while (it.next(s, P, sg)) {
+        for (;;) {
+            if (!s.dyn && !it.next(s, P, sg)) break;
             // one thread waits (bounded); a named barrier hands its outcome to the other 127, so that an abort
-            // takes the whole group out together and no thread is left at a later barrier
-            if (threadIdx.x == kEpiThread0)
-                epi_go[seg & 1] = wait_bounded(&tfull[acc], aph, abort_flag, p.wait_ns, site(2, 2, acc), seg) ? 1 : 0;
+            // takes the whole group out together and no thread is left at a later barrier.  s.dyn: that thread first
+            // takes the segment's unit from the queue (go 2: none left)
+            if (threadIdx.x == kEpiThread0) {
+                int go = 1, u = 0;
+                if (s.dyn) {
+                    const int qs = qi % kPlanUnitQ;
+                    if (!wait_bounded(&uq_full[qs], (uint32_t)((qi / kPlanUnitQ) & 1), abort_flag, p.wait_ns,
+                                      site(2, 9, (uint32_t)qs), seg)) {
+                        go = 0;
+                    } else {
+                        u = uq[qs];
+                        mbar_arrive(&uq_empty[qs]);
+                        ++qi;
+                        if (u < 0) go = 2;
+                    }
+                }
+                if (go == 1) go = wait_bounded(&tfull[acc], aph, abort_flag, p.wait_ns, site(2, 2, acc), seg) ? 1 : 0;
+                epi_unit[seg & 1] = u;
+                epi_go[seg & 1] = go;
+            }
             named_bar_sync(1, 128);
-            if (!epi_go[seg & 1]) break;
+            if (epi_go[seg & 1] != 1) break;
+            if (s.dyn) {
+                sg.unit = epi_unit[seg & 1];
+                unit_seg(s, sg.unit, sg.tile, sg.k0, sg.k1);
+            }
             if (threadIdx.x == kEpiThread0) {
                 BW_TRACE_AT(6);  // the last segment's accumulator is ready (kept: overwritten per segment)
                 BW_TRACE_VAL(8, 0);
@@ -627,10 +693,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // part of a split tile
                 const Fixup f = fixup_of(s, c, P, sg);
                 int* counter = p.counters + (sg.tile - s.dp_tiles) * R + rank;
-                // this block's last segment: its stage ring is idle and can take the partials by bulk copy
+                // this block's last segment: its stage ring is idle and can take the partials by bulk copy (s.dyn:
+                // not known in advance, so never)
                 SegIter peek = it;
                 Seg nx;
-                const bool last_seg = !peek.next(s, P, nx);
+                const bool last_seg = !s.dyn && !peek.next(s, P, nx);
                 // every other partial already written: this block is the last; sum them with its own accumulator
                 // straight from tensor memory (no round trip of its own partial)
                 if (threadIdx.x == kEpiThread0) *reduce_flag = ld_acquire_gpu(counter) == f.nseg - 1 ? 2 : 0;
@@ -719,6 +786,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         cluster_sync();  // neither block leaves while the other may still read its memory or arrive on its barriers
     else
         __syncthreads();
+    if (s.dyn && threadIdx.x == 0) {
+        // this block's producer has taken its last unit: the call's last block to get here puts the counter of the
+        // next unit, and its own count, back to zero for the next call
+        int* next_unit = p.counters + s.sk_tiles * R;
+        __threadfence();
+        if (atomicAdd(next_unit + 1, 1) == (int)gridDim.x - 1) {
+            atomicExch(next_unit, 0);
+            atomicExch(next_unit + 1, 0);
+        }
+    }
     if (warp == 1) {
         __syncwarp();
         tc_fence_after();

@@ -102,14 +102,15 @@ struct Geom {
     static constexpr int kRingBytes = kStages * kStageBytes;
     static constexpr int kWindowOffset = kRingBytes;         // RSV bytes (kEpiRS: the owner's window)
     static constexpr int kBarOffset = kRingBytes + RSV;
-    static constexpr int kNumBars = 2 * kStages + 8;  // full, empty, tmem full x2, tmem empty x2, drain, reduce,
-                                                      // and the K split's go / receive
+    static constexpr int kNumBars = 2 * kStages + 8 + 2 * kPlanUnitQ;  // full, empty, tmem full x2, tmem empty x2,
+                                                                       // drain, reduce, the K split's go / receive,
+                                                                       // the unit queue's full and empty
     static constexpr int kSlotBytes = 128 * kAccN * 4;  // one partial of this block's rows
     static constexpr int kRingSlots = kRingBytes / kSlotBytes;  // partials the idle ring holds at once
     static constexpr int kMaxSum = kRingSlots + 1 < 8 ? kRingSlots + 1 : 8;  // partials the bulk reduction sums
     static constexpr int kMiscOffset = kBarOffset + kNumBars * 8;
     // swap-AB: the epilogue transposes each 16-column chunk through two 16 x 128 fp16 buffers
-    static constexpr int kCStageOffset = (kMiscOffset + 32 + 127) / 128 * 128;
+    static constexpr int kCStageOffset = (kMiscOffset + 64 + 127) / 128 * 128;
     static constexpr int kSmemBytes = 1024 + kCStageOffset + kCStageBytes;  // + slack to align the stages to 1024 B
     static_assert(BN % 16 == 0 && BN >= 16 && (BN <= 256 || (PAIR && BN == 512 && WM == 1)),
                   "MMA N: a multiple of 16 in [16, 256] (pair tiles of 512 columns: two MMAs of 256)");

@@ -131,6 +131,23 @@
                                // alternating by 64-column chunk) and one TMA store per warp and chunk, in place of
                                // whole-line stores from registers (0); the ring loses what the buffers take
 #endif
+#ifndef BW_DYN_UNITS
+#define BW_DYN_UNITS 1         // swap-AB shapes whose tiles outnumber the clusters (stream-K before): every tile cut in
+                               // units of BW_DYN_UNIT_KB K-blocks, each unit taken by whichever block asks next (the
+                               // producer's atomic on a counter in global memory), the partials summed in unit order by
+                               // the tile's last unit (the same bits whoever ran them).  Static stream-K shares left the
+                               // slowest tenth of the blocks 8-10 us behind the median at gateup_m16 (timeline)
+#endif
+#ifndef BW_DYN_UNIT_KB
+#define BW_DYN_UNIT_KB 16      // K-blocks per unit (a unit's MMAs take ~5 us at M = 16)
+#endif
+#ifndef BW_DYN_MAX_COLS
+#define BW_DYN_MAX_COLS 64     // only where the accumulator is at most this many columns (a unit's partial <= 32 KB)
+#endif
+#ifndef BW_DYN_MAX_BYTES
+#define BW_DYN_MAX_BYTES (32u << 20)  // the units' partials of a call at most this many bytes (longer units if need be;
+                                      // so that the no-allocation entry's array holds them too)
+#endif
 #ifndef BW_SK_ONE_WAVE
 #define BW_SK_ONE_WAVE 1       // stream-K over every tile when they make one full wave and part of another (the
                                // split-K tail's units then double a block's work: measured qkv_m512 -12 %)
@@ -168,6 +185,9 @@ inline int plan_cstage_bytes(bool swap) { return swap ? 2 * 16 * 128 * 2 : 0; }
 constexpr int kPlanRsWindowBytes = 2 * 32768;
 // The TMA-store epilogue's staging (BW_EPI_TMA): two buffers of 128 rows x 64 fp16 columns, after the stage ring.
 constexpr int kPlanEpiStageBytes = 2 * 16384;
+// Entries of a block's queue of units (BW_DYN_UNITS: its producer takes units and passes them to the MMA issuer and the
+// epilogue), each with a full and an empty barrier.
+constexpr int kPlanUnitQ = 4;
 inline int plan_stages(int bn, int ranks, bool swap, int wm = 1, int reserve = 0)
 {
     const int s = (BW_SMEM_LIMIT - 1024 - 512 - plan_cstage_bytes(swap) - reserve) / plan_stage_bytes(bn, ranks, wm);
@@ -184,8 +204,8 @@ inline int plan_tmem_cols(int acc_n)
 inline int plan_smem_bytes(int bn, int ranks, bool swap, int wm = 1, int reserve = 0)
 {
     const int st = plan_stages(bn, ranks, swap, wm, reserve);
-    const int misc = st * plan_stage_bytes(bn, ranks, wm) + reserve + (2 * st + 8) * 8;
-    const int cstage = (misc + 32 + 127) / 128 * 128;
+    const int misc = st * plan_stage_bytes(bn, ranks, wm) + reserve + (2 * st + 8 + 2 * kPlanUnitQ) * 8;
+    const int cstage = (misc + 64 + 127) / 128 * 128;
     return 1024 + cstage + plan_cstage_bytes(swap);
 }
 
@@ -393,8 +413,20 @@ inline int make_plan(int M, int N, int K, int sms, int pairs, int variant, bw_pl
         q.tiles_n = (N + 256 * q.wm - 1) / (256 * q.wm);
         q.tiles = q.tiles_n;
     }
+    // BW_DYN_UNITS: the swap-AB stream-K shapes with small accumulators as units of fixed K ranges, taken dynamically
+    const size_t dyn_split_bytes = (size_t)q.tiles * 128 * q.bn * q.wm * sizeof(float);  // one partial of every tile
+    int dyn_splits = (q.kblocks + BW_DYN_UNIT_KB - 1) / BW_DYN_UNIT_KB;
+    if ((size_t)dyn_splits * dyn_split_bytes > BW_DYN_MAX_BYTES) dyn_splits = (int)(BW_DYN_MAX_BYTES / dyn_split_bytes);
+    const bool dyn = BW_DYN_UNITS && swap && stream_k && q.kernel == BW_KERNEL_SWAP && (variant == 0 || variant == 3) &&
+                     q.bn * q.wm <= BW_DYN_MAX_COLS && dyn_splits >= 2 && q.tiles % units != 0 &&
+                     (!work_cap || dyn_splits * dyn_split_bytes <= work_cap);
     if (variant == 1 || q.tiles % units == 0) {
         q.dp_tiles = q.tiles;  // whole tiles only
+    } else if (dyn) {
+        q.dp_tiles = 0;
+        q.sk_tiles = q.tiles;
+        q.splits = dyn_splits;
+        q.dyn = 1;
     } else if (stream_k) {
         // stream-K: at M <= 128 over every tile; above, over the last full wave and the partial one
         const int waves = q.tiles / units;
@@ -436,7 +468,7 @@ inline int make_plan(int M, int N, int K, int sms, int pairs, int variant, bw_pl
     q.stages = plan_stages(q.bn, ranks, swap, q.wm, reserve);
     q.smem_bytes = plan_smem_bytes(q.bn, ranks, swap, q.wm, reserve);
     q.tmem_cols = plan_tmem_cols(q.bn * q.wm);
-    q.counters = q.sk_tiles * ranks;
+    q.counters = q.sk_tiles * ranks + (q.dyn ? 2 : 0);  // dyn: the next unit to take, the blocks that finished
     Sched sc = {};
     sc.sk_tiles = q.sk_tiles;
     sc.splits = q.splits;

@@ -41,7 +41,18 @@ struct Sched {
     int ksplit;           // > 0: each tile's K cut in ksplit ranges on the blocks of a cluster of ksplit (one
                           // segment per block); 0: none
     int row_shift;        // rows of tiles the order is rotated by (the fused reduce-scatter: a rank's own rows last)
+    int dyn;              // 1: the split-K units (every tile split, dp_tiles 0) go to whichever block asks next (a
+                          // counter in global memory, read by each block's producer), not round-robin
 };
+
+// The segment of split-K unit u (split-major: u = split * sk_tiles + tile - dp_tiles).
+BW_HD inline void unit_seg(const Sched& s, int u, int& tile, int& k0, int& k1)
+{
+    const int sp = u / s.sk_tiles, rel = u - sp * s.sk_tiles;
+    tile = s.dp_tiles + rel;
+    k0 = (int)((long long)sp * s.kblocks / s.splits);
+    k1 = (int)((long long)(sp + 1) * s.kblocks / s.splits);
+}
 
 // ------------------------------------------------------------------ stream-K bookkeeping
 BW_HD inline long long sk_begin(const Sched& s, int c, int P) { return s.sk_iters * c / P; }
@@ -107,10 +118,7 @@ struct SegIter {
         // of one segment runs while the MMAs of the next fill the other accumulator), not the end of the kernel
         if (s.splits > 0 && next_u < s.sk_tiles * s.splits) {
             const int u = next_u;
-            const int sp = u / s.sk_tiles, rel = u - sp * s.sk_tiles;
-            seg.tile = s.dp_tiles + rel;
-            seg.k0 = (int)((long long)sp * s.kblocks / s.splits);
-            seg.k1 = (int)((long long)(sp + 1) * s.kblocks / s.splits);
+            unit_seg(s, u, seg.tile, seg.k0, seg.k1);
             seg.unit = u;
             next_u += P;
             return true;

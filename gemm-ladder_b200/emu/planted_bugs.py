@@ -139,8 +139,8 @@ MUTATIONS = [
      "if (false)\n        cluster_sync();  // the leader's barriers exist", 0, "library"),
     # ---------------------------------------------------------------- the epilogue: accumulators and whole tiles
     ("epi_acc_wait_gone", GK,
-     "epi_go[seg & 1] = wait_bounded(&tfull[acc], aph, abort_flag, p.wait_ns, site(2, 2, acc), seg) ? 1 : 0;",
-     "epi_go[seg & 1] = 1;", 0, "library"),
+     "if (go == 1) go = wait_bounded(&tfull[acc], aph, abort_flag, p.wait_ns, site(2, 2, acc), seg) ? 1 : 0;",
+     "(void)aph;", 0, "library"),
     ("epi_acc_parity", GK, "wait_bounded(&tfull[acc], aph,", "wait_bounded(&tfull[acc], aph ^ 1u,", 0, "library"),
     ("epi_whole_tile_kept", GK, "                else\n                    release_acc(acc);\n",
      "                else\n                    (void)acc;\n", 0, "library"),
@@ -276,8 +276,6 @@ MUTATIONS = [
     ("sched_group_row", SC, "tm = g * s.group_rows + r % rows;", "tm = g * s.group_rows + r % rows / 2;", 0, "library"),
     ("sched_group_col", SC, "tn = r / rows;", "tn = r % rows;", 0, "library"),
     ("sched_reverse_off", SC, "if (g & 1) tn = s.tiles_n - 1 - tn;", "if (g & 1) tn = s.tiles_n - tn;", 0, "library"),
-    ("sched_split_k1", SC, "seg.k1 = (int)((long long)(sp + 1) * s.kblocks / s.splits);",
-     "seg.k1 = (int)((long long)(sp + 1) * s.kblocks / s.splits) - (sp == 0);", 0, "library"),
     ("sched_split_stride", SC, "next_u += P;", "next_u += P + 1;", 0, "library"),
     ("sched_dp_stride", SC, "next_dp += P;", "next_dp += 2 * P;", 0, "library"),
     ("sched_sk_last_kblock", SC, "seg.k1 = left < (long long)(s.kblocks - seg.k0) ? seg.k0 + (int)left : s.kblocks;",
@@ -314,6 +312,19 @@ MUTATIONS = [
      "const uint32_t yw = sy;", 0, "wide"),
     ("wide_catch_up_wait", GK, "if (!wait_bounded(&tempty[1], aph ^ 1u, abort_flag, p.wait_ns, site(1, 3, 1), seg)) return false;",
      "(void)0;", 0, "wide"),
+    # ---------------------------------------------------------------- dynamic units (BW_DYN_UNITS)
+    ("dyn_unit_overrun", GK, "if (u >= s.sk_tiles * s.splits) u = -1;", "if (u > s.sk_tiles * s.splits) u = -1;", 0,
+     "library"),
+    ("dyn_empty_count", GK, "mbar_init(&uq_empty[i], 2);", "mbar_init(&uq_empty[i], 1);", 0, "library"),
+    ("dyn_full_parity", GK, "if (!wait_bounded(&uq_full[qs], (uint32_t)((qi / kPlanUnitQ) & 1), abort_flag, p.wait_ns,\n                                  site(1, 9",
+     "if (!wait_bounded(&uq_full[qs], (uint32_t)((qi / kPlanUnitQ) & 1) ^ 1u, abort_flag, p.wait_ns,\n                                  site(1, 9", 0, "library"),
+    ("dyn_epi_slot", GK, "                sg.unit = epi_unit[seg & 1];", "                sg.unit = epi_unit[0];", 0,
+     "library"),
+    ("dyn_no_reset", GK, "            atomicExch(next_unit, 0);\n", "", 0, "library"),
+    ("dyn_last_seg", GK, "const bool last_seg = !s.dyn && !peek.next(s, P, nx);", "const bool last_seg = !peek.next(s, P, nx);",
+     0, "library"),
+    ("dyn_unit_k", SC, "    k1 = (int)((long long)(sp + 1) * s.kblocks / s.splits);\n}",
+     "    k1 = (int)((long long)(sp + 1) * s.kblocks / s.splits) - (sp == 0);\n}", 0, "library"),
     # ---------------------------------------------------------------- the TMA-store epilogue (BW_EPI_TMA)
     ("tma_no_read_wait", EP, "if (lane == 0) bulk_wait_read<1>();", "(void)0;", 0, "tma"),
     ("tma_one_buffer", GK, "(epi_chunks++ & 1u) * 16384u", "(epi_chunks++ & 0u) * 16384u", 0, "tma"),
@@ -362,6 +373,8 @@ CASES = {
         (512, 2560, 4096, 16, 0, 0, False), # four two-way split tiles, each pair's unit before its whole tiles
         (512, 256, 4096, 8, 0, 0, False),   # two two-way split tiles, no whole tiles: the reductions by bulk copies
         (256, 1280, 8192, 16, 0, 0, False), # five three-way split tiles, 15 units on 8 pairs
+        (16, 1280, 4096, 8, 0, 0, False),   # dynamic units: 10 tiles x 4 units on 8 blocks
+        (24, 3200, 2048, 16, 0, 0, True),   # dynamic units, bn 32, a half tile
         (128, 1024, 1024, 8, 0, 0, False),  # the K split over clusters of 2 to 8 (the rule's, then forced sizes)
         (96, 640, 1024, 16, 0, 0, False, 3 * 16 + 1),
         (64, 704, 1024, 16, 0, 0, False, 4 * 16 + 2),

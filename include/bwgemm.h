@@ -168,6 +168,8 @@ typedef struct bw_plan {
     int ksplit;          /* > 0: SWAP with each tile's K cut in ksplit ranges on the blocks of a cluster of ksplit
                             (grid = ksplit x tiles); 0: none */
     int wm;              /* SWAP: 128-column weight blocks per tile (1 or 2; 2 = two MMAs on each stage of A) */
+    int dyn;             /* 1: the split-K units (splits per tile, every tile split) go to whichever block asks next
+                            (a counter in global memory), their partials summed in unit order; 0: a static order */
 } bw_plan;
 
 /*
@@ -190,7 +192,8 @@ int bw_gemm_device_plan(int M, int N, int K, int variant, int noalloc, bw_plan* 
  * a bounded wait gave up since the last clear; *site = role << 16 | barrier kind << 8 | index of the first wait that
  * gave up, *block its block, *segment the segment that block was on.  Kinds: 0 a full stage, 1 an empty stage, 2 a
  * finished accumulator, 3 a free accumulator, 4 partials copied in, 5 and 6 a K-split cluster's pieces and go signal,
- * 7 another rank's partial of the fused reduce-scatter (index: the sender), 8 a rank's ack of the previous call.
+ * 7 another rank's partial of the fused reduce-scatter (index: the sender), 8 a rank's ack of the previous call, 9 an
+ * entry of the block's queue of units (a plan with dyn 1).
  * Returns a CUDA error as BW_ERR_LAUNCH.
  * No reference counterpart as a function: the reference traps in its guarded wait (hopper/step2.cuh:128-145); this
  * rung's waits return instead and leave the context usable.

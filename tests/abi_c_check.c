@@ -53,13 +53,13 @@ int main(void)
     }
     printf("bw_plan size %zu kernel %zu bn %zu stages %zu tiles_m %zu tiles_n %zu tiles %zu kblocks %zu grid %zu "
            "dp_tiles %zu sk_tiles %zu splits %zu sk_iters %zu group_rows %zu workspace_bytes %zu counters %zu "
-           "smem_bytes %zu tmem_cols %zu ksplit %zu wm %zu\n",
+           "smem_bytes %zu tmem_cols %zu ksplit %zu wm %zu dyn %zu\n",
            sizeof(bw_plan), offsetof(bw_plan, kernel), offsetof(bw_plan, bn), offsetof(bw_plan, stages),
            offsetof(bw_plan, tiles_m), offsetof(bw_plan, tiles_n), offsetof(bw_plan, tiles), offsetof(bw_plan, kblocks),
            offsetof(bw_plan, grid), offsetof(bw_plan, dp_tiles), offsetof(bw_plan, sk_tiles),
            offsetof(bw_plan, splits), offsetof(bw_plan, sk_iters), offsetof(bw_plan, group_rows),
            offsetof(bw_plan, workspace_bytes), offsetof(bw_plan, counters), offsetof(bw_plan, smem_bytes),
-           offsetof(bw_plan, tmem_cols), offsetof(bw_plan, ksplit), offsetof(bw_plan, wm));
+           offsetof(bw_plan, tmem_cols), offsetof(bw_plan, ksplit), offsetof(bw_plan, wm), offsetof(bw_plan, dyn));
     printf("OK\n");
     return 0;
 }

@@ -202,6 +202,68 @@ def test_ragged_m_on_the_emulator(emu_builds, oracle_mod, form, tn, build):
     assert r["nonfinite"] == 0 and r["violations"] == 0 and r["normwise"] <= 2e-3, r
 
 
+# swap-AB shapes whose tiles outnumber the clusters and whose accumulators are small: units of 16 K-blocks taken
+# dynamically (BW_DYN_UNITS)
+DYN_FORMS = [
+    (16, 1280, 4096, 8, "10 tiles x 4 units on 8 blocks"),
+    (1, 2304, 2048, 8, "one token, 18 tiles x 2 units"),
+    (24, 3200, 2048, 16, "25 tiles x 2 units, the last tile half outside N, bn 32"),
+    (32, 4224, 4096, 16, "33 tiles x 4 units, bn 32"),
+]
+
+
+@pytest.mark.parametrize("form", DYN_FORMS, ids=lambda f: f"{f[0]}x{f[1]}x{f[2]}")
+@pytest.mark.parametrize("tn", [False, True], ids=["KxN", "NxK"])
+def test_dynamic_units(emu, oracle_mod, form, tn):
+    """BW_DYN_UNITS: every tile cut in units of 16 K-blocks, each taken by whichever block's producer asks next (a
+    counter in global memory) and passed to its MMA issuer and epilogue through a queue in shared memory; a tile's last
+    unit sums the partials in unit order.  Blocks start apart and the epilogues pause at random, so the units go to
+    different blocks on every call: three calls must give the same bits, and the counters (the tiles', the next unit's,
+    the finished blocks') must be back at zero after each."""
+    M, N, K, sms, _ = form
+    q = plan_of(emu, M, N, K, sms)
+    assert q["dyn"] == 1 and q["splits"] >= 2 and q["dp_tiles"] == 0 and q["counters"] == q["tiles"] + 2, q
+    A, B = oracle_mod.lcg_inputs(M, N, K)
+    ref = oracle_mod.gemm_f64(A, B)
+    emu.bw_emu_set(b"ld_delay_us", 10)
+    emu.bw_emu_set(b"start_jitter_us", 20000)
+    try:
+        first = None
+        for _ in range(3):
+            rc, C, status, dirty, nf, msg = emulate(emu, A, B, M, N, K, sms, tn=tn)
+            assert rc == 0 and nf == 0, f"rc {rc}, {nf} findings, first: {msg}"
+            assert status[0] == 0 and dirty == 0, (status, dirty)
+            r = oracle_mod.check(C, ref, K)
+            assert r["nonfinite"] == 0 and r["violations"] == 0 and r["normwise"] <= 2e-3, r
+            first = C.copy() if first is None else first
+            assert np.array_equal(first, C), "calls differ"
+    finally:
+        emu.bw_emu_set(b"ld_delay_us", 0)
+        emu.bw_emu_set(b"start_jitter_us", 0)
+
+
+@pytest.mark.parametrize("drop", [0, 7])
+def test_a_stalled_dynamic_unit_call_ends_with_a_status(emu, drop):
+    """A TMA completion that never arrives under dynamic units: the bounded waits give up (the unit queue's too), the
+    status word names one, every thread leaves; the counter of the next unit and of the finished blocks are back at
+    zero (the last block puts them back even after an abort)."""
+    M, N, K = 16, 1280, 4096
+    A = np.full((M, K), 0x3C00, np.uint16)
+    B = np.full((K, N), 0x3C00, np.uint16)
+    emu.bw_emu_set(b"wait_ns", 300_000_000)
+    emu.bw_emu_set(b"barrier_limit_ms", 30_000)
+    emu.bw_emu_set(b"drop_tma", drop)
+    try:
+        rc, C, status, dirty, nf, msg = emulate(emu, A, B, M, N, K, 8)
+    finally:
+        emu.bw_emu_set(b"drop_tma", -1)
+        emu.bw_emu_set(b"wait_ns", 60_000_000_000)
+        emu.bw_emu_set(b"barrier_limit_ms", 120_000)
+    assert rc == 0 and nf == 0, f"{nf} findings, first: {msg}"
+    role, kind = status[1] >> 16, (status[1] >> 8) & 0xFF
+    assert status[0] == 3 and (role, kind) in ((1, 0), (2, 2), (0, 1), (0, 9), (1, 9), (2, 9)), status
+
+
 @pytest.mark.parametrize("variant", range(1, 8))
 def test_every_variant_on_the_emulator(emu, oracle_mod, variant):
     for M, N, K in ((256, 512, 256), (16, 512, 256), (24, 512, 256), (130, 512, 256)):
