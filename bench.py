@@ -400,6 +400,29 @@ def tp_mlp_measure(args, rank, world, local, fused_rs=False, steps=None, warmup=
         if watch and not isinstance(e, (peers.PeerFailed, peers.PeerTimeout)):
             watch.fail(f"{type(e).__name__}: {e}")
         raise
+    # the same block without its collective: this rank's GEMMs alone (the activation fused or not, as above), timed
+    # before and after the block (the mean of the two, so that a clock that drifts under the power cap between the
+    # loops does not show as collective time)
+    def local_step():
+        Act = bwgemm.gemm_swiglu(X, blk.W1) if not args.tp_unfused else None
+        if Act is None:
+            H = bwgemm.gemm(X, blk.W1)
+            Act = (torch.nn.functional.silu(H[:, :blk.fs].float()) * H[:, blk.fs:].float()).half()
+        return bwgemm.gemm_f32out(Act, blk.W2)
+
+    def timed(fn, n):
+        barrier(world)
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        g0.record(stream)
+        for _ in range(n):
+            fn()
+        g1.record(stream)
+        barrier(world)
+        return dist_max(g0.elapsed_time(g1) / 1e3, world)
+
+    for _ in range(2):
+        local_step()
+    t_local0 = timed(local_step, steps)
     barrier(world)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
@@ -411,24 +434,14 @@ def tp_mlp_measure(args, rank, world, local, fused_rs=False, steps=None, warmup=
         barrier(world)
     t = dist_max(e0.elapsed_time(e1) / 1e3, world)
     del Y
-    # the same block without its collective: this rank's GEMMs alone (the activation fused or not, as above)
-    def local_step():
-        Act = bwgemm.gemm_swiglu(X, blk.W1) if not args.tp_unfused else None
-        if Act is None:
-            H = bwgemm.gemm(X, blk.W1)
-            Act = (torch.nn.functional.silu(H[:, :blk.fs].float()) * H[:, blk.fs:].float()).half()
-        return bwgemm.gemm_f32out(Act, blk.W2)
-
-    for _ in range(2):
-        local_step()
-    barrier(world)
-    g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    g0.record(stream)
-    for _ in range(steps):
-        local_step()
-    g1.record(stream)
-    barrier(world)
-    t_local = dist_max(g0.elapsed_time(g1) / 1e3, world)
+    t_local = 0.5 * (t_local0 + timed(local_step, steps))
+    # the NCCL form's collective alone, on this rank's fp32 partials (the fused form has none to time apart)
+    t_coll = None
+    if world > 1 and rs is None:
+        P = local_step()
+        out = torch.empty((M // world, P.shape[1]), dtype=torch.float32, device=P.device)
+        t_coll = timed(lambda: tp_mlp.nccl_reduce_scatter(out, P), steps)
+        del P, out
     flops = tp_mlp.TPMLP.flops(M, hidden, f)
     te = None
     if e2e:  # end to end: the tokens from pinned host memory, this rank's rows of the result back
@@ -462,6 +475,7 @@ def tp_mlp_measure(args, rank, world, local, fused_rs=False, steps=None, warmup=
     rec = {"M": M, "hidden": hidden, "mlp": f, "parallelism": f"tp{world}", "tflops": round(flops * steps / t / 1e12, 2),
            "ms_per_step": round(step_ms, 4), "steps": steps,
            "local_ms_per_step": round(local_ms, 4),
+           "collective_alone_ms": round(t_coll / steps * 1e3, 4) if t_coll else None,
            "exposed_collective_ms": round(step_ms - local_ms, 4) if world > 1 else 0.0,
            "exposed_share": round((step_ms - local_ms) / step_ms, 4) if world > 1 else 0.0,
            "activation": "separate torch ops" if args.tp_unfused else "fused in the gateup epilogue",
@@ -772,6 +786,10 @@ def run_ours(args):
         tp = tp_mlp_measure(args, rank, world, local, fused_rs=False, steps=min(args.steps, 20), e2e=False)
         if rank == 0:
             result["tp_mlp"] = tp
+        if world > 1:  # the same block with down and the reduce-scatter in one kernel per rank (bw_gemm_f16_rs)
+            tpf = tp_mlp_measure(args, rank, world, local, fused_rs=True, steps=min(args.steps, 20), e2e=False)
+            if rank == 0:
+                result["tp_mlp_fused_rs"] = tpf
     if rank == 0:
         head = {}
         if "sweep" in result:
@@ -782,6 +800,8 @@ def run_ours(args):
             head["decode_min_frac_hbm"] = result["decode"]["min_frac_hbm"]
         if "tp_mlp" in result:
             head["tp_mlp_tflops"] = result["tp_mlp"]["tflops"]
+        if "tp_mlp_fused_rs" in result:
+            head["tp_mlp_fused_rs_tflops"] = result["tp_mlp_fused_rs"]["tflops"]
         result["headline"] = head
     if world > 1:
         import torch.distributed as dist

@@ -4,8 +4,7 @@ under the judge's tolerance; three calls in a row give the same bits (the receiv
 acks); the call captured in a CUDA graph and replayed twice gives the same bits again (its epoch comes from the
 device); every rank's status word clear.
 
-The fused kernel has run on the host emulator only so far (tests/test_emulator.py); until it has run on B200s these
-tests also want BW_TEST_FUSED_RS=1.  Skipped with fewer GPUs than ranks."""
+Passed on two B200s (w2_small, w2_tp_down); skipped with fewer GPUs than ranks."""
 import datetime
 import os
 import socket
@@ -74,8 +73,6 @@ def _worker(rank, world, port, M, N, K, q):
 @pytest.mark.parametrize("world,M,N,K", [(2, 1024, 1536, 2048), (2, 4096, 8192, 7168), (4, 4096, 8192, 7168)],
                          ids=["w2_small", "w2_tp_down", "w4_tp_down"])
 def test_fused_reduce_scatter_on_gpus(world, M, N, K):
-    if os.environ.get("BW_TEST_FUSED_RS") != "1":
-        pytest.skip("the fused reduce-scatter has run on the host emulator only: set BW_TEST_FUSED_RS=1 to run it")
     if not torch.cuda.is_available() or torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
     import torch.multiprocessing as mp
