@@ -174,8 +174,9 @@ int ensure_workspace(DeviceState& d, const bw_plan& q, cudaStream_t st)
 }
 
 // Clusters of two blocks for the SM pair (PAIR), of `ksplit` blocks for a swap-AB plan's K split.
+// pdl: with programmatic stream serialisation (attr holds two entries).
 template <int BN, bool SWAP, bool PAIR, int WM = 1, int EPI = kEpiF16>
-cudaLaunchConfig_t launch_config(int grid, cudaStream_t st, cudaLaunchAttribute* attr, int ksplit = 0)
+cudaLaunchConfig_t launch_config(int grid, cudaStream_t st, cudaLaunchAttribute* attr, int ksplit = 0, bool pdl = false)
 {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
@@ -188,8 +189,13 @@ cudaLaunchConfig_t launch_config(int grid, cudaStream_t st, cudaLaunchAttribute*
     attr[0].val.clusterDim.x = (unsigned)size;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
+    cfg.attrs = cluster ? attr : attr + 1;
     cfg.numAttrs = cluster ? 1 : 0;
+    if (pdl) {
+        attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[1].val.programmaticStreamSerializationAllowed = 1;
+        ++cfg.numAttrs;
+    }
     return cfg;
 }
 
@@ -214,7 +220,7 @@ int pair_occupancy(DeviceState& d)
     if (d.pairs >= 0) return BW_OK;
     int rc = set_smem_limit<256, false, true>(d, kBitPair);
     if (rc) return rc;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     const cudaLaunchConfig_t cfg = launch_config<256, false, true>(2, 0, attr);
     int n = 0;
     cudaError_t e = cudaOccupancyMaxActiveClusters(&n, gemm_kernel<256, false, true>, &cfg);
@@ -251,8 +257,10 @@ int launch_kernel(DeviceState& d, unsigned long long bit, const bw_plan& q, cons
     }
     int rc = set_smem_limit<BN, SWAP, PAIR, EPI, WM>(d, bit);
     if (rc) return rc;
-    cudaLaunchAttribute attr[1];
-    const cudaLaunchConfig_t cfg = launch_config<BN, SWAP, PAIR, WM, EPI>(q.grid, st, attr, q.ksplit);
+    cudaLaunchAttribute attr[2];
+    // the reduce-scatter kernel keeps the plain stream order: its peers' calls pair with this one by epoch
+    const cudaLaunchConfig_t cfg = launch_config<BN, SWAP, PAIR, WM, EPI>(q.grid, st, attr, q.ksplit,
+                                                                          BW_PDL && EPI != kEpiRS);
     cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_kernel<BN, SWAP, PAIR, EPI, WM>, mx, my, mc, p);
     if (e != cudaSuccess) return cuda_fail(e, "kernel launch");
     return BW_OK;

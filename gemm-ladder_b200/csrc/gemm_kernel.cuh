@@ -89,6 +89,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int kr = kp ? (int)cluster_ctarank() : 0;  // this block's K range (0: the first)
     const int P = gridDim.x / R, c = blockIdx.x / R;  // the two blocks of a pair share their segments
 
+    // the next call on the stream (launched with programmatic serialisation) may start its setup on free SMs now
+    griddep_launch();
     if (threadIdx.x == 0) {
         for (int i = 0; i < S; ++i) {
             mbar_init(&full[i], 1);   // the (leader's) producer's arrive.expect_tx; the TMA bytes complete it
@@ -134,6 +136,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    // nothing above touches global memory: from here on the call ahead of this one (operands, counters, status word,
+    // workspace) has finished and its writes are visible
+    griddep_wait();
     if (threadIdx.x == 0) BW_TRACE_AT(1);
 
     if (warp == 0) {

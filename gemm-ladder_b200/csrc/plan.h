@@ -131,12 +131,20 @@
                                // alternating by 64-column chunk) and one TMA store per warp and chunk, in place of
                                // whole-line stores from registers (0); the ring loses what the buffers take
 #endif
+#ifndef BW_PDL
+#define BW_PDL 0               // launch with programmatic stream serialisation (not the reduce-scatter kernel): a call's
+                               // blocks start on SMs the call ahead of it has left, do their setup (barriers, tensor
+                               // memory, descriptor prefetch) and wait (griddepcontrol.wait) for that call to finish
+                               // before their first access to global memory (0: the launch waits, as streams do)
+#endif
 #ifndef BW_DYN_UNITS
-#define BW_DYN_UNITS 1         // swap-AB shapes whose tiles outnumber the clusters (stream-K before): every tile cut in
-                               // units of BW_DYN_UNIT_KB K-blocks, each unit taken by whichever block asks next (the
+#define BW_DYN_UNITS 0         // swap-AB shapes whose tiles outnumber the clusters (stream-K otherwise): every tile cut
+                               // in units of BW_DYN_UNIT_KB K-blocks, each unit taken by whichever block asks next (the
                                // producer's atomic on a counter in global memory), the partials summed in unit order by
-                               // the tile's last unit (the same bits whoever ran them).  Static stream-K shares left the
-                               // slowest tenth of the blocks 8-10 us behind the median at gateup_m16 (timeline)
+                               // the tile's last unit (the same bits whoever ran them).  Static stream-K shares leave the
+                               // slowest tenth of the blocks 8-10 us behind the median at gateup_m16, but the units
+                               // measured slower still (160.1 against 144.7 us there: 352 against 318 ns per K-block
+                               // streamed, and 5.6 us of waits for a free accumulator per block), so off
 #endif
 #ifndef BW_DYN_UNIT_KB
 #define BW_DYN_UNIT_KB 16      // K-blocks per unit (a unit's MMAs take ~5 us at M = 16)

@@ -175,6 +175,13 @@ __device__ __forceinline__ uint64_t policy_evict_last()
 // those stores, not older data.
 __device__ __forceinline__ void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
 
+// Programmatic dependent launch.  griddep_launch: this block no longer holds back the grid launched after it on the
+// stream with programmatic serialisation (once every block of this grid has said so or exited, that grid's blocks may
+// start on free SMs and do their setup).  griddep_wait: waits until every grid this one depends on has completed and
+// its memory writes are visible; it returns at once when the launch had no programmatic dependency.
+__device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // A contiguous copy of `bytes` (a multiple of 16) from global to this block's shared memory by the TMA engine,
 // completing on `bar` (both addresses 16-byte aligned).
 __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar)

@@ -104,7 +104,7 @@ Params make_params(const bw_plan& q, int M, int N, int K, void* C, float* work, 
     p.work = work;
     p.counters = counters;
     p.wait_ns = emu::g_wait_ns;  // long by default (the emulator is slow): a wait that runs out is a protocol fault
-    p.rank_wait_ns = emu::g_wait_ns;
+    p.rank_wait_ns = emu::g_rank_wait_ns ? emu::g_rank_wait_ns : emu::g_wait_ns;
     return p;
 }
 
@@ -249,7 +249,8 @@ int dispatch(const bw_plan& q, const CUtensorMap& mx, const CUtensorMap& my, con
 }  // namespace
 }  // namespace bw
 
-// Sets a knob of the emulator: "wait_ns" (the kernel's limit of one bounded wait), "drop_tma" (the n-th TMA / bulk
+// Sets a knob of the emulator: "wait_ns" (the kernel's limit of one bounded wait), "rank_wait_ns" (the limit of a wait
+// for another rank's flag; 0: wait_ns), "drop_tma" (the n-th TMA / bulk
 // completion of each launch never arrives, -1 none), "barrier_limit_ms" (a thread barrier never completed: a finding
 // after this long), "cluster_batch" (clusters run at once; 0: as many as the host's cores take), "noalloc_cap"
 // (>= 0: fp16 calls of variant 0 plan as bw_gemm_f16_noalloc does, its array this many bytes; -1: the rule),
@@ -262,6 +263,7 @@ extern "C" __attribute__((visibility("default"))) int bw_emu_set(const char* nam
     using namespace bw::emu;
     const std::string n = name ? name : "";
     if (n == "wait_ns") g_wait_ns = (unsigned long long)value;
+    else if (n == "rank_wait_ns") g_rank_wait_ns = (unsigned long long)value;
     else if (n == "cluster_batch") bw::g_cluster_batch = value;
     else if (n == "drop_tma") g_drop_tma = value;
     else if (n == "barrier_limit_ms") g_barrier_limit_ms = value;

@@ -93,6 +93,7 @@ struct Barrier {
 // a TMA or bulk completion that the drop_tma knob takes away (its bytes never arrive: a stall, made on purpose)
 inline bool keep_completion() { return g_tma_count.fetch_add(1) != g_drop_tma; }
 inline unsigned long long g_wait_ns = 60ull * 1000000000ull;  // the kernel's limit of one bounded wait
+inline unsigned long long g_rank_wait_ns = 0;  // the limit of a wait for another rank's flag (0: g_wait_ns)
 
 struct MBar {
     int count = 0, pending = 0;

@@ -45,6 +45,8 @@ BUILDS = {
     "wide": ("BW_PAIR_WIDE=1", "BW_PAIR_WIDE_KB_NS=1", "BW_PAIR_WIDE_EPI_NS=0", "BW_FIXUP_KB=0"),
     # the TMA-store epilogue
     "tma": ("BW_EPI_TMA=1",),
+    # the dynamic units of K for swap-AB stream-K shapes (measured slower than static stream-K, off in the library)
+    "dyn": ("BW_DYN_UNITS=1",),
 }
 
 GK, EP, KC, SC, PL = "csrc/gemm_kernel.cuh", "csrc/epilogue.cuh", "csrc/kernel_common.cuh", "csrc/schedule.h", "csrc/plan.h"
@@ -314,17 +316,17 @@ MUTATIONS = [
      "(void)0;", 0, "wide"),
     # ---------------------------------------------------------------- dynamic units (BW_DYN_UNITS)
     ("dyn_unit_overrun", GK, "if (u >= s.sk_tiles * s.splits) u = -1;", "if (u > s.sk_tiles * s.splits) u = -1;", 0,
-     "library"),
-    ("dyn_empty_count", GK, "mbar_init(&uq_empty[i], 2);", "mbar_init(&uq_empty[i], 1);", 0, "library"),
+     "dyn"),
+    ("dyn_empty_count", GK, "mbar_init(&uq_empty[i], 2);", "mbar_init(&uq_empty[i], 1);", 0, "dyn"),
     ("dyn_full_parity", GK, "if (!wait_bounded(&uq_full[qs], (uint32_t)((qi / kPlanUnitQ) & 1), abort_flag, p.wait_ns,\n                                  site(1, 9",
-     "if (!wait_bounded(&uq_full[qs], (uint32_t)((qi / kPlanUnitQ) & 1) ^ 1u, abort_flag, p.wait_ns,\n                                  site(1, 9", 0, "library"),
+     "if (!wait_bounded(&uq_full[qs], (uint32_t)((qi / kPlanUnitQ) & 1) ^ 1u, abort_flag, p.wait_ns,\n                                  site(1, 9", 0, "dyn"),
     ("dyn_epi_slot", GK, "                sg.unit = epi_unit[seg & 1];", "                sg.unit = epi_unit[0];", 0,
-     "library"),
-    ("dyn_no_reset", GK, "            atomicExch(next_unit, 0);\n", "", 0, "library"),
-    ("dyn_last_seg", GK, "const bool last_seg = !s.dyn && !peek.next(s, P, nx);", "const bool last_seg = !peek.next(s, P, nx);",
-     0, "library"),
+     "dyn"),
+    ("dyn_no_reset", GK, "            atomicExch(next_unit, 0);\n", "", 0, "dyn"),
+    ("dyn_epi_queue_slot", GK, "                        u = uq[qs];", "                        u = uq[(qs + 1) % kPlanUnitQ];", 0,
+     "dyn"),
     ("dyn_unit_k", SC, "    k1 = (int)((long long)(sp + 1) * s.kblocks / s.splits);\n}",
-     "    k1 = (int)((long long)(sp + 1) * s.kblocks / s.splits) - (sp == 0);\n}", 0, "library"),
+     "    k1 = (int)((long long)(sp + 1) * s.kblocks / s.splits) - (sp == 0);\n}", 0, "dyn"),
     # ---------------------------------------------------------------- the TMA-store epilogue (BW_EPI_TMA)
     ("tma_no_read_wait", EP, "if (lane == 0) bulk_wait_read<1>();", "(void)0;", 0, "tma"),
     ("tma_one_buffer", GK, "(epi_chunks++ & 1u) * 16384u", "(epi_chunks++ & 0u) * 16384u", 0, "tma"),
@@ -373,8 +375,8 @@ CASES = {
         (512, 2560, 4096, 16, 0, 0, False), # four two-way split tiles, each pair's unit before its whole tiles
         (512, 256, 4096, 8, 0, 0, False),   # two two-way split tiles, no whole tiles: the reductions by bulk copies
         (256, 1280, 8192, 16, 0, 0, False), # five three-way split tiles, 15 units on 8 pairs
-        (16, 1280, 4096, 8, 0, 0, False),   # dynamic units: 10 tiles x 4 units on 8 blocks
-        (24, 3200, 2048, 16, 0, 0, True),   # dynamic units, bn 32, a half tile
+        (16, 1280, 4096, 8, 0, 0, False),   # swap-AB stream-K: 10 tiles on 8 blocks, partial segments before the last
+        (24, 3200, 2048, 16, 0, 0, True),   # swap-AB stream-K, bn 32, a half tile
         (128, 1024, 1024, 8, 0, 0, False),  # the K split over clusters of 2 to 8 (the rule's, then forced sizes)
         (96, 640, 1024, 16, 0, 0, False, 3 * 16 + 1),
         (64, 704, 1024, 16, 0, 0, False, 4 * 16 + 2),
@@ -410,6 +412,12 @@ CASES = {
         (256, 512, 256, 8, 6, 0, False),    # 128 x 64 tiles
         (256, 256, 128, 8, 0, 0, True),     # B as N x K
     ],
+    "dyn": [
+        (16, 1280, 4096, 8, 0, 0, False),   # dynamic units: 10 tiles x 4 units on 8 blocks
+        (24, 3200, 2048, 16, 0, 0, True),   # dynamic units, bn 32, a half tile
+        (1, 2304, 2048, 8, 0, 0, False),    # one token, 18 tiles x 2 units
+        (64, 2304, 1024, 8, 0, 0, False),   # large accumulators: static stream-K beside the option
+    ],
     "wide": [
         (256, 1024, 256, 8, 0, 0, False),   # 256 x 512 pair tiles, whole waves
         (512, 2048, 512, 8, 0, 0, False),
@@ -421,16 +429,23 @@ CASES = {
 
 
 # ------------------------------------------------------------------------------------------------------ one mutant
-def apply(tree, mutation):
-    name, rel, before, after, nth, _ = mutation
-    path = os.path.join(tree, "gemm-ladder_b200", rel)
-    with open(path) as f:
-        text = f.read()
+def locate(text, mutation):
+    """Where occurrence `nth` of the mutation's text starts in `text` (ValueError if it is not there)."""
+    name, rel, before, _, nth, _ = mutation
     at = -1
     for _ in range(nth + 1):
         at = text.find(before, at + 1)
         if at < 0:
             raise ValueError(f"{name}: occurrence {nth} of its text is not in {rel}")
+    return at
+
+
+def apply(tree, mutation):
+    name, rel, before, after, nth, _ = mutation
+    path = os.path.join(tree, "gemm-ladder_b200", rel)
+    with open(path) as f:
+        text = f.read()
+    at = locate(text, mutation)
     with open(path, "w") as f:
         f.write(text[:at] + after + text[at + len(before):])
 

@@ -118,6 +118,9 @@ inline bool wait_bounded(uint64_t* barp, uint32_t parity, volatile int* abort_fl
 
 // ------------------------------------------------------------------ TMA
 inline void prefetch_tmap(const void*) {}
+// One launch at a time here: a grid never starts before the one ahead of it has finished.
+inline void griddep_launch() {}
+inline void griddep_wait() {}
 // A tiled load into this block's shared memory, carried out later by its TMA engine; its bytes complete on `bar`
 // (a shared::cluster address: possibly the pair leader's) when it lands.
 inline void tma_post(void* dst, const void* tmap, int x, int y, int z, uint32_t bar)

@@ -24,7 +24,8 @@ CUDA_INCLUDE = os.path.join(os.environ.get("CUDA_HOME", "/usr/local/cuda"), "inc
 # The emulator's builds, by name: the kernel as the library builds it; the options built but off by default (stream-K
 # over a part wave of pair tiles and swap-AB on SM pairs, both measured slower, and the TMA-store epilogue); the swap-AB
 # K split in halves on clusters of two (the rule before the K split over clusters of 2 to 8); part-wave stream-K alone;
-# the 256 x 512 pair tile forced wherever the rule allows it; the TMA-store epilogue alone.
+# the 256 x 512 pair tile forced wherever the rule allows it; the TMA-store epilogue alone; the dynamic units of K
+# (measured slower than static stream-K).
 BUILDS = {
     "library": (),
     "next": ("BW_SK_PART_WAVE=1", "BW_SWAP_PAIR=1", "BW_EPI_TMA=1"),
@@ -32,6 +33,7 @@ BUILDS = {
     "part": ("BW_SK_PART_WAVE=1", "BW_PAIR_WIDE=0"),
     "wide": ("BW_PAIR_WIDE=1", "BW_PAIR_WIDE_KB_NS=1", "BW_PAIR_WIDE_EPI_NS=0", "BW_FIXUP_KB=0"),
     "tma": ("BW_EPI_TMA=1",),
+    "dyn": ("BW_DYN_UNITS=1",),
 }
 
 
@@ -94,6 +96,12 @@ def emu_wide(emu_builds):
     """The 256 x 512 pair tile forced wherever the rule allows it (its estimated costs, and the fix-ups', set so that it
     always wins), to run the wide kernel on shapes small enough to emulate."""
     return emu_builds["wide"]
+
+
+@pytest.fixture(scope="module")
+def emu_dyn(emu_builds):
+    """Swap-AB stream-K shapes with small accumulators as units of fixed K ranges taken dynamically (BW_DYN_UNITS 1)."""
+    return emu_builds["dyn"]
 
 
 def plan_of(L, M, N, K, sms, variant=0):
@@ -214,23 +222,23 @@ DYN_FORMS = [
 
 @pytest.mark.parametrize("form", DYN_FORMS, ids=lambda f: f"{f[0]}x{f[1]}x{f[2]}")
 @pytest.mark.parametrize("tn", [False, True], ids=["KxN", "NxK"])
-def test_dynamic_units(emu, oracle_mod, form, tn):
+def test_dynamic_units(emu_dyn, oracle_mod, form, tn):
     """BW_DYN_UNITS: every tile cut in units of 16 K-blocks, each taken by whichever block's producer asks next (a
     counter in global memory) and passed to its MMA issuer and epilogue through a queue in shared memory; a tile's last
     unit sums the partials in unit order.  Blocks start apart and the epilogues pause at random, so the units go to
     different blocks on every call: three calls must give the same bits, and the counters (the tiles', the next unit's,
     the finished blocks') must be back at zero after each."""
     M, N, K, sms, _ = form
-    q = plan_of(emu, M, N, K, sms)
+    q = plan_of(emu_dyn, M, N, K, sms)
     assert q["dyn"] == 1 and q["splits"] >= 2 and q["dp_tiles"] == 0 and q["counters"] == q["tiles"] + 2, q
     A, B = oracle_mod.lcg_inputs(M, N, K)
     ref = oracle_mod.gemm_f64(A, B)
-    emu.bw_emu_set(b"ld_delay_us", 10)
-    emu.bw_emu_set(b"start_jitter_us", 20000)
+    emu_dyn.bw_emu_set(b"ld_delay_us", 10)
+    emu_dyn.bw_emu_set(b"start_jitter_us", 20000)
     try:
         first = None
         for _ in range(3):
-            rc, C, status, dirty, nf, msg = emulate(emu, A, B, M, N, K, sms, tn=tn)
+            rc, C, status, dirty, nf, msg = emulate(emu_dyn, A, B, M, N, K, sms, tn=tn)
             assert rc == 0 and nf == 0, f"rc {rc}, {nf} findings, first: {msg}"
             assert status[0] == 0 and dirty == 0, (status, dirty)
             r = oracle_mod.check(C, ref, K)
@@ -238,27 +246,27 @@ def test_dynamic_units(emu, oracle_mod, form, tn):
             first = C.copy() if first is None else first
             assert np.array_equal(first, C), "calls differ"
     finally:
-        emu.bw_emu_set(b"ld_delay_us", 0)
-        emu.bw_emu_set(b"start_jitter_us", 0)
+        emu_dyn.bw_emu_set(b"ld_delay_us", 0)
+        emu_dyn.bw_emu_set(b"start_jitter_us", 0)
 
 
 @pytest.mark.parametrize("drop", [0, 7])
-def test_a_stalled_dynamic_unit_call_ends_with_a_status(emu, drop):
+def test_a_stalled_dynamic_unit_call_ends_with_a_status(emu_dyn, drop):
     """A TMA completion that never arrives under dynamic units: the bounded waits give up (the unit queue's too), the
     status word names one, every thread leaves; the counter of the next unit and of the finished blocks are back at
     zero (the last block puts them back even after an abort)."""
     M, N, K = 16, 1280, 4096
     A = np.full((M, K), 0x3C00, np.uint16)
     B = np.full((K, N), 0x3C00, np.uint16)
-    emu.bw_emu_set(b"wait_ns", 300_000_000)
-    emu.bw_emu_set(b"barrier_limit_ms", 30_000)
-    emu.bw_emu_set(b"drop_tma", drop)
+    emu_dyn.bw_emu_set(b"wait_ns", 300_000_000)
+    emu_dyn.bw_emu_set(b"barrier_limit_ms", 30_000)
+    emu_dyn.bw_emu_set(b"drop_tma", drop)
     try:
-        rc, C, status, dirty, nf, msg = emulate(emu, A, B, M, N, K, 8)
+        rc, C, status, dirty, nf, msg = emulate(emu_dyn, A, B, M, N, K, 8)
     finally:
-        emu.bw_emu_set(b"drop_tma", -1)
-        emu.bw_emu_set(b"wait_ns", 60_000_000_000)
-        emu.bw_emu_set(b"barrier_limit_ms", 120_000)
+        emu_dyn.bw_emu_set(b"drop_tma", -1)
+        emu_dyn.bw_emu_set(b"wait_ns", 60_000_000_000)
+        emu_dyn.bw_emu_set(b"barrier_limit_ms", 120_000)
     assert rc == 0 and nf == 0, f"{nf} findings, first: {msg}"
     role, kind = status[1] >> 16, (status[1] >> 8) & 0xFF
     assert status[0] == 3 and (role, kind) in ((1, 0), (2, 2), (0, 1), (0, 9), (1, 9), (2, 9)), status
@@ -483,11 +491,12 @@ def test_fused_reduce_scatter_without_a_rank_ends_with_a_status(emu, absent):
     status words say so, and every block of every other rank leaves."""
     world, M, N, K = 2, 512, 512, 256
     As, Bs = rs_inputs(world, M, N, K)
-    emu.bw_emu_set(b"wait_ns", 300_000_000)
+    # only the waits for the other rank run out soon: a pipeline wait slowed by a loaded host keeps the long limit
+    emu.bw_emu_set(b"rank_wait_ns", 300_000_000)
     try:
         rc, Cs, status, nf, msg = emulate_rs(emu, As, Bs, M, N, K, 8, calls=2, absent=absent)
     finally:
-        emu.bw_emu_set(b"wait_ns", 60_000_000_000)
+        emu.bw_emu_set(b"rank_wait_ns", 0)
     assert rc == 0 and nf == 0, f"{nf} findings, first: {msg}"
     other = 1 - absent
     code, where = status[other][0], status[other][1]
