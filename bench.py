@@ -71,6 +71,8 @@ def parse():
     ap.add_argument("--sweep", action="store_true",
                     help="time the judge's 17 shapes against cuBLAS (on by default for the 1-GPU config1 run)")
     ap.add_argument("--no-sweep", action="store_true", help="leave the 17-shape sweep out of the default run")
+    ap.add_argument("--sweep-shapes", default=None,
+                    help="--sweep: only these shapes (comma-separated names of the set, or MxNxK)")
     ap.add_argument("--no-decode", action="store_true", help="leave the decode block (config 3) out")
     ap.add_argument("--no-sustained", action="store_true", help="leave the sustained config-1 run out")
     ap.add_argument("--no-tp", action="store_true", help="leave the tensor-parallel MLP sub-record (config 4) out")
@@ -273,7 +275,9 @@ def cpu_baseline(M, N, K, seconds):
 
 def sweep(args, stream_runs=3):
     """The judge's 17 shapes (+ BASELINE's ladder variants): ours and torch.matmul (cuBLAS), CUDA graphs of G calls
-    on 3 rotating input sets, interleaved rounds, median; ratio = cuBLAS time / ours (the judge's ratio)."""
+    on 3 rotating input sets, interleaved rounds, median; ratio = cuBLAS time / ours (the judge's ratio).  With a third
+    arm (--ab-lib) 4 rounds, each arm first in two of them and last in the other two.  --sweep-shapes: only the named
+    shapes (a name of the set, or MxNxK); the geomean then only if all 17 were run."""
     import ctypes
 
     import torch
@@ -296,9 +300,21 @@ def sweep(args, stream_runs=3):
             raise RuntimeError(f"{args.ab_lib}: status {rc}")
 
     arms = ("ours", "cublas") + (("other",) if other else ())
+    if other:
+        stream_runs = 4
+    shapes = list(JUDGE_B200) + [LADDER_4096, CONFIG1]
+    if args.sweep_shapes:
+        known = {n: (n, M, N, K) for n, M, N, K in shapes}
+        shapes = []
+        for w in args.sweep_shapes.split(","):
+            if w in known:
+                shapes.append(known[w])
+            else:
+                M, N, K = map(int, w.lower().split("x"))
+                shapes.append((w, M, N, K))
     out = {}
     ratios = []
-    for name, M, N, K in list(JUDGE_B200) + [LADDER_4096, CONFIG1]:
+    for name, M, N, K in shapes:
         A, B = make_sets(M, N, K, seed=M * 7 + N)
         C = torch.empty((M, N), dtype=torch.float16, device="cuda")
         flops = 2.0 * M * N * K
@@ -325,8 +341,10 @@ def sweep(args, stream_runs=3):
             torch.cuda.synchronize()
             graphs[arm] = g
         times = {arm: [] for arm in arms}
+        # rounds alternate the arms' order (4 rounds: forward, reversed, reversed, forward)
+        flips = (0, 1, 1, 0) if stream_runs == 4 else [r % 2 for r in range(stream_runs)]
         for rnd in range(stream_runs):
-            for arm in (arms if rnd % 2 == 0 else arms[::-1]):
+            for arm in (arms[::-1] if flips[rnd] else arms):
                 g = graphs[arm]
                 g.replay()  # warm-up
                 e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -349,13 +367,18 @@ def sweep(args, stream_runs=3):
             out[name].update({"other_us": round(t_other * 1e6, 2), "other_ratio": round(t_cub / t_other, 4)})
         del graphs, A, B, C
         torch.cuda.empty_cache()
-    judge = [out[n]["ratio"] for n, *_ in JUDGE_B200]
-    res = {"shapes": out, "geomean_ratio_vs_cublas_17": round(math.exp(sum(map(math.log, judge)) / len(judge)), 4),
+    every = all(n in out for n, *_ in JUDGE_B200)
+
+    def geomean(key):
+        if not every:
+            return None
+        v = [out[n][key] for n, *_ in JUDGE_B200]
+        return round(math.exp(sum(map(math.log, v)) / len(v)), 4)
+
+    res = {"shapes": out, "geomean_ratio_vs_cublas_17": geomean("ratio"),
            "reference": "torch.matmul fp16 (cuBLAS heuristic), CUDA graphs, 3 rotating input sets"}
     if other:
-        judge_o = [out[n]["other_ratio"] for n, *_ in JUDGE_B200]
-        res.update({"other_library": args.ab_lib,
-                    "other_geomean_ratio_vs_cublas_17": round(math.exp(sum(map(math.log, judge_o)) / len(judge_o)), 4)})
+        res.update({"other_library": args.ab_lib, "other_geomean_ratio_vs_cublas_17": geomean("other_ratio")})
     return res
 
 

@@ -121,6 +121,16 @@ unsigned long long initial_rank_wait_ns()
 }
 unsigned long long g_rank_wait_ns = initial_rank_wait_ns();
 
+// Programmatic dependent launch between calls (BW_PDL's default; BWGEMM_PDL=0 or 1 sets it for the process): a call
+// whose stream holds another call ahead of it starts its blocks' set-up before that one has finished.
+bool initial_pdl()
+{
+    const char* e = getenv("BWGEMM_PDL");
+    if (e && (e[0] == '0' || e[0] == '1') && e[1] == 0) return e[0] == '1';
+    return BW_PDL != 0;
+}
+bool g_pdl = initial_pdl();
+
 int device_state(DeviceState** out)
 {
     int dev = 0;
@@ -260,7 +270,7 @@ int launch_kernel(DeviceState& d, unsigned long long bit, const bw_plan& q, cons
     cudaLaunchAttribute attr[2];
     // the reduce-scatter kernel keeps the plain stream order: its peers' calls pair with this one by epoch
     const cudaLaunchConfig_t cfg = launch_config<BN, SWAP, PAIR, WM, EPI>(q.grid, st, attr, q.ksplit,
-                                                                          BW_PDL && EPI != kEpiRS);
+                                                                          g_pdl && EPI != kEpiRS);
     cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_kernel<BN, SWAP, PAIR, EPI, WM>, mx, my, mc, p);
     if (e != cudaSuccess) return cuda_fail(e, "kernel launch");
     return BW_OK;

@@ -235,7 +235,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 ++seg;
             }
-            if (!ok && leader) {  // let the loads in flight land (a pair's land on the leader's barriers)
+            // let the loads in flight land (a pair's land on the leader's barriers) before the block may leave: after
+            // this thread's abort, and after an abort elsewhere that left its last stages unconsumed (on the normal
+            // path they have all landed: no wait)
+            if (leader) {
                 const int n = issued < S ? issued : S;
                 for (int i = 1; i <= n; ++i) {
                     const int q = issued - i;
@@ -389,13 +392,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             BW_TRACE_VAL(12, w_full);
             BW_TRACE_VAL(13, w_acc);
             BW_TRACE_VAL(14, n_kb);
-            if (!ok) {  // let the MMAs in flight finish before the tensor memory is freed
-                if (PAIR)
-                    mma_commit_pair(mapa_shared(smem_u32(drain), 0));
-                else
-                    mma_commit(drain);
-                wait_drain(drain, 0, p.wait_ns);
-            }
+            // the MMAs in flight finish before the tensor memory is freed: after this thread's own abort, and after
+            // an abort elsewhere in the block that left the epilogue without waiting for the last accumulator (on the
+            // normal path the last segment's MMAs, which the epilogue is about to wait for anyway)
+            if (PAIR)
+                mma_commit_pair(mapa_shared(smem_u32(drain), 0));
+            else
+                mma_commit(drain);
+            wait_drain(drain, 0, p.wait_ns);
         }
         __syncwarp();
     } else {
@@ -522,6 +526,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // once every other block has arrived on its kgo barrier (their rings are idle and they expect the
                 // bytes).  One thread waits (bounded) and hands each outcome to the other 127.
                 constexpr int kChunks = AN / 16;
+                constexpr int kKw = 2;  // 16-column tensor-memory loads per wait when sending (four: register spills)
                 const int kc = s.ksplit;
                 const int own0 = ksplit_run(kr, kChunks, kc), own1 = ksplit_run(kr + 1, kChunks, kc);
                 const uint32_t recv_bytes = (uint32_t)((kc - 1) * (own1 - own0)) * 8192u;
@@ -536,22 +541,35 @@ __global__ void __launch_bounds__(kThreads, 1)
                 named_bar_sync(1, 128);
                 const bool go = *reduce_flag != 0;
                 if (go) {
+                    // the chunks this block does not own ([0, own0) and [own1, kChunks)), kKw tensor-memory loads
+                    // per wait
 #pragma unroll 1
-                    for (int ch = 0; ch < kChunks; ++ch) {
-                        if (ch >= own0 && ch < own1) continue;
-                        const int o = ksplit_owner(ch, kChunks, kc);
-                        const int r0 = ksplit_run(o, kChunks, kc), len = ksplit_run(o + 1, kChunks, kc) - r0;
-                        const int piece = (kr < o ? kr : kr - 1) * len + (ch - r0);
-                        const uint32_t dst = mapa_shared(smem_u32(smem), (uint32_t)o) + (uint32_t)piece * 8192u +
-                                             (uint32_t)row * 16u;
-                        const uint32_t bar = mapa_shared(smem_u32(krecv), (uint32_t)o);
-                        uint32_t r[16];
-                        tmem_ld16(tbase + (uint32_t)(ch * 16), r);
-                        tmem_wait_ld();
+                    for (int part = 0; part < 2; ++part) {
+                        const int cb = part ? own1 : 0, ce = part ? kChunks : own0;
+#pragma unroll 1
+                        for (int c4 = cb; c4 < ce; c4 += kKw) {
+                            const int nl = ce - c4 < kKw ? ce - c4 : kKw;
+                            uint32_t r[kKw][16];
 #pragma unroll
-                        for (int j = 0; j < 4; ++j)
-                            st_async_v4(dst + (uint32_t)(j * 128 * 16), r[4 * j], r[4 * j + 1], r[4 * j + 2],
-                                        r[4 * j + 3], bar);
+                            for (int h = 0; h < kKw; ++h)
+                                if (h < nl) tmem_ld16(tbase + (uint32_t)((c4 + h) * 16), r[h]);
+                            tmem_wait_ld();
+#pragma unroll
+                            for (int h = 0; h < kKw; ++h) {
+                                if (h >= nl) continue;
+                                const int ch = c4 + h;
+                                const int o = ksplit_owner(ch, kChunks, kc);
+                                const int r0 = ksplit_run(o, kChunks, kc), len = ksplit_run(o + 1, kChunks, kc) - r0;
+                                const int piece = (kr < o ? kr : kr - 1) * len + (ch - r0);
+                                const uint32_t dst = mapa_shared(smem_u32(smem), (uint32_t)o) + (uint32_t)piece * 8192u +
+                                                     (uint32_t)row * 16u;
+                                const uint32_t bar = mapa_shared(smem_u32(krecv), (uint32_t)o);
+#pragma unroll
+                                for (int j = 0; j < 4; ++j)
+                                    st_async_v4(dst + (uint32_t)(j * 128 * 16), r[h][4 * j], r[h][4 * j + 1],
+                                                r[h][4 * j + 2], r[h][4 * j + 3], bar);
+                            }
+                        }
                     }
                 }
                 bool have = go;

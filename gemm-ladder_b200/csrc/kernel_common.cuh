@@ -168,11 +168,14 @@ __host__ __device__ __forceinline__ uint32_t site(uint32_t role, uint32_t kind, 
     return role << 16 | kind << 8 | idx;
 }
 
-// A wait on a barrier that only bounds time (used to drain copies in flight after an abort).
+// A wait on a barrier that only bounds time (used to drain copies and MMAs in flight after an abort, before the
+// shared and tensor memory they write is given up).  What it waits for is already issued, so it waits at least 1 s
+// whatever the limit of the pipeline's waits: a short limit that caught a stall must not cut the drain short.
 __device__ __forceinline__ void wait_drain(uint64_t* bar, uint32_t parity, uint64_t limit_ns)
 {
     const uint32_t b = smem_u32(bar);
     const uint64_t t0 = globaltimer_ns();
+    if (limit_ns < 1000000000ull) limit_ns = 1000000000ull;
     while (!mbar_try_wait(b, parity))
         if (globaltimer_ns() - t0 > limit_ns) return;
 }

@@ -169,6 +169,10 @@ int launch(const bw_plan& q, const CUtensorMap& mx, const CUtensorMap& my, const
                     gridDim = dim3((unsigned)q.grid);
                     blockDim = dim3((unsigned)emu::kCtaThreads);
                     emu::start_jitter((unsigned)blk, seq);
+                    if (emu::g_lead_skew_us > 0 && cs > 1 && blk % cs == 0)
+                        std::this_thread::sleep_for(std::chrono::microseconds(emu::g_lead_skew_us));
+                    if (emu::g_block_ramp_us > 0)
+                        std::this_thread::sleep_for(std::chrono::microseconds((long long)emu::g_block_ramp_us * blk));
                     gemm_kernel<BN, SWAP, PAIR, EPI, WM>(mx, my, mc, p);
                 });
         gate.set_value();
@@ -255,9 +259,10 @@ int dispatch(const bw_plan& q, const CUtensorMap& mx, const CUtensorMap& my, con
 // after this long), "cluster_batch" (clusters run at once; 0: as many as the host's cores take), "noalloc_cap"
 // (>= 0: fp16 calls of variant 0 plan as bw_gemm_f16_noalloc does, its array this many bytes; -1: the rule),
 // "ld_delay_us" (a random pause of up to this long before each tensor-memory load), "start_jitter_us" (each block starts
-// up to this much later), "engine_delay_us" (the asynchronous units' longest delay), "force_ksplit" (c * 16 + wm: the K
-// split takes clusters of c and tiles of 128 wm columns where they fit; 0: the rule).  Returns 0, or -1 for an unknown
-// name.
+// up to this much later), "lead_skew_us" (the first block of every cluster starts this much later), "block_ramp_us"
+// (block b starts b times this much later), "engine_delay_us"
+// (the asynchronous units' longest delay), "force_ksplit" (c * 16 + wm: the K split takes clusters of c and tiles of
+// 128 wm columns where they fit; 0: the rule).  Returns 0, or -1 for an unknown name.
 extern "C" __attribute__((visibility("default"))) int bw_emu_set(const char* name, long long value)
 {
     using namespace bw::emu;
@@ -270,6 +275,8 @@ extern "C" __attribute__((visibility("default"))) int bw_emu_set(const char* nam
     else if (n == "noalloc_cap") bw::g_noalloc_cap = value;
     else if (n == "ld_delay_us") g_ld_delay_us = (int)value;
     else if (n == "start_jitter_us") g_start_jitter_us = (int)value;
+    else if (n == "lead_skew_us") g_lead_skew_us = (int)value;
+    else if (n == "block_ramp_us") g_block_ramp_us = (int)value;
     else if (n == "engine_delay_us") g_engine_delay_us = (int)value;
     else if (n == "force_ksplit") bw::g_emu_force_ksplit = (int)value;
     else return -1;

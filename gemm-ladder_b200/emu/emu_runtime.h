@@ -112,6 +112,8 @@ inline int g_ld_delay_us = 0;
 // The longest random delay (microseconds) before a block's threads start the kernel (0: none; each block its own),
 // so that a block whose cluster peer has not yet set up its barriers or tensor memory meets them unset.
 inline int g_start_jitter_us = 0;
+inline int g_lead_skew_us = 0;  // the first block of every cluster starts this much later than the others
+inline int g_block_ramp_us = 0;  // block b starts b times this much later than block 0
 
 // One of a block's asynchronous units (its TMA engine, or its tensor core): work issued to it runs later, in issue
 // order, on a host thread of its own, each item after a random delay of up to g_engine_delay_us -- so the kernel sees

@@ -305,6 +305,10 @@ MUTATIONS = [
      0, "library"),
     ("ksplit_sum_order", GK, "const float4* src = ring + (size_t)((sb < kr ? sb : sb - 1) * (own1 - own0) +",
      "const float4* src = ring + (size_t)((sb < kr ? sb : sb) * (own1 - own0) +", 0, "library"),
+    ("ksplit_send_batch_chunk", GK, "const int ch = c4 + h;\n                                const int o = ksplit_owner",
+     "const int ch = c4;\n                                const int o = ksplit_owner", 0, "library"),
+    ("bulk_own_batch_offset", EP, "if (h < nl) tmem_ld16(tbase + (uint32_t)((c4 + h) * 16), r[h]);\n        tmem_wait_ld();",
+     "if (h < nl) tmem_ld16(tbase + (uint32_t)(c4 * 16), r[h]);\n        tmem_wait_ld();", 0, "library"),
     ("ksplit_owner_run", SC, "BW_HD inline int ksplit_run(int o, int n, int c) { return o * n / c; }",
      "BW_HD inline int ksplit_run(int o, int n, int c) { return o * n / c + (o == 1); }", 0, "library"),
     ("wide_first_half_early", GK, "if (G::kHalves && c0 + kLdw == AN / 2) release_acc(0);  // the first half is read",
@@ -540,8 +544,16 @@ def check(lib_path, build_name, cluster_batch):
         A, B = oracle.lcg_inputs(M, N, K)
         ref = oracle.gemm_f64(A, B)
         first = None
-        for rep in range(2):
+        for rep in range(3):
+            # the second launch starts each cluster's first block 20 ms after the others: a block that sends its sums
+            # into the first block's ring before that block says its ring is idle then overwrites live stages.  The
+            # third starts block b 3b ms after block 0: a split tile's later block then finishes its part last while
+            # it has segments to come, and reduces the tile with its stage ring busy
+            L.bw_emu_set(b"lead_skew_us", 20000 if rep == 1 else 0)
+            L.bw_emu_set(b"block_ramp_us", 3000 if rep == 2 else 0)
             rc, Cp, st, dirty, nf, msg = call(A, B, M, N, K, sms, variant, epi, tn)
+            L.bw_emu_set(b"lead_skew_us", 0)
+            L.bw_emu_set(b"block_ramp_us", 0)
             C, pad = Cp[:M], Cp[M:]
             if rc != 0:
                 return report(f"{tag}: status {rc}")

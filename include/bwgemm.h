@@ -206,7 +206,10 @@ int bw_gemm_status(int* code, unsigned* site, unsigned* block, unsigned* segment
 int bw_gemm_clear_status(void);
 
 /* The limit of any single wait on a barrier, in nanoseconds (default 1 s; the BWGEMM_WAIT_NS environment variable
- * sets it at load).  Returns the previous limit. */
+ * sets it at load).  Returns the previous limit.
+ * BWGEMM_PDL=1 in the environment at load launches every call but bw_gemm_f16_rs with programmatic stream
+ * serialisation: its blocks may start their set-up before the call ahead of it on the stream has finished, and wait
+ * for it before their first access to global memory.  Off by default. */
 unsigned long long bw_gemm_set_wait_limit_ns(unsigned long long ns);
 
 /*
