@@ -78,6 +78,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     volatile int* uq = abort_flag + 7;         // s.dyn: the unit queue (kPlanUnitQ entries; -1: no unit left)
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+#ifdef BW_TRACE
+    const long long clk0 = clock64();  // SM cycles from entry to exit (slot 15): the block's mean SM clock
+#endif
     if (threadIdx.x == 0) {
         BW_TRACE_CLEAR();
         BW_TRACE_AT(0);
@@ -827,7 +830,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         else
             tmem_dealloc(tmem_base, G::kTmemCols);
     }
-    if (threadIdx.x == 0) BW_TRACE_AT(5);
+    if (threadIdx.x == 0) {
+        BW_TRACE_AT(5);
+        BW_TRACE_VAL(15, clock64() - clk0);
+    }
 }
 
 }  // namespace bw
