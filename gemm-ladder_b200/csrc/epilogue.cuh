@@ -278,18 +278,13 @@ __device__ __noinline__ bool reduce_tile_bulk(const Params& p, int P, int tile, 
     if (threadIdx.x == kEpiThread0) BW_TRACE_AT(10);
     // [col / 4][row][4] within a slot: consecutive rows are consecutive 16-byte vectors
     const float4* base = reinterpret_cast<const float4*>(ring) + row;
-    // this block's own 16-column chunks c4 .. c4 + nl - 1 (nl <= 2) from tensor memory (own_mine), one wait for both
-    auto load_own = [&](int c4, int nl, uint32_t (&r)[2][16]) {
-        if (!own_mine) return;
-#pragma unroll
-        for (int h = 0; h < 2; ++h)
-            if (h < nl) tmem_ld16(tbase + (uint32_t)((c4 + h) * 16), r[h]);
-        tmem_wait_ld();
-    };
-    // the sum of 16 columns (chunk) of this row, in summation order (r: this block's own, if own_mine)
-    auto sum_chunk = [&](int chunk, const uint32_t (&r)[16], float4 (&acc)[4]) {
+    // the sum of 16 columns (chunk) of this row, in summation order
+    auto sum_chunk = [&](int chunk, float4 (&acc)[4]) {
         float4 own[4];
         if (own_mine) {
+            uint32_t r[16];
+            tmem_ld16(tbase + (uint32_t)(chunk * 16), r);
+            tmem_wait_ld();
 #pragma unroll
             for (int q = 0; q < 4; ++q)
                 own[q] = make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]),
@@ -330,10 +325,8 @@ __device__ __noinline__ bool reduce_tile_bulk(const Params& p, int P, int tile, 
             float v[64];
 #pragma unroll
             for (int h = 0; h < 4; ++h) {
-                uint32_t r[2][16];
-                load_own(c0 / 16 + h, 1, r);
                 float4 acc[4];
-                sum_chunk(c0 / 16 + h, r[0], acc);
+                sum_chunk(c0 / 16 + h, acc);
 #pragma unroll
                 for (int q = 0; q < 4; ++q) {
                     v[16 * h + 4 * q] = acc[q].x;
@@ -346,25 +339,18 @@ __device__ __noinline__ bool reduce_tile_bulk(const Params& p, int P, int tile, 
         }
     } else {
 #pragma unroll 1
-        for (int c4 = 0; c4 < kChunks; c4 += 2) {  // two chunks per tensor-memory wait
-            const int nl = kChunks - c4 < 2 ? kChunks - c4 : 2;
-            uint32_t r[2][16];
-            load_own(c4, nl, r);
+        for (int chunk = 0; chunk < kChunks; ++chunk) {
+            float4 acc[4];
+            sum_chunk(chunk, acc);
+            float v[16];
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                if (h >= nl) continue;
-                float4 acc[4];
-                sum_chunk(c4 + h, r[h], acc);
-                float v[16];
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    v[4 * q] = acc[q].x;
-                    v[4 * q + 1] = acc[q].y;
-                    v[4 * q + 2] = acc[q].z;
-                    v[4 * q + 3] = acc[q].w;
-                }
-                store_chunk<SWAP, EPI, BT>(p, m0, n0, row, (c4 + h) * 16, v, cst);
+            for (int q = 0; q < 4; ++q) {
+                v[4 * q] = acc[q].x;
+                v[4 * q + 1] = acc[q].y;
+                v[4 * q + 2] = acc[q].z;
+                v[4 * q + 3] = acc[q].w;
             }
+            store_chunk<SWAP, EPI, BT>(p, m0, n0, row, chunk * 16, v, cst);
         }
     }
     if (threadIdx.x == kEpiThread0) BW_TRACE_AT(11);

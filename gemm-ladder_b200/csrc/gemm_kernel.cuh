@@ -529,7 +529,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // once every other block has arrived on its kgo barrier (their rings are idle and they expect the
                 // bytes).  One thread waits (bounded) and hands each outcome to the other 127.
                 constexpr int kChunks = AN / 16;
-                constexpr int kKw = 2;  // 16-column tensor-memory loads per wait when sending (four: register spills)
                 const int kc = s.ksplit;
                 const int own0 = ksplit_run(kr, kChunks, kc), own1 = ksplit_run(kr + 1, kChunks, kc);
                 const uint32_t recv_bytes = (uint32_t)((kc - 1) * (own1 - own0)) * 8192u;
@@ -543,84 +542,23 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 named_bar_sync(1, 128);
                 const bool go = *reduce_flag != 0;
-                // BW_KSPLIT_BULK: the chunks to send are staged in this block's idle ring after its receive area, and
-                // each 8 KB piece goes to its owner by one bulk copy instead of 512 st.async of 16 bytes (the staging
-                // is never reused: it stays as it is until the owners' barriers have completed, which the cluster's
-                // last barrier waits for).  Where the staging does not fit in the ring: st.async.
-                const uint32_t send_bytes = (uint32_t)(kChunks - (own1 - own0)) * 8192u;
-                if (go && BW_KSPLIT_BULK && recv_bytes + send_bytes <= (uint32_t)G::kRingBytes) {
-                    float4* stg = reinterpret_cast<float4*>(smem + recv_bytes) + row;  // [chunk][col / 4][row][4]
-                    int sent = 0;
+                if (go) {
 #pragma unroll 1
-                    for (int part = 0; part < 2; ++part) {
-                        const int cb = part ? own1 : 0, ce = part ? kChunks : own0;
-#pragma unroll 1
-                        for (int c4 = cb; c4 < ce; c4 += kKw) {
-                            const int nl = ce - c4 < kKw ? ce - c4 : kKw;
-                            uint32_t r[kKw][16];
+                    for (int ch = 0; ch < kChunks; ++ch) {
+                        if (ch >= own0 && ch < own1) continue;
+                        const int o = ksplit_owner(ch, kChunks, kc);
+                        const int r0 = ksplit_run(o, kChunks, kc), len = ksplit_run(o + 1, kChunks, kc) - r0;
+                        const int piece = (kr < o ? kr : kr - 1) * len + (ch - r0);
+                        const uint32_t dst = mapa_shared(smem_u32(smem), (uint32_t)o) + (uint32_t)piece * 8192u +
+                                             (uint32_t)row * 16u;
+                        const uint32_t bar = mapa_shared(smem_u32(krecv), (uint32_t)o);
+                        uint32_t r[16];
+                        tmem_ld16(tbase + (uint32_t)(ch * 16), r);
+                        tmem_wait_ld();
 #pragma unroll
-                            for (int h = 0; h < kKw; ++h)
-                                if (h < nl) tmem_ld16(tbase + (uint32_t)((c4 + h) * 16), r[h]);
-                            tmem_wait_ld();
-#pragma unroll
-                            for (int h = 0; h < kKw; ++h) {
-                                if (h >= nl) continue;
-#pragma unroll
-                                for (int j = 0; j < 4; ++j)
-                                    stg[(size_t)(sent + h) * 512 + j * 128] =
-                                        make_float4(__uint_as_float(r[h][4 * j]), __uint_as_float(r[h][4 * j + 1]),
-                                                    __uint_as_float(r[h][4 * j + 2]), __uint_as_float(r[h][4 * j + 3]));
-                            }
-                            sent += nl;
-                        }
-                    }
-                    fence_proxy_async_shared();  // the staged chunks visible to the bulk copies
-                    named_bar_sync(1, 128);
-                    if (threadIdx.x == kEpiThread0) {
-                        const uint32_t src0 = smem_u32(smem) + recv_bytes;
-                        int i = 0;
-#pragma unroll 1
-                        for (int ch = 0; ch < kChunks; ++ch) {
-                            if (ch >= own0 && ch < own1) continue;
-                            const int o = ksplit_owner(ch, kChunks, kc);
-                            const int r0 = ksplit_run(o, kChunks, kc), len = ksplit_run(o + 1, kChunks, kc) - r0;
-                            const int piece = (kr < o ? kr : kr - 1) * len + (ch - r0);
-                            bulk_copy_to_cluster(mapa_shared(smem_u32(smem), (uint32_t)o) + (uint32_t)piece * 8192u,
-                                                 src0 + (uint32_t)i * 8192u, 8192u,
-                                                 mapa_shared(smem_u32(krecv), (uint32_t)o));
-                            ++i;
-                        }
-                    }
-                } else if (go) {
-                    // the chunks this block does not own ([0, own0) and [own1, kChunks)), kKw tensor-memory loads
-                    // per wait
-#pragma unroll 1
-                    for (int part = 0; part < 2; ++part) {
-                        const int cb = part ? own1 : 0, ce = part ? kChunks : own0;
-#pragma unroll 1
-                        for (int c4 = cb; c4 < ce; c4 += kKw) {
-                            const int nl = ce - c4 < kKw ? ce - c4 : kKw;
-                            uint32_t r[kKw][16];
-#pragma unroll
-                            for (int h = 0; h < kKw; ++h)
-                                if (h < nl) tmem_ld16(tbase + (uint32_t)((c4 + h) * 16), r[h]);
-                            tmem_wait_ld();
-#pragma unroll
-                            for (int h = 0; h < kKw; ++h) {
-                                if (h >= nl) continue;
-                                const int ch = c4 + h;
-                                const int o = ksplit_owner(ch, kChunks, kc);
-                                const int r0 = ksplit_run(o, kChunks, kc), len = ksplit_run(o + 1, kChunks, kc) - r0;
-                                const int piece = (kr < o ? kr : kr - 1) * len + (ch - r0);
-                                const uint32_t dst = mapa_shared(smem_u32(smem), (uint32_t)o) + (uint32_t)piece * 8192u +
-                                                     (uint32_t)row * 16u;
-                                const uint32_t bar = mapa_shared(smem_u32(krecv), (uint32_t)o);
-#pragma unroll
-                                for (int j = 0; j < 4; ++j)
-                                    st_async_v4(dst + (uint32_t)(j * 128 * 16), r[h][4 * j], r[h][4 * j + 1],
-                                                r[h][4 * j + 2], r[h][4 * j + 3], bar);
-                            }
-                        }
+                        for (int j = 0; j < 4; ++j)
+                            st_async_v4(dst + (uint32_t)(j * 128 * 16), r[4 * j], r[4 * j + 1], r[4 * j + 2],
+                                        r[4 * j + 3], bar);
                     }
                 }
                 bool have = go;

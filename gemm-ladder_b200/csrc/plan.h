@@ -131,11 +131,6 @@
                                // alternating by 64-column chunk) and one TMA store per warp and chunk, in place of
                                // whole-line stores from registers (0); the ring loses what the buffers take
 #endif
-#ifndef BW_KSPLIT_BULK
-#define BW_KSPLIT_BULK 1       // the K split's hand-over: each block stages the chunks it sends in its idle ring and
-                               // forwards each 8 KB piece by one shared-to-cluster bulk copy (0: st.async, 16 bytes per
-                               // thread and instruction)
-#endif
 #ifndef BW_PDL
 #define BW_PDL 0               // launch with programmatic stream serialisation (not the reduce-scatter kernel): a call's
                                // blocks start on SMs the call ahead of it has left, do their setup (barriers, tensor

@@ -257,17 +257,6 @@ __device__ __forceinline__ void st_async_v4(uint32_t dst, uint32_t a, uint32_t b
                  : "memory");
 }
 
-// A contiguous copy of `bytes` (a multiple of 16) from this block's shared memory (`src`, a shared::cta address) into
-// another block's of the cluster (`dst`, a shared::cluster address), by the TMA engine, counted as transaction bytes on
-// that block's barrier `bar` (a shared::cluster address): the receiver waits on its barrier alone.  The source must
-// stay as it is until the receiver's barrier has completed.
-__device__ __forceinline__ void bulk_copy_to_cluster(uint32_t dst, uint32_t src, uint32_t bytes, uint32_t bar)
-{
-    asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
-                 "r"(src), "r"(bytes), "r"(bar)
-                 : "memory");
-}
-
 // Orders this thread's accesses after an acquire at cluster scope (after a wait on a barrier another block arrived on).
 __device__ __forceinline__ void fence_acq_rel_cluster() { asm volatile("fence.acq_rel.cluster;" ::: "memory"); }
 

@@ -490,23 +490,6 @@ inline void remote_store(uint32_t dst, const uint32_t* v, uint32_t bytes)
     std::memcpy(c->smem + off, v, bytes);
 }
 
-// A bulk copy of [src, src + bytes) of this block's shared memory into another block's at `dst` (shared::cluster),
-// read when the copy runs: a source overwritten before the receiver's barrier completed shows in the receiver's data.
-inline void remote_bulk(uint32_t dst, uint32_t src, uint32_t bytes)
-{
-    Cta* c = cta_of(dst);
-    const uint32_t off = off_of(dst);
-    if (off % 16 || src % 16 || bytes % 16 || (src >> 24) != 0) {
-        finding("a shared-to-cluster bulk copy not on 16-byte boundaries or from another block");
-        return;
-    }
-    if (src + bytes > (uint32_t)g_smem_limit || off + bytes > (uint32_t)g_smem_limit || over_mbar(c, off, bytes)) {
-        finding("a shared-to-cluster bulk copy past the shared memory or over an mbarrier");
-        return;
-    }
-    std::memcpy(c->smem + off, t_cta->smem + src, bytes);
-}
-
 // ------------------------------------------------------------------ tensor memory and the MMA
 // A fresh allocation holds what earlier kernels left, not zeros: here a NaN in every column, so that an MMA chain
 // that accumulates onto an accumulator it never cleared (accumulate set on its first MMA) shows in the result.

@@ -305,15 +305,6 @@ MUTATIONS = [
      0, "library"),
     ("ksplit_sum_order", GK, "const float4* src = ring + (size_t)((sb < kr ? sb : sb - 1) * (own1 - own0) +",
      "const float4* src = ring + (size_t)((sb < kr ? sb : sb) * (own1 - own0) +", 0, "library"),
-    ("kbulk_src_offset", GK, "src0 + (uint32_t)i * 8192u, 8192u,", "src0 + (uint32_t)(i ^ 1) * 8192u, 8192u,", 0, "library"),
-    ("kbulk_stage_at_ring_start", GK, "float4* stg = reinterpret_cast<float4*>(smem + recv_bytes) + row;",
-     "float4* stg = reinterpret_cast<float4*>(smem) + row;", 0, "library"),
-    ("kbulk_copy_before_staged", GK, "fence_proxy_async_shared();  // the staged chunks visible to the bulk copies\n                    named_bar_sync(1, 128);",
-     "fence_proxy_async_shared();  // the staged chunks visible to the bulk copies", 0, "library"),
-    ("ksplit_send_batch_chunk", GK, "const int ch = c4 + h;\n                                const int o = ksplit_owner",
-     "const int ch = c4;\n                                const int o = ksplit_owner", 0, "library"),
-    ("bulk_own_batch_offset", EP, "if (h < nl) tmem_ld16(tbase + (uint32_t)((c4 + h) * 16), r[h]);\n        tmem_wait_ld();",
-     "if (h < nl) tmem_ld16(tbase + (uint32_t)(c4 * 16), r[h]);\n        tmem_wait_ld();", 0, "library"),
     ("ksplit_owner_run", SC, "BW_HD inline int ksplit_run(int o, int n, int c) { return o * n / c; }",
      "BW_HD inline int ksplit_run(int o, int n, int c) { return o * n / c + (o == 1); }", 0, "library"),
     ("wide_first_half_early", GK, "if (G::kHalves && c0 + kLdw == AN / 2) release_acc(0);  // the first half is read",
@@ -391,7 +382,7 @@ CASES = {
         (64, 704, 1024, 16, 0, 0, False, 4 * 16 + 2),
         (112, 256, 4096, 16, 0, 0, False, 8 * 16 + 1),
         (96, 448, 2624, 16, 0, 0, True, 7 * 16 + 2),
-        (128, 512, 2048, 16, 0, 0, False, 8 * 16 + 2),  # sends too large to stage: by st.async
+        (128, 512, 2048, 16, 0, 0, False, 8 * 16 + 2),  # 16 chunks over 8 blocks of 256-column tiles
         (16, 256, 2048, 8, 0, 0, False),    # K halves deeper than the stage ring
         (256, 512, 1024, 8, 5, 0, False),   # single-SM tiles deeper than the stage ring
         (64, 2304, 1024, 8, 0, 0, False),   # swap-AB stream-K, 256-column tiles, several tiles per block

@@ -187,13 +187,6 @@ inline void st_async_v4(uint32_t dst, uint32_t a, uint32_t b, uint32_t c, uint32
         emu::mb_complete_tx(emu::cta_of(bar), emu::off_of(bar), 16);
     });
 }
-inline void bulk_copy_to_cluster(uint32_t dst, uint32_t src, uint32_t bytes, uint32_t bar)
-{
-    emu::t_cta->tma.post([=] {
-        emu::remote_bulk(dst, src, bytes);
-        emu::mb_complete_tx(emu::cta_of(bar), emu::off_of(bar), bytes);
-    });
-}
 inline void fence_acq_rel_cluster() { std::atomic_thread_fence(std::memory_order_seq_cst); }
 inline void tma_load_2d_pair(void* dst, const void* tmap, int x, int y, uint32_t bar)
 {

@@ -335,8 +335,7 @@ KSPLIT_FORMS = [
     (32, 128, 1536, 16, 6, 1),   # 2 chunks over 6 blocks
     (96, 448, 2624, 16, 7, 2),   # 12 chunks over 7 (runs of 1 and 2), 41 K-blocks in ranges of 5 and 6
     (112, 256, 4096, 16, 8, 1),  # 7 chunks over 8 blocks (one owns none), 8 K-blocks per block
-    (128, 512, 2048, 16, 8, 2),  # 16 chunks over 8: what each block sends and receives (224 KB) outgrows its ring of
-                                 # 192 KB, so it sends by st.async instead of staging for bulk copies
+    (128, 512, 2048, 16, 8, 2),  # 16 chunks over 8 blocks of 256-column tiles, 2 per block: 112 KB received each
 ]
 
 
