@@ -544,10 +544,11 @@ def check(lib_path, build_name, cluster_batch):
         for rep in range(3):
             # the second launch starts each cluster's first block 20 ms after the others: a block that sends its sums
             # into the first block's ring before that block says its ring is idle then overwrites live stages.  The
-            # third starts block b 3b ms after block 0: a split tile's later block then finishes its part last while
-            # it has segments to come, and reduces the tile with its stage ring busy
+            # third starts block b 100 b ms after block 0 (longer than a segment takes here): a split tile's later
+            # block then finishes its part last while it has segments to come, and reduces the tile with its stage
+            # ring busy
             L.bw_emu_set(b"lead_skew_us", 20000 if rep == 1 else 0)
-            L.bw_emu_set(b"block_ramp_us", 3000 if rep == 2 else 0)
+            L.bw_emu_set(b"block_ramp_us", 100000 if rep == 2 else 0)
             rc, Cp, st, dirty, nf, msg = call(A, B, M, N, K, sms, variant, epi, tn)
             L.bw_emu_set(b"lead_skew_us", 0)
             L.bw_emu_set(b"block_ramp_us", 0)
