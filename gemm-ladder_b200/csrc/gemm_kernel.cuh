@@ -583,6 +583,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 named_bar_sync(1, 128);
                 const bool go = *reduce_flag != 0;
+                if (threadIdx.x == kEpiThread0) {
+                    BW_TRACE_AT(7);  // the others' rings are idle
+                    BW_TRACE_VAL(8, 4 | kc << 8);
+                }
                 if (go) {
 #pragma unroll 1
                     for (int ch = 0; ch < kChunks; ++ch) {
@@ -603,6 +607,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                 }
 #endif
+                if (threadIdx.x == kEpiThread0) BW_TRACE_AT(9);  // this thread's parts sent
                 bool have = go;
                 if (recv_bytes) {
                     // the others' parts of this block's chunks (after a failure, bytes still on their way land first;
@@ -616,6 +621,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     have = *recv_flag != 0;
                     if (have) mbar_try_wait(smem_u32(krecv), 0);  // complete: each thread acquires the bytes
                 }
+                if (threadIdx.x == kEpiThread0) BW_TRACE_AT(10);  // the others' parts of this block's chunks are in
                 if (have) {
                     const float4* ring = reinterpret_cast<const float4*>(smem) + row;  // [piece][col / 4][row][4]
 #pragma unroll 1
@@ -648,6 +654,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         store_chunk<SWAP, EPI, BN>(p, m0, n0, row, ch * 16, v, cst);
                     }
                 }
+                if (threadIdx.x == kEpiThread0) BW_TRACE_AT(11);  // this block's chunks summed and stored
                 release_all(acc);
                 named_bar_sync(1, 128);  // the flags are read by all before the block goes on
 #else
