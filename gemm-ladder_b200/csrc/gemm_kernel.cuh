@@ -532,47 +532,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int kc = s.ksplit;
                 const int own0 = ksplit_run(kr, kChunks, kc), own1 = ksplit_run(kr + 1, kChunks, kc);
                 const uint32_t recv_bytes = (uint32_t)((kc - 1) * (own1 - own0)) * 8192u;
-#if BW_KSPLIT_L2
-                // BW_KSPLIT_L2: the hand-over through L2 instead.  Each block writes the chunks it does not own to its
-                // slots of the workspace ([tile][block][chunk], 8 KB each, laid out as the pieces), fences, and arrives
-                // on the others' kgo barriers; once every other block has arrived on its own, it copies its pieces
-                // into its idle ring by the TMA engine (cp.async.bulk, counted on krecv) and sums them as below.
-                float* parts = p.work + (size_t)(sg.tile * kc + kr) * kChunks * 2048;
-#pragma unroll 1
-                for (int ch = 0; ch < kChunks; ++ch) {
-                    if (ch >= own0 && ch < own1) continue;
-                    uint32_t r[16];
-                    tmem_ld16(tbase + (uint32_t)(ch * 16), r);
-                    tmem_wait_ld();
-                    float4* dst = reinterpret_cast<float4*>(parts + (size_t)ch * 2048) + row;
-#pragma unroll
-                    for (int j = 0; j < 4; ++j)
-                        __stcg(dst + j * 128, make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
-                                                          __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3])));
-                }
-                __threadfence();  // this block's parts in memory before its arrivals
-                named_bar_sync(1, 128);
-                if (threadIdx.x == kEpiThread0) {
-                    for (int o = 0; o < kc; ++o)
-                        if (o != kr) mbar_arrive_cluster(mapa_shared(smem_u32(kgo), (uint32_t)o));
-                    const bool ok = wait_bounded(kgo, 0, abort_flag, p.wait_ns, site(2, 6, 0), seg);
-                    if (ok && recv_bytes) {
-                        fence_acq_rel_cluster();     // after the others' arrivals: their parts are in memory,
-                        fence_proxy_async_global();  // and the bulk copies below read what they wrote
-                        mbar_arrive_expect_tx(krecv, recv_bytes);
-                        for (int sb = 0; sb < kc; ++sb) {
-                            if (sb == kr) continue;
-                            const float* src = p.work + (size_t)(sg.tile * kc + sb) * kChunks * 2048;
-                            for (int ch = own0; ch < own1; ++ch)
-                                bulk_load(smem + (size_t)((sb < kr ? sb : sb - 1) * (own1 - own0) + (ch - own0)) * 8192,
-                                          src + (size_t)ch * 2048, 8192u, krecv);
-                        }
-                    }
-                    *reduce_flag = ok ? 1 : 0;
-                }
-                named_bar_sync(1, 128);
-                const bool go = *reduce_flag != 0;
-#else
                 if (threadIdx.x == kEpiThread0) {
                     if (recv_bytes) mbar_arrive_expect_tx(krecv, recv_bytes);
                     for (int o = 0; o < kc; ++o)
@@ -606,15 +565,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                                         r[4 * j + 3], bar);
                     }
                 }
-#endif
                 if (threadIdx.x == kEpiThread0) BW_TRACE_AT(9);  // this thread's parts sent
                 bool have = go;
                 if (recv_bytes) {
-                    // the others' parts of this block's chunks (after a failure, bytes still on their way land first;
-                    // through L2 they are on their way only if this block issued its copies)
+                    // the others' parts of this block's chunks (after a failure, bytes still on their way land first)
                     if (threadIdx.x == kEpiThread0) {
                         const bool ok = go && wait_bounded(krecv, 0, abort_flag, p.wait_ns, site(2, 5, 0), seg);
-                        if (!ok && (go || !BW_KSPLIT_L2)) wait_drain(krecv, 0, p.wait_ns);
+                        if (!ok) wait_drain(krecv, 0, p.wait_ns);
                         *recv_flag = ok ? 1 : 0;
                     }
                     named_bar_sync(1, 128);

@@ -131,11 +131,6 @@
                                // alternating by 64-column chunk) and one TMA store per warp and chunk, in place of
                                // whole-line stores from registers (0); the ring loses what the buffers take
 #endif
-#ifndef BW_KSPLIT_L2
-#define BW_KSPLIT_L2 0         // the K split's hand-over through L2: each block writes the chunks it does not own to
-                               // the workspace and their owners copy them into their idle rings by cp.async.bulk (0:
-                               // st.async of 16 bytes into the owners' rings, through distributed shared memory)
-#endif
 #ifndef BW_PDL
 #define BW_PDL 0               // launch with programmatic stream serialisation (not the reduce-scatter kernel): a call's
                                // blocks start on SMs the call ahead of it has left, do their setup (barriers, tensor
@@ -396,7 +391,6 @@ inline int make_plan(int M, int N, int K, int sms, int pairs, int variant, bw_pl
 #endif
     }
     if (ks) {
-        const bw_plan q0 = q;  // the plan before the K split, for stream-K below if its workspace does not fit
         q.ksplit = ks;
         q.wm = ks_wm;
         q.tiles_n = (N + 128 * q.wm - 1) / (128 * q.wm);
@@ -408,13 +402,8 @@ inline int make_plan(int M, int N, int K, int sms, int pairs, int variant, bw_pl
         q.stages = plan_stages(q.bn, 1, true, q.wm);
         q.smem_bytes = plan_smem_bytes(q.bn, 1, true, q.wm);
         q.tmem_cols = plan_tmem_cols(q.bn * q.wm);
-        // BW_KSPLIT_L2: every block's chunks of every tile, 8 KB each, in the workspace
-        q.workspace_bytes = BW_KSPLIT_L2 ? (size_t)q.tiles * ks * (q.bn * q.wm / 16) * 8192 : 0;
-        if (!work_cap || q.workspace_bytes <= work_cap) {
-            *p = q;
-            return BW_OK;
-        }
-        q = q0;  // a fixed scratch too small for the hand-over: stream-K below
+        *p = q;
+        return BW_OK;
     }
     // stream-K: tiles of 256 weight columns while they still outnumber the SMs (fewer, larger partials otherwise)
     q.wm = 1;
