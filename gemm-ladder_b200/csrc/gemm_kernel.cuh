@@ -717,6 +717,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 SegIter peek = it;
                 Seg nx;
                 const bool last_seg = !s.dyn && !peek.next(s, P, nx);
+                // the reduction may copy the partials into the stage ring only when no later segment streams into it
+                const bool bulk = last_seg && f.nseg <= G::kMaxSum;
                 // every other partial already written: this block is the last; sum them with its own accumulator
                 // straight from tensor memory (no round trip of its own partial)
                 if (threadIdx.x == kEpiThread0) *reduce_flag = ld_acquire_gpu(counter) == f.nseg - 1 ? 2 : 0;
@@ -727,7 +729,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     BW_TRACE_VAL(8, (fast == 2 ? 2 : 3) | f.nseg << 8 | seg << 16);
                 }
                 if (fast == 2) {
-                    if (last_seg && f.nseg <= G::kMaxSum)
+                    if (bulk)
                         reduce_tile_bulk<AN, SWAP, R, G::kMaxSum, EPI, BN>(p, P, sg.tile, rank, f, true, tbase, row, m0, n0,
                                                                   cst, smem, rbar, abort_flag, seg);
                     else
@@ -764,7 +766,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                             BW_TRACE_AT(9);
                             BW_TRACE_VAL(8, 1 | f.nseg << 8 | seg << 16);
                         }
-                        if (last_seg && f.nseg <= G::kMaxSum)
+                        if (bulk)
                             reduce_tile_bulk<AN, SWAP, R, G::kMaxSum, EPI, BN>(p, P, sg.tile, rank, f, true, tbase, row, m0, n0,
                                                                       cst, smem, rbar, abort_flag, seg);
                         else

@@ -190,8 +190,8 @@ MUTATIONS = [
      "library"),
     ("split_counter_kept_slow", GK, "if (threadIdx.x == kEpiThread0) atomicExch(counter, 0);", "(void)counter;", 1,
      "library"),
-    ("split_bulk_not_last_fast", GK, "if (last_seg && f.nseg <= G::kMaxSum)", "if (f.nseg <= G::kMaxSum)", 0, "library"),
-    ("split_bulk_not_last_slow", GK, "if (last_seg && f.nseg <= G::kMaxSum)", "if (f.nseg <= G::kMaxSum)", 1, "library"),
+    ("split_bulk_not_last", GK, "const bool bulk = last_seg && f.nseg <= G::kMaxSum;",
+     "const bool bulk = f.nseg <= G::kMaxSum;", 0, "library"),
     # ---------------------------------------------------------------- K halves on clusters of two (swap-AB)
     ("khalf_expect_half", GK, "mbar_arrive_expect_tx(krecv, 128u * AN * 4u);", "mbar_arrive_expect_tx(krecv, 128u * AN * 2u);",
      0, "halves"),
