@@ -519,6 +519,8 @@ def check(lib_path, build_name, cluster_batch):
     L.bw_emu_set(b"cluster_batch", cluster_batch)
     L.bw_emu_set(b"ld_delay_us", 30)               # a slow epilogue: an MMA that does not wait for it overwrites
     L.bw_emu_set(b"start_jitter_us", 50000)        # blocks start apart: a peer's barriers unset show
+    if build_name == "tma":                        # TMA stores that lag behind the epilogue: a staging buffer rewritten
+        L.bw_emu_set(b"engine_delay_us", 2000)     # before its store has read it shows in C
 
     def call(A, B, M, N, K, sms, variant, epi, tn):
         Bx = np.ascontiguousarray(np.asarray(B).reshape(K, N).T) if tn else np.ascontiguousarray(B)
