@@ -14,9 +14,14 @@ with host buffers: pinned host -> device copies of A and B and the device -> hos
 `value` with the copies of neighbouring steps overlapping each GEMM as a serving loop runs them, `serial_value` with
 everything in order on one stream),
 roofline (the kernel against the measured cuBLAS peak), cpu_baseline (the fp64 oracle on a bounded sample of rows,
-all host threads), clocks sampled through NVML during the timed region, gpu_launches.  --sweep adds the judge's 17
-B200 shapes timed against torch.matmul (cuBLAS) in CUDA graphs, with the geometric mean of the time ratios
-(--ab-lib libbwgemm_next.so adds a third arm, another build of the library, interleaved with the other two).
+all host threads), clocks sampled through NVML during the timed region, gpu_launches.  The default line also holds,
+at N = 1: sweep (the judge's 17 B200 shapes timed against torch.matmul, cuBLAS, in CUDA graphs, with the geometric
+mean of the time ratios; --sweep-shapes a,b,... times only those; --ab-lib <build> adds a third arm, another build of
+the library, interleaved with the other two), sustained (config 1 back to back for --sustained-seconds, under the
+power cap) and decode (the four weights at M = 1 to 64, GB/s against the measured HBM copy
+bandwidth); at every N: tp_mlp (BASELINE config 4 over the job's ranks, with NCCL's reduce-scatter) and, at N > 1,
+tp_mlp_fused_rs (the same with bw_gemm_f16_rs); and a headline record repeating the main figures.  --no-sweep,
+--no-decode, --no-sustained, --no-tp, --no-e2e and --no-cpu leave parts out.
 
 --impl reference: the reference's CPU path (its fp64 i-k-j GEMM, restated in oracle/oracle.c; the reference's GPU
 harness needs its judge, which needs CUDA 13) timed on the host cores on the same workload, in bounded row samples.
